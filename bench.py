@@ -1,0 +1,343 @@
+#!/usr/bin/env python3
+"""Benchmark of the hot path: op-level non-contiguous paged decode attention.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl native|reference]
+    python -m torch.distributed.run --nnodes=1 --nproc-per-node N --master-addr 127.0.0.1 --master-port P \
+        bench.py --gpus N --steps K --warmup W
+
+One step = one attention pass over one batch: 8 requests per GPU, each with 64 query + 32 response rows attending
+4 selected chunks (16 pages of 256 tokens, any physical order, no gather) plus the bidirectional new rows;
+28 query / 4 KV heads, head_dim 128, bf16. Decode is data-parallel over requests, so every rank runs its own batch
+(weak scaling, no data-path collective). Prints ONE JSON line on rank 0.
+
+Timing: CUDA events on the launching stream, max over ranks. Consecutive steps use different block tables that
+together cover the whole 537 MB pool, so a step never finds its pages in the 126 MB L2.
+`--impl reference` times the CPU restatement of the reference's own path (oracle/, all host threads) on a bounded
+sample of the same workload; it is the only place the product bench executes the oracle, and only as the thing
+being compared against.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import math
+import os
+import subprocess
+import sys
+import threading
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+if ROOT not in sys.path:
+    sys.path.insert(0, ROOT)
+
+import torch  # noqa: E402
+
+# ---- workload: BASELINE.json configs[1] ------------------------------------------------------------------
+NUM_REQ = 8
+HQ, HKV, D = 28, 4, 128
+PAGE = 256
+CHUNKS_IN_POOL, CHUNK_TOKENS, SEL_CHUNKS = 32, 1024, 4
+QUERY_ROWS, RESP_ROWS = 64, 32
+ROWS = QUERY_ROWS + RESP_ROWS
+PAGES_PER_CHUNK = CHUNK_TOKENS // PAGE
+CTX = SEL_CHUNKS * CHUNK_TOKENS
+N_TABLES = CHUNKS_IN_POOL // SEL_CHUNKS  # disjoint selections that together touch the whole pool
+
+FLOPS_PER_STEP = NUM_REQ * 4 * HQ * D * ROWS * (CTX + ROWS)                        # QK^T and PV
+BYTES_PER_STEP = NUM_REQ * (CTX * 2 * HKV * D * 2 + ROWS * (2 * HQ + 2 * HKV) * D * 2)  # KV pages + q/k/v/out rows
+WORKLOAD = ("configs[1] op-level paged decode attention: 8 req x (64 query + 32 response rows), 28/4 heads, d128, "
+            "page 256, 4 of 32 chunks (4096 ctx tokens) per request via block table, bidirectional, N(0,1) bf16")
+
+
+def load_peaks():
+    path = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(path):
+        with open(path) as handle:
+            data = json.load(handle)
+        return dict(hbm=float(data["hbm_gbs"]), tflops=float(data["bf16_tflops"]), source="measured")
+    return dict(hbm=6650.0, tflops=1590.0, source="fallback")
+
+
+class ClockSampler:
+    """Samples SM clock and throttle reasons with nvidia-smi while the timed region runs."""
+
+    FIELDS = ("clocks.sm,clocks.max.sm,clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, index: int):
+        self.index = index
+        self.samples = []
+        self.proc = None
+        self.thread = None
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(["nvidia-smi", f"--id={self.index}", f"--query-gpu={self.FIELDS}",
+                                          "--format=csv,noheader,nounits", "-lms", "100"], stdout=subprocess.PIPE,
+                                         stderr=subprocess.DEVNULL, text=True)
+        except OSError:
+            self.proc = None
+            return
+        self.thread = threading.Thread(target=self._pump, daemon=True)
+        self.thread.start()
+
+    def _pump(self):
+        for line in self.proc.stdout:
+            self.samples.append(line.strip())
+
+    def stop(self):
+        if self.proc is None:
+            return dict(sm_mhz=None, sm_max_mhz=None, reasons=["nvidia-smi unavailable"])
+        time.sleep(0.15)
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except subprocess.TimeoutExpired:
+            self.proc.kill()
+        sm, sm_max, reasons = [], None, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for line in self.samples:
+            parts = [p.strip() for p in line.split(",")]
+            if len(parts) < 6:
+                continue
+            try:
+                sm.append(float(parts[0]))
+                sm_max = float(parts[1])
+            except ValueError:
+                continue
+            for name, val in zip(names, parts[2:6]):
+                if val.lower().startswith("active"):
+                    reasons.add(name)
+        sm.sort()
+        return dict(sm_mhz=sm[len(sm) // 2] if sm else None, sm_max_mhz=sm_max, reasons=sorted(reasons), samples=len(sm))
+
+
+def build_batch(seed: int, device: torch.device):
+    """Seeded synthetic batch of the op-level config. The pool is N(0,1) bf16; block tables come from seeded
+    permutations; N_TABLES tables per request pick disjoint chunk sets so that rotating them sweeps the pool."""
+    g = torch.Generator().manual_seed(seed)
+    pages_per_req = CHUNKS_IN_POOL * PAGES_PER_CHUNK
+    num_pages = NUM_REQ * pages_per_req
+    k_cache = torch.randn(num_pages, PAGE, HKV, D, generator=g, dtype=torch.float32).to(torch.bfloat16)
+    v_cache = torch.randn(num_pages, PAGE, HKV, D, generator=g, dtype=torch.float32).to(torch.bfloat16)
+    tables = torch.empty(N_TABLES, NUM_REQ, SEL_CHUNKS * PAGES_PER_CHUNK, dtype=torch.int32)
+    for r in range(NUM_REQ):
+        perm = torch.randperm(CHUNKS_IN_POOL, generator=g)
+        for t in range(N_TABLES):
+            chosen = perm[t * SEL_CHUNKS:(t + 1) * SEL_CHUNKS].tolist()
+            ids = [r * pages_per_req + c * PAGES_PER_CHUNK + i for c in chosen for i in range(PAGES_PER_CHUNK)]
+            tables[t, r] = torch.tensor(ids, dtype=torch.int32)
+    total = NUM_REQ * ROWS
+    q = torch.randn(total, HQ, D, generator=g).to(torch.bfloat16)
+    k = torch.randn(total, HKV, D, generator=g).to(torch.bfloat16)
+    v = torch.randn(total, HKV, D, generator=g).to(torch.bfloat16)
+    cu = torch.arange(0, total + 1, ROWS, dtype=torch.int32)
+    seq_lens = torch.full((NUM_REQ,), CTX + ROWS, dtype=torch.int32)
+    host = dict(q=q, k=k, v=v, k_cache=k_cache, v_cache=v_cache, tables=tables, cu=cu, seq_lens=seq_lens)
+    if device.type == "cpu":
+        return host, None
+    dev = {name: t.to(device) for name, t in host.items()}
+    return host, dev
+
+
+def run_native(args, rank: int, world: int, local_rank: int):
+    from prefilling_dllm_b200 import ops
+
+    device = torch.device("cuda", local_rank)
+    torch.cuda.set_device(device)
+    host, dev = build_batch(1000 + rank, device)
+    out = torch.empty_like(dev["q"])
+    scale = 1.0 / math.sqrt(D)
+    stream = torch.cuda.current_stream(device)
+
+    def step(i: int):
+        ops.paged_attention(dev["q"], dev["k"], dev["v"], out, cu_seqlens_q=dev["cu"], max_query_len=ROWS,
+                            key_cache=dev["k_cache"], value_cache=dev["v_cache"], block_table=dev["tables"][i % N_TABLES],
+                            seq_lens=dev["seq_lens"], max_seq_len=CTX + ROWS, sm_scale=scale, bidirectional=True)
+
+    for i in range(max(3, args.warmup)):
+        step(i)
+    torch.cuda.synchronize(device)
+    ops.check_status(device)
+    # launches per step: the attention kernel, plus the split-KV merge when the plan split the keys
+    # (a split plan is the only thing that makes the op allocate its "attn" workspace)
+    launches_per_step = 2 if ("attn" in {key for (_, key) in ops._state.workspaces}) else 1
+
+    def barrier():
+        if world > 1:
+            torch.distributed.barrier()
+
+    sampler = ClockSampler(local_rank)
+    if rank == 0:
+        sampler.start()
+
+    # ---- device-resident timing (value) ----
+    barrier()
+    torch.cuda.synchronize(device)
+    start, stop = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    start.record(stream)
+    for i in range(args.steps):
+        step(i)
+    stop.record(stream)
+    torch.cuda.synchronize(device)
+    barrier()
+    ms_total = start.elapsed_time(stop)
+
+    # ---- end to end through the reference-facing op with HOST buffers (e2e) ----
+    pin = {n: host[n].pin_memory() for n in ("q", "k", "v")}
+    tables_pin = host["tables"].pin_memory()
+    out_host = torch.empty_like(host["q"]).pin_memory()
+    dq, dk, dv = torch.empty_like(dev["q"]), torch.empty_like(dev["k"]), torch.empty_like(dev["v"])
+    dtable = torch.empty_like(dev["tables"][0])
+    h2d = sum(pin[n].numel() * 2 for n in pin) + dtable.numel() * 4
+    d2h = out_host.numel() * 2
+    e2e_steps = args.steps
+
+    def e2e_step(i: int):
+        dq.copy_(pin["q"], non_blocking=True)
+        dk.copy_(pin["k"], non_blocking=True)
+        dv.copy_(pin["v"], non_blocking=True)
+        dtable.copy_(tables_pin[i % N_TABLES], non_blocking=True)
+        ops.diffusion_lm_parallel_flash_decoding(dq, dk, dv, out, "auto", dev["k_cache"], dev["v_cache"], dtable, dev["cu"],
+                                                 dev["seq_lens"], CTX + ROWS, ROWS, 1.0, 1.0, RESP_ROWS, None, None, scale,
+                                                 None, True)
+        out_host.copy_(out, non_blocking=True)
+
+    for i in range(3):
+        e2e_step(i)
+    torch.cuda.synchronize(device)
+    barrier()
+    e_start, e_stop = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e_start.record(stream)
+    for i in range(e2e_steps):
+        e2e_step(i)
+    e_stop.record(stream)
+    torch.cuda.synchronize(device)
+    barrier()
+    e2e_ms_total = e_start.elapsed_time(e_stop)
+    clocks = sampler.stop() if rank == 0 else None
+    ops.check_status(device)
+
+    if world > 1:
+        t = torch.tensor([ms_total, e2e_ms_total], dtype=torch.float64, device=device)
+        torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
+        ms_total, e2e_ms_total = float(t[0]), float(t[1])
+    if rank != 0:
+        return None
+
+    ms_per_step = ms_total / args.steps
+    tokens_per_step = world * NUM_REQ * ROWS
+    value = tokens_per_step / (ms_per_step * 1e-3)
+    e2e_value = tokens_per_step / (e2e_ms_total / e2e_steps * 1e-3)
+    peaks = load_peaks()
+    achieved_tf = FLOPS_PER_STEP / (ms_per_step * 1e-3) / 1e12
+    achieved_gb = BYTES_PER_STEP / (ms_per_step * 1e-3) / 1e9
+    traffic = None
+    traffic_path = os.path.join(ROOT, "profiles", "attn_sm100_traffic.json")
+    if os.path.exists(traffic_path):
+        with open(traffic_path) as handle:
+            traffic = json.load(handle).get("dram_bytes_per_launch")
+    line = {
+        "metric": "decode_attention_tok_per_s", "value": value, "unit": "tok/s", "n_gpus": world, "steps": args.steps,
+        "warmup": max(3, args.warmup), "ms_per_step": ms_per_step, "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+        "config": {"workload": WORKLOAD, "requests_per_gpu": NUM_REQ, "rows_per_request": ROWS, "ctx_tokens": CTX,
+                   "parallelism": f"dp{world} (replicas over requests, no data-path collective)",
+                   "l2": f"{N_TABLES} disjoint block tables rotate over a 537 MB K/V pool (> 126 MB L2) between steps"},
+        "roofline": {"bound": "tensor", "achieved": achieved_tf, "peak": peaks["tflops"], "unit": "TFLOP/s",
+                     "frac": achieved_tf / peaks["tflops"], "traffic": traffic, "peak_source": peaks["source"] + " (burst bf16 GEMM)",
+                     "flops_per_launch": FLOPS_PER_STEP, "hbm": {"achieved": achieved_gb, "peak": peaks["hbm"], "unit": "GB/s",
+                                                                "frac": achieved_gb / peaks["hbm"], "bytes_per_launch": BYTES_PER_STEP}},
+        "e2e": {"value": e2e_value, "unit": "tok/s", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
+                "ms_per_step": e2e_ms_total / e2e_steps},
+        "gpu_launches": launches_per_step * args.steps,
+        "clocks": clocks,
+    }
+    if world == 1:
+        line["cpu_baseline"] = cpu_baseline(sample_requests=2)
+    return line
+
+
+def cpu_baseline(sample_requests: int, repeats: int = 1):
+    """The CPU restatement of the reference path, timed on the host cores over a bounded sample of the batch."""
+    from oracle import hotpath as oracle
+
+    cores = os.cpu_count() or 1
+    torch.set_num_threads(cores)
+    host, _ = build_batch(1000, torch.device("cpu"))
+    rows = sample_requests * ROWS
+    args = dict(cu_seqlens_q=host["cu"][: sample_requests + 1].tolist(), k_cache=host["k_cache"], v_cache=host["v_cache"],
+                block_table=host["tables"][0][:sample_requests], seq_lens=host["seq_lens"][:sample_requests].tolist(),
+                sm_scale=1.0 / math.sqrt(D), bidirectional=True)
+    warm = dict(args, cu_seqlens_q=[0, ROWS], block_table=host["tables"][0][:1], seq_lens=[CTX + ROWS])
+    oracle.paged_attention(host["q"][:ROWS], host["k"][:ROWS], host["v"][:ROWS], **warm)  # warm-up: one request
+    t0 = time.perf_counter()
+    for _ in range(repeats):
+        oracle.paged_attention(host["q"][:rows], host["k"][:rows], host["v"][:rows], **args)
+    dt = (time.perf_counter() - t0) / repeats
+    return {"value": rows / dt, "unit": "tok/s", "cores": cores, "kind": "port",
+            "sample": f"{sample_requests} of the batch's {NUM_REQ} requests ({rows} rows), fp32 torch on CPU, {dt:.2f} s"}
+
+
+def run_reference(args, rank: int, world: int):
+    if rank != 0:
+        return None
+    steps = max(1, args.steps)
+    warm = max(0, args.warmup)
+    # every step is the same bounded sample; keep the whole run within a few minutes
+    per = 1
+    for _ in range(min(warm, 1)):
+        cpu_baseline(sample_requests=per)
+    t0 = time.perf_counter()
+    results = [cpu_baseline(sample_requests=per) for _ in range(min(steps, 5))]
+    wall = time.perf_counter() - t0
+    value = sum(r["value"] for r in results) / len(results)
+    base = results[-1]
+    base["value"] = value
+    return {
+        "impl": "reference", "metric": "decode_attention_tok_per_s", "value": value, "unit": "tok/s", "n_gpus": world,
+        "steps": len(results), "warmup": min(warm, 1), "ms_per_step": wall / len(results) * 1e3, "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+        "config": {"workload": WORKLOAD, "sample": base["sample"]},
+        "cpu_baseline": base,
+        "e2e": {"value": value, "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=200)
+    ap.add_argument("--warmup", type=int, default=10)
+    ap.add_argument("--impl", default="native", choices=["native", "reference"])
+    args = ap.parse_args()
+
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    local_rank = int(os.environ.get("LOCAL_RANK", "0"))
+
+    if args.impl == "reference":
+        line = run_reference(args, rank, world)
+        if line is not None:
+            print(json.dumps(line), flush=True)
+        return
+
+    if not torch.cuda.is_available():
+        raise SystemExit("bench.py needs a CUDA device: the product path has no CPU fallback")
+    if world > 1:
+        os.environ.setdefault("MASTER_ADDR", "127.0.0.1")
+        torch.cuda.set_device(local_rank)
+        torch.distributed.init_process_group("nccl", device_id=torch.device("cuda", local_rank))
+    try:
+        line = run_native(args, rank, world, local_rank)
+        if line is not None:
+            print(json.dumps(line), flush=True)
+    finally:
+        if world > 1:
+            torch.distributed.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

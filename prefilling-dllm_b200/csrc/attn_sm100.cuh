@@ -1,0 +1,801 @@
+// Block-table attention on the 5th-generation tensor cores (sm_100a): tcgen05.mma with TMEM accumulators,
+// operands staged by TMA straight out of the paged pool (no gather), online softmax in registers.
+//
+// Work unit (one CTA): one GQA-packed query tile x one contiguous range of 128-key tiles.
+//   * query tile  = up to 128 rows = tpt tokens x G query heads of one KV group (row = token*G + head), so the
+//     K/V pages of a KV head are read once for all G heads that share it;
+//   * key tiles   = the sequence's selected prefix pages in block-table order (any physical order), then the new
+//     rows themselves; a KV split assigns each CTA a sub-range, partials are merged by attn_combine_kernel.
+// Roles: warps 0-3 softmax + epilogue (thread r owns tile row r = TMEM lane r), warp 4 TMA producer + TMEM
+// allocator, warp 5 MMA issuer. TMEM: columns [0,128) hold S (fp32) and then P (bf16 pairs, aliased over S),
+// columns [128,256) hold O (fp32) — 256 columns so two CTAs share an SM and one CTA's softmax overlaps the
+// other's MMAs. Shared memory per CTA: Q 32 KB + K 32 KB + V 32 KB, all in the 128-byte-swizzled layouts
+// that TMA writes and the MMA descriptors read.
+// Every mbarrier wait is bounded; on expiry the CTA raises PDLLM_S_WAIT_TIMEOUT, drains and frees its TMEM.
+#pragma once
+
+#include <cuda.h>
+
+#include <mutex>
+#include <vector>
+
+#include "common.cuh"
+
+namespace pdllm {
+namespace tc {
+
+constexpr int kTileM = 128;
+constexpr int kTileN = 128;
+constexpr int kHeadDim = 128;
+constexpr int kThreads = 192;
+constexpr uint32_t kTmemCols = 256;
+constexpr uint32_t kColS = 0;
+constexpr uint32_t kColO = 128;
+constexpr int kHalfBytes = kTileN * 64 * 2;        // one [128 rows x 64 elems] swizzled sub-tile = 16 KB
+constexpr int kTileBytes = 2 * kHalfBytes;         // 32 KB
+constexpr int kSmemQ = 0;
+constexpr int kSmemK = kTileBytes;
+constexpr int kSmemV = 2 * kTileBytes;
+constexpr int kSmemBar = 3 * kTileBytes;
+constexpr int kSmemBytes = 3 * kTileBytes + 256 + 1024;  // + barriers + slack to align the base to 1024 B
+constexpr long long kWaitLimitCycles = 1ll << 31;  // about a second
+constexpr float kRescaleThreshold = 8.0f;          // log2 units: rescale O only when the row max grew by > 2^8
+
+enum Bar { kQFull = 0, kKFull, kKEmpty, kVFull, kVEmpty, kSFull, kPFull, kPvDone, kNumBars };
+
+struct Args {
+  void* out;
+  const int32_t* block_table; const int32_t* cu_seqlens_q; const int32_t* seq_lens;
+  const uint8_t* mask; int32_t* status;
+  float* part_o; float* part_ml;   // split-KV partials: O as [unit][D][128], (m, l) as [unit][2][128]
+  int64_t out_stride, block_table_stride, mask_stride_m, mask_stride_n, num_pages;
+  int num_seqs, max_pages, num_q_heads, num_kv_heads, group, tpt, q_tiles, num_splits;
+  int page_size, has_cache, mask_mode, bidirectional, block_m, is_bf16;
+  float scale_log2;  // sm_scale * log2(e)
+};
+
+// ---- PTX wrappers ---------------------------------------------------------------------------------------
+__device__ __forceinline__ uint32_t smem_u32(const void* p) { return static_cast<uint32_t>(__cvta_generic_to_shared(p)); }
+
+__device__ __forceinline__ void mbar_init(uint64_t* bar, uint32_t count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count) : "memory");
+}
+__device__ __forceinline__ void mbar_expect_tx(uint64_t* bar, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)), "r"(bytes) : "memory");
+}
+__device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
+}
+__device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.b32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok) : "r"(smem_u32(bar)), "r"(parity) : "memory");
+  return ok != 0;
+}
+// Bounded wait. Returns false when another role already gave up or when the limit expired.
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volatile int* abort_flag, int32_t* status) {
+  if (mbar_try_wait(bar, parity)) return true;
+  long long t0 = clock64();
+  uint32_t spins = 0;
+  while (!mbar_try_wait(bar, parity)) {
+    if (((++spins) & 0x3f) == 0) {
+      if (*abort_flag) return false;
+      if (clock64() - t0 > kWaitLimitCycles) {
+        *abort_flag = 1;
+        report_status(status, PDLLM_S_WAIT_TIMEOUT);
+        return false;
+      }
+    }
+  }
+  return true;
+}
+
+__device__ __forceinline__ void fence_barrier_init() { asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory"); }
+__device__ __forceinline__ void fence_proxy_async() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
+__device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
+__device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
+__device__ __forceinline__ void tc_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
+__device__ __forceinline__ void tc_wait_st() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
+
+__device__ __forceinline__ void tma_load_3d(const CUtensorMap* map, uint64_t* bar, void* dst, int c0, int c1, int c2) {
+  asm volatile(
+      "cp.async.bulk.tensor.3d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%3, %4, %5}], [%2];"
+      ::"r"(smem_u32(dst)), "l"(reinterpret_cast<uint64_t>(map)), "r"(smem_u32(bar)), "r"(c0), "r"(c1), "r"(c2)
+      : "memory");
+}
+__device__ __forceinline__ void tma_load_4d(const CUtensorMap* map, uint64_t* bar, void* dst, int c0, int c1, int c2, int c3) {
+  asm volatile(
+      "cp.async.bulk.tensor.4d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%3, %4, %5, %6}], [%2];"
+      ::"r"(smem_u32(dst)), "l"(reinterpret_cast<uint64_t>(map)), "r"(smem_u32(bar)), "r"(c0), "r"(c1), "r"(c2), "r"(c3)
+      : "memory");
+}
+
+__device__ __forceinline__ void tmem_alloc(uint32_t* dst_smem, uint32_t cols) {
+  asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(dst_smem)), "r"(cols) : "memory");
+  asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+}
+__device__ __forceinline__ void tmem_dealloc(uint32_t taddr, uint32_t cols) {
+  asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(cols) : "memory");
+}
+
+// D[tmem] (+)= A[smem] * B[smem]
+__device__ __forceinline__ void umma_ss(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc, uint32_t idesc, uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}"
+      ::"r"(d_tmem), "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate) : "memory");
+}
+// D[tmem] (+)= A[tmem] * B[smem]
+__device__ __forceinline__ void umma_ts(uint32_t d_tmem, uint32_t a_tmem, uint64_t b_desc, uint32_t idesc, uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n\t}"
+      ::"r"(d_tmem), "r"(a_tmem), "l"(b_desc), "r"(idesc), "r"(accumulate) : "memory");
+}
+// mbarrier arrives once every tcgen05 operation issued so far by this thread has completed
+__device__ __forceinline__ void umma_commit(uint64_t* bar) {
+  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_u32(bar)) : "memory");
+}
+
+#define PDLLM_R32(a, o) \
+  "=r"(a[o + 0]), "=r"(a[o + 1]), "=r"(a[o + 2]), "=r"(a[o + 3]), "=r"(a[o + 4]), "=r"(a[o + 5]), "=r"(a[o + 6]), "=r"(a[o + 7]), \
+  "=r"(a[o + 8]), "=r"(a[o + 9]), "=r"(a[o + 10]), "=r"(a[o + 11]), "=r"(a[o + 12]), "=r"(a[o + 13]), "=r"(a[o + 14]), "=r"(a[o + 15])
+#define PDLLM_W16(a, o) \
+  "r"(a[o + 0]), "r"(a[o + 1]), "r"(a[o + 2]), "r"(a[o + 3]), "r"(a[o + 4]), "r"(a[o + 5]), "r"(a[o + 6]), "r"(a[o + 7]), \
+  "r"(a[o + 8]), "r"(a[o + 9]), "r"(a[o + 10]), "r"(a[o + 11]), "r"(a[o + 12]), "r"(a[o + 13]), "r"(a[o + 14]), "r"(a[o + 15])
+
+// 32 lanes x 32 consecutive 32-bit columns: thread t reads lane (base + t), registers = columns
+__device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t* r) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x32.b32 "
+      "{%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15, "
+      "%16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31}, [%32];"
+      : PDLLM_R32(r, 0), PDLLM_R32(r, 16)
+      : "r"(taddr));
+}
+__device__ __forceinline__ void tmem_st32(uint32_t taddr, const uint32_t* r) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], "
+      "{%1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15, %16, "
+      "%17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31, %32};"
+      ::"r"(taddr), PDLLM_W16(r, 0), PDLLM_W16(r, 16)
+      : "memory");
+}
+__device__ __forceinline__ void tmem_st16(uint32_t taddr, const uint32_t* r) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], "
+      "{%1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15, %16};"
+      ::"r"(taddr), PDLLM_W16(r, 0)
+      : "memory");
+}
+
+__device__ __forceinline__ float ex2(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+
+// ---- shared-memory matrix descriptors (version 1 = Blackwell, 128-byte swizzle) -----------------------------
+// K-major operand: rows of 64 elements (128 B), 8-row swizzle atoms stacked 1024 B apart.
+__device__ __forceinline__ uint64_t desc_kmajor_sw128(uint32_t saddr) {
+  return static_cast<uint64_t>((saddr & 0x3FFFFu) >> 4) | (1ull << 16) | (64ull << 32) | (1ull << 46) | (2ull << 61);
+}
+// MN-major operand (V as B of P*V): 64 contiguous N elements per row, 8 K-rows per atom (1024 B apart along K),
+// second 64-element N group `lbo_bytes` away.
+__device__ __forceinline__ uint64_t desc_mnmajor_sw128(uint32_t saddr, uint32_t lbo_bytes) {
+  return static_cast<uint64_t>((saddr & 0x3FFFFu) >> 4) | (static_cast<uint64_t>(lbo_bytes >> 4) << 16) | (64ull << 32) |
+         (1ull << 46) | (2ull << 61);
+}
+// instruction descriptor, kind::f16: fp32 accumulate, A/B bf16 (1) or fp16 (0), M=128, N=128
+__host__ __device__ constexpr uint32_t make_idesc(bool bf16, bool b_mn_major) {
+  return (1u << 4) | ((bf16 ? 1u : 0u) << 7) | ((bf16 ? 1u : 0u) << 10) | ((b_mn_major ? 1u : 0u) << 16) |
+         ((kTileN >> 3) << 17) | ((kTileM >> 4) << 24);
+}
+
+struct TileInfo {
+  bool is_ctx;
+  int key0;    // first key of the tile: context position, or new-row index
+  int nvalid;  // keys of the tile that exist (<= 128)
+};
+
+__device__ __forceinline__ TileInfo tile_info(int t, int n_ctx_tiles, int ctx_len, int new_end) {
+  TileInfo ti;
+  ti.is_ctx = t < n_ctx_tiles;
+  if (ti.is_ctx) {
+    ti.key0 = t * kTileN;
+    ti.nvalid = min(kTileN, ctx_len - ti.key0);
+  } else {
+    ti.key0 = (t - n_ctx_tiles) * kTileN;
+    ti.nvalid = min(kTileN, new_end - ti.key0);
+  }
+  return ti;
+}
+
+__global__ void __launch_bounds__(kThreads, 2)
+attn_sm100_kernel(const __grid_constant__ CUtensorMap q_map, const __grid_constant__ CUtensorMap kn_map,
+                  const __grid_constant__ CUtensorMap vn_map, const __grid_constant__ CUtensorMap kc_map,
+                  const __grid_constant__ CUtensorMap vc_map, const Args a) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + kSmemBar);
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + kSmemBar + 128);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + kSmemBar + 136);
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+
+  // ---- decode the work unit ----
+  int u = blockIdx.x;
+  const int split = u % a.num_splits; u /= a.num_splits;
+  const int qt = u % a.q_tiles; u /= a.q_tiles;
+  const int kvh = u % a.num_kv_heads;
+  const int seq = u / a.num_kv_heads;
+  const int unit = blockIdx.x;
+
+  const int q_start = a.cu_seqlens_q[seq];
+  const int q_len = a.cu_seqlens_q[seq + 1] - q_start;
+  int ctx_len = a.has_cache ? (a.seq_lens[seq] - q_len) : 0;
+  if (ctx_len < 0) ctx_len = 0;
+  const int tok0 = qt * a.tpt;
+  const int n_tok = min(a.tpt, q_len - tok0);
+  const int G = a.group;
+
+  // keys among the new rows that any row of this tile may see
+  int new_end = q_len;
+  if (n_tok > 0) {
+    const int last_m = tok0 + n_tok - 1;
+    if (a.mask_mode == PDLLM_MASK_CAUSAL) new_end = min(q_len, last_m + 1);
+    else if (!a.bidirectional) new_end = min(q_len, (last_m / a.block_m + 1) * a.block_m);
+  }
+  const int n_ctx_tiles = (ctx_len + kTileN - 1) / kTileN;
+  const int n_new_tiles = (new_end + kTileN - 1) / kTileN;
+  const int total_tiles = n_ctx_tiles + n_new_tiles;
+  const int per_split = (total_tiles + a.num_splits - 1) / a.num_splits;
+  const int t_begin = split * per_split;
+  const int t_end = min(total_tiles, t_begin + per_split);
+  const int n_iter = t_end - t_begin;
+
+  if (n_tok <= 0 || n_iter <= 0) {
+    // Nothing to attend in this unit: publish a neutral partial so the merge ignores it.
+    if (a.num_splits > 1 && threadIdx.x < kTileM) {
+      a.part_ml[(static_cast<int64_t>(unit) * 2 + 0) * kTileM + threadIdx.x] = -INFINITY;
+      a.part_ml[(static_cast<int64_t>(unit) * 2 + 1) * kTileM + threadIdx.x] = 0.f;
+    }
+    return;
+  }
+
+  // ---- set-up: barriers, TMEM ----
+  if (warp == 4) {
+    if (lane == 0) {
+      for (int i = 0; i < kNumBars; ++i) mbar_init(&bars[i], i == kPFull ? 128u : 1u);
+      abort_flag[0] = 0;
+      abort_flag[1] = 0;  // never set: lets the producer's drain waits run although abort_flag[0] is up
+      fence_barrier_init();
+    }
+    __syncwarp();
+    tmem_alloc(tmem_slot, kTmemCols);
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+
+  const uint32_t idesc_qk = make_idesc(a.is_bf16 != 0, false);
+  const uint32_t idesc_pv = make_idesc(a.is_bf16 != 0, true);
+
+  if (warp == 4) {
+    // =========================== TMA producer ===========================
+    if (lane == 0) {
+      const uint32_t q_bytes = 2u * 64u * 2u * static_cast<uint32_t>(G * a.tpt);
+      mbar_expect_tx(&bars[kQFull], q_bytes);
+      tma_load_3d(&q_map, &bars[kQFull], smem + kSmemQ, 0, kvh * G, q_start + tok0);
+      tma_load_3d(&q_map, &bars[kQFull], smem + kSmemQ + kHalfBytes, 64, kvh * G, q_start + tok0);
+      bool ok = true;
+      int issued = 0;
+      for (int it = 0; it < n_iter && ok; ++it) {
+        const uint32_t ph = it & 1;
+        const TileInfo ti = tile_info(t_begin + it, n_ctx_tiles, ctx_len, new_end);
+        int page = 0, off = 0;
+        if (ti.is_ctx) {
+          const int pidx = ti.key0 / a.page_size;
+          off = ti.key0 - pidx * a.page_size;
+          page = (pidx < a.max_pages) ? a.block_table[seq * a.block_table_stride + pidx] : -1;
+          if (page < 0 || page >= a.num_pages) {
+            report_status(a.status, PDLLM_S_BAD_PAGE);
+            page = 0;  // keep the copy in bounds; the softmax warps see the same bad id and mask the tile
+          }
+        }
+        ok = mbar_wait(&bars[kKEmpty], ph ^ 1, abort_flag, a.status);
+        if (!ok) break;
+        mbar_expect_tx(&bars[kKFull], kTileBytes);
+        if (ti.is_ctx) {
+          tma_load_4d(&kc_map, &bars[kKFull], smem + kSmemK, 0, kvh, off, page);
+          tma_load_4d(&kc_map, &bars[kKFull], smem + kSmemK + kHalfBytes, 64, kvh, off, page);
+        } else {
+          tma_load_3d(&kn_map, &bars[kKFull], smem + kSmemK, 0, kvh, q_start + ti.key0);
+          tma_load_3d(&kn_map, &bars[kKFull], smem + kSmemK + kHalfBytes, 64, kvh, q_start + ti.key0);
+        }
+        ok = mbar_wait(&bars[kVEmpty], ph ^ 1, abort_flag, a.status);
+        if (!ok) { issued = it * 2 + 1; break; }
+        mbar_expect_tx(&bars[kVFull], kTileBytes);
+        if (ti.is_ctx) {
+          tma_load_4d(&vc_map, &bars[kVFull], smem + kSmemV, 0, kvh, off, page);
+          tma_load_4d(&vc_map, &bars[kVFull], smem + kSmemV + kHalfBytes, 64, kvh, off, page);
+        } else {
+          tma_load_3d(&vn_map, &bars[kVFull], smem + kSmemV, 0, kvh, q_start + ti.key0);
+          tma_load_3d(&vn_map, &bars[kVFull], smem + kSmemV + kHalfBytes, 64, kvh, q_start + ti.key0);
+        }
+        issued = it * 2 + 2;
+      }
+      if (!ok && issued > 0) {
+        // Gave up mid-way: let the copies already in flight land before the CTA retires.
+        const int it_k = (issued - 1) / 2;
+        (void)mbar_wait(&bars[kKFull], it_k & 1, abort_flag + 1, nullptr);
+        if ((issued & 1) == 0) (void)mbar_wait(&bars[kVFull], it_k & 1, abort_flag + 1, nullptr);
+      }
+    }
+    __syncwarp();
+  } else if (warp == 5) {
+    // =========================== MMA issuer ===========================
+    const uint32_t sq = smem_u32(smem + kSmemQ), sk = smem_u32(smem + kSmemK), sv = smem_u32(smem + kSmemV);
+    const uint32_t tS = tmem_base + kColS, tO = tmem_base + kColO;
+    bool ok = mbar_wait(&bars[kQFull], 0, abort_flag, a.status);
+    for (int it = 0; it < n_iter && ok; ++it) {
+      const uint32_t ph = it & 1;
+      const TileInfo ti = tile_info(t_begin + it, n_ctx_tiles, ctx_len, new_end);
+      ok = mbar_wait(&bars[kKFull], ph, abort_flag, a.status);
+      if (ok && it > 0) ok = mbar_wait(&bars[kPvDone], (it - 1) & 1, abort_flag, a.status);  // S/P columns free again
+      if (!ok) break;
+      tc_fence_after();
+      if (lane == 0) {
+#pragma unroll
+        for (int kk = 0; kk < kHeadDim / 16; ++kk) {
+          const uint32_t koff = (kk >> 2) * kHalfBytes + (kk & 3) * 32;
+          umma_ss(tS, desc_kmajor_sw128(sq + koff), desc_kmajor_sw128(sk + koff), idesc_qk, kk > 0 ? 1u : 0u);
+        }
+        umma_commit(&bars[kSFull]);
+        umma_commit(&bars[kKEmpty]);
+      }
+      __syncwarp();
+      ok = mbar_wait(&bars[kVFull], ph, abort_flag, a.status);
+      if (!ok) break;
+      if (ti.nvalid < kTileN) {
+        // Rows of the V tile past the last valid key may hold anything (stale page contents, another
+        // sequence's rows); P is 0 there but 0 * NaN is NaN, so clear them before the MMA reads the tile.
+        const int n_rows = kTileN - ti.nvalid;
+        for (int i = lane; i < n_rows * 16; i += 32) {
+          const int r = ti.nvalid + (i >> 4);
+          const int c = i & 15;
+          uint4* dst = reinterpret_cast<uint4*>(smem + kSmemV + (c >> 3) * kHalfBytes + r * 128 + (c & 7) * 16);
+          *dst = make_uint4(0, 0, 0, 0);
+        }
+        fence_proxy_async();
+        __syncwarp();
+      }
+      ok = mbar_wait(&bars[kPFull], ph, abort_flag, a.status);
+      if (!ok) break;
+      tc_fence_after();
+      if (lane == 0) {
+#pragma unroll
+        for (int kk = 0; kk < kTileN / 16; ++kk) {
+          umma_ts(tO, tS + kk * 8, desc_mnmajor_sw128(sv + kk * 2048, kHalfBytes), idesc_pv, (it > 0 || kk > 0) ? 1u : 0u);
+        }
+        umma_commit(&bars[kPvDone]);
+        umma_commit(&bars[kVEmpty]);
+      }
+      __syncwarp();
+    }
+  } else {
+    // =========================== softmax + epilogue (warps 0-3) ===========================
+    const int r = threadIdx.x;                 // tile row == TMEM lane
+    const uint32_t lane_base = static_cast<uint32_t>(warp * 32) << 16;
+    const uint32_t tS = tmem_base + lane_base + kColS;
+    const uint32_t tO = tmem_base + lane_base + kColO;
+    const int tok_local = r / G;               // token of this row inside the tile
+    const int head_local = r - tok_local * G;
+    const bool row_valid = tok_local < n_tok;
+    const int m = tok0 + tok_local;            // sequence-local new-row index
+    // last visible new key (exclusive) for this row
+    int row_new_end = q_len;
+    if (a.mask_mode == PDLLM_MASK_CAUSAL) row_new_end = min(q_len, m + 1);
+    else if (!a.bidirectional) row_new_end = min(q_len, (m / a.block_m + 1) * a.block_m);
+    const bool dense_mask = (a.mask != nullptr) && (a.mask_mode == PDLLM_MASK_BLOCK);
+
+    float m_ref = -INFINITY;  // running reference maximum, log2 domain
+    float l_run = 0.f;
+    bool ok = true;
+    uint32_t v[32];
+
+    for (int it = 0; it < n_iter; ++it) {
+      const uint32_t ph = it & 1;
+      const TileInfo ti = tile_info(t_begin + it, n_ctx_tiles, ctx_len, new_end);
+      int cmax = ti.nvalid;  // columns [0, cmax) are visible to this row
+      if (ti.is_ctx) {
+        const int pidx = ti.key0 / a.page_size;
+        const int page = (pidx < a.max_pages) ? a.block_table[seq * a.block_table_stride + pidx] : -1;
+        if (page < 0 || page >= a.num_pages) cmax = 0;
+      } else {
+        cmax = min(cmax, row_new_end - ti.key0);
+      }
+      const bool use_dense = dense_mask && !ti.is_ctx && row_valid;
+      const bool need_mask = (cmax < kTileN) || use_dense;
+      const uint8_t* mrow = use_dense ? a.mask + static_cast<int64_t>(m) * a.mask_stride_m + static_cast<int64_t>(ti.key0) * a.mask_stride_n : nullptr;
+
+      ok = mbar_wait(&bars[kSFull], ph, abort_flag, a.status);
+      if (!ok) break;
+      tc_fence_after();
+
+      // pass 1: row maximum of the visible scores
+      float mx = -INFINITY;
+#pragma unroll 1
+      for (int c = 0; c < 4; ++c) {
+        tmem_ld32(tS + c * 32, v);
+        tc_wait_ld();
+        if (!need_mask) {
+#pragma unroll
+          for (int j = 0; j < 32; ++j) mx = fmaxf(mx, __uint_as_float(v[j]));
+        } else {
+#pragma unroll
+          for (int j = 0; j < 32; ++j) {
+            const int col = c * 32 + j;
+            bool vis = col < cmax;
+            if (vis && use_dense) vis = mrow[col * a.mask_stride_n] != 0;
+            if (vis) mx = fmaxf(mx, __uint_as_float(v[j]));
+          }
+        }
+      }
+      const float m_tile = mx * a.scale_log2;  // scale > 0, so max commutes with the scaling
+
+      // lazy rescale: only when the maximum grew by more than 2^8 (or on the first tile that sets it)
+      if (it == 0) {
+        m_ref = m_tile;
+      } else {
+        const bool grow = m_tile > m_ref + kRescaleThreshold;
+        if (__any_sync(0xffffffffu, grow)) {
+          const float m_new = grow ? m_tile : m_ref;
+          const float alpha = grow ? ex2(m_ref - m_new) : 1.f;  // m_ref = -inf gives 0
+          l_run *= alpha;
+#pragma unroll 1
+          for (int c = 0; c < 4; ++c) {
+            tmem_ld32(tO + c * 32, v);
+            tc_wait_ld();
+#pragma unroll
+            for (int j = 0; j < 32; ++j) v[j] = __float_as_uint(__uint_as_float(v[j]) * alpha);
+            tmem_st32(tO + c * 32, v);
+          }
+          tc_wait_st();
+          m_ref = m_new;
+        }
+      }
+      const float m_use = (m_ref == -INFINITY) ? 0.f : m_ref;
+
+      // pass 2: P = exp2(S*scale - m_ref) → bf16/fp16 pairs, written over the S columns already consumed
+#pragma unroll 1
+      for (int c = 0; c < 4; ++c) {
+        tmem_ld32(tS + c * 32, v);
+        tc_wait_ld();
+        uint32_t packed[16];
+#pragma unroll
+        for (int j = 0; j < 32; j += 2) {
+          float p0 = ex2(fmaf(__uint_as_float(v[j]), a.scale_log2, -m_use));
+          float p1 = ex2(fmaf(__uint_as_float(v[j + 1]), a.scale_log2, -m_use));
+          if (need_mask) {
+            const int col = c * 32 + j;
+            bool vis0 = col < cmax, vis1 = (col + 1) < cmax;
+            if (use_dense) {
+              if (vis0) vis0 = mrow[col * a.mask_stride_n] != 0;
+              if (vis1) vis1 = mrow[(col + 1) * a.mask_stride_n] != 0;
+            }
+            if (!vis0) p0 = 0.f;
+            if (!vis1) p1 = 0.f;
+          }
+          l_run += p0 + p1;
+          if (a.is_bf16) {
+            __nv_bfloat162 h = __floats2bfloat162_rn(p0, p1);
+            packed[j >> 1] = *reinterpret_cast<uint32_t*>(&h);
+          } else {
+            __half2 h = __floats2half2_rn(p0, p1);
+            packed[j >> 1] = *reinterpret_cast<uint32_t*>(&h);
+          }
+        }
+        tmem_st16(tS + c * 16, packed);
+      }
+      tc_wait_st();
+      tc_fence_before();
+      mbar_arrive(&bars[kPFull]);
+    }
+
+    // ---- epilogue ----
+    if (ok) ok = mbar_wait(&bars[kPvDone], (n_iter - 1) & 1, abort_flag, a.status);
+    if (ok) {
+      tc_fence_after();
+      if (a.num_splits == 1) {
+        const float inv = (l_run > 0.f) ? 1.f / l_run : 0.f;
+        uint8_t* out_row = reinterpret_cast<uint8_t*>(a.out) +
+                           ((static_cast<int64_t>(q_start + m)) * a.out_stride + static_cast<int64_t>(kvh * G + head_local) * kHeadDim) * 2;
+#pragma unroll 1
+        for (int c = 0; c < 4; ++c) {
+          tmem_ld32(tO + c * 32, v);
+          tc_wait_ld();
+          if (row_valid) {
+            uint32_t packed[16];
+#pragma unroll
+            for (int j = 0; j < 32; j += 2) {
+              const float o0 = __uint_as_float(v[j]) * inv, o1 = __uint_as_float(v[j + 1]) * inv;
+              if (a.is_bf16) {
+                __nv_bfloat162 h = __floats2bfloat162_rn(o0, o1);
+                packed[j >> 1] = *reinterpret_cast<uint32_t*>(&h);
+              } else {
+                __half2 h = __floats2half2_rn(o0, o1);
+                packed[j >> 1] = *reinterpret_cast<uint32_t*>(&h);
+              }
+            }
+            uint4* dst = reinterpret_cast<uint4*>(out_row + c * 64);
+#pragma unroll
+            for (int j = 0; j < 4; ++j) dst[j] = make_uint4(packed[4 * j], packed[4 * j + 1], packed[4 * j + 2], packed[4 * j + 3]);
+          }
+        }
+      } else {
+        float* po = a.part_o + static_cast<int64_t>(unit) * kHeadDim * kTileM;
+#pragma unroll 1
+        for (int c = 0; c < 4; ++c) {
+          tmem_ld32(tO + c * 32, v);
+          tc_wait_ld();
+#pragma unroll
+          for (int j = 0; j < 32; ++j) po[static_cast<int64_t>(c * 32 + j) * kTileM + r] = __uint_as_float(v[j]);
+        }
+        a.part_ml[(static_cast<int64_t>(unit) * 2 + 0) * kTileM + r] = m_ref;
+        a.part_ml[(static_cast<int64_t>(unit) * 2 + 1) * kTileM + r] = l_run;
+      }
+    }
+  }
+
+  // ---- teardown ----
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 4) {
+    tc_fence_after();
+    tmem_dealloc(tmem_base, kTmemCols);
+  }
+}
+
+// Merge of the split-KV partials. One thread per (unit-row, 4 output columns).
+// out[row] = sum_s 2^(m_s - M) O_s / sum_s 2^(m_s - M) l_s.
+__global__ void attn_combine_kernel(const Args a) {
+  const int64_t tile = blockIdx.x;  // (seq, kvh, qt)
+  int u = static_cast<int>(tile);
+  const int qt = u % a.q_tiles; u /= a.q_tiles;
+  const int kvh = u % a.num_kv_heads;
+  const int seq = u / a.num_kv_heads;
+  const int q_start = a.cu_seqlens_q[seq];
+  const int q_len = a.cu_seqlens_q[seq + 1] - q_start;
+  const int tok0 = qt * a.tpt;
+  const int n_tok = min(a.tpt, q_len - tok0);
+  if (n_tok <= 0) return;
+  const int G = a.group;
+  const int r = threadIdx.x & (kTileM - 1);   // row: consecutive threads read consecutive partial addresses
+  const int dq = threadIdx.x / kTileM;        // which quarter of the 128 columns
+  const int tok_local = r / G;
+  if (tok_local >= n_tok) return;
+  const int head_local = r - tok_local * G;
+  const int64_t unit0 = tile * a.num_splits;
+
+  float M = -INFINITY;
+  for (int s = 0; s < a.num_splits; ++s) M = fmaxf(M, a.part_ml[((unit0 + s) * 2 + 0) * kTileM + r]);
+  float wsum = 0.f;
+  float w[32];
+  for (int s = 0; s < a.num_splits && s < 32; ++s) {
+    const float ms = a.part_ml[((unit0 + s) * 2 + 0) * kTileM + r];
+    const float ls = a.part_ml[((unit0 + s) * 2 + 1) * kTileM + r];
+    w[s] = (ms == -INFINITY) ? 0.f : exp2f(ms - M);
+    wsum += w[s] * ls;
+  }
+  const float inv = wsum > 0.f ? 1.f / wsum : 0.f;
+  uint8_t* out_row = reinterpret_cast<uint8_t*>(a.out) +
+                     ((static_cast<int64_t>(q_start + tok0 + tok_local)) * a.out_stride + static_cast<int64_t>(kvh * G + head_local) * kHeadDim) * 2;
+  for (int d0 = dq * 32; d0 < dq * 32 + 32; d0 += 8) {
+    float acc[8];
+#pragma unroll
+    for (int j = 0; j < 8; ++j) acc[j] = 0.f;
+    for (int s = 0; s < a.num_splits && s < 32; ++s) {
+      if (w[s] == 0.f) continue;
+      const float* po = a.part_o + (unit0 + s) * kHeadDim * kTileM;
+#pragma unroll
+      for (int j = 0; j < 8; ++j) acc[j] = fmaf(w[s], po[static_cast<int64_t>(d0 + j) * kTileM + r], acc[j]);
+    }
+    uint32_t packed[4];
+#pragma unroll
+    for (int j = 0; j < 8; j += 2) {
+      if (a.is_bf16) {
+        __nv_bfloat162 h = __floats2bfloat162_rn(acc[j] * inv, acc[j + 1] * inv);
+        packed[j >> 1] = *reinterpret_cast<uint32_t*>(&h);
+      } else {
+        __half2 h = __floats2half2_rn(acc[j] * inv, acc[j + 1] * inv);
+        packed[j >> 1] = *reinterpret_cast<uint32_t*>(&h);
+      }
+    }
+    *reinterpret_cast<uint4*>(out_row + d0 * 2) = make_uint4(packed[0], packed[1], packed[2], packed[3]);
+  }
+}
+
+// ---- host side: tensor maps, split choice, launch ---------------------------------------------------------
+typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*, const cuuint64_t*,
+                                  const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave, CUtensorMapSwizzle,
+                                  CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+inline EncodeTiledFn encode_fn() {
+  static EncodeTiledFn fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult qres;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &qres) == cudaSuccess &&
+        qres == cudaDriverEntryPointSuccess) {
+      fn = reinterpret_cast<EncodeTiledFn>(p);
+    }
+  });
+  return fn;
+}
+
+// rank-3 or rank-4 map over 2-byte elements, 128-byte swizzle, zero fill outside the tensor
+inline int encode_map(CUtensorMap* map, bool bf16, const void* base, int rank, const uint64_t* dims,
+                      const uint64_t* strides_bytes /* rank-1 entries */, const uint32_t* box) {
+  EncodeTiledFn fn = encode_fn();
+  if (fn == nullptr) return fail(PDLLM_E_DRIVER, "cuTensorMapEncodeTiled entry point not available");
+  cuuint64_t gdim[5]; cuuint64_t gstr[4]; cuuint32_t bdim[5]; cuuint32_t estr[5];
+  for (int i = 0; i < rank; ++i) { gdim[i] = dims[i]; bdim[i] = box[i]; estr[i] = 1; }
+  for (int i = 0; i < rank - 1; ++i) gstr[i] = strides_bytes[i];
+  CUresult r = fn(map, bf16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16, rank,
+                  const_cast<void*>(base), gdim, gstr, bdim, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                  CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return fail(PDLLM_E_DRIVER, "cuTensorMapEncodeTiled failed with CUresult %d", static_cast<int>(r));
+  return 0;
+}
+
+inline bool supported(const pdllm_attn_params* p, const char** why) {
+  const char* w = nullptr;
+  if (p->dtype != PDLLM_BF16 && p->dtype != PDLLM_F16) w = "dtype must be bf16 or fp16";
+  else if (p->head_dim != kHeadDim) w = "head_dim must be 128";
+  else if (p->num_q_heads % p->num_kv_heads != 0) w = "query heads must be a multiple of KV heads";
+  else if (p->num_q_heads / p->num_kv_heads > kTileM) w = "GQA group larger than 128";
+  else if (p->kv_layout == PDLLM_KV_DISTINCT) w = "distinct cache layout runs on the SIMT kernel";
+  else if (p->kv_layout == PDLLM_KV_UNIFIED && (p->page_size % kTileN != 0)) w = "page_size must be a multiple of 128";
+  else if (p->kv_layout == PDLLM_KV_UNIFIED && p->page_size > 256 * kTileN) w = "page_size too large";
+  else if ((reinterpret_cast<uintptr_t>(p->q) | reinterpret_cast<uintptr_t>(p->k_new) | reinterpret_cast<uintptr_t>(p->v_new) |
+            reinterpret_cast<uintptr_t>(p->out) | reinterpret_cast<uintptr_t>(p->k_cache) | reinterpret_cast<uintptr_t>(p->v_cache)) & 15) w = "pointers must be 16-byte aligned";
+  else if ((p->q_stride | p->k_stride | p->v_stride | p->out_stride) % 8 != 0) w = "row strides must be multiples of 8 elements";
+  else if (p->total_q >= (1ll << 31) || p->num_pages >= (1ll << 31)) w = "extent exceeds the tensor-map coordinate range";
+  if (why) *why = w;
+  return w == nullptr;
+}
+
+struct Plan {
+  int group, tpt, q_tiles, num_splits;
+  int64_t tiles, units;
+};
+
+inline Plan make_plan(const pdllm_attn_params* p) {
+  Plan pl;
+  pl.group = p->num_q_heads / p->num_kv_heads;
+  pl.tpt = kTileM / pl.group;
+  pl.q_tiles = (p->max_query_len + pl.tpt - 1) / pl.tpt;
+  if (pl.q_tiles < 1) pl.q_tiles = 1;
+  pl.tiles = static_cast<int64_t>(p->num_seqs) * p->num_kv_heads * pl.q_tiles;
+  int max_key_tiles = (p->max_seq_len + kTileN - 1) / kTileN + 1;
+  int splits = p->num_splits;
+  if (splits <= 0) {
+    // Fill a whole number of waves of 2 CTAs per SM; each split keeps at least two key tiles.
+    const int64_t slots = 2ll * sm_count();
+    int cap = max_key_tiles / 2; if (cap < 1) cap = 1; if (cap > 32) cap = 32;
+    double best_eff = -1.0; splits = 1;
+    for (int s = 1; s <= cap; ++s) {
+      const int64_t n = pl.tiles * s;
+      const int64_t waves = (n + slots - 1) / slots;
+      const double eff = static_cast<double>(n) / static_cast<double>(waves * slots);
+      if (eff > best_eff + 0.03) { best_eff = eff; splits = s; }
+      if (eff >= 0.9) break;
+    }
+  }
+  if (splits > 32) splits = 32;
+  if (splits > max_key_tiles) splits = max_key_tiles;
+  if (splits < 1) splits = 1;
+  pl.num_splits = splits;
+  pl.units = pl.tiles * splits;
+  return pl;
+}
+
+inline int64_t workspace_bytes(const pdllm_attn_params* p) {
+  Plan pl = make_plan(p);
+  if (pl.num_splits <= 1) return 0;
+  return pl.units * (static_cast<int64_t>(kHeadDim) * kTileM + 2 * kTileM) * 4;
+}
+
+inline int launch(const pdllm_attn_params* p, cudaStream_t stream) {
+  const char* why = nullptr;
+  if (!supported(p, &why)) return fail(PDLLM_E_UNSUPPORTED, "tcgen05 attention: %s", why);
+  if (p->total_q == 0 || p->num_seqs == 0) return 0;
+  const Plan pl = make_plan(p);
+  const bool bf16 = p->dtype == PDLLM_BF16;
+  const bool has_cache = p->kv_layout == PDLLM_KV_UNIFIED && p->k_cache != nullptr && p->num_pages > 0;
+
+  if (pl.num_splits > 1) {
+    const int64_t need = workspace_bytes(p);
+    if (p->workspace == nullptr || p->workspace_bytes < need) {
+      return fail(PDLLM_E_WORKSPACE, "attention needs %lld workspace bytes for %d KV splits, got %lld",
+                  static_cast<long long>(need), pl.num_splits, static_cast<long long>(p->workspace_bytes));
+    }
+  }
+
+  CUtensorMap q_map, kn_map, vn_map, kc_map, vc_map;
+  int rc;
+  {
+    uint64_t dims[3] = {static_cast<uint64_t>(kHeadDim), static_cast<uint64_t>(p->num_q_heads), static_cast<uint64_t>(p->total_q)};
+    uint64_t str[2] = {static_cast<uint64_t>(kHeadDim) * 2, static_cast<uint64_t>(p->q_stride) * 2};
+    uint32_t box[3] = {64, static_cast<uint32_t>(pl.group), static_cast<uint32_t>(pl.tpt)};
+    if ((rc = encode_map(&q_map, bf16, p->q, 3, dims, str, box)) != 0) return rc;
+  }
+  {
+    uint64_t dims[3] = {static_cast<uint64_t>(kHeadDim), static_cast<uint64_t>(p->num_kv_heads), static_cast<uint64_t>(p->total_q)};
+    uint32_t box[3] = {64, 1, kTileN};
+    uint64_t strk[2] = {static_cast<uint64_t>(kHeadDim) * 2, static_cast<uint64_t>(p->k_stride) * 2};
+    uint64_t strv[2] = {static_cast<uint64_t>(kHeadDim) * 2, static_cast<uint64_t>(p->v_stride) * 2};
+    if ((rc = encode_map(&kn_map, bf16, p->k_new, 3, dims, strk, box)) != 0) return rc;
+    if ((rc = encode_map(&vn_map, bf16, p->v_new, 3, dims, strv, box)) != 0) return rc;
+  }
+  if (has_cache) {
+    uint64_t dims[4] = {static_cast<uint64_t>(kHeadDim), static_cast<uint64_t>(p->num_kv_heads),
+                        static_cast<uint64_t>(p->page_size), static_cast<uint64_t>(p->num_pages)};
+    uint64_t str[3] = {static_cast<uint64_t>(kHeadDim) * 2, static_cast<uint64_t>(kHeadDim) * 2 * p->num_kv_heads,
+                       static_cast<uint64_t>(kHeadDim) * 2 * p->num_kv_heads * p->page_size};
+    uint32_t box[4] = {64, 1, kTileN, 1};
+    if ((rc = encode_map(&kc_map, bf16, p->k_cache, 4, dims, str, box)) != 0) return rc;
+    if ((rc = encode_map(&vc_map, bf16, p->v_cache, 4, dims, str, box)) != 0) return rc;
+  } else {
+    kc_map = kn_map; vc_map = vn_map;  // never dereferenced: no context tiles exist
+  }
+
+  Args a;
+  a.out = p->out; a.block_table = p->block_table; a.cu_seqlens_q = p->cu_seqlens_q; a.seq_lens = p->seq_lens;
+  a.mask = p->mask; a.status = p->status;
+  a.part_o = reinterpret_cast<float*>(p->workspace);
+  a.part_ml = a.part_o ? a.part_o + pl.units * static_cast<int64_t>(kHeadDim) * kTileM : nullptr;
+  a.out_stride = p->out_stride; a.block_table_stride = p->block_table_stride;
+  a.mask_stride_m = p->mask_stride_m; a.mask_stride_n = p->mask_stride_n; a.num_pages = has_cache ? p->num_pages : 0;
+  a.num_seqs = p->num_seqs; a.max_pages = p->max_pages; a.num_q_heads = p->num_q_heads; a.num_kv_heads = p->num_kv_heads;
+  a.group = pl.group; a.tpt = pl.tpt; a.q_tiles = pl.q_tiles; a.num_splits = pl.num_splits;
+  a.page_size = p->page_size > 0 ? p->page_size : kTileN; a.has_cache = has_cache ? 1 : 0;
+  a.mask_mode = p->mask_mode; a.bidirectional = p->bidirectional;
+  a.block_m = 2 * (p->diffusion_blk > 0 ? p->diffusion_blk : 32);
+  a.is_bf16 = bf16 ? 1 : 0;
+  a.scale_log2 = p->sm_scale * 1.4426950408889634f;
+
+  {
+    // the opt-in shared-memory size is a per-device function attribute
+    static std::mutex mu;
+    static bool done[64] = {false};
+    int dev = 0;
+    cudaGetDevice(&dev);
+    std::lock_guard<std::mutex> lock(mu);
+    if (dev < 0 || dev >= 64 || !done[dev]) {
+      cudaError_t e = cudaFuncSetAttribute(attn_sm100_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes);
+      if (e != cudaSuccess) return fail(static_cast<int>(e), "cudaFuncSetAttribute: %s", cudaGetErrorString(e));
+      if (dev >= 0 && dev < 64) done[dev] = true;
+    }
+  }
+
+  attn_sm100_kernel<<<static_cast<unsigned>(pl.units), kThreads, kSmemBytes, stream>>>(q_map, kn_map, vn_map, kc_map, vc_map, a);
+  if ((rc = check_launch("attn_sm100_kernel")) != 0) return rc;
+  if (pl.num_splits > 1) {
+    attn_combine_kernel<<<static_cast<unsigned>(pl.tiles), 4 * kTileM, 0, stream>>>(a);
+    if ((rc = check_launch("attn_combine_kernel")) != 0) return rc;
+  }
+  return 0;
+}
+
+}  // namespace tc
+}  // namespace pdllm

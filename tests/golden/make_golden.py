@@ -1,0 +1,218 @@
+"""Generates tests/golden/toy_reference.json by running the UNMODIFIED reference class on CPU.
+
+Run where the reference checkout exists:  python tests/golden/make_golden.py [--reference /path/to/reference]
+It needs only CPU. The reference's model plug-in (Fast-dLLM v1, absent from the reference tree) is supplied by
+oracle/contract_model; everything else — chunking, chunk BOS, draft rounds, self-information scoring, ranking,
+token eviction, position bookkeeping, block denoising — is the reference's own code
+(prefilling_dllm_eval/fastdllm_parallelcomp.py). The JSON it writes is what pins oracle/hotpath.py and the
+GPU path; the GPU box never needs the reference.
+
+Workload = BASELINE config "CPU toy": Dream architecture, 2 layers, hidden 256, 4 query / 2 KV heads, head_dim 64,
+MLP 688, vocab 1024, RoPE theta 1e6, fp32, seeded N(0, 0.02) init; 4096 uniform random context ids (seed 0) and a
+32-token query; chunk_size 512 with chunk BOS, topk 4, 4 draft tokens / 1 partial round, block 32, 32 new tokens,
+threshold 0.9, greedy. Token ids: BOS 1, EOS 2, MASK 1023; sampled ids avoid them.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import sys
+import tempfile
+
+import torch
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+ROOT = os.path.dirname(os.path.dirname(HERE))
+sys.path.insert(0, ROOT)
+
+TOY = dict(vocab_size=1024, hidden_size=256, intermediate_size=688, num_hidden_layers=2, num_attention_heads=4,
+           num_key_value_heads=2, max_position_embeddings=32768, rope_theta=1000000.0, rms_norm_eps=1e-6,
+           initializer_range=0.02, mask_token_id=1023, pad_token_id=0, bos_token_id=1, eos_token_id=2)
+BOS, EOS, MASK = 1, 2, 1023
+
+
+def toy_inputs(context_len=4096, query_len=32, seed=0):
+    g = torch.Generator().manual_seed(seed)
+    context = torch.randint(3, 1023, (context_len,), generator=g).tolist()
+    query = torch.randint(3, 1023, (query_len,), generator=g).tolist()
+    return context, query
+
+
+def write_toy_checkpoint(path: str, seed: int = 0) -> None:
+    """config.json + seeded-init model.safetensors + a 1024-word tokenizer."""
+    from safetensors.torch import save_file
+    from tokenizers import Tokenizer
+    from tokenizers.models import WordLevel
+    from tokenizers.pre_tokenizers import Whitespace
+
+    from oracle.contract_model.model.configuration_dream import DreamConfig
+    from oracle.contract_model.model.modeling_dream import DreamModel, init_weights_
+
+    os.makedirs(path, exist_ok=True)
+    with open(os.path.join(path, "config.json"), "w") as handle:
+        json.dump(dict(TOY, model_type="Dream", torch_dtype="float32"), handle)
+    model = DreamModel(DreamConfig(**TOY))
+    init_weights_(model, seed)
+    save_file({k: v.contiguous() for k, v in model.state_dict().items()}, os.path.join(path, "model.safetensors"))
+    vocab = {f"t{i}": i for i in range(TOY["vocab_size"])}
+    vocab.pop("t1"), vocab.pop("t2"), vocab.pop("t1023"), vocab.pop("t0")
+    vocab.update({"<pad>": 0, "<bos>": BOS, "<eos>": EOS, "<mask>": MASK})
+    tok = Tokenizer(WordLevel(vocab, unk_token="<pad>"))
+    tok.pre_tokenizer = Whitespace()
+    tok.save(os.path.join(path, "tokenizer.json"))
+    with open(os.path.join(path, "tokenizer_config.json"), "w") as handle:
+        json.dump({"tokenizer_class": "PreTrainedTokenizerFast", "bos_token": "<bos>", "eos_token": "<eos>",
+                   "mask_token": "<mask>", "pad_token": "<pad>", "unk_token": "<pad>"}, handle)
+
+
+README_FLAGS = dict(  # the reference README's canonical long-context flags (README.md:117-145)
+    cache_build_mode="full_prompt_mask", score_mode="draft_self_information", score_draft_tokens=4,
+    score_draft_partial_rounds=1, score_context_mode="single_chunk", score_attention_mask="causal", score_batch_size=8,
+    chunk_position_mode="continuous", query_position_mode="after_selected_chunks", token_capacity=0,
+    chunk_size=512, topk_chunks=4, block_length=32, max_new_tokens=32, threshold=0.9, temperature=0.0,
+)
+
+
+def load_reference(reference_root: str, ckpt: str, **flags):
+    eval_dir = os.path.join(reference_root, "prefilling_dllm_eval")
+    if eval_dir not in sys.path:
+        sys.path.insert(0, eval_dir)
+    import fastdllm_parallelcomp as ref  # the reference module, unmodified
+
+    runtime = ref.load_fastdllm_parallelcomp(
+        pretrained=ckpt, fastdllm_dream_dir=os.path.join(ROOT, "oracle", "contract_model"), device="cpu", dtype="float32",
+        trust_remote_code=False, **flags)
+    return ref, runtime
+
+
+def record_run(runtime, context, query, *, capture_steps=True):
+    """generate() with the intermediate quantities captured by wrapping bound methods (no reference edits)."""
+    rec = {}
+    orig_draft = runtime.generate_partial_draft_rounds_from_cache
+    orig_keep = runtime._keep_positions_for_chunk
+    orig_keep_ph = runtime._keep_positions_per_layer_per_head_for_chunk
+    orig_tok_scores = runtime.query_attention_token_scores
+    orig_denoise = runtime._denoise_block_confidence_threshold
+    orig_fwd_replace = runtime._forward_generation_block_replace
+
+    def draft(**kw):
+        ids, mask = orig_draft(**kw)
+        rec["draft_ids"], rec["draft_confirmed"] = list(ids), list(mask)
+        return ids, mask
+
+    def keep(prefix_ids, chunk_ids, query_ids):
+        out = orig_keep(prefix_ids, chunk_ids, query_ids)
+        rec.setdefault("keep_positions", []).append(list(out))
+        return out
+
+    def keep_ph(prefix_ids, chunk_ids, query_ids):
+        out = orig_keep_ph(prefix_ids, chunk_ids, query_ids)
+        rec.setdefault("keep_positions_per_head", []).append([t.tolist() for t in out])
+        return out
+
+    def tok_scores(*a, **kw):
+        out = orig_tok_scores(*a, **kw)
+        rec.setdefault("token_scores", []).append([float(x) for x in out.tolist()])
+        return out
+
+    steps = []
+
+    def fwd_replace(block_ids, **kw):
+        logits, cache = orig_fwd_replace(block_ids, **kw)
+        if capture_steps:
+            steps.append(block_ids[0].tolist())
+        return logits, cache
+
+    runtime.generate_partial_draft_rounds_from_cache = draft
+    runtime._keep_positions_for_chunk = keep
+    runtime._keep_positions_per_layer_per_head_for_chunk = keep_ph
+    runtime.query_attention_token_scores = tok_scores
+    runtime._forward_generation_block_replace = fwd_replace
+    try:
+        result = runtime.generate(prefix_ids=runtime.bos_ids(), context_ids=context, query_ids=query)
+    finally:
+        runtime.generate_partial_draft_rounds_from_cache = orig_draft
+        runtime._keep_positions_for_chunk = orig_keep
+        runtime._keep_positions_per_layer_per_head_for_chunk = orig_keep_ph
+        runtime.query_attention_token_scores = orig_tok_scores
+        runtime._forward_generation_block_replace = orig_fwd_replace
+    rec.update(
+        sequences=list(result.sequences), selected_chunk_indices=list(result.selected_chunk_indices),
+        chunk_scores={str(k): float(v) for k, v in result.chunk_scores.items()}, cache_tokens=result.cache_tokens,
+        removed_tokens=result.removed_tokens, candidate_chunks=result.candidate_chunks, prefix_tokens=result.prefix_tokens,
+        generation_blocks=result.generation_blocks,
+        chunk_meta=[dict(chunk_index=m.chunk_index, original_tokens=m.original_tokens, kept_tokens=m.kept_tokens,
+                         cache_start=m.cache_start, cache_end=m.cache_end, rope_start=m.rope_start, rope_end=m.rope_end)
+                    for m in result.chunk_meta],
+        block_states_before_each_forward=steps,
+    )
+    return rec
+
+
+def cross_check_vendored_dream(reference_root: str, ckpt: str) -> float:
+    """Max |logit| difference between the contract model and the Dream model the reference vendors
+    (prefilling_dllm_eval/model_cache/dream/model_dream.py) on a plain full-attention forward."""
+    eval_dir = os.path.join(reference_root, "prefilling_dllm_eval")
+    if eval_dir not in sys.path:
+        sys.path.insert(0, eval_dir)
+    from fastdllm_v1_model import _ensure_default_rope_init
+
+    _ensure_default_rope_init()
+    from model_cache.dream.configuration_dream import DreamConfig as VendoredConfig
+    from model_cache.dream.model_dream import DreamModel as VendoredDream
+    from safetensors.torch import load_file
+
+    from oracle.contract_model.model.modeling_dream import DreamModel
+
+    vend = VendoredDream(VendoredConfig(**{k: v for k, v in TOY.items()}))
+    state = load_file(os.path.join(ckpt, "model.safetensors"))
+    vend.load_state_dict(state, strict=False)
+    vend = vend.float().eval()
+    mine = DreamModel.from_pretrained(ckpt).eval()
+    ids = torch.randint(3, 1023, (1, 77), generator=torch.Generator().manual_seed(5))
+    with torch.no_grad():
+        a = vend(ids, attention_mask=None, position_ids=torch.arange(77).unsqueeze(0)).logits
+        b = mine(ids, attention_mask="full", position_ids=torch.arange(77).unsqueeze(0)).logits
+    return float((a - b).abs().max())
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--reference", default="/root/reference")
+    ap.add_argument("--out", default=os.path.join(HERE, "toy_reference.json"))
+    args = ap.parse_args()
+    torch.manual_seed(0)
+    torch.set_num_threads(max(1, os.cpu_count() or 1))
+    context, query = toy_inputs()
+    golden = {"config": dict(TOY), "flags": dict(README_FLAGS), "context_seed": 0, "runs": {}}
+    with tempfile.TemporaryDirectory() as tmp:
+        ckpt = os.path.join(tmp, "ckpt_toy")
+        write_toy_checkpoint(ckpt)
+        try:
+            golden["vendored_dream_max_abs_logit_diff"] = cross_check_vendored_dream(args.reference, ckpt)
+        except Exception as exc:  # the vendored model depends on the installed transformers version
+            golden["vendored_dream_max_abs_logit_diff"] = None
+            golden["vendored_dream_error"] = f"{type(exc).__name__}: {exc}"
+        variants = {
+            "readme_full_prompt_mask": dict(README_FLAGS),
+            "chunk_query_reuse": dict(README_FLAGS, cache_build_mode="chunk_query", chunk_position_mode="reuse",
+                                      query_position_mode="after_reused_window"),
+            "evict_global_cap128": dict(README_FLAGS, token_capacity=128),
+            "evict_per_head_cap128_chunk_query": dict(README_FLAGS, token_capacity=128, token_eviction_granularity="per_head",
+                                                      cache_build_mode="chunk_query", chunk_position_mode="reuse",
+                                                      query_position_mode="after_reused_window"),
+            "two_blocks": dict(README_FLAGS, max_new_tokens=64),
+        }
+        for name, flags in variants.items():
+            _, runtime = load_reference(args.reference, ckpt, **flags)
+            golden["runs"][name] = dict(flags=flags, **record_run(runtime, context, query))
+            print(name, golden["runs"][name]["selected_chunk_indices"], golden["runs"][name]["sequences"][:8])
+    with open(args.out, "w") as handle:
+        json.dump(golden, handle)
+    print("wrote", args.out, os.path.getsize(args.out), "bytes")
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,520 @@
+"""Parity of every CUDA op (called through the C-ABI via prefilling_dllm_b200.ops) against the CPU oracle.
+
+Integer / index outputs must be bit-exact; fp32 reductions within 1e-5 relative; bf16 attention within the
+1e-2 relative error the north star states (measured as ||out-ref||_F / ||ref||_F, plus a max-abs guard).
+"""
+
+import math
+
+import pytest
+import torch
+
+from oracle import hotpath as oracle
+
+pytestmark = pytest.mark.gpu
+
+ATTN_REL_TOL = 1e-2  # bf16 attention outputs, relative Frobenius error
+
+
+@pytest.fixture(scope="module")
+def ops(cuda_device):
+    from prefilling_dllm_b200 import ops as _ops
+
+    return _ops
+
+
+def rel_err(a: torch.Tensor, b: torch.Tensor) -> float:
+    a, b = a.float().cpu(), b.float().cpu()
+    return float((a - b).norm() / b.norm().clamp_min(1e-12))
+
+
+# ----------------------------------------------------------------------------------------------- (5)
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float32])
+def test_store_kvcache_unified(ops, cuda_device, dtype):
+    g = torch.Generator().manual_seed(1)
+    n, hkv, d, pages, page = 300, 4, 128, 6, 256
+    key = torch.randn(n, hkv, d, generator=g).to(dtype)
+    value = torch.randn(n, hkv, d, generator=g).to(dtype)
+    slots = torch.randperm(pages * page, generator=g)[:n].to(torch.int32)
+    slots[::7] = -1  # skipped tokens
+    k_ref = torch.zeros(pages, page, hkv, d, dtype=dtype)
+    v_ref = torch.zeros_like(k_ref)
+    oracle.store_kvcache_unified(key, value, k_ref, v_ref, slots)
+    k_c = torch.zeros_like(k_ref, device=cuda_device)
+    v_c = torch.zeros_like(k_c)
+    ops.store_kvcache_unified_layout(key.to(cuda_device), value.to(cuda_device), k_c, v_c, slots.to(cuda_device), "diffusion_lm")
+    ops.check_status(cuda_device)
+    assert torch.equal(k_c.cpu(), k_ref) and torch.equal(v_c.cpu(), v_ref)
+
+
+def test_store_kvcache_unified_strided_rows_and_bad_slot(ops, cuda_device):
+    g = torch.Generator().manual_seed(2)
+    n, hkv, d = 33, 2, 64
+    qkv = torch.randn(n, 3 * hkv * d, generator=g).bfloat16().to(cuda_device)
+    key = qkv[:, hkv * d:2 * hkv * d].view(n, hkv, d)      # row stride 3*Hkv*D: the fused-QKV case
+    value = qkv[:, 2 * hkv * d:].view(n, hkv, d)
+    slots = torch.arange(n, dtype=torch.int32)
+    k_c = torch.zeros(1, 64, hkv, d, dtype=torch.bfloat16, device=cuda_device)
+    v_c = torch.zeros_like(k_c)
+    ops.store_kvcache_unified_layout(key, value, k_c, v_c, slots.to(cuda_device), "diffusion_lm")
+    ops.check_status(cuda_device)
+    assert torch.equal(k_c.view(-1, hkv, d)[:n], key) and torch.equal(v_c.view(-1, hkv, d)[:n], value)
+    bad = slots.clone()
+    bad[5] = 64 * 1 + 3  # beyond the pool: must be skipped and flagged, not written
+    ops.store_kvcache_unified_layout(key, value, k_c, v_c, bad.to(cuda_device), "diffusion_lm")
+    with pytest.raises(RuntimeError, match="slot_mapping"):
+        ops.check_status(cuda_device)
+    assert ops.check_status(cuda_device) == 0  # reading resets the word
+
+
+def test_store_kvcache_empty(ops, cuda_device):
+    key = torch.empty(0, 4, 128, dtype=torch.bfloat16, device=cuda_device)
+    cache = torch.zeros(2, 256, 4, 128, dtype=torch.bfloat16, device=cuda_device)
+    ops.store_kvcache_unified_layout(key, key.clone(), cache, cache.clone(), torch.empty(0, dtype=torch.int32, device=cuda_device), "diffusion_lm")
+    assert float(cache.abs().sum()) == 0.0
+
+
+def test_store_kvcache_distinct(ops, cuda_device):
+    g = torch.Generator().manual_seed(3)
+    n, hkv, d, pages, page, x = 200, 4, 128, 3, 256, 8
+    key = torch.randn(n, hkv, d, generator=g).bfloat16()
+    value = torch.randn(n, hkv, d, generator=g).bfloat16()
+    slots = torch.randperm(pages * page, generator=g)[:n].to(torch.int32)
+    slots[3] = -1
+    k_ref = torch.zeros(pages, hkv, d // x, page, x, dtype=torch.bfloat16)
+    v_ref = torch.zeros(pages, hkv, d, page, dtype=torch.bfloat16)
+    oracle.store_kvcache_distinct(key, value, k_ref, v_ref, slots)
+    k_c, v_c = torch.zeros_like(k_ref, device=cuda_device), torch.zeros_like(v_ref, device=cuda_device)
+    ops.store_kvcache_distinct_layout(key.to(cuda_device), value.to(cuda_device), k_c, v_c, slots.to(cuda_device), "diffusion_lm")
+    ops.check_status(cuda_device)
+    assert torch.equal(k_c.cpu(), k_ref) and torch.equal(v_c.cpu(), v_ref)
+
+
+class _Ctx:
+    pass
+
+
+def test_load_kvcache_matches_gather(ops, cuda_device):
+    g = torch.Generator().manual_seed(4)
+    hkv, d, page, pages = 4, 128, 256, 12
+    ctx_lens = [300, 0, 512]
+    new_lens = [32, 64, 32]
+    k_cache = torch.randn(pages, page, hkv, d, generator=g).bfloat16()
+    v_cache = torch.randn(pages, page, hkv, d, generator=g).bfloat16()
+    bt = torch.tensor([[7, 2, -1], [-1, -1, -1], [0, 11, -1]], dtype=torch.int32)
+    cu_q = [0]
+    for n in new_lens:
+        cu_q.append(cu_q[-1] + n)
+    cu_k = [0]
+    for c, n in zip(ctx_lens, new_lens):
+        cu_k.append(cu_k[-1] + c + n)
+    k_new = torch.randn(cu_q[-1], hkv, d, generator=g).bfloat16()
+    v_new = torch.randn(cu_q[-1], hkv, d, generator=g).bfloat16()
+    k_ref, v_ref = oracle.load_kvcache(k_cache, v_cache, bt, ctx_lens, cu_q, k_new, v_new)
+    ctx = _Ctx()
+    ctx.block_tables = bt.to(cuda_device)
+    ctx.context_lens = torch.tensor(ctx_lens, dtype=torch.int32, device=cuda_device)
+    ctx.seq_lens_ts = torch.tensor(new_lens, dtype=torch.int32, device=cuda_device)
+    ctx.cu_seqlens_q = torch.tensor(cu_q, dtype=torch.int32, device=cuda_device)
+    ctx.cu_seqlens_k = torch.tensor(cu_k, dtype=torch.int32, device=cuda_device)
+    k_out, v_out = ops.load_kvcache(k_cache.to(cuda_device), v_cache.to(cuda_device), ctx, k_new.to(cuda_device), v_new.to(cuda_device))
+    ops.check_status(cuda_device)
+    assert torch.equal(k_out.cpu(), k_ref) and torch.equal(v_out.cpu(), v_ref)
+
+
+# ----------------------------------------------------------------------------------------------- (3)+(1)
+def _attention_case(seed, *, num_seqs, hq, hkv, d, page, chunks_in_pool, pages_per_chunk, sel_chunks, q_lens, dtype,
+                    ctx_tail=0, layout="unified"):
+    """Build the op-level workload: a pool of chunks per request, sel_chunks picked by a seeded permutation."""
+    g = torch.Generator().manual_seed(seed)
+    pages_per_req = chunks_in_pool * pages_per_chunk
+    num_pages = num_seqs * pages_per_req
+    k_cache = torch.randn(num_pages, page, hkv, d, generator=g).to(dtype)
+    v_cache = torch.randn(num_pages, page, hkv, d, generator=g).to(dtype)
+    bt = torch.full((num_seqs, sel_chunks * pages_per_chunk + 1), -1, dtype=torch.int32)
+    seq_lens, cu = [], [0]
+    for s in range(num_seqs):
+        chosen = torch.randperm(chunks_in_pool, generator=g)[:sel_chunks]
+        ids = []
+        for c in chosen.tolist():
+            ids += [s * pages_per_req + c * pages_per_chunk + i for i in range(pages_per_chunk)]
+        bt[s, :len(ids)] = torch.tensor(ids, dtype=torch.int32)
+        ctx = len(ids) * page - (ctx_tail if s % 2 == 1 else 0)
+        seq_lens.append(ctx + q_lens[s])
+        cu.append(cu[-1] + q_lens[s])
+    t = cu[-1]
+    q = torch.randn(t, hq, d, generator=g).to(dtype)
+    k = torch.randn(t, hkv, d, generator=g).to(dtype)
+    v = torch.randn(t, hkv, d, generator=g).to(dtype)
+    return dict(q=q, k=k, v=v, k_cache=k_cache, v_cache=v_cache, bt=bt, seq_lens=seq_lens, cu=cu)
+
+
+def _run_attention(ops, dev, case, *, impl, mask=None, bidirectional=True, causal=False, diffusion_blk=32, num_splits=0,
+                   with_cache=True, sm_scale=None):
+    q, k, v = (case[n].to(dev) for n in ("q", "k", "v"))
+    out = torch.full_like(q, float("nan"))
+    kwargs = {}
+    if with_cache:
+        kwargs = dict(key_cache=case["k_cache"].to(dev), value_cache=case["v_cache"].to(dev), block_table=case["bt"].to(dev),
+                      seq_lens=torch.tensor(case["seq_lens"], dtype=torch.int32, device=dev), max_seq_len=max(case["seq_lens"]))
+    cu = torch.tensor(case["cu"], dtype=torch.int32, device=dev)
+    q_lens = [case["cu"][i + 1] - case["cu"][i] for i in range(len(case["cu"]) - 1)]
+    used = ops.paged_attention(q, k, v, out, cu_seqlens_q=cu, max_query_len=max(q_lens), sm_scale=sm_scale,
+                               mask=None if mask is None else mask.to(dev), causal=causal, bidirectional=bidirectional,
+                               diffusion_blk_sz=diffusion_blk, impl=impl, num_splits=num_splits, **kwargs)
+    ops.check_status(dev)
+    return out, used
+
+
+def _ref_attention(case, *, mask=None, bidirectional=True, causal=False, diffusion_blk=32, with_cache=True, sm_scale=None):
+    return oracle.paged_attention(case["q"], case["k"], case["v"], cu_seqlens_q=case["cu"],
+                                  k_cache=case["k_cache"] if with_cache else None, v_cache=case["v_cache"] if with_cache else None,
+                                  block_table=case["bt"] if with_cache else None, seq_lens=case["seq_lens"] if with_cache else None,
+                                  sm_scale=sm_scale, mask=mask, bidirectional=bidirectional, diffusion_blk=diffusion_blk, causal=causal)
+
+
+def test_attention_simt_fp32_toy_shape(ops, cuda_device):
+    # config "CPU toy": 4 query / 2 KV heads, head_dim 64, fp32
+    case = _attention_case(10, num_seqs=2, hq=4, hkv=2, d=64, page=256, chunks_in_pool=4, pages_per_chunk=2, sel_chunks=2,
+                           q_lens=[32, 64], dtype=torch.float32, ctx_tail=100)
+    out, used = _run_attention(ops, cuda_device, case, impl="auto")
+    assert used == "simt"
+    ref = _ref_attention(case)
+    assert rel_err(out, ref) < 1e-5
+
+
+@pytest.mark.parametrize("layout", ["unified", "distinct"])
+def test_attention_simt_bf16_layouts(ops, cuda_device, layout):
+    case = _attention_case(11, num_seqs=3, hq=28, hkv=4, d=128, page=256, chunks_in_pool=3, pages_per_chunk=1, sel_chunks=2,
+                           q_lens=[32, 96, 7], dtype=torch.bfloat16, ctx_tail=37)
+    ref = _ref_attention(case)
+    if layout == "distinct":
+        x = 8
+        pages, page, hkv, d = case["k_cache"].shape
+        kd = case["k_cache"].view(pages, page, hkv, d // x, x).permute(0, 2, 3, 1, 4).contiguous()
+        vd = case["v_cache"].permute(0, 2, 3, 1).contiguous()
+        ku, vu = oracle.distinct_to_unified(kd, vd)
+        assert torch.equal(ku, case["k_cache"]) and torch.equal(vu, case["v_cache"])
+        case = dict(case, k_cache=kd, v_cache=vd)
+    out, used = _run_attention(ops, cuda_device, case, impl="simt")
+    assert used == "simt"
+    assert rel_err(out, ref) < ATTN_REL_TOL
+
+
+def test_attention_simt_masks(ops, cuda_device):
+    case = _attention_case(12, num_seqs=2, hq=8, hkv=2, d=64, page=256, chunks_in_pool=2, pages_per_chunk=1, sel_chunks=1,
+                           q_lens=[96, 96], dtype=torch.float32)
+    g = torch.Generator().manual_seed(5)
+    dense = torch.rand(96, 96, generator=g) > 0.3
+    dense[5, :] = False  # a row whose new keys are all hidden still sees the context
+    for kwargs in (dict(mask=dense, bidirectional=True), dict(bidirectional=False), dict(mask=dense, bidirectional=False),
+                   dict(causal=True)):
+        out, _ = _run_attention(ops, cuda_device, case, impl="simt", **kwargs)
+        assert rel_err(out, _ref_attention(case, **kwargs)) < 1e-5, kwargs
+    # no context at all + a fully hidden row → zeros, as the reference kernel produces
+    out, _ = _run_attention(ops, cuda_device, case, impl="simt", mask=dense, with_cache=False)
+    ref = _ref_attention(case, mask=dense, with_cache=False)
+    assert rel_err(out, ref) < 1e-5
+    assert float(out[5].abs().max()) == 0.0
+
+
+def test_attention_tc_small_single_tile(ops, cuda_device):
+    # one request, one KV group tile: the smallest shape the tcgen05 kernel takes
+    case = _attention_case(20, num_seqs=1, hq=28, hkv=4, d=128, page=256, chunks_in_pool=2, pages_per_chunk=1, sel_chunks=1,
+                           q_lens=[16], dtype=torch.bfloat16)
+    out, used = _run_attention(ops, cuda_device, case, impl="tc", num_splits=1)
+    assert used == "tc"
+    assert rel_err(out, _ref_attention(case)) < ATTN_REL_TOL
+
+
+@pytest.mark.parametrize("num_splits", [1, 3, 0])
+def test_attention_tc_ragged_batch(ops, cuda_device, num_splits):
+    case = _attention_case(21, num_seqs=3, hq=28, hkv=4, d=128, page=256, chunks_in_pool=4, pages_per_chunk=2, sel_chunks=2,
+                           q_lens=[96, 32, 50], dtype=torch.bfloat16, ctx_tail=77)
+    out, used = _run_attention(ops, cuda_device, case, impl="tc", num_splits=num_splits)
+    assert used == "tc"
+    ref = _ref_attention(case)
+    assert rel_err(out, ref) < ATTN_REL_TOL
+    assert float((out.float().cpu() - ref).abs().max()) < 0.05
+
+
+def test_attention_tc_masks_and_prefill(ops, cuda_device):
+    case = _attention_case(22, num_seqs=2, hq=28, hkv=4, d=128, page=256, chunks_in_pool=2, pages_per_chunk=1, sel_chunks=1,
+                           q_lens=[200, 160], dtype=torch.bfloat16)
+    g = torch.Generator().manual_seed(6)
+    dense = torch.rand(200, 200, generator=g) > 0.3
+    dense[9, :] = False
+    for kwargs in (dict(mask=dense, bidirectional=True), dict(bidirectional=False), dict(causal=True),
+                   dict(causal=True, with_cache=False), dict(with_cache=False), dict(mask=dense, with_cache=False)):
+        out, used = _run_attention(ops, cuda_device, case, impl="tc", **kwargs)
+        assert used == "tc"
+        assert rel_err(out, _ref_attention(case, **kwargs)) < ATTN_REL_TOL, kwargs
+        assert not torch.isnan(out).any(), kwargs
+
+
+def test_attention_tc_mha_fp16(ops, cuda_device):
+    # LLaDA-like: MHA (group 1), fp16 inputs
+    case = _attention_case(23, num_seqs=2, hq=8, hkv=8, d=128, page=256, chunks_in_pool=2, pages_per_chunk=2, sel_chunks=1,
+                           q_lens=[32, 32], dtype=torch.float16)
+    out, used = _run_attention(ops, cuda_device, case, impl="auto")
+    assert used == "tc"
+    assert rel_err(out, _ref_attention(case)) < ATTN_REL_TOL
+
+
+def test_attention_tc_uninitialised_pool_tail_is_harmless(ops, cuda_device):
+    # rows of a page past the context length may hold NaN bit patterns; they must not leak into the output
+    case = _attention_case(24, num_seqs=2, hq=28, hkv=4, d=128, page=256, chunks_in_pool=2, pages_per_chunk=1, sel_chunks=1,
+                           q_lens=[32, 32], dtype=torch.bfloat16, ctx_tail=100)
+    ref = _ref_attention(case)
+    poisoned = dict(case)
+    kc, vc = case["k_cache"].clone(), case["v_cache"].clone()
+    page = int(case["bt"][1, 0])
+    kc[page, 156:] = float("nan")
+    vc[page, 156:] = float("nan")
+    poisoned["k_cache"], poisoned["v_cache"] = kc, vc
+    for impl in ("tc", "simt"):
+        out, _ = _run_attention(ops, cuda_device, poisoned, impl=impl)
+        assert not torch.isnan(out).any(), impl
+        assert rel_err(out, ref) < ATTN_REL_TOL, impl
+
+
+def test_attention_op_level_config_full_size(ops, cuda_device):
+    """8 requests, 28/4 heads, d 128, page 256, pool of 32 chunks x 1024 tokens per request,
+    4 chunks picked by a seeded permutation, 64 query + 32 response rows, bidirectional."""
+    case = _attention_case(0, num_seqs=8, hq=28, hkv=4, d=128, page=256, chunks_in_pool=32, pages_per_chunk=4, sel_chunks=4,
+                           q_lens=[96] * 8, dtype=torch.bfloat16)
+    out, used = _run_attention(ops, cuda_device, case, impl="auto")
+    assert used == "tc"
+    ref = _ref_attention(case)
+    assert rel_err(out, ref) < ATTN_REL_TOL
+    # the SIMT kernel is an independent on-device witness of the same answer
+    out_simt, _ = _run_attention(ops, cuda_device, case, impl="simt")
+    assert rel_err(out_simt, ref) < ATTN_REL_TOL
+    # linearity in V: attention(q, k, 2v) == 2 attention(q, k, v) exactly in bf16 (power-of-two scaling)
+    doubled = dict(case, v=case["v"] * 2, v_cache=case["v_cache"] * 2)
+    out2, _ = _run_attention(ops, cuda_device, doubled, impl="auto")
+    assert torch.equal(out2.float(), out.float() * 2)
+
+
+def test_flash_decoding_shim_reference_signature(ops, cuda_device):
+    case = _attention_case(25, num_seqs=1, hq=28, hkv=4, d=128, page=256, chunks_in_pool=2, pages_per_chunk=2, sel_chunks=2,
+                           q_lens=[32], dtype=torch.bfloat16)
+    dev = cuda_device
+    q, k, v = (case[n].to(dev) for n in ("q", "k", "v"))
+    out = torch.empty_like(q)
+    scale = 1.0 / math.sqrt(128)
+    ops.diffusion_lm_parallel_flash_decoding(
+        q, k, v, out, "auto", case["k_cache"].to(dev), case["v_cache"].to(dev), case["bt"].to(dev),
+        torch.tensor(case["cu"], dtype=torch.int32, device=dev), torch.tensor(case["seq_lens"], dtype=torch.int32, device=dev),
+        max(case["seq_lens"]), 32, 1.0, 1.0, 32, None, None, scale, torch.ones(32, 32, dtype=torch.bool, device=dev))
+    ops.check_status(dev)
+    # bidirectional defaults to False: with a 32-row block and BLOCK_M = 64 every new key is still visible
+    assert rel_err(out, _ref_attention(case, bidirectional=False, sm_scale=scale)) < ATTN_REL_TOL
+    with pytest.raises(NotImplementedError):
+        ops.diffusion_lm_parallel_flash_decoding(q, k, v, out, "fp8_e4m3", case["k_cache"].to(dev), case["v_cache"].to(dev),
+                                                 case["bt"].to(dev), torch.tensor(case["cu"], dtype=torch.int32, device=dev),
+                                                 torch.tensor(case["seq_lens"], dtype=torch.int32, device=dev), 0, 32, 1.0, 1.0)
+
+
+# ----------------------------------------------------------------------------------------------- (4)
+def _peaked_logits(g, rows, vocab, peaks):
+    """rows x vocab logits whose max softmax probability is (about) peaks[r]."""
+    logits = torch.randn(rows, vocab, generator=g) * 0.1
+    for r, p in enumerate(peaks):
+        if p is None:
+            continue
+        # one dominant logit: p = e^a / (e^a + sum_rest)
+        rest = torch.logsumexp(torch.cat([logits[r, :7], logits[r, 8:]]), dim=0)
+        logits[r, 7] = rest + math.log(p / (1 - p))
+    return logits
+
+
+@pytest.mark.parametrize("mode", ["engine_fp32", "eval_bf16", "eval_fp32", "llada_noshift"])
+def test_unmask_step_matches_reference_rule(ops, cuda_device, mode):
+    g = torch.Generator().manual_seed(30)
+    block_len, vocab, mask_id = 32, 4099, 4098
+    peaks = [None] * block_len
+    for r, p in ((3, 0.95), (4, 0.9001), (5, 0.8999), (6, 0.9), (9, 0.5), (12, 0.999)):
+        peaks[r] = p
+    logits = _peaked_logits(g, block_len, vocab, peaks)
+    last = torch.randn(vocab, generator=g)
+    dtype = torch.bfloat16 if mode == "eval_bf16" else torch.float32
+    softmax_dtype = torch.float32 if mode == "engine_fp32" else None
+    shift = mode != "llada_noshift"
+    logits, last = logits.to(dtype), last.to(dtype)
+    ids = torch.full((block_len,), mask_id, dtype=torch.int64)
+    ids[0] = 11
+    ids[20:24] = torch.tensor([5, 6, 7, 8])
+    ref_ids, ref_conf, ref_x0 = oracle.unmask_step(logits, ids, mask_token_id=mask_id, threshold=0.9, last_logit=last, shift=shift,
+                                                   softmax_dtype=softmax_dtype)
+    dev_ids = ids.to(cuda_device)
+    counts, conf, x0 = ops.unmask_step(logits.to(cuda_device), dev_ids, mask_token_id=mask_id, threshold=0.9,
+                                       last_logit=last.to(cuda_device), shift=shift, softmax_dtype=softmax_dtype, return_details=True)
+    assert torch.equal(dev_ids.cpu(), ref_ids)
+    assert torch.equal(x0.cpu(), ref_x0)
+    finite = torch.isfinite(ref_conf.float())
+    assert torch.allclose(conf.cpu()[finite], ref_conf.float()[finite], rtol=2e-6 if dtype == torch.float32 else 0, atol=0)
+    before = int((ids == mask_id).sum())
+    after = int((ref_ids == mask_id).sum())
+    assert counts.cpu().tolist() == [before, before - after, after]
+    assert before - after >= 2  # the threshold branch fired, not only the always-accepted top slot
+
+
+def test_unmask_step_flat_logits_make_exactly_one_step(ops, cuda_device):
+    # random-init models: max probability ~ 1/V, so exactly the most confident slot is filled each step
+    g = torch.Generator().manual_seed(31)
+    block_len, vocab, mask_id = 32, 152064, 151666
+    logits = (torch.randn(block_len, vocab, generator=g) * 1.2).bfloat16()
+    ids = torch.full((block_len,), mask_id, dtype=torch.int64)
+    ids[0] = 42
+    dev_ids, dev_logits = ids.to(cuda_device), logits.to(cuda_device)
+    steps = 0
+    ref = ids.clone()
+    while bool((ref == mask_id).any()):
+        ref, _, _ = oracle.unmask_step(logits, ref, mask_token_id=mask_id, threshold=0.9, last_logit=None, shift=True, softmax_dtype=torch.float32)
+        counts = ops.unmask_step(dev_logits, dev_ids, mask_token_id=mask_id, threshold=0.9, shift=True, softmax_dtype=torch.float32)
+        steps += 1
+        assert torch.equal(dev_ids.cpu(), ref), steps
+        assert counts.cpu().tolist()[1] == 1
+    assert steps == 31
+    # nothing left to fill: a further call is a no-op and reports zero candidates
+    counts = ops.unmask_step(dev_logits, dev_ids, mask_token_id=mask_id, threshold=0.9)
+    assert counts.cpu().tolist() == [0, 0, 0] and torch.equal(dev_ids.cpu(), ref)
+
+
+# ----------------------------------------------------------------------------------------------- (2a)(2b)
+@pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16])
+def test_self_information_scores(ops, cuda_device, dtype):
+    g = torch.Generator().manual_seed(40)
+    n_chunks, n_labels, vocab = 8, 34, 1024 if dtype == torch.float32 else 152064
+    rows = (torch.randn(n_chunks, n_labels, vocab, generator=g) * 1.3).to(dtype)
+    labels = torch.randint(0, vocab, (n_labels,), generator=g)
+    ref_scores, ref_nll = oracle.self_information_scores(rows, labels)
+    scores, nll = ops.self_information_scores(rows.view(-1, vocab).to(cuda_device), labels.to(cuda_device), n_chunks, return_nll=True)
+    ops.check_status(cuda_device)
+    assert torch.allclose(nll.cpu(), ref_nll, rtol=1e-5, atol=1e-5)
+    assert torch.allclose(scores.cpu(), ref_scores, rtol=1e-5, atol=1e-5)
+    # the ranking the scores feed is identical
+    sel, cnt = ops.topk_chunks(scores, 4)
+    assert sel.cpu()[: int(cnt.item())].tolist() == oracle.rank_chunks(ref_scores.tolist(), 4)
+
+
+def test_self_information_bad_label_is_flagged(ops, cuda_device):
+    rows = torch.zeros(2, 16, dtype=torch.float32, device=cuda_device)
+    labels = torch.tensor([99], dtype=torch.int64, device=cuda_device)
+    scores = ops.self_information_scores(rows, labels, 2)
+    assert scores.cpu().tolist() == [float("-inf")] * 2
+    with pytest.raises(RuntimeError, match="label"):
+        ops.check_status(cuda_device)
+
+
+def test_topk_chunks_stable_ties_and_edges(ops, cuda_device):
+    cases = [
+        ([0.5, 0.7, 0.7, 0.1, 0.7, float("nan"), float("inf"), -1.0], 3, False),
+        ([0.5, 0.7, 0.7, 0.1, 0.7, 0.2, 0.3, -1.0], 2, True),
+        ([1.0, 1.0, 1.0, 1.0], 2, False),
+        ([3.0, 2.0, 1.0], 0, False),
+        ([3.0, 2.0, 1.0], 10, False),
+        ([float("-inf")] * 5, 2, False),
+        ([-6.93 + 1e-6 * ((i * 7919) % 13) for i in range(32)], 8, False),
+    ]
+    for scores, k, keep_first in cases:
+        t = torch.tensor(scores, dtype=torch.float32)
+        sel, cnt = ops.topk_chunks(t.to(cuda_device), k, keep_first)
+        expect = oracle.rank_chunks(t.tolist(), k, keep_first)
+        assert sel.cpu()[: int(cnt.item())].tolist() == expect, (scores, k, keep_first)
+    sel, cnt = ops.topk_chunks(torch.empty(0, dtype=torch.float32, device=cuda_device), 4)
+    assert int(cnt.item()) == 0
+
+
+# ----------------------------------------------------------------------------------------------- (2c)
+@pytest.mark.parametrize("dtype,hq,hkv,d", [(torch.float32, 4, 2, 64), (torch.bfloat16, 28, 4, 128)])
+def test_query_to_chunk_scores(ops, cuda_device, dtype, hq, hkv, d):
+    g = torch.Generator().manual_seed(50)
+    prefix, chunk, w = 1, 700, 8
+    length = prefix + chunk + w
+    q = torch.randn(length, hq, d, generator=g).to(dtype)
+    k = torch.randn(length, hkv, d, generator=g).to(dtype)
+    scale = d ** -0.5
+    for mask, reduce in (("causal", "sum"), ("full", "mean")):
+        ref = oracle.query_to_chunk_scores(q, k, prefix_len=prefix, chunk_len=chunk, query_len=w, scale=scale, reduce_mode=reduce,
+                                           causal=mask == "causal")
+        out = ops.query_to_chunk_attention_scores(q.to(cuda_device), k.to(cuda_device), prefix_len=prefix, chunk_len=chunk, query_len=w,
+                                                  scale=scale, reduce_mode=reduce, attention_mask=mask)
+        assert out.shape == (hq, chunk) and out.dtype == torch.float32
+        assert torch.allclose(out.cpu(), ref, rtol=2e-4, atol=1e-7), (mask, reduce)
+
+
+def test_query_to_chunk_scores_error_behaviour(ops, cuda_device):
+    q = torch.randn(20, 4, 64)
+    with pytest.raises(ValueError, match="CUDA"):
+        ops.query_to_chunk_attention_scores(q, q[:, :2], prefix_len=1, chunk_len=10, query_len=8, scale=1.0)
+    qc = q.to(cuda_device)
+    with pytest.raises(ValueError, match="too large"):
+        ops.query_to_chunk_attention_scores(qc.repeat(8, 1, 1), qc.repeat(8, 1, 1)[:, :2], prefix_len=1, chunk_len=10, query_len=65, scale=1.0)
+    assert ops.query_to_chunk_attention_scores(qc, qc[:, :2], prefix_len=1, chunk_len=0, query_len=8, scale=1.0).numel() == 0
+
+
+@pytest.mark.parametrize("per_head", [False, True])
+def test_evict_select_matches_reference_rule(ops, cuda_device, per_head):
+    g = torch.Generator().manual_seed(60)
+    n_layers, hq, hkv, chunk, cap = 2, 4, 2, 512, 129
+    scores = torch.rand(n_layers, hq, chunk, generator=g)
+    scores[:, :, 100:140] = 0.0  # a flat stretch: max-pool plateaus and exact ties
+    if per_head:
+        pooled_ref = torch.stack([oracle.per_head_token_scores(scores[l], hkv) for l in range(n_layers)])
+        keep_ref = torch.stack([torch.stack([oracle.select_positions_from_token_scores(pooled_ref[l, h], capacity=cap, chunk_len=chunk)
+                                             for h in range(hkv)]) for l in range(n_layers)])
+    else:
+        pooled_ref = oracle.global_token_scores([scores[l] for l in range(n_layers)]).unsqueeze(0)
+        keep_ref = oracle.select_positions_from_token_scores(pooled_ref[0], capacity=cap, chunk_len=chunk).unsqueeze(0)
+    keep, pooled = ops.evict_select(scores.to(cuda_device), num_kv_heads=hkv, keep_count=cap, per_head=per_head, return_pooled=True)
+    assert torch.allclose(pooled.cpu(), pooled_ref, rtol=1e-6, atol=1e-7)
+    # rank on the device's own pooled values so that ulp-level reduction-order differences cannot move the cut
+    if per_head:
+        keep_dev_rule = torch.stack([torch.stack([oracle.select_positions_from_token_scores(pooled.cpu()[l, h], capacity=cap, chunk_len=chunk)
+                                                  for h in range(hkv)]) for l in range(n_layers)])
+    else:
+        keep_dev_rule = oracle.select_positions_from_token_scores(pooled.cpu()[0], capacity=cap, chunk_len=chunk).unsqueeze(0)
+    assert torch.equal(keep.cpu(), keep_dev_rule)
+    assert torch.equal(keep.cpu(), keep_ref)
+    assert bool((keep.cpu()[..., 0] == 0).all())                       # chunk BOS always kept
+    assert bool((keep.cpu()[..., 1:] > keep.cpu()[..., :-1]).all())    # ascending, no duplicates
+
+
+def test_evict_select_low_and_no_bos(ops, cuda_device):
+    g = torch.Generator().manual_seed(61)
+    scores = torch.rand(1, 2, 64, generator=g)
+    pooled = oracle.global_token_scores([scores[0]], pooling="none")
+    for keep_high, force in ((False, True), (True, False), (False, False)):
+        ref = oracle.select_positions_from_token_scores(pooled, capacity=10, chunk_len=64, keep_high=keep_high, force_keep_first=force)
+        keep = ops.evict_select(scores.to(cuda_device), num_kv_heads=2, keep_count=10, pool_kernel=1, force_keep_first=force, keep_high=keep_high)
+        assert keep.cpu()[0].tolist() == ref.tolist()
+    # capacity >= chunk: everything is kept
+    keep = ops.evict_select(scores.to(cuda_device), num_kv_heads=2, keep_count=64)
+    assert keep.cpu()[0].tolist() == list(range(64))
+
+
+# ----------------------------------------------------------------------------------------------- PD boundary
+def test_gather_scatter_compact_pages(ops, cuda_device):
+    g = torch.Generator().manual_seed(70)
+    pages, page, hkv, d = 10, 256, 4, 128
+    cache = torch.randn(pages, page, hkv, d, generator=g).bfloat16()
+    page_ids = [7, 2, 9]
+    n_tokens = 2 * page + 57
+    dense_ref = torch.cat([cache[p] for p in page_ids])[:n_tokens]
+    dev_cache = cache.to(cuda_device)
+    dense = ops.gather_pages(dev_cache, page_ids, n_tokens)
+    assert torch.equal(dense.cpu(), dense_ref)
+    # scatter into other pages of another pool and read back
+    pool2 = torch.zeros_like(dev_cache)
+    ops.scatter_pages(dense, pool2, [1, 4, 5])
+    assert torch.equal(ops.gather_pages(pool2, [1, 4, 5], n_tokens).cpu(), dense_ref)
+    # per-head compaction in place to the front of the same pages
+    keep = torch.stack([torch.sort(torch.randperm(n_tokens, generator=g)[:300]).values for _ in range(hkv)])
+    ref = oracle.compact_per_head(dense_ref, keep)
+    ops.compact_pages_per_head(dev_cache, page_ids, page_ids, keep.to(cuda_device), src_tokens=n_tokens)
+    ops.check_status(cuda_device)
+    assert torch.equal(ops.gather_pages(dev_cache, page_ids, 300).cpu(), ref)
+    with pytest.raises(ValueError):
+        ops.gather_pages(dev_cache, [1], 2 * page)
