@@ -53,8 +53,8 @@ __global__ void __launch_bounds__(128) attn_simt_kernel(AttnSimtArgs a) {
   const int m = static_cast<int>(row - q_start);
   T* out_row = reinterpret_cast<T*>(a.out) + row * a.out_stride + static_cast<int64_t>(head) * D;
   if (m >= q_len) return;
-  int ctx_len = a.seq_lens[s] - q_len;
-  if (ctx_len < 0 || a.kv_layout == PDLLM_KV_NONE) ctx_len = 0;
+  int ctx_len = 0;  // seq_lens may be null when there is no cache
+  if (a.kv_layout != PDLLM_KV_NONE) ctx_len = max(0, a.seq_lens[s] - q_len);
 
   const T* q_row = reinterpret_cast<const T*>(a.q) + row * a.q_stride + static_cast<int64_t>(head) * D;
   float qv[DPL];
