@@ -44,7 +44,7 @@ class AttnParams(Structure):
         ("q", c_void_p), ("k_new", c_void_p), ("v_new", c_void_p), ("out", c_void_p),
         ("k_cache", c_void_p), ("v_cache", c_void_p),
         ("block_table", c_void_p), ("cu_seqlens_q", c_void_p), ("seq_lens", c_void_p),
-        ("mask", c_void_p), ("status", c_void_p), ("workspace", c_void_p),
+        ("mask", c_void_p), ("status", c_void_p), ("workspace", c_void_p), ("trace", c_void_p),
         ("workspace_bytes", c_int64),
         ("q_stride", c_int64), ("k_stride", c_int64), ("v_stride", c_int64), ("out_stride", c_int64),
         ("block_table_stride", c_int64),

@@ -102,8 +102,8 @@ __global__ void __launch_bounds__(128) attn_simt_kernel(AttnSimtArgs a) {
       for (int i = 0; i < DPL; ++i) dot = fmaf(qv[i], kf[i], dot);
       dot = warp_sum(dot);
       float m_new = fmaxf(m_run, dot);
-      float alpha = __expf(m_run - m_new);
-      float p = __expf(dot - m_new);
+      float alpha = expf(m_run - m_new);
+      float p = expf(dot - m_new);
       l_run = l_run * alpha + p;
 #pragma unroll
       for (int i = 0; i < DPL; ++i) acc[i] = fmaf(p, vf[i], acc[i] * alpha);
@@ -127,8 +127,8 @@ __global__ void __launch_bounds__(128) attn_simt_kernel(AttnSimtArgs a) {
     for (int i = 0; i < DPL; ++i) { dot = fmaf(qv[i], to_f32<T>(kr[lane + 32 * i]), dot); vf[i] = to_f32<T>(vr[lane + 32 * i]); }
     dot = warp_sum(dot);
     float m_new = fmaxf(m_run, dot);
-    float alpha = __expf(m_run - m_new);
-    float p = __expf(dot - m_new);
+    float alpha = expf(m_run - m_new);
+    float p = expf(dot - m_new);
     l_run = l_run * alpha + p;
 #pragma unroll
     for (int i = 0; i < DPL; ++i) acc[i] = fmaf(p, vf[i], acc[i] * alpha);

@@ -47,6 +47,7 @@ struct Args {
   void* out;
   const int32_t* block_table; const int32_t* cu_seqlens_q; const int32_t* seq_lens;
   const uint8_t* mask; int32_t* status;
+  long long* trace;                // optional pipeline timestamps, see trace_event
   float* part_o; float* part_ml;   // split-KV partials: O as [unit][D][128], (m, l) as [unit][2][128]
   int64_t out_stride, block_table_stride, mask_stride_m, mask_stride_n, num_pages;
   int num_seqs, max_pages, num_q_heads, num_kv_heads, group, tpt, q_tiles, num_splits;
@@ -166,6 +167,13 @@ __device__ __forceinline__ void tmem_st32(uint32_t taddr, const uint32_t* r) {
       ::"r"(taddr), PDLLM_W16(r, 0), PDLLM_W16(r, 16)
       : "memory");
 }
+__device__ __forceinline__ void tmem_ld16(uint32_t taddr, uint32_t* r) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x16.b32 "
+      "{%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15}, [%16];"
+      : PDLLM_R32(r, 0)
+      : "r"(taddr));
+}
 __device__ __forceinline__ void tmem_st16(uint32_t taddr, const uint32_t* r) {
   asm volatile(
       "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], "
@@ -197,6 +205,17 @@ __host__ __device__ constexpr uint32_t make_idesc(bool bf16, bool b_mn_major) {
          ((kTileN >> 3) << 17) | ((kTileM >> 4) << 24);
 }
 
+// Optional timestamps (clock64) of CTA 0..7 for profiling the pipeline: trace[cta][iteration][event].
+#define PDLLM_TRACE_ON (a.trace != nullptr)
+constexpr int kTraceEvents = 8;
+constexpr int kTraceIters = 64;
+constexpr int kTraceCtas = 8;
+__device__ __forceinline__ void trace_event(const Args& a, int it, int ev) {
+  if (blockIdx.x < kTraceCtas && it < kTraceIters && (threadIdx.x & 31) == 0 && (threadIdx.x == 0 || threadIdx.x >= 128)) {
+    a.trace[(static_cast<int64_t>(blockIdx.x) * kTraceIters + it) * kTraceEvents + ev] = clock64();
+  }
+}
+
 struct TileInfo {
   bool is_ctx;
   int key0;    // first key of the tile: context position, or new-row index
@@ -225,6 +244,7 @@ attn_sm100_kernel(const __grid_constant__ CUtensorMap q_map, const __grid_consta
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + kSmemBar);
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + kSmemBar + 128);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + kSmemBar + 136);
+  volatile int* tile_flags = reinterpret_cast<volatile int*>(smem + kSmemBar + 144);  // [2]: page of the tile in flight was unreadable
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
@@ -305,13 +325,16 @@ attn_sm100_kernel(const __grid_constant__ CUtensorMap q_map, const __grid_consta
           const int pidx = ti.key0 / a.page_size;
           off = ti.key0 - pidx * a.page_size;
           page = (pidx < a.max_pages) ? a.block_table[seq * a.block_table_stride + pidx] : -1;
-          if (page < 0 || page >= a.num_pages) {
-            report_status(a.status, PDLLM_S_BAD_PAGE);
-            page = 0;  // keep the copy in bounds; the softmax warps see the same bad id and mask the tile
-          }
+        }
+        const bool bad_page = ti.is_ctx && (page < 0 || page >= a.num_pages);
+        if (bad_page) {
+          report_status(a.status, PDLLM_S_BAD_PAGE);
+          page = 0;  // keep the copy in bounds; the softmax warps hide the whole tile
         }
         ok = mbar_wait(&bars[kKEmpty], ph ^ 1, abort_flag, a.status);
         if (!ok) break;
+        tile_flags[ph] = bad_page ? 1 : 0;  // published to the softmax warps through the barrier chain K-full → S-full
+        if (PDLLM_TRACE_ON) trace_event(a, it, 5);
         mbar_expect_tx(&bars[kKFull], kTileBytes);
         if (ti.is_ctx) {
           tma_load_4d(&kc_map, &bars[kKFull], smem + kSmemK, 0, kvh, off, page);
@@ -322,6 +345,7 @@ attn_sm100_kernel(const __grid_constant__ CUtensorMap q_map, const __grid_consta
         }
         ok = mbar_wait(&bars[kVEmpty], ph ^ 1, abort_flag, a.status);
         if (!ok) { issued = it * 2 + 1; break; }
+        if (PDLLM_TRACE_ON) trace_event(a, it, 6);
         mbar_expect_tx(&bars[kVFull], kTileBytes);
         if (ti.is_ctx) {
           tma_load_4d(&vc_map, &bars[kVFull], smem + kSmemV, 0, kvh, off, page);
@@ -352,6 +376,7 @@ attn_sm100_kernel(const __grid_constant__ CUtensorMap q_map, const __grid_consta
       if (ok && it > 0) ok = mbar_wait(&bars[kPvDone], (it - 1) & 1, abort_flag, a.status);  // S/P columns free again
       if (!ok) break;
       tc_fence_after();
+      if (PDLLM_TRACE_ON) trace_event(a, it, 3);
       if (lane == 0) {
 #pragma unroll
         for (int kk = 0; kk < kHeadDim / 16; ++kk) {
@@ -380,6 +405,7 @@ attn_sm100_kernel(const __grid_constant__ CUtensorMap q_map, const __grid_consta
       ok = mbar_wait(&bars[kPFull], ph, abort_flag, a.status);
       if (!ok) break;
       tc_fence_after();
+      if (PDLLM_TRACE_ON) trace_event(a, it, 4);
       if (lane == 0) {
 #pragma unroll
         for (int kk = 0; kk < kTileN / 16; ++kk) {
@@ -409,49 +435,51 @@ attn_sm100_kernel(const __grid_constant__ CUtensorMap q_map, const __grid_consta
     float m_ref = -INFINITY;  // running reference maximum, log2 domain
     float l_run = 0.f;
     bool ok = true;
-    uint32_t v[32];
+    uint32_t s[kTileN];       // one row of S; later reused chunk-wise for O
+    constexpr uint32_t kNegInf = 0xff800000u;
 
     for (int it = 0; it < n_iter; ++it) {
       const uint32_t ph = it & 1;
       const TileInfo ti = tile_info(t_begin + it, n_ctx_tiles, ctx_len, new_end);
       int cmax = ti.nvalid;  // columns [0, cmax) are visible to this row
-      if (ti.is_ctx) {
-        const int pidx = ti.key0 / a.page_size;
-        const int page = (pidx < a.max_pages) ? a.block_table[seq * a.block_table_stride + pidx] : -1;
-        if (page < 0 || page >= a.num_pages) cmax = 0;
-      } else {
-        cmax = min(cmax, row_new_end - ti.key0);
-      }
+      if (!ti.is_ctx) cmax = min(cmax, row_new_end - ti.key0);
       const bool use_dense = dense_mask && !ti.is_ctx && row_valid;
-      const bool need_mask = (cmax < kTileN) || use_dense;
       const uint8_t* mrow = use_dense ? a.mask + static_cast<int64_t>(m) * a.mask_stride_m + static_cast<int64_t>(ti.key0) * a.mask_stride_n : nullptr;
 
       ok = mbar_wait(&bars[kSFull], ph, abort_flag, a.status);
       if (!ok) break;
       tc_fence_after();
+      if (PDLLM_TRACE_ON) trace_event(a, it, 0);
 
-      // pass 1: row maximum of the visible scores
-      float mx = -INFINITY;
-#pragma unroll 1
-      for (int c = 0; c < 4; ++c) {
-        tmem_ld32(tS + c * 32, v);
-        tc_wait_ld();
-        if (!need_mask) {
+      // the whole row of S in one TMEM round trip
+      tmem_ld32(tS + 0, s);
+      tmem_ld32(tS + 32, s + 32);
+      tmem_ld32(tS + 64, s + 64);
+      tmem_ld32(tS + 96, s + 96);
+      tc_wait_ld();
+      if (PDLLM_TRACE_ON) trace_event(a, it, 1);
+      if (tile_flags[ph]) cmax = 0;  // the producer could not read this tile's page: hide all of it
+      if (cmax < kTileN || use_dense) {
 #pragma unroll
-          for (int j = 0; j < 32; ++j) mx = fmaxf(mx, __uint_as_float(v[j]));
-        } else {
-#pragma unroll
-          for (int j = 0; j < 32; ++j) {
-            const int col = c * 32 + j;
-            bool vis = col < cmax;
-            if (vis && use_dense) vis = mrow[col * a.mask_stride_n] != 0;
-            if (vis) mx = fmaxf(mx, __uint_as_float(v[j]));
-          }
+        for (int j = 0; j < kTileN; ++j) {
+          bool vis = j < cmax;
+          if (vis && use_dense) vis = mrow[j * a.mask_stride_n] != 0;
+          if (!vis) s[j] = kNegInf;
         }
       }
-      const float m_tile = mx * a.scale_log2;  // scale > 0, so max commutes with the scaling
 
-      // lazy rescale: only when the maximum grew by more than 2^8 (or on the first tile that sets it)
+      // row maximum, four independent chains
+      float mx0 = -INFINITY, mx1 = -INFINITY, mx2 = -INFINITY, mx3 = -INFINITY;
+#pragma unroll
+      for (int j = 0; j < kTileN; j += 4) {
+        mx0 = fmaxf(mx0, __uint_as_float(s[j]));
+        mx1 = fmaxf(mx1, __uint_as_float(s[j + 1]));
+        mx2 = fmaxf(mx2, __uint_as_float(s[j + 2]));
+        mx3 = fmaxf(mx3, __uint_as_float(s[j + 3]));
+      }
+      const float m_tile = fmaxf(fmaxf(mx0, mx1), fmaxf(mx2, mx3)) * a.scale_log2;  // scale > 0: max commutes
+
+      // lazy rescale: only when the maximum grew by more than 2^8 (the first tile just sets the reference)
       if (it == 0) {
         m_ref = m_tile;
       } else {
@@ -460,13 +488,14 @@ attn_sm100_kernel(const __grid_constant__ CUtensorMap q_map, const __grid_consta
           const float m_new = grow ? m_tile : m_ref;
           const float alpha = grow ? ex2(m_ref - m_new) : 1.f;  // m_ref = -inf gives 0
           l_run *= alpha;
+          uint32_t o[16];
 #pragma unroll 1
-          for (int c = 0; c < 4; ++c) {
-            tmem_ld32(tO + c * 32, v);
+          for (int c = 0; c < kHeadDim / 16; ++c) {
+            tmem_ld16(tO + c * 16, o);
             tc_wait_ld();
 #pragma unroll
-            for (int j = 0; j < 32; ++j) v[j] = __float_as_uint(__uint_as_float(v[j]) * alpha);
-            tmem_st32(tO + c * 32, v);
+            for (int j = 0; j < 16; ++j) o[j] = __float_as_uint(__uint_as_float(o[j]) * alpha);
+            tmem_st16(tO + c * 16, o);
           }
           tc_wait_st();
           m_ref = m_new;
@@ -474,40 +503,36 @@ attn_sm100_kernel(const __grid_constant__ CUtensorMap q_map, const __grid_consta
       }
       const float m_use = (m_ref == -INFINITY) ? 0.f : m_ref;
 
-      // pass 2: P = exp2(S*scale - m_ref) → bf16/fp16 pairs, written over the S columns already consumed
-#pragma unroll 1
-      for (int c = 0; c < 4; ++c) {
-        tmem_ld32(tS + c * 32, v);
-        tc_wait_ld();
-        uint32_t packed[16];
+      // P = exp2(S*scale - m_ref) → bf16/fp16 pairs over the S columns (all of S is in registers by now)
+      float l0 = 0.f, l1 = 0.f, l2 = 0.f, l3 = 0.f;
 #pragma unroll
-        for (int j = 0; j < 32; j += 2) {
-          float p0 = ex2(fmaf(__uint_as_float(v[j]), a.scale_log2, -m_use));
-          float p1 = ex2(fmaf(__uint_as_float(v[j + 1]), a.scale_log2, -m_use));
-          if (need_mask) {
-            const int col = c * 32 + j;
-            bool vis0 = col < cmax, vis1 = (col + 1) < cmax;
-            if (use_dense) {
-              if (vis0) vis0 = mrow[col * a.mask_stride_n] != 0;
-              if (vis1) vis1 = mrow[(col + 1) * a.mask_stride_n] != 0;
-            }
-            if (!vis0) p0 = 0.f;
-            if (!vis1) p1 = 0.f;
-          }
-          l_run += p0 + p1;
+      for (int half = 0; half < 2; ++half) {
+        uint32_t packed[32];
+#pragma unroll
+        for (int j = 0; j < 64; j += 4) {
+          const int c = half * 64 + j;
+          const float p0 = ex2(fmaf(__uint_as_float(s[c]), a.scale_log2, -m_use));
+          const float p1 = ex2(fmaf(__uint_as_float(s[c + 1]), a.scale_log2, -m_use));
+          const float p2 = ex2(fmaf(__uint_as_float(s[c + 2]), a.scale_log2, -m_use));
+          const float p3 = ex2(fmaf(__uint_as_float(s[c + 3]), a.scale_log2, -m_use));
+          l0 += p0; l1 += p1; l2 += p2; l3 += p3;
           if (a.is_bf16) {
-            __nv_bfloat162 h = __floats2bfloat162_rn(p0, p1);
-            packed[j >> 1] = *reinterpret_cast<uint32_t*>(&h);
+            __nv_bfloat162 h0 = __floats2bfloat162_rn(p0, p1), h1 = __floats2bfloat162_rn(p2, p3);
+            packed[j >> 1] = *reinterpret_cast<uint32_t*>(&h0);
+            packed[(j >> 1) + 1] = *reinterpret_cast<uint32_t*>(&h1);
           } else {
-            __half2 h = __floats2half2_rn(p0, p1);
-            packed[j >> 1] = *reinterpret_cast<uint32_t*>(&h);
+            __half2 h0 = __floats2half2_rn(p0, p1), h1 = __floats2half2_rn(p2, p3);
+            packed[j >> 1] = *reinterpret_cast<uint32_t*>(&h0);
+            packed[(j >> 1) + 1] = *reinterpret_cast<uint32_t*>(&h1);
           }
         }
-        tmem_st16(tS + c * 16, packed);
+        tmem_st32(tS + half * 32, packed);
       }
+      l_run += (l0 + l1) + (l2 + l3);
       tc_wait_st();
       tc_fence_before();
       mbar_arrive(&bars[kPFull]);
+      if (PDLLM_TRACE_ON) trace_event(a, it, 2);
     }
 
     // ---- epilogue ----
@@ -520,13 +545,13 @@ attn_sm100_kernel(const __grid_constant__ CUtensorMap q_map, const __grid_consta
                            ((static_cast<int64_t>(q_start + m)) * a.out_stride + static_cast<int64_t>(kvh * G + head_local) * kHeadDim) * 2;
 #pragma unroll 1
         for (int c = 0; c < 4; ++c) {
-          tmem_ld32(tO + c * 32, v);
+          tmem_ld32(tO + c * 32, s);
           tc_wait_ld();
           if (row_valid) {
             uint32_t packed[16];
 #pragma unroll
             for (int j = 0; j < 32; j += 2) {
-              const float o0 = __uint_as_float(v[j]) * inv, o1 = __uint_as_float(v[j + 1]) * inv;
+              const float o0 = __uint_as_float(s[j]) * inv, o1 = __uint_as_float(s[j + 1]) * inv;
               if (a.is_bf16) {
                 __nv_bfloat162 h = __floats2bfloat162_rn(o0, o1);
                 packed[j >> 1] = *reinterpret_cast<uint32_t*>(&h);
@@ -544,10 +569,10 @@ attn_sm100_kernel(const __grid_constant__ CUtensorMap q_map, const __grid_consta
         float* po = a.part_o + static_cast<int64_t>(unit) * kHeadDim * kTileM;
 #pragma unroll 1
         for (int c = 0; c < 4; ++c) {
-          tmem_ld32(tO + c * 32, v);
+          tmem_ld32(tO + c * 32, s);
           tc_wait_ld();
 #pragma unroll
-          for (int j = 0; j < 32; ++j) po[static_cast<int64_t>(c * 32 + j) * kTileM + r] = __uint_as_float(v[j]);
+          for (int j = 0; j < 32; ++j) po[static_cast<int64_t>(c * 32 + j) * kTileM + r] = __uint_as_float(s[j]);
         }
         a.part_ml[(static_cast<int64_t>(unit) * 2 + 0) * kTileM + r] = m_ref;
         a.part_ml[(static_cast<int64_t>(unit) * 2 + 1) * kTileM + r] = l_run;
@@ -762,6 +787,7 @@ inline int launch(const pdllm_attn_params* p, cudaStream_t stream) {
   Args a;
   a.out = p->out; a.block_table = p->block_table; a.cu_seqlens_q = p->cu_seqlens_q; a.seq_lens = p->seq_lens;
   a.mask = p->mask; a.status = p->status;
+  a.trace = reinterpret_cast<long long*>(p->trace);
   a.part_o = reinterpret_cast<float*>(p->workspace);
   a.part_ml = a.part_o ? a.part_o + pl.units * static_cast<int64_t>(kHeadDim) * kTileM : nullptr;
   a.out_stride = p->out_stride; a.block_table_stride = p->block_table_stride;

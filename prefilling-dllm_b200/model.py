@@ -1,0 +1,347 @@
+"""Dream / LLaDA-architecture transformer over a paged KV pool, GPU only.
+
+The dense layers (embedding, RMSNorm, QKV / O / MLP / LM-head GEMMs, RoPE, SwiGLU) are plain torch on the current
+CUDA stream (cuBLAS GEMMs); the parts of the hot path that this package owns — KV page writes and attention over
+[selected prefix pages ‖ new rows] — go through the sm_100a kernels in `ops`. Arithmetic follows the Dream model the
+reference vendors (prefilling_dllm_eval/model_cache/dream/model_dream.py:117-131 RMSNorm in fp32, :208-264 rotate-half
+RoPE with fp32 tables, :326-329 biased q/k/v, :277-278 SwiGLU, :689-711 pre-norm residual) and the engine's own
+restatement (prefilling_dllm_engine/prefilling_dllm/models/dream.py:26-237). Keys are stored in pages AFTER RoPE, like
+the engine does (models/dream.py:88-101 → attention_v4.py:330-331), so a page is valid for exactly the positions it was
+written with.
+"""
+
+from __future__ import annotations
+
+import json
+import math
+import os
+import threading
+from collections import deque
+from dataclasses import dataclass
+from typing import Dict, List, Optional, Sequence, Tuple
+
+import torch
+import torch.nn.functional as F
+
+from . import ops
+
+
+@dataclass
+class DreamArch:
+    vocab_size: int
+    hidden_size: int
+    intermediate_size: int
+    num_hidden_layers: int
+    num_attention_heads: int
+    num_key_value_heads: int
+    rms_norm_eps: float = 1e-6
+    rope_theta: float = 1000000.0
+    max_position_embeddings: int = 131072
+    mask_token_id: int = 151666
+    bos_token_id: Optional[int] = 151643
+    eos_token_id: Optional[int] = 151643
+    initializer_range: float = 0.02
+    attention_bias: bool = True   # Dream: biased q/k/v; LLaDA-8B: none
+    logit_shift: bool = True      # Dream predicts token p from logits[p-1]; LLaDA does not shift
+
+    @property
+    def head_dim(self) -> int:
+        return self.hidden_size // self.num_attention_heads
+
+    @classmethod
+    def from_pretrained(cls, path: str) -> "DreamArch":
+        with open(os.path.join(path, "config.json")) as handle:
+            data = json.load(handle)
+        names = {f for f in cls.__dataclass_fields__}
+        return cls(**{k: v for k, v in data.items() if k in names})
+
+    @classmethod
+    def toy(cls) -> "DreamArch":
+        """BASELINE config 'CPU toy'."""
+        return cls(vocab_size=1024, hidden_size=256, intermediate_size=688, num_hidden_layers=2, num_attention_heads=4,
+                   num_key_value_heads=2, rope_theta=1e6, max_position_embeddings=32768, mask_token_id=1023,
+                   bos_token_id=1, eos_token_id=2)
+
+    @classmethod
+    def dream_7b(cls) -> "DreamArch":
+        return cls(vocab_size=152064, hidden_size=3584, intermediate_size=18944, num_hidden_layers=28,
+                   num_attention_heads=28, num_key_value_heads=4, rope_theta=1e6, mask_token_id=151666,
+                   bos_token_id=151643, eos_token_id=151643)
+
+    @classmethod
+    def llada_8b(cls) -> "DreamArch":
+        return cls(vocab_size=126464, hidden_size=4096, intermediate_size=12288, num_hidden_layers=32,
+                   num_attention_heads=32, num_key_value_heads=32, rope_theta=500000.0, rms_norm_eps=1e-5,
+                   mask_token_id=126336, bos_token_id=126080, eos_token_id=126081, attention_bias=False, logit_shift=False)
+
+
+class PageAllocator:
+    """Free-list page allocator with reference counts and a whole-prompt prefix cache.
+
+    Same behaviour as _PrefixPageAllocator (prefilling_dllm_engine/prefilling_dllm/fastdllm_engine.py:88-167): FIFO free
+    list, RuntimeError when pages run out, prefixes keyed by a 64-bit hash of the prompt ids, `evict_one` drops a
+    cached prefix nobody uses. Thread-safe (prefill may run on the pd-prefetch thread while decode runs on the main one).
+    """
+
+    def __init__(self, num_pages: int, page_size: int):
+        self.num_pages = int(num_pages)
+        self.page_size = int(page_size)
+        self.free_pages = deque(range(self.num_pages))
+        self.page_ref_count = [0] * self.num_pages
+        self.hash_to_prefix: Dict[int, "CachedPrefix"] = {}
+        self._lock = threading.RLock()
+
+    @staticmethod
+    def compute_prompt_hash(prompt_ids: Sequence[int]) -> int:
+        import numpy as np
+
+        data = np.array(list(prompt_ids), dtype=np.int64).tobytes()
+        try:
+            import xxhash
+
+            return xxhash.xxh64(data).intdigest()
+        except ImportError:  # same role, different 64-bit hash
+            import hashlib
+
+            return int.from_bytes(hashlib.blake2b(data, digest_size=8).digest(), "little")
+
+    @property
+    def num_free_pages(self) -> int:
+        with self._lock:
+            return len(self.free_pages)
+
+    def allocate_pages(self, n: int) -> List[int]:
+        with self._lock:
+            if n > len(self.free_pages):
+                raise RuntimeError(f"Cannot allocate {n} pages, only {len(self.free_pages)} free")
+            pages = [self.free_pages.popleft() for _ in range(n)]
+            for p in pages:
+                self.page_ref_count[p] = 1
+            return pages
+
+    def ref_pages(self, pages: Sequence[int]) -> None:
+        with self._lock:
+            for p in pages:
+                self.page_ref_count[p] += 1
+
+    def release_pages(self, pages: Sequence[int]) -> None:
+        with self._lock:
+            for p in pages:
+                self.page_ref_count[p] -= 1
+                if self.page_ref_count[p] == 0:
+                    self.free_pages.append(p)
+
+    def lookup_prefix(self, prompt_ids: Sequence[int]):
+        with self._lock:
+            return self.hash_to_prefix.get(self.compute_prompt_hash(prompt_ids))
+
+    def register_prefix(self, prompt_ids, page_ids, prompt_len, last_context_logit):
+        with self._lock:
+            h = self.compute_prompt_hash(prompt_ids)
+            entry = CachedPrefix(prompt_hash=h, page_ids=list(page_ids), prompt_len=prompt_len,
+                                 last_context_logit=last_context_logit.detach(), ref_count=0)
+            self.hash_to_prefix[h] = entry
+            return entry
+
+    def release_prefix(self, prompt_ids) -> None:
+        with self._lock:
+            entry = self.hash_to_prefix.get(self.compute_prompt_hash(prompt_ids))
+            if entry is not None:
+                entry.ref_count -= 1
+
+    def evict_one(self) -> bool:
+        with self._lock:
+            for h, entry in list(self.hash_to_prefix.items()):
+                if entry.ref_count <= 0:
+                    self.release_pages(entry.page_ids)
+                    del self.hash_to_prefix[h]
+                    return True
+            return False
+
+    def ensure_free(self, n: int) -> None:
+        """Evict unused cached prefixes until n pages are free (or nothing is left to evict)."""
+        while self.num_free_pages < n:
+            if not self.evict_one():
+                break
+
+
+@dataclass
+class CachedPrefix:
+    prompt_hash: int
+    page_ids: List[int]
+    prompt_len: int
+    last_context_logit: torch.Tensor
+    ref_count: int = 1
+
+
+def slots_for(page_ids: Sequence[int], start_token: int, num_tokens: int, page_size: int) -> List[int]:
+    """Pool slots of logical tokens [start_token, start_token + num_tokens) laid over `page_ids`."""
+    return [page_ids[t // page_size] * page_size + t % page_size for t in range(start_token, start_token + num_tokens)]
+
+
+class PagedDreamModel:
+    """Weights + paged KV pool + forward. One instance per device."""
+
+    def __init__(self, arch: DreamArch, state: Dict[str, torch.Tensor], *, device, dtype: torch.dtype,
+                 num_pages: int, page_size: int = 256):
+        if not torch.cuda.is_available():
+            raise RuntimeError("PagedDreamModel needs a CUDA device; there is no CPU path")
+        self.arch = arch
+        self.device = torch.device(device)
+        self.dtype = dtype
+        self.page_size = int(page_size)
+        self.num_pages = int(num_pages)
+        a = arch
+        dev, dt = self.device, dtype
+
+        def get(name):
+            return state[name].to(device=dev, dtype=dt).contiguous()
+
+        self.embed = get("model.embed_tokens.weight")
+        self.final_norm = get("model.norm.weight")
+        self.lm_head = get("lm_head.weight") if "lm_head.weight" in state else self.embed
+        self.layers = []
+        for i in range(a.num_hidden_layers):
+            p = f"model.layers.{i}."
+            wqkv = torch.cat([get(p + "self_attn.q_proj.weight"), get(p + "self_attn.k_proj.weight"), get(p + "self_attn.v_proj.weight")], dim=0)
+            bqkv = None
+            if a.attention_bias and (p + "self_attn.q_proj.bias") in state:
+                bqkv = torch.cat([get(p + "self_attn.q_proj.bias"), get(p + "self_attn.k_proj.bias"), get(p + "self_attn.v_proj.bias")], dim=0)
+            self.layers.append(dict(
+                ln1=get(p + "input_layernorm.weight"), ln2=get(p + "post_attention_layernorm.weight"),
+                wqkv=wqkv.contiguous(), bqkv=bqkv, wo=get(p + "self_attn.o_proj.weight"),
+                wgu=torch.cat([get(p + "mlp.gate_proj.weight"), get(p + "mlp.up_proj.weight")], dim=0).contiguous(),
+                wd=get(p + "mlp.down_proj.weight")))
+        self.inv_freq = (1.0 / (a.rope_theta ** (torch.arange(0, a.head_dim, 2, dtype=torch.int64).float() / a.head_dim))).to(dev)
+        # pool [2 (k,v), layers, pages, page_size, Hkv, D] — same shape as the engine's kv_cache (engine/model_runner.py:557-567)
+        self.kv_cache = torch.zeros((2, a.num_hidden_layers, self.num_pages, self.page_size, a.num_key_value_heads, a.head_dim),
+                                    dtype=dt, device=dev)
+        self.allocator = PageAllocator(self.num_pages, self.page_size)
+        self.scale = a.head_dim ** -0.5
+
+    # ---- construction helpers ----
+    @classmethod
+    def from_pretrained(cls, path: str, *, device, dtype: torch.dtype, num_pages: int, page_size: int = 256, arch: Optional[DreamArch] = None):
+        from safetensors.torch import load_file
+
+        arch = arch or DreamArch.from_pretrained(path)
+        files = sorted(f for f in os.listdir(path) if f.endswith(".safetensors"))
+        state: Dict[str, torch.Tensor] = {}
+        for name in files:
+            state.update(load_file(os.path.join(path, name)))
+        return cls(arch, state, device=device, dtype=dtype, num_pages=num_pages, page_size=page_size)
+
+    @classmethod
+    def random_init(cls, arch: DreamArch, *, device, dtype: torch.dtype, num_pages: int, page_size: int = 256, seed: int = 0):
+        """Seeded N(0, initializer_range) linears/embeddings, unit norms, zero biases, generated ON the device layer by
+        layer (a 7B random model never exists on the host). Not bit-identical to a CPU-seeded checkpoint: use
+        from_pretrained when weights must match another implementation."""
+        dev = torch.device(device)
+        g = torch.Generator(device=dev).manual_seed(seed)
+        a = arch
+        std = a.initializer_range
+
+        def w(*shape):
+            return (torch.randn(*shape, generator=g, device=dev, dtype=torch.float32) * std).to(dtype)
+
+        kv = a.num_key_value_heads * a.head_dim
+        state = {"model.embed_tokens.weight": w(a.vocab_size, a.hidden_size), "lm_head.weight": w(a.vocab_size, a.hidden_size),
+                 "model.norm.weight": torch.ones(a.hidden_size, device=dev, dtype=dtype)}
+        for i in range(a.num_hidden_layers):
+            p = f"model.layers.{i}."
+            state[p + "self_attn.q_proj.weight"] = w(a.hidden_size, a.hidden_size)
+            state[p + "self_attn.k_proj.weight"] = w(kv, a.hidden_size)
+            state[p + "self_attn.v_proj.weight"] = w(kv, a.hidden_size)
+            if a.attention_bias:
+                state[p + "self_attn.q_proj.bias"] = torch.zeros(a.hidden_size, device=dev, dtype=dtype)
+                state[p + "self_attn.k_proj.bias"] = torch.zeros(kv, device=dev, dtype=dtype)
+                state[p + "self_attn.v_proj.bias"] = torch.zeros(kv, device=dev, dtype=dtype)
+            state[p + "self_attn.o_proj.weight"] = w(a.hidden_size, a.hidden_size)
+            state[p + "mlp.gate_proj.weight"] = w(a.intermediate_size, a.hidden_size)
+            state[p + "mlp.up_proj.weight"] = w(a.intermediate_size, a.hidden_size)
+            state[p + "mlp.down_proj.weight"] = w(a.hidden_size, a.intermediate_size)
+            state[p + "input_layernorm.weight"] = torch.ones(a.hidden_size, device=dev, dtype=dtype)
+            state[p + "post_attention_layernorm.weight"] = torch.ones(a.hidden_size, device=dev, dtype=dtype)
+        return cls(arch, state, device=dev, dtype=dtype, num_pages=num_pages, page_size=page_size)
+
+    # ---- pieces ----
+    def _rmsnorm(self, x: torch.Tensor, weight: torch.Tensor) -> torch.Tensor:
+        xf = x.float()
+        xf = xf * torch.rsqrt(xf.pow(2).mean(-1, keepdim=True) + self.arch.rms_norm_eps)
+        return weight * xf.to(x.dtype)
+
+    def _rope_tables(self, positions: torch.Tensor) -> Tuple[torch.Tensor, torch.Tensor]:
+        freqs = positions.float().unsqueeze(-1) * self.inv_freq.unsqueeze(0)  # [T, D/2] fp32
+        emb = torch.cat((freqs, freqs), dim=-1)
+        return emb.cos().to(self.dtype).unsqueeze(1), emb.sin().to(self.dtype).unsqueeze(1)  # [T, 1, D]
+
+    @staticmethod
+    def _rotate_half(x: torch.Tensor) -> torch.Tensor:
+        half = x.shape[-1] // 2
+        return torch.cat((-x[..., half:], x[..., :half]), dim=-1)
+
+    def layer_cache(self, layer: int) -> Tuple[torch.Tensor, torch.Tensor]:
+        return self.kv_cache[0, layer], self.kv_cache[1, layer]
+
+    # ---- forward ----
+    @torch.inference_mode()
+    def forward(self, ids: torch.Tensor, positions: torch.Tensor, *, cu_seqlens: torch.Tensor, max_query_len: int,
+                slot_mapping: Optional[torch.Tensor] = None, block_table: Optional[torch.Tensor] = None,
+                seq_lens: Optional[torch.Tensor] = None, max_seq_len: int = 0, causal: bool = False,
+                logit_rows: Optional[torch.Tensor] = None, want_logits: bool = True,
+                capture_qk_layers: Optional[Sequence[int]] = None):
+        """Packed forward of `ids` [T] (several sequences delimited by cu_seqlens) at RoPE `positions` [T].
+
+        slot_mapping [T] int32 (optional): where each row's K/V goes in the pool (-1 = do not store).
+        block_table / seq_lens (optional): cached context each sequence attends before its own rows.
+        causal: scoring mask (row sees itself and earlier rows); otherwise rows see each other bidirectionally.
+        logit_rows: indices of the rows whose logits are wanted (LM head runs on those rows only).
+        capture_qk_layers: layers whose rotated (q, k) are returned for the eviction scorer.
+        Returns (logits or None, {layer: (q, k)}).
+        """
+        a = self.arch
+        hq, hkv, d = a.num_attention_heads, a.num_key_value_heads, a.head_dim
+        x = self.embed[ids]                                              # [T, hidden]
+        cos, sin = self._rope_tables(positions)
+        captured = {}
+        capture = set(capture_qk_layers) if capture_qk_layers is not None else ()
+        total = ids.numel()
+        attn_out = torch.empty((total, hq, d), dtype=self.dtype, device=self.device)
+        for li, w in enumerate(self.layers):
+            h = self._rmsnorm(x, w["ln1"])
+            qkv = F.linear(h, w["wqkv"], w["bqkv"])
+            q = qkv[:, : hq * d].view(total, hq, d)
+            k = qkv[:, hq * d: (hq + hkv) * d].view(total, hkv, d)
+            v = qkv[:, (hq + hkv) * d:].view(total, hkv, d)
+            q = (q * cos + self._rotate_half(q) * sin).contiguous()
+            k = (k * cos + self._rotate_half(k) * sin).contiguous()
+            v = v.contiguous()
+            if li in capture:
+                captured[li] = (q, k)
+            k_cache, v_cache = self.layer_cache(li)
+            if slot_mapping is not None:
+                ops.store_kvcache_unified_layout(k, v, k_cache, v_cache, slot_mapping, "diffusion_lm")
+            if block_table is not None:
+                ops.paged_attention(q, k, v, attn_out, cu_seqlens_q=cu_seqlens, max_query_len=max_query_len, key_cache=k_cache,
+                                    value_cache=v_cache, block_table=block_table, seq_lens=seq_lens, max_seq_len=max_seq_len,
+                                    sm_scale=self.scale, causal=causal, bidirectional=True)
+            else:
+                ops.paged_attention(q, k, v, attn_out, cu_seqlens_q=cu_seqlens, max_query_len=max_query_len,
+                                    sm_scale=self.scale, causal=causal, bidirectional=True)
+            x = x + F.linear(attn_out.view(total, hq * d), w["wo"])
+            h = self._rmsnorm(x, w["ln2"])
+            gu = F.linear(h, w["wgu"])
+            inter = a.intermediate_size
+            x = x + F.linear(F.silu(gu[:, :inter]) * gu[:, inter:], w["wd"])
+        logits = None
+        if want_logits:
+            rows = x if logit_rows is None else x.index_select(0, logit_rows)
+            logits = F.linear(self._rmsnorm(rows, self.final_norm), self.lm_head)
+        return logits, captured
+
+    # ---- small tensor helpers ----
+    def ids_tensor(self, ids: Sequence[int]) -> torch.Tensor:
+        return torch.tensor(list(ids), dtype=torch.long, device=self.device)
+
+    def i32(self, values: Sequence[int]) -> torch.Tensor:
+        return torch.tensor(list(values), dtype=torch.int32, device=self.device)

@@ -187,7 +187,7 @@ def paged_attention(query: torch.Tensor, key: torch.Tensor, value: torch.Tensor,
                     block_table: Optional[torch.Tensor] = None, seq_lens: Optional[torch.Tensor] = None,
                     max_seq_len: int = 0, sm_scale: Optional[float] = None, mask: Optional[torch.Tensor] = None,
                     causal: bool = False, bidirectional: bool = True, diffusion_blk_sz: int = 32,
-                    impl: str = "auto", num_splits: int = 0) -> str:
+                    impl: str = "auto", num_splits: int = 0, trace: Optional[torch.Tensor] = None) -> str:
     """New rows attend `[selected prefix pages (block-table order) ‖ new rows]`; writes `output` in place.
 
     query/output `[T, Hq, D]`, key/value `[T, Hkv, D]` (the new rows of all sequences, packed by
@@ -256,6 +256,10 @@ def paged_attention(query: torch.Tensor, key: torch.Tensor, value: torch.Tensor,
     p.impl = _IMPL_CODE[impl]
     p.num_splits = int(num_splits)
     p.status = status_word(device).data_ptr()
+    if trace is not None:  # profiling aid: zeroed int64 [8, 64, 8] buffer for the tcgen05 kernel's timestamps
+        if trace.dtype != torch.int64 or trace.numel() < 8 * 64 * 8 or not trace.is_cuda:
+            raise ValueError("trace must be a CUDA int64 tensor with at least 8*64*8 elements")
+        p.trace = trace.data_ptr()
     lib = _lib.load()
     chosen = lib.pdllm_attn_select_impl(ctypes.byref(p))
     if chosen < 0:
