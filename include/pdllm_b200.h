@@ -114,7 +114,7 @@ typedef struct pdllm_attn_params {
   const uint8_t* mask;          /* optional bool mask over new rows x new keys, sequence-LOCAL indices */
   int32_t* status;              /* optional device status word */
   void* workspace;              /* split-KV partials; pdllm_attn_workspace_bytes() */
-  void* trace;                  /* optional profiling aid of the tcgen05 kernel: int64 [8 CTAs][64 iterations][8 events]
+  void* trace;                  /* optional profiling aid of the tcgen05 kernel: int64 [8 CTAs][64 iterations][16 events]
                                    of clock64() timestamps, zero-initialised by the caller; NULL (the default) = off */
   int64_t workspace_bytes;
   int64_t q_stride, k_stride, v_stride, out_stride; /* row strides, elements */

@@ -41,7 +41,11 @@ constexpr int kSmemBytes = 3 * kTileBytes + 256 + 1024;  // + barriers + slack t
 constexpr long long kWaitLimitCycles = 1ll << 31;  // about a second
 constexpr float kRescaleThreshold = 8.0f;          // log2 units: rescale O only when the row max grew by > 2^8
 
-enum Bar { kQFull = 0, kKFull, kKEmpty, kVFull, kVEmpty, kSFull, kPFull, kPvDone, kNumBars };
+// every pipeline resource exists once per 64-key half b of the key tile: K_b, V_b, S_b/P_b (two interleaved streams)
+// S-full doubles as "K half free" and PV-done as "V half free" for the producer
+enum Bar { kQFull = 0, kKFull0, kKFull1, kVFull0, kVFull1, kSFull0, kSFull1, kPFull0, kPFull1, kPvDone0, kPvDone1, kNumBars };
+constexpr int kHalfN = kTileN / 2;  // keys per S buffer
+constexpr int kSlotBytes = kHalfN * kHeadDim * 2;  // one K_b or V_b slot: [2 halves of the head dim][64 keys][128 B] = 16 KB
 
 struct Args {
   void* out;
@@ -77,11 +81,15 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
   return ok != 0;
 }
 // Bounded wait. Returns false when another role already gave up or when the limit expired.
+template <bool kBackoff = false>
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volatile int* abort_flag, int32_t* status) {
   if (mbar_try_wait(bar, parity)) return true;
   long long t0 = clock64();
   uint32_t spins = 0;
   while (!mbar_try_wait(bar, parity)) {
+    // the producer and MMA warps share their scheduler with a softmax warp: sleep between polls instead of
+    // competing with it for issue slots
+    if (kBackoff) __nanosleep(40);
     if (((++spins) & 0x3f) == 0) {
       if (*abort_flag) return false;
       if (clock64() - t0 > kWaitLimitCycles) {
@@ -111,6 +119,13 @@ __device__ __forceinline__ void tma_load_4d(const CUtensorMap* map, uint64_t* ba
   asm volatile(
       "cp.async.bulk.tensor.4d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%3, %4, %5, %6}], [%2];"
       ::"r"(smem_u32(dst)), "l"(reinterpret_cast<uint64_t>(map)), "r"(smem_u32(bar)), "r"(c0), "r"(c1), "r"(c2), "r"(c3)
+      : "memory");
+}
+
+__device__ __forceinline__ void tma_load_5d(const CUtensorMap* map, uint64_t* bar, void* dst, int c0, int c1, int c2, int c3, int c4) {
+  asm volatile(
+      "cp.async.bulk.tensor.5d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%3, %4, %5, %6, %7}], [%2];"
+      ::"r"(smem_u32(dst)), "l"(reinterpret_cast<uint64_t>(map)), "r"(smem_u32(bar)), "r"(c0), "r"(c1), "r"(c2), "r"(c3), "r"(c4)
       : "memory");
 }
 
@@ -200,14 +215,14 @@ __device__ __forceinline__ uint64_t desc_mnmajor_sw128(uint32_t saddr, uint32_t 
          (1ull << 46) | (2ull << 61);
 }
 // instruction descriptor, kind::f16: fp32 accumulate, A/B bf16 (1) or fp16 (0), M=128, N=128
-__host__ __device__ constexpr uint32_t make_idesc(bool bf16, bool b_mn_major) {
+__host__ __device__ constexpr uint32_t make_idesc(bool bf16, bool b_mn_major, int n) {
   return (1u << 4) | ((bf16 ? 1u : 0u) << 7) | ((bf16 ? 1u : 0u) << 10) | ((b_mn_major ? 1u : 0u) << 16) |
-         ((kTileN >> 3) << 17) | ((kTileM >> 4) << 24);
+         (static_cast<uint32_t>(n >> 3) << 17) | ((kTileM >> 4) << 24);
 }
 
 // Optional timestamps (clock64) of CTA 0..7 for profiling the pipeline: trace[cta][iteration][event].
 #define PDLLM_TRACE_ON (a.trace != nullptr)
-constexpr int kTraceEvents = 8;
+constexpr int kTraceEvents = 16;
 constexpr int kTraceIters = 64;
 constexpr int kTraceCtas = 8;
 __device__ __forceinline__ void trace_event(const Args& a, int it, int ev) {
@@ -244,7 +259,7 @@ attn_sm100_kernel(const __grid_constant__ CUtensorMap q_map, const __grid_consta
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + kSmemBar);
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + kSmemBar + 128);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + kSmemBar + 136);
-  volatile int* tile_flags = reinterpret_cast<volatile int*>(smem + kSmemBar + 144);  // [2]: page of the tile in flight was unreadable
+  volatile int* tile_flags = reinterpret_cast<volatile int*>(smem + kSmemBar + 144);  // [4]: page of tile (it & 3) was unreadable
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
@@ -292,7 +307,7 @@ attn_sm100_kernel(const __grid_constant__ CUtensorMap q_map, const __grid_consta
   // ---- set-up: barriers, TMEM ----
   if (warp == 4) {
     if (lane == 0) {
-      for (int i = 0; i < kNumBars; ++i) mbar_init(&bars[i], i == kPFull ? 128u : 1u);
+      for (int i = 0; i < kNumBars; ++i) mbar_init(&bars[i], (i == kPFull0 || i == kPFull1) ? 128u : 1u);
       abort_flag[0] = 0;
       abort_flag[1] = 0;  // never set: lets the producer's drain waits run although abort_flag[0] is up
       fence_barrier_init();
@@ -305,116 +320,149 @@ attn_sm100_kernel(const __grid_constant__ CUtensorMap q_map, const __grid_consta
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
 
-  const uint32_t idesc_qk = make_idesc(a.is_bf16 != 0, false);
-  const uint32_t idesc_pv = make_idesc(a.is_bf16 != 0, true);
+  const uint32_t idesc_qk = make_idesc(a.is_bf16 != 0, false, kHalfN);    // S_b[128 x 64] = Q[128 x 128] K_b^T
+  const uint32_t idesc_pv = make_idesc(a.is_bf16 != 0, true, kHeadDim);   // O[128 x 128] += P_b[128 x 64] V_b
 
   if (warp == 4) {
     // =========================== TMA producer ===========================
+    // One thread issues every copy, in the order in which the MMA pipeline frees the slots:
+    //   V_0(t+1) after P·V_0(t), K_0(t+2) after Q·K_0(t+1), V_1(t+1) after P·V_1(t), K_1(t+2) after Q·K_1(t+1).
     if (lane == 0) {
       const uint32_t q_bytes = 2u * 64u * 2u * static_cast<uint32_t>(G * a.tpt);
       mbar_expect_tx(&bars[kQFull], q_bytes);
       tma_load_3d(&q_map, &bars[kQFull], smem + kSmemQ, 0, kvh * G, q_start + tok0);
       tma_load_3d(&q_map, &bars[kQFull], smem + kSmemQ + kHalfBytes, 64, kvh * G, q_start + tok0);
-      bool ok = true;
-      int issued = 0;
-      for (int it = 0; it < n_iter && ok; ++it) {
-        const uint32_t ph = it & 1;
+
+      // K_b / V_b of tile `it`: rows [64b, 64b+64) of both 64-column halves of the head dimension
+      auto load_half = [&](bool is_v, int it, int b) {
         const TileInfo ti = tile_info(t_begin + it, n_ctx_tiles, ctx_len, new_end);
-        int page = 0, off = 0;
+        uint64_t* bar = &bars[(is_v ? kVFull0 : kKFull0) + b];
+        uint8_t* dst = smem + (is_v ? kSmemV : kSmemK) + b * kSlotBytes;
+        mbar_expect_tx(bar, kSlotBytes);
+        // one copy per slot: the tensor maps put the two 64-column halves of the head dimension in their outermost
+        // box dimension, so the slot receives [half][64 keys][128 B]
         if (ti.is_ctx) {
           const int pidx = ti.key0 / a.page_size;
-          off = ti.key0 - pidx * a.page_size;
-          page = (pidx < a.max_pages) ? a.block_table[seq * a.block_table_stride + pidx] : -1;
-        }
-        const bool bad_page = ti.is_ctx && (page < 0 || page >= a.num_pages);
-        if (bad_page) {
-          report_status(a.status, PDLLM_S_BAD_PAGE);
-          page = 0;  // keep the copy in bounds; the softmax warps hide the whole tile
-        }
-        ok = mbar_wait(&bars[kKEmpty], ph ^ 1, abort_flag, a.status);
-        if (!ok) break;
-        tile_flags[ph] = bad_page ? 1 : 0;  // published to the softmax warps through the barrier chain K-full → S-full
-        if (PDLLM_TRACE_ON) trace_event(a, it, 5);
-        mbar_expect_tx(&bars[kKFull], kTileBytes);
-        if (ti.is_ctx) {
-          tma_load_4d(&kc_map, &bars[kKFull], smem + kSmemK, 0, kvh, off, page);
-          tma_load_4d(&kc_map, &bars[kKFull], smem + kSmemK + kHalfBytes, 64, kvh, off, page);
+          const int off = ti.key0 - pidx * a.page_size + b * kHalfN;
+          int page = (pidx < a.max_pages) ? a.block_table[seq * a.block_table_stride + pidx] : -1;
+          const bool bad_page = page < 0 || page >= a.num_pages;
+          if (bad_page) {
+            report_status(a.status, PDLLM_S_BAD_PAGE);
+            page = 0;  // keep the copy in bounds; the softmax warps hide the whole tile
+          }
+          if (!is_v && b == 0) tile_flags[it & 3] = bad_page ? 1 : 0;  // reaches the softmax warps through K-full → S-full
+          tma_load_5d(is_v ? &vc_map : &kc_map, bar, dst, 0, off, 0, kvh, page);
         } else {
-          tma_load_3d(&kn_map, &bars[kKFull], smem + kSmemK, 0, kvh, q_start + ti.key0);
-          tma_load_3d(&kn_map, &bars[kKFull], smem + kSmemK + kHalfBytes, 64, kvh, q_start + ti.key0);
+          if (!is_v && b == 0) tile_flags[it & 3] = 0;
+          tma_load_4d(is_v ? &vn_map : &kn_map, bar, dst, 0, q_start + ti.key0 + b * kHalfN, 0, kvh);
         }
-        ok = mbar_wait(&bars[kVEmpty], ph ^ 1, abort_flag, a.status);
-        if (!ok) { issued = it * 2 + 1; break; }
-        if (PDLLM_TRACE_ON) trace_event(a, it, 6);
-        mbar_expect_tx(&bars[kVFull], kTileBytes);
-        if (ti.is_ctx) {
-          tma_load_4d(&vc_map, &bars[kVFull], smem + kSmemV, 0, kvh, off, page);
-          tma_load_4d(&vc_map, &bars[kVFull], smem + kSmemV + kHalfBytes, 64, kvh, off, page);
-        } else {
-          tma_load_3d(&vn_map, &bars[kVFull], smem + kSmemV, 0, kvh, q_start + ti.key0);
-          tma_load_3d(&vn_map, &bars[kVFull], smem + kSmemV + kHalfBytes, 64, kvh, q_start + ti.key0);
+      };
+      load_half(false, 0, 0);
+      load_half(false, 0, 1);
+      load_half(true, 0, 0);
+      load_half(true, 0, 1);
+      bool ok = true;
+      if (n_iter > 1) {
+        for (int b = 0; b < 2 && ok; ++b) {
+          ok = mbar_wait<true>(&bars[kSFull0 + b], 0, abort_flag, a.status);  // Q·K_b(0) done: the K_b slot is free
+          if (ok) load_half(false, 1, b);
         }
-        issued = it * 2 + 2;
       }
-      if (!ok && issued > 0) {
-        // Gave up mid-way: let the copies already in flight land before the CTA retires.
-        const int it_k = (issued - 1) / 2;
-        (void)mbar_wait(&bars[kKFull], it_k & 1, abort_flag + 1, nullptr);
-        if ((issued & 1) == 0) (void)mbar_wait(&bars[kVFull], it_k & 1, abort_flag + 1, nullptr);
+      for (int it = 0; it < n_iter && ok; ++it) {
+        const uint32_t ph = it & 1;
+        for (int b = 0; b < 2 && ok; ++b) {
+          if (it + 1 < n_iter) {
+            ok = mbar_wait<true>(&bars[kPvDone0 + b], ph, abort_flag, a.status);       // P·V_b(it) done: the V_b slot is free
+            if (PDLLM_TRACE_ON) trace_event(a, it, 8 + b);
+            if (ok) load_half(true, it + 1, b);
+          }
+          if (ok && it + 2 < n_iter) {
+            ok = mbar_wait<true>(&bars[kSFull0 + b], ph ^ 1, abort_flag, a.status);    // Q·K_b(it+1) done: the K_b slot is free
+            if (PDLLM_TRACE_ON) trace_event(a, it, 10 + b);
+            if (ok) load_half(false, it + 2, b);
+          }
+        }
+      }
+      // Every copy issued above is consumed by an MMA that the epilogue waits for, unless a wait gave up; then the
+      // CTA is abandoning its result and only has to let copies in flight land: give them a bounded moment.
+      if (!ok) {
+        const long long t0 = clock64();
+        while (clock64() - t0 < 200000) { }
       }
     }
     __syncwarp();
   } else if (warp == 5) {
     // =========================== MMA issuer ===========================
+    // Software-pipelined over the two S buffers: ... PV_0(t), QK_0(t+1), PV_1(t), QK_1(t+1) ... so that the next
+    // tile's scores for buffer b are produced while the softmax warps still work on buffer b^1.
     const uint32_t sq = smem_u32(smem + kSmemQ), sk = smem_u32(smem + kSmemK), sv = smem_u32(smem + kSmemV);
-    const uint32_t tS = tmem_base + kColS, tO = tmem_base + kColO;
-    bool ok = mbar_wait(&bars[kQFull], 0, abort_flag, a.status);
+    const uint32_t tO = tmem_base + kColO;
+    auto issue_qk = [&](int b) {   // S_b = Q K[64b .. 64b+64)^T
+      const uint32_t tSb = tmem_base + kColS + b * kHalfN;
+#pragma unroll
+      for (int kk = 0; kk < kHeadDim / 16; ++kk) {
+        const uint32_t koff = (kk >> 2) * kHalfBytes + (kk & 3) * 32;
+        const uint32_t kboff = b * kSlotBytes + (kk >> 2) * (kSlotBytes / 2) + (kk & 3) * 32;
+        umma_ss(tSb, desc_kmajor_sw128(sq + koff), desc_kmajor_sw128(sk + kboff), idesc_qk, kk > 0 ? 1u : 0u);
+      }
+      umma_commit(&bars[kSFull0 + b]);
+    };
+    bool ok = mbar_wait<true>(&bars[kQFull], 0, abort_flag, a.status);
+    for (int b = 0; b < 2 && ok; ++b) {
+      ok = mbar_wait<true>(&bars[kKFull0 + b], 0, abort_flag, a.status);
+      if (!ok) break;
+      tc_fence_after();
+      if (lane == 0) issue_qk(b);
+      __syncwarp();
+    }
     for (int it = 0; it < n_iter && ok; ++it) {
       const uint32_t ph = it & 1;
       const TileInfo ti = tile_info(t_begin + it, n_ctx_tiles, ctx_len, new_end);
-      ok = mbar_wait(&bars[kKFull], ph, abort_flag, a.status);
-      if (ok && it > 0) ok = mbar_wait(&bars[kPvDone], (it - 1) & 1, abort_flag, a.status);  // S/P columns free again
-      if (!ok) break;
-      tc_fence_after();
-      if (PDLLM_TRACE_ON) trace_event(a, it, 3);
-      if (lane == 0) {
+      const bool has_next = it + 1 < n_iter;
 #pragma unroll
-        for (int kk = 0; kk < kHeadDim / 16; ++kk) {
-          const uint32_t koff = (kk >> 2) * kHalfBytes + (kk & 3) * 32;
-          umma_ss(tS, desc_kmajor_sw128(sq + koff), desc_kmajor_sw128(sk + koff), idesc_qk, kk > 0 ? 1u : 0u);
+      for (int b = 0; b < 2; ++b) {
+        ok = mbar_wait<true>(&bars[kVFull0 + b], ph, abort_flag, a.status);
+        if (!ok) break;
+        if (PDLLM_TRACE_ON) trace_event(a, it, 12 + b);
+        if (ti.nvalid < (b + 1) * kHalfN) {
+          // Rows of V_b past the last valid key may hold anything (stale page contents, another sequence's
+          // rows); P is 0 there but 0 * NaN is NaN, so clear them before the MMA reads the half tile.
+          const int first = max(ti.nvalid, b * kHalfN);
+          const int n_rows = (b + 1) * kHalfN - first;
+          for (int i = lane; i < n_rows * 16; i += 32) {
+            const int r = first + (i >> 4) - b * kHalfN;  // row inside the slot
+            const int c = i & 15;
+            uint4* dst = reinterpret_cast<uint4*>(smem + kSmemV + b * kSlotBytes + (c >> 3) * (kSlotBytes / 2) + r * 128 + (c & 7) * 16);
+            *dst = make_uint4(0, 0, 0, 0);
+          }
+          fence_proxy_async();
+          __syncwarp();
         }
-        umma_commit(&bars[kSFull]);
-        umma_commit(&bars[kKEmpty]);
-      }
-      __syncwarp();
-      ok = mbar_wait(&bars[kVFull], ph, abort_flag, a.status);
-      if (!ok) break;
-      if (ti.nvalid < kTileN) {
-        // Rows of the V tile past the last valid key may hold anything (stale page contents, another
-        // sequence's rows); P is 0 there but 0 * NaN is NaN, so clear them before the MMA reads the tile.
-        const int n_rows = kTileN - ti.nvalid;
-        for (int i = lane; i < n_rows * 16; i += 32) {
-          const int r = ti.nvalid + (i >> 4);
-          const int c = i & 15;
-          uint4* dst = reinterpret_cast<uint4*>(smem + kSmemV + (c >> 3) * kHalfBytes + r * 128 + (c & 7) * 16);
-          *dst = make_uint4(0, 0, 0, 0);
+        ok = mbar_wait<true>(&bars[kPFull0 + b], ph, abort_flag, a.status);
+        if (!ok) break;
+        tc_fence_after();
+        if (PDLLM_TRACE_ON) trace_event(a, it, 4 + b);
+        if (lane == 0) {
+          const uint32_t tPb = tmem_base + kColS + b * kHalfN;
+#pragma unroll
+          for (int kk = 0; kk < kHalfN / 16; ++kk) {
+            umma_ts(tO, tPb + kk * 8, desc_mnmajor_sw128(sv + b * kSlotBytes + kk * 2048, kSlotBytes / 2), idesc_pv,
+                    (it > 0 || b > 0 || kk > 0) ? 1u : 0u);
+          }
+          umma_commit(&bars[kPvDone0 + b]);
         }
-        fence_proxy_async();
         __syncwarp();
-      }
-      ok = mbar_wait(&bars[kPFull], ph, abort_flag, a.status);
-      if (!ok) break;
-      tc_fence_after();
-      if (PDLLM_TRACE_ON) trace_event(a, it, 4);
-      if (lane == 0) {
-#pragma unroll
-        for (int kk = 0; kk < kTileN / 16; ++kk) {
-          umma_ts(tO, tS + kk * 8, desc_mnmajor_sw128(sv + kk * 2048, kHalfBytes), idesc_pv, (it > 0 || kk > 0) ? 1u : 0u);
+        if (has_next) {
+          ok = mbar_wait<true>(&bars[kKFull0 + b], ph ^ 1, abort_flag, a.status);
+          if (PDLLM_TRACE_ON) trace_event(a, it, 14 + b);
+          if (ok) ok = mbar_wait<true>(&bars[kPvDone0 + b], ph, abort_flag, a.status);  // S_b / P_b columns are free again
+          if (!ok) break;
+          tc_fence_after();
+          if (PDLLM_TRACE_ON) trace_event(a, it, 2 + b);
+          if (lane == 0) issue_qk(b);
+          __syncwarp();
         }
-        umma_commit(&bars[kPvDone]);
-        umma_commit(&bars[kVEmpty]);
       }
-      __syncwarp();
     }
   } else {
     // =========================== softmax + epilogue (warps 0-3) ===========================
@@ -435,86 +483,89 @@ attn_sm100_kernel(const __grid_constant__ CUtensorMap q_map, const __grid_consta
     float m_ref = -INFINITY;  // running reference maximum, log2 domain
     float l_run = 0.f;
     bool ok = true;
-    uint32_t s[kTileN];       // one row of S; later reused chunk-wise for O
+    uint32_t s[kHalfN];       // one row of one S buffer; the epilogue reuses it for O
     constexpr uint32_t kNegInf = 0xff800000u;
 
-    for (int it = 0; it < n_iter; ++it) {
+    for (int it = 0; it < n_iter && ok; ++it) {
       const uint32_t ph = it & 1;
       const TileInfo ti = tile_info(t_begin + it, n_ctx_tiles, ctx_len, new_end);
-      int cmax = ti.nvalid;  // columns [0, cmax) are visible to this row
-      if (!ti.is_ctx) cmax = min(cmax, row_new_end - ti.key0);
+      int cmax_tile = ti.nvalid;  // columns [0, cmax_tile) of the 128-key tile are visible to this row
+      if (!ti.is_ctx) cmax_tile = min(cmax_tile, row_new_end - ti.key0);
       const bool use_dense = dense_mask && !ti.is_ctx && row_valid;
       const uint8_t* mrow = use_dense ? a.mask + static_cast<int64_t>(m) * a.mask_stride_m + static_cast<int64_t>(ti.key0) * a.mask_stride_n : nullptr;
 
-      ok = mbar_wait(&bars[kSFull], ph, abort_flag, a.status);
-      if (!ok) break;
-      tc_fence_after();
-      if (PDLLM_TRACE_ON) trace_event(a, it, 0);
-
-      // the whole row of S in one TMEM round trip
-      tmem_ld32(tS + 0, s);
-      tmem_ld32(tS + 32, s + 32);
-      tmem_ld32(tS + 64, s + 64);
-      tmem_ld32(tS + 96, s + 96);
-      tc_wait_ld();
-      if (PDLLM_TRACE_ON) trace_event(a, it, 1);
-      if (tile_flags[ph]) cmax = 0;  // the producer could not read this tile's page: hide all of it
-      if (cmax < kTileN || use_dense) {
 #pragma unroll
-        for (int j = 0; j < kTileN; ++j) {
-          bool vis = j < cmax;
-          if (vis && use_dense) vis = mrow[j * a.mask_stride_n] != 0;
-          if (!vis) s[j] = kNegInf;
-        }
-      }
+      for (int b = 0; b < 2; ++b) {
+        const uint32_t tSb = tS + b * kHalfN;
+        ok = mbar_wait(&bars[kSFull0 + b], ph, abort_flag, a.status);
+        if (!ok) break;
+        tc_fence_after();
+        if (PDLLM_TRACE_ON) trace_event(a, it, b);
 
-      // row maximum, four independent chains
-      float mx0 = -INFINITY, mx1 = -INFINITY, mx2 = -INFINITY, mx3 = -INFINITY;
+        tmem_ld32(tSb, s);
+        tmem_ld32(tSb + 32, s + 32);
+        tc_wait_ld();
+        int cmax = cmax_tile - b * kHalfN;
+        if (tile_flags[it & 3]) cmax = 0;  // the producer could not read this tile's page: hide all of it
+        if (cmax < kHalfN || use_dense) {
 #pragma unroll
-      for (int j = 0; j < kTileN; j += 4) {
-        mx0 = fmaxf(mx0, __uint_as_float(s[j]));
-        mx1 = fmaxf(mx1, __uint_as_float(s[j + 1]));
-        mx2 = fmaxf(mx2, __uint_as_float(s[j + 2]));
-        mx3 = fmaxf(mx3, __uint_as_float(s[j + 3]));
-      }
-      const float m_tile = fmaxf(fmaxf(mx0, mx1), fmaxf(mx2, mx3)) * a.scale_log2;  // scale > 0: max commutes
-
-      // lazy rescale: only when the maximum grew by more than 2^8 (the first tile just sets the reference)
-      if (it == 0) {
-        m_ref = m_tile;
-      } else {
-        const bool grow = m_tile > m_ref + kRescaleThreshold;
-        if (__any_sync(0xffffffffu, grow)) {
-          const float m_new = grow ? m_tile : m_ref;
-          const float alpha = grow ? ex2(m_ref - m_new) : 1.f;  // m_ref = -inf gives 0
-          l_run *= alpha;
-          uint32_t o[16];
-#pragma unroll 1
-          for (int c = 0; c < kHeadDim / 16; ++c) {
-            tmem_ld16(tO + c * 16, o);
-            tc_wait_ld();
-#pragma unroll
-            for (int j = 0; j < 16; ++j) o[j] = __float_as_uint(__uint_as_float(o[j]) * alpha);
-            tmem_st16(tO + c * 16, o);
+          for (int j = 0; j < kHalfN; ++j) {
+            bool vis = j < cmax;
+            if (vis && use_dense) vis = mrow[(b * kHalfN + j) * a.mask_stride_n] != 0;
+            if (!vis) s[j] = kNegInf;
           }
-          tc_wait_st();
-          m_ref = m_new;
         }
-      }
-      const float m_use = (m_ref == -INFINITY) ? 0.f : m_ref;
 
-      // P = exp2(S*scale - m_ref) → bf16/fp16 pairs over the S columns (all of S is in registers by now)
-      float l0 = 0.f, l1 = 0.f, l2 = 0.f, l3 = 0.f;
+        // row maximum of this half, four independent chains
+        float mx0 = -INFINITY, mx1 = -INFINITY, mx2 = -INFINITY, mx3 = -INFINITY;
 #pragma unroll
-      for (int half = 0; half < 2; ++half) {
-        uint32_t packed[32];
+        for (int j = 0; j < kHalfN; j += 4) {
+          mx0 = fmaxf(mx0, __uint_as_float(s[j]));
+          mx1 = fmaxf(mx1, __uint_as_float(s[j + 1]));
+          mx2 = fmaxf(mx2, __uint_as_float(s[j + 2]));
+          mx3 = fmaxf(mx3, __uint_as_float(s[j + 3]));
+        }
+        const float m_half = fmaxf(fmaxf(mx0, mx1), fmaxf(mx2, mx3)) * a.scale_log2;  // scale > 0: max commutes
+
+        // lazy rescale: only when the maximum grew by more than 2^8 (the very first half just sets the reference)
+        if (it == 0 && b == 0) {
+          m_ref = m_half;
+        } else {
+          const bool grow = m_half > m_ref + kRescaleThreshold;
+          if (__any_sync(0xffffffffu, grow)) {
+            // O must hold every product issued so far: the previous half's P·V may still be in flight
+            const int pb = b ^ 1;
+            const uint32_t pph = (b == 1) ? ph : (ph ^ 1);
+            ok = mbar_wait(&bars[kPvDone0 + pb], pph, abort_flag, a.status);
+            if (!ok) break;
+            tc_fence_after();
+            const float m_new = grow ? m_half : m_ref;
+            const float alpha = grow ? ex2(m_ref - m_new) : 1.f;  // m_ref = -inf gives 0
+            l_run *= alpha;
+            uint32_t o[16];
+#pragma unroll 1
+            for (int c = 0; c < kHeadDim / 16; ++c) {
+              tmem_ld16(tO + c * 16, o);
+              tc_wait_ld();
 #pragma unroll
-        for (int j = 0; j < 64; j += 4) {
-          const int c = half * 64 + j;
-          const float p0 = ex2(fmaf(__uint_as_float(s[c]), a.scale_log2, -m_use));
-          const float p1 = ex2(fmaf(__uint_as_float(s[c + 1]), a.scale_log2, -m_use));
-          const float p2 = ex2(fmaf(__uint_as_float(s[c + 2]), a.scale_log2, -m_use));
-          const float p3 = ex2(fmaf(__uint_as_float(s[c + 3]), a.scale_log2, -m_use));
+              for (int j = 0; j < 16; ++j) o[j] = __float_as_uint(__uint_as_float(o[j]) * alpha);
+              tmem_st16(tO + c * 16, o);
+            }
+            tc_wait_st();
+            m_ref = m_new;
+          }
+        }
+        const float m_use = (m_ref == -INFINITY) ? 0.f : m_ref;
+
+        // P_b = exp2(S_b*scale - m_ref) → bf16/fp16 pairs over the first 32 columns of S_b
+        float l0 = 0.f, l1 = 0.f, l2 = 0.f, l3 = 0.f;
+        uint32_t packed[kHalfN / 2];
+#pragma unroll
+        for (int j = 0; j < kHalfN; j += 4) {
+          const float p0 = ex2(fmaf(__uint_as_float(s[j]), a.scale_log2, -m_use));
+          const float p1 = ex2(fmaf(__uint_as_float(s[j + 1]), a.scale_log2, -m_use));
+          const float p2 = ex2(fmaf(__uint_as_float(s[j + 2]), a.scale_log2, -m_use));
+          const float p3 = ex2(fmaf(__uint_as_float(s[j + 3]), a.scale_log2, -m_use));
           l0 += p0; l1 += p1; l2 += p2; l3 += p3;
           if (a.is_bf16) {
             __nv_bfloat162 h0 = __floats2bfloat162_rn(p0, p1), h1 = __floats2bfloat162_rn(p2, p3);
@@ -526,17 +577,17 @@ attn_sm100_kernel(const __grid_constant__ CUtensorMap q_map, const __grid_consta
             packed[(j >> 1) + 1] = *reinterpret_cast<uint32_t*>(&h1);
           }
         }
-        tmem_st32(tS + half * 32, packed);
+        tmem_st32(tSb, packed);
+        l_run += (l0 + l1) + (l2 + l3);
+        tc_wait_st();
+        tc_fence_before();
+        mbar_arrive(&bars[kPFull0 + b]);
+        if (PDLLM_TRACE_ON) trace_event(a, it, 6 + b);
       }
-      l_run += (l0 + l1) + (l2 + l3);
-      tc_wait_st();
-      tc_fence_before();
-      mbar_arrive(&bars[kPFull]);
-      if (PDLLM_TRACE_ON) trace_event(a, it, 2);
     }
 
     // ---- epilogue ----
-    if (ok) ok = mbar_wait(&bars[kPvDone], (n_iter - 1) & 1, abort_flag, a.status);
+    if (ok) ok = mbar_wait(&bars[kPvDone1], (n_iter - 1) & 1, abort_flag, a.status);  // in-order MMAs: PV_1 done implies all done
     if (ok) {
       tc_fence_after();
       if (a.num_splits == 1) {
@@ -765,21 +816,22 @@ inline int launch(const pdllm_attn_params* p, cudaStream_t stream) {
     if ((rc = encode_map(&q_map, bf16, p->q, 3, dims, str, box)) != 0) return rc;
   }
   {
-    uint64_t dims[3] = {static_cast<uint64_t>(kHeadDim), static_cast<uint64_t>(p->num_kv_heads), static_cast<uint64_t>(p->total_q)};
-    uint32_t box[3] = {64, 1, kTileN};
-    uint64_t strk[2] = {static_cast<uint64_t>(kHeadDim) * 2, static_cast<uint64_t>(p->k_stride) * 2};
-    uint64_t strv[2] = {static_cast<uint64_t>(kHeadDim) * 2, static_cast<uint64_t>(p->v_stride) * 2};
-    if ((rc = encode_map(&kn_map, bf16, p->k_new, 3, dims, strk, box)) != 0) return rc;
-    if ((rc = encode_map(&vn_map, bf16, p->v_new, 3, dims, strv, box)) != 0) return rc;
+    // new K/V rows [T, Hkv, D] seen as (64 cols, T rows, 2 column halves, Hkv): one box = [2][64 rows][64 cols]
+    uint64_t dims[4] = {64, static_cast<uint64_t>(p->total_q), 2, static_cast<uint64_t>(p->num_kv_heads)};
+    uint32_t box[4] = {64, kHalfN, 2, 1};
+    uint64_t strk[3] = {static_cast<uint64_t>(p->k_stride) * 2, 128, static_cast<uint64_t>(kHeadDim) * 2};
+    uint64_t strv[3] = {static_cast<uint64_t>(p->v_stride) * 2, 128, static_cast<uint64_t>(kHeadDim) * 2};
+    if ((rc = encode_map(&kn_map, bf16, p->k_new, 4, dims, strk, box)) != 0) return rc;
+    if ((rc = encode_map(&vn_map, bf16, p->v_new, 4, dims, strv, box)) != 0) return rc;
   }
   if (has_cache) {
-    uint64_t dims[4] = {static_cast<uint64_t>(kHeadDim), static_cast<uint64_t>(p->num_kv_heads),
-                        static_cast<uint64_t>(p->page_size), static_cast<uint64_t>(p->num_pages)};
-    uint64_t str[3] = {static_cast<uint64_t>(kHeadDim) * 2, static_cast<uint64_t>(kHeadDim) * 2 * p->num_kv_heads,
-                       static_cast<uint64_t>(kHeadDim) * 2 * p->num_kv_heads * p->page_size};
-    uint32_t box[4] = {64, 1, kTileN, 1};
-    if ((rc = encode_map(&kc_map, bf16, p->k_cache, 4, dims, str, box)) != 0) return rc;
-    if ((rc = encode_map(&vc_map, bf16, p->v_cache, 4, dims, str, box)) != 0) return rc;
+    // pool [pages, page_size, Hkv, D] seen as (64 cols, page_size rows, 2 column halves, Hkv, pages)
+    const uint64_t row = static_cast<uint64_t>(kHeadDim) * 2 * p->num_kv_heads;
+    uint64_t dims[5] = {64, static_cast<uint64_t>(p->page_size), 2, static_cast<uint64_t>(p->num_kv_heads), static_cast<uint64_t>(p->num_pages)};
+    uint64_t str[4] = {row, 128, static_cast<uint64_t>(kHeadDim) * 2, row * p->page_size};
+    uint32_t box[5] = {64, kHalfN, 2, 1, 1};
+    if ((rc = encode_map(&kc_map, bf16, p->k_cache, 5, dims, str, box)) != 0) return rc;
+    if ((rc = encode_map(&vc_map, bf16, p->v_cache, 5, dims, str, box)) != 0) return rc;
   } else {
     kc_map = kn_map; vc_map = vn_map;  // never dereferenced: no context tiles exist
   }

@@ -256,9 +256,9 @@ def paged_attention(query: torch.Tensor, key: torch.Tensor, value: torch.Tensor,
     p.impl = _IMPL_CODE[impl]
     p.num_splits = int(num_splits)
     p.status = status_word(device).data_ptr()
-    if trace is not None:  # profiling aid: zeroed int64 [8, 64, 8] buffer for the tcgen05 kernel's timestamps
-        if trace.dtype != torch.int64 or trace.numel() < 8 * 64 * 8 or not trace.is_cuda:
-            raise ValueError("trace must be a CUDA int64 tensor with at least 8*64*8 elements")
+    if trace is not None:  # profiling aid: zeroed int64 [8, 64, 16] buffer for the tcgen05 kernel's timestamps
+        if trace.dtype != torch.int64 or trace.numel() < 8 * 64 * 16 or not trace.is_cuda:
+            raise ValueError("trace must be a CUDA int64 tensor with at least 8*64*16 elements")
         p.trace = trace.data_ptr()
     lib = _lib.load()
     chosen = lib.pdllm_attn_select_impl(ctypes.byref(p))
