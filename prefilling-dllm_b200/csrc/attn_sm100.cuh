@@ -1,16 +1,20 @@
 // Block-table attention on the 5th-generation tensor cores (sm_100a): tcgen05.mma with TMEM accumulators,
 // operands staged by TMA straight out of the paged pool (no gather), online softmax in registers.
 //
-// Work unit (one CTA): one GQA-packed query tile x one contiguous range of 128-key tiles.
+// Work unit (one CTA, one per SM): TWO GQA-packed query tiles of one (sequence, KV head) x one contiguous range
+// of 128-key tiles.
 //   * query tile  = up to 128 rows = tpt tokens x G query heads of one KV group (row = token*G + head), so the
-//     K/V pages of a KV head are read once for all G heads that share it;
+//     K/V pages of a KV head are read once for all G heads that share it, and once for both query tiles;
 //   * key tiles   = the sequence's selected prefix pages in block-table order (any physical order), then the new
 //     rows themselves; a KV split assigns each CTA a sub-range, partials are merged by attn_combine_kernel.
-// Roles: warps 0-3 softmax + epilogue (thread r owns tile row r = TMEM lane r), warp 4 TMA producer + TMEM
-// allocator, warp 5 MMA issuer. TMEM: columns [0,128) hold S (fp32) and then P (bf16 pairs, aliased over S),
-// columns [128,256) hold O (fp32) — 256 columns so two CTAs share an SM and one CTA's softmax overlaps the
-// other's MMAs. Shared memory per CTA: Q 32 KB + K 32 KB + V 32 KB, all in the 128-byte-swizzled layouts
-// that TMA writes and the MMA descriptors read.
+// Every key tile is processed as two 64-key halves b, so four chains (query tile X) x (half b) run interleaved:
+// while the softmax warps of X work on S_Xb, the tensor core computes P·V and the next Q·K of the other chains.
+// Roles: warps 0-3 softmax + epilogue of query tile A, warps 4-7 of query tile B (thread r owns tile row r = TMEM
+// lane r), warp 8 TMA producer + TMEM allocator, warps 9-12 MMA issuers (one per chain). TMEM (all 512 columns): S_A0 S_A1 S_B0 S_B1
+// (64 fp32 columns each; P, bf16 pairs, aliases the first 32) and O_A, O_B (128 columns each). Shared memory:
+// Q_A, Q_B 32 KB each, and two rings of four 16 KB slots for K and V half-tiles, all in the 128-byte-swizzled
+// layouts that TMA writes and the MMA descriptors read; the rings keep three copies in flight per operand,
+// which covers the ~2000-cycle latency of a TMA copy.
 // Every mbarrier wait is bounded; on expiry the CTA raises PDLLM_S_WAIT_TIMEOUT, drains and frees its TMEM.
 #pragma once
 
@@ -27,25 +31,35 @@ namespace tc {
 constexpr int kTileM = 128;
 constexpr int kTileN = 128;
 constexpr int kHeadDim = 128;
-constexpr int kThreads = 192;
-constexpr uint32_t kTmemCols = 256;
-constexpr uint32_t kColS = 0;
-constexpr uint32_t kColO = 128;
-constexpr int kHalfBytes = kTileN * 64 * 2;        // one [128 rows x 64 elems] swizzled sub-tile = 16 KB
-constexpr int kTileBytes = 2 * kHalfBytes;         // 32 KB
+constexpr int kHalfN = kTileN / 2;                  // keys per S buffer
+constexpr int kThreads = 416;                       // warps 0-7 softmax (two query tiles), warp 8 producer, warps 9-12 MMA issuers
+constexpr int kProducerWarp = 8;
+constexpr int kMmaWarp0 = 9;                       // one issuer warp per chain (query tile, key half)
+constexpr uint32_t kTmemCols = 512;
+constexpr uint32_t kColS = 0;                       // S_A0, S_A1, S_B0, S_B1: 64 columns each (P aliases the first 32)
+constexpr uint32_t kColO = 256;                     // O_A, O_B: 128 columns each
+constexpr int kHalfBytes = kTileM * 64 * 2;         // one [128 rows x 64 cols] swizzled half of a Q tile = 16 KB
+constexpr int kTileBytes = 2 * kHalfBytes;          // 32 KB per Q tile
+constexpr int kSlotBytes = kHalfN * kHeadDim * 2;   // one K_b or V_b slot: [2 halves of the head dim][64 keys][128 B] = 16 KB
+constexpr int kRing = 4;                            // slots per ring (K and V each): copies run up to 3 half-tiles ahead
 constexpr int kSmemQ = 0;
-constexpr int kSmemK = kTileBytes;
-constexpr int kSmemV = 2 * kTileBytes;
-constexpr int kSmemBar = 3 * kTileBytes;
-constexpr int kSmemBytes = 3 * kTileBytes + 256 + 1024;  // + barriers + slack to align the base to 1024 B
-constexpr long long kWaitLimitCycles = 1ll << 31;  // about a second
-constexpr float kRescaleThreshold = 8.0f;          // log2 units: rescale O only when the row max grew by > 2^8
+constexpr int kSmemK = 2 * kTileBytes;
+constexpr int kSmemV = kSmemK + kRing * kSlotBytes;
+constexpr int kSmemBar = kSmemV + kRing * kSlotBytes;
+constexpr int kSmemBytes = kSmemBar + 512 + 1024;   // + barriers/flags + slack to align the base to 1024 B
+constexpr long long kWaitLimitCycles = 1ll << 31;   // about a second
+constexpr float kRescaleThreshold = 8.0f;           // log2 units: rescale O only when the row max grew by > 2^8
 
-// every pipeline resource exists once per 64-key half b of the key tile: K_b, V_b, S_b/P_b (two interleaved streams)
-// S-full doubles as "K half free" and PV-done as "V half free" for the producer
-enum Bar { kQFull = 0, kKFull0, kKFull1, kVFull0, kVFull1, kSFull0, kSFull1, kPFull0, kPFull1, kPvDone0, kPvDone1, kNumBars };
-constexpr int kHalfN = kTileN / 2;  // keys per S buffer
-constexpr int kSlotBytes = kHalfN * kHeadDim * 2;  // one K_b or V_b slot: [2 halves of the head dim][64 keys][128 B] = 16 KB
+// barrier indices
+constexpr int kQFull = 0;
+constexpr int kKFull = 1;              // [kRing]
+constexpr int kVFull = kKFull + kRing; // [kRing]
+constexpr int kSFull = kVFull + kRing; // [query tile][half] = 4
+constexpr int kPFull = kSFull + 4;     // 4, 128 arrivals each
+constexpr int kPvDone = kPFull + 4;    // 4
+constexpr int kKFree = kPvDone + 4;    // [kRing], one arrival per active query tile: every Q·K on the slot is done
+constexpr int kVFree = kKFree + kRing; // [kRing], likewise for P·V
+constexpr int kNumBars = kVFree + kRing;
 
 struct Args {
   void* out;
@@ -54,7 +68,7 @@ struct Args {
   long long* trace;                // optional pipeline timestamps, see trace_event
   float* part_o; float* part_ml;   // split-KV partials: O as [unit][D][128], (m, l) as [unit][2][128]
   int64_t out_stride, block_table_stride, mask_stride_m, mask_stride_n, num_pages;
-  int num_seqs, max_pages, num_q_heads, num_kv_heads, group, tpt, q_tiles, num_splits;
+  int num_seqs, max_pages, num_q_heads, num_kv_heads, group, tpt, q_tiles, q_pairs, num_splits;
   int page_size, has_cache, mask_mode, bidirectional, block_m, is_bf16;
   float scale_log2;  // sm_scale * log2(e)
 };
@@ -81,8 +95,8 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
   return ok != 0;
 }
 // Bounded wait. Returns false when another role already gave up or when the limit expired.
-template <bool kBackoff = false>
-__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volatile int* abort_flag, int32_t* status) {
+template <bool kBackoff = false, class ArgsT>
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volatile int* abort_flag, const ArgsT& a) {
   if (mbar_try_wait(bar, parity)) return true;
   long long t0 = clock64();
   uint32_t spins = 0;
@@ -94,7 +108,11 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volati
       if (*abort_flag) return false;
       if (clock64() - t0 > kWaitLimitCycles) {
         *abort_flag = 1;
-        report_status(status, PDLLM_S_WAIT_TIMEOUT);
+        // low byte: the status code; above it, for diagnosis: barrier index in the CTA's barrier array, warp, parity
+        const int which = static_cast<int>((smem_u32(bar) & 0x3ff) >> 3);
+        const int code = PDLLM_S_WAIT_TIMEOUT | (which << 8) | ((threadIdx.x >> 5) << 16) | (parity << 24);
+        report_status(a.status, code);
+        if (a.trace != nullptr && (threadIdx.x & 31) == 0) a.trace[8 * 64 * 16 - 64 + (threadIdx.x >> 5)] = code;  // per-warp record
         return false;
       }
     }
@@ -226,8 +244,13 @@ constexpr int kTraceEvents = 16;
 constexpr int kTraceIters = 64;
 constexpr int kTraceCtas = 8;
 __device__ __forceinline__ void trace_event(const Args& a, int it, int ev) {
-  if (blockIdx.x < kTraceCtas && it < kTraceIters && (threadIdx.x & 31) == 0 && (threadIdx.x == 0 || threadIdx.x >= 128)) {
-    a.trace[(static_cast<int64_t>(blockIdx.x) * kTraceIters + it) * kTraceEvents + ev] = clock64();
+  // slots 0-3: the first four CTAs of the grid; slots 4-7: the last four (they run in the last wave)
+  const int slot = blockIdx.x < 4 ? static_cast<int>(blockIdx.x)
+                                  : (blockIdx.x + 4 >= gridDim.x ? 4 + static_cast<int>(blockIdx.x + 4 - gridDim.x) : -1);
+  if (slot >= 0 && it < kTraceIters && (threadIdx.x & 31) == 0 && (threadIdx.x == 0 || threadIdx.x == 128 || threadIdx.x >= 256)) {
+    long long t = clock64();
+    if (it == kTraceIters - 2) asm volatile("mov.u64 %0, %globaltimer;" : "=l"(t));  // row 62: wall-clock nanoseconds
+    a.trace[(static_cast<int64_t>(slot) * kTraceIters + it) * kTraceEvents + ev] = t;
   }
 }
 
@@ -250,40 +273,42 @@ __device__ __forceinline__ TileInfo tile_info(int t, int n_ctx_tiles, int ctx_le
   return ti;
 }
 
-__global__ void __launch_bounds__(kThreads, 2)
+__global__ void __launch_bounds__(kThreads, 1)
 attn_sm100_kernel(const __grid_constant__ CUtensorMap q_map, const __grid_constant__ CUtensorMap kn_map,
                   const __grid_constant__ CUtensorMap vn_map, const __grid_constant__ CUtensorMap kc_map,
                   const __grid_constant__ CUtensorMap vc_map, const Args a) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + kSmemBar);
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + kSmemBar + 128);
-  volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + kSmemBar + 136);
-  volatile int* tile_flags = reinterpret_cast<volatile int*>(smem + kSmemBar + 144);  // [4]: page of tile (it & 3) was unreadable
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + kSmemBar + 256);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + kSmemBar + 264);
+  volatile int* tile_flags = reinterpret_cast<volatile int*>(smem + kSmemBar + 272);  // [4]: page of tile (it & 3) was unreadable
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
 
-  // ---- decode the work unit ----
+  // ---- decode the work unit: (sequence, KV head, pair of query tiles, KV split) ----
   int u = blockIdx.x;
   const int split = u % a.num_splits; u /= a.num_splits;
-  const int qt = u % a.q_tiles; u /= a.q_tiles;
+  const int pair = u % a.q_pairs; u /= a.q_pairs;
   const int kvh = u % a.num_kv_heads;
   const int seq = u / a.num_kv_heads;
-  const int unit = blockIdx.x;
 
   const int q_start = a.cu_seqlens_q[seq];
   const int q_len = a.cu_seqlens_q[seq + 1] - q_start;
   int ctx_len = a.has_cache ? (a.seq_lens[seq] - q_len) : 0;
   if (ctx_len < 0) ctx_len = 0;
-  const int tok0 = qt * a.tpt;
-  const int n_tok = min(a.tpt, q_len - tok0);
   const int G = a.group;
+  // query tile X (0 = A, 1 = B) covers tokens [tok0[X], tok0[X] + n_tok[X])
+  const int tokA = (2 * pair) * a.tpt, tokB = (2 * pair + 1) * a.tpt;
+  const int n_tokA = min(a.tpt, q_len - tokA), n_tokB = min(a.tpt, q_len - tokB);
+  const bool b_active = n_tokB > 0;
+  const int n_q = b_active ? 2 : 1;
 
-  // keys among the new rows that any row of this tile may see
+  // keys among the new rows that any row of this CTA may see (tile B holds the later rows)
   int new_end = q_len;
-  if (n_tok > 0) {
-    const int last_m = tok0 + n_tok - 1;
+  if (n_tokA > 0) {
+    const int last_m = b_active ? (tokB + n_tokB - 1) : (tokA + n_tokA - 1);
     if (a.mask_mode == PDLLM_MASK_CAUSAL) new_end = min(q_len, last_m + 1);
     else if (!a.bidirectional) new_end = min(q_len, (last_m / a.block_m + 1) * a.block_m);
   }
@@ -294,22 +319,28 @@ attn_sm100_kernel(const __grid_constant__ CUtensorMap q_map, const __grid_consta
   const int t_begin = split * per_split;
   const int t_end = min(total_tiles, t_begin + per_split);
   const int n_iter = t_end - t_begin;
+  // index of a query tile's split-KV partial
+  const int64_t unit_base = ((static_cast<int64_t>(seq) * a.num_kv_heads + kvh) * a.q_tiles + 2 * pair) * a.num_splits + split;
 
-  if (n_tok <= 0 || n_iter <= 0) {
-    // Nothing to attend in this unit: publish a neutral partial so the merge ignores it.
-    if (a.num_splits > 1 && threadIdx.x < kTileM) {
-      a.part_ml[(static_cast<int64_t>(unit) * 2 + 0) * kTileM + threadIdx.x] = -INFINITY;
-      a.part_ml[(static_cast<int64_t>(unit) * 2 + 1) * kTileM + threadIdx.x] = 0.f;
+  if (n_tokA <= 0) return;
+  if (n_iter <= 0) {
+    // Nothing to attend in this split: publish neutral partials so the merge ignores them.
+    if (a.num_splits > 1 && threadIdx.x < 2 * kTileM && (threadIdx.x < kTileM || b_active)) {
+      const int64_t unit = unit_base + (threadIdx.x >> 7) * a.num_splits;
+      const int r = threadIdx.x & (kTileM - 1);
+      a.part_ml[(unit * 2 + 0) * kTileM + r] = -INFINITY;
+      a.part_ml[(unit * 2 + 1) * kTileM + r] = 0.f;
     }
     return;
   }
 
   // ---- set-up: barriers, TMEM ----
-  if (warp == 4) {
+  if (warp == kProducerWarp) {
     if (lane == 0) {
-      for (int i = 0; i < kNumBars; ++i) mbar_init(&bars[i], (i == kPFull0 || i == kPFull1) ? 128u : 1u);
+      for (int i = 0; i < kNumBars; ++i) {
+        mbar_init(&bars[i], (i >= kPFull && i < kPFull + 4) ? 128u : (i >= kKFree ? static_cast<uint32_t>(n_q) : 1u));
+      }
       abort_flag[0] = 0;
-      abort_flag[1] = 0;  // never set: lets the producer's drain waits run although abort_flag[0] is up
       fence_barrier_init();
     }
     __syncwarp();
@@ -320,24 +351,27 @@ attn_sm100_kernel(const __grid_constant__ CUtensorMap q_map, const __grid_consta
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
 
-  const uint32_t idesc_qk = make_idesc(a.is_bf16 != 0, false, kHalfN);    // S_b[128 x 64] = Q[128 x 128] K_b^T
-  const uint32_t idesc_pv = make_idesc(a.is_bf16 != 0, true, kHeadDim);   // O[128 x 128] += P_b[128 x 64] V_b
+  const uint32_t idesc_qk = make_idesc(a.is_bf16 != 0, false, kHalfN);    // S_Xb[128 x 64] = Q_X[128 x 128] K_b^T
+  const uint32_t idesc_pv = make_idesc(a.is_bf16 != 0, true, kHeadDim);   // O_X[128 x 128] += P_Xb[128 x 64] V_b
 
-  if (warp == 4) {
+  if (warp == kProducerWarp) {
     // =========================== TMA producer ===========================
-    // One thread issues every copy, in the order in which the MMA pipeline frees the slots:
-    //   V_0(t+1) after P·V_0(t), K_0(t+2) after Q·K_0(t+1), V_1(t+1) after P·V_1(t), K_1(t+2) after Q·K_1(t+1).
+    // Key half-tiles h = 2*it + b stream through two rings of kRing slots (K and V). Slot h % kRing is free again
+    // once both query tiles' MMAs on half-tile h - kRing are done (the K-free / V-free barriers).
     if (lane == 0) {
       const uint32_t q_bytes = 2u * 64u * 2u * static_cast<uint32_t>(G * a.tpt);
-      mbar_expect_tx(&bars[kQFull], q_bytes);
-      tma_load_3d(&q_map, &bars[kQFull], smem + kSmemQ, 0, kvh * G, q_start + tok0);
-      tma_load_3d(&q_map, &bars[kQFull], smem + kSmemQ + kHalfBytes, 64, kvh * G, q_start + tok0);
-
-      // K_b / V_b of tile `it`: rows [64b, 64b+64) of both 64-column halves of the head dimension
-      auto load_half = [&](bool is_v, int it, int b) {
+      mbar_expect_tx(&bars[kQFull], q_bytes * n_q);
+      for (int x = 0; x < n_q; ++x) {
+        const int tok0 = x == 0 ? tokA : tokB;
+        tma_load_3d(&q_map, &bars[kQFull], smem + kSmemQ + x * kTileBytes, 0, kvh * G, q_start + tok0);
+        tma_load_3d(&q_map, &bars[kQFull], smem + kSmemQ + x * kTileBytes + kHalfBytes, 64, kvh * G, q_start + tok0);
+      }
+      auto load_half = [&](bool is_v, int h) {
+        const int it = h >> 1, b = h & 1;
+        const int slot = h % kRing;
         const TileInfo ti = tile_info(t_begin + it, n_ctx_tiles, ctx_len, new_end);
-        uint64_t* bar = &bars[(is_v ? kVFull0 : kKFull0) + b];
-        uint8_t* dst = smem + (is_v ? kSmemV : kSmemK) + b * kSlotBytes;
+        uint64_t* bar = &bars[(is_v ? kVFull : kKFull) + slot];
+        uint8_t* dst = smem + (is_v ? kSmemV : kSmemK) + slot * kSlotBytes;
         mbar_expect_tx(bar, kSlotBytes);
         // one copy per slot: the tensor maps put the two 64-column halves of the head dimension in their outermost
         // box dimension, so the slot receives [half][64 keys][128 B]
@@ -357,31 +391,19 @@ attn_sm100_kernel(const __grid_constant__ CUtensorMap q_map, const __grid_consta
           tma_load_4d(is_v ? &vn_map : &kn_map, bar, dst, 0, q_start + ti.key0 + b * kHalfN, 0, kvh);
         }
       };
-      load_half(false, 0, 0);
-      load_half(false, 0, 1);
-      load_half(true, 0, 0);
-      load_half(true, 0, 1);
+      const int n_half = 2 * n_iter;
+      for (int h = 0; h < n_half && h < kRing; ++h) load_half(false, h);
+      for (int h = 0; h < n_half && h < kRing; ++h) load_half(true, h);
       bool ok = true;
-      if (n_iter > 1) {
-        for (int b = 0; b < 2 && ok; ++b) {
-          ok = mbar_wait<true>(&bars[kSFull0 + b], 0, abort_flag, a.status);  // Q·K_b(0) done: the K_b slot is free
-          if (ok) load_half(false, 1, b);
-        }
-      }
-      for (int it = 0; it < n_iter && ok; ++it) {
-        const uint32_t ph = it & 1;
-        for (int b = 0; b < 2 && ok; ++b) {
-          if (it + 1 < n_iter) {
-            ok = mbar_wait<true>(&bars[kPvDone0 + b], ph, abort_flag, a.status);       // P·V_b(it) done: the V_b slot is free
-            if (PDLLM_TRACE_ON) trace_event(a, it, 8 + b);
-            if (ok) load_half(true, it + 1, b);
-          }
-          if (ok && it + 2 < n_iter) {
-            ok = mbar_wait<true>(&bars[kSFull0 + b], ph ^ 1, abort_flag, a.status);    // Q·K_b(it+1) done: the K_b slot is free
-            if (PDLLM_TRACE_ON) trace_event(a, it, 10 + b);
-            if (ok) load_half(false, it + 2, b);
-          }
-        }
+      for (int h = 0; h + kRing < n_half && ok; ++h) {
+        // a slot's "free" barrier completes once per use of the slot, and the slot cannot be used again before this
+        // loop refills it, so the wait below is never more than one phase behind
+        const int slot = h % kRing;
+        const uint32_t use = (h / kRing) & 1;
+        ok = mbar_wait<true>(&bars[kKFree + slot], use, abort_flag, a);   // every Q·K on half-tile h is done
+        if (ok) load_half(false, h + kRing);
+        if (ok) ok = mbar_wait<true>(&bars[kVFree + slot], use, abort_flag, a);  // every P·V on half-tile h is done
+        if (ok) load_half(true, h + kRing);
       }
       // Every copy issued above is consumed by an MMA that the epilogue waits for, unless a wait gave up; then the
       // CTA is abandoning its result and only has to let copies in flight land: give them a bounded moment.
@@ -391,26 +413,30 @@ attn_sm100_kernel(const __grid_constant__ CUtensorMap q_map, const __grid_consta
       }
     }
     __syncwarp();
-  } else if (warp == 5) {
-    // =========================== MMA issuer ===========================
-    // Software-pipelined over the two S buffers: ... PV_0(t), QK_0(t+1), PV_1(t), QK_1(t+1) ... so that the next
-    // tile's scores for buffer b are produced while the softmax warps still work on buffer b^1.
-    const uint32_t sq = smem_u32(smem + kSmemQ), sk = smem_u32(smem + kSmemK), sv = smem_u32(smem + kSmemV);
-    const uint32_t tO = tmem_base + kColO;
-    auto issue_qk = [&](int b) {   // S_b = Q K[64b .. 64b+64)^T
-      const uint32_t tSb = tmem_base + kColS + b * kHalfN;
+  } else if (warp >= kMmaWarp0) {
+    // =========================== MMA issuers: one warp per chain (query tile x, key half b) ===========================
+    // A single thread sustains only about one tcgen05.mma per ~110 cycles; four concurrent issuers keep the tensor
+    // pipe fed. Each chain loops: P·V_xb(tile) once its softmax warps delivered P, then Q·K_xb of the next tile as
+    // soon as that product released the S/P columns.
+    const int chain = warp - kMmaWarp0;
+    const int x = chain >> 1, b = chain & 1;
+    if (x < n_q) {
+    const uint32_t sq = smem_u32(smem + kSmemQ) + x * kTileBytes, sk = smem_u32(smem + kSmemK), sv = smem_u32(smem + kSmemV);
+    const uint32_t tS = tmem_base + kColS + chain * kHalfN;   // S_xb, then P_xb in its first 32 columns
+    const uint32_t tO = tmem_base + kColO + x * kHeadDim;
+    auto issue_qk = [&](int slot) {   // S_xb = Q_x K_b^T
 #pragma unroll
       for (int kk = 0; kk < kHeadDim / 16; ++kk) {
-        const uint32_t koff = (kk >> 2) * kHalfBytes + (kk & 3) * 32;
-        const uint32_t kboff = b * kSlotBytes + (kk >> 2) * (kSlotBytes / 2) + (kk & 3) * 32;
-        umma_ss(tSb, desc_kmajor_sw128(sq + koff), desc_kmajor_sw128(sk + kboff), idesc_qk, kk > 0 ? 1u : 0u);
+        const uint32_t qoff = (kk >> 2) * kHalfBytes + (kk & 3) * 32;
+        const uint32_t koff = slot * kSlotBytes + (kk >> 2) * (kSlotBytes / 2) + (kk & 3) * 32;
+        umma_ss(tS, desc_kmajor_sw128(sq + qoff), desc_kmajor_sw128(sk + koff), idesc_qk, kk > 0 ? 1u : 0u);
       }
-      umma_commit(&bars[kSFull0 + b]);
+      umma_commit(&bars[kSFull + chain]);
+      umma_commit(&bars[kKFree + slot]);
     };
-    bool ok = mbar_wait<true>(&bars[kQFull], 0, abort_flag, a.status);
-    for (int b = 0; b < 2 && ok; ++b) {
-      ok = mbar_wait<true>(&bars[kKFull0 + b], 0, abort_flag, a.status);
-      if (!ok) break;
+    bool ok = mbar_wait<true>(&bars[kQFull], 0, abort_flag, a);
+    if (ok) ok = mbar_wait<true>(&bars[kKFull + b], 0, abort_flag, a);  // half-tile b of tile 0 sits in slot b, first use
+    if (ok) {
       tc_fence_after();
       if (lane == 0) issue_qk(b);
       __syncwarp();
@@ -418,62 +444,72 @@ attn_sm100_kernel(const __grid_constant__ CUtensorMap q_map, const __grid_consta
     for (int it = 0; it < n_iter && ok; ++it) {
       const uint32_t ph = it & 1;
       const TileInfo ti = tile_info(t_begin + it, n_ctx_tiles, ctx_len, new_end);
-      const bool has_next = it + 1 < n_iter;
-#pragma unroll
-      for (int b = 0; b < 2; ++b) {
-        ok = mbar_wait<true>(&bars[kVFull0 + b], ph, abort_flag, a.status);
-        if (!ok) break;
-        if (PDLLM_TRACE_ON) trace_event(a, it, 12 + b);
-        if (ti.nvalid < (b + 1) * kHalfN) {
-          // Rows of V_b past the last valid key may hold anything (stale page contents, another sequence's
-          // rows); P is 0 there but 0 * NaN is NaN, so clear them before the MMA reads the half tile.
-          const int first = max(ti.nvalid, b * kHalfN);
-          const int n_rows = (b + 1) * kHalfN - first;
-          for (int i = lane; i < n_rows * 16; i += 32) {
-            const int r = first + (i >> 4) - b * kHalfN;  // row inside the slot
-            const int c = i & 15;
-            uint4* dst = reinterpret_cast<uint4*>(smem + kSmemV + b * kSlotBytes + (c >> 3) * (kSlotBytes / 2) + r * 128 + (c & 7) * 16);
-            *dst = make_uint4(0, 0, 0, 0);
-          }
-          fence_proxy_async();
-          __syncwarp();
+      const int h = 2 * it + b;
+      const int slot = h % kRing;
+      ok = mbar_wait<true>(&bars[kVFull + slot], (h / kRing) & 1, abort_flag, a);
+      if (!ok) break;
+      if (ti.nvalid < (b + 1) * kHalfN) {
+        // Rows of V_b past the last valid key may hold anything (stale page contents, another sequence's
+        // rows); P is 0 there but 0 * NaN is NaN, so clear them before the MMA reads the half tile. Both query
+        // tiles' issuers do this for the slot they share: the writes are identical zeros.
+        const int first = max(ti.nvalid, b * kHalfN) - b * kHalfN;  // first row to clear inside the slot
+        const int n_rows = kHalfN - first;
+        for (int i = lane; i < n_rows * 16; i += 32) {
+          const int r = first + (i >> 4);
+          const int c = i & 15;
+          uint4* dst = reinterpret_cast<uint4*>(smem + kSmemV + slot * kSlotBytes + (c >> 3) * (kSlotBytes / 2) + r * 128 + (c & 7) * 16);
+          *dst = make_uint4(0, 0, 0, 0);
         }
-        ok = mbar_wait<true>(&bars[kPFull0 + b], ph, abort_flag, a.status);
+        fence_proxy_async();
+        __syncwarp();
+      }
+      ok = mbar_wait<true>(&bars[kPFull + chain], ph, abort_flag, a);
+      // O_x is accumulated by both chains of query tile x, from two threads: keep their products strictly
+      // alternating (x,0)(x,1)(x,0)... by waiting for the sibling's previous product. The softmax warps deliver P in
+      // that order anyway, so this wait is normally already satisfied.
+      if (ok && b == 1) ok = mbar_wait<true>(&bars[kPvDone + chain - 1], ph, abort_flag, a);
+      if (ok && b == 0 && it > 0) ok = mbar_wait<true>(&bars[kPvDone + chain + 1], ph ^ 1, abort_flag, a);
+      if (!ok) break;
+      tc_fence_after();
+      if (PDLLM_TRACE_ON) trace_event(a, it, 4 + chain);
+      if (lane == 0) {
+#pragma unroll
+        for (int kk = 0; kk < kHalfN / 16; ++kk) {
+          umma_ts(tO, tS + kk * 8, desc_mnmajor_sw128(sv + slot * kSlotBytes + kk * 2048, kSlotBytes / 2), idesc_pv,
+                  (it > 0 || b > 0 || kk > 0) ? 1u : 0u);
+        }
+        umma_commit(&bars[kPvDone + chain]);
+        umma_commit(&bars[kVFree + slot]);
+      }
+      __syncwarp();
+      if (it + 1 < n_iter) {
+        const int hn = h + 2;
+        const int nslot = hn % kRing;
+        ok = mbar_wait<true>(&bars[kKFull + nslot], (hn / kRing) & 1, abort_flag, a);
+        if (ok) ok = mbar_wait<true>(&bars[kPvDone + chain], ph, abort_flag, a);  // S_xb / P_xb columns are free again
         if (!ok) break;
         tc_fence_after();
-        if (PDLLM_TRACE_ON) trace_event(a, it, 4 + b);
-        if (lane == 0) {
-          const uint32_t tPb = tmem_base + kColS + b * kHalfN;
-#pragma unroll
-          for (int kk = 0; kk < kHalfN / 16; ++kk) {
-            umma_ts(tO, tPb + kk * 8, desc_mnmajor_sw128(sv + b * kSlotBytes + kk * 2048, kSlotBytes / 2), idesc_pv,
-                    (it > 0 || b > 0 || kk > 0) ? 1u : 0u);
-          }
-          umma_commit(&bars[kPvDone0 + b]);
-        }
+        if (PDLLM_TRACE_ON) trace_event(a, it, 12 + chain);
+        if (lane == 0) issue_qk(nslot);
         __syncwarp();
-        if (has_next) {
-          ok = mbar_wait<true>(&bars[kKFull0 + b], ph ^ 1, abort_flag, a.status);
-          if (PDLLM_TRACE_ON) trace_event(a, it, 14 + b);
-          if (ok) ok = mbar_wait<true>(&bars[kPvDone0 + b], ph, abort_flag, a.status);  // S_b / P_b columns are free again
-          if (!ok) break;
-          tc_fence_after();
-          if (PDLLM_TRACE_ON) trace_event(a, it, 2 + b);
-          if (lane == 0) issue_qk(b);
-          __syncwarp();
-        }
       }
     }
+    }  // x < n_q
   } else {
-    // =========================== softmax + epilogue (warps 0-3) ===========================
-    const int r = threadIdx.x;                 // tile row == TMEM lane
-    const uint32_t lane_base = static_cast<uint32_t>(warp * 32) << 16;
-    const uint32_t tS = tmem_base + lane_base + kColS;
-    const uint32_t tO = tmem_base + lane_base + kColO;
+    // =========================== softmax + epilogue (warps 0-3: query tile A, warps 4-7: query tile B) ===========
+    const int x = warp >> 2;
+    if (x < n_q) {
+    const int r = threadIdx.x & (kTileM - 1);   // tile row == TMEM lane
+    const uint32_t lane_base = static_cast<uint32_t>((warp & 3) * 32) << 16;
+    const uint32_t tS = tmem_base + lane_base + kColS + x * 2 * kHalfN;
+    const uint32_t tO = tmem_base + lane_base + kColO + x * kHeadDim;
+    const int tok0 = x == 0 ? tokA : tokB;
+    const int n_tok = x == 0 ? n_tokA : n_tokB;
     const int tok_local = r / G;               // token of this row inside the tile
     const int head_local = r - tok_local * G;
     const bool row_valid = tok_local < n_tok;
     const int m = tok0 + tok_local;            // sequence-local new-row index
+    const int64_t unit = unit_base + x * a.num_splits;
     // last visible new key (exclusive) for this row
     int row_new_end = q_len;
     if (a.mask_mode == PDLLM_MASK_CAUSAL) row_new_end = min(q_len, m + 1);
@@ -484,6 +520,7 @@ attn_sm100_kernel(const __grid_constant__ CUtensorMap q_map, const __grid_consta
     float l_run = 0.f;
     bool ok = true;
     uint32_t s[kHalfN];       // one row of one S buffer; the epilogue reuses it for O
+    if (PDLLM_TRACE_ON) { trace_event(a, kTraceIters - 1, 0); trace_event(a, kTraceIters - 2, 0); }
     constexpr uint32_t kNegInf = 0xff800000u;
 
     for (int it = 0; it < n_iter && ok; ++it) {
@@ -497,10 +534,10 @@ attn_sm100_kernel(const __grid_constant__ CUtensorMap q_map, const __grid_consta
 #pragma unroll
       for (int b = 0; b < 2; ++b) {
         const uint32_t tSb = tS + b * kHalfN;
-        ok = mbar_wait(&bars[kSFull0 + b], ph, abort_flag, a.status);
+        ok = mbar_wait(&bars[kSFull + x * 2 + b], ph, abort_flag, a);
         if (!ok) break;
         tc_fence_after();
-        if (PDLLM_TRACE_ON) trace_event(a, it, b);
+        if (PDLLM_TRACE_ON) trace_event(a, it, x * 2 + b);
 
         tmem_ld32(tSb, s);
         tmem_ld32(tSb + 32, s + 32);
@@ -536,7 +573,7 @@ attn_sm100_kernel(const __grid_constant__ CUtensorMap q_map, const __grid_consta
             // O must hold every product issued so far: the previous half's P·V may still be in flight
             const int pb = b ^ 1;
             const uint32_t pph = (b == 1) ? ph : (ph ^ 1);
-            ok = mbar_wait(&bars[kPvDone0 + pb], pph, abort_flag, a.status);
+            ok = mbar_wait(&bars[kPvDone + x * 2 + pb], pph, abort_flag, a);
             if (!ok) break;
             tc_fence_after();
             const float m_new = grow ? m_half : m_ref;
@@ -581,13 +618,15 @@ attn_sm100_kernel(const __grid_constant__ CUtensorMap q_map, const __grid_consta
         l_run += (l0 + l1) + (l2 + l3);
         tc_wait_st();
         tc_fence_before();
-        mbar_arrive(&bars[kPFull0 + b]);
-        if (PDLLM_TRACE_ON) trace_event(a, it, 6 + b);
+        mbar_arrive(&bars[kPFull + x * 2 + b]);
+        if (PDLLM_TRACE_ON) trace_event(a, it, 8 + x * 2 + b);
       }
     }
 
     // ---- epilogue ----
-    if (ok) ok = mbar_wait(&bars[kPvDone1], (n_iter - 1) & 1, abort_flag, a.status);  // in-order MMAs: PV_1 done implies all done
+    if (PDLLM_TRACE_ON) trace_event(a, kTraceIters - 1, 1);
+    if (ok) ok = mbar_wait(&bars[kPvDone + x * 2 + 1], (n_iter - 1) & 1, abort_flag, a);  // in-order MMAs: the last P·V done implies all done
+    if (PDLLM_TRACE_ON) trace_event(a, kTraceIters - 1, 2);
     if (ok) {
       tc_fence_after();
       if (a.num_splits == 1) {
@@ -617,7 +656,7 @@ attn_sm100_kernel(const __grid_constant__ CUtensorMap q_map, const __grid_consta
           }
         }
       } else {
-        float* po = a.part_o + static_cast<int64_t>(unit) * kHeadDim * kTileM;
+        float* po = a.part_o + unit * kHeadDim * kTileM;
 #pragma unroll 1
         for (int c = 0; c < 4; ++c) {
           tmem_ld32(tO + c * 32, s);
@@ -625,25 +664,30 @@ attn_sm100_kernel(const __grid_constant__ CUtensorMap q_map, const __grid_consta
 #pragma unroll
           for (int j = 0; j < 32; ++j) po[static_cast<int64_t>(c * 32 + j) * kTileM + r] = __uint_as_float(s[j]);
         }
-        a.part_ml[(static_cast<int64_t>(unit) * 2 + 0) * kTileM + r] = m_ref;
-        a.part_ml[(static_cast<int64_t>(unit) * 2 + 1) * kTileM + r] = l_run;
+        a.part_ml[(unit * 2 + 0) * kTileM + r] = m_ref;
+        a.part_ml[(unit * 2 + 1) * kTileM + r] = l_run;
       }
     }
+    if (PDLLM_TRACE_ON) { trace_event(a, kTraceIters - 1, 3); trace_event(a, kTraceIters - 2, 1); }
+    }  // x < n_q
   }
 
   // ---- teardown ----
   tc_fence_before();
   __syncthreads();
-  if (warp == 4) {
+  if (warp == kProducerWarp) {
     tc_fence_after();
     tmem_dealloc(tmem_base, kTmemCols);
   }
 }
 
-// Merge of the split-KV partials. One thread per (unit-row, 4 output columns).
-// out[row] = sum_s 2^(m_s - M) O_s / sum_s 2^(m_s - M) l_s.
-__global__ void attn_combine_kernel(const Args a) {
-  const int64_t tile = blockIdx.x;  // (seq, kvh, qt)
+// Merge of the split-KV partials: out[row] = sum_s 2^(m_s - M) O_s / sum_s 2^(m_s - M) l_s.
+// One CTA per (query tile, 32-column slab); thread r owns tile row r, so every partial read is a coalesced 512-byte
+// line of the [D][128] partial layout. All loads of a step are issued before they are reduced.
+constexpr int kCombineMaxSplits = 32;
+__global__ void __launch_bounds__(kTileM) attn_combine_kernel(const Args a) {
+  const int64_t tile = blockIdx.x >> 2;  // (seq, kvh, qt)
+  const int slab = blockIdx.x & 3;
   int u = static_cast<int>(tile);
   const int qt = u % a.q_tiles; u /= a.q_tiles;
   const int kvh = u % a.num_kv_heads;
@@ -654,35 +698,44 @@ __global__ void attn_combine_kernel(const Args a) {
   const int n_tok = min(a.tpt, q_len - tok0);
   if (n_tok <= 0) return;
   const int G = a.group;
-  const int r = threadIdx.x & (kTileM - 1);   // row: consecutive threads read consecutive partial addresses
-  const int dq = threadIdx.x / kTileM;        // which quarter of the 128 columns
+  const int r = threadIdx.x;
   const int tok_local = r / G;
   if (tok_local >= n_tok) return;
   const int head_local = r - tok_local * G;
   const int64_t unit0 = tile * a.num_splits;
+  const int S = a.num_splits;
 
   float M = -INFINITY;
-  for (int s = 0; s < a.num_splits; ++s) M = fmaxf(M, a.part_ml[((unit0 + s) * 2 + 0) * kTileM + r]);
+  for (int s = 0; s < S; ++s) M = fmaxf(M, a.part_ml[((unit0 + s) * 2 + 0) * kTileM + r]);
   float wsum = 0.f;
-  float w[32];
-  for (int s = 0; s < a.num_splits && s < 32; ++s) {
-    const float ms = a.part_ml[((unit0 + s) * 2 + 0) * kTileM + r];
-    const float ls = a.part_ml[((unit0 + s) * 2 + 1) * kTileM + r];
-    w[s] = (ms == -INFINITY) ? 0.f : exp2f(ms - M);
-    wsum += w[s] * ls;
+  float w[kCombineMaxSplits];
+#pragma unroll
+  for (int s = 0; s < kCombineMaxSplits; ++s) {
+    w[s] = 0.f;
+    if (s < S) {
+      const float ms = a.part_ml[((unit0 + s) * 2 + 0) * kTileM + r];
+      const float ls = a.part_ml[((unit0 + s) * 2 + 1) * kTileM + r];
+      w[s] = (ms == -INFINITY) ? 0.f : exp2f(ms - M);  // a neutral partial has no O data behind it: weight 0, never read
+      wsum += w[s] * ls;
+    }
   }
   const float inv = wsum > 0.f ? 1.f / wsum : 0.f;
   uint8_t* out_row = reinterpret_cast<uint8_t*>(a.out) +
                      ((static_cast<int64_t>(q_start + tok0 + tok_local)) * a.out_stride + static_cast<int64_t>(kvh * G + head_local) * kHeadDim) * 2;
-  for (int d0 = dq * 32; d0 < dq * 32 + 32; d0 += 8) {
+#pragma unroll 1
+  for (int d0 = slab * 32; d0 < slab * 32 + 32; d0 += 8) {
     float acc[8];
 #pragma unroll
     for (int j = 0; j < 8; ++j) acc[j] = 0.f;
-    for (int s = 0; s < a.num_splits && s < 32; ++s) {
-      if (w[s] == 0.f) continue;
-      const float* po = a.part_o + (unit0 + s) * kHeadDim * kTileM;
+#pragma unroll 4
+    for (int s = 0; s < S; ++s) {
+      const float ws = w[s];
+      const float* po = a.part_o + (unit0 + s) * kHeadDim * kTileM + static_cast<int64_t>(d0) * kTileM + r;
+      float v[8];
 #pragma unroll
-      for (int j = 0; j < 8; ++j) acc[j] = fmaf(w[s], po[static_cast<int64_t>(d0 + j) * kTileM + r], acc[j]);
+      for (int j = 0; j < 8; ++j) v[j] = (ws != 0.f) ? po[j * kTileM] : 0.f;
+#pragma unroll
+      for (int j = 0; j < 8; ++j) acc[j] = fmaf(ws, v[j], acc[j]);
     }
     uint32_t packed[4];
 #pragma unroll
@@ -751,8 +804,9 @@ inline bool supported(const pdllm_attn_params* p, const char** why) {
 }
 
 struct Plan {
-  int group, tpt, q_tiles, num_splits;
-  int64_t tiles, units;
+  int group, tpt, q_tiles, q_pairs, num_splits;
+  int64_t tiles;  // query tiles = split-KV partial groups
+  int64_t ctas;   // CTAs launched: pairs of query tiles x splits
 };
 
 inline Plan make_plan(const pdllm_attn_params* p) {
@@ -761,16 +815,18 @@ inline Plan make_plan(const pdllm_attn_params* p) {
   pl.tpt = kTileM / pl.group;
   pl.q_tiles = (p->max_query_len + pl.tpt - 1) / pl.tpt;
   if (pl.q_tiles < 1) pl.q_tiles = 1;
+  pl.q_pairs = (pl.q_tiles + 1) / 2;
   pl.tiles = static_cast<int64_t>(p->num_seqs) * p->num_kv_heads * pl.q_tiles;
+  const int64_t base_ctas = static_cast<int64_t>(p->num_seqs) * p->num_kv_heads * pl.q_pairs;
   int max_key_tiles = (p->max_seq_len + kTileN - 1) / kTileN + 1;
   int splits = p->num_splits;
   if (splits <= 0) {
-    // Fill a whole number of waves of 2 CTAs per SM; each split keeps at least two key tiles.
-    const int64_t slots = 2ll * sm_count();
+    // One CTA per SM: fill a whole number of waves; each split keeps at least two key tiles.
+    const int64_t slots = sm_count();
     int cap = max_key_tiles / 2; if (cap < 1) cap = 1; if (cap > 32) cap = 32;
     double best_eff = -1.0; splits = 1;
     for (int s = 1; s <= cap; ++s) {
-      const int64_t n = pl.tiles * s;
+      const int64_t n = base_ctas * s;
       const int64_t waves = (n + slots - 1) / slots;
       const double eff = static_cast<double>(n) / static_cast<double>(waves * slots);
       if (eff > best_eff + 0.03) { best_eff = eff; splits = s; }
@@ -781,14 +837,14 @@ inline Plan make_plan(const pdllm_attn_params* p) {
   if (splits > max_key_tiles) splits = max_key_tiles;
   if (splits < 1) splits = 1;
   pl.num_splits = splits;
-  pl.units = pl.tiles * splits;
+  pl.ctas = base_ctas * splits;
   return pl;
 }
 
 inline int64_t workspace_bytes(const pdllm_attn_params* p) {
   Plan pl = make_plan(p);
   if (pl.num_splits <= 1) return 0;
-  return pl.units * (static_cast<int64_t>(kHeadDim) * kTileM + 2 * kTileM) * 4;
+  return pl.tiles * pl.num_splits * (static_cast<int64_t>(kHeadDim) * kTileM + 2 * kTileM) * 4;
 }
 
 inline int launch(const pdllm_attn_params* p, cudaStream_t stream) {
@@ -841,11 +897,11 @@ inline int launch(const pdllm_attn_params* p, cudaStream_t stream) {
   a.mask = p->mask; a.status = p->status;
   a.trace = reinterpret_cast<long long*>(p->trace);
   a.part_o = reinterpret_cast<float*>(p->workspace);
-  a.part_ml = a.part_o ? a.part_o + pl.units * static_cast<int64_t>(kHeadDim) * kTileM : nullptr;
+  a.part_ml = a.part_o ? a.part_o + pl.tiles * pl.num_splits * static_cast<int64_t>(kHeadDim) * kTileM : nullptr;
   a.out_stride = p->out_stride; a.block_table_stride = p->block_table_stride;
   a.mask_stride_m = p->mask_stride_m; a.mask_stride_n = p->mask_stride_n; a.num_pages = has_cache ? p->num_pages : 0;
   a.num_seqs = p->num_seqs; a.max_pages = p->max_pages; a.num_q_heads = p->num_q_heads; a.num_kv_heads = p->num_kv_heads;
-  a.group = pl.group; a.tpt = pl.tpt; a.q_tiles = pl.q_tiles; a.num_splits = pl.num_splits;
+  a.group = pl.group; a.tpt = pl.tpt; a.q_tiles = pl.q_tiles; a.q_pairs = pl.q_pairs; a.num_splits = pl.num_splits;
   a.page_size = p->page_size > 0 ? p->page_size : kTileN; a.has_cache = has_cache ? 1 : 0;
   a.mask_mode = p->mask_mode; a.bidirectional = p->bidirectional;
   a.block_m = 2 * (p->diffusion_blk > 0 ? p->diffusion_blk : 32);
@@ -866,10 +922,10 @@ inline int launch(const pdllm_attn_params* p, cudaStream_t stream) {
     }
   }
 
-  attn_sm100_kernel<<<static_cast<unsigned>(pl.units), kThreads, kSmemBytes, stream>>>(q_map, kn_map, vn_map, kc_map, vc_map, a);
+  attn_sm100_kernel<<<static_cast<unsigned>(pl.ctas), kThreads, kSmemBytes, stream>>>(q_map, kn_map, vn_map, kc_map, vc_map, a);
   if ((rc = check_launch("attn_sm100_kernel")) != 0) return rc;
   if (pl.num_splits > 1) {
-    attn_combine_kernel<<<static_cast<unsigned>(pl.tiles), 4 * kTileM, 0, stream>>>(a);
+    attn_combine_kernel<<<static_cast<unsigned>(pl.tiles * 4), kTileM, 0, stream>>>(a);
     if ((rc = check_launch("attn_combine_kernel")) != 0) return rc;
   }
   return 0;

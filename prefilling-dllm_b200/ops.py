@@ -80,7 +80,8 @@ def check_status(device: Optional[torch.device] = None, *, reset: bool = True) -
     if code != 0 and reset:
         word.zero_()
     if code != 0:
-        raise RuntimeError(f"pdllm_b200 device status {code}: {_lib.STATUS_NAMES.get(code, 'unknown')}")
+        detail = f" (barrier {(code >> 8) & 0xff}, warp {(code >> 16) & 0xff}, parity {(code >> 24) & 1})" if code > 0xff else ""
+        raise RuntimeError(f"pdllm_b200 device status {code & 0xff}: {_lib.STATUS_NAMES.get(code & 0xff, 'unknown')}{detail}")
     return code
 
 
