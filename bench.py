@@ -47,6 +47,9 @@ N_TABLES = CHUNKS_IN_POOL // SEL_CHUNKS  # disjoint selections that together tou
 
 FLOPS_PER_STEP = NUM_REQ * 4 * HQ * D * ROWS * (CTX + ROWS)                        # QK^T and PV
 BYTES_PER_STEP = NUM_REQ * (CTX * 2 * HKV * D * 2 + ROWS * (2 * HQ + 2 * HKV) * D * 2)  # KV pages + q/k/v/out rows
+# dram__bytes_read.sum + dram__bytes_write.sum of one attn_sm100_kernel launch on this workload, from the ncu capture
+# summarised in profiles/attn_sm100_kernel_op_config.md (algorithmic minimum: BYTES_PER_STEP)
+TRAFFIC_BYTES_PER_LAUNCH = 80_560_128
 WORKLOAD = ("configs[1] op-level paged decode attention: 8 req x (64 query + 32 response rows), 28/4 heads, d128, "
             "page 256, 4 of 32 chunks (4096 ctx tokens) per request via block table, bidirectional, N(0,1) bf16")
 
@@ -234,11 +237,7 @@ def run_native(args, rank: int, world: int, local_rank: int):
     peaks = load_peaks()
     achieved_tf = FLOPS_PER_STEP / (ms_per_step * 1e-3) / 1e12
     achieved_gb = BYTES_PER_STEP / (ms_per_step * 1e-3) / 1e9
-    traffic = None
-    traffic_path = os.path.join(ROOT, "profiles", "attn_sm100_traffic.json")
-    if os.path.exists(traffic_path):
-        with open(traffic_path) as handle:
-            traffic = json.load(handle).get("dram_bytes_per_launch")
+    traffic = TRAFFIC_BYTES_PER_LAUNCH
     line = {
         "metric": "decode_attention_tok_per_s", "value": value, "unit": "tok/s", "n_gpus": world, "steps": args.steps,
         "warmup": max(3, args.warmup), "ms_per_step": ms_per_step, "higher_is_better": True, "scaling": "weak",
