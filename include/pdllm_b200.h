@@ -163,6 +163,23 @@ int pdllm_unmask_step(const void* logits, int64_t logits_stride, const void* las
                       float threshold, int conf_dtype, int32_t* out_counts, float* out_conf,
                       int64_t* out_x0, void* workspace, int64_t workspace_bytes, void* stream);
 
+/* Same step as pdllm_unmask_step, for callers that cannot hand over device scratch. It has no counterpart in the
+ * reference. Some hosts of the decode loop have given every byte of device memory they may use to the KV page pool
+ * and run the loop under a rule of "no allocation after start-up" (an allocation there can fail, and cudaMalloc
+ * stalls the whole device while it runs); others sit behind an interface that carries only inputs and outputs.
+ * For them the partial-reduction scratch lives inside the library: a fixed array of about 7 KB that every GPU which
+ * loads the library holds until the process exits, enough for block_len <= PDLLM_UNMASK_STATIC_MAX_BLOCK; longer
+ * blocks are refused with PDLLM_E_INVALID. The call allocates nothing. The first call on a device looks up the
+ * array's device address (a one-time set-up; make that first call before any stream capture begins). All calls share
+ * the one array and it keeps the previous call's contents: the entry point clears the words that must start at zero,
+ * and two calls whose kernels overlap on the GPU (different streams, no ordering between them) race on it — issue
+ * them on one stream or order them with events. */
+#define PDLLM_UNMASK_STATIC_MAX_BLOCK 64
+int pdllm_unmask_step_static(const void* logits, int64_t logits_stride, const void* last_logit, int dtype,
+                             int block_len, int64_t vocab, int shift, int64_t* block_ids, int64_t mask_id,
+                             float threshold, int conf_dtype, int32_t* out_counts, float* out_conf,
+                             int64_t* out_x0, void* stream);
+
 /* ------------------------------------------------------------------------------------------------
  * (2a) draft-self-information score tail
  * replaces index_select(label_pos-1) → log_softmax(fp32) → gather(labels) → −mean NLL

@@ -6,6 +6,8 @@
 #include "kv_pages.cuh"
 #include "score.cuh"
 
+#include <mutex>
+
 using namespace pdllm;
 
 namespace {
@@ -189,6 +191,52 @@ int pdllm_unmask_step(const void* logits, int64_t logits_stride, const void* las
         threshold, conf_dtype, out_counts, out_conf, out_x0, static_cast<float*>(workspace));
     return check_launch("unmask_kernel");
   });
+}
+
+// Scratch of pdllm_unmask_step_static: lives in the library image, one copy per GPU that loads the library, held
+// until the process exits. Sized for PDLLM_UNMASK_STATIC_MAX_BLOCK slots (about 7 KB).
+static __device__ __align__(256) float g_unmask_static_scratch[(PDLLM_UNMASK_STATIC_MAX_BLOCK * (3 * kUnmaskChunks + 3) + 1 + 63) / 64 * 64];
+
+// The array's name is only a host-side handle: the device address has to be looked up, per device, with that device
+// current. Done on the first call for a device and cached.
+static int unmask_static_scratch_ptr(float** out) {
+  static std::mutex mu;
+  static float* cached[64] = {nullptr};
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return fail(static_cast<int>(e), "cudaGetDevice: %s", cudaGetErrorString(e));
+  if (dev < 0 || dev >= 64) return fail(PDLLM_E_UNSUPPORTED, "unmask_step_static: device ordinal %d not supported", dev);
+  std::lock_guard<std::mutex> lock(mu);
+  if (cached[dev] == nullptr) {
+    void* ptr = nullptr;
+    e = cudaGetSymbolAddress(&ptr, g_unmask_static_scratch);
+    if (e != cudaSuccess || ptr == nullptr)
+      return fail(e != cudaSuccess ? static_cast<int>(e) : PDLLM_E_DRIVER, "cudaGetSymbolAddress(unmask scratch): %s", cudaGetErrorString(e));
+    cached[dev] = static_cast<float*>(ptr);
+  }
+  *out = cached[dev];
+  return 0;
+}
+
+int pdllm_unmask_step_static(const void* logits, int64_t logits_stride, const void* last_logit, int dtype,
+                             int block_len, int64_t vocab, int shift, int64_t* block_ids, int64_t mask_id,
+                             float threshold, int conf_dtype, int32_t* out_counts, float* out_conf,
+                             int64_t* out_x0, void* stream) {
+  if (block_len > PDLLM_UNMASK_STATIC_MAX_BLOCK)
+    return fail(PDLLM_E_INVALID, "unmask_step_static: block_len %d exceeds the built-in scratch (max %d); use pdllm_unmask_step with a caller workspace",
+                block_len, PDLLM_UNMASK_STATIC_MAX_BLOCK);
+  if (block_len <= 0) return fail(PDLLM_E_INVALID, "unmask_step_static: block_len must be positive");
+  float* scratch = nullptr;
+  int rc = unmask_static_scratch_ptr(&scratch);
+  if (rc != 0) return rc;
+  // The counters at the tail of the scratch must be zero when the kernel starts. The kernel leaves them zeroed, but
+  // the array is shared by every call and keeps whatever an interrupted call left: clear them on the stream first.
+  const int64_t words = unmask_ws_words(block_len);
+  const int64_t counter_words = block_len + 1;
+  cudaError_t e = cudaMemsetAsync(scratch + (words - counter_words), 0, counter_words * 4, as_stream(stream));
+  if (e != cudaSuccess) return fail(static_cast<int>(e), "cudaMemsetAsync: %s", cudaGetErrorString(e));
+  return pdllm_unmask_step(logits, logits_stride, last_logit, dtype, block_len, vocab, shift, block_ids, mask_id, threshold,
+                           conf_dtype, out_counts, out_conf, out_x0, scratch, words * 4, stream);
 }
 
 // ------------------------------------------------------------------------------------------------ (2a)(2b)
