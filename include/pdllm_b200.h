@@ -253,6 +253,18 @@ int pdllm_compact_pages_per_head(void* cache, const int32_t* src_page_ids, const
                                  int elem_bytes, int64_t num_pages, void* staging, int32_t* status,
                                  void* stream);
 
+/* Rotary embedding of K rows that are already in pages and were stored UN-rotated: tokens [start, start + n_tokens)
+ * of the page list, every KV head, in place; cos_tab / sin_tab are [n_tokens, head_dim] in the cache dtype (the
+ * model's own tables: cat(freqs, freqs)). Arithmetic rounds each product and the sum to the cache dtype, like the
+ * eager `k * cos + rotate_half(k) * sin`.
+ * Serves the eval class's per-head eviction, whose model caches un-rotated keys and rotates them at read time
+ * with the COMPACTED positions (kept row j of every head gets chunk_positions[j], not its original position):
+ *   prefilling_dllm_eval/fastdllm_parallelcomp.py:1076-1125 (_gather_cache_per_layer_per_head), :2284-2288,
+ *   :2890-2912 (active_positions_after_prefill). */
+int pdllm_rope_pages(void* k_cache, const int32_t* page_ids, int64_t start, int64_t n_tokens, const void* cos_tab,
+                     const void* sin_tab, int page_size, int num_kv_heads, int head_dim, int dtype,
+                     int64_t num_pages, int32_t* status, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

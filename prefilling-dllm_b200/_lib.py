@@ -92,6 +92,8 @@ _SIGNATURES = {
     "pdllm_scatter_pages": (c_int, [c_void_p, c_void_p, c_int64, c_int, c_int64, c_int, c_int64, c_void_p, c_void_p, c_void_p]),
     "pdllm_compact_pages_per_head": (c_int, [c_void_p, c_void_p, c_void_p, c_void_p, c_int64, c_int64, c_int64, c_int, c_int,
                                              c_int, c_int, c_int64, c_void_p, c_void_p, c_void_p]),
+    "pdllm_rope_pages": (c_int, [c_void_p, c_void_p, c_int64, c_int64, c_void_p, c_void_p, c_int, c_int, c_int, c_int, c_int64,
+                                 c_void_p, c_void_p]),
 }
 
 EXPORTED_SYMBOLS = tuple(_SIGNATURES)

@@ -199,6 +199,42 @@ __global__ void compact_scatter_kernel(uint4* __restrict__ cache, const int32_t*
   }
 }
 
+// ---- rotary embedding applied to rows already in pages -----------------------------------------------
+// K rows of tokens [start, start + n) were stored UN-rotated; rotate them in place with the table row of each
+// token: out = x * cos + rotate_half(x) * sin, every product and the sum rounded to T as the eager model
+// computes them (no fused multiply-add). One thread per (token, head, pair i / i + D/2).
+template <typename T>
+__global__ void rope_pages_kernel(T* __restrict__ cache, const int32_t* __restrict__ page_ids, int64_t start,
+                                  int64_t n_tokens, const T* __restrict__ cos_tab, const T* __restrict__ sin_tab,
+                                  int page_size, int num_kv_heads, int head_dim, int64_t num_pages,
+                                  int32_t* status) {
+  const int half = head_dim / 2;
+  const int64_t per_tok = static_cast<int64_t>(num_kv_heads) * half;
+  const int64_t total = n_tokens * per_tok;
+  int64_t idx = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+  for (; idx < total; idx += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    int64_t j = idx / per_tok;
+    int rem = static_cast<int>(idx - j * per_tok);
+    int h = rem / half, i = rem - h * half;
+    int64_t tok = start + j;
+    int64_t page = page_ids[tok / page_size];
+    if (page < 0 || page >= num_pages) {
+      if (rem == 0) report_status(status, PDLLM_S_BAD_PAGE);
+      continue;
+    }
+    T* row = cache + ((page * page_size + tok % page_size) * num_kv_heads + h) * head_dim;
+    const T* c = cos_tab + j * head_dim;
+    const T* s = sin_tab + j * head_dim;
+    float x1 = to_f32<T>(row[i]), x2 = to_f32<T>(row[i + half]);
+    float a1 = to_f32<T>(from_f32<T>(__fmul_rn(x1, to_f32<T>(c[i]))));
+    float b1 = to_f32<T>(from_f32<T>(__fmul_rn(-x2, to_f32<T>(s[i]))));
+    float a2 = to_f32<T>(from_f32<T>(__fmul_rn(x2, to_f32<T>(c[i + half]))));
+    float b2 = to_f32<T>(from_f32<T>(__fmul_rn(x1, to_f32<T>(s[i + half]))));
+    row[i] = from_f32<T>(__fadd_rn(a1, b1));
+    row[i + half] = from_f32<T>(__fadd_rn(a2, b2));
+  }
+}
+
 inline int grid_for(int64_t work_items, int threads) {
   int64_t blocks = (work_items + threads - 1) / threads;
   int64_t cap = static_cast<int64_t>(sm_count()) * 16;  // a few resident CTAs per SM, grid-stride beyond

@@ -361,6 +361,27 @@ int pdllm_scatter_pages(const void* src, const int32_t* page_ids, int64_t n_toke
   return check_launch("scatter_pages");
 }
 
+int pdllm_rope_pages(void* k_cache, const int32_t* page_ids, int64_t start, int64_t n_tokens, const void* cos_tab,
+                     const void* sin_tab, int page_size, int num_kv_heads, int head_dim, int dtype,
+                     int64_t num_pages, int32_t* status, void* stream) {
+  if (n_tokens < 0 || start < 0 || page_size <= 0 || num_kv_heads <= 0 || head_dim <= 0 || head_dim % 2 != 0)
+    return fail(PDLLM_E_INVALID, "rope_pages: bad sizes");
+  if (n_tokens == 0) return 0;
+  if (!k_cache || !page_ids || !cos_tab || !sin_tab) return fail(PDLLM_E_INVALID, "rope_pages: null pointer");
+  const int grid = grid_for(n_tokens * num_kv_heads * (head_dim / 2), 256);
+#define PDLLM_ROPE_LAUNCH(T)                                                                                        \
+  rope_pages_kernel<T><<<grid, 256, 0, as_stream(stream)>>>(static_cast<T*>(k_cache), page_ids, start, n_tokens,    \
+                                                            static_cast<const T*>(cos_tab),                         \
+                                                            static_cast<const T*>(sin_tab), page_size,              \
+                                                            num_kv_heads, head_dim, num_pages, status)
+  if (dtype == PDLLM_F32) PDLLM_ROPE_LAUNCH(float);
+  else if (dtype == PDLLM_BF16) PDLLM_ROPE_LAUNCH(__nv_bfloat16);
+  else if (dtype == PDLLM_F16) PDLLM_ROPE_LAUNCH(__half);
+  else return fail(PDLLM_E_UNSUPPORTED, "rope_pages: dtype must be f32, bf16 or f16");
+#undef PDLLM_ROPE_LAUNCH
+  return check_launch("rope_pages");
+}
+
 int pdllm_compact_pages_per_head(void* cache, const int32_t* src_page_ids, const int32_t* dst_page_ids,
                                  const int64_t* keep, int64_t keep_count, int64_t src_tokens,
                                  int64_t dst_start, int page_size, int num_kv_heads, int head_dim,

@@ -289,10 +289,16 @@ class PagedDreamModel:
                 slot_mapping: Optional[torch.Tensor] = None, block_table: Optional[torch.Tensor] = None,
                 seq_lens: Optional[torch.Tensor] = None, max_seq_len: int = 0, causal: bool = False,
                 logit_rows: Optional[torch.Tensor] = None, want_logits: bool = True,
-                capture_qk_layers: Optional[Sequence[int]] = None):
+                capture_qk_layers: Optional[Sequence[int]] = None, store_after_attention: bool = False,
+                store_unrotated_k: bool = False):
         """Packed forward of `ids` [T] (several sequences delimited by cu_seqlens) at RoPE `positions` [T].
 
         slot_mapping [T] int32 (optional): where each row's K/V goes in the pool (-1 = do not store).
+        store_after_attention: write the rows' K/V only after the layer's attention has read the pool, for a forward whose
+        target slots still hold keys that this same forward must attend (committing a finished block over stale slots).
+        store_unrotated_k: the K written to the pool is the projection BEFORE the rotary embedding (attention over the rows
+        themselves still uses rotated keys); the caller rotates the stored rows later with `rope_rows` — per-head
+        eviction assigns positions only after compaction.
         block_table / seq_lens (optional): cached context each sequence attends before its own rows.
         causal: scoring mask (row sees itself and earlier rows); otherwise rows see each other bidirectionally.
         logit_rows: indices of the rows whose logits are wanted (LM head runs on those rows only).
@@ -313,14 +319,16 @@ class PagedDreamModel:
             q = qkv[:, : hq * d].view(total, hq, d)
             k = qkv[:, hq * d: (hq + hkv) * d].view(total, hkv, d)
             v = qkv[:, (hq + hkv) * d:].view(total, hkv, d)
+            k_raw = k.contiguous() if store_unrotated_k else None
             q = (q * cos + self._rotate_half(q) * sin).contiguous()
             k = (k * cos + self._rotate_half(k) * sin).contiguous()
+            k_store = k_raw if store_unrotated_k else k
             v = v.contiguous()
             if li in capture:
                 captured[li] = (q, k)
             k_cache, v_cache = self.layer_cache(li)
-            if slot_mapping is not None:
-                ops.store_kvcache_unified_layout(k, v, k_cache, v_cache, slot_mapping, "diffusion_lm")
+            if slot_mapping is not None and not store_after_attention:
+                ops.store_kvcache_unified_layout(k_store, v, k_cache, v_cache, slot_mapping, "diffusion_lm")
             if block_table is not None:
                 ops.paged_attention(q, k, v, attn_out, cu_seqlens_q=cu_seqlens, max_query_len=max_query_len, key_cache=k_cache,
                                     value_cache=v_cache, block_table=block_table, seq_lens=seq_lens, max_seq_len=max_seq_len,
@@ -328,6 +336,8 @@ class PagedDreamModel:
             else:
                 ops.paged_attention(q, k, v, attn_out, cu_seqlens_q=cu_seqlens, max_query_len=max_query_len,
                                     sm_scale=self.scale, causal=causal, bidirectional=True)
+            if slot_mapping is not None and store_after_attention:
+                ops.store_kvcache_unified_layout(k_store, v, k_cache, v_cache, slot_mapping, "diffusion_lm")
             x = x + F.linear(attn_out.view(total, hq * d), w["wo"])
             h = self._rmsnorm(x, w["ln2"])
             gu = F.linear(h, w["wgu"])
@@ -338,6 +348,14 @@ class PagedDreamModel:
             rows = x if logit_rows is None else x.index_select(0, logit_rows)
             logits = F.linear(self._rmsnorm(rows, self.final_norm), self.lm_head)
         return logits, captured
+
+    def rope_rows(self, page_ids, start: int, positions: Sequence[int]) -> None:
+        """Rotate the un-rotated K rows `[start, start + len(positions))` of `page_ids` in place, in every layer."""
+        if not positions:
+            return
+        cos, sin = self._rope_tables(torch.tensor(list(positions), dtype=torch.long, device=self.device))
+        for layer in range(self.arch.num_hidden_layers):
+            ops.rope_pages(self.layer_cache(layer)[0], page_ids, start, cos, sin)
 
     # ---- small tensor helpers ----
     def ids_tensor(self, ids: Sequence[int]) -> torch.Tensor:

@@ -530,3 +530,23 @@ def compact_pages_per_head(cache: torch.Tensor, src_page_ids, dst_page_ids, keep
                                                    keep_count, int(src_tokens), int(dst_start), page_size, hkv, d,
                                                    cache.element_size(), cache.shape[0], staging.data_ptr(),
                                                    status_word(device).data_ptr(), _stream(device)))
+
+
+def rope_pages(k_cache: torch.Tensor, page_ids, start: int, cos: torch.Tensor, sin: torch.Tensor) -> None:
+    """Rotate, in place, the K rows of tokens `[start, start + n)` of a unified pool that were stored un-rotated.
+
+    cos / sin: `[n, D]` (or `[n, 1, D]`) tables in the cache dtype. Used after a per-head compaction, where kept row j of
+    every head takes position j of the compacted span (reference eval class :2284-2288, :2890-2912)."""
+    device = _require_cuda(k_cache, cos, sin)
+    _, page_size, hkv, d = k_cache.shape
+    cos = cos.reshape(-1, d).contiguous()
+    sin = sin.reshape(-1, d).contiguous()
+    n = cos.shape[0]
+    if sin.shape != cos.shape or cos.dtype != k_cache.dtype or sin.dtype != k_cache.dtype:
+        raise ValueError("cos / sin must be [n, head_dim] tables in the cache dtype")
+    ids = _page_ids_tensor(page_ids, device)
+    if start < 0 or start + n > ids.numel() * page_size:
+        raise ValueError("token range exceeds the capacity of page_ids")
+    check(_lib.load().pdllm_rope_pages(k_cache.data_ptr(), ids.data_ptr(), int(start), n, cos.data_ptr(), sin.data_ptr(), page_size,
+                                       hkv, d, dtype_code(k_cache.dtype), k_cache.shape[0], status_word(device).data_ptr(),
+                                       _stream(device)))

@@ -1,0 +1,977 @@
+"""GPU-native runtime with the public interface of the reference's `FastDLLMParallelComp`.
+
+Reference: prefilling_dllm_eval/fastdllm_parallelcomp.py — config dataclass :43-110, result dataclasses :113-142,
+`split_token_chunks` :158-180, class `FastDLLMParallelComp` :368 with `select_chunks` :1857, `build_prefill_cache`
+:2201, `generate_from_cache` :2678, `generate_full_prompt_mask` :2776, `generate` :3026, `generate_from_text_parts`
+:3093, factory `load_fastdllm_parallelcomp` :3113. Same names, arguments, result fields and exception types; the
+algorithm steps (chunk BOS truncation, draft rounds, label set of the self-information score, stable top-K, keep
+lists, RoPE position modes, dual-cache block denoising) follow the reference line by line in BEHAVIOUR, but the
+machinery is different: KV lives in a paged pool instead of per-call tensor lists, evicted tokens are dropped by the
+slot mapping of the page write, every model call is a packed var-len forward over the sm_100a kernels, and the
+sampling / scoring tails are single fused kernels (`ops.unmask_step`, `ops.self_information_scores`, ...).
+
+Where the reference hands tensors around (`past_key_values`), this class hands a `PagedCache` handle.
+Not built (raise NotImplementedError): sampling with temperature / top-p / top-k, `alg` other than
+"confidence_threshold", score modes other than none / self_information / draft_self_information, avg-pooling and
+non-default head/layer reductions, the LLaDA leave-one-out scorer.
+"""
+
+from __future__ import annotations
+
+import math
+import os
+import time
+from dataclasses import dataclass, field, fields, is_dataclass
+from typing import Dict, List, Optional, Sequence, Tuple
+
+import torch
+
+from . import ops
+from .model import DreamArch, PagedDreamModel, slots_for
+
+
+@dataclass
+class FastDLLMParallelCompConfig:
+    """Field-for-field the reference's config (fastdllm_parallelcomp.py:43-110)."""
+
+    fastdllm_dream_dir: str
+    pretrained: str
+    model_backend: str = "dream"
+    fastdllm_llada_dir: Optional[str] = None
+    device: str = "cuda"
+    dtype: str = "auto"
+    trust_remote_code: bool = True
+    llada_score_batch_size: int = 8
+
+    max_new_tokens: int = 32
+    max_length: int = 4096
+    block_length: int = 32
+    diffusion_steps: Optional[int] = None
+    temperature: float = 0.0
+    top_p: Optional[float] = None
+    top_k: Optional[int] = None
+    alg: str = "confidence_threshold"
+    alg_temp: Optional[float] = 0.0
+    threshold: float = 0.9
+    add_bos_token: bool = True
+    rope_scale_factor: float = 1.0
+    rope_scaling_type: str = "yarn"
+
+    chunk_size: int = 1024
+    topk_chunks: int = 4
+    keep_first_chunk: bool = False
+    split_from_tail: bool = False
+    chunk_bos: bool = True
+    force_keep_chunk_bos: bool = True
+    cache_build_mode: str = "chunk_query"
+
+    score_mode: str = "draft_self_information"
+    score_query_window: int = 0
+    score_draft_tokens: int = 16
+    score_draft_steps: Optional[int] = None
+    score_draft_fixed_steps: bool = False
+    score_draft_partial_steps: Optional[int] = None
+    score_draft_partial_rounds: Optional[int] = None
+    score_draft_score_all_slots: bool = False
+    score_llada_shift_logits: bool = False
+    score_attention_mask: str = "causal"
+    score_context_mode: str = "single_chunk"
+    score_batch_size: int = 8
+    attention_score_layers: int = 4
+    attention_query_window: int = 0
+
+    token_capacity: int = 0
+    token_score_query_window: int = 8
+    token_score_layers: int = 0
+    token_score_layer_mode: str = "all"
+    token_score_reduce: str = "sum"
+    token_score_pooling: str = "maxpool"
+    token_score_pool_kernel: int = 7
+    token_score_head_reduce: str = "sum"
+    token_score_layer_reduce: str = "mean"
+    token_score_direction: str = "query_to_chunk"
+    token_score_keep: str = "high"
+    token_score_include_prefix: bool = True
+    token_attention_mask: str = "causal"
+    token_score_use_generated: bool = False
+    token_eviction_granularity: str = "global"
+
+    chunk_position_mode: str = "reuse"
+    chunk_query_position_mode: str = "after_reused_window"
+    query_position_mode: str = "after_reused_window"
+    generation_position_mode: str = "after_query"
+
+    # not in the reference: size of the paged KV pool (pages of 256 tokens); 0 = derive from max_length
+    num_kv_pages: int = 0
+
+
+@dataclass
+class FastDLLMChunkMeta:
+    chunk_index: int
+    original_tokens: int
+    kept_tokens: int
+    removed_tokens: int
+    cache_start: int
+    cache_end: int
+    rope_start: int
+    rope_end: int
+    score: Optional[float] = None
+    kept_positions: List[int] = field(default_factory=list)
+
+
+@dataclass
+class FastDLLMParallelCompResult:
+    text: str
+    sequences: List[int]
+    selected_chunk_indices: List[int]
+    chunk_scores: Dict[int, float]
+    cache_build_mode: str
+    prefix_tokens: int
+    query_tokens: int
+    raw_context_tokens: int
+    candidate_chunks: int
+    cache_tokens: int
+    removed_tokens: int
+    chunk_meta: List[FastDLLMChunkMeta]
+    generation_blocks: int
+    generation_block_length: int
+
+
+def dataclass_to_jsonable(obj):
+    if is_dataclass(obj):
+        return {f.name: dataclass_to_jsonable(getattr(obj, f.name)) for f in fields(obj)}
+    if isinstance(obj, dict):
+        return {k: dataclass_to_jsonable(v) for k, v in obj.items()}
+    if isinstance(obj, (list, tuple)):
+        return [dataclass_to_jsonable(v) for v in obj]
+    return obj
+
+
+def split_token_chunks(token_ids: Sequence[int], chunk_size: int, split_from_tail: bool = False) -> List[List[int]]:
+    """Fixed-size split; with `split_from_tail` a leading remainder chunk (reference :158-180)."""
+    ids = list(token_ids)
+    if not ids:
+        return []
+    if chunk_size <= 0 or len(ids) <= chunk_size:
+        return [ids]
+    out: List[List[int]] = []
+    start = len(ids) % chunk_size if split_from_tail else 0
+    if start:
+        out.append(ids[:start])
+    out.extend(ids[i:i + chunk_size] for i in range(start, len(ids), chunk_size))
+    return out
+
+
+class PagedCache:
+    """Handle to a request's KV in the paged pool: logical token order → pages, plus the RoPE position of each token."""
+
+    def __init__(self, runtime: "FastDLLMParallelComp", capacity_tokens: int):
+        self.model = runtime.model
+        n_pages = max(1, math.ceil(capacity_tokens / self.model.page_size))
+        self.model.allocator.ensure_free(n_pages)
+        self.page_ids: List[int] = self.model.allocator.allocate_pages(n_pages)
+        self.length = 0                    # tokens currently valid
+        self.positions: List[int] = []     # RoPE position of every valid token
+        self._table = self.model.i32(self.page_ids).view(1, -1)
+        self.released = False
+
+    @property
+    def capacity(self) -> int:
+        return len(self.page_ids) * self.model.page_size
+
+    def slots(self, start: int, n: int) -> List[int]:
+        if start + n > self.capacity:
+            raise RuntimeError(f"paged cache overflow: need {start + n} tokens, capacity {self.capacity}")
+        return slots_for(self.page_ids, start, n, self.model.page_size)
+
+    def table(self) -> torch.Tensor:
+        return self._table
+
+    def release(self) -> None:
+        if not self.released:
+            self.model.allocator.release_pages(self.page_ids)
+            self.released = True
+
+
+class _SimpleTokenizer:
+    """Stand-in when the checkpoint ships no tokenizer files: ids only."""
+
+    def __init__(self, arch: DreamArch):
+        self.bos_token_id = arch.bos_token_id
+        self.eos_token_id = arch.eos_token_id
+        self.mask_token_id = arch.mask_token_id
+        self.eos_token = None
+        self.bos_token = None
+
+    def encode(self, text, add_special_tokens=False):
+        raise NotImplementedError("this checkpoint has no tokenizer; pass token ids")
+
+    def decode(self, ids, skip_special_tokens=False):
+        return " ".join(str(int(i)) for i in ids)
+
+
+class FastDLLMParallelComp:
+    def __init__(self, config: FastDLLMParallelCompConfig, model: Optional[PagedDreamModel] = None, tokenizer=None):
+        self.config = config
+        self.model_backend = (config.model_backend or "dream").lower()
+        if self.model_backend not in {"dream", "llada"}:
+            raise ValueError(f"Unsupported model_backend: {config.model_backend}")
+        if not torch.cuda.is_available():
+            raise RuntimeError("FastDLLMParallelComp (B200) needs a CUDA device; there is no CPU path")
+        self.device = torch.device(config.device if str(config.device).startswith("cuda") else "cuda")
+        if self.device.index is None:
+            self.device = torch.device("cuda", torch.cuda.current_device())
+        self.max_new_tokens = int(config.max_new_tokens)
+        self.block_length = int(config.block_length)
+        if self.max_new_tokens <= 0:
+            raise ValueError("max_new_tokens must be positive")
+        if self.block_length <= 0:
+            raise ValueError("block_length must be positive")
+        self.diffusion_steps = int(config.diffusion_steps) if config.diffusion_steps is not None else max(
+            1, math.ceil(self.max_new_tokens / self.block_length))
+        if config.token_score_direction not in {"query_to_chunk", "chunk_to_query", "bidirectional"}:
+            raise ValueError(f"Unsupported token_score_direction: {config.token_score_direction}")
+        if config.token_score_keep not in {"high", "low"}:
+            raise ValueError(f"Unsupported token_score_keep: {config.token_score_keep}")
+        if config.token_eviction_granularity not in {"global", "per_head"}:
+            raise ValueError(f"Unsupported token_eviction_granularity: {config.token_eviction_granularity}")
+        if config.temperature and config.temperature > 0 or config.top_p is not None or config.top_k is not None:
+            raise NotImplementedError("only greedy decoding (temperature 0, no top-p / top-k) is built")
+        if config.alg != "confidence_threshold":
+            raise NotImplementedError(f"alg={config.alg!r} is not built; only 'confidence_threshold'")
+        if config.token_score_direction != "query_to_chunk":
+            raise NotImplementedError("only token_score_direction='query_to_chunk' is built")
+        if float(config.rope_scale_factor or 1.0) > 1.0:
+            raise NotImplementedError("RoPE (YaRN) scaling is not built")
+
+        if model is None:
+            dtype = _resolve_dtype(config.dtype)
+            arch = DreamArch.from_pretrained(config.pretrained)
+            if self.model_backend == "llada":
+                arch.logit_shift = False
+            if dtype in (None, "auto"):
+                dtype = torch.bfloat16
+            pages = int(config.num_kv_pages) or (4 * math.ceil((config.max_length + config.max_new_tokens) / 256) + 8)
+            model = PagedDreamModel.from_pretrained(config.pretrained, device=self.device, dtype=dtype, num_pages=pages, arch=arch)
+        self.model = model
+        self.arch = model.arch
+        if tokenizer is None:
+            tokenizer = _load_tokenizer(config.pretrained, config.trust_remote_code) or _SimpleTokenizer(self.arch)
+        self.tokenizer = tokenizer
+        self.generated_token_num = 0
+        self.total_generation_time = 0.0
+
+    # ------------------------------------------------------------------------------------------------ small helpers
+    def _mask_token_id(self) -> int:
+        mask = getattr(self.tokenizer, "mask_token_id", None)
+        if mask is None:
+            mask = self.arch.mask_token_id
+        if mask is None:
+            raise ValueError(f"Fast-dLLM {self.model_backend} mask_token_id is not available")
+        return int(mask)
+
+    def _get_bos_token_ids(self) -> List[int]:
+        bos = getattr(self.tokenizer, "bos_token_id", None)
+        if bos is not None:
+            return [int(bos)]
+        token = getattr(self.tokenizer, "bos_token", None)
+        if token:
+            return self.tokenizer.encode(token, add_special_tokens=False)
+        return []
+
+    def _maybe_prepend_bos_to_chunk(self, chunk_ids: Sequence[int]) -> List[int]:
+        ids = list(chunk_ids)
+        if not self.config.chunk_bos:
+            return ids
+        bos = self._get_bos_token_ids()
+        if not bos or ids[:len(bos)] == bos:
+            return ids
+        out = bos + ids
+        size = int(self.config.chunk_size or 0)
+        return out[:size] if size > 0 and len(out) > size else out  # a full chunk loses its last token (reference :904-908)
+
+    @staticmethod
+    def _window_query(query_ids: Sequence[int], window: int) -> List[int]:
+        ids = list(query_ids)
+        return ids[-window:] if window and window > 0 else ids
+
+    @staticmethod
+    def _range_positions(start: int, length: int) -> List[int]:
+        return list(range(int(start), int(start) + int(length)))
+
+    def _chunk_rope_start(self, prefix_len: int, chunk_order: int, chunk_index: int) -> int:
+        mode = self.config.chunk_position_mode
+        size = max(1, self.config.chunk_size)
+        if mode == "reuse":
+            return prefix_len
+        if mode == "continuous":
+            return prefix_len + chunk_order * size
+        if mode == "absolute":
+            return prefix_len + chunk_index * size
+        raise ValueError(f"Unsupported chunk_position_mode: {mode}")
+
+    def _chunk_query_rope_start(self, prefix_len: int, chunk_start: int, chunk_len: int) -> int:
+        mode = self.config.chunk_query_position_mode
+        if mode == "after_reused_window":
+            return prefix_len + max(1, self.config.chunk_size)
+        if mode == "after_chunk":
+            return chunk_start + chunk_len
+        raise ValueError(f"Unsupported chunk_query_position_mode: {mode}")
+
+    def _final_query_rope_start(self, prefix_len: int, cache_positions: Sequence[int], selected_count: int) -> int:
+        mode = self.config.query_position_mode
+        if mode == "after_reused_window":
+            return prefix_len + max(1, self.config.chunk_size)
+        if mode == "after_selected_chunks":
+            return prefix_len + selected_count * max(1, self.config.chunk_size)
+        if mode == "after_cache":
+            return (max(cache_positions) + 1) if cache_positions else prefix_len
+        raise ValueError(f"Unsupported query_position_mode: {mode}")
+
+    def _select_attention_layer_indices(self, total_layers: int, layer_window: int, layer_mode: str) -> List[int]:
+        if total_layers <= 0:
+            return []
+        if layer_mode == "all" or layer_window <= 0:
+            return list(range(total_layers))
+        window = min(max(1, int(layer_window)), total_layers)
+        if layer_mode == "first":
+            return list(range(window))
+        if layer_mode == "last":
+            return list(range(total_layers - window, total_layers))
+        raise ValueError(f"Unsupported attention layer mode: {layer_mode}")
+
+    @staticmethod
+    def _mask_is_causal(mode: str) -> bool:
+        mode = (mode or "full").lower()
+        if mode in {"full", "none"}:
+            return False
+        if mode == "causal":
+            return True
+        if mode == "query_to_chunk":
+            raise NotImplementedError("attention mask 'query_to_chunk' is not built")
+        raise ValueError(f"Unsupported attention mask mode: {mode}")
+
+    # ------------------------------------------------------------------------------------------------ model calls
+    def _forward_packed(self, seqs_ids: Sequence[Sequence[int]], seqs_positions: Sequence[Sequence[int]], *, causal: bool,
+                        cache: Optional[PagedCache] = None, ctx_len: int = 0, store_slots: Optional[Sequence[int]] = None,
+                        logit_rows: Optional[Sequence[int]] = None, want_logits: bool = True, capture_layers=None,
+                        ids_tensor: Optional[torch.Tensor] = None, store_after_attention: bool = False,
+                        store_unrotated_k: bool = False):
+        """One packed forward over several sequences; every sequence sees the first `ctx_len` tokens of `cache`."""
+        m = self.model
+        flat_pos = [p for seq in seqs_positions for p in seq]
+        if ids_tensor is None:
+            ids_tensor = m.ids_tensor([t for seq in seqs_ids for t in seq])
+        lens = [len(seq) for seq in seqs_positions]
+        cu = [0]
+        for n in lens:
+            cu.append(cu[-1] + n)
+        kwargs = {}
+        if cache is not None and ctx_len > 0:
+            kwargs = dict(block_table=cache.table().expand(len(lens), -1).contiguous(),
+                          seq_lens=m.i32([ctx_len + n for n in lens]), max_seq_len=ctx_len + max(lens))
+        return m.forward(ids_tensor, torch.tensor(flat_pos, dtype=torch.long, device=m.device), cu_seqlens=m.i32(cu),
+                         max_query_len=max(lens), slot_mapping=None if store_slots is None else m.i32(store_slots),
+                         causal=causal, logit_rows=None if logit_rows is None else m.ids_tensor(logit_rows),
+                         want_logits=want_logits, capture_qk_layers=capture_layers, store_after_attention=store_after_attention,
+                         store_unrotated_k=store_unrotated_k, **kwargs)
+
+    # ------------------------------------------------------------------------------------------------ draft
+    @torch.inference_mode()
+    def generate_partial_draft_rounds_from_cache(self, *, past_key_values: Optional[PagedCache], cache_positions: Sequence[int],
+                                                 query_ids: Sequence[int], query_rope_start: int, max_new_tokens: int,
+                                                 partial_rounds: int) -> Tuple[List[int], List[bool]]:
+        """Draft `max_new_tokens` slots after the query: slot 0 from the last context logit, then `partial_rounds` rounds
+        each confirming the single most confident masked slot (reference :2595-2676). Unfilled slots stay MASK."""
+        draft_len = int(max_new_tokens)
+        if draft_len <= 0:
+            return [], []
+        if past_key_values is not None:
+            raise NotImplementedError("drafting on top of an existing cache is not needed by the selection path")
+        query_ids = list(query_ids)
+        mask_id = self._mask_token_id()
+        q_pos = self._range_positions(query_rope_start, len(query_ids))
+        cache = PagedCache(self, len(query_ids) + draft_len)
+        try:
+            last_logit = None
+            if query_ids:
+                logits, _ = self._forward_packed([query_ids], [q_pos], causal=False, store_slots=cache.slots(0, len(query_ids)),
+                                                 logit_rows=[len(query_ids) - 1])
+                last_logit = logits[0]
+                cache.length = len(query_ids)
+            block_pos = self._range_positions(query_rope_start + len(query_ids), draft_len)
+            block = torch.full((draft_len,), mask_id, dtype=torch.long, device=self.device)
+            confirmed = torch.zeros(draft_len, dtype=torch.bool, device=self.device)
+            if last_logit is not None:
+                block[0] = torch.argmax(last_logit)  # softmax is monotone: the arg-max of the logit
+            else:
+                raise ValueError("draft needs at least one context token")
+            confirmed[0] = True
+            for _ in range(max(0, int(partial_rounds))):
+                before = block.clone()
+                logits, _ = self._forward_packed([[0] * draft_len], [block_pos], causal=False, cache=cache, ctx_len=cache.length,
+                                                 ids_tensor=block)
+                # only the top-1 slot is transferred in a draft round: a threshold above any probability
+                ops.unmask_step(logits, block, mask_token_id=mask_id, threshold=2.0, last_logit=last_logit,
+                                shift=self.arch.logit_shift)
+                confirmed |= block != before
+            return block.tolist(), confirmed.tolist()
+        finally:
+            cache.release()
+
+    def _selection_query_ids_with_score_target(self, prefix_ids, scoring_query_ids):
+        selection = list(scoring_query_ids)
+        score_token_mask: Optional[List[bool]] = None
+        cfg = self.config
+        if cfg.score_mode == "draft_self_information" and cfg.score_draft_tokens > 0:
+            if cfg.score_draft_partial_rounds is None:
+                raise NotImplementedError("score_draft_partial_rounds=None (full draft generation) is not built; set it (README uses 1)")
+            draft_ids, draft_mask = self.generate_partial_draft_rounds_from_cache(
+                past_key_values=None, cache_positions=[], query_ids=list(prefix_ids) + list(scoring_query_ids), query_rope_start=0,
+                max_new_tokens=int(cfg.score_draft_tokens), partial_rounds=int(cfg.score_draft_partial_rounds))
+            if cfg.score_draft_score_all_slots:
+                score_token_mask = [True] * len(scoring_query_ids) + [True] * len(draft_ids)
+            else:
+                score_token_mask = [True] * len(scoring_query_ids) + list(draft_mask)
+            selection = list(scoring_query_ids) + draft_ids
+        return selection, None, score_token_mask
+
+    # ------------------------------------------------------------------------------------------------ scoring + ranking
+    @torch.inference_mode()
+    def score_chunks_self_information_batched(self, prefix_ids, candidate_chunks, query_ids, score_token_count=None,
+                                              score_token_mask=None) -> Dict[int, float]:
+        """mean log p(label | prefix, chunk, earlier query) per chunk (reference :1314-1423): causal forward of
+        [prefix‖chunk‖query‖draft] rows batched by chunk length, LM head on the label rows only, fused fp32 tail."""
+        cfg = self.config
+        if score_token_count is not None:
+            raise NotImplementedError("score_token_count is not built")
+        if score_token_mask is None:
+            query_ids = self._window_query(query_ids, cfg.score_query_window)
+        query_ids, prefix_ids = list(query_ids), list(prefix_ids)
+        if not query_ids:
+            return {i: float("-inf") for i in range(len(candidate_chunks))}
+        p_len, q_len = len(prefix_ids), len(query_ids)
+        scores: Dict[int, float] = {}
+        groups: Dict[int, List[Tuple[int, List[int]]]] = {}
+        for idx, chunk in enumerate(candidate_chunks):
+            chunk = list(chunk)
+            if not chunk:
+                scores[idx] = float("-inf")
+            else:
+                groups.setdefault(len(chunk), []).append((idx, chunk))
+        causal = self._mask_is_causal(cfg.score_attention_mask)
+        batch_size = max(1, int(cfg.score_batch_size or 1))
+        for c_len, group in groups.items():
+            if score_token_mask is not None:
+                if len(score_token_mask) != q_len:
+                    scores.update({idx: float("-inf") for idx, _ in group})
+                    continue
+                local = [i for i, keep in enumerate(score_token_mask) if keep]
+            else:
+                window = min(q_len, cfg.score_query_window or q_len)
+                local = list(range(q_len - window, q_len))
+            if not local:
+                scores.update({idx: float("-inf") for idx, _ in group})
+                continue
+            label_pos = [p_len + c_len + i for i in local]
+            if min(label_pos) <= 0:
+                scores.update({idx: float("-inf") for idx, _ in group})
+                continue
+            labels = self.model.ids_tensor([query_ids[i] for i in local])
+            row_len = p_len + c_len + q_len
+            positions = list(range(row_len))
+            for off in range(0, len(group), batch_size):
+                batch = group[off:off + batch_size]
+                rows = [prefix_ids + chunk + query_ids for _, chunk in batch]
+                logit_rows = [b * row_len + (p - 1) for b in range(len(batch)) for p in label_pos]  # label p reads logits[p-1]
+                logits, _ = self._forward_packed(rows, [positions] * len(batch), causal=causal, logit_rows=logit_rows)
+                vals = ops.self_information_scores(logits, labels, len(batch)).tolist()
+                for (idx, _), v in zip(batch, vals):
+                    scores[idx] = v if math.isfinite(v) else float("-inf")
+        return scores
+
+    def select_chunks(self, prefix_ids, candidate_chunks, scoring_query_ids):
+        """(selected ascending, scores, selection query ids, label mask) — reference :1857-1953."""
+        cfg = self.config
+        if not candidate_chunks:
+            return [], {}, list(scoring_query_ids), None
+        selection, count, mask = self._selection_query_ids_with_score_target(prefix_ids, scoring_query_ids)
+        if cfg.score_mode == "none" or not selection:
+            selected = list(range(len(candidate_chunks)))
+            if cfg.topk_chunks > 0:
+                selected = selected[:cfg.topk_chunks]
+            return selected, {}, selection, mask
+        if cfg.score_mode not in {"self_information", "draft_self_information"}:
+            raise NotImplementedError(f"score_mode={cfg.score_mode!r} is not built")
+        if cfg.score_context_mode != "single_chunk":
+            raise NotImplementedError(f"score_context_mode={cfg.score_context_mode!r} is not built")
+        scores = self.score_chunks_self_information_batched(prefix_ids, candidate_chunks, selection, score_token_count=count,
+                                                            score_token_mask=mask)
+        dense = torch.tensor([scores.get(i, float("-inf")) for i in range(len(candidate_chunks))], dtype=torch.float32,
+                             device=self.device)
+        sel, cnt = ops.topk_chunks(dense, int(cfg.topk_chunks), bool(cfg.keep_first_chunk))
+        selected = sel[: int(cnt.item())].tolist()
+        return selected, scores, selection, mask
+
+    def _token_eviction_query_ids(self, scoring_query_ids, selection_query_ids, score_token_mask):
+        if not self.config.token_score_use_generated:
+            return list(scoring_query_ids)
+        if score_token_mask is not None and len(score_token_mask) == len(selection_query_ids):
+            return [int(t) for t, keep in zip(selection_query_ids, score_token_mask) if keep]
+        return list(selection_query_ids)
+
+    # ------------------------------------------------------------------------------------------------ token eviction
+    @torch.inference_mode()
+    def _chunk_head_scores(self, prefix_ids, chunk_ids, query_ids) -> Optional[Tuple[torch.Tensor, List[int]]]:
+        """fp32 [selected layers, Hq, chunk_len] query→chunk attention mass of the last `token_score_query_window` query
+        tokens (reference query_attention_token_scores :1531-1637, via the fused scorer instead of eager attention)."""
+        cfg = self.config
+        query_ids = self._window_query(query_ids, cfg.token_score_query_window)
+        if not chunk_ids or not query_ids:
+            return None
+        prefix = list(prefix_ids) if cfg.token_score_include_prefix else []
+        joint = prefix + list(chunk_ids) + list(query_ids)
+        layers = self._select_attention_layer_indices(self.arch.num_hidden_layers, cfg.token_score_layers, cfg.token_score_layer_mode)
+        if not layers:
+            return None
+        causal = self._mask_is_causal(cfg.token_attention_mask)
+        _, captured = self._forward_packed([joint], [list(range(len(joint)))], causal=causal, want_logits=False, capture_layers=layers)
+        per_layer = [ops.query_to_chunk_attention_scores(captured[l][0], captured[l][1], prefix_len=len(prefix), chunk_len=len(chunk_ids),
+                                                         query_len=len(query_ids), scale=self.model.scale,
+                                                         reduce_mode=cfg.token_score_reduce, attention_mask=cfg.token_attention_mask)
+                     for l in layers]
+        return torch.stack(per_layer, dim=0).contiguous(), layers
+
+    def _check_reductions(self):
+        cfg = self.config
+        pooling = (cfg.token_score_pooling or "none").lower()
+        if pooling not in {"none", "maxpool"}:
+            raise NotImplementedError(f"token_score_pooling={pooling!r} is not built (maxpool / none)")
+        if (cfg.token_score_head_reduce or "sum").lower() != "sum" or (cfg.token_score_layer_reduce or "mean").lower() != "mean":
+            raise NotImplementedError("only head_reduce='sum' and layer_reduce='mean' are built")
+        return 1 if pooling == "none" else int(cfg.token_score_pool_kernel or 1)
+
+    def _keep_positions_for_chunk(self, prefix_ids, chunk_ids, query_ids) -> List[int]:
+        cfg = self.config
+        capacity, chunk_len = int(cfg.token_capacity or 0), len(chunk_ids)
+        if capacity <= 0 or chunk_len <= capacity:
+            return list(range(chunk_len))
+        pool_kernel = self._check_reductions()
+        scored = self._chunk_head_scores(prefix_ids, chunk_ids, query_ids)
+        force_bos = bool(cfg.force_keep_chunk_bos and cfg.chunk_bos)
+        if scored is None:
+            head = capacity // 2
+            keep = sorted(set(list(range(head)) + list(range(chunk_len - (capacity - head), chunk_len))))
+        else:
+            keep = ops.evict_select(scored[0], num_kv_heads=self.arch.num_key_value_heads, keep_count=min(max(1, capacity), chunk_len),
+                                    pool_kernel=pool_kernel, per_head=False, force_keep_first=force_bos,
+                                    keep_high=cfg.token_score_keep == "high")[0].tolist()
+        if force_bos and chunk_len > 0:
+            keep = sorted(set([0] + keep))
+            if len(keep) > capacity:
+                keep = sorted([0] + [i for i in keep if i != 0][-max(0, capacity - 1):])
+        return keep
+
+    def _keep_positions_per_layer_per_head_for_chunk(self, prefix_ids, chunk_ids, query_ids) -> List[torch.Tensor]:
+        cfg = self.config
+        capacity, chunk_len = int(cfg.token_capacity or 0), len(chunk_ids)
+        n_layers, hkv = self.arch.num_hidden_layers, self.arch.num_key_value_heads
+        if chunk_len <= 0:
+            return []
+        if capacity <= 0 or chunk_len <= capacity:
+            base = torch.arange(chunk_len, device=self.device, dtype=torch.long)
+            return [base.unsqueeze(0).expand(hkv, -1).clone() for _ in range(n_layers)]
+        pool_kernel = self._check_reductions()
+        keep_count = min(capacity, chunk_len)
+        scored = self._chunk_head_scores(prefix_ids, chunk_ids, query_ids)
+        if scored is None:
+            head = keep_count // 2
+            fb = torch.tensor(sorted(set(list(range(head)) + list(range(chunk_len - (keep_count - head), chunk_len))))[:keep_count],
+                              device=self.device, dtype=torch.long)
+            return [fb.unsqueeze(0).expand(hkv, -1).clone() for _ in range(n_layers)]
+        head_scores, layers = scored
+        keep = ops.evict_select(head_scores, num_kv_heads=hkv, keep_count=keep_count, pool_kernel=pool_kernel, per_head=True,
+                                force_keep_first=bool(cfg.force_keep_chunk_bos and cfg.chunk_bos), keep_high=cfg.token_score_keep == "high")
+        by_layer: List[Optional[torch.Tensor]] = [None] * n_layers
+        for i, l in enumerate(layers):
+            by_layer[l] = keep[i]
+        fallback = keep[0]
+        return [k if k is not None else fallback.clone() for k in by_layer]
+
+    # ------------------------------------------------------------------------------------------------ block denoising
+    def _denoise_blocks(self, cache: PagedCache, *, suffix_pos_start: int, last_logit: torch.Tensor,
+                        first_token: Optional[torch.Tensor], tail_in_cache: int, max_new: int) -> List[int]:
+        """Fast-dLLM dual-cache block loop over the paged cache (reference :2932-2998, :2399-2441).
+
+        Cache layout while block b is active: [prompt ‖ finished blocks ‖ MASK slots of the later blocks]; the active
+        block's rows are the new rows of every forward, so they replace their own slots by construction. After the block
+        is committed its K/V take the place of the first later-MASK slots and the later slots are recomputed.
+        `tail_in_cache`: later-block MASK slots already stored behind the prompt by the prefill (full_prompt_mask mode).
+        """
+        mask_id = self._mask_token_id()
+        n0 = cache.length - tail_in_cache          # prompt (+ query) tokens
+        num_blocks = max(1, math.ceil(max_new / self.block_length))
+        generated: List[int] = []
+        tail_len = tail_in_cache
+        for b in range(num_blocks):
+            start = b * self.block_length
+            blen = min(self.block_length, max_new - start)
+            if blen <= 0:
+                break
+            if self.config.generation_position_mode != "after_query":
+                raise ValueError(f"Unsupported generation_position_mode: {self.config.generation_position_mode}")
+            done = n0 + start                       # prompt + finished blocks
+            block_pos = self._range_positions(suffix_pos_start + start, blen)
+            later = max_new - start - blen          # MASK slots of the blocks after this one
+            if first_token is None or b > 0:
+                # suffix initialisation (reference :2368-2397): forward all remaining MASKs against prompt+finished; the
+                # later blocks' K/V go behind the finished ones, the active block's rows are not stored
+                if later > 0:
+                    suffix_pos = self._range_positions(suffix_pos_start + start, blen + later)
+                    slots = [-1] * blen + cache.slots(done, later)
+                    self._forward_packed([[mask_id] * (blen + later)], [suffix_pos], causal=False, cache=cache, ctx_len=done,
+                                         store_slots=slots, want_logits=False)
+                tail_len = later
+                first = torch.argmax(last_logit) if self.arch.logit_shift else None
+                if first is None:
+                    raise NotImplementedError("un-shifted (LLaDA) block initialisation is not built")
+            else:
+                first = first_token
+            ctx = done + tail_len
+            block = torch.full((blen,), mask_id, dtype=torch.long, device=self.device)
+            block[0] = first
+            guard = 0
+            remaining = blen - 1
+            while remaining > 0:
+                guard += 1
+                if guard > blen + 8:
+                    break
+                logits, _ = self._forward_packed([[0] * blen], [block_pos], causal=False, cache=cache, ctx_len=ctx, ids_tensor=block)
+                counts = ops.unmask_step(logits, block, mask_token_id=mask_id, threshold=float(self.config.threshold),
+                                         last_logit=last_logit, shift=self.arch.logit_shift)
+                remaining = int(counts[2].item())   # the one host read per denoise step
+            generated.extend(block.tolist())
+            # commit forward: the finished block's K/V take the first slots behind prompt+finished; its last logit is the
+            # next block's "last context logit". The store comes after attention so the later-MASK slots are still seen.
+            logits, _ = self._forward_packed([[0] * blen], [block_pos], causal=False, cache=cache, ctx_len=ctx, ids_tensor=block,
+                                             store_slots=cache.slots(done, blen), logit_rows=[blen - 1], store_after_attention=True)
+            last_logit = logits[0]
+            cache.length = done + blen
+            tail_len = 0
+        return generated[:max_new]
+
+    # ------------------------------------------------------------------------------------------------ chunk-local caches
+    @torch.inference_mode()
+    def build_prefill_cache(self, *, prefix_ids, context_ids, query_ids, scoring_query_ids=None):
+        """Independent per-chunk prefill (cache_build_mode chunk_query / chunk_only) → (PagedCache, cache_positions, meta).
+
+        Reference :2201-2328. Each selected chunk is forwarded against the prefix KV only (with the query window behind it
+        in chunk_query mode) and only its kept rows are written to pages — eviction is the slot mapping, no gather."""
+        cfg = self.config
+        prefix_ids, context_ids, query_ids = list(prefix_ids), list(context_ids), list(query_ids)
+        scoring_query_ids = list(scoring_query_ids if scoring_query_ids is not None else query_ids)
+        if cfg.cache_build_mode in {"full_prompt_mask", "full_prompt_query"}:
+            raise ValueError(f"{cfg.cache_build_mode} uses generate_full_prompt_mask instead of build_prefill_cache")
+        if cfg.cache_build_mode not in {"chunk_query", "chunk_only"}:
+            raise ValueError(f"Unsupported cache_build_mode: {cfg.cache_build_mode}")
+        chunks, selected, scores, selection_q, mask = self._prepare_candidate_chunks(prefix_ids=prefix_ids, context_ids=context_ids,
+                                                                                    scoring_query_ids=scoring_query_ids)
+        evict_q = self._token_eviction_query_ids(scoring_query_ids, selection_q, mask)
+        p_len = len(prefix_ids)
+        capacity = p_len + sum(len(chunks[i]) for i in selected) + len(query_ids) + self.max_new_tokens + 2 * self.model.page_size
+        cache = PagedCache(self, capacity)
+        try:
+            prefix_pos = self._range_positions(0, p_len)
+            cache_positions: List[int] = []
+            if prefix_ids:
+                self._forward_packed([prefix_ids], [prefix_pos], causal=False, store_slots=cache.slots(0, p_len), want_logits=False)
+                cache.length = p_len
+                cache_positions.extend(prefix_pos)
+            meta: List[FastDLLMChunkMeta] = []
+            total_removed = 0
+            per_head = cfg.token_eviction_granularity == "per_head"
+            window_q = self._window_query(selection_q, cfg.token_score_query_window)
+            causal = cfg.cache_build_mode == "chunk_query" and self._mask_is_causal(cfg.token_attention_mask)
+            for order, ci in enumerate(selected):
+                chunk = list(chunks[ci])
+                c_start = self._chunk_rope_start(p_len, order, ci)
+                c_pos = self._range_positions(c_start, len(chunk))
+                if per_head:
+                    keep_ph = self._keep_positions_per_layer_per_head_for_chunk(prefix_ids, chunk, evict_q)
+                    keep_union = sorted({int(v) for k in keep_ph for v in k.reshape(-1).tolist()}) if keep_ph else []
+                    kept = int(keep_ph[0].shape[1]) if keep_ph else len(chunk)
+                else:
+                    keep_ph = None
+                    keep_union = self._keep_positions_for_chunk(prefix_ids, chunk, evict_q)
+                    kept = len(keep_union)
+                rows_ids, rows_pos = chunk, c_pos
+                if cfg.cache_build_mode == "chunk_query":
+                    tq_start = self._chunk_query_rope_start(p_len, c_start, len(chunk))
+                    rows_ids = chunk + window_q
+                    rows_pos = c_pos + self._range_positions(tq_start, len(window_q))
+                dst = cache.length
+                if per_head and keep_ph and kept < len(chunk):
+                    # all chunk rows go to a staging area behind the destination, K un-rotated; a per-head compaction moves
+                    # the kept ones; then kept row j of EVERY head is rotated to the j-th chunk position, as the reference's
+                    # model does when it rotates cached keys at read time with the compacted position list (:2284-2288)
+                    stage = dst + kept
+                    slots = cache.slots(stage, len(chunk)) + [-1] * (len(rows_ids) - len(chunk))
+                    self._forward_packed([rows_ids], [rows_pos], causal=causal, cache=cache if p_len else None, ctx_len=p_len,
+                                         store_slots=slots, want_logits=False, store_unrotated_k=True)
+                    for layer in range(self.arch.num_hidden_layers):
+                        for kv in self.model.layer_cache(layer):
+                            ops.compact_pages_per_head(kv, cache.page_ids, cache.page_ids, keep_ph[layer] + stage,
+                                                       src_tokens=stage + len(chunk), dst_start=dst)
+                    kept_pos = c_pos[:kept]
+                    self.model.rope_rows(cache.page_ids, dst, kept_pos)
+                else:
+                    keep_set = set(keep_union)
+                    next_slot = iter(cache.slots(dst, kept))
+                    slots = [next(next_slot) if i in keep_set else -1 for i in range(len(chunk))] + [-1] * (len(rows_ids) - len(chunk))
+                    self._forward_packed([rows_ids], [rows_pos], causal=causal, cache=cache if p_len else None, ctx_len=p_len,
+                                         store_slots=slots, want_logits=False)
+                    kept_pos = [c_pos[i] for i in keep_union]
+                removed = max(0, len(chunk) - kept)
+                total_removed += removed
+                cache.length = dst + kept
+                cache_positions.extend(kept_pos)
+                meta.append(FastDLLMChunkMeta(chunk_index=ci, original_tokens=len(chunk), kept_tokens=kept, removed_tokens=removed,
+                                              cache_start=dst, cache_end=dst + kept, rope_start=c_start, rope_end=c_start + len(chunk),
+                                              score=scores.get(ci), kept_positions=list(keep_union)))
+            cache.positions = list(cache_positions)
+            q_start = self._final_query_rope_start(p_len, cache_positions, selected_count=len(selected))
+        except BaseException:
+            cache.release()
+            raise
+        return cache, cache_positions, {
+            "selected_indices": selected, "chunk_scores": scores, "cache_build_mode": cfg.cache_build_mode, "prefix_tokens": p_len,
+            "query_rope_start": q_start, "raw_context_tokens": len(context_ids), "candidate_chunks": len(chunks),
+            "cache_tokens": cache.length, "removed_tokens": total_removed, "chunk_meta": meta,
+        }
+
+    @torch.inference_mode()
+    def generate_from_cache(self, *, past_key_values: Optional[PagedCache], cache_positions: Sequence[int], query_ids, query_rope_start: int,
+                            max_new_tokens: Optional[int] = None, diffusion_steps=None, force_diffusion: bool = False) -> List[int]:
+        """Prefill the query on top of `past_key_values` (a PagedCache) and denoise block by block (reference :2678-2774)."""
+        if force_diffusion:
+            raise NotImplementedError("force_diffusion (fixed-step diffusion) is not built")
+        max_new = int(max_new_tokens if max_new_tokens is not None else self.max_new_tokens)
+        if max_new <= 0:
+            return []
+        query_ids = list(query_ids)
+        own = past_key_values is None
+        cache = past_key_values if not own else PagedCache(self, len(query_ids) + max_new + self.model.page_size)
+        try:
+            if cache.length + len(query_ids) + max_new > cache.capacity:
+                raise RuntimeError("paged cache too small for the query and the generation blocks")
+            if not query_ids:
+                raise ValueError("generate_from_cache needs a non-empty query")
+            q_pos = self._range_positions(query_rope_start, len(query_ids))
+            base = cache.length
+            logits, _ = self._forward_packed([query_ids], [q_pos], causal=False, cache=cache if base else None, ctx_len=base,
+                                             store_slots=cache.slots(base, len(query_ids)), logit_rows=[len(query_ids) - 1])
+            cache.length = base + len(query_ids)
+            return self._denoise_blocks(cache, suffix_pos_start=query_rope_start + len(query_ids), last_logit=logits[0],
+                                        first_token=None, tail_in_cache=0, max_new=max_new)
+        finally:
+            if own:
+                cache.release()
+
+    # ------------------------------------------------------------------------------------------------ joint prefill
+    def _prepare_candidate_chunks(self, *, prefix_ids, context_ids, scoring_query_ids):
+        chunks = split_token_chunks(context_ids, self.config.chunk_size, split_from_tail=self.config.split_from_tail)
+        chunks = [self._maybe_prepend_bos_to_chunk(c) for c in chunks]
+        selected, scores, selection_q, mask = self.select_chunks(prefix_ids, chunks, scoring_query_ids)
+        return chunks, selected, scores, selection_q, mask
+
+    @torch.inference_mode()
+    def generate_full_prompt_mask(self, *, prefix_ids, context_ids, query_ids, scoring_query_ids=None) -> FastDLLMParallelCompResult:
+        """Select, evict, then ONE bidirectional prefill over [prefix ‖ kept chunk tokens ‖ query (‖ MASKs)] and block
+        denoising (reference :2776-3024)."""
+        t0 = time.time()
+        cfg = self.config
+        prefix_ids, context_ids, query_ids = list(prefix_ids), list(context_ids), list(query_ids)
+        scoring_query_ids = list(scoring_query_ids if scoring_query_ids is not None else query_ids)
+        chunks, selected, scores, selection_q, mask = self._prepare_candidate_chunks(prefix_ids=prefix_ids, context_ids=context_ids,
+                                                                                    scoring_query_ids=scoring_query_ids)
+        evict_q = self._token_eviction_query_ids(scoring_query_ids, selection_q, mask)
+        p_len = len(prefix_ids)
+        prompt_ids, prompt_pos = list(prefix_ids), self._range_positions(0, p_len)
+        cache_positions = list(prompt_pos)
+        meta: List[FastDLLMChunkMeta] = []
+        total_removed, compressed_len = 0, p_len
+        per_head = cfg.token_eviction_granularity == "per_head"
+        spans: List[Tuple[int, int, List[torch.Tensor]]] = []
+        for order, ci in enumerate(selected):
+            chunk = list(chunks[ci])
+            c_start = self._chunk_rope_start(p_len, order, ci)
+            c_pos = self._range_positions(c_start, len(chunk))
+            span_start = len(prompt_ids)
+            if per_head:
+                keep_ph = self._keep_positions_per_layer_per_head_for_chunk(prefix_ids, chunk, evict_q)
+                keep = sorted({int(v) for k in keep_ph for v in k.reshape(-1).tolist()}) if keep_ph else []
+                kept = int(keep_ph[0].shape[1]) if keep_ph else len(chunk)
+                ids_in, pos_in, comp_pos = chunk, c_pos, c_pos[:kept]
+            else:
+                keep_ph = None
+                keep = self._keep_positions_for_chunk(prefix_ids, chunk, evict_q)
+                ids_in, pos_in = [chunk[i] for i in keep], [c_pos[i] for i in keep]
+                kept, comp_pos = len(ids_in), pos_in
+            prompt_ids.extend(ids_in)
+            prompt_pos.extend(pos_in)
+            if keep_ph is not None:
+                spans.append((span_start, len(prompt_ids), keep_ph))
+            removed = max(0, len(chunk) - kept)
+            total_removed += removed
+            meta.append(FastDLLMChunkMeta(chunk_index=ci, original_tokens=len(chunk), kept_tokens=kept, removed_tokens=removed,
+                                          cache_start=compressed_len, cache_end=compressed_len + kept, rope_start=c_start,
+                                          rope_end=c_start + len(chunk), score=scores.get(ci), kept_positions=list(keep)))
+            cache_positions.extend(comp_pos)
+            compressed_len += kept
+
+        q_start = self._final_query_rope_start(p_len, cache_positions, selected_count=len(selected))
+        full_q_start = self._final_query_rope_start(p_len, prompt_pos, selected_count=len(selected))
+        max_new = int(self.max_new_tokens)
+        mask_id = self._mask_token_id()
+        full_prompt_len = len(prompt_ids) + len(query_ids)
+        with_masks = cfg.cache_build_mode == "full_prompt_mask"
+        blen0 = min(self.block_length, max_new)
+        later0 = max_new - blen0
+        full_ids = prompt_ids + query_ids + ([mask_id] * max_new if with_masks else [])
+        full_pos = prompt_pos + self._range_positions(full_q_start, len(query_ids)) + (
+            self._range_positions(full_q_start + len(query_ids), max_new) if with_masks else [])
+        compacting = per_head and any(int(s[2][0].shape[1]) < (s[1] - s[0]) for s in spans)
+
+        cache = PagedCache(self, len(full_ids) + self.model.page_size)
+        try:
+            # rows stored: prompt + query, then (full_prompt_mask) the later blocks' MASK slots; the first block's MASK rows
+            # are the new rows of every denoise forward and are never stored
+            if with_masks:
+                slots = cache.slots(0, full_prompt_len) + [-1] * blen0 + cache.slots(full_prompt_len, later0)
+            else:
+                slots = cache.slots(0, full_prompt_len)
+            logits, _ = self._forward_packed([full_ids], [full_pos], causal=False, store_slots=slots, logit_rows=[full_prompt_len - 1],
+                                             store_unrotated_k=compacting)
+            last_logit = logits[0]
+            cache.length = full_prompt_len + (later0 if with_masks else 0)
+            if compacting:
+                # per-head eviction after the joint prefill (reference :2906-2912): keep lists cover prefix, kept chunk rows,
+                # query and the stored MASK slots; compaction is in place, per layer and KV head
+                seq_len = cache.length
+                keep_global = self._full_prompt_keep_indices(seq_len=seq_len, spans=spans)
+                for layer in range(self.arch.num_hidden_layers):
+                    for kv in self.model.layer_cache(layer):
+                        ops.compact_pages_per_head(kv, cache.page_ids, cache.page_ids, keep_global[layer], src_tokens=seq_len)
+                cache.length = int(keep_global[0].shape[1])
+                suffix_start = q_start + len(query_ids)
+                # keys were stored un-rotated; they take the COMPACTED positions (reference :2890, :2912)
+                stored_pos = list(cache_positions) + self._range_positions(q_start, len(query_ids))
+                if with_masks:
+                    stored_pos += self._range_positions(suffix_start + blen0, later0)
+                assert len(stored_pos) == cache.length
+                self.model.rope_rows(cache.page_ids, 0, stored_pos)
+            else:
+                suffix_start = full_q_start + len(query_ids)
+            first = torch.argmax(last_logit) if (with_masks and self.arch.logit_shift) else None
+            generated = self._denoise_blocks(cache, suffix_pos_start=suffix_start, last_logit=last_logit, first_token=first,
+                                             tail_in_cache=later0 if with_masks else 0, max_new=max_new)
+        finally:
+            cache.release()
+
+        self.total_generation_time += time.time() - t0
+        eos = getattr(self.tokenizer, "eos_token_id", None)
+        self.generated_token_num += sum(1 for t in generated if t != eos)
+        return self._result(generated, selected, scores, cfg.cache_build_mode, p_len, len(query_ids), len(context_ids), len(chunks),
+                            len(cache_positions), total_removed, meta)
+
+    def _full_prompt_keep_indices(self, *, seq_len: int, spans) -> List[torch.Tensor]:
+        """Per layer [Hkv, active_len] indices into the stored joint sequence (reference :2094-2127)."""
+        out = []
+        hkv = self.arch.num_key_value_heads
+        for layer in range(self.arch.num_hidden_layers):
+            heads = []
+            for h in range(hkv):
+                pieces, cursor = [], 0
+                for start, end, keep_ph in spans:
+                    if start > cursor:
+                        pieces.append(torch.arange(cursor, start, device=self.device))
+                    lk = keep_ph[min(layer, len(keep_ph) - 1)]
+                    pieces.append(lk[min(h, lk.shape[0] - 1)].to(self.device) + start)
+                    cursor = end
+                if cursor < seq_len:
+                    pieces.append(torch.arange(cursor, seq_len, device=self.device))
+                heads.append(torch.cat(pieces))
+            out.append(torch.stack(heads))
+        return out
+
+    # ------------------------------------------------------------------------------------------------ public entry points
+    def _result(self, generated, selected, scores, mode, p_len, q_len, raw_ctx, n_chunks, cache_tokens, removed, meta):
+        text = self.tokenizer.decode(generated, skip_special_tokens=False)
+        eos = getattr(self.tokenizer, "eos_token", None)
+        if eos and eos in text:
+            text = text.split(eos)[0]
+        return FastDLLMParallelCompResult(
+            text=text, sequences=list(generated), selected_chunk_indices=list(selected), chunk_scores=dict(scores), cache_build_mode=mode,
+            prefix_tokens=p_len, query_tokens=q_len, raw_context_tokens=raw_ctx, candidate_chunks=n_chunks, cache_tokens=cache_tokens,
+            removed_tokens=removed, chunk_meta=meta, generation_blocks=max(1, math.ceil(self.max_new_tokens / self.block_length)),
+            generation_block_length=self.block_length)
+
+    @torch.inference_mode()
+    def generate(self, *, prefix_ids, context_ids, query_ids, scoring_query_ids=None) -> FastDLLMParallelCompResult:
+        mode = self.config.cache_build_mode
+        if mode in {"full_prompt_mask", "full_prompt_query"}:
+            return self.generate_full_prompt_mask(prefix_ids=prefix_ids, context_ids=context_ids, query_ids=query_ids,
+                                                  scoring_query_ids=scoring_query_ids)
+        if mode not in {"chunk_query", "chunk_only"}:
+            raise ValueError(f"Unsupported cache_build_mode: {mode}")
+        t0 = time.time()
+        cache, cache_positions, meta = self.build_prefill_cache(prefix_ids=prefix_ids, context_ids=context_ids, query_ids=query_ids,
+                                                                scoring_query_ids=scoring_query_ids)
+        try:
+            generated = self.generate_from_cache(past_key_values=cache, cache_positions=cache_positions, query_ids=query_ids,
+                                                 query_rope_start=meta["query_rope_start"])
+        finally:
+            cache.release()
+        self.total_generation_time += time.time() - t0
+        eos = getattr(self.tokenizer, "eos_token_id", None)
+        self.generated_token_num += sum(1 for t in generated if t != eos)
+        return self._result(generated, meta["selected_indices"], meta["chunk_scores"], meta["cache_build_mode"], meta["prefix_tokens"],
+                            len(list(query_ids)), meta["raw_context_tokens"], meta["candidate_chunks"], meta["cache_tokens"],
+                            meta["removed_tokens"], meta["chunk_meta"])
+
+    def encode_fragment(self, text: str) -> List[int]:
+        return self.tokenizer.encode(text, add_special_tokens=False) if text else []
+
+    def bos_ids(self) -> List[int]:
+        return self._get_bos_token_ids() if self.config.add_bos_token else []
+
+    def generate_from_text_parts(self, *, prefix: str, context: str, query: str, scoring_query: Optional[str] = None):
+        return self.generate(prefix_ids=self.bos_ids() + self.encode_fragment(prefix), context_ids=self.encode_fragment(context),
+                             query_ids=self.encode_fragment(query),
+                             scoring_query_ids=self.encode_fragment(scoring_query if scoring_query is not None else query))
+
+
+def _resolve_dtype(dtype):
+    """prefilling_dllm_eval/fastdllm_v1_model.py:43-48."""
+    if dtype in (None, "auto"):
+        return dtype
+    if isinstance(dtype, torch.dtype):
+        return dtype
+    return getattr(torch, str(dtype), torch.bfloat16)
+
+
+def _load_tokenizer(path: str, trust_remote_code: bool):
+    if not os.path.exists(os.path.join(path, "tokenizer.json")) and not os.path.exists(os.path.join(path, "tokenizer_config.json")):
+        return None
+    import transformers
+
+    return transformers.AutoTokenizer.from_pretrained(path, trust_remote_code=trust_remote_code)
+
+
+def load_fastdllm_parallelcomp(pretrained: str, fastdllm_dream_dir: Optional[str] = None, model_backend: str = "dream",
+                               fastdllm_llada_dir: Optional[str] = None, **kwargs) -> FastDLLMParallelComp:
+    """Same factory as the reference (:3113-3127). `fastdllm_dream_dir` is accepted and ignored: the model arithmetic is
+    built in, there is no external model plug-in to import."""
+    config = FastDLLMParallelCompConfig(fastdllm_dream_dir=fastdllm_dream_dir or "", model_backend=model_backend,
+                                        fastdllm_llada_dir=fastdllm_llada_dir, pretrained=pretrained, **kwargs)
+    return FastDLLMParallelComp(config)

@@ -518,3 +518,33 @@ def test_gather_scatter_compact_pages(ops, cuda_device):
     assert torch.equal(ops.gather_pages(dev_cache, page_ids, 300).cpu(), ref)
     with pytest.raises(ValueError):
         ops.gather_pages(dev_cache, [1], 2 * page)
+
+
+@pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16])
+def test_rope_pages_in_place(ops, cuda_device, dtype):
+    """K rows stored un-rotated, rotated in place afterwards == the eager `k * cos + rotate_half(k) * sin` (bit-exact:
+    the kernel rounds each product and the sum to the cache dtype like the eager expression does)."""
+    g = torch.Generator().manual_seed(71)
+    pages, page, hkv, d = 6, 128, 2, 128
+    cache = torch.randn(pages, page, hkv, d, generator=g).to(dtype)
+    page_ids = [4, 1, 3]
+    start, n = 100, 200                       # crosses two page boundaries
+    positions = torch.randint(0, 40000, (n,), generator=g)
+    inv_freq = 1.0 / (1e6 ** (torch.arange(0, d, 2).float() / d))
+    freqs = positions.float().unsqueeze(-1) * inv_freq
+    emb = torch.cat((freqs, freqs), dim=-1)
+    cos, sin = emb.cos().to(dtype), emb.sin().to(dtype)
+    dense = torch.cat([cache[p] for p in page_ids])
+    rows = dense[start:start + n]
+    rot = torch.cat((-rows[..., d // 2:], rows[..., : d // 2]), dim=-1)
+    expect = dense.clone()
+    expect[start:start + n] = rows * cos.unsqueeze(1) + rot * sin.unsqueeze(1)
+    dev_cache = cache.to(cuda_device)
+    ops.rope_pages(dev_cache, page_ids, start, cos.to(cuda_device), sin.to(cuda_device))
+    ops.check_status(cuda_device)
+    got = ops.gather_pages(dev_cache, page_ids, 3 * page).cpu()
+    assert torch.equal(got, expect)
+    untouched = [p for p in range(pages) if p not in page_ids]
+    assert torch.equal(dev_cache.cpu()[untouched], cache[untouched])
+    with pytest.raises(ValueError):
+        ops.rope_pages(dev_cache, [0], 0, cos.to(cuda_device), sin.to(cuda_device))
