@@ -204,6 +204,9 @@ def main():
                                                       cache_build_mode="chunk_query", chunk_position_mode="reuse",
                                                       query_position_mode="after_reused_window"),
             "two_blocks": dict(README_FLAGS, max_new_tokens=64),
+            "evict_per_head_cap128_full_prompt_two_blocks": dict(README_FLAGS, token_capacity=128, max_new_tokens=64,
+                                                                 token_eviction_granularity="per_head"),
+            "full_prompt_query": dict(README_FLAGS, cache_build_mode="full_prompt_query"),
         }
         for name, flags in variants.items():
             _, runtime = load_reference(args.reference, ckpt, **flags)

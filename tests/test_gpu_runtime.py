@@ -94,7 +94,8 @@ def _match_fraction(a, b):
 
 
 @pytest.mark.parametrize("variant", ["readme_full_prompt_mask", "chunk_query_reuse", "evict_global_cap128",
-                                     "evict_per_head_cap128_chunk_query", "two_blocks"])
+                                     "evict_per_head_cap128_chunk_query", "two_blocks",
+                                     "evict_per_head_cap128_full_prompt_two_blocks", "full_prompt_query"])
 def test_runtime_matches_reference_golden(golden, toy_ckpt, variant):
     ref = golden["runs"][variant]
     capture = {}
