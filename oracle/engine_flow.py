@@ -1,0 +1,203 @@
+"""CPU restatement of the reference ENGINE's prefill/decode flow. Test infrastructure: not imported by the product.
+
+Follows prefilling_dllm_engine/prefilling_dllm/fastdllm_engine.py on the CPU contract model
+(oracle/contract_model): joint `[prompt ‖ MASK block]` prefill (:2004-2040, :2084-2088), block denoising against the
+prompt KV with an fp32 softmax (:2111-2157, :1658-1681), the engine's own draft for chunk selection, which re-forwards
+the whole prompt every round (:1014-1060), chunk scoring (:1097-1152) and the chunk-local KV generate (:1683-1876).
+
+Parity unpinned: the reference engine cannot be imported without a GPU (its model runner initialises CUDA and NCCL at
+construction), and it ships no golden vectors for this path, so these functions are checked only against the call
+sites they restate. The arithmetic they share with the eval class (model, unmask rule, score tail) is pinned by
+tests/golden/toy_reference.json.
+
+The contract model caches un-rotated keys and takes the position of every key on each call, which expresses the
+engine's post-RoPE pages exactly as long as all KV heads keep the same tokens (one position list per key).
+"""
+
+from __future__ import annotations
+
+from typing import List, Optional, Sequence, Tuple
+
+import torch
+
+from . import hotpath as O
+
+
+def _positions(values: Sequence[int]) -> torch.Tensor:
+    return torch.tensor([list(values)], dtype=torch.long)
+
+
+def _additive(mask_bool: torch.Tensor) -> torch.Tensor:
+    out = torch.zeros(mask_bool.shape, dtype=torch.float32)
+    out[~mask_bool] = float("-inf")
+    return out.view(1, 1, *mask_bool.shape)
+
+
+def selection_mask(mode: str, seq_len: int, prefix_len: int, chunk_len: int) -> Optional[torch.Tensor]:
+    """fastdllm_engine.py:930-953 as an additive mask (None = full)."""
+    mode = (mode or "full").lower()
+    if mode in {"full", "none"}:
+        return None
+    if mode == "causal":
+        return _additive(torch.tril(torch.ones(seq_len, seq_len, dtype=torch.bool)))
+    if mode == "query_to_chunk":
+        mask = torch.ones(seq_len, seq_len, dtype=torch.bool)
+        mask[prefix_len:prefix_len + chunk_len, prefix_len + chunk_len:] = False
+        return _additive(mask)
+    raise ValueError(mode)
+
+
+def denoise_block(model, past, key_positions: Sequence[int], block_positions: Sequence[int], first_token: int,
+                  last_context_logit: torch.Tensor, *, mask_id: int, threshold: float) -> Tuple[List[int], int]:
+    """:2133-2157 — every step forwards the whole block against `past` (concatenated, not stored)."""
+    block = torch.full((len(block_positions),), mask_id, dtype=torch.long)
+    block[0] = first_token
+    steps = 0
+    pos = _positions(list(key_positions) + list(block_positions))
+    with torch.no_grad():
+        while bool((block == mask_id).any()):
+            steps += 1
+            out = model(block.unsqueeze(0), attention_mask=None, position_ids=pos, past_key_values=past, use_cache=False)
+            block, _, _ = O.unmask_step(out.logits[0], block, mask_token_id=mask_id, threshold=threshold,
+                                        last_logit=last_context_logit, softmax_dtype=torch.float32)
+    return block.tolist(), steps
+
+
+def prefill_and_decode(model, prompt_ids: Sequence[int], *, block_length: int, mask_id: int, threshold: float,
+                       prompt_positions: Optional[Sequence[int]] = None, keep: Optional[Sequence[int]] = None):
+    """prefill_to_pd_record + decode_from_pd_record. `keep`: ONE ascending index list applied to every layer and KV
+    head (post-hoc eviction with head-independent indices); keys keep the rotation of their original position and
+    the block moves to max(kept positions) + 1 (:1953-1958).
+    Returns dict(first_token, last_context_logit, token_ids, n_diff_steps, k_by_layer, v_by_layer)."""
+    prompt_ids = list(prompt_ids)
+    n = len(prompt_ids)
+    prompt_positions = list(range(n)) if prompt_positions is None else list(prompt_positions)
+    suffix_start = max(prompt_positions) + 1
+    full_pos = prompt_positions + list(range(suffix_start, suffix_start + block_length))
+    with torch.no_grad():
+        out = model(torch.tensor([prompt_ids + [mask_id] * block_length]), attention_mask=None, position_ids=_positions(full_pos),
+                    use_cache=True)
+    last = out.logits[0, n - 1]
+    first = int(torch.argmax(last))
+    idx = torch.arange(n) if keep is None else torch.tensor(list(keep), dtype=torch.long)
+    past = [(k[:, idx], v[:, idx]) for k, v in out.past_key_values]
+    key_positions = [prompt_positions[i] for i in idx.tolist()]
+    block_start = max(key_positions) + 1
+    ids, steps = denoise_block(model, past, key_positions, list(range(block_start, block_start + block_length)), first, last,
+                               mask_id=mask_id, threshold=threshold)
+    return dict(first_token=first, last_context_logit=last, token_ids=ids, n_diff_steps=steps, past=past, key_positions=key_positions)
+
+
+def engine_draft(model, prompt_ids: Sequence[int], *, draft_len: int, partial_rounds: int, mask_id: int) -> Tuple[List[int], List[bool]]:
+    """generate_partial_draft_rounds_for_selection :1014-1060 — nothing cached, one full bidirectional forward per round."""
+    prompt_ids = list(prompt_ids)
+    p = len(prompt_ids)
+    block = [mask_id] * draft_len
+    confirmed = [False] * draft_len
+    pos = _positions(range(p + draft_len))
+
+    def shifted_block_logits():
+        with torch.no_grad():
+            logits = model(torch.tensor([prompt_ids + block]), attention_mask=None, position_ids=pos).logits[0]
+        return logits[p - 1:p + draft_len - 1]       # slot j reads row p + j - 1
+
+    block[0] = int(torch.argmax(shifted_block_logits()[0]))
+    confirmed[0] = True
+    for _ in range(max(0, partial_rounds)):
+        masked = [i for i, t in enumerate(block) if t == mask_id]
+        if not masked:
+            break
+        conf, x0 = O.sample_tokens_greedy(shifted_block_logits()[masked], torch.float32)
+        best = int(torch.argmax(conf))
+        block[masked[best]] = int(x0[best])
+        confirmed[masked[best]] = True
+    return block, confirmed
+
+
+def score_chunk(model, prefix_ids, chunk_ids, query_ids, label_mask, attention_mask: str = "causal") -> float:
+    """score_chunk_self_information_engine :1097-1152."""
+    joint = list(prefix_ids) + list(chunk_ids) + list(query_ids)
+    positions, labels = O.score_labels(len(prefix_ids), len(chunk_ids), query_ids, label_mask)
+    mask = selection_mask(attention_mask, len(joint), len(prefix_ids), len(chunk_ids))
+    with torch.no_grad():
+        logits = model(torch.tensor([joint]), attention_mask=mask, position_ids=_positions(range(len(joint)))).logits[0]
+    score, _ = O.self_information_scores(logits[[p - 1 for p in positions]].unsqueeze(0), torch.tensor(labels))
+    return float(score[0])
+
+
+def per_head_keep(model, prefix_ids, chunk_ids, window_ids, *, capacity: int, num_kv_heads: int, layers: Sequence[int],
+                  attention_mask: str = "causal", pool_kernel: int = 7) -> Tuple[List[torch.Tensor], List[torch.Tensor]]:
+    """compute_prompt_keep_indices_per_layer_per_head :1365-1470 for one chunk: the hidden states run under FULL attention
+    and only the score softmax applies `attention_mask`. Returns (keep [Hkv, capacity] per selected layer, pooled scores)."""
+    joint = list(prefix_ids) + list(chunk_ids) + list(window_ids)
+    length, p, c, w = len(joint), len(prefix_ids), len(chunk_ids), len(window_ids)
+    captured = {}
+    hooks = []
+    for li in layers:
+        attn = model.model.layers[li].self_attn
+        hooks.append(attn.register_forward_pre_hook(
+            lambda mod, args, kwargs, li=li: captured.__setitem__(li, (args[0] if args else kwargs["hidden_states"]).detach()), with_kwargs=True))
+    try:
+        with torch.no_grad():
+            model(torch.tensor([joint]), attention_mask=None, position_ids=_positions(range(length)))
+    finally:
+        for h in hooks:
+            h.remove()
+    keeps, pooled_all = [], []
+    cos, sin = model.model.rotary_emb(torch.zeros(1, length, 1), _positions(range(length)))
+    for li in layers:
+        attn = model.model.layers[li].self_attn
+        hidden = captured[li]
+        q = attn.q_proj(hidden).view(length, attn.num_heads, attn.head_dim)
+        k = attn.k_proj(hidden).view(length, attn.num_key_value_heads, attn.head_dim)
+
+        def rot(x):
+            half = x.shape[-1] // 2
+            return x * cos[0].unsqueeze(1) + torch.cat((-x[..., half:], x[..., :half]), dim=-1) * sin[0].unsqueeze(1)
+
+        scores = O.query_to_chunk_scores(rot(q), rot(k), prefix_len=p, chunk_len=c, query_len=w, scale=attn.head_dim ** -0.5,
+                                         causal=(attention_mask == "causal"))
+        pooled = O.per_head_token_scores(scores, num_kv_heads, "maxpool", pool_kernel)
+        keeps.append(torch.stack([O.select_positions_from_token_scores(pooled[h], capacity=capacity, chunk_len=c) for h in range(num_kv_heads)]))
+        pooled_all.append(pooled)
+    return keeps, pooled_all
+
+
+def chunk_local_generate(model, *, prefix_ids, prefix_positions, chunk_ids_list, chunk_positions_list, keep_list, query_ids,
+                         query_positions, local_query_ids, block_length: int, mask_id: int, threshold: float,
+                         local_attention_mask: str = "causal"):
+    """generate_token_ids_from_chunk_local_kv :1683-1876 with ONE keep list per chunk (the same for all layers / heads)."""
+    prefix_ids, prefix_positions = list(prefix_ids), list(prefix_positions)
+    p = len(prefix_ids)
+    with torch.no_grad():
+        parts = []
+        key_positions: List[int] = []
+        if prefix_ids:
+            out = model(torch.tensor([prefix_ids]), attention_mask=None, position_ids=_positions(prefix_positions), use_cache=True)
+            parts.append(out.past_key_values)
+            key_positions += prefix_positions
+        for chunk_ids, chunk_pos, keep in zip(chunk_ids_list, chunk_positions_list, keep_list):
+            chunk_ids, chunk_pos = list(chunk_ids), list(chunk_pos)
+            lq_start = max(chunk_pos) + 1
+            local = prefix_ids + chunk_ids + list(local_query_ids)
+            local_pos = prefix_positions + chunk_pos + list(range(lq_start, lq_start + len(local_query_ids)))
+            mask = selection_mask(local_attention_mask, len(local), p, len(chunk_ids))
+            out = model(torch.tensor([local]), attention_mask=mask, position_ids=_positions(local_pos), use_cache=True)
+            idx = torch.tensor([p + i for i in keep], dtype=torch.long)
+            parts.append([(k[:, idx], v[:, idx]) for k, v in out.past_key_values])
+            key_positions += [chunk_pos[i] for i in keep]
+        layers = len(parts[0])
+        past = [(torch.cat([part[l][0] for part in parts], dim=1), torch.cat([part[l][1] for part in parts], dim=1)) for l in range(layers)]
+        suffix_start = max(query_positions) + 1
+        block_positions = list(range(suffix_start, suffix_start + block_length))
+        suffix = list(query_ids) + [mask_id] * block_length
+        out = model(torch.tensor([suffix]), attention_mask=None, position_ids=_positions(key_positions + list(query_positions) + block_positions),
+                    past_key_values=past, use_cache=True)
+        q = len(query_ids)
+        last = out.logits[0, q - 1]
+        first = int(torch.argmax(last))
+        base = len(key_positions)
+        past_q = [(k[:, :base + q], v[:, :base + q]) for k, v in out.past_key_values]
+    ids, steps = denoise_block(model, past_q, key_positions + list(query_positions), block_positions, first, last, mask_id=mask_id,
+                               threshold=threshold)
+    return dict(first_token=first, token_ids=ids, n_diff_steps=steps)

@@ -1,0 +1,989 @@
+"""Prefill/decode (PD) engine facade over the paged model: the reference engine's boundary, field for field.
+
+Mirrors `FastDLLMDreamEngine` (prefilling_dllm_engine/prefilling_dllm/fastdllm_engine.py:170-2556): the six PD methods
+(`prefill_to_pd_record`, `snapshot_pd_record_kv`, `make_pd_record_from_kv_snapshot`, `make_pd_record_from_remote_engine`,
+`decode_from_pd_record`, `release_pd_record`), the records they exchange (`DreamPrefillRecord :32-49`, `DreamKVSnapshot
+:52-61`), the engine twins of chunk selection and per-head eviction (`select_chunks_by_engine :1154`,
+`compute_prompt_keep_indices_per_layer_per_head :1325`, `generate_token_ids_from_chunk_local_kv :1683`) and the page
+allocator with its whole-prompt prefix cache (`_PrefixPageAllocator :88-167`, here `model.PageAllocator`).
+
+What differs in mechanism, not in result:
+  * attention reads the prompt pages in place through the block table (no per-layer gather of the prompt KV, no mask
+    tensor of [block, prompt + block]);
+  * the LM head runs only on the rows whose logits are read (one row after a prefill, the label rows of a scoring
+    forward) instead of on every row;
+  * the unmask step is one kernel with one host read per step (reference :2135-2157 reads once per slot);
+  * KV snapshots, loads and per-head compaction are page-copy kernels over all layers (reference: 2 x layers
+    advanced-index gathers / scatters, staged through the CPU by default).
+Not built (the arguments are accepted and rejected with NotImplementedError): sparse "eviction_mask" prefill with
+delta correction, the decode delta reservoir, sampling with temperature / top-p / top-k, tensor parallelism, the
+"distinct" KV layout for this facade, chunk_to_query / bidirectional token-score directions.
+"""
+
+from __future__ import annotations
+
+import math
+from dataclasses import dataclass
+from typing import Dict, Iterable, List, Optional, Sequence, Tuple
+
+import torch
+
+from . import ops
+from .model import CachedPrefix, DreamArch, PageAllocator, PagedDreamModel, slots_for
+
+_OFF = {"none", "off", "0", ""}
+
+
+@dataclass
+class FastDLLMEngineOutput:
+    text: str
+    token_ids: List[int]
+    n_diff_steps: int
+
+
+@dataclass
+class DreamPrefillRecord:
+    """Boundary state between prefill and decode (reference :32-49, same fields in the same order)."""
+
+    prompt_ids: List[int]
+    prompt_positions: List[int]
+    suffix_positions: List[int]
+    prompt_len: int
+    full_prompt_len: int
+    decode_len: int
+    prompt_page_ids: List[int]
+    block_page_ids: List[int]
+    first_token_id: int
+    last_context_logit: Optional[torch.Tensor]
+    decode_delta_state: Optional[dict]
+    owns_prompt_pages: bool
+    cached_prefix: Optional[CachedPrefix] = None
+    kv_mode: str = "full_dense"
+
+
+@dataclass
+class DreamKVSnapshot:
+    """Transferable prompt KV payload (reference :52-61): per layer K and V as [prompt_len, Hkv, D]."""
+
+    prompt_len: int
+    page_size: int
+    kv_mode: str
+    k_by_layer: List[torch.Tensor]
+    v_by_layer: List[torch.Tensor]
+    last_context_logit: Optional[torch.Tensor] = None
+
+
+@dataclass
+class _EngineConfig:
+    """The fields of the reference Config that callers of the facade read (config.py)."""
+
+    model: str
+    max_model_len: int
+    max_num_batched_tokens: int
+    max_num_seqs: int
+    tensor_parallel_size: int
+    device_start: int
+    gpu_memory_utilization: float
+    enforce_eager: bool
+    kv_cache_layout: str
+    mask_token_id: int
+    diffusion_block_size: int
+    num_kvcache_blocks: int
+    kvcache_block_size: int
+    model_name: str = "dream"
+    model_type: str = "diffusion_lm"
+
+
+class FastDLLMDreamEngine:
+    """One model replica with its KV pool on one GPU; prefill and decode halves joined by a DreamPrefillRecord."""
+
+    def __init__(self, model, *, max_model_len: int = 8192, block_length: int = 32, tensor_parallel_size: int = 1,
+                 device_start: int = 0, gpu_memory_utilization: float = 0.60, max_num_batched_tokens: Optional[int] = None,
+                 max_num_seqs: int = 1, mask_token_id: int = 151666, threshold: float = 0.9, temperature: float = 0.0,
+                 top_p: Optional[float] = None, top_k: Optional[int] = None, enforce_eager: bool = True,
+                 kv_cache_layout: str = "unified", master_port: int = 2333, shm_name: str = "prefilling_dllm_fastdllm",
+                 dtype: Optional[torch.dtype] = None, num_kv_pages: Optional[int] = None, page_size: int = 256) -> None:
+        """`model`: checkpoint directory (config.json + safetensors [+ tokenizer]) or a ready PagedDreamModel.
+        Beyond the reference signature: `dtype` (default bf16), `num_kv_pages` (default: what fits in
+        gpu_memory_utilization of the device after the weights) and `page_size` (reference Config default 256)."""
+        self.block_length = int(block_length)
+        self.mask_token_id = int(mask_token_id)
+        self.threshold = float(threshold)
+        self.temperature = float(temperature)
+        self.top_p = top_p
+        self.top_k = top_k
+        if kv_cache_layout not in ("unified", "distinct"):
+            raise ValueError(f"FastDLLMDreamEngine supports kv_cache_layout='unified' or 'distinct', got '{kv_cache_layout}'.")
+        if kv_cache_layout != "unified":
+            raise NotImplementedError("this facade keeps its pool in the unified layout; the distinct layout is served by the ops only")
+        if int(tensor_parallel_size) != 1:
+            raise NotImplementedError("tensor parallelism is not built: one replica per GPU, data parallel over requests")
+        if self.temperature > 0 or top_p is not None or top_k is not None:
+            raise NotImplementedError("only greedy decoding (temperature 0, no top-p / top-k) is built")
+        if not torch.cuda.is_available():
+            raise RuntimeError("FastDLLMDreamEngine needs a CUDA device; there is no CPU path")
+        self.tokenizer = None
+        if isinstance(model, PagedDreamModel):
+            self.model = model
+            model_name = "<PagedDreamModel>"
+        else:
+            device = torch.device("cuda", int(device_start))
+            dtype = dtype or torch.bfloat16
+            arch = DreamArch.from_pretrained(model)
+            if num_kv_pages is None:
+                num_kv_pages = self._pages_that_fit(arch, device, dtype, page_size, gpu_memory_utilization)
+            self.model = PagedDreamModel.from_pretrained(model, device=device, dtype=dtype, num_pages=int(num_kv_pages),
+                                                         page_size=int(page_size), arch=arch)
+            model_name = str(model)
+            try:
+                from transformers import AutoTokenizer
+
+                self.tokenizer = AutoTokenizer.from_pretrained(model, use_fast=True, trust_remote_code=False)
+            except Exception:  # ids in, ids out still works without a tokenizer; `text` is then empty
+                self.tokenizer = None
+        self.device = self.model.device
+        self.page_size = self.model.page_size
+        self._prefix_cache: PageAllocator = self.model.allocator
+        self._active_decode_delta_state = None
+        self.config = _EngineConfig(
+            model=model_name, max_model_len=int(max_model_len), max_num_batched_tokens=int(max_num_batched_tokens or max_model_len),
+            max_num_seqs=int(max_num_seqs), tensor_parallel_size=1, device_start=int(device_start),
+            gpu_memory_utilization=float(gpu_memory_utilization), enforce_eager=bool(enforce_eager), kv_cache_layout="unified",
+            mask_token_id=self.mask_token_id, diffusion_block_size=self.block_length, num_kvcache_blocks=self.model.num_pages,
+            kvcache_block_size=self.page_size)
+
+    @staticmethod
+    def _pages_that_fit(arch: DreamArch, device, dtype, page_size: int, utilization: float) -> int:
+        elem = torch.empty((), dtype=dtype).element_size()
+        page_bytes = 2 * arch.num_hidden_layers * page_size * arch.num_key_value_heads * arch.head_dim * elem
+        layer = (2 * arch.hidden_size * arch.hidden_size + 2 * arch.hidden_size * arch.num_key_value_heads * arch.head_dim
+                 + 3 * arch.hidden_size * arch.intermediate_size)
+        weight_bytes = (arch.num_hidden_layers * layer + 2 * arch.vocab_size * arch.hidden_size) * elem
+        total = torch.cuda.get_device_properties(device).total_memory
+        budget = int(total * float(utilization)) - weight_bytes - torch.cuda.memory_allocated(device)
+        return max(4, budget // page_bytes)
+
+    def close(self) -> None:
+        self.model = None
+
+    # ------------------------------------------------------------------------------------------------ forwards
+    def _forward(self, ids, positions: Sequence[int], *, ctx_page_ids: Optional[Sequence[int]] = None, ctx_len: int = 0,
+                 store_slots: Optional[Sequence[int]] = None, causal: bool = False, mask: Optional[torch.Tensor] = None,
+                 logit_rows: Optional[Sequence[int]] = None, want_logits: bool = True, capture_layers=None):
+        """One sequence of new rows at `positions`, seeing the first `ctx_len` tokens held by `ctx_page_ids`."""
+        m = self.model
+        ids_t = ids if isinstance(ids, torch.Tensor) else m.ids_tensor(ids)
+        n = int(ids_t.numel())
+        if n != len(positions):
+            raise ValueError(f"ids/positions length mismatch: {n} vs {len(positions)}")
+        kwargs = {}
+        if ctx_page_ids is not None and ctx_len > 0:
+            kwargs = dict(block_table=m.i32(list(ctx_page_ids)).view(1, -1), seq_lens=m.i32([ctx_len + n]), max_seq_len=ctx_len + n)
+        with torch.cuda.device(self.device):
+            return m.forward(ids_t, torch.tensor(list(positions), dtype=torch.long, device=m.device), cu_seqlens=m.i32([0, n]),
+                             max_query_len=n, slot_mapping=None if store_slots is None else m.i32(list(store_slots)),
+                             causal=causal, new_row_mask=mask, logit_rows=None if logit_rows is None else m.ids_tensor(logit_rows),
+                             want_logits=want_logits, capture_qk_layers=capture_layers, **kwargs)
+
+    def _selection_mask(self, mode: str, *, seq_len: int, prefix_len: int, chunk_len: int, query_len: int):
+        """(causal flag, dense mask or None) for a selection forward (reference _selection_prefill_mask :930-953)."""
+        mode = (mode or "full").lower()
+        if mode in {"full", "none"}:
+            return False, None
+        if mode == "causal":
+            return True, None
+        if mode == "query_to_chunk":
+            mask = torch.ones((seq_len, seq_len), dtype=torch.bool, device=self.device)
+            q_start = prefix_len + chunk_len
+            if query_len > 0 and q_start < seq_len:
+                mask[prefix_len:q_start, q_start:] = False
+            return False, mask
+        raise ValueError(f"Unsupported selection attention mask: {mode}")
+
+    # ------------------------------------------------------------------------------------------------ KV movement
+    def _layer_pools(self):
+        """The pool seen as one unified cache of 2 * layers * pages pages, so one page list addresses every layer."""
+        kv = self.model.kv_cache                     # [2, layers, pages, page_size, Hkv, D]
+        return kv.view(2 * kv.shape[1] * kv.shape[2], kv.shape[3], kv.shape[4], kv.shape[5])
+
+    def _all_layer_page_ids(self, page_ids: Sequence[int]) -> torch.Tensor:
+        """Page ids of `page_ids` in every (k|v, layer) plane of `_layer_pools()`, plane-major."""
+        kv = self.model.kv_cache
+        planes, pages = 2 * kv.shape[1], kv.shape[2]
+        base = torch.tensor(list(page_ids), dtype=torch.int32, device=self.device)
+        offsets = torch.arange(planes, dtype=torch.int32, device=self.device) * pages
+        return (offsets.view(-1, 1) + base.view(1, -1)).reshape(-1).contiguous()
+
+    def _normalize_per_head_keep_indices(self, keep_indices_per_layer_per_head, *, full_prompt_len: int) -> Tuple[List[torch.Tensor], int]:
+        """Validation of reference :560-605, same messages."""
+        kv = self.model.kv_cache
+        num_layers, num_heads = int(kv.shape[1]), int(kv.shape[4])
+        if len(keep_indices_per_layer_per_head) != num_layers:
+            raise ValueError("per-head keep index layer count mismatch: "
+                             f"got {len(keep_indices_per_layer_per_head)}, expected {num_layers}")
+        normalized: List[torch.Tensor] = []
+        active_len: Optional[int] = None
+        for layer_idx, layer_keep in enumerate(keep_indices_per_layer_per_head):
+            keep = torch.as_tensor(layer_keep, dtype=torch.long, device=self.device)
+            if keep.ndim != 2:
+                raise ValueError(f"Layer {layer_idx} keep indices must be [num_heads, active_len], got {tuple(keep.shape)}")
+            if int(keep.shape[0]) != num_heads:
+                raise ValueError(f"Layer {layer_idx} keep head count mismatch: got {keep.shape[0]}, expected {num_heads}")
+            if active_len is None:
+                active_len = int(keep.shape[1])
+            elif int(keep.shape[1]) != active_len:
+                raise ValueError(f"Layer {layer_idx} active length mismatch: got {keep.shape[1]}, expected {active_len}")
+            if keep.numel() > 0 and (int(keep.min().item()) < 0 or int(keep.max().item()) >= full_prompt_len):
+                raise ValueError(f"Layer {layer_idx} keep indices are outside full prompt length {full_prompt_len}.")
+            normalized.append(keep.contiguous())
+        return normalized, int(active_len or 0)
+
+    def _compact_prompt_cache_per_layer_per_head(self, prompt_page_ids: List[int], keep_indices_per_layer_per_head, *,
+                                                 src_tokens: Optional[int] = None) -> int:
+        """In-place compaction of the kept tokens to the front of the prompt pages, per layer and KV head (:607-638)."""
+        if not keep_indices_per_layer_per_head:
+            return 0
+        active_len = int(keep_indices_per_layer_per_head[0].shape[1])
+        if active_len <= 0:
+            return 0
+        src_tokens = int(src_tokens if src_tokens is not None else len(prompt_page_ids) * self.page_size)
+        for layer_idx, keep in enumerate(keep_indices_per_layer_per_head):
+            for cache in self.model.layer_cache(layer_idx):
+                ops.compact_pages_per_head(cache, prompt_page_ids, prompt_page_ids, keep, src_tokens=src_tokens)
+        return active_len
+
+    def _copy_chunk_local_kv_to_prompt_pages(self, *, src_page_ids: List[int], dst_page_ids: List[int], src_chunk_start: int,
+                                             dst_start: int, keep_indices_per_layer_per_head) -> int:
+        """Kept tokens of a locally prefilled chunk → `dst_start...` of the prompt pages, per layer and KV head (:525-558)."""
+        if not keep_indices_per_layer_per_head:
+            return 0
+        keep_count = int(keep_indices_per_layer_per_head[0].shape[1])
+        if keep_count <= 0:
+            return 0
+        src_tokens = len(src_page_ids) * self.page_size
+        for layer_idx, keep in enumerate(keep_indices_per_layer_per_head):
+            if int(keep.shape[1]) != keep_count:
+                raise ValueError(f"Layer {layer_idx} keep_count mismatch in chunk-local KV copy")
+            for cache in self.model.layer_cache(layer_idx):
+                ops.compact_pages_per_head(cache, src_page_ids, dst_page_ids, keep + int(src_chunk_start), src_tokens=src_tokens,
+                                           dst_start=int(dst_start))
+        return keep_count
+
+    def _gather_prompt_pages_all_layers(self, prompt_page_ids: Sequence[int], prompt_len: int) -> torch.Tensor:
+        """[2, layers, n_pages * page_size, Hkv, D]: every layer's K and V of the prompt pages, ONE gather launch."""
+        kv = self.model.kv_cache
+        n_pages = math.ceil(prompt_len / self.page_size)
+        ids = self._all_layer_page_ids(list(prompt_page_ids)[:n_pages])
+        with torch.cuda.device(self.device):
+            dense = ops.gather_pages(self._layer_pools(), ids, int(ids.numel()) * self.page_size)
+        return dense.view(2, kv.shape[1], n_pages * self.page_size, kv.shape[4], kv.shape[5])
+
+    def _snapshot_prompt_cache_per_layer(self, prompt_page_ids: List[int], prompt_len: int) -> Tuple[List[torch.Tensor], List[torch.Tensor]]:
+        if prompt_len <= 0:
+            return [], []
+        dense = self._gather_prompt_pages_all_layers(prompt_page_ids, prompt_len)
+        layers = dense.shape[1]
+        return [dense[0, i, :prompt_len] for i in range(layers)], [dense[1, i, :prompt_len] for i in range(layers)]
+
+    def _load_prompt_cache_per_layer(self, prompt_page_ids: List[int], prompt_len: int, k_by_layer, v_by_layer) -> None:
+        """Per-layer [prompt_len, Hkv, D] tensors → the prompt pages of every layer, ONE scatter launch (:664-698)."""
+        if prompt_len <= 0:
+            return
+        kv = self.model.kv_cache
+        layers = int(kv.shape[1])
+        if len(k_by_layer) != layers or len(v_by_layer) != layers:
+            raise ValueError(f"PD KV snapshot layer count mismatch: k={len(k_by_layer)} v={len(v_by_layer)} expected={layers}")
+        expected = (int(prompt_len), int(kv.shape[4]), int(kv.shape[5]))
+        for layer_idx, (layer_k, layer_v) in enumerate(zip(k_by_layer, v_by_layer)):
+            if tuple(layer_k.shape) != expected or tuple(layer_v.shape) != expected:
+                raise ValueError(f"PD KV snapshot shape mismatch at layer {layer_idx}: "
+                                 f"k={tuple(layer_k.shape)} v={tuple(layer_v.shape)} expected={expected}")
+        n_pages = math.ceil(prompt_len / self.page_size)
+        padded = n_pages * self.page_size
+        with torch.cuda.device(self.device):
+            staged = torch.zeros((2, layers, padded) + expected[1:], dtype=kv.dtype, device=self.device)
+            for plane, tensors in enumerate((k_by_layer, v_by_layer)):
+                for layer_idx, t in enumerate(tensors):
+                    staged[plane, layer_idx, :prompt_len].copy_(t, non_blocking=True)
+            ids = self._all_layer_page_ids(list(prompt_page_ids)[:n_pages])
+            ops.scatter_pages(staged.view(-1, expected[1], expected[2]), self._layer_pools(), ids)
+
+    def snapshot_pd_record_kv(self, record: DreamPrefillRecord, *, device="cpu") -> DreamKVSnapshot:
+        """Copy the prompt KV a record refers to into fresh tensors on `device` (reference :700-726)."""
+        target = torch.device(device)
+        if target.type == "cuda" and target.index is None:
+            target = torch.device("cuda", torch.cuda.current_device())
+        k_by_layer: List[torch.Tensor] = []
+        v_by_layer: List[torch.Tensor] = []
+        if record.prompt_len > 0:
+            dense = self._gather_prompt_pages_all_layers(record.prompt_page_ids, record.prompt_len)
+            if target != self.device:
+                dense = dense.to(device=target)      # one copy for all layers
+            layers = dense.shape[1]
+            k_by_layer = [dense[0, i, :record.prompt_len] for i in range(layers)]
+            v_by_layer = [dense[1, i, :record.prompt_len] for i in range(layers)]
+        last = record.last_context_logit
+        if last is not None:
+            last = last.detach().to(device=target).contiguous()
+        return DreamKVSnapshot(prompt_len=record.prompt_len, page_size=self.page_size, kv_mode=record.kv_mode, k_by_layer=k_by_layer,
+                               v_by_layer=v_by_layer, last_context_logit=last)
+
+    def _allocate_prompt_and_block_pages(self, prompt_len: int, decode_len: int) -> Tuple[List[int], List[int]]:
+        n_prompt = math.ceil(prompt_len / self.page_size)
+        n_block = math.ceil(decode_len / self.page_size)
+        self._prefix_cache.ensure_free(n_prompt + n_block)
+        prompt_pages = self._prefix_cache.allocate_pages(n_prompt)
+        try:
+            block_pages = self._prefix_cache.allocate_pages(n_block)
+        except BaseException:
+            self._prefix_cache.release_pages(prompt_pages)
+            raise
+        return prompt_pages, block_pages
+
+    def _record_like(self, source: DreamPrefillRecord, prompt_page_ids, block_page_ids, last_context_logit, decode_delta_state):
+        return DreamPrefillRecord(
+            prompt_ids=list(source.prompt_ids), prompt_positions=list(source.prompt_positions),
+            suffix_positions=list(source.suffix_positions), prompt_len=source.prompt_len, full_prompt_len=source.full_prompt_len,
+            decode_len=source.decode_len, prompt_page_ids=prompt_page_ids, block_page_ids=block_page_ids,
+            first_token_id=source.first_token_id, last_context_logit=last_context_logit, decode_delta_state=decode_delta_state,
+            owns_prompt_pages=True, cached_prefix=None, kv_mode=source.kv_mode)
+
+    def make_pd_record_from_kv_snapshot(self, source: DreamPrefillRecord, snapshot: DreamKVSnapshot) -> DreamPrefillRecord:
+        """Allocate local pages, load a snapshot into them, return a decode-ready record (reference :728-781)."""
+        if snapshot.page_size != self.page_size:
+            raise ValueError(f"PD KV snapshot page_size mismatch: snapshot={snapshot.page_size}, engine={self.page_size}")
+        if snapshot.prompt_len != source.prompt_len:
+            raise ValueError(f"PD KV snapshot prompt_len mismatch: snapshot={snapshot.prompt_len}, source={source.prompt_len}")
+        if snapshot.kv_mode != source.kv_mode:
+            raise ValueError(f"PD KV snapshot mode mismatch: snapshot={snapshot.kv_mode}, source={source.kv_mode}")
+        prompt_pages, block_pages = self._allocate_prompt_and_block_pages(source.prompt_len, source.decode_len)
+        try:
+            self._load_prompt_cache_per_layer(prompt_pages, source.prompt_len, snapshot.k_by_layer, snapshot.v_by_layer)
+        except BaseException:
+            self._prefix_cache.release_pages(prompt_pages + block_pages)
+            raise
+        last = snapshot.last_context_logit
+        if last is not None:
+            last = last.to(device=self.device).contiguous()
+        return self._record_like(source, prompt_pages, block_pages, last, source.decode_delta_state)
+
+    def make_pd_record_from_remote_engine(self, source_engine: "FastDLLMDreamEngine", source: DreamPrefillRecord, *,
+                                          non_blocking: bool = True) -> DreamPrefillRecord:
+        """Copy prompt KV from another engine's pool (same or another GPU) into this one (reference :800-881).
+
+        One gather on the source GPU, one device-to-device copy of the whole payload (NVLink peer copy between GPUs),
+        one scatter here — instead of 2 x layers gathers, copies and scatters."""
+        if self.page_size != source_engine.page_size:
+            raise ValueError(f"remote-engine PD page_size mismatch: source={source_engine.page_size}, target={self.page_size}")
+        src_kv, dst_kv = source_engine.model.kv_cache, self.model.kv_cache
+        if int(src_kv.shape[1]) != int(dst_kv.shape[1]):
+            raise ValueError(f"remote-engine PD layer mismatch: source={int(src_kv.shape[1])}, target={int(dst_kv.shape[1])}")
+        prompt_len = int(source.prompt_len)
+        prompt_pages, block_pages = self._allocate_prompt_and_block_pages(prompt_len, source.decode_len)
+        try:
+            if prompt_len > 0:
+                dense = source_engine._gather_prompt_pages_all_layers(source.prompt_page_ids, prompt_len)
+                if dense.device != self.device or dense.dtype != dst_kv.dtype:
+                    dense = dense.to(device=self.device, dtype=dst_kv.dtype, non_blocking=non_blocking)
+                n_pages = math.ceil(prompt_len / self.page_size)
+                with torch.cuda.device(self.device):
+                    ops.scatter_pages(dense.view(-1, dst_kv.shape[4], dst_kv.shape[5]), self._layer_pools(),
+                                      self._all_layer_page_ids(prompt_pages[:n_pages]))
+        except BaseException:
+            self._prefix_cache.release_pages(prompt_pages + block_pages)
+            raise
+        last = source.last_context_logit
+        if last is not None:
+            last = last.to(device=self.device).contiguous()
+        if source.decode_delta_state is not None:
+            raise NotImplementedError("decode delta state is not built")
+        return self._record_like(source, prompt_pages, block_pages, last, None)
+
+    # ------------------------------------------------------------------------------------------------ prefill half
+    @staticmethod
+    def _reject_unbuilt_modes(*, prefill_sparse_mode, prefill_delta_mode, prefill_delta_selection_mode, prefill_delta_direction,
+                              decode_delta_mode, has_keep: bool) -> None:
+        """Argument checks of reference :1924-1935, :2012-2017, :2074-2075, then the refusal of what is not built."""
+        sparse = (prefill_sparse_mode or "none").lower()
+        use_sparse = sparse not in _OFF
+        if use_sparse and sparse != "eviction_mask":
+            raise ValueError(f"Unsupported prefill_sparse_mode: {sparse}")
+        if use_sparse and not has_keep:
+            raise ValueError("prefill_sparse_mode=eviction_mask requires prompt_keep_indices_per_layer_per_head.")
+        if use_sparse:
+            if (prefill_delta_mode or "none").lower() not in _OFF | {"s4_left3", "delta_s4_left3", "sampled_delta_s4_left3"}:
+                raise ValueError(f"Unsupported prefill_delta_mode: {prefill_delta_mode}")
+            if (prefill_delta_selection_mode or "none").lower() not in _OFF | {"selection_dense_replace", "selection_dense_add"}:
+                raise ValueError(f"Unsupported prefill_delta_selection_mode: {prefill_delta_selection_mode}")
+            if (prefill_delta_direction or "left").lower() not in {"left", "right", "both"}:
+                raise ValueError(f"Unsupported prefill_delta_direction: {prefill_delta_direction}")
+            raise NotImplementedError("prefill_sparse_mode=eviction_mask (sparse prefill with delta correction) is not built")
+        delta = (decode_delta_mode or "none").lower()
+        if delta in {"s4_left3", "delta_s4_left3", "sampled_delta_s4_left3"}:
+            raise NotImplementedError("decode_delta_mode (delta attention over a full-KV reservoir) is not built")
+        if delta not in _OFF and has_keep:
+            raise ValueError(f"Unsupported decode_delta_mode: {delta}")
+
+    @torch.inference_mode()
+    def prefill_to_pd_record(self, prompt_ids: Sequence[int], *, max_new_tokens: int, prompt_positions: Optional[Sequence[int]] = None,
+                             active_prompt_positions: Optional[Sequence[int]] = None,
+                             prompt_keep_indices_per_layer_per_head=None, decode_delta_mode: str = "none", decode_delta_stride: int = 4,
+                             decode_delta_left: int = 3, decode_delta_scale: float = 1.0, decode_delta_debug: bool = False,
+                             prefill_sparse_mode: str = "none", prefill_delta_mode: str = "none", prefill_delta_stride: int = 8,
+                             prefill_delta_left: int = 7, prefill_delta_right: int = 0, prefill_delta_direction: str = "left",
+                             prefill_delta_scale: float = 1.0, prefill_delta_debug: bool = False,
+                             prefill_delta_selection_mode: str = "none", prefill_delta_selection_scale: float = 1.0,
+                             prefill_selection_dense_outputs: Optional[dict] = None) -> DreamPrefillRecord:
+        """Prefill `[prompt ‖ MASK x block_length]` bidirectionally into pages and return the decode-ready boundary state
+        (reference :1879-2108). With keep indices the prompt KV is compacted per layer and KV head after the prefill
+        ("compacted_posthoc_eviction"); without them the whole prompt is registered in the prefix cache and reused by
+        the next request with the same prompt ids."""
+        if max_new_tokens <= 0:
+            raise ValueError("prefill_to_pd_record requires max_new_tokens > 0")
+        if max_new_tokens > self.block_length:
+            raise NotImplementedError("The first FastDLLMDreamEngine version supports one generation block only. "
+                                      f"Got max_new_tokens={max_new_tokens}, block_length={self.block_length}.")
+        prompt_ids = [int(x) for x in prompt_ids]
+        prompt_positions = list(range(len(prompt_ids))) if prompt_positions is None else [int(x) for x in prompt_positions]
+        if len(prompt_ids) != len(prompt_positions):
+            raise ValueError(f"prompt_ids/prompt_positions length mismatch: {len(prompt_ids)} vs {len(prompt_positions)}")
+        decode_len = self.block_length
+        has_keep = prompt_keep_indices_per_layer_per_head is not None
+        self._reject_unbuilt_modes(prefill_sparse_mode=prefill_sparse_mode, prefill_delta_mode=prefill_delta_mode,
+                                   prefill_delta_selection_mode=prefill_delta_selection_mode,
+                                   prefill_delta_direction=prefill_delta_direction, decode_delta_mode=decode_delta_mode, has_keep=has_keep)
+        keep: Optional[List[torch.Tensor]] = None
+        active_len: Optional[int] = None
+        if has_keep:
+            keep, active_len = self._normalize_per_head_keep_indices(prompt_keep_indices_per_layer_per_head, full_prompt_len=len(prompt_ids))
+            if active_prompt_positions is None:
+                raise ValueError("active_prompt_positions is required for per-head KV eviction.")
+            active_prompt_positions = [int(x) for x in active_prompt_positions]
+            if len(active_prompt_positions) != active_len:
+                raise ValueError("active_prompt_positions length mismatch: "
+                                 f"{len(active_prompt_positions)} vs per-head active length {active_len}")
+        elif active_prompt_positions is not None:
+            raise ValueError("active_prompt_positions requires prompt_keep_indices_per_layer_per_head.")
+
+        prefill_suffix_start = (max(prompt_positions) + 1) if prompt_positions else 0
+        prefill_suffix_positions = list(range(prefill_suffix_start, prefill_suffix_start + decode_len))
+        if keep is not None:
+            suffix_start = (max(active_prompt_positions) + 1) if active_prompt_positions else 0
+            suffix_positions = list(range(suffix_start, suffix_start + decode_len))
+            prompt_len, full_prompt_len, kv_mode = int(active_len or 0), len(prompt_ids), "compacted_posthoc_eviction"
+        else:
+            suffix_positions = prefill_suffix_positions
+            prompt_len = full_prompt_len = len(prompt_ids)
+            kv_mode = "full_dense"
+        if full_prompt_len + decode_len > self.config.max_model_len:
+            raise ValueError(f"full_prompt_mask length {full_prompt_len + decode_len} exceeds max_model_len={self.config.max_model_len}")
+
+        n_prompt_pages = math.ceil(full_prompt_len / self.page_size)
+        n_block_pages = math.ceil(decode_len / self.page_size)
+        use_prefix_cache = keep is None
+        cached = self._prefix_cache.lookup_prefix(prompt_ids) if use_prefix_cache else None
+        owns_prompt_pages = False
+        if cached is not None:
+            prompt_page_ids = cached.page_ids
+            cached.ref_count += 1
+            last_context_logit = cached.last_context_logit
+            try:
+                self._prefix_cache.ensure_free(n_block_pages)
+                block_page_ids = self._prefix_cache.allocate_pages(n_block_pages)
+            except BaseException:
+                cached.ref_count -= 1
+                raise
+            # the reference runs an all-MASK replace forward here (:2088-2094) and reads only row 0 of its SHIFTED logits,
+            # which is the cached last-context logit: the forward changes nothing, so it is not run
+            first_token = int(torch.argmax(last_context_logit).item())
+        else:
+            self._prefix_cache.ensure_free(n_prompt_pages + n_block_pages)
+            prompt_page_ids = self._prefix_cache.allocate_pages(n_prompt_pages)
+            try:
+                block_page_ids = self._prefix_cache.allocate_pages(n_block_pages)
+            except BaseException:
+                self._prefix_cache.release_pages(prompt_page_ids)
+                raise
+            owns_prompt_pages = not use_prefix_cache
+            try:
+                if full_prompt_len <= 0:
+                    raise ValueError("prefill_to_pd_record needs at least one prompt token")
+                full_ids = prompt_ids + [self.mask_token_id] * decode_len
+                slots = slots_for(prompt_page_ids, 0, full_prompt_len, self.page_size) + slots_for(block_page_ids, 0, decode_len, self.page_size)
+                # Dream reads token p from logits[p - 1]: the first block token and the "last context logit" are both the
+                # row of the last prompt token, the only row the LM head is run on
+                logits, _ = self._forward(full_ids, list(prompt_positions) + prefill_suffix_positions, store_slots=slots,
+                                          logit_rows=[full_prompt_len - 1])
+                last_context_logit = logits[0].detach()
+                first_token = int(torch.argmax(last_context_logit).item())
+                if keep is not None:
+                    self._compact_prompt_cache_per_layer_per_head(prompt_page_ids, keep, src_tokens=full_prompt_len)
+                    active_pages = math.ceil(prompt_len / self.page_size)
+                    if active_pages < len(prompt_page_ids):
+                        self._prefix_cache.release_pages(prompt_page_ids[active_pages:])
+                        prompt_page_ids = prompt_page_ids[:active_pages]
+                ops.check_status(self.device)
+            except BaseException:
+                self._prefix_cache.release_pages(block_page_ids)
+                self._prefix_cache.release_pages(prompt_page_ids)
+                raise
+            if use_prefix_cache:
+                self._prefix_cache.register_prefix(prompt_ids, prompt_page_ids, prompt_len, last_context_logit)
+        return DreamPrefillRecord(
+            prompt_ids=prompt_ids, prompt_positions=prompt_positions, suffix_positions=suffix_positions, prompt_len=prompt_len,
+            full_prompt_len=full_prompt_len, decode_len=decode_len, prompt_page_ids=prompt_page_ids, block_page_ids=block_page_ids,
+            first_token_id=first_token, last_context_logit=last_context_logit, decode_delta_state=None,
+            owns_prompt_pages=owns_prompt_pages, cached_prefix=cached, kv_mode=kv_mode)
+
+    # ------------------------------------------------------------------------------------------------ decode half
+    def _denoise_block(self, *, ctx_page_ids: Sequence[int], ctx_len: int, block_slots: Sequence[int], block_positions: Sequence[int],
+                       first_token_id: int, last_context_logit: Optional[torch.Tensor]) -> Tuple[torch.Tensor, int]:
+        """Confidence-threshold denoising of one block against `ctx_len` cached tokens (reference :2133-2157): every
+        step forwards the whole block (its K/V replace their slots), softmax in fp32, the most confident masked slot is
+        always accepted and every other one whose confidence reaches the threshold."""
+        decode_len = len(block_positions)
+        block = torch.full((decode_len,), self.mask_token_id, dtype=torch.long, device=self.device)
+        block[0] = int(first_token_id)
+        n_steps = 0
+        remaining = decode_len - 1
+        while remaining > 0:
+            n_steps += 1
+            logits, _ = self._forward(block, block_positions, ctx_page_ids=ctx_page_ids, ctx_len=ctx_len, store_slots=block_slots)
+            with torch.cuda.device(self.device):
+                counts = ops.unmask_step(logits, block, mask_token_id=self.mask_token_id, threshold=self.threshold,
+                                         last_logit=last_context_logit, shift=True, softmax_dtype=torch.float32)
+            remaining = int(counts[2].item())      # the one host read of a step
+            if n_steps > decode_len + 8:
+                raise RuntimeError("denoising did not converge: every step must unmask at least one slot")
+        return block, n_steps
+
+    def _finish(self, block: torch.Tensor, max_new_tokens: int, stop_token_ids, n_steps: int) -> FastDLLMEngineOutput:
+        generated = block[:max_new_tokens].tolist()
+        if stop_token_ids:
+            stop_set = set(int(x) for x in stop_token_ids)
+            for idx, token_id in enumerate(generated):
+                if token_id in stop_set:
+                    generated = generated[:idx]
+                    break
+        text = ""
+        if self.tokenizer is not None:
+            text = self.tokenizer.decode(generated, skip_special_tokens=False)
+            eos = getattr(self.tokenizer, "eos_token", None)
+            if eos and eos in text:
+                text = text.split(eos)[0]
+        return FastDLLMEngineOutput(text=text, token_ids=generated, n_diff_steps=n_steps)
+
+    @torch.inference_mode()
+    def decode_from_pd_record(self, record: DreamPrefillRecord, *, max_new_tokens: int,
+                              stop_token_ids: Optional[Iterable[int]] = None) -> FastDLLMEngineOutput:
+        """Denoise the block of a record against its prompt pages; CONSUMES the record (pages released in `finally`,
+        reference :2111-2190)."""
+        if max_new_tokens <= 0:
+            return FastDLLMEngineOutput(text="", token_ids=[], n_diff_steps=0)
+        if max_new_tokens > record.decode_len:
+            raise ValueError(f"max_new_tokens={max_new_tokens} exceeds record decode_len={record.decode_len}.")
+        try:
+            block, n_steps = self._denoise_block(
+                ctx_page_ids=record.prompt_page_ids, ctx_len=record.prompt_len,
+                block_slots=slots_for(record.block_page_ids, 0, record.decode_len, self.page_size),
+                block_positions=record.suffix_positions, first_token_id=record.first_token_id,
+                last_context_logit=record.last_context_logit)
+            ops.check_status(self.device)
+            return self._finish(block, max_new_tokens, stop_token_ids, n_steps)
+        finally:
+            self.release_pd_record(record)
+
+    def release_pd_record(self, record: DreamPrefillRecord) -> None:
+        """Release the pages of a record that will not be decoded (reference :2192-2198)."""
+        self._prefix_cache.release_pages(record.block_page_ids)
+        if record.owns_prompt_pages:
+            self._prefix_cache.release_pages(record.prompt_page_ids)
+        if record.cached_prefix is not None:
+            record.cached_prefix.ref_count -= 1
+
+    @torch.inference_mode()
+    def generate_token_ids_pd_split(self, prompt_ids: Sequence[int], *, max_new_tokens: int, stop_token_ids: Optional[Iterable[int]] = None,
+                                    **prefill_kwargs) -> FastDLLMEngineOutput:
+        """Prefill then decode through the explicit boundary (reference :2201-2255)."""
+        record = self.prefill_to_pd_record(prompt_ids, max_new_tokens=max_new_tokens, **prefill_kwargs)
+        return self.decode_from_pd_record(record, max_new_tokens=max_new_tokens, stop_token_ids=stop_token_ids)
+
+    @torch.inference_mode()
+    def generate_token_ids(self, prompt_ids: Sequence[int], *, max_new_tokens: int, stop_token_ids: Optional[Iterable[int]] = None,
+                           **prefill_kwargs) -> FastDLLMEngineOutput:
+        """Same result as the PD split; the reference keeps a fused copy of the two halves (:2258-2528)."""
+        if max_new_tokens <= 0:
+            return FastDLLMEngineOutput(text="", token_ids=[], n_diff_steps=0)
+        return self.generate_token_ids_pd_split(prompt_ids, max_new_tokens=max_new_tokens, stop_token_ids=stop_token_ids, **prefill_kwargs)
+
+    def generate(self, prompts, sampling_params) -> List[FastDLLMEngineOutput]:
+        """`sampling_params`: any object with `max_tokens` and `stop_token_ids` (list of lists), reference :2530-2556."""
+        stop_token_ids = None
+        if getattr(sampling_params, "stop_token_ids", None):
+            stop_token_ids = [item for group in sampling_params.stop_token_ids for item in group]
+        outputs = []
+        for prompt in prompts:
+            if isinstance(prompt, str):
+                if self.tokenizer is None:
+                    raise ValueError("text prompts need a tokenizer in the checkpoint directory")
+                prompt_ids = self.tokenizer.encode(prompt)
+            else:
+                prompt_ids = list(prompt)
+            outputs.append(self.generate_token_ids(prompt_ids, max_new_tokens=int(sampling_params.max_tokens), stop_token_ids=stop_token_ids))
+        return outputs
+
+    # ------------------------------------------------------------------------------------------------ chunk selection
+    @staticmethod
+    def _select_attention_layer_indices(total_layers: int, layer_window: int, layer_mode: str) -> List[int]:
+        if total_layers <= 0:
+            return []
+        if layer_mode == "all" or layer_window <= 0:
+            return list(range(total_layers))
+        window = min(max(1, int(layer_window)), total_layers)
+        if layer_mode == "first":
+            return list(range(window))
+        if layer_mode == "last":
+            return list(range(total_layers - window, total_layers))
+        raise ValueError(f"Unsupported attention layer mode: {layer_mode}")
+
+    @staticmethod
+    def _window_query(query_ids: Sequence[int], window: int) -> List[int]:
+        ids = [int(x) for x in query_ids]
+        return ids[-int(window):] if window and window > 0 else ids
+
+    @torch.inference_mode()
+    def generate_partial_draft_rounds_for_selection(self, prompt_ids: Sequence[int], *, max_new_tokens: int,
+                                                    partial_rounds: int) -> Tuple[List[int], List[bool]]:
+        """Engine draft (reference :1014-1060): every round is ONE bidirectional forward over `[prompt ‖ draft block]`
+        with nothing cached (prompt rows see the MASK slots — unlike the eval class, which drafts against a cached
+        prompt). Slot 0 comes from the last prompt row; each further round confirms the most confident masked slot."""
+        draft_len = int(max_new_tokens or 0)
+        if draft_len <= 0:
+            return [], []
+        prompt_ids = [int(x) for x in prompt_ids]
+        p_len = len(prompt_ids)
+        if p_len <= 0:
+            raise ValueError("the draft needs at least one prompt token")
+        positions = list(range(p_len + draft_len))
+        block = torch.full((draft_len,), self.mask_token_id, dtype=torch.long, device=self.device)
+        prompt_t = self.model.ids_tensor(prompt_ids)
+        rows = list(range(p_len - 1, p_len + draft_len - 1))        # shifted: slot j reads the logits of row p_len + j - 1
+        logits, _ = self._forward(torch.cat([prompt_t, block]), positions, logit_rows=rows[:1])
+        block[0] = torch.argmax(logits[0])
+        confirmed = torch.zeros(draft_len, dtype=torch.bool, device=self.device)
+        confirmed[0] = True
+        for _ in range(max(0, int(partial_rounds or 0))):
+            if not bool((block == self.mask_token_id).any()):
+                break
+            before = block.clone()
+            logits, _ = self._forward(torch.cat([prompt_t, block]), positions, logit_rows=rows)
+            with torch.cuda.device(self.device):
+                # rows are already the shifted ones; a threshold no probability reaches leaves only the top-1 transfer
+                ops.unmask_step(logits, block, mask_token_id=self.mask_token_id, threshold=2.0, shift=False, softmax_dtype=torch.float32)
+            confirmed |= block != before
+        return block.tolist(), confirmed.tolist()
+
+    def _selection_query_ids_with_score_target_engine(self, prefix_ids, scoring_query_ids, *, score_mode: str, score_draft_tokens: int = 0,
+                                                      score_draft_partial_rounds: Optional[int] = None,
+                                                      score_draft_score_all_slots: bool = False):
+        selection = [int(x) for x in scoring_query_ids]
+        mask: Optional[List[bool]] = None
+        if (score_mode or "").lower() == "draft_self_information" and int(score_draft_tokens or 0) > 0:
+            if score_draft_partial_rounds is not None:
+                draft_ids, draft_mask = self.generate_partial_draft_rounds_for_selection(
+                    list(prefix_ids) + list(scoring_query_ids), max_new_tokens=int(score_draft_tokens),
+                    partial_rounds=int(score_draft_partial_rounds))
+                mask = [True] * len(scoring_query_ids) + ([True] * len(draft_ids) if score_draft_score_all_slots else list(draft_mask))
+            else:
+                draft_ids = list(self.generate_token_ids(list(prefix_ids) + list(scoring_query_ids),
+                                                         max_new_tokens=int(score_draft_tokens), stop_token_ids=None).token_ids)
+            selection = list(scoring_query_ids) + list(draft_ids)
+        return selection, None, mask
+
+    @staticmethod
+    def _label_positions(prefix_len: int, chunk_len: int, query_ids: Sequence[int], score_token_count, score_token_mask):
+        """(label positions, label ids) of one scoring row, or None when the row scores -inf (reference :1118-1140)."""
+        query_len = len(query_ids)
+        start = prefix_len + chunk_len
+        if score_token_mask is not None:
+            if len(score_token_mask) != query_len:
+                return None
+            local = [i for i, keep in enumerate(score_token_mask) if keep]
+            if not local:
+                return None
+            positions, labels = [start + i for i in local], [query_ids[i] for i in local]
+        elif score_token_count is None:
+            positions, labels = list(range(start, start + query_len)), list(query_ids)
+        else:
+            target = min(query_len, max(0, int(score_token_count)))
+            if target <= 0:
+                return None
+            positions, labels = list(range(start, start + target)), list(query_ids[:target])
+        if not positions or min(positions) <= 0:
+            return None
+        return positions, labels
+
+    @torch.inference_mode()
+    def score_chunk_self_information_engine(self, prefix_ids, chunk_ids, query_ids, *, score_token_count: Optional[int] = None,
+                                            score_token_mask: Optional[Sequence[bool]] = None, score_attention_mask: str = "causal") -> float:
+        """mean log p(label | prefix, chunk, earlier query) of one chunk (reference :1097-1152); LM head on label rows only."""
+        prefix_ids, chunk_ids, query_ids = [int(x) for x in prefix_ids], [int(x) for x in chunk_ids], [int(x) for x in query_ids]
+        if not chunk_ids or not query_ids:
+            return float("-inf")
+        target = self._label_positions(len(prefix_ids), len(chunk_ids), query_ids, score_token_count, score_token_mask)
+        if target is None:
+            return float("-inf")
+        positions, labels = target
+        joint = prefix_ids + chunk_ids + query_ids
+        causal, mask = self._selection_mask(score_attention_mask, seq_len=len(joint), prefix_len=len(prefix_ids),
+                                            chunk_len=len(chunk_ids), query_len=len(query_ids))
+        logits, _ = self._forward(joint, list(range(len(joint))), causal=causal, mask=mask, logit_rows=[p - 1 for p in positions])
+        with torch.cuda.device(self.device):
+            score = float(ops.self_information_scores(logits, self.model.ids_tensor(labels), 1)[0].item())
+        return score if math.isfinite(score) else float("-inf")
+
+    @torch.inference_mode()
+    def select_chunks_by_engine(self, prefix_ids, candidate_chunks, scoring_query_ids, *, topk_chunks: int,
+                                score_mode: str = "draft_self_information", score_draft_tokens: int = 4,
+                                score_draft_partial_rounds: Optional[int] = 1, score_draft_score_all_slots: bool = False,
+                                score_attention_mask: str = "causal", score_context_mode: str = "single_chunk",
+                                keep_first_chunk: bool = False, score_batch_size: int = 8):
+        """(selected ascending, scores, selection query ids, label mask) — reference :1154-1204. Chunks of equal length are
+        scored `score_batch_size` at a time in one packed forward (the reference forwards one chunk at a time); the
+        ranking is the stable descending sort of the reference, run by the top-K kernel."""
+        if not candidate_chunks:
+            return [], {}, list(scoring_query_ids), None
+        selection, count, mask = self._selection_query_ids_with_score_target_engine(
+            prefix_ids, scoring_query_ids, score_mode=score_mode, score_draft_tokens=score_draft_tokens,
+            score_draft_partial_rounds=score_draft_partial_rounds, score_draft_score_all_slots=score_draft_score_all_slots)
+        if (score_mode or "none").lower() == "none" or not selection:
+            selected = list(range(len(candidate_chunks)))
+            if int(topk_chunks or 0) > 0:
+                selected = selected[:int(topk_chunks)]
+            return selected, {}, selection, mask
+        if score_context_mode != "single_chunk":
+            raise ValueError(f"Engine chunk selection currently supports score_context_mode='single_chunk', got {score_context_mode!r}.")
+        if (score_mode or "").lower() not in {"self_information", "draft_self_information"}:
+            raise ValueError(f"Engine chunk selection currently supports self_information/draft_self_information, got {score_mode!r}.")
+        scores = self._score_chunks_batched([int(x) for x in prefix_ids], candidate_chunks, selection, count, mask,
+                                            score_attention_mask, max(1, int(score_batch_size or 1)))
+        dense = torch.tensor([scores[i] for i in range(len(candidate_chunks))], dtype=torch.float32, device=self.device)
+        with torch.cuda.device(self.device):
+            sel, cnt = ops.topk_chunks(dense, int(topk_chunks or 0), bool(keep_first_chunk))
+        return sel[: int(cnt.item())].tolist(), scores, selection, mask
+
+    def _score_chunks_batched(self, prefix_ids, candidate_chunks, query_ids, count, mask, attention_mask: str, batch_size: int) -> Dict[int, float]:
+        m = self.model
+        scores: Dict[int, float] = {}
+        groups: Dict[int, List[Tuple[int, List[int]]]] = {}
+        for idx, chunk in enumerate(candidate_chunks):
+            chunk = [int(x) for x in chunk]
+            if not chunk or not query_ids:
+                scores[idx] = float("-inf")
+            else:
+                groups.setdefault(len(chunk), []).append((idx, chunk))
+        mode = (attention_mask or "full").lower()
+        for c_len, group in groups.items():
+            target = self._label_positions(len(prefix_ids), c_len, query_ids, count, mask)
+            if target is None:
+                scores.update({idx: float("-inf") for idx, _ in group})
+                continue
+            positions, labels = target
+            if mode == "query_to_chunk":   # needs a dense mask, which is per sequence: one chunk per forward
+                for idx, chunk in group:
+                    scores[idx] = self.score_chunk_self_information_engine(prefix_ids, chunk, query_ids, score_token_count=count,
+                                                                           score_token_mask=mask, score_attention_mask=attention_mask)
+                continue
+            causal, _ = self._selection_mask(mode, seq_len=0, prefix_len=0, chunk_len=0, query_len=0)
+            row_len = len(prefix_ids) + c_len + len(query_ids)
+            labels_t = m.ids_tensor(labels)
+            for off in range(0, len(group), batch_size):
+                batch = group[off:off + batch_size]
+                flat = [t for _, chunk in batch for t in (prefix_ids + chunk + list(query_ids))]
+                cu = [b * row_len for b in range(len(batch) + 1)]
+                rows = [b * row_len + (p - 1) for b in range(len(batch)) for p in positions]
+                with torch.cuda.device(self.device):
+                    logits, _ = m.forward(m.ids_tensor(flat), torch.arange(row_len, device=m.device).repeat(len(batch)),
+                                          cu_seqlens=m.i32(cu), max_query_len=row_len, causal=causal, logit_rows=m.ids_tensor(rows))
+                    vals = ops.self_information_scores(logits, labels_t, len(batch)).tolist()
+                for (idx, _), v in zip(batch, vals):
+                    scores[idx] = v if math.isfinite(v) else float("-inf")
+        return scores
+
+    # ------------------------------------------------------------------------------------------------ token eviction
+    @torch.inference_mode()
+    def compute_prompt_keep_indices_per_layer_per_head(self, *, full_prompt_len: int, prefix_ids, chunk_spans, query_ids, token_capacity: int,
+                                                       token_score_query_window: int = 8, token_score_layers: int = 1,
+                                                       token_score_layer_mode: str = "first", token_score_reduce: str = "sum",
+                                                       token_score_pooling: str = "maxpool", token_score_pool_kernel: int = 7,
+                                                       token_score_direction: str = "query_to_chunk", token_score_keep: str = "high",
+                                                       token_score_include_prefix: bool = True, token_attention_mask: str = "causal",
+                                                       token_score_backend: str = "torch", return_selection_dense_outputs: bool = False):
+        """Per layer and KV head, which prompt tokens stay (reference :1325-1563).
+
+        `chunk_spans`: dicts with `chunk_ids`, `start`, `end` (span of the chunk inside the full prompt). For a chunk
+        longer than `token_capacity`: one bidirectional forward over `[prefix ‖ chunk ‖ query window]` with nothing
+        stored, the rotated q / k of the selected layers go to the fused scorer (query→chunk attention mass under
+        `token_attention_mask`), then max-pool, mean over each KV head's query heads, BOS + top-(capacity - 1), ascending.
+        Returns (keep `[layers][Hkv][active_len]` as nested lists, per-chunk meta). `token_score_backend` is accepted for
+        signature parity: there is one backend."""
+        if return_selection_dense_outputs:
+            raise NotImplementedError("selection dense outputs (for the sparse delta prefill) are not built")
+        if (token_score_direction or "query_to_chunk").lower() != "query_to_chunk":
+            raise NotImplementedError("only token_score_direction='query_to_chunk' is built")
+        pooling = (token_score_pooling or "none").lower()
+        if pooling not in {"none", "maxpool"}:
+            if pooling == "avgpool":
+                raise NotImplementedError("token_score_pooling='avgpool' is not built (maxpool / none)")
+            raise ValueError(f"Unsupported token_score_pooling: {token_score_pooling}")
+        pool_kernel = 1 if pooling == "none" else int(token_score_pool_kernel or 1)
+        capacity = int(token_capacity or 0)
+        query_ids = self._window_query(query_ids, token_score_query_window)
+        arch = self.model.arch
+        num_layers, hkv = arch.num_hidden_layers, arch.num_key_value_heads
+        selected_layers = self._select_attention_layer_indices(num_layers, token_score_layers, token_score_layer_mode) or [0]
+        all_layer_keeps: List[List[torch.Tensor]] = [[] for _ in range(num_layers)]
+        chunk_meta: List[Dict[str, int]] = []
+        for span in chunk_spans:
+            chunk_ids = [int(x) for x in span["chunk_ids"]]
+            start, end = int(span["start"]), int(span["end"])
+            chunk_len = len(chunk_ids)
+            keep_count = min(max(1, capacity), chunk_len) if capacity > 0 else chunk_len
+            if chunk_len <= 0:
+                chunk_meta.append({"start": start, "end": end, "kept_tokens": 0, "union_kept_tokens": 0})
+                continue
+            if capacity <= 0 or chunk_len <= capacity or not query_ids:
+                base = torch.arange(chunk_len, device=self.device, dtype=torch.long)
+                per_layer_keep = [base.unsqueeze(0).expand(hkv, -1).clone() for _ in range(num_layers)]
+            else:
+                prefix = [int(x) for x in prefix_ids] if token_score_include_prefix else []
+                joint = prefix + chunk_ids + list(query_ids)
+                # the hidden states run under FULL attention; only the score softmax applies `token_attention_mask`
+                _, captured = self._forward(joint, list(range(len(joint))), want_logits=False, capture_layers=selected_layers)
+                with torch.cuda.device(self.device):
+                    head_scores = torch.stack([
+                        ops.query_to_chunk_attention_scores(captured[l][0], captured[l][1], prefix_len=len(prefix), chunk_len=chunk_len,
+                                                            query_len=len(query_ids), scale=self.model.scale, reduce_mode=token_score_reduce,
+                                                            attention_mask=token_attention_mask)
+                        for l in selected_layers], dim=0).contiguous()
+                    keeps = ops.evict_select(head_scores, num_kv_heads=hkv, keep_count=keep_count, pool_kernel=pool_kernel, per_head=True,
+                                             force_keep_first=True, keep_high=token_score_keep == "high")
+                per_layer_keep = [keeps[min(layer_idx, len(selected_layers) - 1)].clone() for layer_idx in range(num_layers)]
+            union = torch.unique(torch.cat([k.reshape(-1) for k in per_layer_keep]))
+            for layer_idx, layer_keep in enumerate(per_layer_keep):
+                all_layer_keeps[layer_idx].append(layer_keep + start)
+            chunk_meta.append({"start": start, "end": end, "kept_tokens": keep_count, "union_kept_tokens": int(union.numel())})
+
+        spans_with_keep = [s for s in chunk_spans if len(s["chunk_ids"]) > 0]
+        prompt_keep: List[List[List[int]]] = []
+        for layer_idx, layer_parts in enumerate(all_layer_keeps):
+            if not layer_parts:
+                base = torch.arange(full_prompt_len, device=self.device, dtype=torch.long)
+                prompt_keep.append(base.unsqueeze(0).expand(hkv, -1).tolist())
+                continue
+            heads = []
+            for head_idx in range(int(layer_parts[0].shape[0])):
+                pieces, cursor = [], 0
+                for span, layer_keep in zip(spans_with_keep, layer_parts):
+                    start, end = int(span["start"]), int(span["end"])
+                    if start > cursor:
+                        pieces.append(torch.arange(cursor, start, device=self.device, dtype=torch.long))
+                    pieces.append(layer_keep[head_idx])
+                    cursor = end
+                if cursor < full_prompt_len:
+                    pieces.append(torch.arange(cursor, full_prompt_len, device=self.device, dtype=torch.long))
+                heads.append(torch.cat(pieces, dim=0))
+            prompt_keep.append(torch.stack(heads, dim=0).tolist())
+        ops.check_status(self.device)
+        return prompt_keep, chunk_meta
+
+    # ------------------------------------------------------------------------------------------------ chunk-local KV
+    @torch.inference_mode()
+    def generate_token_ids_from_chunk_local_kv(self, *, prefix_ids, prefix_positions, chunk_ids_list, chunk_positions_list,
+                                               chunk_keep_indices_per_layer_per_head, query_ids, query_positions,
+                                               local_query_ids: Optional[Sequence[int]] = None, local_attention_mask: str = "causal",
+                                               max_new_tokens: int, stop_token_ids: Optional[Iterable[int]] = None) -> FastDLLMEngineOutput:
+        """Generate from independently prefilled chunks (reference :1683-1876): every chunk is forwarded as
+        `[prefix ‖ chunk ‖ local query]` into scratch pages, its kept tokens are copied per layer and KV head behind the
+        prefix in the prompt pages, then `[query ‖ MASK block]` is appended and the block is denoised."""
+        if max_new_tokens <= 0:
+            return FastDLLMEngineOutput(text="", token_ids=[], n_diff_steps=0)
+        if max_new_tokens > self.block_length:
+            raise NotImplementedError("FastDLLMDreamEngine chunk-local KV path supports one generation block only. "
+                                      f"Got max_new_tokens={max_new_tokens}, block_length={self.block_length}.")
+        prefix_ids, prefix_positions = [int(x) for x in prefix_ids], [int(x) for x in prefix_positions]
+        query_ids, query_positions = [int(x) for x in query_ids], [int(x) for x in query_positions]
+        if len(prefix_ids) != len(prefix_positions):
+            raise ValueError("prefix_ids/prefix_positions length mismatch")
+        if len(query_ids) != len(query_positions):
+            raise ValueError("query_ids/query_positions length mismatch")
+        if len(chunk_ids_list) != len(chunk_positions_list):
+            raise ValueError("chunk ids/positions list length mismatch")
+        if len(chunk_ids_list) != len(chunk_keep_indices_per_layer_per_head):
+            raise ValueError("chunk ids/keep-indices list length mismatch")
+        decode_len = self.block_length
+        local_query_ids = [int(x) for x in (local_query_ids if local_query_ids is not None else query_ids)]
+        keeps: List[List[torch.Tensor]] = []
+        kept_counts: List[int] = []
+        for chunk_ids, chunk_keep in zip(chunk_ids_list, chunk_keep_indices_per_layer_per_head):
+            tensors, active_len = self._normalize_per_head_keep_indices(chunk_keep, full_prompt_len=len(chunk_ids))
+            keeps.append(tensors)
+            kept_counts.append(active_len)
+        p_len = len(prefix_ids)
+        base_len = p_len + sum(kept_counts)
+        prompt_len = base_len + len(query_ids)
+        suffix_start = (max(query_positions) + 1) if query_positions else (max(prefix_positions) + 1 if prefix_positions else 0)
+        block_positions = list(range(suffix_start, suffix_start + decode_len))
+        total_slots = prompt_len + decode_len
+        if total_slots > self.config.max_model_len:
+            raise ValueError(f"chunk-local KV prompt length {total_slots} exceeds max_model_len={self.config.max_model_len}")
+        total_pages = math.ceil(total_slots / self.page_size)
+        self._prefix_cache.ensure_free(total_pages)
+        all_pages = self._prefix_cache.allocate_pages(total_pages)
+        scratch: List[int] = []
+        try:
+            if prefix_ids:
+                self._forward(prefix_ids, prefix_positions, store_slots=slots_for(all_pages, 0, p_len, self.page_size), want_logits=False)
+            dst = p_len
+            for chunk_ids_raw, chunk_pos_raw, chunk_keep in zip(chunk_ids_list, chunk_positions_list, keeps):
+                chunk_ids, chunk_pos = [int(x) for x in chunk_ids_raw], [int(x) for x in chunk_pos_raw]
+                if len(chunk_ids) != len(chunk_pos):
+                    raise ValueError("chunk ids/positions length mismatch")
+                if not chunk_ids:
+                    continue
+                lq_start = max(chunk_pos) + 1
+                local_ids = prefix_ids + chunk_ids + local_query_ids
+                local_pos = prefix_positions + chunk_pos + list(range(lq_start, lq_start + len(local_query_ids)))
+                n_scratch = math.ceil(len(local_ids) / self.page_size)
+                self._prefix_cache.ensure_free(n_scratch)
+                scratch = self._prefix_cache.allocate_pages(n_scratch)
+                causal, mask = self._selection_mask(local_attention_mask, seq_len=len(local_ids), prefix_len=p_len,
+                                                    chunk_len=len(chunk_ids), query_len=len(local_query_ids))
+                self._forward(local_ids, local_pos, store_slots=slots_for(scratch, 0, len(local_ids), self.page_size), causal=causal,
+                              mask=mask, want_logits=False)
+                dst += self._copy_chunk_local_kv_to_prompt_pages(src_page_ids=scratch, dst_page_ids=all_pages, src_chunk_start=p_len,
+                                                                 dst_start=dst, keep_indices_per_layer_per_head=chunk_keep)
+                self._prefix_cache.release_pages(scratch)
+                scratch = []
+            if dst != base_len:
+                raise ValueError(f"chunk-local KV base length mismatch: {dst} vs {base_len}")
+            # [query ‖ MASK block] appended behind the compacted base; the reference pads this forward to a multiple of the
+            # block length and hides the padding from the valid rows, so the padding is simply not forwarded here
+            suffix_ids = query_ids + [self.mask_token_id] * decode_len
+            q_len = len(query_ids)
+            if q_len <= 0:
+                raise ValueError("generate_token_ids_from_chunk_local_kv needs a non-empty query")
+            logits, _ = self._forward(suffix_ids, query_positions + block_positions, ctx_page_ids=all_pages, ctx_len=base_len,
+                                      store_slots=slots_for(all_pages, base_len, len(suffix_ids), self.page_size), logit_rows=[q_len - 1])
+            last_context_logit = logits[0].detach()
+            first_token = int(torch.argmax(last_context_logit).item())
+            block, n_steps = self._denoise_block(ctx_page_ids=all_pages, ctx_len=prompt_len,
+                                                 block_slots=slots_for(all_pages, prompt_len, decode_len, self.page_size),
+                                                 block_positions=block_positions, first_token_id=first_token,
+                                                 last_context_logit=last_context_logit)
+            ops.check_status(self.device)
+        finally:
+            if scratch:
+                self._prefix_cache.release_pages(scratch)
+            self._prefix_cache.release_pages(all_pages)
+        return self._finish(block, max_new_tokens, stop_token_ids, n_steps)

@@ -290,7 +290,7 @@ class PagedDreamModel:
                 seq_lens: Optional[torch.Tensor] = None, max_seq_len: int = 0, causal: bool = False,
                 logit_rows: Optional[torch.Tensor] = None, want_logits: bool = True,
                 capture_qk_layers: Optional[Sequence[int]] = None, store_after_attention: bool = False,
-                store_unrotated_k: bool = False):
+                store_unrotated_k: bool = False, new_row_mask: Optional[torch.Tensor] = None):
         """Packed forward of `ids` [T] (several sequences delimited by cu_seqlens) at RoPE `positions` [T].
 
         slot_mapping [T] int32 (optional): where each row's K/V goes in the pool (-1 = do not store).
@@ -299,6 +299,8 @@ class PagedDreamModel:
         store_unrotated_k: the K written to the pool is the projection BEFORE the rotary embedding (attention over the rows
         themselves still uses rotated keys); the caller rotates the stored rows later with `rope_rows` — per-head
         eviction assigns positions only after compaction.
+        new_row_mask: bool [rows, rows] visibility among the new rows of ONE sequence (row i sees new row j iff True); the
+        cached context stays fully visible. None = all visible (or the causal rule).
         block_table / seq_lens (optional): cached context each sequence attends before its own rows.
         causal: scoring mask (row sees itself and earlier rows); otherwise rows see each other bidirectionally.
         logit_rows: indices of the rows whose logits are wanted (LM head runs on those rows only).
@@ -332,10 +334,10 @@ class PagedDreamModel:
             if block_table is not None:
                 ops.paged_attention(q, k, v, attn_out, cu_seqlens_q=cu_seqlens, max_query_len=max_query_len, key_cache=k_cache,
                                     value_cache=v_cache, block_table=block_table, seq_lens=seq_lens, max_seq_len=max_seq_len,
-                                    sm_scale=self.scale, causal=causal, bidirectional=True)
+                                    sm_scale=self.scale, causal=causal, bidirectional=True, mask=new_row_mask)
             else:
                 ops.paged_attention(q, k, v, attn_out, cu_seqlens_q=cu_seqlens, max_query_len=max_query_len,
-                                    sm_scale=self.scale, causal=causal, bidirectional=True)
+                                    sm_scale=self.scale, causal=causal, bidirectional=True, mask=new_row_mask)
             if slot_mapping is not None and store_after_attention:
                 ops.store_kvcache_unified_layout(k_store, v, k_cache, v_cache, slot_mapping, "diffusion_lm")
             x = x + F.linear(attn_out.view(total, hq * d), w["wo"])

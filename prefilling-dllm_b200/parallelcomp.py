@@ -661,6 +661,52 @@ class FastDLLMParallelComp:
         return generated[:max_new]
 
     # ------------------------------------------------------------------------------------------------ chunk-local caches
+    def _prefill_one_chunk(self, cache: "PagedCache", dst: int, prefix_ids, chunk, order: int, ci: int, evict_q, window_q):
+        """Forward one selected chunk (with the query window behind it in chunk_query mode) against the prefix KV already in
+        `cache` and leave its KEPT rows at cache tokens [dst, dst + kept). Returns (kept, kept positions, union of kept chunk
+        indices, rope start). `order` is the chunk's rank among the selected ones, `ci` its index among the candidates."""
+        cfg = self.config
+        p_len = len(prefix_ids)
+        per_head = cfg.token_eviction_granularity == "per_head"
+        causal = cfg.cache_build_mode == "chunk_query" and self._mask_is_causal(cfg.token_attention_mask)
+        c_start = self._chunk_rope_start(p_len, order, ci)
+        c_pos = self._range_positions(c_start, len(chunk))
+        if per_head:
+            keep_ph = self._keep_positions_per_layer_per_head_for_chunk(prefix_ids, chunk, evict_q)
+            keep_union = sorted({int(v) for k in keep_ph for v in k.reshape(-1).tolist()}) if keep_ph else []
+            kept = int(keep_ph[0].shape[1]) if keep_ph else len(chunk)
+        else:
+            keep_ph = None
+            keep_union = self._keep_positions_for_chunk(prefix_ids, chunk, evict_q)
+            kept = len(keep_union)
+        rows_ids, rows_pos = chunk, c_pos
+        if cfg.cache_build_mode == "chunk_query":
+            tq_start = self._chunk_query_rope_start(p_len, c_start, len(chunk))
+            rows_ids = chunk + window_q
+            rows_pos = c_pos + self._range_positions(tq_start, len(window_q))
+        if per_head and keep_ph and kept < len(chunk):
+            # all chunk rows go to a staging area behind the destination, K un-rotated; a per-head compaction moves
+            # the kept ones; then kept row j of EVERY head is rotated to the j-th chunk position, as the reference's
+            # model does when it rotates cached keys at read time with the compacted position list (:2284-2288)
+            stage = dst + kept
+            slots = cache.slots(stage, len(chunk)) + [-1] * (len(rows_ids) - len(chunk))
+            self._forward_packed([rows_ids], [rows_pos], causal=causal, cache=cache if p_len else None, ctx_len=p_len,
+                                 store_slots=slots, want_logits=False, store_unrotated_k=True)
+            for layer in range(self.arch.num_hidden_layers):
+                for kv in self.model.layer_cache(layer):
+                    ops.compact_pages_per_head(kv, cache.page_ids, cache.page_ids, keep_ph[layer] + stage,
+                                               src_tokens=stage + len(chunk), dst_start=dst)
+            kept_pos = c_pos[:kept]
+            self.model.rope_rows(cache.page_ids, dst, kept_pos)
+        else:
+            keep_set = set(keep_union)
+            next_slot = iter(cache.slots(dst, kept))
+            slots = [next(next_slot) if i in keep_set else -1 for i in range(len(chunk))] + [-1] * (len(rows_ids) - len(chunk))
+            self._forward_packed([rows_ids], [rows_pos], causal=causal, cache=cache if p_len else None, ctx_len=p_len,
+                                 store_slots=slots, want_logits=False)
+            kept_pos = [c_pos[i] for i in keep_union]
+        return kept, kept_pos, keep_union, c_start
+
     @torch.inference_mode()
     def build_prefill_cache(self, *, prefix_ids, context_ids, query_ids, scoring_query_ids=None):
         """Independent per-chunk prefill (cache_build_mode chunk_query / chunk_only) → (PagedCache, cache_positions, meta).
@@ -689,48 +735,11 @@ class FastDLLMParallelComp:
                 cache_positions.extend(prefix_pos)
             meta: List[FastDLLMChunkMeta] = []
             total_removed = 0
-            per_head = cfg.token_eviction_granularity == "per_head"
             window_q = self._window_query(selection_q, cfg.token_score_query_window)
-            causal = cfg.cache_build_mode == "chunk_query" and self._mask_is_causal(cfg.token_attention_mask)
             for order, ci in enumerate(selected):
                 chunk = list(chunks[ci])
-                c_start = self._chunk_rope_start(p_len, order, ci)
-                c_pos = self._range_positions(c_start, len(chunk))
-                if per_head:
-                    keep_ph = self._keep_positions_per_layer_per_head_for_chunk(prefix_ids, chunk, evict_q)
-                    keep_union = sorted({int(v) for k in keep_ph for v in k.reshape(-1).tolist()}) if keep_ph else []
-                    kept = int(keep_ph[0].shape[1]) if keep_ph else len(chunk)
-                else:
-                    keep_ph = None
-                    keep_union = self._keep_positions_for_chunk(prefix_ids, chunk, evict_q)
-                    kept = len(keep_union)
-                rows_ids, rows_pos = chunk, c_pos
-                if cfg.cache_build_mode == "chunk_query":
-                    tq_start = self._chunk_query_rope_start(p_len, c_start, len(chunk))
-                    rows_ids = chunk + window_q
-                    rows_pos = c_pos + self._range_positions(tq_start, len(window_q))
                 dst = cache.length
-                if per_head and keep_ph and kept < len(chunk):
-                    # all chunk rows go to a staging area behind the destination, K un-rotated; a per-head compaction moves
-                    # the kept ones; then kept row j of EVERY head is rotated to the j-th chunk position, as the reference's
-                    # model does when it rotates cached keys at read time with the compacted position list (:2284-2288)
-                    stage = dst + kept
-                    slots = cache.slots(stage, len(chunk)) + [-1] * (len(rows_ids) - len(chunk))
-                    self._forward_packed([rows_ids], [rows_pos], causal=causal, cache=cache if p_len else None, ctx_len=p_len,
-                                         store_slots=slots, want_logits=False, store_unrotated_k=True)
-                    for layer in range(self.arch.num_hidden_layers):
-                        for kv in self.model.layer_cache(layer):
-                            ops.compact_pages_per_head(kv, cache.page_ids, cache.page_ids, keep_ph[layer] + stage,
-                                                       src_tokens=stage + len(chunk), dst_start=dst)
-                    kept_pos = c_pos[:kept]
-                    self.model.rope_rows(cache.page_ids, dst, kept_pos)
-                else:
-                    keep_set = set(keep_union)
-                    next_slot = iter(cache.slots(dst, kept))
-                    slots = [next(next_slot) if i in keep_set else -1 for i in range(len(chunk))] + [-1] * (len(rows_ids) - len(chunk))
-                    self._forward_packed([rows_ids], [rows_pos], causal=causal, cache=cache if p_len else None, ctx_len=p_len,
-                                         store_slots=slots, want_logits=False)
-                    kept_pos = [c_pos[i] for i in keep_union]
+                kept, kept_pos, keep_union, c_start = self._prefill_one_chunk(cache, dst, prefix_ids, chunk, order, ci, evict_q, window_q)
                 removed = max(0, len(chunk) - kept)
                 total_removed += removed
                 cache.length = dst + kept

@@ -1,0 +1,247 @@
+"""GPU parity of the PD engine facade (prefilling_dllm_b200.engine) with the CPU restatement of the reference engine.
+
+The reference engine cannot run without CUDA + NCCL, so its flow is restated on the CPU contract model
+(oracle/engine_flow.py); the toy checkpoint is the one the goldens were made with. fp32, SIMT attention kernel.
+Gates: first token, number of denoise steps and token ids equal; chunk scores within 1e-4; selected chunks and keep
+lists bit-exact (up to exact ties at the cut); KV payloads bit-exact across snapshot / load / engine-to-engine copy.
+"""
+
+import os
+import sys
+
+import pytest
+import torch
+
+pytestmark = pytest.mark.gpu
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, os.path.join(HERE, "golden"))
+sys.path.insert(0, os.path.dirname(HERE))
+
+BOS, MASK, BLOCK = 1, 1023, 32
+
+
+@pytest.fixture(scope="module")
+def ckpt(tmp_path_factory):
+    import make_golden
+
+    path = str(tmp_path_factory.mktemp("ckpt_engine"))
+    make_golden.write_toy_checkpoint(path)
+    return path
+
+
+@pytest.fixture(scope="module")
+def cpu_model(ckpt):
+    from oracle.contract_model.model.modeling_dream import DreamModel
+
+    return DreamModel.from_pretrained(ckpt).eval()
+
+
+def _engine(ckpt, pages=24, **kw):
+    from prefilling_dllm_b200.engine import FastDLLMDreamEngine
+
+    return FastDLLMDreamEngine(ckpt, max_model_len=8192, block_length=BLOCK, mask_token_id=MASK, threshold=0.9, dtype=torch.float32,
+                               num_kv_pages=pages, **kw)
+
+
+@pytest.fixture(scope="module")
+def engine(ckpt):
+    return _engine(ckpt)
+
+
+def _prompt(n=600, seed=3):
+    g = torch.Generator().manual_seed(seed)
+    return [BOS] + torch.randint(3, 1023, (n - 1,), generator=g).tolist()
+
+
+def _rotate(k, positions, theta=1e6):
+    """[S, Hkv, D] un-rotated keys → rotated at `positions` (what the engine keeps in its pages)."""
+    d = k.shape[-1]
+    inv = 1.0 / (theta ** (torch.arange(0, d, 2).float() / d))
+    f = torch.tensor(positions).float().unsqueeze(-1) * inv
+    emb = torch.cat((f, f), dim=-1)
+    cos, sin = emb.cos().unsqueeze(1), emb.sin().unsqueeze(1)
+    return k * cos + torch.cat((-k[..., d // 2:], k[..., : d // 2]), dim=-1) * sin
+
+
+def test_pd_split_matches_the_restated_engine(engine, cpu_model):
+    from oracle import engine_flow as E
+
+    prompt = _prompt()
+    want = E.prefill_and_decode(cpu_model, prompt, block_length=BLOCK, mask_id=MASK, threshold=0.9)
+    free0 = engine._prefix_cache.num_free_pages
+    rec = engine.prefill_to_pd_record(prompt, max_new_tokens=BLOCK)
+    assert (rec.prompt_len, rec.full_prompt_len, rec.decode_len, rec.kv_mode) == (600, 600, BLOCK, "full_dense")
+    assert rec.suffix_positions == list(range(600, 600 + BLOCK)) and rec.prompt_positions == list(range(600))
+    assert len(rec.prompt_page_ids) == 3 and len(rec.block_page_ids) == 1 and not rec.owns_prompt_pages
+    assert rec.first_token_id == want["first_token"]
+    assert torch.allclose(rec.last_context_logit.cpu(), want["last_context_logit"], atol=2e-4)
+    snap = engine.snapshot_pd_record_kv(rec)
+    assert snap.prompt_len == 600 and snap.page_size == 256 and snap.kv_mode == "full_dense" and len(snap.k_by_layer) == 2
+    for layer, (k_ref, v_ref) in enumerate(want["past"]):
+        assert snap.k_by_layer[layer].device.type == "cpu" and tuple(snap.k_by_layer[layer].shape) == (600, 2, 64)
+        assert torch.allclose(snap.v_by_layer[layer], v_ref[0].view(600, 2, 64), atol=1e-5)
+        assert torch.allclose(snap.k_by_layer[layer], _rotate(k_ref[0].view(600, 2, 64), list(range(600))), atol=1e-4)
+    out = engine.decode_from_pd_record(rec, max_new_tokens=BLOCK)
+    assert out.token_ids == want["token_ids"] and out.n_diff_steps == want["n_diff_steps"]
+    # the record is consumed: block pages are back, the prompt pages stay with the prefix cache
+    assert engine._prefix_cache.num_free_pages == free0 - 3
+    again = engine.prefill_to_pd_record(prompt, max_new_tokens=BLOCK)
+    assert again.cached_prefix is not None and again.prompt_page_ids == rec.prompt_page_ids and again.first_token_id == rec.first_token_id
+    short = engine.decode_from_pd_record(again, max_new_tokens=5, stop_token_ids=[want["token_ids"][3]])
+    assert short.token_ids == want["token_ids"][:3]
+    assert engine._prefix_cache.evict_one() and engine._prefix_cache.num_free_pages == free0
+
+
+def test_snapshot_load_and_engine_to_engine_copy(engine, ckpt):
+    other = _engine(ckpt, pages=16)
+    prompt = _prompt(700, seed=5)
+    rec = engine.prefill_to_pd_record(prompt, max_new_tokens=BLOCK)
+    snap_cpu = engine.snapshot_pd_record_kv(rec)
+    snap_gpu = engine.snapshot_pd_record_kv(rec, device="cuda")
+    assert snap_gpu.k_by_layer[0].is_cuda and torch.equal(snap_gpu.k_by_layer[1].cpu(), snap_cpu.k_by_layer[1])
+    loaded = other.make_pd_record_from_kv_snapshot(rec, snap_cpu)
+    copied = other.make_pd_record_from_remote_engine(engine, rec)
+    assert loaded.owns_prompt_pages and copied.owns_prompt_pages and loaded.cached_prefix is None
+    assert set(loaded.prompt_page_ids).isdisjoint(copied.prompt_page_ids)
+    for rec_b in (loaded, copied):
+        snap_b = other.snapshot_pd_record_kv(rec_b)
+        for layer in range(2):
+            assert torch.equal(snap_b.k_by_layer[layer], snap_cpu.k_by_layer[layer])
+            assert torch.equal(snap_b.v_by_layer[layer], snap_cpu.v_by_layer[layer])
+    ids = engine.decode_from_pd_record(rec, max_new_tokens=BLOCK).token_ids
+    assert other.decode_from_pd_record(loaded, max_new_tokens=BLOCK).token_ids == ids
+    assert other.decode_from_pd_record(copied, max_new_tokens=BLOCK).token_ids == ids
+    assert other._prefix_cache.num_free_pages == 16
+    # validation at the boundary (reference :734-745, :683-690)
+    rec2 = engine.prefill_to_pd_record(prompt, max_new_tokens=BLOCK)
+    try:
+        from dataclasses import replace
+
+        with pytest.raises(ValueError, match="page_size mismatch"):
+            other.make_pd_record_from_kv_snapshot(rec2, replace(snap_cpu, page_size=128))
+        with pytest.raises(ValueError, match="prompt_len mismatch"):
+            other.make_pd_record_from_kv_snapshot(rec2, replace(snap_cpu, prompt_len=699))
+        with pytest.raises(ValueError, match="mode mismatch"):
+            other.make_pd_record_from_kv_snapshot(rec2, replace(snap_cpu, kv_mode="compacted_posthoc_eviction"))
+        with pytest.raises(ValueError, match="shape mismatch"):
+            other.make_pd_record_from_kv_snapshot(rec2, replace(snap_cpu, k_by_layer=[t[:-1] for t in snap_cpu.k_by_layer]))
+        with pytest.raises(ValueError, match="layer count mismatch"):
+            other.make_pd_record_from_kv_snapshot(rec2, replace(snap_cpu, k_by_layer=snap_cpu.k_by_layer[:1]))
+        assert other._prefix_cache.num_free_pages == 16, "a rejected snapshot must not leak pages"
+    finally:
+        engine.release_pd_record(rec2)
+    engine._prefix_cache.evict_one()
+
+
+def test_posthoc_eviction_with_head_independent_keep(engine, cpu_model):
+    from oracle import engine_flow as E
+
+    prompt = _prompt(600, seed=7)
+    keep = [0] + list(range(1, 600, 3))                      # 201 tokens: fits one page, two tail pages are released
+    want = E.prefill_and_decode(cpu_model, prompt, block_length=BLOCK, mask_id=MASK, threshold=0.9, keep=keep)
+    nested = [[keep, keep] for _ in range(2)]
+    free0 = engine._prefix_cache.num_free_pages
+    rec = engine.prefill_to_pd_record(prompt, max_new_tokens=BLOCK, prompt_keep_indices_per_layer_per_head=nested,
+                                      active_prompt_positions=keep)
+    assert rec.kv_mode == "compacted_posthoc_eviction" and rec.owns_prompt_pages and rec.cached_prefix is None
+    assert (rec.prompt_len, rec.full_prompt_len, len(rec.prompt_page_ids)) == (len(keep), 600, 1)
+    assert rec.suffix_positions[0] == max(keep) + 1 and rec.first_token_id == want["first_token"]
+    out = engine.decode_from_pd_record(rec, max_new_tokens=BLOCK)
+    assert out.token_ids == want["token_ids"] and out.n_diff_steps == want["n_diff_steps"]
+    assert engine._prefix_cache.num_free_pages == free0
+    with pytest.raises(ValueError, match="active_prompt_positions is required"):
+        engine.prefill_to_pd_record(prompt, max_new_tokens=BLOCK, prompt_keep_indices_per_layer_per_head=nested)
+    with pytest.raises(ValueError, match="layer count mismatch"):
+        engine.prefill_to_pd_record(prompt, max_new_tokens=BLOCK, prompt_keep_indices_per_layer_per_head=nested[:1], active_prompt_positions=keep)
+    with pytest.raises(ValueError, match="outside full prompt length"):
+        engine.prefill_to_pd_record(prompt, max_new_tokens=BLOCK, prompt_keep_indices_per_layer_per_head=[[[0, 600]] * 2] * 2,
+                                    active_prompt_positions=[0, 1])
+    assert engine._prefix_cache.num_free_pages == free0
+
+
+def test_rejections(engine):
+    prompt = _prompt(64)
+    with pytest.raises(ValueError):
+        engine.prefill_to_pd_record(prompt, max_new_tokens=0)
+    with pytest.raises(NotImplementedError, match="one generation block"):
+        engine.prefill_to_pd_record(prompt, max_new_tokens=BLOCK + 1)
+    with pytest.raises(ValueError, match="Unsupported prefill_sparse_mode"):
+        engine.prefill_to_pd_record(prompt, max_new_tokens=8, prefill_sparse_mode="banded")
+    with pytest.raises(ValueError, match="requires prompt_keep_indices"):
+        engine.prefill_to_pd_record(prompt, max_new_tokens=8, prefill_sparse_mode="eviction_mask")
+    with pytest.raises(ValueError, match="length mismatch"):
+        engine.prefill_to_pd_record(prompt, max_new_tokens=8, prompt_positions=[0, 1])
+    with pytest.raises(ValueError, match="requires prompt_keep_indices"):
+        engine.prefill_to_pd_record(prompt, max_new_tokens=8, active_prompt_positions=[0])
+    rec = engine.prefill_to_pd_record(prompt, max_new_tokens=8)
+    with pytest.raises(ValueError, match="exceeds record decode_len"):
+        engine.decode_from_pd_record(rec, max_new_tokens=BLOCK + 1)
+    assert engine.decode_from_pd_record(rec, max_new_tokens=0).token_ids == []
+    engine.release_pd_record(rec)
+    engine._prefix_cache.evict_one()
+    assert engine._prefix_cache.num_free_pages == engine._prefix_cache.num_pages
+    with pytest.raises(RuntimeError, match="Cannot allocate"):
+        engine.prefill_to_pd_record(_prompt(7000), max_new_tokens=8)
+    assert engine._prefix_cache.num_free_pages == engine._prefix_cache.num_pages
+
+
+def test_selection_twins(engine, cpu_model):
+    import make_golden
+    from oracle import engine_flow as E
+    from oracle import hotpath as O
+
+    context, query = make_golden.toy_inputs()
+    chunks = [O.maybe_prepend_bos_to_chunk(c, [BOS], 512) for c in O.split_token_chunks(context, 512)]
+    draft = E.engine_draft(cpu_model, [BOS] + query, draft_len=4, partial_rounds=1, mask_id=MASK)
+    assert engine.generate_partial_draft_rounds_for_selection([BOS] + query, max_new_tokens=4, partial_rounds=1) == draft
+    selection, label_mask = query + draft[0], [True] * len(query) + draft[1]
+    want_scores = [E.score_chunk(cpu_model, [BOS], c, selection, label_mask) for c in chunks]
+    selected, scores, sel_ids, mask = engine.select_chunks_by_engine([BOS], chunks, query, topk_chunks=4)
+    assert sel_ids == selection and mask == label_mask
+    assert max(abs(scores[i] - want_scores[i]) for i in range(len(chunks))) < 1e-4
+    assert selected == O.rank_chunks(want_scores, 4)
+    one = engine.score_chunk_self_information_engine([BOS], chunks[2], selection, score_token_mask=label_mask)
+    assert abs(one - want_scores[2]) < 1e-4
+    q2c = engine.score_chunk_self_information_engine([BOS], chunks[2], selection, score_token_mask=label_mask, score_attention_mask="query_to_chunk")
+    assert abs(q2c - E.score_chunk(cpu_model, [BOS], chunks[2], selection, label_mask, "query_to_chunk")) < 1e-4
+    # per-head keep indices over a prompt of [BOS ‖ chunk a ‖ chunk b ‖ query]
+    a, b = chunks[selected[0]], chunks[selected[1]]
+    spans = [dict(chunk_ids=a, start=1, end=1 + len(a)), dict(chunk_ids=b, start=1 + len(a), end=1 + len(a) + len(b))]
+    full_len = 1 + len(a) + len(b) + len(query)
+    keep, meta = engine.compute_prompt_keep_indices_per_layer_per_head(full_prompt_len=full_len, prefix_ids=[BOS], chunk_spans=spans,
+                                                                      query_ids=query, token_capacity=128)
+    assert len(keep) == 2 and len(keep[0]) == 2 and len(keep[0][0]) == 1 + 128 + 128 + len(query)
+    assert [m["kept_tokens"] for m in meta] == [128, 128] and all(m["union_kept_tokens"] >= 128 for m in meta)
+    for span, chunk in zip(spans, (a, b)):
+        ref_keep, pooled = E.per_head_keep(cpu_model, [BOS], chunk, query[-8:], capacity=128, num_kv_heads=2, layers=[0])
+        for layer in range(2):           # token_score_layers=1: layer 0's indices serve every layer
+            for h in range(2):
+                mine = [i - span["start"] for i in keep[layer][h] if span["start"] <= i < span["end"]]
+                theirs = ref_keep[0][h].tolist()
+                diff = set(mine) ^ set(theirs)
+                cut = min(float(pooled[0][h][i]) for i in theirs[1:])
+                assert len(mine) == 128 and all(abs(float(pooled[0][h][i]) - cut) <= 1e-6 * abs(cut) for i in diff)
+        assert keep[0][0][0] == 0 and keep[0][0][-len(query):] == list(range(full_len - len(query), full_len))
+
+
+def test_chunk_local_kv_generate(engine, cpu_model):
+    import make_golden
+    from oracle import engine_flow as E
+    from oracle import hotpath as O
+
+    context, query = make_golden.toy_inputs()
+    chunks = [O.maybe_prepend_bos_to_chunk(c, [BOS], 512) for c in O.split_token_chunks(context, 512)][:2]
+    keeps = [[0] + list(range(5, 512, 4)), [0] + list(range(2, 512, 4))]
+    chunk_pos = [list(range(1, 513)), list(range(1, 513))]                 # "reuse" positions: every chunk at 1..512
+    q_pos = list(range(513, 513 + len(query)))
+    kw = dict(prefix_ids=[BOS], prefix_positions=[0], chunk_ids_list=chunks, chunk_positions_list=chunk_pos, query_ids=query,
+              query_positions=q_pos, local_query_ids=query[-8:])
+    want = E.chunk_local_generate(cpu_model, keep_list=keeps, block_length=BLOCK, mask_id=MASK, threshold=0.9, **kw)
+    nested = [[[k, k] for _ in range(2)] for k in keeps]
+    free0 = engine._prefix_cache.num_free_pages
+    out = engine.generate_token_ids_from_chunk_local_kv(chunk_keep_indices_per_layer_per_head=nested, max_new_tokens=BLOCK, **kw)
+    assert out.token_ids == want["token_ids"] and out.n_diff_steps == want["n_diff_steps"]
+    assert engine._prefix_cache.num_free_pages == free0
+    with pytest.raises(ValueError, match="keep-indices list length mismatch"):
+        engine.generate_token_ids_from_chunk_local_kv(chunk_keep_indices_per_layer_per_head=nested[:1], max_new_tokens=BLOCK, **kw)
