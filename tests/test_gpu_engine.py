@@ -88,8 +88,9 @@ def test_pd_split_matches_the_restated_engine(engine, cpu_model):
     assert engine._prefix_cache.num_free_pages == free0 - 3
     again = engine.prefill_to_pd_record(prompt, max_new_tokens=BLOCK)
     assert again.cached_prefix is not None and again.prompt_page_ids == rec.prompt_page_ids and again.first_token_id == rec.first_token_id
-    short = engine.decode_from_pd_record(again, max_new_tokens=5, stop_token_ids=[want["token_ids"][3]])
-    assert short.token_ids == want["token_ids"][:3]
+    stop = want["token_ids"][3]
+    short = engine.decode_from_pd_record(again, max_new_tokens=5, stop_token_ids=[stop])
+    assert short.token_ids == want["token_ids"][:want["token_ids"].index(stop)]      # cut at the first stop token
     assert engine._prefix_cache.evict_one() and engine._prefix_cache.num_free_pages == free0
 
 
@@ -220,7 +221,7 @@ def test_selection_twins(engine, cpu_model):
                 mine = [i - span["start"] for i in keep[layer][h] if span["start"] <= i < span["end"]]
                 theirs = ref_keep[0][h].tolist()
                 diff = set(mine) ^ set(theirs)
-                cut = min(float(pooled[0][h][i]) for i in theirs[1:])
+                cut = min(float(pooled[0][h][i].detach()) for i in theirs[1:])
                 assert len(mine) == 128 and all(abs(float(pooled[0][h][i]) - cut) <= 1e-6 * abs(cut) for i in diff)
         assert keep[0][0][0] == 0 and keep[0][0][-len(query):] == list(range(full_len - len(query), full_len))
 
