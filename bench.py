@@ -164,9 +164,9 @@ def run_native(args, rank: int, world: int, local_rank: int):
         step(i)
     torch.cuda.synchronize(device)
     ops.check_status(device)
-    # launches per step: the attention kernel, plus the split-KV merge when the plan split the keys
-    # (a split plan is the only thing that makes the op allocate its "attn" workspace)
-    launches_per_step = 2 if ("attn" in {key for (_, key) in ops._state.workspaces}) else 1
+    # launches per step: the attention kernel (split-KV partials are merged inside it by the last CTA of a tile pair;
+    # the 4-byte-per-pair arrival counters are cleared by a memset node, not a kernel)
+    launches_per_step = 1
 
     def barrier():
         if world > 1:

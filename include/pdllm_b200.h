@@ -23,7 +23,7 @@
 extern "C" {
 #endif
 
-#define PDLLM_ABI_VERSION 1
+#define PDLLM_ABI_VERSION 2
 
 /* element types of floating-point tensors */
 #define PDLLM_F32 0
@@ -113,7 +113,7 @@ typedef struct pdllm_attn_params {
   const int32_t* seq_lens;      /* [num_seqs] context + new rows (the reference's b_seq_len) */
   const uint8_t* mask;          /* optional bool mask over new rows x new keys, sequence-LOCAL indices */
   int32_t* status;              /* optional device status word */
-  void* workspace;              /* split-KV partials; pdllm_attn_workspace_bytes() */
+  void* workspace;              /* split-KV arrival counters + partials; pdllm_attn_workspace_bytes(); 256-byte aligned */
   void* trace;                  /* optional profiling aid of the tcgen05 kernel: int64 [8 CTAs][64 iterations][16 events]
                                    of clock64() timestamps, zero-initialised by the caller; NULL (the default) = off */
   int64_t workspace_bytes;
@@ -134,6 +134,9 @@ typedef struct pdllm_attn_params {
   int32_t impl;                /* PDLLM_ATTN_* */
   int32_t num_splits;          /* 0 = choose; >=1 forces the KV split count of the tcgen05 kernel */
   float sm_scale;
+  int32_t workspace_zeroed;    /* non-zero: the caller zero-filled `workspace` once and after any launch that raised
+                                  PDLLM_S_WAIT_TIMEOUT; the split-KV arrival counters in its first 64 KB are then known to
+                                  be zero (every launch returns them to zero) and no memset is enqueued. 0 = clear them */
 } pdllm_attn_params;
 
 int64_t pdllm_attn_workspace_bytes(const pdllm_attn_params* p);

@@ -58,6 +58,7 @@ class AttnParams(Structure):
         ("max_query_len", c_int32), ("max_seq_len", c_int32),
         ("impl", c_int32), ("num_splits", c_int32),
         ("sm_scale", c_float),
+        ("workspace_zeroed", c_int32),
     ]
 
 
@@ -128,8 +129,8 @@ def load() -> ctypes.CDLL:
             fn = getattr(lib, name)
             fn.restype = restype
             fn.argtypes = argtypes
-        if lib.pdllm_abi_version() != 1:
-            raise ImportError(f"{LIB_PATH} has ABI version {lib.pdllm_abi_version()}, expected 1")
+        if lib.pdllm_abi_version() != 2:
+            raise ImportError(f"{LIB_PATH} has ABI version {lib.pdllm_abi_version()}, expected 2")
         _lib = lib
     return _lib
 

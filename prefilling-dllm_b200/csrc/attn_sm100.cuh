@@ -6,7 +6,7 @@
 //   * query tile  = up to 128 rows = tpt tokens x G query heads of one KV group (row = token*G + head), so the
 //     K/V pages of a KV head are read once for all G heads that share it, and once for both query tiles;
 //   * key tiles   = the sequence's selected prefix pages in block-table order (any physical order), then the new
-//     rows themselves; a KV split assigns each CTA a sub-range, partials are merged by attn_combine_kernel.
+//     rows themselves; a KV split assigns each CTA a sub-range; the CTA that finishes a query-tile pair last merges the partials.
 // Every key tile is processed as two 64-key halves b, so four chains (query tile X) x (half b) run interleaved:
 // while the softmax warps of X work on S_Xb, the tensor core computes P·V and the next Q·K of the other chains.
 // Roles: warps 0-3 softmax + epilogue of query tile A, warps 4-7 of query tile B (thread r owns tile row r = TMEM
@@ -67,8 +67,11 @@ struct Args {
   const uint8_t* mask; int32_t* status;
   long long* trace;                // optional pipeline timestamps, see trace_event
   float* part_o; float* part_ml;   // split-KV partials: O as [unit][D][128], (m, l) as [unit][2][128]
+  int* split_arrivals;             // [seq][kv head][query-tile pair]: splits finished so far (zeroed before the launch)
   int64_t out_stride, block_table_stride, mask_stride_m, mask_stride_n, num_pages;
   int num_seqs, max_pages, num_q_heads, num_kv_heads, group, tpt, q_tiles, q_pairs, num_splits;
+  int first_permille;  // uneven two-way split: share (in 1/1000) of a unit's key tiles that split 0 takes; 0 = even splits
+  int base_ctas;       // (sequence, KV head, query-tile pair) units; blockIdx = split * base_ctas + unit
   int page_size, has_cache, mask_mode, bidirectional, block_m, is_bf16;
   float scale_log2;  // sm_scale * log2(e)
 };
@@ -273,6 +276,83 @@ __device__ __forceinline__ TileInfo tile_info(int t, int n_ctx_tiles, int ctx_le
   return ti;
 }
 
+// Merge of the split-KV partials of one query-tile row: out[row] = sum_s 2^(m_s - M) O_s / sum_s 2^(m_s - M) l_s,
+// splits added in index order whoever runs it. Partials were written by other CTAs: read them past L1. 32 columns of
+// every split are in flight per thread before they are reduced.
+__device__ __forceinline__ void merge_split_row(const float* __restrict__ part_o, const float* __restrict__ part_ml, int S, int is_bf16,
+                                                int64_t unit0, int r, uint8_t* out_row) {
+  float M = -INFINITY;
+  for (int s = 0; s < S; ++s) {
+    const float ms = __ldcg(&part_ml[((unit0 + s) * 2 + 0) * kTileM + r]);
+    if (ms > -INFINITY) M = fmaxf(M, ms);
+  }
+  float wsum = 0.f;
+  for (int s = 0; s < S; ++s) {
+    const float ms = __ldcg(&part_ml[((unit0 + s) * 2 + 0) * kTileM + r]);
+    const float ls = __ldcg(&part_ml[((unit0 + s) * 2 + 1) * kTileM + r]);
+    if (ms > -INFINITY) wsum += exp2f(ms - M) * ls;
+  }
+  const float inv = wsum > 0.f ? 1.f / wsum : 0.f;
+#pragma unroll 1
+  for (int d0 = 0; d0 < kHeadDim; d0 += 32) {
+    float acc[32];
+#pragma unroll
+    for (int j = 0; j < 32; ++j) acc[j] = 0.f;
+#pragma unroll 2
+    for (int s = 0; s < S; ++s) {
+      const float ms = __ldcg(&part_ml[((unit0 + s) * 2 + 0) * kTileM + r]);
+      if (ms == -INFINITY) continue;   // a neutral partial has no O data behind it
+      const float ws = exp2f(ms - M);
+      const float* po = part_o + (unit0 + s) * kHeadDim * kTileM + static_cast<int64_t>(d0) * kTileM + r;
+      float v[32];
+#pragma unroll
+      for (int j = 0; j < 32; ++j) v[j] = __ldcg(po + j * kTileM);
+#pragma unroll
+      for (int j = 0; j < 32; ++j) acc[j] = fmaf(ws, v[j], acc[j]);
+    }
+    uint32_t packed[16];
+#pragma unroll
+    for (int j = 0; j < 32; j += 2) {
+      if (is_bf16) {
+        __nv_bfloat162 h = __floats2bfloat162_rn(acc[j] * inv, acc[j + 1] * inv);
+        packed[j >> 1] = *reinterpret_cast<uint32_t*>(&h);
+      } else {
+        __half2 h = __floats2half2_rn(acc[j] * inv, acc[j + 1] * inv);
+        packed[j >> 1] = *reinterpret_cast<uint32_t*>(&h);
+      }
+    }
+    uint4* dst = reinterpret_cast<uint4*>(out_row + d0 * 2);
+#pragma unroll
+    for (int j = 0; j < 4; ++j) dst[j] = make_uint4(packed[4 * j], packed[4 * j + 1], packed[4 * j + 2], packed[4 * j + 3]);
+  }
+}
+
+// Called by every thread of a CTA once its partials are written and fenced. The CTA that arrives last for its
+// (sequence, KV head, query-tile pair) merges all splits of both query tiles: no CTA ever waits for another.
+__device__ __forceinline__ void finish_split(const Args& a, int seq, int kvh, int pair, int q_start, int tokA, int n_tokA, int tokB,
+                                             int n_tokB) {
+  __shared__ int is_last;
+  const int64_t pair_id = (static_cast<int64_t>(seq) * a.num_kv_heads + kvh) * a.q_pairs + pair;
+  if (threadIdx.x == 0) {
+    is_last = (atomicAdd(&a.split_arrivals[pair_id], 1) == a.num_splits - 1) ? 1 : 0;
+    if (is_last) a.split_arrivals[pair_id] = 0;   // every split has arrived: leave the counter ready for the next launch
+  }
+  __syncthreads();
+  if (!is_last || threadIdx.x >= 2 * kTileM) return;
+  __threadfence();
+  const int x = threadIdx.x >> 7;
+  const int r = threadIdx.x & (kTileM - 1);
+  const int tok0 = x == 0 ? tokA : tokB;
+  const int n_tok = x == 0 ? n_tokA : n_tokB;
+  const int tok_local = r / a.group;
+  if (tok_local >= n_tok) return;
+  const int head_local = r - tok_local * a.group;
+  const int64_t unit0 = ((static_cast<int64_t>(seq) * a.num_kv_heads + kvh) * a.q_tiles + 2 * pair + x) * a.num_splits;
+  uint8_t* out_row = reinterpret_cast<uint8_t*>(a.out) +
+                     ((static_cast<int64_t>(q_start + tok0 + tok_local)) * a.out_stride + static_cast<int64_t>(kvh * a.group + head_local) * kHeadDim) * 2;
+  merge_split_row(a.part_o, a.part_ml, a.num_splits, a.is_bf16, unit0, r, out_row);
+}
+
 __global__ void __launch_bounds__(kThreads, 1)
 attn_sm100_kernel(const __grid_constant__ CUtensorMap q_map, const __grid_constant__ CUtensorMap kn_map,
                   const __grid_constant__ CUtensorMap vn_map, const __grid_constant__ CUtensorMap kc_map,
@@ -288,8 +368,10 @@ attn_sm100_kernel(const __grid_constant__ CUtensorMap q_map, const __grid_consta
   const int lane = threadIdx.x & 31;
 
   // ---- decode the work unit: (sequence, KV head, pair of query tiles, KV split) ----
-  int u = blockIdx.x;
-  const int split = u % a.num_splits; u /= a.num_splits;
+  // Splits are the slowest index: all first splits come first in launch order. With an uneven two-way split those are
+  // the long CTAs, so the short second splits fill in behind them and the last wave stays short.
+  int u = blockIdx.x % a.base_ctas;
+  const int split = blockIdx.x / a.base_ctas;
   const int pair = u % a.q_pairs; u /= a.q_pairs;
   const int kvh = u % a.num_kv_heads;
   const int seq = u / a.num_kv_heads;
@@ -315,9 +397,16 @@ attn_sm100_kernel(const __grid_constant__ CUtensorMap q_map, const __grid_consta
   const int n_ctx_tiles = (ctx_len + kTileN - 1) / kTileN;
   const int n_new_tiles = (new_end + kTileN - 1) / kTileN;
   const int total_tiles = n_ctx_tiles + n_new_tiles;
-  const int per_split = (total_tiles + a.num_splits - 1) / a.num_splits;
-  const int t_begin = split * per_split;
-  const int t_end = min(total_tiles, t_begin + per_split);
+  int t_begin, t_end;
+  if (a.first_permille > 0) {   // two splits: [0, cut) and [cut, total)
+    const int cut = min(total_tiles, (total_tiles * a.first_permille + 999) / 1000);
+    t_begin = split == 0 ? 0 : cut;
+    t_end = split == 0 ? cut : total_tiles;
+  } else {
+    const int per_split = (total_tiles + a.num_splits - 1) / a.num_splits;
+    t_begin = split * per_split;
+    t_end = min(total_tiles, t_begin + per_split);
+  }
   const int n_iter = t_end - t_begin;
   // index of a query tile's split-KV partial
   const int64_t unit_base = ((static_cast<int64_t>(seq) * a.num_kv_heads + kvh) * a.q_tiles + 2 * pair) * a.num_splits + split;
@@ -330,6 +419,11 @@ attn_sm100_kernel(const __grid_constant__ CUtensorMap q_map, const __grid_consta
       const int r = threadIdx.x & (kTileM - 1);
       a.part_ml[(unit * 2 + 0) * kTileM + r] = -INFINITY;
       a.part_ml[(unit * 2 + 1) * kTileM + r] = 0.f;
+    }
+    if (a.num_splits > 1) {
+      __threadfence();
+      __syncthreads();
+      finish_split(a, seq, kvh, pair, q_start, tokA, n_tokA, tokB, n_tokB);
     }
     return;
   }
@@ -674,82 +768,13 @@ attn_sm100_kernel(const __grid_constant__ CUtensorMap q_map, const __grid_consta
 
   // ---- teardown ----
   tc_fence_before();
+  if (a.num_splits > 1) __threadfence();   // this CTA's partials are visible before it counts itself in
   __syncthreads();
   if (warp == kProducerWarp) {
     tc_fence_after();
     tmem_dealloc(tmem_base, kTmemCols);
   }
-}
-
-// Merge of the split-KV partials: out[row] = sum_s 2^(m_s - M) O_s / sum_s 2^(m_s - M) l_s.
-// One CTA per (query tile, 32-column slab); thread r owns tile row r, so every partial read is a coalesced 512-byte
-// line of the [D][128] partial layout. All loads of a step are issued before they are reduced.
-constexpr int kCombineMaxSplits = 32;
-__global__ void __launch_bounds__(kTileM) attn_combine_kernel(const Args a) {
-  const int64_t tile = blockIdx.x >> 2;  // (seq, kvh, qt)
-  const int slab = blockIdx.x & 3;
-  int u = static_cast<int>(tile);
-  const int qt = u % a.q_tiles; u /= a.q_tiles;
-  const int kvh = u % a.num_kv_heads;
-  const int seq = u / a.num_kv_heads;
-  const int q_start = a.cu_seqlens_q[seq];
-  const int q_len = a.cu_seqlens_q[seq + 1] - q_start;
-  const int tok0 = qt * a.tpt;
-  const int n_tok = min(a.tpt, q_len - tok0);
-  if (n_tok <= 0) return;
-  const int G = a.group;
-  const int r = threadIdx.x;
-  const int tok_local = r / G;
-  if (tok_local >= n_tok) return;
-  const int head_local = r - tok_local * G;
-  const int64_t unit0 = tile * a.num_splits;
-  const int S = a.num_splits;
-
-  float M = -INFINITY;
-  for (int s = 0; s < S; ++s) M = fmaxf(M, a.part_ml[((unit0 + s) * 2 + 0) * kTileM + r]);
-  float wsum = 0.f;
-  float w[kCombineMaxSplits];
-#pragma unroll
-  for (int s = 0; s < kCombineMaxSplits; ++s) {
-    w[s] = 0.f;
-    if (s < S) {
-      const float ms = a.part_ml[((unit0 + s) * 2 + 0) * kTileM + r];
-      const float ls = a.part_ml[((unit0 + s) * 2 + 1) * kTileM + r];
-      w[s] = (ms == -INFINITY) ? 0.f : exp2f(ms - M);  // a neutral partial has no O data behind it: weight 0, never read
-      wsum += w[s] * ls;
-    }
-  }
-  const float inv = wsum > 0.f ? 1.f / wsum : 0.f;
-  uint8_t* out_row = reinterpret_cast<uint8_t*>(a.out) +
-                     ((static_cast<int64_t>(q_start + tok0 + tok_local)) * a.out_stride + static_cast<int64_t>(kvh * G + head_local) * kHeadDim) * 2;
-#pragma unroll 1
-  for (int d0 = slab * 32; d0 < slab * 32 + 32; d0 += 8) {
-    float acc[8];
-#pragma unroll
-    for (int j = 0; j < 8; ++j) acc[j] = 0.f;
-#pragma unroll 4
-    for (int s = 0; s < S; ++s) {
-      const float ws = w[s];
-      const float* po = a.part_o + (unit0 + s) * kHeadDim * kTileM + static_cast<int64_t>(d0) * kTileM + r;
-      float v[8];
-#pragma unroll
-      for (int j = 0; j < 8; ++j) v[j] = (ws != 0.f) ? po[j * kTileM] : 0.f;
-#pragma unroll
-      for (int j = 0; j < 8; ++j) acc[j] = fmaf(ws, v[j], acc[j]);
-    }
-    uint32_t packed[4];
-#pragma unroll
-    for (int j = 0; j < 8; j += 2) {
-      if (a.is_bf16) {
-        __nv_bfloat162 h = __floats2bfloat162_rn(acc[j] * inv, acc[j + 1] * inv);
-        packed[j >> 1] = *reinterpret_cast<uint32_t*>(&h);
-      } else {
-        __half2 h = __floats2half2_rn(acc[j] * inv, acc[j + 1] * inv);
-        packed[j >> 1] = *reinterpret_cast<uint32_t*>(&h);
-      }
-    }
-    *reinterpret_cast<uint4*>(out_row + d0 * 2) = make_uint4(packed[0], packed[1], packed[2], packed[3]);
-  }
+  if (a.num_splits > 1) finish_split(a, seq, kvh, pair, q_start, tokA, n_tokA, tokB, n_tokB);
 }
 
 // ---- host side: tensor maps, split choice, launch ---------------------------------------------------------
@@ -805,6 +830,7 @@ inline bool supported(const pdllm_attn_params* p, const char** why) {
 
 struct Plan {
   int group, tpt, q_tiles, q_pairs, num_splits;
+  int first_permille;  // see Args
   int64_t tiles;  // query tiles = split-KV partial groups
   int64_t ctas;   // CTAs launched: pairs of query tiles x splits
 };
@@ -820,6 +846,26 @@ inline Plan make_plan(const pdllm_attn_params* p) {
   const int64_t base_ctas = static_cast<int64_t>(p->num_seqs) * p->num_kv_heads * pl.q_pairs;
   int max_key_tiles = (p->max_seq_len + kTileN - 1) / kTileN + 1;
   int splits = p->num_splits;
+  pl.first_permille = 0;
+  const int64_t sms = sm_count();
+  if (splits <= 0 && base_ctas < sms && 2 * base_ctas > sms && max_key_tiles >= 6) {
+    // More units than half the SMs but fewer than all of them: an even split either leaves SMs idle (1 split) or
+    // runs two full waves (3 splits). Cut every unit in two UNEVEN parts instead: the long parts occupy base_ctas SMs
+    // for the whole kernel, the short parts run k at a time on each of the other SMs, and the cut makes both kinds
+    // of SM finish together: long = ovh + B t, short = k (ovh + S t), B + S = T, with the per-CTA overhead ovh
+    // (prologue, epilogue, its share of the merge) worth about 4.5 key-tile times t: the cut that was fastest on the
+    // op-level shape (33 key tiles, 96 units, 148 SMs) is 24 + 9.
+    const int64_t rest = sms - base_ctas;
+    const int64_t k = (base_ctas + rest - 1) / rest;
+    const double T = max_key_tiles - 1, ovh = 4.5;
+    double S = (T - (k - 1) * ovh) / (k + 1);
+    if (S >= 2.0) {
+      splits = 2;
+      pl.first_permille = static_cast<int>(1000.0 * (T - S) / T + 0.5);
+      if (pl.first_permille < 500) pl.first_permille = 500;
+      if (pl.first_permille > 950) pl.first_permille = 950;
+    }
+  }
   if (splits <= 0) {
     // One CTA per SM: fill a whole number of waves; each split keeps at least two key tiles.
     const int64_t slots = sm_count();
@@ -841,10 +887,16 @@ inline Plan make_plan(const pdllm_attn_params* p) {
   return pl;
 }
 
+// The arrival counters sit at the start of the workspace in a header of fixed size, so that a workspace that was
+// zero-filled once keeps zeroed counters whatever shapes it serves (the kernel returns each counter to zero).
+constexpr int64_t kCounterHeaderBytes = 64 * 1024;
+inline int64_t counter_bytes(int64_t pairs) { return pairs * 4 <= kCounterHeaderBytes ? kCounterHeaderBytes : ((pairs * 4 + 255) / 256) * 256; }
+
 inline int64_t workspace_bytes(const pdllm_attn_params* p) {
   Plan pl = make_plan(p);
   if (pl.num_splits <= 1) return 0;
-  return pl.tiles * pl.num_splits * (static_cast<int64_t>(kHeadDim) * kTileM + 2 * kTileM) * 4;
+  const int64_t pairs = static_cast<int64_t>(p->num_seqs) * p->num_kv_heads * pl.q_pairs;
+  return counter_bytes(pairs) + pl.tiles * pl.num_splits * (static_cast<int64_t>(kHeadDim) * kTileM + 2 * kTileM) * 4;
 }
 
 inline int launch(const pdllm_attn_params* p, cudaStream_t stream) {
@@ -896,12 +948,22 @@ inline int launch(const pdllm_attn_params* p, cudaStream_t stream) {
   a.out = p->out; a.block_table = p->block_table; a.cu_seqlens_q = p->cu_seqlens_q; a.seq_lens = p->seq_lens;
   a.mask = p->mask; a.status = p->status;
   a.trace = reinterpret_cast<long long*>(p->trace);
-  a.part_o = reinterpret_cast<float*>(p->workspace);
+  const int64_t pairs = static_cast<int64_t>(p->num_seqs) * p->num_kv_heads * pl.q_pairs;
+  a.split_arrivals = reinterpret_cast<int*>(p->workspace);
+  a.part_o = p->workspace ? reinterpret_cast<float*>(static_cast<char*>(p->workspace) + counter_bytes(pairs)) : nullptr;
   a.part_ml = a.part_o ? a.part_o + pl.tiles * pl.num_splits * static_cast<int64_t>(kHeadDim) * kTileM : nullptr;
+  if (pl.num_splits > 1 && !(p->workspace_zeroed && pairs * 4 <= kCounterHeaderBytes)) {
+    // The kernel leaves every counter at zero again, so a caller that zero-filled its workspace once (and again after
+    // any launch that reported a wait time-out) can say so and save this memset node on every call.
+    cudaError_t e = cudaMemsetAsync(a.split_arrivals, 0, static_cast<size_t>(pairs) * 4, stream);
+    if (e != cudaSuccess) return fail(static_cast<int>(e), "cudaMemsetAsync(split counters): %s", cudaGetErrorString(e));
+  }
   a.out_stride = p->out_stride; a.block_table_stride = p->block_table_stride;
   a.mask_stride_m = p->mask_stride_m; a.mask_stride_n = p->mask_stride_n; a.num_pages = has_cache ? p->num_pages : 0;
   a.num_seqs = p->num_seqs; a.max_pages = p->max_pages; a.num_q_heads = p->num_q_heads; a.num_kv_heads = p->num_kv_heads;
   a.group = pl.group; a.tpt = pl.tpt; a.q_tiles = pl.q_tiles; a.q_pairs = pl.q_pairs; a.num_splits = pl.num_splits;
+  a.first_permille = pl.num_splits == 2 ? pl.first_permille : 0;
+  a.base_ctas = static_cast<int>(pl.ctas / pl.num_splits);
   a.page_size = p->page_size > 0 ? p->page_size : kTileN; a.has_cache = has_cache ? 1 : 0;
   a.mask_mode = p->mask_mode; a.bidirectional = p->bidirectional;
   a.block_m = 2 * (p->diffusion_blk > 0 ? p->diffusion_blk : 32);
@@ -924,10 +986,6 @@ inline int launch(const pdllm_attn_params* p, cudaStream_t stream) {
 
   attn_sm100_kernel<<<static_cast<unsigned>(pl.ctas), kThreads, kSmemBytes, stream>>>(q_map, kn_map, vn_map, kc_map, vc_map, a);
   if ((rc = check_launch("attn_sm100_kernel")) != 0) return rc;
-  if (pl.num_splits > 1) {
-    attn_combine_kernel<<<static_cast<unsigned>(pl.tiles * 4), kTileM, 0, stream>>>(a);
-    if ((rc = check_launch("attn_combine_kernel")) != 0) return rc;
-  }
   return 0;
 }
 

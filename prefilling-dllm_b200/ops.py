@@ -66,7 +66,8 @@ _state = _DeviceState()
 def status_word(device: torch.device) -> torch.Tensor:
     word = _state.status.get(device)
     if word is None:
-        word = torch.zeros(1, dtype=torch.int32, device=device)
+        with torch.inference_mode(False):   # long-lived and reset in place later: must not be an inference tensor
+            word = torch.zeros(1, dtype=torch.int32, device=device)
         _state.status[device] = word
     return word
 
@@ -79,6 +80,11 @@ def check_status(device: Optional[torch.device] = None, *, reset: bool = True) -
     code = int(word.item())
     if code != 0 and reset:
         word.zero_()
+    if (code & 0xff) == _lib.S_WAIT_TIMEOUT:
+        # an abandoned attention launch may have left split-KV arrival counters behind in the workspace header
+        ws = _state.workspaces.get((torch.device(device), "attn"))
+        if ws is not None:
+            ws[: 64 * 1024].zero_()
     if code != 0:
         detail = f" (barrier {(code >> 8) & 0xff}, warp {(code >> 16) & 0xff}, parity {(code >> 24) & 1})" if code > 0xff else ""
         raise RuntimeError(f"pdllm_b200 device status {code & 0xff}: {_lib.STATUS_NAMES.get(code & 0xff, 'unknown')}{detail}")
@@ -89,7 +95,8 @@ def _workspace(device: torch.device, key: str, nbytes: int, *, zero: bool = Fals
     buf = _state.workspaces.get((device, key))
     if buf is None or buf.numel() < nbytes:
         alloc = max(int(nbytes), 256)
-        buf = torch.zeros(alloc, dtype=torch.uint8, device=device) if zero else torch.empty(alloc, dtype=torch.uint8, device=device)
+        with torch.inference_mode(False):   # kept across calls and cleared in place after a time-out
+            buf = torch.zeros(alloc, dtype=torch.uint8, device=device) if zero else torch.empty(alloc, dtype=torch.uint8, device=device)
         _state.workspaces[(device, key)] = buf
     return buf
 
@@ -269,8 +276,9 @@ def paged_attention(query: torch.Tensor, key: torch.Tensor, value: torch.Tensor,
     if need < 0:
         check(int(need))
     if need > 0:
-        ws = _workspace(device, "attn", int(need))
-        p.workspace, p.workspace_bytes = ws.data_ptr(), ws.numel()
+        # zero-filled when it is created; the kernel keeps its arrival counters at zero between launches
+        ws = _workspace(device, "attn", int(need), zero=True)
+        p.workspace, p.workspace_bytes, p.workspace_zeroed = ws.data_ptr(), ws.numel(), 1
     check(lib.pdllm_paged_attention(ctypes.byref(p), _stream(device)))
     return "tc" if chosen == _lib.ATTN_TC else "simt"
 
