@@ -268,6 +268,25 @@ int pdllm_rope_pages(void* k_cache, const int32_t* page_ids, int64_t start, int6
                      const void* sin_tab, int page_size, int num_kv_heads, int head_dim, int dtype,
                      int64_t num_pages, int32_t* status, void* stream);
 
+/* ------------------------------------------------------------------------------------------------
+ * Row-wise pieces of the transformer block between the GEMMs (one launch each instead of 3-10 eager ones)
+ * replaces RMSNorm.rms_forward / add_rms_forward   prefilling_dllm_engine/prefilling_dllm/layers/layernorm.py:18-41
+ *          apply_rotary_emb / RotaryEmbedding.forward  .../layers/rotary_embedding.py:6-65
+ *          SiluAndMul.forward                          .../layers/activation.py:12-14
+ * with the rounding of the eval model the reference vendors (prefilling_dllm_eval/model_cache/dream/model_dream.py
+ * :117-131, :208-264, :277-278): every intermediate eager mode would hold in the model dtype is rounded to it.
+ * ---------------------------------------------------------------------------------------------- */
+/* if delta != NULL: x[t,:] += delta[t,:] (in place); then out[t,:] = weight * dtype(x[t,:] * rsqrt(mean(x^2) + eps)) */
+int pdllm_add_rmsnorm(void* x, const void* delta, const void* weight, void* out, int64_t n_tokens, int hidden, int64_t x_stride,
+                      int64_t delta_stride, int64_t out_stride, float eps, int dtype, void* stream);
+/* rotate the first num_heads heads of every row of x [n_tokens, *, head_dim] (row stride in elements) in place;
+ * cos_tab / sin_tab: [n_tokens, head_dim] in the same dtype (cat(freqs, freqs) layout) */
+int pdllm_rope_inplace(void* x, const void* cos_tab, const void* sin_tab, int64_t n_tokens, int num_heads, int head_dim,
+                       int64_t row_stride, int dtype, void* stream);
+/* out[t, i] = dtype(silu(gate_up[t, i])) * gate_up[t, inter + i] */
+int pdllm_silu_mul(const void* gate_up, void* out, int64_t n_tokens, int inter, int64_t gu_stride, int64_t out_stride, int dtype,
+                   void* stream);
+
 #ifdef __cplusplus
 }
 #endif

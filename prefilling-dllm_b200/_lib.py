@@ -93,6 +93,9 @@ _SIGNATURES = {
     "pdllm_scatter_pages": (c_int, [c_void_p, c_void_p, c_int64, c_int, c_int64, c_int, c_int64, c_void_p, c_void_p, c_void_p]),
     "pdllm_compact_pages_per_head": (c_int, [c_void_p, c_void_p, c_void_p, c_void_p, c_int64, c_int64, c_int64, c_int, c_int,
                                              c_int, c_int, c_int64, c_void_p, c_void_p, c_void_p]),
+    "pdllm_add_rmsnorm": (c_int, [c_void_p, c_void_p, c_void_p, c_void_p, c_int64, c_int, c_int64, c_int64, c_int64, c_float, c_int, c_void_p]),
+    "pdllm_rope_inplace": (c_int, [c_void_p, c_void_p, c_void_p, c_int64, c_int, c_int, c_int64, c_int, c_void_p]),
+    "pdllm_silu_mul": (c_int, [c_void_p, c_void_p, c_int64, c_int, c_int64, c_int64, c_int, c_void_p]),
     "pdllm_rope_pages": (c_int, [c_void_p, c_void_p, c_int64, c_int64, c_void_p, c_void_p, c_int, c_int, c_int, c_int, c_int64,
                                  c_void_p, c_void_p]),
 }

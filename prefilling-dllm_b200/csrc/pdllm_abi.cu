@@ -3,6 +3,7 @@
 #include "attn_simt.cuh"
 #include "attn_sm100.cuh"
 #include "common.cuh"
+#include "dense.cuh"
 #include "kv_pages.cuh"
 #include "score.cuh"
 
@@ -359,6 +360,53 @@ int pdllm_scatter_pages(const void* src, const int32_t* page_ids, int64_t n_toke
   page_copy_kernel<true><<<grid_for(n_tokens * segs, 256), 256, 0, as_stream(stream)>>>(
       static_cast<const uint4*>(src), static_cast<uint4*>(cache), page_ids, n_tokens, page_size, segs, num_pages, status);
   return check_launch("scatter_pages");
+}
+
+// ------------------------------------------------------------------------------------------------ dense row ops
+#define PDLLM_DISPATCH_DTYPE(dtype, what, ...)                                    \
+  do {                                                                            \
+    if ((dtype) == PDLLM_F32) { using T = float; __VA_ARGS__; }                   \
+    else if ((dtype) == PDLLM_BF16) { using T = __nv_bfloat16; __VA_ARGS__; }     \
+    else if ((dtype) == PDLLM_F16) { using T = __half; __VA_ARGS__; }             \
+    else return fail(PDLLM_E_UNSUPPORTED, what ": dtype must be f32, bf16 or f16"); \
+  } while (0)
+
+int pdllm_add_rmsnorm(void* x, const void* delta, const void* weight, void* out, int64_t n_tokens, int hidden, int64_t x_stride,
+                      int64_t delta_stride, int64_t out_stride, float eps, int dtype, void* stream) {
+  if (n_tokens < 0 || hidden <= 0) return fail(PDLLM_E_INVALID, "add_rmsnorm: bad sizes");
+  if (n_tokens == 0) return 0;
+  if (!x || !weight || !out) return fail(PDLLM_E_INVALID, "add_rmsnorm: null pointer");
+  const int threads = hidden >= 2048 ? 512 : 256;
+  PDLLM_DISPATCH_DTYPE(dtype, "add_rmsnorm",
+                       add_rmsnorm_kernel<T><<<static_cast<unsigned>(n_tokens), threads, 0, as_stream(stream)>>>(
+                           static_cast<T*>(x), static_cast<const T*>(delta), static_cast<const T*>(weight), static_cast<T*>(out), hidden,
+                           x_stride, delta_stride, out_stride, eps));
+  return check_launch("add_rmsnorm");
+}
+
+int pdllm_rope_inplace(void* x, const void* cos_tab, const void* sin_tab, int64_t n_tokens, int num_heads, int head_dim,
+                       int64_t row_stride, int dtype, void* stream) {
+  if (n_tokens < 0 || num_heads <= 0 || head_dim <= 0 || head_dim % 2 != 0) return fail(PDLLM_E_INVALID, "rope_inplace: bad sizes");
+  if (n_tokens == 0) return 0;
+  if (!x || !cos_tab || !sin_tab) return fail(PDLLM_E_INVALID, "rope_inplace: null pointer");
+  const int grid = grid_for(n_tokens * num_heads * (head_dim / 2), 256);
+  PDLLM_DISPATCH_DTYPE(dtype, "rope_inplace",
+                       rope_inplace_kernel<T><<<grid, 256, 0, as_stream(stream)>>>(static_cast<T*>(x), static_cast<const T*>(cos_tab),
+                                                                                   static_cast<const T*>(sin_tab), n_tokens, num_heads,
+                                                                                   head_dim, row_stride));
+  return check_launch("rope_inplace");
+}
+
+int pdllm_silu_mul(const void* gate_up, void* out, int64_t n_tokens, int inter, int64_t gu_stride, int64_t out_stride, int dtype,
+                   void* stream) {
+  if (n_tokens < 0 || inter <= 0) return fail(PDLLM_E_INVALID, "silu_mul: bad sizes");
+  if (n_tokens == 0) return 0;
+  if (!gate_up || !out) return fail(PDLLM_E_INVALID, "silu_mul: null pointer");
+  const int grid = grid_for(n_tokens * inter, 256);
+  PDLLM_DISPATCH_DTYPE(dtype, "silu_mul",
+                       silu_mul_kernel<T><<<grid, 256, 0, as_stream(stream)>>>(static_cast<const T*>(gate_up), static_cast<T*>(out), n_tokens,
+                                                                               inter, gu_stride, out_stride));
+  return check_launch("silu_mul");
 }
 
 int pdllm_rope_pages(void* k_cache, const int32_t* page_ids, int64_t start, int64_t n_tokens, const void* cos_tab,

@@ -542,20 +542,21 @@ class FastDLLMDreamEngine:
         step forwards the whole block (its K/V replace their slots), softmax in fp32, the most confident masked slot is
         always accepted and every other one whose confidence reaches the threshold."""
         decode_len = len(block_positions)
-        block = torch.full((decode_len,), self.mask_token_id, dtype=torch.long, device=self.device)
-        block[0] = int(first_token_id)
         n_steps = 0
         remaining = decode_len - 1
+        runner = self.model.block_step_runner(block_len=decode_len, positions=block_positions, ctx_page_ids=ctx_page_ids, ctx_len=ctx_len,
+                                              mask_token_id=self.mask_token_id, threshold=self.threshold, last_logit=last_context_logit,
+                                              shift=True, softmax_dtype=torch.float32, store_slots=block_slots,
+                                              use_graph=not self.config.enforce_eager)
+        block = runner.block                          # the step's ids buffer, updated in place by the unmask kernel
+        block.fill_(self.mask_token_id)
+        block[0] = int(first_token_id)
         while remaining > 0:
             n_steps += 1
-            logits, _ = self._forward(block, block_positions, ctx_page_ids=ctx_page_ids, ctx_len=ctx_len, store_slots=block_slots)
-            with torch.cuda.device(self.device):
-                counts = ops.unmask_step(logits, block, mask_token_id=self.mask_token_id, threshold=self.threshold,
-                                         last_logit=last_context_logit, shift=True, softmax_dtype=torch.float32)
-            remaining = int(counts[2].item())      # the one host read of a step
+            remaining = runner.run()      # forward + unmask kernel (CUDA graph replays unless enforce_eager); one host read
             if n_steps > decode_len + 8:
                 raise RuntimeError("denoising did not converge: every step must unmask at least one slot")
-        return block, n_steps
+        return block.clone(), n_steps
 
     def _finish(self, block: torch.Tensor, max_new_tokens: int, stop_token_ids, n_steps: int) -> FastDLLMEngineOutput:
         generated = block[:max_new_tokens].tolist()

@@ -1,8 +1,8 @@
 """Dream / LLaDA-architecture transformer over a paged KV pool, GPU only.
 
-The dense layers (embedding, RMSNorm, QKV / O / MLP / LM-head GEMMs, RoPE, SwiGLU) are plain torch on the current
-CUDA stream (cuBLAS GEMMs); the parts of the hot path that this package owns — KV page writes and attention over
-[selected prefix pages ‖ new rows] — go through the sm_100a kernels in `ops`. Arithmetic follows the Dream model the
+The GEMMs (QKV / O / MLP / LM head) and the embedding gather are torch on the current CUDA stream (cuBLAS); everything
+between them — RMSNorm with the residual add, RoPE in place on the fused QKV output, SiLU·mul, KV page writes and
+attention over [selected prefix pages ‖ new rows] — goes through the sm_100a kernels in `ops`: 11 launches per layer. Arithmetic follows the Dream model the
 reference vendors (prefilling_dllm_eval/model_cache/dream/model_dream.py:117-131 RMSNorm in fp32, :208-264 rotate-half
 RoPE with fp32 tables, :326-329 biased q/k/v, :277-278 SwiGLU, :689-711 pre-norm residual) and the engine's own
 restatement (prefilling_dllm_engine/prefilling_dllm/models/dream.py:26-237). Keys are stored in pages AFTER RoPE, like
@@ -265,20 +265,10 @@ class PagedDreamModel:
         return cls(arch, state, device=dev, dtype=dtype, num_pages=num_pages, page_size=page_size)
 
     # ---- pieces ----
-    def _rmsnorm(self, x: torch.Tensor, weight: torch.Tensor) -> torch.Tensor:
-        xf = x.float()
-        xf = xf * torch.rsqrt(xf.pow(2).mean(-1, keepdim=True) + self.arch.rms_norm_eps)
-        return weight * xf.to(x.dtype)
-
     def _rope_tables(self, positions: torch.Tensor) -> Tuple[torch.Tensor, torch.Tensor]:
         freqs = positions.float().unsqueeze(-1) * self.inv_freq.unsqueeze(0)  # [T, D/2] fp32
         emb = torch.cat((freqs, freqs), dim=-1)
         return emb.cos().to(self.dtype).unsqueeze(1), emb.sin().to(self.dtype).unsqueeze(1)  # [T, 1, D]
-
-    @staticmethod
-    def _rotate_half(x: torch.Tensor) -> torch.Tensor:
-        half = x.shape[-1] // 2
-        return torch.cat((-x[..., half:], x[..., :half]), dim=-1)
 
     def layer_cache(self, layer: int) -> Tuple[torch.Tensor, torch.Tensor]:
         return self.kv_cache[0, layer], self.kv_cache[1, layer]
@@ -309,28 +299,29 @@ class PagedDreamModel:
         """
         a = self.arch
         hq, hkv, d = a.num_attention_heads, a.num_key_value_heads, a.head_dim
-        x = self.embed[ids]                                              # [T, hidden]
+        if store_unrotated_k and store_after_attention:
+            raise ValueError("store_unrotated_k and store_after_attention are not combined by any caller")
+        x = self.embed[ids]                                              # [T, hidden], the residual stream
         cos, sin = self._rope_tables(positions)
+        cos2, sin2 = cos.reshape(-1, d), sin.reshape(-1, d)
         captured = {}
         capture = set(capture_qk_layers) if capture_qk_layers is not None else ()
         total = ids.numel()
         attn_out = torch.empty((total, hq, d), dtype=self.dtype, device=self.device)
+        eps = a.rms_norm_eps
+        delta = None                                                     # output of the previous sub-block, not yet added to x
         for li, w in enumerate(self.layers):
-            h = self._rmsnorm(x, w["ln1"])
-            qkv = F.linear(h, w["wqkv"], w["bqkv"])
-            q = qkv[:, : hq * d].view(total, hq, d)
-            k = qkv[:, hq * d: (hq + hkv) * d].view(total, hkv, d)
-            v = qkv[:, (hq + hkv) * d:].view(total, hkv, d)
-            k_raw = k.contiguous() if store_unrotated_k else None
-            q = (q * cos + self._rotate_half(q) * sin).contiguous()
-            k = (k * cos + self._rotate_half(k) * sin).contiguous()
-            k_store = k_raw if store_unrotated_k else k
-            v = v.contiguous()
-            if li in capture:
-                captured[li] = (q, k)
+            h = ops.add_rmsnorm(x, w["ln1"], eps, delta)                 # x += delta; h = norm(x)
+            qkv = F.linear(h, w["wqkv"], w["bqkv"]).view(total, hq + 2 * hkv, d)
+            q, k, v = qkv[:, :hq], qkv[:, hq:hq + hkv], qkv[:, hq + hkv:]   # strided views of one buffer: no copies
             k_cache, v_cache = self.layer_cache(li)
-            if slot_mapping is not None and not store_after_attention:
-                ops.store_kvcache_unified_layout(k_store, v, k_cache, v_cache, slot_mapping, "diffusion_lm")
+            if slot_mapping is not None and store_unrotated_k:
+                ops.store_kvcache_unified_layout(k, v, k_cache, v_cache, slot_mapping, "diffusion_lm")
+            ops.rope_inplace(qkv[:, :hq + hkv], cos2, sin2)              # q and k heads are adjacent: one launch
+            if li in capture:
+                captured[li] = (q.contiguous(), k.contiguous())
+            if slot_mapping is not None and not store_after_attention and not store_unrotated_k:
+                ops.store_kvcache_unified_layout(k, v, k_cache, v_cache, slot_mapping, "diffusion_lm")
             if block_table is not None:
                 ops.paged_attention(q, k, v, attn_out, cu_seqlens_q=cu_seqlens, max_query_len=max_query_len, key_cache=k_cache,
                                     value_cache=v_cache, block_table=block_table, seq_lens=seq_lens, max_seq_len=max_seq_len,
@@ -339,16 +330,16 @@ class PagedDreamModel:
                 ops.paged_attention(q, k, v, attn_out, cu_seqlens_q=cu_seqlens, max_query_len=max_query_len,
                                     sm_scale=self.scale, causal=causal, bidirectional=True, mask=new_row_mask)
             if slot_mapping is not None and store_after_attention:
-                ops.store_kvcache_unified_layout(k_store, v, k_cache, v_cache, slot_mapping, "diffusion_lm")
-            x = x + F.linear(attn_out.view(total, hq * d), w["wo"])
-            h = self._rmsnorm(x, w["ln2"])
-            gu = F.linear(h, w["wgu"])
-            inter = a.intermediate_size
-            x = x + F.linear(F.silu(gu[:, :inter]) * gu[:, inter:], w["wd"])
+                ops.store_kvcache_unified_layout(k, v, k_cache, v_cache, slot_mapping, "diffusion_lm")
+            proj = F.linear(attn_out.view(total, hq * d), w["wo"])
+            h = ops.add_rmsnorm(x, w["ln2"], eps, proj)                  # x += attention output; h = norm(x)
+            delta = F.linear(ops.silu_mul(F.linear(h, w["wgu"])), w["wd"])
+        if delta is not None:
+            x = x + delta
         logits = None
         if want_logits:
             rows = x if logit_rows is None else x.index_select(0, logit_rows)
-            logits = F.linear(self._rmsnorm(rows, self.final_norm), self.lm_head)
+            logits = F.linear(ops.add_rmsnorm(rows.contiguous(), self.final_norm, eps), self.lm_head)
         return logits, captured
 
     def rope_rows(self, page_ids, start: int, positions: Sequence[int]) -> None:
@@ -359,9 +350,107 @@ class PagedDreamModel:
         for layer in range(self.arch.num_hidden_layers):
             ops.rope_pages(self.layer_cache(layer)[0], page_ids, start, cos, sin)
 
+    def block_step_runner(self, *, block_len: int, positions: Sequence[int], ctx_page_ids: Sequence[int], ctx_len: int,
+                          mask_token_id: int, threshold: float, last_logit: Optional[torch.Tensor], shift: bool,
+                          softmax_dtype: Optional[torch.dtype], store_slots: Optional[Sequence[int]] = None,
+                          use_graph: bool = True) -> "BlockStepRunner":
+        """One denoise step = forward of the block rows against `ctx_len` cached tokens + the unmask kernel, repeated
+        with identical shapes until the block is full. Returns a runner whose `.block` (int64 [block_len]) the caller
+        fills with the initial ids; `.run()` performs a step and returns the number of MASK slots left."""
+        return BlockStepRunner(self, block_len=block_len, positions=positions, ctx_page_ids=ctx_page_ids, ctx_len=ctx_len,
+                               mask_token_id=mask_token_id, threshold=threshold, last_logit=last_logit, shift=shift,
+                               softmax_dtype=softmax_dtype, store_slots=store_slots, use_graph=use_graph)
+
     # ---- small tensor helpers ----
     def ids_tensor(self, ids: Sequence[int]) -> torch.Tensor:
         return torch.tensor(list(ids), dtype=torch.long, device=self.device)
 
     def i32(self, values: Sequence[int]) -> torch.Tensor:
         return torch.tensor(list(values), dtype=torch.int32, device=self.device)
+
+
+
+class _StepGraph:
+    """A captured denoise step and the device buffers it reads: per request only their CONTENTS change."""
+
+    def __init__(self, model: "PagedDreamModel", n: int, pages: int, has_last: bool, stores: bool):
+        dev = model.device
+        self.block = torch.zeros(n, dtype=torch.long, device=dev)
+        self.positions = torch.zeros(n, dtype=torch.long, device=dev)
+        self.table = torch.zeros((1, pages), dtype=torch.int32, device=dev)
+        self.seq_lens = torch.zeros(1, dtype=torch.int32, device=dev)
+        self.last_logit = torch.zeros(model.arch.vocab_size, dtype=model.dtype, device=dev) if has_last else None
+        self.slots = torch.full((n,), -1, dtype=torch.int32, device=dev) if stores else None
+        self.cu = model.i32([0, n])
+        self.graph: Optional[torch.cuda.CUDAGraph] = None
+        self.counts: Optional[torch.Tensor] = None
+        self.eager_steps = 0
+
+
+class BlockStepRunner:
+    """The inner loop of block denoising: every step launches the same ~12 kernels per layer on the same 32 rows, so on
+    a 7B model a step is bound by launch overhead (hundreds of launches of microseconds each), not by the 15 GB of
+    weights it reads. A step is therefore captured into a CUDA graph, once per shape class — (block length, context
+    pages rounded up to a multiple of four, unmask rule) — and kept with the model; a request only copies its ids,
+    positions, page list, context length and last-context logit into the graph's input buffers and replays. The first
+    step of a new shape class runs eagerly (it also initialises library handles and grow-only workspaces), the second
+    is the capture. Capturing costs about as much as a hundred steps, so it pays from the second request on."""
+
+    _PAGE_BUCKET = 4
+    _MAX_CACHED = 8
+
+    def __init__(self, model: PagedDreamModel, *, block_len, positions, ctx_page_ids, ctx_len, mask_token_id, threshold, last_logit,
+                 shift, softmax_dtype, store_slots, use_graph):
+        self.m = model
+        n = int(block_len)
+        need_pages = max(1, -(-int(ctx_len) // model.page_size))
+        pages = -(-need_pages // self._PAGE_BUCKET) * self._PAGE_BUCKET
+        key = (n, pages, int(mask_token_id), float(threshold), last_logit is not None, bool(shift), softmax_dtype, store_slots is not None)
+        cache = model.__dict__.setdefault("_step_graphs", {})
+        entry = cache.pop(key, None) if use_graph else None
+        if entry is None:
+            with torch.inference_mode(False):
+                entry = _StepGraph(model, n, pages, last_logit is not None, store_slots is not None)
+        if use_graph:
+            cache[key] = entry                      # most recently used last
+            while len(cache) > self._MAX_CACHED:
+                cache.pop(next(iter(cache)))
+        self.e = entry
+        self.n, self.use_graph = n, bool(use_graph)
+        self.block = entry.block
+        dev = model.device
+        entry.positions.copy_(torch.tensor(list(positions), dtype=torch.long, device=dev))
+        ids = list(ctx_page_ids)[:need_pages]
+        entry.table[0, : len(ids)].copy_(model.i32(ids))
+        entry.seq_lens.fill_(int(ctx_len) + n)
+        if entry.last_logit is not None:
+            entry.last_logit.copy_(last_logit.reshape(-1))
+        if entry.slots is not None:
+            entry.slots.copy_(model.i32(list(store_slots)))
+        self.kwargs = dict(block_table=entry.table, seq_lens=entry.seq_lens, max_seq_len=pages * model.page_size + n)
+        self.unmask = dict(mask_token_id=int(mask_token_id), threshold=float(threshold), last_logit=entry.last_logit, shift=bool(shift),
+                           softmax_dtype=softmax_dtype)
+        if int(ctx_len) <= 0:
+            raise ValueError("block denoising needs a cached context")
+
+    def _step(self) -> torch.Tensor:
+        e = self.e
+        logits, _ = self.m.forward(e.block, e.positions, cu_seqlens=e.cu, max_query_len=self.n, slot_mapping=e.slots, causal=False,
+                                   **self.kwargs)
+        return ops.unmask_step(logits, e.block, **self.unmask)
+
+    def run(self) -> int:
+        e = self.e
+        with torch.cuda.device(self.m.device):
+            if not self.use_graph or (e.graph is None and e.eager_steps == 0):
+                e.eager_steps += 1
+                counts = self._step()
+            else:
+                if e.graph is None:
+                    graph = torch.cuda.CUDAGraph()
+                    with torch.cuda.graph(graph):
+                        e.counts = self._step()
+                    e.graph = graph                  # capturing records the launches without running them
+                e.graph.replay()
+                counts = e.counts
+            return int(counts[2].item())

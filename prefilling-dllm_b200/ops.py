@@ -558,3 +558,44 @@ def rope_pages(k_cache: torch.Tensor, page_ids, start: int, cos: torch.Tensor, s
     check(_lib.load().pdllm_rope_pages(k_cache.data_ptr(), ids.data_ptr(), int(start), n, cos.data_ptr(), sin.data_ptr(), page_size,
                                        hkv, d, dtype_code(k_cache.dtype), k_cache.shape[0], status_word(device).data_ptr(),
                                        _stream(device)))
+
+
+# ---------------------------------------------------------------------------------------------------
+# row-wise pieces of the transformer block
+# ---------------------------------------------------------------------------------------------------
+def add_rmsnorm(x: torch.Tensor, weight: torch.Tensor, eps: float, delta: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """`x += delta` in place when `delta` is given, then returns RMSNorm(x) * weight (new tensor). x, delta: `[T, hidden]`."""
+    device = _require_cuda(x, weight, delta)
+    if x.dim() != 2 or x.stride(1) != 1 or weight.numel() != x.shape[1] or not weight.is_contiguous():
+        raise ValueError("add_rmsnorm expects x [tokens, hidden] with contiguous rows and weight [hidden]")
+    if delta is not None and (delta.shape != x.shape or delta.stride(1) != 1 or delta.dtype != x.dtype):
+        raise ValueError("delta must match x")
+    out = torch.empty((x.shape[0], x.shape[1]), dtype=x.dtype, device=device)
+    check(_lib.load().pdllm_add_rmsnorm(x.data_ptr(), _ptr(delta), weight.data_ptr(), out.data_ptr(), x.shape[0], x.shape[1], x.stride(0),
+                                        0 if delta is None else delta.stride(0), out.stride(0), float(eps), dtype_code(x.dtype),
+                                        _stream(device)))
+    return out
+
+
+def rope_inplace(x: torch.Tensor, cos: torch.Tensor, sin: torch.Tensor) -> None:
+    """Rotate the heads of `x` `[T, heads, D]` (any row stride; heads and D contiguous) in place with tables `[T, D]`."""
+    device = _require_cuda(x, cos, sin)
+    t, h, d = x.shape
+    if x.stride(2) != 1 or x.stride(1) != d:
+        raise ValueError("x must have contiguous heads and head_dim")
+    cos, sin = cos.reshape(-1, d), sin.reshape(-1, d)
+    if cos.shape[0] != t or sin.shape != cos.shape or cos.dtype != x.dtype or sin.dtype != x.dtype or not (cos.is_contiguous() and sin.is_contiguous()):
+        raise ValueError("cos / sin must be contiguous [tokens, head_dim] tables in the dtype of x")
+    check(_lib.load().pdllm_rope_inplace(x.data_ptr(), cos.data_ptr(), sin.data_ptr(), t, h, d, x.stride(0), dtype_code(x.dtype), _stream(device)))
+
+
+def silu_mul(gate_up: torch.Tensor) -> torch.Tensor:
+    """`silu(gate_up[:, :I]) * gate_up[:, I:]` for `[T, 2I]` rows."""
+    device = _require_cuda(gate_up)
+    if gate_up.dim() != 2 or gate_up.stride(1) != 1 or gate_up.shape[1] % 2 != 0:
+        raise ValueError("gate_up must be [tokens, 2 * intermediate] with contiguous rows")
+    inter = gate_up.shape[1] // 2
+    out = torch.empty((gate_up.shape[0], inter), dtype=gate_up.dtype, device=device)
+    check(_lib.load().pdllm_silu_mul(gate_up.data_ptr(), out.data_ptr(), gate_up.shape[0], inter, gate_up.stride(0), out.stride(0),
+                                     dtype_code(gate_up.dtype), _stream(device)))
+    return out

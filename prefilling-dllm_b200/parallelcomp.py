@@ -103,6 +103,7 @@ class FastDLLMParallelCompConfig:
 
     # not in the reference: size of the paged KV pool (pages of 256 tokens); 0 = derive from max_length
     num_kv_pages: int = 0
+    decode_cuda_graph: bool = True   # replay the denoise step (forward + unmask) of a block as a CUDA graph
 
 
 @dataclass
@@ -638,7 +639,12 @@ class FastDLLMParallelComp:
             else:
                 first = first_token
             ctx = done + tail_len
-            block = torch.full((blen,), mask_id, dtype=torch.long, device=self.device)
+            runner = self.model.block_step_runner(block_len=blen, positions=block_pos, ctx_page_ids=cache.page_ids, ctx_len=ctx,
+                                                  mask_token_id=mask_id, threshold=float(self.config.threshold), last_logit=last_logit,
+                                                  shift=self.arch.logit_shift, softmax_dtype=None,
+                                                  use_graph=bool(self.config.decode_cuda_graph))
+            block = runner.block                      # the step's ids buffer, updated in place by the unmask kernel
+            block.fill_(mask_id)
             block[0] = first
             guard = 0
             remaining = blen - 1
@@ -646,10 +652,7 @@ class FastDLLMParallelComp:
                 guard += 1
                 if guard > blen + 8:
                     break
-                logits, _ = self._forward_packed([[0] * blen], [block_pos], causal=False, cache=cache, ctx_len=ctx, ids_tensor=block)
-                counts = ops.unmask_step(logits, block, mask_token_id=mask_id, threshold=float(self.config.threshold),
-                                         last_logit=last_logit, shift=self.arch.logit_shift)
-                remaining = int(counts[2].item())   # the one host read per denoise step
+                remaining = runner.run()   # forward + unmask kernel (a CUDA graph replay from the third step on); one host read
             generated.extend(block.tolist())
             # commit forward: the finished block's K/V take the first slots behind prompt+finished; its last logit is the
             # next block's "last context logit". The store comes after attention so the later-MASK slots are still seen.

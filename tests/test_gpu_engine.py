@@ -40,7 +40,7 @@ def cpu_model(ckpt):
 def _engine(ckpt, pages=24, **kw):
     from prefilling_dllm_b200.engine import FastDLLMDreamEngine
 
-    return FastDLLMDreamEngine(ckpt, max_model_len=8192, block_length=BLOCK, mask_token_id=MASK, threshold=0.9, dtype=torch.float32,
+    return FastDLLMDreamEngine(ckpt, max_model_len=8192, block_length=BLOCK, mask_token_id=MASK, threshold=0.9, dtype=torch.float32, enforce_eager=kw.pop("enforce_eager", False),
                                num_kv_pages=pages, **kw)
 
 

@@ -548,3 +548,46 @@ def test_rope_pages_in_place(ops, cuda_device, dtype):
     assert torch.equal(dev_cache.cpu()[untouched], cache[untouched])
     with pytest.raises(ValueError):
         ops.rope_pages(dev_cache, [0], 0, cos.to(cuda_device), sin.to(cuda_device))
+
+
+@pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16])
+def test_dense_row_ops_match_eager(ops, cuda_device, dtype):
+    """RMSNorm (+ residual add), in-place RoPE on a strided QKV buffer and SiLU*mul against the eager expressions of the
+    model they replace, with eager's rounding of every intermediate (bit-exact in bf16 except where a reduction order
+    can move the last bit of the fp32 mean)."""
+    g = torch.Generator().manual_seed(90)
+    t, hidden, hq, hkv, d, inter = 37, 512, 4, 2, 128, 688
+    x = torch.randn(t, hidden, generator=g).to(dtype)
+    delta = torch.randn(t, hidden, generator=g).to(dtype)
+    w = (1 + 0.1 * torch.randn(hidden, generator=g)).to(dtype)
+    xd, dd = x.to(cuda_device), delta.to(cuda_device)
+    out = ops.add_rmsnorm(xd, w.to(cuda_device), 1e-6, dd)
+    x_ref = x + delta
+    xf = x_ref.float()
+    ref = w * (xf * torch.rsqrt(xf.pow(2).mean(-1, keepdim=True) + 1e-6)).to(dtype)
+    assert torch.equal(xd.cpu(), x_ref)
+    tol = dict(rtol=1e-5, atol=1e-6) if dtype == torch.float32 else dict(rtol=2 ** -7, atol=1e-3)
+    assert torch.allclose(out.cpu().float(), ref.float(), **tol)
+    if dtype == torch.bfloat16:   # all but a stray last-bit difference are identical (fp32: the reduction order shows)
+        assert (out.cpu() != ref).float().mean() < 0.01
+    plain = ops.add_rmsnorm(x.to(cuda_device), w.to(cuda_device), 1e-6)
+    xf = x.float()
+    assert torch.allclose(plain.cpu().float(), (w * (xf * torch.rsqrt(xf.pow(2).mean(-1, keepdim=True) + 1e-6)).to(dtype)).float(), **tol)
+    # rope on the q and k heads of a fused [T, hq + 2 hkv, d] buffer; v must stay untouched
+    qkv = torch.randn(t, hq + 2 * hkv, d, generator=g).to(dtype)
+    pos = torch.randint(0, 30000, (t,), generator=g)
+    inv = 1.0 / (1e6 ** (torch.arange(0, d, 2).float() / d))
+    emb = torch.cat((pos.float().unsqueeze(-1) * inv,) * 2, dim=-1)
+    cos, sin = emb.cos().to(dtype), emb.sin().to(dtype)
+    dev = qkv.to(cuda_device)
+    ops.rope_inplace(dev[:, : hq + hkv], cos.to(cuda_device), sin.to(cuda_device))
+    part = qkv[:, : hq + hkv]
+    rot = torch.cat((-part[..., d // 2:], part[..., : d // 2]), dim=-1)
+    assert torch.equal(dev.cpu()[:, : hq + hkv], part * cos.unsqueeze(1) + rot * sin.unsqueeze(1))
+    assert torch.equal(dev.cpu()[:, hq + hkv:], qkv[:, hq + hkv:])
+    gu = torch.randn(t, 2 * inter, generator=g).to(dtype)
+    got = ops.silu_mul(gu.to(cuda_device)).cpu()
+    want = torch.nn.functional.silu(gu[:, :inter]) * gu[:, inter:]
+    assert torch.allclose(got.float(), want.float(), **tol)
+    if dtype == torch.bfloat16:
+        assert (got != want).float().mean() < 0.01
