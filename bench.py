@@ -305,12 +305,109 @@ def run_reference(args, rank: int, world: int):
     }
 
 
+def run_request(args, rank: int, world: int, local_rank: int):
+    """End-to-end request latency and decode rate of the whole hot path at BASELINE configs[2] / configs[3] shapes:
+    Dream-7B architecture (random init, bf16), random prefix + 64-token query through the eval-class runtime.
+
+    dream7b_8k : 8192-token prefix, chunk 1024, top-4, joint full_prompt_mask prefill, 32 new tokens, ONE GPU per replica
+                 (with --gpus N every rank serves its own request: weak scaling, no collective).
+    dream7b_32k: 32768-token prefix, 32 chunks, top-8, token_capacity 256, chunk_query mode, 64 new tokens; chunk scoring
+                 and chunk prefill sharded over the N ranks (score all-gather, KV hand-off to the decode rank)."""
+    from prefilling_dllm_b200 import ops
+    from prefilling_dllm_b200.model import DreamArch, PagedDreamModel
+    from prefilling_dllm_b200.parallelcomp import FastDLLMParallelComp, FastDLLMParallelCompConfig
+    from prefilling_dllm_b200.sharded import ShardedChunkPrefill
+
+    device = torch.device("cuda", local_rank)
+    torch.cuda.set_device(device)
+    long_ctx = args.workload == "dream7b_32k"
+    prefix_len, topk, new_tokens = (32768, 8, 64) if long_ctx else (8192, 4, 32)
+    model = PagedDreamModel.random_init(DreamArch.dream_7b(), device=device, dtype=torch.bfloat16, num_pages=160, page_size=256, seed=0)
+    cfg = FastDLLMParallelCompConfig(
+        fastdllm_dream_dir="", pretrained="", device="cuda", dtype="bfloat16", chunk_size=1024, topk_chunks=topk,
+        score_mode="draft_self_information", score_draft_tokens=4, score_draft_partial_rounds=1, score_context_mode="single_chunk",
+        score_attention_mask="causal", score_batch_size=8, block_length=32, max_new_tokens=new_tokens, threshold=0.9, temperature=0.0,
+        cache_build_mode="chunk_query" if long_ctx else "full_prompt_mask",
+        chunk_position_mode="reuse" if long_ctx else "continuous",
+        query_position_mode="after_reused_window" if long_ctx else "after_selected_chunks",
+        token_capacity=256 if long_ctx else 0)
+    rt = FastDLLMParallelComp(cfg, model=model)
+    sharded = ShardedChunkPrefill(rt) if (long_ctx and world > 1) else None
+    gen = torch.Generator().manual_seed(0 if long_ctx else rank)
+    context = torch.randint(0, 151000, (prefix_len,), generator=gen).tolist()
+    query = torch.randint(0, 151000, (64,), generator=gen).tolist()
+
+    def request():
+        if sharded is not None:
+            return sharded.generate(prefix_ids=rt.bos_ids(), context_ids=context, query_ids=query, decode_rank=0)
+        return rt.generate(prefix_ids=rt.bos_ids(), context_ids=context, query_ids=query)
+
+    def barrier():
+        if world > 1:
+            torch.distributed.barrier()
+        torch.cuda.synchronize(device)
+
+    steps, warmup = max(1, min(args.steps, 20)), max(3, min(args.warmup, 5))
+    for _ in range(warmup):
+        request()
+    ops.check_status(device)
+    sampler = ClockSampler(local_rank)
+    if rank == 0:
+        sampler.start()
+    decode_s0 = rt.total_generation_time
+    phase = {"decode": 0.0}
+    inner = rt._denoise_blocks
+
+    def timed_denoise(*a, **k):
+        torch.cuda.synchronize(device)
+        t0 = time.perf_counter()
+        out = inner(*a, **k)
+        torch.cuda.synchronize(device)
+        phase["decode"] += time.perf_counter() - t0
+        return out
+
+    rt._denoise_blocks = timed_denoise
+    barrier()
+    start, stop = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    start.record()
+    for _ in range(steps):
+        request()
+    stop.record()
+    barrier()
+    ms = torch.tensor([start.elapsed_time(stop) / steps], device=device)
+    dec = torch.tensor([phase["decode"] / steps], device=device)
+    if world > 1:
+        torch.distributed.all_reduce(ms, op=torch.distributed.ReduceOp.MAX)
+        torch.distributed.all_reduce(dec, op=torch.distributed.ReduceOp.MAX)
+    clocks = sampler.stop() if rank == 0 else None
+    ops.check_status(device)
+    if rank != 0:
+        return None
+    ms_per_request, decode_s = float(ms.item()), float(dec.item())
+    requests_in_flight = 1 if long_ctx else world
+    return {
+        "metric": "request_latency_ms", "value": ms_per_request, "unit": "ms", "n_gpus": world, "steps": steps, "warmup": warmup,
+        "ms_per_step": ms_per_request, "higher_is_better": False, "scaling": "strong" if long_ctx else "weak", "vs_baseline": None,
+        "dtype": "bf16", "data": "synthetic",
+        "config": {"workload": f"{args.workload}: Dream-7B architecture, random init, {prefix_len}-token random prefix + 64-token query, "
+                               f"chunk 1024, top-{topk}, block 32, {new_tokens} new tokens, threshold 0.9, greedy, "
+                               + ("token_capacity 256, chunk_query, chunks sharded over the ranks" if long_ctx else "full_prompt_mask"),
+                   "parallelism": (f"chunks over {world} ranks, decode on rank 0" if long_ctx else f"dp{world} (one request per rank)")},
+        "decode_tok_per_s": requests_in_flight * new_tokens / decode_s if decode_s > 0 else None,
+        "decode_ms_per_request": decode_s * 1e3,
+        "requests_per_s": requests_in_flight * 1e3 / ms_per_request,
+        "clocks": clocks,
+    }
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=200)
     ap.add_argument("--warmup", type=int, default=10)
     ap.add_argument("--impl", default="native", choices=["native", "reference"])
+    ap.add_argument("--workload", default="op", choices=["op", "dream7b_8k", "dream7b_32k"],
+                    help="op (default): BASELINE configs[1], the op-level decode attention; the others time whole requests")
     args = ap.parse_args()
 
     rank = int(os.environ.get("RANK", "0"))
@@ -330,7 +427,7 @@ def main():
         torch.cuda.set_device(local_rank)
         torch.distributed.init_process_group("nccl", device_id=torch.device("cuda", local_rank))
     try:
-        line = run_native(args, rank, world, local_rank)
+        line = run_native(args, rank, world, local_rank) if args.workload == "op" else run_request(args, rank, world, local_rank)
         if line is not None:
             print(json.dumps(line), flush=True)
     finally:

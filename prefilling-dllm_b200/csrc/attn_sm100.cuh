@@ -866,6 +866,21 @@ inline Plan make_plan(const pdllm_attn_params* p) {
       if (pl.first_permille > 950) pl.first_permille = 950;
     }
   }
+  if (splits <= 0 && 2 * base_ctas <= sms) {
+    // Few units (the decode shape: one block of rows per request): everything fits in one wave, so more splits shorten
+    // every CTA but lengthen the merge, which one CTA per tile pair runs over S partials. In key-tile times:
+    // cost(S) = ovh + ceil(T / S) + merge * S with ovh ~ 2.3 and merge ~ 0.35 per partial (measured).
+    const int T = max_key_tiles - 1;
+    int64_t s_max = sms / base_ctas;
+    if (s_max > 32) s_max = 32;
+    if (s_max > T) s_max = T > 0 ? T : 1;
+    double best = 1e30;
+    splits = 1;
+    for (int s = 1; s <= s_max; ++s) {
+      const double cost = 2.3 + (T + s - 1) / s + (s > 1 ? 0.35 * s : 0.0);
+      if (cost < best - 1e-9) { best = cost; splits = s; }
+    }
+  }
   if (splits <= 0) {
     // One CTA per SM: fill a whole number of waves; each split keeps at least two key tiles.
     const int64_t slots = sm_count();
