@@ -72,6 +72,7 @@ struct Args {
   int num_seqs, max_pages, num_q_heads, num_kv_heads, group, tpt, q_tiles, q_pairs, num_splits;
   int first_permille;  // uneven two-way split: share (in 1/1000) of a unit's key tiles that split 0 takes; 0 = even splits
   int base_ctas;       // (sequence, KV head, query-tile pair) units; blockIdx = split * base_ctas + unit
+  int fused_merge;     // 1: the last CTA of a tile pair merges the splits; 0: attn_combine_kernel does, after this kernel
   int page_size, has_cache, mask_mode, bidirectional, block_m, is_bf16;
   float scale_log2;  // sm_scale * log2(e)
 };
@@ -420,7 +421,7 @@ attn_sm100_kernel(const __grid_constant__ CUtensorMap q_map, const __grid_consta
       a.part_ml[(unit * 2 + 0) * kTileM + r] = -INFINITY;
       a.part_ml[(unit * 2 + 1) * kTileM + r] = 0.f;
     }
-    if (a.num_splits > 1) {
+    if (a.num_splits > 1 && a.fused_merge) {
       __threadfence();
       __syncthreads();
       finish_split(a, seq, kvh, pair, q_start, tokA, n_tokA, tokB, n_tokB);
@@ -768,13 +769,74 @@ attn_sm100_kernel(const __grid_constant__ CUtensorMap q_map, const __grid_consta
 
   // ---- teardown ----
   tc_fence_before();
-  if (a.num_splits > 1) __threadfence();   // this CTA's partials are visible before it counts itself in
+  if (a.num_splits > 1 && a.fused_merge) __threadfence();   // this CTA's partials are visible before it counts itself in
   __syncthreads();
   if (warp == kProducerWarp) {
     tc_fence_after();
     tmem_dealloc(tmem_base, kTmemCols);
   }
-  if (a.num_splits > 1) finish_split(a, seq, kvh, pair, q_start, tokA, n_tokA, tokB, n_tokB);
+  if (a.num_splits > 1 && a.fused_merge) finish_split(a, seq, kvh, pair, q_start, tokA, n_tokA, tokB, n_tokB);
+}
+
+// Stand-alone merge for shapes with few (sequence, KV head, tile pair) units and many splits (a single block of
+// decode rows): there the fused merge would pull S partial tiles through ONE SM per unit, while this grid spreads the
+// same reads over (query tiles x 8 column slabs) CTAs. Thread r owns tile row r and 16 columns; 64 loads in flight.
+constexpr int kCombineCols = 16;
+__global__ void __launch_bounds__(kTileM) attn_combine_kernel(const Args a) {
+  const int64_t tile = blockIdx.x / (kHeadDim / kCombineCols);  // (seq, kvh, qt)
+  const int d0 = static_cast<int>(blockIdx.x % (kHeadDim / kCombineCols)) * kCombineCols;
+  int u = static_cast<int>(tile);
+  const int qt = u % a.q_tiles; u /= a.q_tiles;
+  const int kvh = u % a.num_kv_heads;
+  const int seq = u / a.num_kv_heads;
+  const int q_start = a.cu_seqlens_q[seq];
+  const int q_len = a.cu_seqlens_q[seq + 1] - q_start;
+  const int tok0 = qt * a.tpt;
+  const int n_tok = min(a.tpt, q_len - tok0);
+  const int r = threadIdx.x;
+  const int tok_local = r / a.group;
+  if (n_tok <= 0 || tok_local >= n_tok) return;
+  const int head_local = r - tok_local * a.group;
+  const int64_t unit0 = tile * a.num_splits;
+  const int S = a.num_splits;
+  float M = -INFINITY;
+  for (int s = 0; s < S; ++s) M = fmaxf(M, a.part_ml[((unit0 + s) * 2 + 0) * kTileM + r]);
+  float wsum = 0.f;
+  for (int s = 0; s < S; ++s) {
+    const float ms = a.part_ml[((unit0 + s) * 2 + 0) * kTileM + r];
+    if (ms > -INFINITY) wsum += exp2f(ms - M) * a.part_ml[((unit0 + s) * 2 + 1) * kTileM + r];
+  }
+  const float inv = wsum > 0.f ? 1.f / wsum : 0.f;
+  float acc[kCombineCols];
+#pragma unroll
+  for (int j = 0; j < kCombineCols; ++j) acc[j] = 0.f;
+#pragma unroll 4
+  for (int s = 0; s < S; ++s) {
+    const float ms = a.part_ml[((unit0 + s) * 2 + 0) * kTileM + r];
+    const float ws = ms == -INFINITY ? 0.f : exp2f(ms - M);   // a neutral partial has no O data behind it
+    const float* po = a.part_o + (unit0 + s) * kHeadDim * kTileM + static_cast<int64_t>(d0) * kTileM + r;
+    float v[kCombineCols];
+#pragma unroll
+    for (int j = 0; j < kCombineCols; ++j) v[j] = ws != 0.f ? po[j * kTileM] : 0.f;
+#pragma unroll
+    for (int j = 0; j < kCombineCols; ++j) acc[j] = fmaf(ws, v[j], acc[j]);
+  }
+  uint32_t packed[kCombineCols / 2];
+#pragma unroll
+  for (int j = 0; j < kCombineCols; j += 2) {
+    if (a.is_bf16) {
+      __nv_bfloat162 h = __floats2bfloat162_rn(acc[j] * inv, acc[j + 1] * inv);
+      packed[j >> 1] = *reinterpret_cast<uint32_t*>(&h);
+    } else {
+      __half2 h = __floats2half2_rn(acc[j] * inv, acc[j + 1] * inv);
+      packed[j >> 1] = *reinterpret_cast<uint32_t*>(&h);
+    }
+  }
+  uint8_t* out_row = reinterpret_cast<uint8_t*>(a.out) +
+                     ((static_cast<int64_t>(q_start + tok0 + tok_local)) * a.out_stride + static_cast<int64_t>(kvh * a.group + head_local) * kHeadDim) * 2;
+  uint4* dst = reinterpret_cast<uint4*>(out_row + d0 * 2);
+  dst[0] = make_uint4(packed[0], packed[1], packed[2], packed[3]);
+  dst[1] = make_uint4(packed[4], packed[5], packed[6], packed[7]);
 }
 
 // ---- host side: tensor maps, split choice, launch ---------------------------------------------------------
@@ -831,6 +893,7 @@ inline bool supported(const pdllm_attn_params* p, const char** why) {
 struct Plan {
   int group, tpt, q_tiles, q_pairs, num_splits;
   int first_permille;  // see Args
+  int fused_merge;     // see Args
   int64_t tiles;  // query tiles = split-KV partial groups
   int64_t ctas;   // CTAs launched: pairs of query tiles x splits
 };
@@ -866,19 +929,23 @@ inline Plan make_plan(const pdllm_attn_params* p) {
       if (pl.first_permille > 950) pl.first_permille = 950;
     }
   }
-  if (splits <= 0 && 2 * base_ctas <= sms) {
-    // Few units (the decode shape: one block of rows per request): everything fits in one wave, so more splits shorten
-    // every CTA but lengthen the merge, which one CTA per tile pair runs over S partials. In key-tile times:
-    // cost(S) = ovh + ceil(T / S) + merge * S with ovh ~ 2.3 and merge ~ 0.35 per partial (measured).
-    const int T = max_key_tiles - 1;
-    int64_t s_max = sms / base_ctas;
-    if (s_max > 32) s_max = 32;
-    if (s_max > T) s_max = T > 0 ? T : 1;
-    double best = 1e30;
-    splits = 1;
-    for (int s = 1; s <= s_max; ++s) {
-      const double cost = 2.3 + (T + s - 1) / s + (s > 1 ? 0.35 * s : 0.0);
-      if (cost < best - 1e-9) { best = cost; splits = s; }
+  pl.fused_merge = 1;
+  if (2 * base_ctas <= sms) {
+    // Few units (the decode shape: one block of rows per request): everything fits in one wave, and the merge of S
+    // partial tiles per unit is better spread over a grid of its own than pulled through the one SM that finishes
+    // last. In key-tile times: cost(S) = ovh + ceil(T / S) + launch + traffic * S, ovh ~ 2.3, launch ~ 1, traffic ~ 0.03.
+    pl.fused_merge = 0;
+    if (splits <= 0) {
+      const int T = max_key_tiles - 1;
+      int64_t s_max = sms / base_ctas;
+      if (s_max > 32) s_max = 32;
+      if (s_max > T) s_max = T > 0 ? T : 1;
+      double best = 2.3 + T;
+      splits = 1;
+      for (int s = 2; s <= s_max; ++s) {
+        const double cost = 2.3 + (T + s - 1) / s + 1.0 + 0.03 * s;
+        if (cost < best - 1e-9) { best = cost; splits = s; }
+      }
     }
   }
   if (splits <= 0) {
@@ -967,7 +1034,7 @@ inline int launch(const pdllm_attn_params* p, cudaStream_t stream) {
   a.split_arrivals = reinterpret_cast<int*>(p->workspace);
   a.part_o = p->workspace ? reinterpret_cast<float*>(static_cast<char*>(p->workspace) + counter_bytes(pairs)) : nullptr;
   a.part_ml = a.part_o ? a.part_o + pl.tiles * pl.num_splits * static_cast<int64_t>(kHeadDim) * kTileM : nullptr;
-  if (pl.num_splits > 1 && !(p->workspace_zeroed && pairs * 4 <= kCounterHeaderBytes)) {
+  if (pl.num_splits > 1 && pl.fused_merge && !(p->workspace_zeroed && pairs * 4 <= kCounterHeaderBytes)) {
     // The kernel leaves every counter at zero again, so a caller that zero-filled its workspace once (and again after
     // any launch that reported a wait time-out) can say so and save this memset node on every call.
     cudaError_t e = cudaMemsetAsync(a.split_arrivals, 0, static_cast<size_t>(pairs) * 4, stream);
@@ -979,6 +1046,7 @@ inline int launch(const pdllm_attn_params* p, cudaStream_t stream) {
   a.group = pl.group; a.tpt = pl.tpt; a.q_tiles = pl.q_tiles; a.q_pairs = pl.q_pairs; a.num_splits = pl.num_splits;
   a.first_permille = pl.num_splits == 2 ? pl.first_permille : 0;
   a.base_ctas = static_cast<int>(pl.ctas / pl.num_splits);
+  a.fused_merge = pl.fused_merge;
   a.page_size = p->page_size > 0 ? p->page_size : kTileN; a.has_cache = has_cache ? 1 : 0;
   a.mask_mode = p->mask_mode; a.bidirectional = p->bidirectional;
   a.block_m = 2 * (p->diffusion_blk > 0 ? p->diffusion_blk : 32);
@@ -1001,6 +1069,10 @@ inline int launch(const pdllm_attn_params* p, cudaStream_t stream) {
 
   attn_sm100_kernel<<<static_cast<unsigned>(pl.ctas), kThreads, kSmemBytes, stream>>>(q_map, kn_map, vn_map, kc_map, vc_map, a);
   if ((rc = check_launch("attn_sm100_kernel")) != 0) return rc;
+  if (pl.num_splits > 1 && !pl.fused_merge) {
+    attn_combine_kernel<<<static_cast<unsigned>(pl.tiles * (kHeadDim / kCombineCols)), kTileM, 0, stream>>>(a);
+    if ((rc = check_launch("attn_combine_kernel")) != 0) return rc;
+  }
   return 0;
 }
 
