@@ -247,6 +247,17 @@ int pdllm_gather_pages(const void* cache, const int32_t* page_ids, int64_t n_tok
 int pdllm_scatter_pages(const void* src, const int32_t* page_ids, int64_t n_tokens, int page_size,
                         int64_t row_elems, int elem_bytes, int64_t num_pages, void* cache,
                         int32_t* status, void* stream);
+/* pool -> pool: for each of n_lists page lists (one per layer and K/V plane, `ceil(tokens_per_list / page_size)` ids
+ * each, concatenated) copy the first tokens_per_list tokens of the src pages into the dst pages. src_cache may be the
+ * pool of ANOTHER GPU mapped by peer access (pdllm_enable_peer_access): the kernel, launched on the destination GPU,
+ * then reads it across NVLink with plain loads — no staging copy. Both id lists are read by the kernel on the
+ * launching device. Replaces the per-layer gather / .to() / scatter of make_pd_record_from_remote_engine
+ *   prefilling_dllm_engine/prefilling_dllm/fastdllm_engine.py:845-859 */
+int pdllm_copy_pages(const void* src_cache, const int32_t* src_page_ids, void* dst_cache, const int32_t* dst_page_ids,
+                     int64_t n_lists, int64_t tokens_per_list, int page_size, int64_t row_elems, int elem_bytes,
+                     int64_t src_num_pages, int64_t dst_num_pages, int32_t* status, void* stream);
+/* map peer_device's memory into device's address space (idempotent); PDLLM_E_UNSUPPORTED if the GPUs have no peer path */
+int pdllm_enable_peer_access(int device, int peer_device);
 /* per-(KV head) compaction: dst token j of head h := src token keep[h, j]; src and dst page lists may be the
  * same pages (in-place compaction to the front): the kernel stages through `staging`
  * ([keep_count, Hkv, D] elements) so overlapping ranges are safe. */

@@ -91,6 +91,8 @@ _SIGNATURES = {
                                    c_void_p, c_void_p]),
     "pdllm_gather_pages": (c_int, [c_void_p, c_void_p, c_int64, c_int, c_int64, c_int, c_int64, c_void_p, c_void_p, c_void_p]),
     "pdllm_scatter_pages": (c_int, [c_void_p, c_void_p, c_int64, c_int, c_int64, c_int, c_int64, c_void_p, c_void_p, c_void_p]),
+    "pdllm_copy_pages": (c_int, [c_void_p, c_void_p, c_void_p, c_void_p, c_int64, c_int64, c_int, c_int64, c_int, c_int64, c_int64, c_void_p, c_void_p]),
+    "pdllm_enable_peer_access": (c_int, [c_int, c_int]),
     "pdllm_compact_pages_per_head": (c_int, [c_void_p, c_void_p, c_void_p, c_void_p, c_int64, c_int64, c_int64, c_int, c_int,
                                              c_int, c_int, c_int64, c_void_p, c_void_p, c_void_p]),
     "pdllm_add_rmsnorm": (c_int, [c_void_p, c_void_p, c_void_p, c_void_p, c_int64, c_int, c_int64, c_int64, c_int64, c_float, c_int, c_void_p]),

@@ -150,6 +150,34 @@ __global__ void page_copy_kernel(const uint4* __restrict__ src, uint4* __restric
   }
 }
 
+// ---- pool -> pool ------------------------------------------------------------------------------------
+// dst pages := src pages, token by token, for the first n_tokens of the two page lists. The source pool may be another
+// GPU's memory mapped through peer access: the loads then cross NVLink directly (plain 16-byte loads, no staging
+// buffer, no TMA), which is the prefill -> decode hand-off of the KV of a request.
+__global__ void page_to_page_kernel(const uint4* __restrict__ src, const int32_t* __restrict__ src_pages,
+                                    uint4* __restrict__ dst, const int32_t* __restrict__ dst_pages, int64_t n_tokens,
+                                    int tokens_per_list, int page_size, int segs_per_row, int64_t src_num_pages,
+                                    int64_t dst_num_pages, int32_t* status) {
+  // the lists hold `tokens_per_list` tokens each (one list per layer and K/V plane, concatenated)
+  int64_t idx = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+  const int64_t total = n_tokens * segs_per_row;
+  const int pages_per_list = (tokens_per_list + page_size - 1) / page_size;
+  for (; idx < total; idx += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    const int64_t tok = idx / segs_per_row;
+    const int seg = static_cast<int>(idx - tok * segs_per_row);
+    const int64_t list = tok / tokens_per_list;
+    const int64_t t = tok - list * tokens_per_list;
+    const int64_t entry = list * pages_per_list + t / page_size;
+    const int64_t sp = src_pages[entry], dp = dst_pages[entry];
+    if (sp < 0 || sp >= src_num_pages || dp < 0 || dp >= dst_num_pages) {
+      if (seg == 0) report_status(status, PDLLM_S_BAD_PAGE);
+      continue;
+    }
+    const int64_t off = t % page_size;
+    dst[(dp * page_size + off) * segs_per_row + seg] = src[(sp * page_size + off) * segs_per_row + seg];
+  }
+}
+
 // ---- per-head compaction -----------------------------------------------------------------------------
 // Phase A: staging[j, h, :] = cache[src token keep[h, j], h, :]; phase B: cache[dst token dst_start + j, h, :] =
 // staging[j, h, :]. Two launches, so an in-place compaction (dst range overlapping src range) never reads a

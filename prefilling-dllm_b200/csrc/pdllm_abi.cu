@@ -430,6 +430,39 @@ int pdllm_rope_pages(void* k_cache, const int32_t* page_ids, int64_t start, int6
   return check_launch("rope_pages");
 }
 
+int pdllm_copy_pages(const void* src_cache, const int32_t* src_page_ids, void* dst_cache, const int32_t* dst_page_ids,
+                     int64_t n_lists, int64_t tokens_per_list, int page_size, int64_t row_elems, int elem_bytes,
+                     int64_t src_num_pages, int64_t dst_num_pages, int32_t* status, void* stream) {
+  if (n_lists < 0 || tokens_per_list < 0 || page_size <= 0 || row_elems <= 0) return fail(PDLLM_E_INVALID, "copy_pages: bad sizes");
+  if (n_lists == 0 || tokens_per_list == 0) return 0;
+  if (!src_cache || !dst_cache || !src_page_ids || !dst_page_ids) return fail(PDLLM_E_INVALID, "copy_pages: null pointer");
+  if (tokens_per_list >= (1ll << 31)) return fail(PDLLM_E_INVALID, "copy_pages: list too long");
+  const int64_t row_bytes = row_elems * elem_bytes;
+  if (row_bytes % 16 != 0 || !aligned16(src_cache) || !aligned16(dst_cache)) return fail(PDLLM_E_UNSUPPORTED, "copy_pages: rows must be 16-byte multiples");
+  const int segs = static_cast<int>(row_bytes / 16);
+  const int64_t n_tokens = n_lists * tokens_per_list;
+  page_to_page_kernel<<<grid_for(n_tokens * segs, 256), 256, 0, as_stream(stream)>>>(
+      static_cast<const uint4*>(src_cache), src_page_ids, static_cast<uint4*>(dst_cache), dst_page_ids, n_tokens,
+      static_cast<int>(tokens_per_list), page_size, segs, src_num_pages, dst_num_pages, status);
+  return check_launch("copy_pages");
+}
+
+int pdllm_enable_peer_access(int device, int peer_device) {
+  if (device == peer_device) return 0;
+  int can = 0;
+  cudaError_t e = cudaDeviceCanAccessPeer(&can, device, peer_device);
+  if (e != cudaSuccess) return fail(static_cast<int>(e), "cudaDeviceCanAccessPeer: %s", cudaGetErrorString(e));
+  if (!can) return fail(PDLLM_E_UNSUPPORTED, "device %d cannot map the memory of device %d", device, peer_device);
+  int prev = 0;
+  cudaGetDevice(&prev);
+  cudaSetDevice(device);
+  e = cudaDeviceEnablePeerAccess(peer_device, 0);
+  cudaSetDevice(prev);
+  if (e == cudaErrorPeerAccessAlreadyEnabled) { cudaGetLastError(); return 0; }
+  if (e != cudaSuccess) return fail(static_cast<int>(e), "cudaDeviceEnablePeerAccess: %s", cudaGetErrorString(e));
+  return 0;
+}
+
 int pdllm_compact_pages_per_head(void* cache, const int32_t* src_page_ids, const int32_t* dst_page_ids,
                                  const int64_t* keep, int64_t keep_count, int64_t src_tokens,
                                  int64_t dst_start, int page_size, int num_kv_heads, int head_dim,

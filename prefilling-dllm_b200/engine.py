@@ -34,6 +34,18 @@ from .model import CachedPrefix, DreamArch, PageAllocator, PagedDreamModel, slot
 _OFF = {"none", "off", "0", ""}
 
 
+def _on_device(method):
+    """Run an engine method with the engine's GPU as the current CUDA device (kernels launch on the current device)."""
+    import functools
+
+    @functools.wraps(method)
+    def wrapper(self, *args, **kwargs):
+        with torch.cuda.device(self.device):
+            return method(self, *args, **kwargs)
+
+    return wrapper
+
+
 @dataclass
 class FastDLLMEngineOutput:
     text: str
@@ -308,6 +320,7 @@ class FastDLLMDreamEngine:
             ids = self._all_layer_page_ids(list(prompt_page_ids)[:n_pages])
             ops.scatter_pages(staged.view(-1, expected[1], expected[2]), self._layer_pools(), ids)
 
+    @_on_device
     def snapshot_pd_record_kv(self, record: DreamPrefillRecord, *, device="cpu") -> DreamKVSnapshot:
         """Copy the prompt KV a record refers to into fresh tensors on `device` (reference :700-726)."""
         target = torch.device(device)
@@ -348,6 +361,7 @@ class FastDLLMDreamEngine:
             first_token_id=source.first_token_id, last_context_logit=last_context_logit, decode_delta_state=decode_delta_state,
             owns_prompt_pages=True, cached_prefix=None, kv_mode=source.kv_mode)
 
+    @_on_device
     def make_pd_record_from_kv_snapshot(self, source: DreamPrefillRecord, snapshot: DreamKVSnapshot) -> DreamPrefillRecord:
         """Allocate local pages, load a snapshot into them, return a decode-ready record (reference :728-781)."""
         if snapshot.page_size != self.page_size:
@@ -367,12 +381,15 @@ class FastDLLMDreamEngine:
             last = last.to(device=self.device).contiguous()
         return self._record_like(source, prompt_pages, block_pages, last, source.decode_delta_state)
 
+    @_on_device
     def make_pd_record_from_remote_engine(self, source_engine: "FastDLLMDreamEngine", source: DreamPrefillRecord, *,
                                           non_blocking: bool = True) -> DreamPrefillRecord:
         """Copy prompt KV from another engine's pool (same or another GPU) into this one (reference :800-881).
 
-        One gather on the source GPU, one device-to-device copy of the whole payload (NVLink peer copy between GPUs),
-        one scatter here — instead of 2 x layers gathers, copies and scatters."""
+        ONE kernel on this GPU reads the source pages of every layer through peer access (across NVLink when the engines
+        sit on different GPUs) and writes them into the freshly allocated local pages — no staging buffer, instead of
+        2 x layers gathers, copies and scatters. `non_blocking` is accepted for signature parity: the copy is always
+        asynchronous on this device's current stream, ordered after the source device's current stream."""
         if self.page_size != source_engine.page_size:
             raise ValueError(f"remote-engine PD page_size mismatch: source={source_engine.page_size}, target={self.page_size}")
         src_kv, dst_kv = source_engine.model.kv_cache, self.model.kv_cache
@@ -382,13 +399,18 @@ class FastDLLMDreamEngine:
         prompt_pages, block_pages = self._allocate_prompt_and_block_pages(prompt_len, source.decode_len)
         try:
             if prompt_len > 0:
-                dense = source_engine._gather_prompt_pages_all_layers(source.prompt_page_ids, prompt_len)
-                if dense.device != self.device or dense.dtype != dst_kv.dtype:
-                    dense = dense.to(device=self.device, dtype=dst_kv.dtype, non_blocking=non_blocking)
                 n_pages = math.ceil(prompt_len / self.page_size)
-                with torch.cuda.device(self.device):
-                    ops.scatter_pages(dense.view(-1, dst_kv.shape[4], dst_kv.shape[5]), self._layer_pools(),
-                                      self._all_layer_page_ids(prompt_pages[:n_pages]))
+                planes = 2 * int(dst_kv.shape[1])
+                src_ids = source_engine._all_layer_page_ids(source.prompt_page_ids[:n_pages]).to(self.device)
+                dst_ids = self._all_layer_page_ids(prompt_pages[:n_pages])
+                if src_kv.dtype != dst_kv.dtype:
+                    raise ValueError(f"remote-engine PD dtype mismatch: source={src_kv.dtype}, target={dst_kv.dtype}")
+                # the source must have finished writing these pages before this GPU reads them
+                if source_engine.device != self.device:
+                    done = torch.cuda.Event()
+                    done.record(torch.cuda.current_stream(source_engine.device))
+                    torch.cuda.current_stream(self.device).wait_event(done)
+                ops.copy_pages(source_engine._layer_pools(), src_ids, self._layer_pools(), dst_ids, n_lists=planes, tokens_per_list=prompt_len)
         except BaseException:
             self._prefix_cache.release_pages(prompt_pages + block_pages)
             raise
@@ -424,6 +446,7 @@ class FastDLLMDreamEngine:
         if delta not in _OFF and has_keep:
             raise ValueError(f"Unsupported decode_delta_mode: {delta}")
 
+    @_on_device
     @torch.inference_mode()
     def prefill_to_pd_record(self, prompt_ids: Sequence[int], *, max_new_tokens: int, prompt_positions: Optional[Sequence[int]] = None,
                              active_prompt_positions: Optional[Sequence[int]] = None,
@@ -574,6 +597,7 @@ class FastDLLMDreamEngine:
                 text = text.split(eos)[0]
         return FastDLLMEngineOutput(text=text, token_ids=generated, n_diff_steps=n_steps)
 
+    @_on_device
     @torch.inference_mode()
     def decode_from_pd_record(self, record: DreamPrefillRecord, *, max_new_tokens: int,
                               stop_token_ids: Optional[Iterable[int]] = None) -> FastDLLMEngineOutput:
@@ -652,6 +676,7 @@ class FastDLLMDreamEngine:
         ids = [int(x) for x in query_ids]
         return ids[-int(window):] if window and window > 0 else ids
 
+    @_on_device
     @torch.inference_mode()
     def generate_partial_draft_rounds_for_selection(self, prompt_ids: Sequence[int], *, max_new_tokens: int,
                                                     partial_rounds: int) -> Tuple[List[int], List[bool]]:
@@ -724,6 +749,7 @@ class FastDLLMDreamEngine:
             return None
         return positions, labels
 
+    @_on_device
     @torch.inference_mode()
     def score_chunk_self_information_engine(self, prefix_ids, chunk_ids, query_ids, *, score_token_count: Optional[int] = None,
                                             score_token_mask: Optional[Sequence[bool]] = None, score_attention_mask: str = "causal") -> float:
@@ -743,6 +769,7 @@ class FastDLLMDreamEngine:
             score = float(ops.self_information_scores(logits, self.model.ids_tensor(labels), 1)[0].item())
         return score if math.isfinite(score) else float("-inf")
 
+    @_on_device
     @torch.inference_mode()
     def select_chunks_by_engine(self, prefix_ids, candidate_chunks, scoring_query_ids, *, topk_chunks: int,
                                 score_mode: str = "draft_self_information", score_draft_tokens: int = 4,
@@ -812,6 +839,7 @@ class FastDLLMDreamEngine:
         return scores
 
     # ------------------------------------------------------------------------------------------------ token eviction
+    @_on_device
     @torch.inference_mode()
     def compute_prompt_keep_indices_per_layer_per_head(self, *, full_prompt_len: int, prefix_ids, chunk_spans, query_ids, token_capacity: int,
                                                        token_score_query_window: int = 8, token_score_layers: int = 1,
@@ -899,6 +927,7 @@ class FastDLLMDreamEngine:
         return prompt_keep, chunk_meta
 
     # ------------------------------------------------------------------------------------------------ chunk-local KV
+    @_on_device
     @torch.inference_mode()
     def generate_token_ids_from_chunk_local_kv(self, *, prefix_ids, prefix_positions, chunk_ids_list, chunk_positions_list,
                                                chunk_keep_indices_per_layer_per_head, query_ids, query_positions,

@@ -448,7 +448,9 @@ class BlockStepRunner:
             else:
                 if e.graph is None:
                     graph = torch.cuda.CUDAGraph()
-                    with torch.cuda.graph(graph):
+                    # torch keeps ONE default capture stream per process, created on whichever device captured first:
+                    # with engines on several GPUs in one process the capture stream has to be this device's own
+                    with torch.cuda.graph(graph, stream=torch.cuda.Stream(device=self.m.device)):
                         e.counts = self._step()
                     e.graph = graph                  # capturing records the launches without running them
                 e.graph.replay()

@@ -599,3 +599,31 @@ def silu_mul(gate_up: torch.Tensor) -> torch.Tensor:
     check(_lib.load().pdllm_silu_mul(gate_up.data_ptr(), out.data_ptr(), gate_up.shape[0], inter, gate_up.stride(0), out.stride(0),
                                      dtype_code(gate_up.dtype), _stream(device)))
     return out
+
+
+
+def copy_pages(src_cache: torch.Tensor, src_page_ids: torch.Tensor, dst_cache: torch.Tensor, dst_page_ids: torch.Tensor, *,
+               n_lists: int, tokens_per_list: int) -> None:
+    """Pool to pool copy of `n_lists` page lists (`tokens_per_list` tokens each); `src_cache` may live on another GPU.
+
+    Launched on the device of `dst_cache`; both id tensors (int32) must be on that device. When the pools are on
+    different GPUs the source is read through peer access, straight across NVLink."""
+    device = _require_cuda(dst_cache, src_page_ids, dst_page_ids)
+    if not src_cache.is_cuda:
+        raise ValueError("pdllm_b200 ops require CUDA tensors (there is no CPU path)")
+    if src_cache.dim() != 4 or dst_cache.dim() != 4 or src_cache.shape[1:] != dst_cache.shape[1:] or src_cache.dtype != dst_cache.dtype:
+        raise ValueError("pools must be unified [pages, page_size, Hkv, D] of one shape per page and one dtype")
+    if src_page_ids.dtype != torch.int32 or dst_page_ids.dtype != torch.int32 or src_page_ids.numel() != dst_page_ids.numel():
+        raise ValueError("page id lists must be int32 and of equal length")
+    _, page_size, hkv, d = dst_cache.shape
+    per_list = -(-int(tokens_per_list) // page_size)
+    if src_page_ids.numel() != int(n_lists) * per_list:
+        raise ValueError(f"expected {int(n_lists) * per_list} page ids, got {src_page_ids.numel()}")
+    lib = _lib.load()
+    if src_cache.device != device:
+        check(lib.pdllm_enable_peer_access(device.index, src_cache.device.index))
+    with torch.cuda.device(device):
+        check(lib.pdllm_copy_pages(src_cache.data_ptr(), src_page_ids.contiguous().data_ptr(), dst_cache.data_ptr(),
+                                   dst_page_ids.contiguous().data_ptr(), int(n_lists), int(tokens_per_list), page_size, hkv * d,
+                                   dst_cache.element_size(), src_cache.shape[0], dst_cache.shape[0], status_word(device).data_ptr(),
+                                   _stream(device)))

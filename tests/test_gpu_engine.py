@@ -246,3 +246,24 @@ def test_chunk_local_kv_generate(engine, cpu_model):
     assert engine._prefix_cache.num_free_pages == free0
     with pytest.raises(ValueError, match="keep-indices list length mismatch"):
         engine.generate_token_ids_from_chunk_local_kv(chunk_keep_indices_per_layer_per_head=nested[:1], max_new_tokens=BLOCK, **kw)
+
+
+@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs two GPUs")
+def test_engine_to_engine_copy_across_gpus(engine, ckpt):
+    """Prefill on GPU 0, hand the prompt KV to an engine on GPU 1 with ONE kernel that reads GPU 0's pages through peer
+    access, decode there: same KV bits, same ids as decoding where the prefill ran."""
+    other = _engine(ckpt, pages=16, device_start=1)
+    prompt = _prompt(700, seed=11)
+    rec = engine.prefill_to_pd_record(prompt, max_new_tokens=BLOCK)
+    remote = other.make_pd_record_from_remote_engine(engine, rec)
+    assert remote.last_context_logit.device == torch.device("cuda", 1) and remote.owns_prompt_pages
+    a, b = engine.snapshot_pd_record_kv(rec), other.snapshot_pd_record_kv(remote)
+    for layer in range(2):
+        assert torch.equal(a.k_by_layer[layer], b.k_by_layer[layer]) and torch.equal(a.v_by_layer[layer], b.v_by_layer[layer])
+    ids = engine.decode_from_pd_record(rec, max_new_tokens=BLOCK).token_ids
+    assert other.decode_from_pd_record(remote, max_new_tokens=BLOCK).token_ids == ids
+    from prefilling_dllm_b200 import ops
+
+    ops.check_status(torch.device("cuda", 1))
+    assert other._prefix_cache.num_free_pages == 16
+    engine._prefix_cache.evict_one()
