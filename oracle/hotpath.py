@@ -18,7 +18,7 @@ parity of the model arithmetic itself is therefore "unpinned" against Fast-dLLM 
 from __future__ import annotations
 
 import math
-from typing import Dict, List, Optional, Sequence, Tuple
+from typing import List, Optional, Sequence, Tuple
 
 import torch
 import torch.nn.functional as F

@@ -13,7 +13,6 @@ written with.
 from __future__ import annotations
 
 import json
-import math
 import os
 import threading
 from collections import deque

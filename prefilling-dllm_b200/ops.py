@@ -92,6 +92,13 @@ def check_status(device: Optional[torch.device] = None, *, reset: bool = True) -
 
 
 def _workspace(device: torch.device, key: str, nbytes: int, *, zero: bool = False) -> torch.Tensor:
+    if torch.cuda.is_current_stream_capturing():
+        # A captured launch keeps the pointer it was given. The grow-only buffers below are replaced when a larger shape
+        # comes along, which would leave a graph writing into freed memory: scratch of a captured launch is allocated
+        # inside the capture instead, so it belongs to the graph's own memory pool and lives exactly as long as the graph
+        # (a zero-filled one becomes a memset node that runs on every replay).
+        alloc = max(int(nbytes), 256)
+        return torch.zeros(alloc, dtype=torch.uint8, device=device) if zero else torch.empty(alloc, dtype=torch.uint8, device=device)
     buf = _state.workspaces.get((device, key))
     if buf is None or buf.numel() < nbytes:
         alloc = max(int(nbytes), 256)
