@@ -98,6 +98,17 @@ def test_dataclasses_match_the_reference_field_for_field():
     with open(os.path.join(os.path.dirname(os.path.abspath(__file__)), "golden", "config_defaults.json")) as handle:
         ref = json.load(handle)
     ours_only = {"FastDLLMParallelCompConfig": {"num_kv_pages", "decode_cuda_graph"}}
+    methods = ref.pop("FastDLLMParallelComp.methods")
+    functions = ref.pop("module_functions")
+    import inspect
+
+    for name, params in methods.items():      # public methods: same parameter names, kinds and defaults
+        fn = getattr(pc.FastDLLMParallelComp, name)
+        mine = [[p.name, p.kind == p.KEYWORD_ONLY, "<required>" if p.default is inspect.Parameter.empty else p.default]
+                for p in list(inspect.signature(fn).parameters.values())[1:]]
+        assert mine == params, name
+    for name, params in functions.items():
+        assert [p.name for p in inspect.signature(getattr(pc, name)).parameters.values()] == params, name
     for name, fields in ref.items():
         mine = {}
         for f in dataclasses.fields(getattr(pc, name)):
@@ -113,3 +124,38 @@ def test_dataclasses_match_the_reference_field_for_field():
     arch = DreamArch.dream_7b()
     assert arch.head_dim == 128 and arch.num_attention_heads // arch.num_key_value_heads == 7 and arch.logit_shift
     assert not DreamArch.llada_8b().logit_shift and not DreamArch.llada_8b().attention_bias
+
+
+def test_engine_facade_has_the_reference_api():
+    """tests/golden/engine_api.json: dataclass fields and method signatures of the reference engine, extracted from its
+    source by tests/golden/make_engine_api.py. Records must match field for field (name, order, default); every
+    reference parameter must be accepted under the same name with the same default."""
+    import dataclasses
+    import inspect
+    import json
+
+    from prefilling_dllm_b200 import engine as E
+
+    with open(os.path.join(os.path.dirname(os.path.abspath(__file__)), "golden", "engine_api.json")) as handle:
+        api = json.load(handle)
+    for name, fields in api["dataclasses"].items():
+        mine = [[f.name, f.default if f.default is not dataclasses.MISSING else "<required>"] for f in dataclasses.fields(getattr(E, name))]
+        assert mine == fields, name
+    for name, sig in api["methods"].items():
+        fn = getattr(E.FastDLLMDreamEngine, name)
+        params = list(inspect.signature(fn).parameters.values())[1:]
+        by_name = {p.name: p for p in params}
+        forwards = any(p.kind == p.VAR_KEYWORD for p in params)
+        n_req = len(sig["positional"]) - len(sig["positional_defaults"])
+        ref = [(n, "<required>" if i < n_req else sig["positional_defaults"][i - n_req], False) for i, n in enumerate(sig["positional"])]
+        ref += [(n, d, True) for n, d in sig["keyword_only"]]
+        for pname, default, kw_only in ref:
+            if pname not in by_name:
+                assert forwards, f"{name}: parameter {pname} is missing"
+                continue
+            p = by_name[pname]
+            assert (p.kind == p.KEYWORD_ONLY) == kw_only, f"{name}.{pname}: positional / keyword-only differs"
+            if default == "<required>":
+                assert p.default is inspect.Parameter.empty, f"{name}.{pname} must be required"
+            elif isinstance(default, (int, float, str, bool)) or default is None:
+                assert p.default == default, f"{name}.{pname}: default {p.default!r} != {default!r}"
