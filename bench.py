@@ -400,13 +400,88 @@ def run_request(args, rank: int, world: int, local_rank: int):
     }
 
 
+def run_step_breakdown(args, local_rank: int):
+    """Where one denoise step of Dream-7B (32 block rows against 4161 cached tokens, bf16) spends its time: each group
+    of launches captured in a CUDA graph of its own and replayed, CUDA-event timed. One GPU."""
+    import torch.nn.functional as F
+
+    from prefilling_dllm_b200 import ops
+    from prefilling_dllm_b200.model import DreamArch, PagedDreamModel
+
+    device = torch.device("cuda", local_rank)
+    torch.cuda.set_device(device)
+    arch = DreamArch.dream_7b()
+    m = PagedDreamModel.random_init(arch, device=device, dtype=torch.bfloat16, num_pages=64, page_size=256)
+    rows, ctx = 32, 4161
+    hq, hkv, d, hidden, inter = arch.num_attention_heads, arch.num_key_value_heads, arch.head_dim, arch.hidden_size, arch.intermediate_size
+    h = torch.randn(rows, hidden, device=device, dtype=torch.bfloat16)
+    hi = torch.randn(rows, inter, device=device, dtype=torch.bfloat16)
+    gu = torch.randn(rows, 2 * inter, device=device, dtype=torch.bfloat16)
+    qkv = torch.randn(rows, hq + 2 * hkv, d, device=device, dtype=torch.bfloat16)
+    cos, sin = m._rope_tables(torch.arange(rows, device=device) + ctx)
+    n_pages = -(-ctx // 256)
+    table = torch.arange(4 * -(-n_pages // 4), dtype=torch.int32, device=device).view(1, -1)
+    seq_lens = torch.tensor([ctx + rows], dtype=torch.int32, device=device)
+    cu = torch.tensor([0, rows], dtype=torch.int32, device=device)
+    out = torch.empty(rows, hq, d, device=device, dtype=torch.bfloat16)
+    kc, vc = m.layer_cache(0)
+    layers = arch.num_hidden_layers
+
+    def gemms():
+        for w in m.layers:
+            F.linear(h, w["wqkv"], w["bqkv"]); F.linear(h, w["wo"]); F.linear(h, w["wgu"]); F.linear(hi, w["wd"])
+        F.linear(h[:1], m.lm_head)
+
+    def row_ops():
+        for _ in range(layers):
+            ops.add_rmsnorm(h, m.layers[0]["ln1"], 1e-6, h)
+            ops.rope_inplace(qkv[:, : hq + hkv], cos.reshape(-1, d), sin.reshape(-1, d))
+            ops.add_rmsnorm(h, m.layers[0]["ln2"], 1e-6, h)
+            ops.silu_mul(gu)
+
+    def attention():
+        for _ in range(layers):
+            ops.paged_attention(qkv[:, :hq], qkv[:, hq:hq + hkv], qkv[:, hq + hkv:], out, cu_seqlens_q=cu, max_query_len=rows, key_cache=kc,
+                                value_cache=vc, block_table=table, seq_lens=seq_lens, max_seq_len=table.shape[1] * 256 + rows, sm_scale=d ** -0.5)
+
+    def timed(fn):
+        fn()
+        torch.cuda.synchronize(device)
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph, stream=torch.cuda.Stream(device=device)):
+            fn()
+        for _ in range(3):
+            graph.replay()
+        start, stop = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        start.record()
+        for _ in range(max(5, min(args.steps, 20))):
+            graph.replay()
+        stop.record()
+        torch.cuda.synchronize(device)
+        return start.elapsed_time(stop) / max(5, min(args.steps, 20))
+
+    t_gemm, t_rows, t_attn = timed(gemms), timed(row_ops), timed(attention)
+    ops.check_status(device)
+    weight_bytes = sum(w[k].numel() for w in m.layers for k in ("wqkv", "wo", "wgu", "wd")) * 2
+    kv_bytes = layers * (ctx * 2 * hkv * d * 2 + rows * (2 * hq + 2 * hkv) * d * 2)
+    peaks = load_peaks()
+    return {
+        "metric": "denoise_step_ms", "value": t_gemm + t_rows + t_attn, "unit": "ms", "n_gpus": 1, "higher_is_better": False,
+        "dtype": "bf16", "data": "synthetic",
+        "config": {"workload": "dream7b_step: one denoise step of Dream-7B, 32 block rows, 4161 cached tokens, groups replayed as CUDA graphs"},
+        "breakdown_ms": {"cublas_gemms": t_gemm, "row_ops_4_per_layer": t_rows, "attention_28_layers": t_attn},
+        "gemm_weight_gbs": weight_bytes / (t_gemm * 1e-3) / 1e9, "attention_kv_gbs": kv_bytes / (t_attn * 1e-3) / 1e9,
+        "hbm_peak_gbs": peaks["hbm"], "peak_source": peaks["source"],
+    }
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=200)
     ap.add_argument("--warmup", type=int, default=10)
     ap.add_argument("--impl", default="native", choices=["native", "reference"])
-    ap.add_argument("--workload", default="op", choices=["op", "dream7b_8k", "dream7b_32k"],
+    ap.add_argument("--workload", default="op", choices=["op", "dream7b_8k", "dream7b_32k", "dream7b_step"],
                     help="op (default): BASELINE configs[1], the op-level decode attention; the others time whole requests")
     args = ap.parse_args()
 
@@ -427,7 +502,12 @@ def main():
         torch.cuda.set_device(local_rank)
         torch.distributed.init_process_group("nccl", device_id=torch.device("cuda", local_rank))
     try:
-        line = run_native(args, rank, world, local_rank) if args.workload == "op" else run_request(args, rank, world, local_rank)
+        if args.workload == "op":
+            line = run_native(args, rank, world, local_rank)
+        elif args.workload == "dream7b_step":
+            line = run_step_breakdown(args, local_rank) if rank == 0 else None
+        else:
+            line = run_request(args, rank, world, local_rank)
         if line is not None:
             print(json.dumps(line), flush=True)
     finally:
