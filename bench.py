@@ -430,7 +430,7 @@ def run_step_breakdown(args, local_rank: int):
     def gemms():
         for w in m.layers:
             F.linear(h, w["wqkv"], w["bqkv"]); F.linear(h, w["wo"]); F.linear(h, w["wgu"]); F.linear(hi, w["wd"])
-        F.linear(h[:1], m.lm_head)
+        F.linear(h, m.lm_head)
 
     def row_ops():
         for _ in range(layers):
@@ -462,7 +462,7 @@ def run_step_breakdown(args, local_rank: int):
 
     t_gemm, t_rows, t_attn = timed(gemms), timed(row_ops), timed(attention)
     ops.check_status(device)
-    weight_bytes = sum(w[k].numel() for w in m.layers for k in ("wqkv", "wo", "wgu", "wd")) * 2
+    weight_bytes = (sum(w[k].numel() for w in m.layers for k in ("wqkv", "wo", "wgu", "wd")) + m.lm_head.numel()) * 2
     kv_bytes = layers * (ctx * 2 * hkv * d * 2 + rows * (2 * hq + 2 * hkv) * d * 2)
     peaks = load_peaks()
     return {
