@@ -400,6 +400,65 @@ def run_request(args, rank: int, world: int, local_rank: int):
     }
 
 
+def run_decode_batch(args, rank: int, world: int, local_rank: int):
+    """Decode throughput of the PD engine facade with `--concurrent` requests per GPU sharing every denoise step:
+    Dream-7B architecture (random init, bf16), each request a 4193-token prompt (what is left of an 8K prefix after
+    top-4 chunk selection, plus the query) prefilled into pages beforehand; timed: `decode_from_pd_records` of one
+    32-token block per request. Replicas over GPUs (every rank its own requests, no collective)."""
+    from prefilling_dllm_b200 import ops
+    from prefilling_dllm_b200.engine import FastDLLMDreamEngine
+    from prefilling_dllm_b200.model import DreamArch, PagedDreamModel
+
+    device = torch.device("cuda", local_rank)
+    torch.cuda.set_device(device)
+    n_req, prompt_len, block = max(1, args.concurrent), 4193, 32
+    pages_per_req = -(-prompt_len // 256) + 1
+    model = PagedDreamModel.random_init(DreamArch.dream_7b(), device=device, dtype=torch.bfloat16, num_pages=n_req * pages_per_req + 8, page_size=256)
+    engine = FastDLLMDreamEngine(model, max_model_len=8192, block_length=block, mask_token_id=151666, threshold=0.9, enforce_eager=False)
+    gen = torch.Generator().manual_seed(100 + rank)
+    prompts = [torch.randint(0, 151000, (prompt_len,), generator=gen).tolist() for _ in range(n_req)]
+
+    def one_round():
+        records = [engine.prefill_to_pd_record(p, max_new_tokens=block) for p in prompts]     # prefix-cache hits after the first round
+        torch.cuda.synchronize(device)
+        t0 = time.perf_counter()
+        outs = engine.decode_from_pd_records(records, max_new_tokens=block)
+        torch.cuda.synchronize(device)
+        return time.perf_counter() - t0, outs
+
+    steps, warmup = max(1, min(args.steps, 10)), max(3, min(args.warmup, 4))
+    for _ in range(warmup):
+        one_round()
+    ops.check_status(device)
+    sampler = ClockSampler(local_rank)
+    if rank == 0:
+        sampler.start()
+    if world > 1:
+        torch.distributed.barrier()
+    total, n_steps = 0.0, 0
+    for _ in range(steps):
+        dt, outs = one_round()
+        total += dt
+        n_steps = max(o.n_diff_steps for o in outs)
+    sec = torch.tensor([total / steps], device=device)
+    if world > 1:
+        torch.distributed.all_reduce(sec, op=torch.distributed.ReduceOp.MAX)
+    clocks = sampler.stop() if rank == 0 else None
+    ops.check_status(device)
+    if rank != 0:
+        return None
+    seconds = float(sec.item())
+    return {
+        "metric": "decode_tok_per_s", "value": world * n_req * block / seconds, "unit": "tok/s", "n_gpus": world, "steps": steps,
+        "warmup": warmup, "ms_per_step": seconds * 1e3, "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
+        "data": "synthetic",
+        "config": {"workload": f"dream7b_decode_batch: {n_req} concurrent requests per GPU, Dream-7B architecture random init, {prompt_len}-token "
+                               f"prompt in pages, one {block}-token block each, threshold 0.9, greedy; {n_steps} shared denoise steps per block",
+                   "parallelism": f"dp{world} (replicas over requests, no data-path collective)"},
+        "ms_per_denoise_step": seconds * 1e3 / max(1, n_steps), "clocks": clocks,
+    }
+
+
 def run_step_breakdown(args, local_rank: int):
     """Where one denoise step of Dream-7B (32 block rows against 4161 cached tokens, bf16) spends its time: each group
     of launches captured in a CUDA graph of its own and replayed, CUDA-event timed. One GPU."""
@@ -481,8 +540,9 @@ def main():
     ap.add_argument("--steps", type=int, default=200)
     ap.add_argument("--warmup", type=int, default=10)
     ap.add_argument("--impl", default="native", choices=["native", "reference"])
-    ap.add_argument("--workload", default="op", choices=["op", "dream7b_8k", "dream7b_32k", "dream7b_step"],
+    ap.add_argument("--workload", default="op", choices=["op", "dream7b_8k", "dream7b_32k", "dream7b_step", "dream7b_decode_batch"],
                     help="op (default): BASELINE configs[1], the op-level decode attention; the others time whole requests")
+    ap.add_argument("--concurrent", type=int, default=16, help="requests per GPU that share a denoise step (dream7b_decode_batch)")
     args = ap.parse_args()
 
     rank = int(os.environ.get("RANK", "0"))
@@ -504,6 +564,8 @@ def main():
     try:
         if args.workload == "op":
             line = run_native(args, rank, world, local_rank)
+        elif args.workload == "dream7b_decode_batch":
+            line = run_decode_batch(args, rank, world, local_rank)
         elif args.workload == "dream7b_step":
             line = run_step_breakdown(args, local_rank) if rank == 0 else None
         else:

@@ -933,7 +933,8 @@ inline Plan make_plan(const pdllm_attn_params* p) {
   if (2 * base_ctas <= sms) {
     // Few units (the decode shape: one block of rows per request): everything fits in one wave, and the merge of S
     // partial tiles per unit is better spread over a grid of its own than pulled through the one SM that finishes
-    // last. In key-tile times: cost(S) = ovh + ceil(T / S) + launch + traffic * S, ovh ~ 2.3, launch ~ 1, traffic ~ 0.03.
+    // last. In key-tile times: cost(S) = ovh + ceil(T / S) + launch + merge * S, ovh ~ 2.3, launch ~ 1, merge ~ 0.25 (a sweep
+    // at 32 rows x 4161 keys is flat between 8 and 16 splits, 28 us, and rises on both sides).
     pl.fused_merge = 0;
     if (splits <= 0) {
       const int T = max_key_tiles - 1;
@@ -943,7 +944,7 @@ inline Plan make_plan(const pdllm_attn_params* p) {
       double best = 2.3 + T;
       splits = 1;
       for (int s = 2; s <= s_max; ++s) {
-        const double cost = 2.3 + (T + s - 1) / s + 1.0 + 0.03 * s;
+        const double cost = 2.3 + (T + s - 1) / s + 1.0 + 0.25 * s;
         if (cost < best - 1e-9) { best = cost; splits = s; }
       }
     }

@@ -618,6 +618,52 @@ class FastDLLMDreamEngine:
         finally:
             self.release_pd_record(record)
 
+    @_on_device
+    @torch.inference_mode()
+    def decode_from_pd_records(self, records: Sequence[DreamPrefillRecord], *, max_new_tokens: int,
+                               stop_token_ids: Optional[Iterable[int]] = None) -> List[FastDLLMEngineOutput]:
+        """Denoise the blocks of SEVERAL records in shared steps: their rows are packed into one forward per step (each
+        against its own prompt pages), so the model's weights are read once per step for all of them instead of once
+        per request. Same result per request as `decode_from_pd_record`; consumes every record. Not in the reference
+        facade, whose decode loop serves one request (its batching lives in the scheduler of the underlying engine)."""
+        records = list(records)
+        if not records:
+            return []
+        if max_new_tokens <= 0:
+            return [FastDLLMEngineOutput(text="", token_ids=[], n_diff_steps=0) for _ in records]
+        decode_len = records[0].decode_len
+        try:
+            for r in records:
+                if r.decode_len != decode_len:
+                    raise ValueError("records of one batch must share decode_len")
+                if max_new_tokens > r.decode_len:
+                    raise ValueError(f"max_new_tokens={max_new_tokens} exceeds record decode_len={r.decode_len}.")
+            requests = [dict(positions=r.suffix_positions, ctx_page_ids=r.prompt_page_ids, ctx_len=r.prompt_len,
+                             last_logit=r.last_context_logit, store_slots=slots_for(r.block_page_ids, 0, decode_len, self.page_size))
+                        for r in records]
+            runner = self.model.batched_step_runner(block_len=decode_len, requests=requests, mask_token_id=self.mask_token_id,
+                                                    threshold=self.threshold, shift=True, softmax_dtype=torch.float32,
+                                                    use_graph=not self.config.enforce_eager)
+            for block, r in zip(runner.blocks, records):
+                block.fill_(self.mask_token_id)
+                block[0] = int(r.first_token_id)
+            steps_needed = [0] * len(records)
+            step, left = 0, [decode_len - 1] * len(records)
+            while any(x > 0 for x in left):
+                step += 1
+                runner.run()
+                for i, (before, after) in enumerate(zip(left, runner.remaining)):
+                    if before > 0 and after == 0:
+                        steps_needed[i] = step
+                left = list(runner.remaining)
+                if step > decode_len + 8:
+                    raise RuntimeError("denoising did not converge: every step must unmask at least one slot")
+            ops.check_status(self.device)
+            return [self._finish(block.clone(), max_new_tokens, stop_token_ids, steps_needed[i]) for i, block in enumerate(runner.blocks)]
+        finally:
+            for r in records:
+                self.release_pd_record(r)
+
     def release_pd_record(self, record: DreamPrefillRecord) -> None:
         """Release the pages of a record that will not be decoded (reference :2192-2198)."""
         self._prefix_cache.release_pages(record.block_page_ids)

@@ -356,9 +356,15 @@ class PagedDreamModel:
         """One denoise step = forward of the block rows against `ctx_len` cached tokens + the unmask kernel, repeated
         with identical shapes until the block is full. Returns a runner whose `.block` (int64 [block_len]) the caller
         fills with the initial ids; `.run()` performs a step and returns the number of MASK slots left."""
-        return BlockStepRunner(self, block_len=block_len, positions=positions, ctx_page_ids=ctx_page_ids, ctx_len=ctx_len,
-                               mask_token_id=mask_token_id, threshold=threshold, last_logit=last_logit, shift=shift,
-                               softmax_dtype=softmax_dtype, store_slots=store_slots, use_graph=use_graph)
+        request = dict(positions=positions, ctx_page_ids=ctx_page_ids, ctx_len=ctx_len, last_logit=last_logit, store_slots=store_slots)
+        return BlockStepRunner(self, block_len=block_len, requests=[request], mask_token_id=mask_token_id, threshold=threshold,
+                               shift=shift, softmax_dtype=softmax_dtype, use_graph=use_graph)
+
+    def batched_step_runner(self, *, block_len: int, requests: Sequence[dict], mask_token_id: int, threshold: float, shift: bool,
+                            softmax_dtype: Optional[torch.dtype], use_graph: bool = True) -> "BlockStepRunner":
+        """The same step for the blocks of several requests at once (`.blocks[i]`, `.remaining[i]`)."""
+        return BlockStepRunner(self, block_len=block_len, requests=list(requests), mask_token_id=mask_token_id, threshold=threshold,
+                               shift=shift, softmax_dtype=softmax_dtype, use_graph=use_graph)
 
     # ---- small tensor helpers ----
     def ids_tensor(self, ids: Sequence[int]) -> torch.Tensor:
@@ -372,86 +378,103 @@ class PagedDreamModel:
 class _StepGraph:
     """A captured denoise step and the device buffers it reads: per request only their CONTENTS change."""
 
-    def __init__(self, model: "PagedDreamModel", n: int, pages: int, has_last: bool, stores: bool):
+    def __init__(self, model: "PagedDreamModel", n: int, batch: int, pages: int, has_last: bool, stores: bool):
         dev = model.device
-        self.block = torch.zeros(n, dtype=torch.long, device=dev)
-        self.positions = torch.zeros(n, dtype=torch.long, device=dev)
-        self.table = torch.zeros((1, pages), dtype=torch.int32, device=dev)
-        self.seq_lens = torch.zeros(1, dtype=torch.int32, device=dev)
-        self.last_logit = torch.zeros(model.arch.vocab_size, dtype=model.dtype, device=dev) if has_last else None
-        self.slots = torch.full((n,), -1, dtype=torch.int32, device=dev) if stores else None
-        self.cu = model.i32([0, n])
+        self.block = torch.zeros(batch * n, dtype=torch.long, device=dev)
+        self.positions = torch.zeros(batch * n, dtype=torch.long, device=dev)
+        self.table = torch.zeros((batch, pages), dtype=torch.int32, device=dev)
+        self.seq_lens = torch.zeros(batch, dtype=torch.int32, device=dev)
+        self.last_logit = torch.zeros((batch, model.arch.vocab_size), dtype=model.dtype, device=dev) if has_last else None
+        self.slots = torch.full((batch * n,), -1, dtype=torch.int32, device=dev) if stores else None
+        self.cu = model.i32([i * n for i in range(batch + 1)])
         self.graph: Optional[torch.cuda.CUDAGraph] = None
-        self.counts: Optional[torch.Tensor] = None
+        self.left: Optional[torch.Tensor] = None      # [batch] MASK slots left after the captured step
         self.eager_steps = 0
 
 
 class BlockStepRunner:
-    """The inner loop of block denoising: every step launches the same ~12 kernels per layer on the same 32 rows, so on
-    a 7B model a step is bound by launch overhead (hundreds of launches of microseconds each), not by the 15 GB of
-    weights it reads. A step is therefore captured into a CUDA graph, once per shape class — (block length, context
-    pages rounded up to a multiple of four, unmask rule) — and kept with the model; a request only copies its ids,
-    positions, page list, context length and last-context logit into the graph's input buffers and replays. The first
-    step of a new shape class runs eagerly (it also initialises library handles and grow-only workspaces), the second
-    is the capture. Capturing costs about as much as a hundred steps, so it pays from the second request on."""
+    """The inner loop of block denoising: every step launches the same ~11 kernels per layer on the same few rows, so on
+    a 7B model a step is bound by launch overhead (hundreds of launches of microseconds each) and by the 15 GB of
+    weights it reads, whatever the number of rows. Two consequences:
+      * a step is captured into a CUDA graph, once per shape class — (block length, number of requests, context pages
+        rounded up to a multiple of four, unmask rule) — and kept with the model; a request only copies its ids,
+        positions, page list, context length and last-context logit into the graph's input buffers and replays. The
+        first step of a new shape class runs eagerly (it also initialises library handles and grow-only workspaces),
+        the second is the capture. Capturing costs about as much as a hundred steps, so it pays from the second
+        request on;
+      * the blocks of several requests can share a step: their rows are packed into one forward (each with its own
+        page list and context length), so the weights are read once for all of them.
+    `requests`: one dict per request with `positions`, `ctx_page_ids`, `ctx_len`, `last_logit`, `store_slots`."""
 
     _PAGE_BUCKET = 4
     _MAX_CACHED = 8
 
-    def __init__(self, model: PagedDreamModel, *, block_len, positions, ctx_page_ids, ctx_len, mask_token_id, threshold, last_logit,
-                 shift, softmax_dtype, store_slots, use_graph):
+    def __init__(self, model: PagedDreamModel, *, block_len, requests, mask_token_id, threshold, shift, softmax_dtype, use_graph):
         self.m = model
-        n = int(block_len)
-        need_pages = max(1, -(-int(ctx_len) // model.page_size))
-        pages = -(-need_pages // self._PAGE_BUCKET) * self._PAGE_BUCKET
-        key = (n, pages, int(mask_token_id), float(threshold), last_logit is not None, bool(shift), softmax_dtype, store_slots is not None)
+        n, batch = int(block_len), len(requests)
+        if batch < 1:
+            raise ValueError("no request to step")
+        if any(int(r["ctx_len"]) <= 0 for r in requests):
+            raise ValueError("block denoising needs a cached context")
+        has_last = requests[0].get("last_logit") is not None
+        stores = requests[0].get("store_slots") is not None
+        if any((r.get("last_logit") is not None) != has_last or (r.get("store_slots") is not None) != stores for r in requests):
+            raise ValueError("requests of one step must agree on last_logit / store_slots being given")
+        need = [max(1, -(-int(r["ctx_len"]) // model.page_size)) for r in requests]
+        pages = -(-max(need) // self._PAGE_BUCKET) * self._PAGE_BUCKET
+        key = (n, batch, pages, int(mask_token_id), float(threshold), has_last, bool(shift), softmax_dtype, stores)
         cache = model.__dict__.setdefault("_step_graphs", {})
         entry = cache.pop(key, None) if use_graph else None
         if entry is None:
             with torch.inference_mode(False):
-                entry = _StepGraph(model, n, pages, last_logit is not None, store_slots is not None)
+                entry = _StepGraph(model, n, batch, pages, has_last, stores)
         if use_graph:
             cache[key] = entry                      # most recently used last
             while len(cache) > self._MAX_CACHED:
                 cache.pop(next(iter(cache)))
         self.e = entry
-        self.n, self.use_graph = n, bool(use_graph)
-        self.block = entry.block
+        self.n, self.batch, self.use_graph = n, batch, bool(use_graph)
+        self.blocks = [entry.block[i * n:(i + 1) * n] for i in range(batch)]
+        self.block = self.blocks[0]
+        self.remaining = [n] * batch
         dev = model.device
-        entry.positions.copy_(torch.tensor(list(positions), dtype=torch.long, device=dev))
-        ids = list(ctx_page_ids)[:need_pages]
-        entry.table[0, : len(ids)].copy_(model.i32(ids))
-        entry.seq_lens.fill_(int(ctx_len) + n)
-        if entry.last_logit is not None:
-            entry.last_logit.copy_(last_logit.reshape(-1))
-        if entry.slots is not None:
-            entry.slots.copy_(model.i32(list(store_slots)))
+        entry.positions.copy_(torch.tensor([p for r in requests for p in r["positions"]], dtype=torch.long, device=dev))
+        entry.table.zero_()
+        for i, r in enumerate(requests):
+            ids = list(r["ctx_page_ids"])[:need[i]]
+            entry.table[i, : len(ids)].copy_(model.i32(ids))
+            if has_last:
+                entry.last_logit[i].copy_(r["last_logit"].reshape(-1))
+        entry.seq_lens.copy_(model.i32([int(r["ctx_len"]) + n for r in requests]))
+        if stores:
+            entry.slots.copy_(model.i32([sl for r in requests for sl in r["store_slots"]]))
         self.kwargs = dict(block_table=entry.table, seq_lens=entry.seq_lens, max_seq_len=pages * model.page_size + n)
-        self.unmask = dict(mask_token_id=int(mask_token_id), threshold=float(threshold), last_logit=entry.last_logit, shift=bool(shift),
-                           softmax_dtype=softmax_dtype)
-        if int(ctx_len) <= 0:
-            raise ValueError("block denoising needs a cached context")
+        self.unmask = dict(mask_token_id=int(mask_token_id), threshold=float(threshold), shift=bool(shift), softmax_dtype=softmax_dtype)
 
     def _step(self) -> torch.Tensor:
-        e = self.e
-        logits, _ = self.m.forward(e.block, e.positions, cu_seqlens=e.cu, max_query_len=self.n, slot_mapping=e.slots, causal=False,
+        e, n = self.e, self.n
+        logits, _ = self.m.forward(e.block, e.positions, cu_seqlens=e.cu, max_query_len=n, slot_mapping=e.slots, causal=False,
                                    **self.kwargs)
-        return ops.unmask_step(logits, e.block, **self.unmask)
+        left = [ops.unmask_step(logits[i * n:(i + 1) * n], self.blocks[i], last_logit=None if e.last_logit is None else e.last_logit[i],
+                                **self.unmask)[2] for i in range(self.batch)]
+        return torch.stack(left)
 
     def run(self) -> int:
+        """One step for every request; returns the total number of MASK slots left (per request: `.remaining`)."""
         e = self.e
         with torch.cuda.device(self.m.device):
             if not self.use_graph or (e.graph is None and e.eager_steps == 0):
                 e.eager_steps += 1
-                counts = self._step()
+                left = self._step()
             else:
                 if e.graph is None:
                     graph = torch.cuda.CUDAGraph()
                     # torch keeps ONE default capture stream per process, created on whichever device captured first:
                     # with engines on several GPUs in one process the capture stream has to be this device's own
                     with torch.cuda.graph(graph, stream=torch.cuda.Stream(device=self.m.device)):
-                        e.counts = self._step()
+                        e.left = self._step()
                     e.graph = graph                  # capturing records the launches without running them
                 e.graph.replay()
-                counts = e.counts
-            return int(counts[2].item())
+                left = e.left
+            self.remaining = left.tolist()           # the one host read of a step
+            return int(sum(self.remaining))

@@ -267,3 +267,20 @@ def test_engine_to_engine_copy_across_gpus(engine, ckpt):
     ops.check_status(torch.device("cuda", 1))
     assert other._prefix_cache.num_free_pages == 16
     engine._prefix_cache.evict_one()
+
+
+def test_batched_decode_equals_one_by_one(engine):
+    """Three requests with different prompt lengths denoised in shared steps: same ids and step counts as decoding each
+    record on its own; every page comes back."""
+    prompts = [_prompt(600, seed=21), _prompt(300, seed=22), _prompt(777, seed=23)]
+    free0 = engine._prefix_cache.num_free_pages
+    single = [engine.decode_from_pd_record(engine.prefill_to_pd_record(p, max_new_tokens=BLOCK), max_new_tokens=BLOCK) for p in prompts]
+    records = [engine.prefill_to_pd_record(p, max_new_tokens=BLOCK) for p in prompts]      # prefix-cache hits
+    assert all(r.cached_prefix is not None for r in records)
+    batched = engine.decode_from_pd_records(records, max_new_tokens=BLOCK)
+    for one, many in zip(single, batched):
+        assert many.token_ids == one.token_ids and many.n_diff_steps == one.n_diff_steps
+    assert engine.decode_from_pd_records([], max_new_tokens=BLOCK) == []
+    while engine._prefix_cache.evict_one():
+        pass
+    assert engine._prefix_cache.num_free_pages == free0
