@@ -238,6 +238,25 @@ def test_attention_tc_ragged_batch(ops, cuda_device, num_splits):
     assert float((out.float().cpu() - ref).abs().max()) < 0.05
 
 
+def test_attention_tc_uneven_split_and_fused_merge_ragged(ops, cuda_device):
+    """96 (sequence, KV head, tile pair) units on 148 SMs: the plan cuts every unit in two uneven KV splits and the last
+    CTA of a pair merges them. Ragged: query lengths from one tile to three, every other context a partial page, so
+    some second splits get nothing to attend (neutral partials) and some pairs have an empty second tile."""
+    q_lens = [50, 36, 18, 40, 7, 36, 36, 19, 36, 25, 36, 36]          # 12 sequences x 4 KV heads x 2 pairs where q_len > 36
+    case = _attention_case(31, num_seqs=12, hq=28, hkv=4, d=128, page=256, chunks_in_pool=4, pages_per_chunk=2, sel_chunks=3,
+                           q_lens=q_lens, dtype=torch.bfloat16, ctx_tail=200)     # 13 key tiles: long enough for the uneven cut
+    for kwargs in (dict(), dict(causal=True), dict(bidirectional=False)):
+        out, used = _run_attention(ops, cuda_device, case, impl="tc", **kwargs)
+        assert used == "tc"
+        ref = _ref_attention(case, **kwargs)
+        assert rel_err(out, ref) < ATTN_REL_TOL, kwargs
+        assert not torch.isnan(out).any(), kwargs
+    # twice in a row through the same workspace: the arrival counters must have returned to zero
+    again, _ = _run_attention(ops, cuda_device, case, impl="tc")
+    first, _ = _run_attention(ops, cuda_device, case, impl="tc")
+    assert torch.equal(again, first)
+
+
 def test_attention_tc_masks_and_prefill(ops, cuda_device):
     case = _attention_case(22, num_seqs=2, hq=28, hkv=4, d=128, page=256, chunks_in_pool=2, pages_per_chunk=1, sel_chunks=1,
                            q_lens=[200, 160], dtype=torch.bfloat16)
