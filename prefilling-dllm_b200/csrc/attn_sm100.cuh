@@ -354,6 +354,7 @@ __device__ __forceinline__ void finish_split(const Args& a, int seq, int kvh, in
   merge_split_row(a.part_o, a.part_ml, a.num_splits, a.is_bf16, unit0, r, out_row);
 }
 
+template <bool kBf16>
 __global__ void __launch_bounds__(kThreads, 1)
 attn_sm100_kernel(const __grid_constant__ CUtensorMap q_map, const __grid_constant__ CUtensorMap kn_map,
                   const __grid_constant__ CUtensorMap vn_map, const __grid_constant__ CUtensorMap kc_map,
@@ -446,8 +447,8 @@ attn_sm100_kernel(const __grid_constant__ CUtensorMap q_map, const __grid_consta
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
 
-  const uint32_t idesc_qk = make_idesc(a.is_bf16 != 0, false, kHalfN);    // S_Xb[128 x 64] = Q_X[128 x 128] K_b^T
-  const uint32_t idesc_pv = make_idesc(a.is_bf16 != 0, true, kHeadDim);   // O_X[128 x 128] += P_Xb[128 x 64] V_b
+  const uint32_t idesc_qk = make_idesc(kBf16, false, kHalfN);    // S_Xb[128 x 64] = Q_X[128 x 128] K_b^T
+  const uint32_t idesc_pv = make_idesc(kBf16, true, kHeadDim);   // O_X[128 x 128] += P_Xb[128 x 64] V_b
 
   if (warp == kProducerWarp) {
     // =========================== TMA producer ===========================
@@ -699,7 +700,7 @@ attn_sm100_kernel(const __grid_constant__ CUtensorMap q_map, const __grid_consta
           const float p2 = ex2(fmaf(__uint_as_float(s[j + 2]), a.scale_log2, -m_use));
           const float p3 = ex2(fmaf(__uint_as_float(s[j + 3]), a.scale_log2, -m_use));
           l0 += p0; l1 += p1; l2 += p2; l3 += p3;
-          if (a.is_bf16) {
+          if (kBf16) {
             __nv_bfloat162 h0 = __floats2bfloat162_rn(p0, p1), h1 = __floats2bfloat162_rn(p2, p3);
             packed[j >> 1] = *reinterpret_cast<uint32_t*>(&h0);
             packed[(j >> 1) + 1] = *reinterpret_cast<uint32_t*>(&h1);
@@ -737,7 +738,7 @@ attn_sm100_kernel(const __grid_constant__ CUtensorMap q_map, const __grid_consta
 #pragma unroll
             for (int j = 0; j < 32; j += 2) {
               const float o0 = __uint_as_float(s[j]) * inv, o1 = __uint_as_float(s[j + 1]) * inv;
-              if (a.is_bf16) {
+              if (kBf16) {
                 __nv_bfloat162 h = __floats2bfloat162_rn(o0, o1);
                 packed[j >> 1] = *reinterpret_cast<uint32_t*>(&h);
               } else {
@@ -1062,13 +1063,15 @@ inline int launch(const pdllm_attn_params* p, cudaStream_t stream) {
     cudaGetDevice(&dev);
     std::lock_guard<std::mutex> lock(mu);
     if (dev < 0 || dev >= 64 || !done[dev]) {
-      cudaError_t e = cudaFuncSetAttribute(attn_sm100_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes);
+      cudaError_t e = cudaFuncSetAttribute(attn_sm100_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes);
+      if (e == cudaSuccess) e = cudaFuncSetAttribute(attn_sm100_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes);
       if (e != cudaSuccess) return fail(static_cast<int>(e), "cudaFuncSetAttribute: %s", cudaGetErrorString(e));
       if (dev >= 0 && dev < 64) done[dev] = true;
     }
   }
 
-  attn_sm100_kernel<<<static_cast<unsigned>(pl.ctas), kThreads, kSmemBytes, stream>>>(q_map, kn_map, vn_map, kc_map, vc_map, a);
+  if (bf16) attn_sm100_kernel<true><<<static_cast<unsigned>(pl.ctas), kThreads, kSmemBytes, stream>>>(q_map, kn_map, vn_map, kc_map, vc_map, a);
+  else attn_sm100_kernel<false><<<static_cast<unsigned>(pl.ctas), kThreads, kSmemBytes, stream>>>(q_map, kn_map, vn_map, kc_map, vc_map, a);
   if ((rc = check_launch("attn_sm100_kernel")) != 0) return rc;
   if (pl.num_splits > 1 && !pl.fused_merge) {
     attn_combine_kernel<<<static_cast<unsigned>(pl.tiles * (kHeadDim / kCombineCols)), kTileM, 0, stream>>>(a);
