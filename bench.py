@@ -459,6 +459,81 @@ def run_decode_batch(args, rank: int, world: int, local_rank: int):
     }
 
 
+def run_mha_decode_attention(args, rank: int, world: int, local_rank: int):
+    """The HBM-bound side of the decode-attention kernel: LLaDA-8B-shaped heads (32 query = 32 KV heads, d128, bf16),
+    `--concurrent` requests per GPU (default 16), each one 32-row response block attending 8256 cached tokens (4 selected
+    chunks of 2048 + a 64-token query) through a block table of pages in random physical order. One attention launch
+    per step = one layer of one denoise step. The K/V pool (2 x 1.1 GB at 16 requests) is far larger than L2.
+    Replicas over GPUs (every rank its own requests, no collective)."""
+    from prefilling_dllm_b200 import ops
+
+    device = torch.device("cuda", local_rank)
+    torch.cuda.set_device(device)
+    n_req, rows, ctx, heads, page = max(1, args.concurrent), 32, 4 * 2048 + 64, 32, 256
+    pages_per = -(-ctx // page)
+    g = torch.Generator(device=device).manual_seed(2000 + rank)
+    k_cache = torch.randn(n_req * pages_per, page, heads, D, device=device, dtype=torch.bfloat16, generator=g)
+    v_cache = torch.randn(n_req * pages_per, page, heads, D, device=device, dtype=torch.bfloat16, generator=g)
+    table = torch.randperm(n_req * pages_per, device=device, generator=g).to(torch.int32).view(n_req, pages_per).contiguous()
+    qkv = torch.randn(n_req * rows, 3 * heads, D, device=device, dtype=torch.bfloat16, generator=g)
+    q, k, v = qkv[:, :heads], qkv[:, heads:2 * heads], qkv[:, 2 * heads:]
+    out = torch.empty(n_req * rows, heads, D, device=device, dtype=torch.bfloat16)
+    cu = (torch.arange(n_req + 1, device=device) * rows).to(torch.int32)
+    seq_lens = torch.full((n_req,), ctx + rows, dtype=torch.int32, device=device)
+    scale = 1.0 / math.sqrt(D)
+    stream = torch.cuda.current_stream(device)
+
+    def step():
+        return ops.paged_attention(q, k, v, out, cu_seqlens_q=cu, max_query_len=rows, key_cache=k_cache, value_cache=v_cache,
+                                   block_table=table, seq_lens=seq_lens, max_seq_len=pages_per * page + rows, sm_scale=scale,
+                                   bidirectional=True)
+
+    warmup = max(3, args.warmup)
+    for _ in range(warmup):
+        used = step()
+    torch.cuda.synchronize(device)
+    ops.check_status(device)
+    if used != "tc":
+        raise RuntimeError(f"expected the tcgen05 attention kernel, ran {used}")
+    sampler = ClockSampler(local_rank)
+    if rank == 0:
+        sampler.start()
+    if world > 1:
+        torch.distributed.barrier()
+    torch.cuda.synchronize(device)
+    start, stop = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    start.record(stream)
+    for _ in range(args.steps):
+        step()
+    stop.record(stream)
+    torch.cuda.synchronize(device)
+    ms = torch.tensor([start.elapsed_time(stop) / args.steps], dtype=torch.float64, device=device)
+    if world > 1:
+        torch.distributed.all_reduce(ms, op=torch.distributed.ReduceOp.MAX)
+    clocks = sampler.stop() if rank == 0 else None
+    ops.check_status(device)
+    if rank != 0:
+        return None
+    ms_per_step = float(ms.item())
+    bytes_per_launch = n_req * (ctx * 2 * heads * D * 2 + rows * 4 * heads * D * 2)     # K/V pages once + q, k, v, out rows
+    flops_per_launch = n_req * 4 * heads * D * rows * (ctx + rows)
+    peaks = load_peaks()
+    gbs = bytes_per_launch / (ms_per_step * 1e-3) / 1e9
+    return {
+        "metric": "decode_attention_tok_per_s", "value": world * n_req * rows / (ms_per_step * 1e-3), "unit": "tok/s", "n_gpus": world,
+        "steps": args.steps, "warmup": warmup, "ms_per_step": ms_per_step, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+        "dtype": "bf16", "data": "synthetic",
+        "config": {"workload": f"op_mha_decode: {n_req} req x 32 response rows, 32/32 heads (LLaDA-8B shape), d128, page 256, {ctx} cached "
+                               "tokens per request via block table (random page order), bidirectional, N(0,1) bf16",
+                   "parallelism": f"dp{world} (replicas over requests, no data-path collective)",
+                   "l2": "K/V pool of 2 x %.2f GB read once per step (> 126 MB L2)" % (k_cache.numel() * 2 / 1e9)},
+        "roofline": {"bound": "hbm", "achieved": gbs, "peak": peaks["hbm"], "unit": "GB/s", "frac": gbs / peaks["hbm"], "traffic": None,
+                     "peak_source": peaks["source"], "bytes_per_launch": bytes_per_launch,
+                     "tensor": {"achieved": flops_per_launch / (ms_per_step * 1e-3) / 1e12, "unit": "TFLOP/s"}},
+        "gpu_launches": args.steps, "clocks": clocks,
+    }
+
+
 def run_step_breakdown(args, local_rank: int):
     """Where one denoise step of Dream-7B (32 block rows against 4161 cached tokens, bf16) spends its time: each group
     of launches captured in a CUDA graph of its own and replayed, CUDA-event timed. One GPU."""
@@ -540,8 +615,9 @@ def main():
     ap.add_argument("--steps", type=int, default=200)
     ap.add_argument("--warmup", type=int, default=10)
     ap.add_argument("--impl", default="native", choices=["native", "reference"])
-    ap.add_argument("--workload", default="op", choices=["op", "dream7b_8k", "dream7b_32k", "dream7b_step", "dream7b_decode_batch"],
-                    help="op (default): BASELINE configs[1], the op-level decode attention; the others time whole requests")
+    ap.add_argument("--workload", default="op", choices=["op", "op_mha_decode", "dream7b_8k", "dream7b_32k", "dream7b_step", "dream7b_decode_batch"],
+                    help="op (default): BASELINE configs[1], the op-level decode attention; op_mha_decode: the same kernel on an HBM-bound "
+                         "MHA shape; the others time whole requests")
     ap.add_argument("--concurrent", type=int, default=16, help="requests per GPU that share a denoise step (dream7b_decode_batch)")
     args = ap.parse_args()
 
@@ -564,6 +640,8 @@ def main():
     try:
         if args.workload == "op":
             line = run_native(args, rank, world, local_rank)
+        elif args.workload == "op_mha_decode":
+            line = run_mha_decode_attention(args, rank, world, local_rank)
         elif args.workload == "dream7b_decode_batch":
             line = run_decode_batch(args, rank, world, local_rank)
         elif args.workload == "dream7b_step":

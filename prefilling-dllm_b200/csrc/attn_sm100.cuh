@@ -71,7 +71,10 @@ struct Args {
   int64_t out_stride, block_table_stride, mask_stride_m, mask_stride_n, num_pages;
   int num_seqs, max_pages, num_q_heads, num_kv_heads, group, tpt, q_tiles, q_pairs, num_splits;
   int first_permille;  // uneven two-way split: share (in 1/1000) of a unit's key tiles that split 0 takes; 0 = even splits
-  int base_ctas;       // (sequence, KV head, query-tile pair) units; blockIdx = split * base_ctas + unit
+  int base_ctas;       // (sequence, KV head, query-tile pair) units
+  int n_whole;         // the first n_whole units run unsplit in CTAs [0, n_whole), ahead of the others' splits:
+                       // blockIdx = n_whole + split * (base_ctas - n_whole) + (unit - n_whole)
+  int tile0;           // first query tile of unit n_whole: partials exist for query tiles >= tile0 only
   int fused_merge;     // 1: the last CTA of a tile pair merges the splits; 0: attn_combine_kernel does, after this kernel
   int page_size, has_cache, mask_mode, bidirectional, block_m, is_bf16;
   float scale_log2;  // sm_scale * log2(e)
@@ -348,7 +351,7 @@ __device__ __forceinline__ void finish_split(const Args& a, int seq, int kvh, in
   const int tok_local = r / a.group;
   if (tok_local >= n_tok) return;
   const int head_local = r - tok_local * a.group;
-  const int64_t unit0 = ((static_cast<int64_t>(seq) * a.num_kv_heads + kvh) * a.q_tiles + 2 * pair + x) * a.num_splits;
+  const int64_t unit0 = ((static_cast<int64_t>(seq) * a.num_kv_heads + kvh) * a.q_tiles + 2 * pair + x - a.tile0) * a.num_splits;
   uint8_t* out_row = reinterpret_cast<uint8_t*>(a.out) +
                      ((static_cast<int64_t>(q_start + tok0 + tok_local)) * a.out_stride + static_cast<int64_t>(kvh * a.group + head_local) * kHeadDim) * 2;
   merge_split_row(a.part_o, a.part_ml, a.num_splits, a.is_bf16, unit0, r, out_row);
@@ -370,10 +373,18 @@ attn_sm100_kernel(const __grid_constant__ CUtensorMap q_map, const __grid_consta
   const int lane = threadIdx.x & 31;
 
   // ---- decode the work unit: (sequence, KV head, pair of query tiles, KV split) ----
-  // Splits are the slowest index: all first splits come first in launch order. With an uneven two-way split those are
-  // the long CTAs, so the short second splits fill in behind them and the last wave stays short.
-  int u = blockIdx.x % a.base_ctas;
-  const int split = blockIdx.x / a.base_ctas;
+  // Unsplit units come first in launch order, then the split ones with the split as the slowest index: all first
+  // splits, all second splits, ... With an uneven two-way split the first are the long CTAs, so the short second
+  // splits fill in behind them and the last wave stays short.
+  int u, split;
+  if (static_cast<int>(blockIdx.x) < a.n_whole) {
+    u = blockIdx.x; split = 0;
+  } else {
+    const int idx = blockIdx.x - a.n_whole, rest = a.base_ctas - a.n_whole;
+    u = a.n_whole + idx % rest; split = idx / rest;
+  }
+  // CTAs that share this unit's key tiles (recomputed where it is needed rather than kept in a register)
+#define PDLLM_NSPLIT (static_cast<int>(blockIdx.x) < a.n_whole ? 1 : a.num_splits)
   const int pair = u % a.q_pairs; u /= a.q_pairs;
   const int kvh = u % a.num_kv_heads;
   const int seq = u / a.num_kv_heads;
@@ -400,29 +411,30 @@ attn_sm100_kernel(const __grid_constant__ CUtensorMap q_map, const __grid_consta
   const int n_new_tiles = (new_end + kTileN - 1) / kTileN;
   const int total_tiles = n_ctx_tiles + n_new_tiles;
   int t_begin, t_end;
-  if (a.first_permille > 0) {   // two splits: [0, cut) and [cut, total)
+  if (a.first_permille > 0 && PDLLM_NSPLIT == 2) {   // two splits: [0, cut) and [cut, total)
     const int cut = min(total_tiles, (total_tiles * a.first_permille + 999) / 1000);
     t_begin = split == 0 ? 0 : cut;
     t_end = split == 0 ? cut : total_tiles;
   } else {
-    const int per_split = (total_tiles + a.num_splits - 1) / a.num_splits;
+    const int nsplit = PDLLM_NSPLIT;
+    const int per_split = (total_tiles + nsplit - 1) / nsplit;
     t_begin = split * per_split;
     t_end = min(total_tiles, t_begin + per_split);
   }
   const int n_iter = t_end - t_begin;
   // index of a query tile's split-KV partial
-  const int64_t unit_base = ((static_cast<int64_t>(seq) * a.num_kv_heads + kvh) * a.q_tiles + 2 * pair) * a.num_splits + split;
+  const int64_t unit_base = ((static_cast<int64_t>(seq) * a.num_kv_heads + kvh) * a.q_tiles + 2 * pair - a.tile0) * a.num_splits + split;
 
   if (n_tokA <= 0) return;
   if (n_iter <= 0) {
     // Nothing to attend in this split: publish neutral partials so the merge ignores them.
-    if (a.num_splits > 1 && threadIdx.x < 2 * kTileM && (threadIdx.x < kTileM || b_active)) {
+    if (PDLLM_NSPLIT > 1 && threadIdx.x < 2 * kTileM && (threadIdx.x < kTileM || b_active)) {
       const int64_t unit = unit_base + (threadIdx.x >> 7) * a.num_splits;
       const int r = threadIdx.x & (kTileM - 1);
       a.part_ml[(unit * 2 + 0) * kTileM + r] = -INFINITY;
       a.part_ml[(unit * 2 + 1) * kTileM + r] = 0.f;
     }
-    if (a.num_splits > 1 && a.fused_merge) {
+    if (PDLLM_NSPLIT > 1 && a.fused_merge) {
       __threadfence();
       __syncthreads();
       finish_split(a, seq, kvh, pair, q_start, tokA, n_tokA, tokB, n_tokB);
@@ -725,7 +737,7 @@ attn_sm100_kernel(const __grid_constant__ CUtensorMap q_map, const __grid_consta
     if (PDLLM_TRACE_ON) trace_event(a, kTraceIters - 1, 2);
     if (ok) {
       tc_fence_after();
-      if (a.num_splits == 1) {
+      if (PDLLM_NSPLIT == 1) {
         const float inv = (l_run > 0.f) ? 1.f / l_run : 0.f;
         uint8_t* out_row = reinterpret_cast<uint8_t*>(a.out) +
                            ((static_cast<int64_t>(q_start + m)) * a.out_stride + static_cast<int64_t>(kvh * G + head_local) * kHeadDim) * 2;
@@ -770,13 +782,14 @@ attn_sm100_kernel(const __grid_constant__ CUtensorMap q_map, const __grid_consta
 
   // ---- teardown ----
   tc_fence_before();
-  if (a.num_splits > 1 && a.fused_merge) __threadfence();   // this CTA's partials are visible before it counts itself in
+  if (PDLLM_NSPLIT > 1 && a.fused_merge) __threadfence();   // this CTA's partials are visible before it counts itself in
   __syncthreads();
   if (warp == kProducerWarp) {
     tc_fence_after();
     tmem_dealloc(tmem_base, kTmemCols);
   }
-  if (a.num_splits > 1 && a.fused_merge) finish_split(a, seq, kvh, pair, q_start, tokA, n_tokA, tokB, n_tokB);
+  if (PDLLM_NSPLIT > 1 && a.fused_merge) finish_split(a, seq, kvh, pair, q_start, tokA, n_tokA, tokB, n_tokB);
+#undef PDLLM_NSPLIT
 }
 
 // Stand-alone merge for shapes with few (sequence, KV head, tile pair) units and many splits (a single block of
@@ -895,8 +908,11 @@ struct Plan {
   int group, tpt, q_tiles, q_pairs, num_splits;
   int first_permille;  // see Args
   int fused_merge;     // see Args
-  int64_t tiles;  // query tiles = split-KV partial groups
-  int64_t ctas;   // CTAs launched: pairs of query tiles x splits
+  int64_t tiles;  // query tiles
+  int64_t units;  // (sequence, KV head, query-tile pair) units
+  int64_t n_whole;  // units that run unsplit, see Args
+  int64_t tile0;    // first query tile that has split-KV partials, see Args
+  int64_t ctas;   // CTAs launched: n_whole + (units - n_whole) x splits
 };
 
 inline Plan make_plan(const pdllm_attn_params* p) {
@@ -950,24 +966,34 @@ inline Plan make_plan(const pdllm_attn_params* p) {
       }
     }
   }
+  pl.n_whole = 0;
   if (splits <= 0) {
-    // One CTA per SM: fill a whole number of waves; each split keeps at least two key tiles.
+    // At least one unit per SM. Whole waves of unsplit units first (no partials, no merge), then the remaining units
+    // cut into splits that fill the last wave(s), so that the tail of the kernel is a fraction of a unit long. In
+    // key-tile times a wave costs its key tiles plus a per-CTA overhead of about 1 (unsplit) or 4 (split: partials
+    // and merge): 16 x 32 units of 65 key tiles on 148 SMs ran 501 / 518 / 569 us with 1 / 2 / 3 even splits.
     const int64_t slots = sm_count();
-    int cap = max_key_tiles / 2; if (cap < 1) cap = 1; if (cap > 32) cap = 32;
-    double best_eff = -1.0; splits = 1;
-    for (int s = 1; s <= cap; ++s) {
-      const int64_t n = base_ctas * s;
-      const int64_t waves = (n + slots - 1) / slots;
-      const double eff = static_cast<double>(n) / static_cast<double>(waves * slots);
-      if (eff > best_eff + 0.03) { best_eff = eff; splits = s; }
-      if (eff >= 0.9) break;
+    int cap = max_key_tiles / 4; if (cap < 1) cap = 1; if (cap > 8) cap = 8;   // a split keeps at least four key tiles
+    const int T = max_key_tiles - 1 > 0 ? max_key_tiles - 1 : 1;
+    double best = -1.0; splits = 1;
+    for (int64_t w = base_ctas / slots; w >= 0; --w) {
+      const int64_t rest = base_ctas - w * slots;
+      for (int s = 1; s <= cap; ++s) {
+        if (rest == 0 && s > 1) break;
+        const int64_t waves = (rest * s + slots - 1) / slots;
+        const double cost = static_cast<double>(w) * (1.0 + T) + static_cast<double>(waves) * ((s > 1 ? 4.0 : 1.0) + (T + s - 1) / s);
+        if (best < 0.0 || cost < best * 0.97) { best = cost; splits = s; pl.n_whole = s > 1 ? w * slots : 0; }
+      }
     }
   }
   if (splits > 32) splits = 32;
   if (splits > max_key_tiles) splits = max_key_tiles;
   if (splits < 1) splits = 1;
+  if (splits == 1) pl.n_whole = 0;
   pl.num_splits = splits;
-  pl.ctas = base_ctas * splits;
+  pl.units = base_ctas;
+  pl.tile0 = (pl.n_whole / pl.q_pairs) * pl.q_tiles + 2 * (pl.n_whole % pl.q_pairs);
+  pl.ctas = pl.n_whole + (base_ctas - pl.n_whole) * splits;
   return pl;
 }
 
@@ -980,7 +1006,7 @@ inline int64_t workspace_bytes(const pdllm_attn_params* p) {
   Plan pl = make_plan(p);
   if (pl.num_splits <= 1) return 0;
   const int64_t pairs = static_cast<int64_t>(p->num_seqs) * p->num_kv_heads * pl.q_pairs;
-  return counter_bytes(pairs) + pl.tiles * pl.num_splits * (static_cast<int64_t>(kHeadDim) * kTileM + 2 * kTileM) * 4;
+  return counter_bytes(pairs) + (pl.tiles - pl.tile0) * pl.num_splits * (static_cast<int64_t>(kHeadDim) * kTileM + 2 * kTileM) * 4;
 }
 
 inline int launch(const pdllm_attn_params* p, cudaStream_t stream) {
@@ -1035,7 +1061,7 @@ inline int launch(const pdllm_attn_params* p, cudaStream_t stream) {
   const int64_t pairs = static_cast<int64_t>(p->num_seqs) * p->num_kv_heads * pl.q_pairs;
   a.split_arrivals = reinterpret_cast<int*>(p->workspace);
   a.part_o = p->workspace ? reinterpret_cast<float*>(static_cast<char*>(p->workspace) + counter_bytes(pairs)) : nullptr;
-  a.part_ml = a.part_o ? a.part_o + pl.tiles * pl.num_splits * static_cast<int64_t>(kHeadDim) * kTileM : nullptr;
+  a.part_ml = a.part_o ? a.part_o + (pl.tiles - pl.tile0) * pl.num_splits * static_cast<int64_t>(kHeadDim) * kTileM : nullptr;
   if (pl.num_splits > 1 && pl.fused_merge && !(p->workspace_zeroed && pairs * 4 <= kCounterHeaderBytes)) {
     // The kernel leaves every counter at zero again, so a caller that zero-filled its workspace once (and again after
     // any launch that reported a wait time-out) can say so and save this memset node on every call.
@@ -1047,7 +1073,7 @@ inline int launch(const pdllm_attn_params* p, cudaStream_t stream) {
   a.num_seqs = p->num_seqs; a.max_pages = p->max_pages; a.num_q_heads = p->num_q_heads; a.num_kv_heads = p->num_kv_heads;
   a.group = pl.group; a.tpt = pl.tpt; a.q_tiles = pl.q_tiles; a.q_pairs = pl.q_pairs; a.num_splits = pl.num_splits;
   a.first_permille = pl.num_splits == 2 ? pl.first_permille : 0;
-  a.base_ctas = static_cast<int>(pl.ctas / pl.num_splits);
+  a.base_ctas = static_cast<int>(pl.units); a.n_whole = static_cast<int>(pl.n_whole); a.tile0 = static_cast<int>(pl.tile0);
   a.fused_merge = pl.fused_merge;
   a.page_size = p->page_size > 0 ? p->page_size : kTileN; a.has_cache = has_cache ? 1 : 0;
   a.mask_mode = p->mask_mode; a.bidirectional = p->bidirectional;

@@ -280,6 +280,56 @@ def test_attention_tc_mha_fp16(ops, cuda_device):
     assert rel_err(out, _ref_attention(case)) < ATTN_REL_TOL
 
 
+@pytest.mark.parametrize("num_splits", [0, 1, 3])
+def test_attention_tc_mha_one_query_tile_ragged(ops, cuda_device, num_splits):
+    """MHA decode shape: every sequence has at most 128 (token x head) rows per KV head, so every CTA has one query tile
+    and its second half idles. Ragged query lengths up to a full tile, contexts of 3 pages or 3 pages minus 250 tokens
+    (odd and even numbers of key tiles), every mask mode, splits forced and chosen."""
+    q_lens = [32, 7, 128, 64, 1]
+    case = _attention_case(41, num_seqs=5, hq=8, hkv=8, d=128, page=256, chunks_in_pool=4, pages_per_chunk=1, sel_chunks=3,
+                           q_lens=q_lens, dtype=torch.bfloat16, ctx_tail=250)
+    g = torch.Generator().manual_seed(8)
+    dense = torch.rand(128, 128, generator=g) > 0.4
+    dense[3, :] = False
+    for kwargs in (dict(), dict(bidirectional=False), dict(causal=True), dict(mask=dense, bidirectional=True)):
+        out, used = _run_attention(ops, cuda_device, case, impl="tc", num_splits=num_splits, **kwargs)
+        assert used == "tc"
+        ref = _ref_attention(case, **kwargs)
+        assert not torch.isnan(out).any(), kwargs
+        assert rel_err(out, ref) < ATTN_REL_TOL, kwargs
+    again, _ = _run_attention(ops, cuda_device, case, impl="tc", num_splits=num_splits)
+    first, _ = _run_attention(ops, cuda_device, case, impl="tc", num_splits=num_splits)
+    assert torch.equal(again, first)
+
+
+def test_attention_tc_short_contexts_single_key_tile(ops, cuda_device):
+    """Contexts of one 128-token page or 68 tokens: CTAs with one or two key tiles, and splits that get none."""
+    case = _attention_case(42, num_seqs=3, hq=4, hkv=4, d=128, page=128, chunks_in_pool=2, pages_per_chunk=1, sel_chunks=1,
+                           q_lens=[16, 100, 128], dtype=torch.float16, ctx_tail=60)
+    for num_splits in (0, 1, 2):
+        out, used = _run_attention(ops, cuda_device, case, impl="tc", num_splits=num_splits)
+        assert used == "tc"
+        assert rel_err(out, _ref_attention(case)) < ATTN_REL_TOL, num_splits
+
+
+def test_attention_tc_whole_waves_then_split_tail(ops, cuda_device):
+    """160 (sequence, KV head) units of 17 key tiles on 148 SMs: the plan runs 148 units unsplit in the first wave and
+    cuts the last 12 in three, so CTAs that write the output directly and CTAs that publish partials share one launch.
+    Ragged contexts; repeated launches must agree bit for bit (the arrival counters return to zero)."""
+    q_lens = [32, 20, 32, 32, 5, 32, 32, 32, 17, 32]
+    case = _attention_case(43, num_seqs=10, hq=16, hkv=16, d=128, page=256, chunks_in_pool=2, pages_per_chunk=4, sel_chunks=2,
+                           q_lens=q_lens, dtype=torch.bfloat16, ctx_tail=300)
+    for kwargs in (dict(), dict(bidirectional=False)):
+        out, used = _run_attention(ops, cuda_device, case, impl="tc", **kwargs)
+        assert used == "tc"
+        ref = _ref_attention(case, **kwargs)
+        assert not torch.isnan(out).any(), kwargs
+        assert rel_err(out, ref) < ATTN_REL_TOL, kwargs
+    again, _ = _run_attention(ops, cuda_device, case, impl="tc")
+    first, _ = _run_attention(ops, cuda_device, case, impl="tc")
+    assert torch.equal(again, first)
+
+
 def test_attention_tc_uninitialised_pool_tail_is_harmless(ops, cuda_device):
     # rows of a page past the context length may hold NaN bit patterns; they must not leak into the output
     case = _attention_case(24, num_seqs=2, hq=28, hkv=4, d=128, page=256, chunks_in_pool=2, pages_per_chunk=1, sel_chunks=1,
