@@ -527,7 +527,10 @@ def run_mha_decode_attention(args, rank: int, world: int, local_rank: int):
                                "tokens per request via block table (random page order), bidirectional, N(0,1) bf16",
                    "parallelism": f"dp{world} (replicas over requests, no data-path collective)",
                    "l2": "K/V pool of 2 x %.2f GB read once per step (> 126 MB L2)" % (k_cache.numel() * 2 / 1e9)},
-        "roofline": {"bound": "hbm", "achieved": gbs, "peak": peaks["hbm"], "unit": "GB/s", "frac": gbs / peaks["hbm"], "traffic": None,
+        "roofline": {"bound": "hbm", "achieved": gbs, "peak": peaks["hbm"], "unit": "GB/s", "frac": gbs / peaks["hbm"],
+                     # dram bytes of one launch at 16 requests from the ncu capture summarised in
+                     # profiles/attn_sm100_kernel_mha_decode.md; other request counts were not captured
+                     "traffic": 2_208_000_000 if n_req == 16 else None,
                      "peak_source": peaks["source"], "bytes_per_launch": bytes_per_launch,
                      "tensor": {"achieved": flops_per_launch / (ms_per_step * 1e-3) / 1e12, "unit": "TFLOP/s"}},
         "gpu_launches": args.steps, "clocks": clocks,
