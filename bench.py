@@ -537,6 +537,110 @@ def run_mha_decode_attention(args, rank: int, world: int, local_rank: int):
     }
 
 
+def run_byte_kernels(args, local_rank: int):
+    """Achieved HBM rate of each byte-moving kernel of the path at the shapes of BASELINE's Dream-7B configs, one GPU.
+    Every kernel runs over several independent input sets in turn, together larger than L2 (so no launch finds its input
+    in the 126 MB L2), as a replayed CUDA graph of 16 launches, CUDA-event timed; bytes are the algorithmic ones (inputs read once + outputs written once)."""
+    from prefilling_dllm_b200 import ops
+
+    device = torch.device("cuda", local_rank)
+    torch.cuda.set_device(device)
+    g = torch.Generator(device=device).manual_seed(7)
+    peaks = load_peaks()
+    vocab, hkv, d, page = 152064, 4, D, PAGE
+    results = []
+
+    def timed(name, unit_note, nbytes, make_call, n_sets):
+        # warm up eagerly (workspaces get allocated), then capture a graph of `calls` launches over the rotating input
+        # sets and replay it: Python's per-call overhead (10-20 us) would otherwise hide kernels this short
+        for i in range(max(3, args.warmup)):
+            make_call(i % n_sets)
+        torch.cuda.synchronize(device)
+        calls = n_sets * max(1, 16 // n_sets)
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph, stream=torch.cuda.Stream(device=device)):
+            for i in range(calls):
+                make_call(i % n_sets)
+        replays = max(3, min(args.steps, 200) // calls)
+        for _ in range(2):
+            graph.replay()
+        torch.cuda.synchronize(device)
+        start, stop = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        start.record()
+        for _ in range(replays):
+            graph.replay()
+        stop.record()
+        torch.cuda.synchronize(device)
+        ops.check_status(device)
+        us = start.elapsed_time(stop) / (replays * calls) * 1e3
+        gbs = nbytes / us / 1e3
+        results.append({"kernel": name, "shape": unit_note, "us": round(us, 2), "bytes": nbytes, "GB/s": round(gbs, 1),
+                        "frac_of_hbm_peak": round(gbs / peaks["hbm"], 3)})
+
+    # (4) unmask step: 16 requests x 32 rows of bf16 logits over the Dream vocabulary (one launch per request block,
+    # as the engine issues them); 8 sets of 16 x 9.7 MB
+    rows = 32
+    logit_sets = [torch.randn(16, rows, vocab, device=device, dtype=torch.bfloat16, generator=g) for _ in range(2)]
+    ids = torch.full((rows,), vocab - 1, dtype=torch.int64, device=device)
+    last = torch.randn(vocab, device=device, dtype=torch.bfloat16, generator=g)
+
+    ids_init = ids.clone()
+    ids_init[0] = 5
+
+    def unmask(i):
+        ids.copy_(ids_init)
+        ops.unmask_step(logit_sets[i % 2][i % 16], ids, mask_token_id=vocab - 1, threshold=0.9, last_logit=last, shift=True,
+                        softmax_dtype=torch.float32)
+    timed("unmask_kernel (+ a 256-byte copy that resets the block)", "[32, 152064] bf16 logits, one block", rows * vocab * 2, unmask, 32)
+
+    # (2a) self-information tail: 8 chunks x 66 label rows of bf16 logits
+    n_chunks, n_lab = 8, 66
+    label_sets = [torch.randn(n_chunks * n_lab, vocab, device=device, dtype=torch.bfloat16, generator=g) for _ in range(2)]
+    labels = torch.randint(0, vocab, (n_lab,), device=device, generator=g)
+    timed("self_info_nll_kernel", "[8 x 66, 152064] bf16 label rows", n_chunks * n_lab * vocab * 2,
+          lambda i: ops.self_information_scores(label_sets[i % 2], labels, n_chunks), 2)
+    del logit_sets, label_sets
+
+    # (5) KV page write: the 4193 rows of the joint prefill of one layer, K and V, read + write
+    n_tok = 4193
+    pool_pages = 640                                   # 2 x 335 MB per pool: rotating 16 disjoint slot sets sweeps it
+    k_cache = torch.zeros(pool_pages, page, hkv, d, device=device, dtype=torch.bfloat16)
+    v_cache = torch.zeros_like(k_cache)
+    kv_sets = [torch.randn(n_tok, 2 * hkv, d, device=device, dtype=torch.bfloat16, generator=g) for _ in range(16)]
+    slot_sets = [(torch.randperm(40 * page, device=device, generator=g)[:n_tok] + i * 40 * page).to(torch.int32) for i in range(16)]
+    timed("store_unified_vec16_kernel", "4193 rows x (K + V) x 4 heads x 128, scattered slots", n_tok * 2 * hkv * d * 2 * 2,
+          lambda i: ops.store_kvcache_unified_layout(kv_sets[i][:, :hkv], kv_sets[i][:, hkv:], k_cache, v_cache, slot_sets[i], "diffusion_lm"), 16)
+
+    # PD snapshot / load of one layer plane: gather and scatter of 4161 prompt rows
+    page_sets = [torch.randperm(pool_pages, device=device, generator=g)[:17].to(torch.int32) for _ in range(16)]
+    n_rows = 4161
+    timed("page_copy_kernel (gather)", "4161 rows x 4 heads x 128 out of 17 pages", n_rows * hkv * d * 2 * 2,
+          lambda i: ops.gather_pages(k_cache, page_sets[i], n_rows), 16)
+    dense = torch.randn(n_rows, hkv, d, device=device, dtype=torch.bfloat16, generator=g)
+    timed("page_copy_kernel (scatter)", "4161 rows x 4 heads x 128 into 17 pages", n_rows * hkv * d * 2 * 2,
+          lambda i: ops.scatter_pages(dense, k_cache, page_sets[i]), 16)
+
+    # (2c) eviction scorer of one (chunk, layer): 8 window rows against prefix + chunk + window keys, 28/4 heads
+    length, c_len, w = 1 + 1024 + 8, 1024, 8
+    qk_sets = [(torch.randn(length, HQ, d, device=device, dtype=torch.bfloat16, generator=g),
+                torch.randn(length, hkv, d, device=device, dtype=torch.bfloat16, generator=g)) for _ in range(8)]
+    ev_bytes = length * hkv * d * 2 + w * HQ * d * 2 + HQ * c_len * 4
+    timed("evict_logits + evict_reduce kernels", "L = 1033 keys, 8 query rows, 28/4 heads -> [28, 1024] fp32", ev_bytes,
+          lambda i: ops.query_to_chunk_attention_scores(qk_sets[i][0], qk_sets[i][1], prefix_len=1, chunk_len=c_len, query_len=w,
+                                                        scale=d ** -0.5, reduce_mode="sum", attention_mask="causal"), 8)
+    head_scores = torch.rand(28, HQ, c_len, device=device, generator=g)
+    timed("evict_select kernel (pool, reduce, rank)", "[28 layers, 28 heads, 1024] fp32 -> 256 kept per (layer, KV head)",
+          head_scores.numel() * 4 + 28 * hkv * 256 * 8,
+          lambda i: ops.evict_select(head_scores, num_kv_heads=hkv, keep_count=256, per_head=True), 1)
+    return {
+        "metric": "achieved_hbm_gb_per_s", "value": None, "unit": "GB/s", "n_gpus": 1, "steps": max(20, min(args.steps, 200)),
+        "warmup": max(3, args.warmup), "higher_is_better": True, "dtype": "bf16", "data": "synthetic",
+        "config": {"workload": "byte_kernels: each HBM-bound kernel of the path at Dream-7B shapes, inputs rotated so that no launch "
+                               "finds them in L2 (except evict_select, whose 3.2 MB input is L2-resident by design)"},
+        "hbm_peak": peaks["hbm"], "peak_source": peaks["source"], "kernels": results,
+    }
+
+
 def run_step_breakdown(args, local_rank: int):
     """Where one denoise step of Dream-7B (32 block rows against 4161 cached tokens, bf16) spends its time: each group
     of launches captured in a CUDA graph of its own and replayed, CUDA-event timed. One GPU."""
@@ -618,7 +722,7 @@ def main():
     ap.add_argument("--steps", type=int, default=200)
     ap.add_argument("--warmup", type=int, default=10)
     ap.add_argument("--impl", default="native", choices=["native", "reference"])
-    ap.add_argument("--workload", default="op", choices=["op", "op_mha_decode", "dream7b_8k", "dream7b_32k", "dream7b_step", "dream7b_decode_batch"],
+    ap.add_argument("--workload", default="op", choices=["op", "op_mha_decode", "byte_kernels", "dream7b_8k", "dream7b_32k", "dream7b_step", "dream7b_decode_batch"],
                     help="op (default): BASELINE configs[1], the op-level decode attention; op_mha_decode: the same kernel on an HBM-bound "
                          "MHA shape; the others time whole requests")
     ap.add_argument("--concurrent", type=int, default=16, help="requests per GPU that share a denoise step (dream7b_decode_batch)")
@@ -645,6 +749,8 @@ def main():
             line = run_native(args, rank, world, local_rank)
         elif args.workload == "op_mha_decode":
             line = run_mha_decode_attention(args, rank, world, local_rank)
+        elif args.workload == "byte_kernels":
+            line = run_byte_kernels(args, local_rank) if rank == 0 else None
         elif args.workload == "dream7b_decode_batch":
             line = run_decode_batch(args, rank, world, local_rank)
         elif args.workload == "dream7b_step":

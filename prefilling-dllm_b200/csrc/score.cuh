@@ -238,15 +238,35 @@ self_info_nll_kernel(const T* __restrict__ rows, int64_t row_stride, int n_label
   constexpr int VEC = Vec16<T>::N;
   float mx = -INFINITY, sm = 0.f;
   auto feed = [&](float x) {
-    if (x > mx) { sm = sm * expf(mx - x) + 1.f; mx = x; } else sm += expf(x - mx);
+    if (x > mx) { sm = sm * expf(mx - x) + 1.f; mx = x; } else if (mx > -INFINITY) sm += expf(x - mx);
+  };
+  // one rescale per 16-byte vector instead of one branch per element
+  auto feed_vec = [&](const float* f) {
+    float vm = f[0];
+#pragma unroll
+    for (int j = 1; j < VEC; ++j) vm = fmaxf(vm, f[j]);
+    if (vm > mx) { sm *= expf(mx - vm); mx = vm; }
+    if (mx > -INFINITY) {
+#pragma unroll
+      for (int j = 0; j < VEC; ++j) sm += expf(f[j] - mx);
+    }
   };
   if ((reinterpret_cast<uintptr_t>(row) & 15) == 0) {
     const int64_t nvec = vocab / VEC;
-    for (int64_t v = tid; v < nvec; v += kScoreThreads) {
+    // four 16-byte loads in flight per thread: one row is 300 KB and a CTA streams it alone
+    constexpr int kInFlight = 4;
+    int64_t v = tid;
+    for (; v + (kInFlight - 1) * kScoreThreads < nvec; v += kInFlight * kScoreThreads) {
+      float f[kInFlight][VEC];
+#pragma unroll
+      for (int u = 0; u < kInFlight; ++u) Vec16<T>::load(row + (v + u * kScoreThreads) * VEC, f[u]);
+#pragma unroll
+      for (int u = 0; u < kInFlight; ++u) feed_vec(f[u]);
+    }
+    for (; v < nvec; v += kScoreThreads) {
       float f[VEC];
       Vec16<T>::load(row + v * VEC, f);
-#pragma unroll
-      for (int j = 0; j < VEC; ++j) feed(f[j]);
+      feed_vec(f);
     }
     for (int64_t i = nvec * VEC + tid; i < vocab; i += kScoreThreads) feed(to_f32<T>(row[i]));
   } else {
