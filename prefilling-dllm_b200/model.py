@@ -12,6 +12,8 @@ written with.
 
 from __future__ import annotations
 
+import gc
+
 import json
 import os
 import threading
@@ -471,8 +473,18 @@ class BlockStepRunner:
                     graph = torch.cuda.CUDAGraph()
                     # torch keeps ONE default capture stream per process, created on whichever device captured first:
                     # with engines on several GPUs in one process the capture stream has to be this device's own
-                    with torch.cuda.graph(graph, stream=torch.cuda.Stream(device=self.m.device)):
-                        e.left = self._step()
+                    # Python's cycle collector may run at any allocation; if it finalises an older model's graphs or
+                    # tensors in the middle of the capture, their cudaFree invalidates it. Collect now, then keep the
+                    # collector off until the capture has ended.
+                    gc_was_on = gc.isenabled()
+                    gc.collect()
+                    gc.disable()
+                    try:
+                        with torch.cuda.graph(graph, stream=torch.cuda.Stream(device=self.m.device)):
+                            e.left = self._step()
+                    finally:
+                        if gc_was_on:
+                            gc.enable()
                     e.graph = graph                  # capturing records the launches without running them
                 e.graph.replay()
                 left = e.left
