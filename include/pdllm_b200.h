@@ -166,6 +166,17 @@ int pdllm_unmask_step(const void* logits, int64_t logits_stride, const void* las
                       float threshold, int conf_dtype, int32_t* out_counts, float* out_conf,
                       int64_t* out_x0, void* workspace, int64_t workspace_bytes, void* stream);
 
+/* The same step for `batch` blocks in ONE launch (requests that share a denoise step, as the engine's decode of
+ * several sequences does, fastdllm_engine.py:2133-2157 run per sequence there). Request z reads logits rows at
+ * logits + z * batch_stride (elements), its last logit at last_logit + z * last_stride, its ids at
+ * block_ids + z * block_len; out_counts is [batch][3], out_conf / out_x0 are [batch][block_len]; the workspace holds
+ * batch * pdllm_unmask_workspace_bytes(block_len) bytes, zero-initialised once by the caller. batch <= 65535. */
+int pdllm_unmask_step_batched(const void* logits, int64_t logits_stride, int64_t batch_stride, const void* last_logit,
+                              int64_t last_stride, int dtype, int batch, int block_len, int64_t vocab, int shift,
+                              int64_t* block_ids, int64_t mask_id, float threshold, int conf_dtype,
+                              int32_t* out_counts, float* out_conf, int64_t* out_x0, void* workspace,
+                              int64_t workspace_bytes, void* stream);
+
 /* Same step as pdllm_unmask_step, for callers that cannot hand over device scratch. It has no counterpart in the
  * reference. Some hosts of the decode loop have given every byte of device memory they may use to the KV page pool
  * and run the loop under a rule of "no allocation after start-up" (an allocation there can fail, and cudaMalloc

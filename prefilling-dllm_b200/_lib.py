@@ -79,6 +79,8 @@ _SIGNATURES = {
     "pdllm_unmask_workspace_bytes": (c_int64, [c_int]),
     "pdllm_unmask_step": (c_int, [c_void_p, c_int64, c_void_p, c_int, c_int, c_int64, c_int, c_void_p, c_int64, c_float,
                                   c_int, c_void_p, c_void_p, c_void_p, c_void_p, c_int64, c_void_p]),
+    "pdllm_unmask_step_batched": (c_int, [c_void_p, c_int64, c_int64, c_void_p, c_int64, c_int, c_int, c_int, c_int64, c_int, c_void_p,
+                                          c_int64, c_float, c_int, c_void_p, c_void_p, c_void_p, c_void_p, c_int64, c_void_p]),
     "pdllm_unmask_step_static": (c_int, [c_void_p, c_int64, c_void_p, c_int, c_int, c_int64, c_int, c_void_p, c_int64, c_float,
                                          c_int, c_void_p, c_void_p, c_void_p, c_void_p]),
     "pdllm_self_information_scores": (c_int, [c_void_p, c_int64, c_int, c_int, c_int, c_int64, c_void_p, c_void_p,

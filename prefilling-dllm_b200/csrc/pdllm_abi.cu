@@ -178,18 +178,28 @@ int pdllm_unmask_step(const void* logits, int64_t logits_stride, const void* las
                       int block_len, int64_t vocab, int shift, int64_t* block_ids, int64_t mask_id,
                       float threshold, int conf_dtype, int32_t* out_counts, float* out_conf,
                       int64_t* out_x0, void* workspace, int64_t workspace_bytes, void* stream) {
+  return pdllm_unmask_step_batched(logits, logits_stride, 0, last_logit, 0, dtype, 1, block_len, vocab, shift, block_ids, mask_id,
+                                   threshold, conf_dtype, out_counts, out_conf, out_x0, workspace, workspace_bytes, stream);
+}
+
+int pdllm_unmask_step_batched(const void* logits, int64_t logits_stride, int64_t batch_stride, const void* last_logit,
+                              int64_t last_stride, int dtype, int batch, int block_len, int64_t vocab, int shift,
+                              int64_t* block_ids, int64_t mask_id, float threshold, int conf_dtype, int32_t* out_counts,
+                              float* out_conf, int64_t* out_x0, void* workspace, int64_t workspace_bytes, void* stream) {
+  if (batch < 0 || batch > 65535) return fail(PDLLM_E_INVALID, "unmask_step: batch %d must be in [0, 65535]", batch);
+  if (batch == 0) return 0;
   if (block_len <= 0 || block_len > kUnmaskMaxBlock || vocab <= 0 || vocab >= (1ll << 31))
     return fail(PDLLM_E_INVALID, "unmask_step: block_len %d must be in [1,%d], vocab %lld in [1, 2^31)", block_len, kUnmaskMaxBlock, (long long)vocab);
   if (!logits || !block_ids) return fail(PDLLM_E_INVALID, "unmask_step: null pointer");
   if (conf_dtype != PDLLM_F32 && conf_dtype != PDLLM_BF16 && conf_dtype != PDLLM_F16) return fail(PDLLM_E_INVALID, "unmask_step: bad conf_dtype %d", conf_dtype);
-  if (!workspace || workspace_bytes < pdllm_unmask_workspace_bytes(block_len))
-    return fail(PDLLM_E_WORKSPACE, "unmask_step: workspace of %lld bytes required", (long long)pdllm_unmask_workspace_bytes(block_len));
-  dim3 grid(kUnmaskChunks, block_len);
+  if (!workspace || workspace_bytes < batch * pdllm_unmask_workspace_bytes(block_len))
+    return fail(PDLLM_E_WORKSPACE, "unmask_step: workspace of %lld bytes required", (long long)(batch * pdllm_unmask_workspace_bytes(block_len)));
+  dim3 grid(kUnmaskChunks, block_len, batch);
   return dispatch_dtype(dtype, [&](auto* tag) -> int {
     using T = std::remove_pointer_t<decltype(tag)>;
     unmask_kernel<T><<<grid, kUnmaskThreads, 0, as_stream(stream)>>>(
         static_cast<const T*>(logits), logits_stride, static_cast<const T*>(last_logit), block_len, vocab, shift, block_ids, mask_id,
-        threshold, conf_dtype, out_counts, out_conf, out_x0, static_cast<float*>(workspace));
+        threshold, conf_dtype, out_counts, out_conf, out_x0, static_cast<float*>(workspace), batch_stride, last_stride);
     return check_launch("unmask_kernel");
   });
 }

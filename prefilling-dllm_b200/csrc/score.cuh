@@ -40,7 +40,18 @@ __global__ void __launch_bounds__(kUnmaskThreads)
 unmask_kernel(const T* __restrict__ logits, int64_t stride, const T* __restrict__ last_logit, int block_len,
               int64_t vocab, int shift, int64_t* __restrict__ block_ids, int64_t mask_id, float threshold,
               int conf_dtype, int32_t* __restrict__ out_counts, float* __restrict__ out_conf,
-              int64_t* __restrict__ out_x0, float* __restrict__ ws) {
+              int64_t* __restrict__ out_x0, float* __restrict__ ws, int64_t batch_stride, int64_t last_stride) {
+  // blockIdx.z: one block of slots per request, each with its own logits rows, ids, outputs and scratch
+  {
+    const int64_t z = blockIdx.z;
+    logits += z * batch_stride;
+    if (last_logit != nullptr) last_logit += z * last_stride;
+    block_ids += z * block_len;
+    if (out_counts != nullptr) out_counts += z * 3;
+    if (out_conf != nullptr) out_conf += z * block_len;
+    if (out_x0 != nullptr) out_x0 += z * block_len;
+    ws += z * unmask_ws_words(block_len);
+  }
   float* pmax = ws;
   float* psum = pmax + block_len * kUnmaskChunks;
   int* pidx = reinterpret_cast<int*>(psum + block_len * kUnmaskChunks);

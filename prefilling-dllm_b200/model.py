@@ -457,9 +457,10 @@ class BlockStepRunner:
         e, n = self.e, self.n
         logits, _ = self.m.forward(e.block, e.positions, cu_seqlens=e.cu, max_query_len=n, slot_mapping=e.slots, causal=False,
                                    **self.kwargs)
-        left = [ops.unmask_step(logits[i * n:(i + 1) * n], self.blocks[i], last_logit=None if e.last_logit is None else e.last_logit[i],
-                                **self.unmask)[2] for i in range(self.batch)]
-        return torch.stack(left)
+        # one launch for the blocks of all requests
+        counts = ops.unmask_step_batched(logits.view(self.batch, n, -1), e.block.view(self.batch, n), last_logit=e.last_logit,
+                                         **self.unmask)
+        return counts[:, 2]
 
     def run(self) -> int:
         """One step for every request; returns the total number of MASK slots left (per request: `.remaining`)."""

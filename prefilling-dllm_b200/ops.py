@@ -370,6 +370,37 @@ def unmask_step(logits: torch.Tensor, block_ids: torch.Tensor, *, mask_token_id:
     return counts
 
 
+def unmask_step_batched(logits: torch.Tensor, block_ids: torch.Tensor, *, mask_token_id: int, threshold: float,
+                        last_logit: Optional[torch.Tensor] = None, shift: bool = True,
+                        softmax_dtype: Optional[torch.dtype] = None) -> torch.Tensor:
+    """`unmask_step` for several requests that share a denoise step, in one launch.
+
+    logits `[batch, block_len, vocab]` (any batch stride, contiguous rows), block_ids int64 `[batch, block_len]` contiguous
+    (updated in place), last_logit `[batch, vocab]` or None. Returns int32 `[batch, 3]` counts on the device.
+    """
+    device = _require_cuda(logits, block_ids)
+    if logits.dim() != 3 or logits.stride(2) != 1:
+        raise ValueError(f"logits must be [batch, block_len, vocab] with contiguous rows, got {tuple(logits.shape)}")
+    batch, block_len, vocab = logits.shape
+    if block_ids.dtype != torch.int64 or tuple(block_ids.shape) != (batch, block_len) or not block_ids.is_contiguous():
+        raise ValueError("block_ids must be a contiguous int64 [batch, block_len] tensor")
+    last_stride = 0
+    if last_logit is not None:
+        if tuple(last_logit.shape) != (batch, vocab) or last_logit.dtype != logits.dtype or last_logit.stride(1) != 1:
+            raise ValueError("last_logit must be [batch, vocab] of the logits dtype with contiguous rows")
+        last_stride = last_logit.stride(0)
+    conf_dtype = dtype_code(softmax_dtype if softmax_dtype is not None else logits.dtype)
+    lib = _lib.load()
+    ws_bytes = batch * int(lib.pdllm_unmask_workspace_bytes(block_len))
+    ws = _workspace(device, f"unmask{block_len}x{batch}", ws_bytes, zero=True)
+    counts = torch.empty((batch, 3), dtype=torch.int32, device=device)
+    check(lib.pdllm_unmask_step_batched(logits.data_ptr(), logits.stride(1), logits.stride(0), _ptr(last_logit), last_stride,
+                                        dtype_code(logits.dtype), batch, block_len, vocab, 1 if shift else 0, block_ids.data_ptr(),
+                                        int(mask_token_id), float(threshold), conf_dtype, counts.data_ptr(), None, None,
+                                        ws.data_ptr(), ws.numel(), _stream(device)))
+    return counts
+
+
 # ---------------------------------------------------------------------------------------------------
 # (2) scoring, selection, eviction
 # ---------------------------------------------------------------------------------------------------

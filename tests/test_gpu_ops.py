@@ -429,6 +429,38 @@ def test_unmask_step_matches_reference_rule(ops, cuda_device, mode):
     assert before - after >= 2  # the threshold branch fired, not only the always-accepted top slot
 
 
+@pytest.mark.parametrize("mode", ["engine_fp32", "eval_bf16", "llada_noshift"])
+def test_unmask_step_batched_equals_per_request_steps(ops, cuda_device, mode):
+    """Several requests in one launch: each block must come out exactly as the oracle's single-request step gives it,
+    with its own last logit, its own ids and its own counts; repeated steps reuse the (self-clearing) workspace."""
+    g = torch.Generator().manual_seed(33)
+    batch, block_len, vocab, mask_id = 5, 32, 4099, 4098
+    dtype = torch.bfloat16 if mode == "eval_bf16" else torch.float32
+    softmax_dtype = torch.float32 if mode == "engine_fp32" else None
+    shift = mode != "llada_noshift"
+    logits = torch.stack([_peaked_logits(g, block_len, vocab, [0.95 if (r + b) % 5 == 0 else None for r in range(block_len)])
+                          for b in range(batch)]).to(dtype)
+    last = torch.randn(batch, vocab, generator=g).to(dtype)
+    ids = torch.full((batch, block_len), mask_id, dtype=torch.int64)
+    ids[:, 0] = torch.arange(batch) + 3
+    ids[2, 10:20] = 7                   # a partly filled block
+    ids[4, :] = 9                       # a finished block: no candidates
+    dev_ids = ids.to(cuda_device)
+    dev_logits, dev_last = logits.to(cuda_device), last.to(cuda_device)
+    ref = ids.clone()
+    for step in range(3):
+        counts = ops.unmask_step_batched(dev_logits, dev_ids, mask_token_id=mask_id, threshold=0.9, last_logit=dev_last if shift else None,
+                                         shift=shift, softmax_dtype=softmax_dtype)
+        for b in range(batch):
+            before = int((ref[b] == mask_id).sum())
+            ref[b], _, _ = oracle.unmask_step(logits[b], ref[b], mask_token_id=mask_id, threshold=0.9, last_logit=last[b] if shift else None,
+                                              shift=shift, softmax_dtype=softmax_dtype)
+            after = int((ref[b] == mask_id).sum())
+            assert counts[b].cpu().tolist() == [before, before - after, after], (step, b)
+        assert torch.equal(dev_ids.cpu(), ref), step
+    ops.check_status(cuda_device)
+
+
 def test_unmask_step_flat_logits_make_exactly_one_step(ops, cuda_device):
     # random-init models: max probability ~ 1/V, so exactly the most confident slot is filled each step
     g = torch.Generator().manual_seed(31)
