@@ -385,6 +385,36 @@ def run_request(args, rank: int, world: int, local_rank: int):
         return None
     ms_per_request, decode_s = float(ms.item()), float(dec.item())
     requests_in_flight = 1 if long_ctx else world
+    naive = None
+    if args.naive and world == 1:
+        # What the path avoids (the comparison the reference's README quotes): no selection, no cache — every denoise
+        # step re-encodes [BOS ‖ context ‖ query ‖ generated ‖ block] bidirectionally on the same model and kernels; the LM
+        # head runs on the block's 32 (shifted) rows only. One request, CUDA-event timed.
+        mask_id = rt._mask_token_id()
+        prompt = list(rt.bos_ids()) + context + query
+        torch.cuda.synchronize(device)
+        n_start, n_stop = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        n_start.record()
+        done, n_steps = [], 0
+        with torch.inference_mode():
+            while len(done) < new_tokens:
+                blen = min(32, new_tokens - len(done))
+                block = torch.full((blen,), mask_id, dtype=torch.int64, device=device)
+                base = len(prompt) + len(done)
+                while bool((block == mask_id).any()):
+                    ids = torch.cat([rt.model.ids_tensor(prompt + done), block])
+                    rows = list(range(base - 1, base + blen - 1))
+                    logits, _ = rt._forward_packed([[0] * (base + blen)], [list(range(base + blen))], causal=False, ids_tensor=ids,
+                                                   logit_rows=rows)
+                    ops.unmask_step(logits, block, mask_token_id=mask_id, threshold=0.9, shift=False)
+                    n_steps += 1
+                done += block.tolist()
+        n_stop.record()
+        torch.cuda.synchronize(device)
+        ops.check_status(device)
+        naive_ms = n_start.elapsed_time(n_stop)
+        naive = {"ms_per_request": naive_ms, "denoise_steps": n_steps, "rows_per_step": len(prompt) + new_tokens,
+                 "speedup_of_this_path": naive_ms / ms_per_request}
     return {
         "metric": "request_latency_ms", "value": ms_per_request, "unit": "ms", "n_gpus": world, "steps": steps, "warmup": warmup,
         "ms_per_step": ms_per_request, "higher_is_better": False, "scaling": "strong" if long_ctx else "weak", "vs_baseline": None,
@@ -396,6 +426,7 @@ def run_request(args, rank: int, world: int, local_rank: int):
         "decode_tok_per_s": requests_in_flight * new_tokens / decode_s if decode_s > 0 else None,
         "decode_ms_per_request": decode_s * 1e3,
         "requests_per_s": requests_in_flight * 1e3 / ms_per_request,
+        "full_reencode_every_step": naive,
         "clocks": clocks,
     }
 
@@ -725,6 +756,8 @@ def main():
     ap.add_argument("--workload", default="op", choices=["op", "op_mha_decode", "byte_kernels", "dream7b_8k", "dream7b_32k", "dream7b_step", "dream7b_decode_batch"],
                     help="op (default): BASELINE configs[1], the op-level decode attention; op_mha_decode: the same kernel on an HBM-bound "
                          "MHA shape; the others time whole requests")
+    ap.add_argument("--naive", action="store_true", help="dream7b_8k / dream7b_32k on one GPU: also time one request that "
+                    "re-encodes the full context at every denoise step")
     ap.add_argument("--concurrent", type=int, default=16, help="requests per GPU that share a denoise step (dream7b_decode_batch)")
     args = ap.parse_args()
 
