@@ -442,12 +442,18 @@ def run_decode_batch(args, rank: int, world: int, local_rank: int):
 
     device = torch.device("cuda", local_rank)
     torch.cuda.set_device(device)
-    n_req, prompt_len, block = max(1, args.concurrent), 4193, 32
+    # llada8b_decode_batch: the decode side of BASELINE configs[4] — LLaDA-8B architecture (32 MHA heads, un-shifted logits),
+    # each request 4 selected chunks of 2048 tokens + a 64-token query in pages
+    llada = args.workload == "llada8b_decode_batch"
+    arch = DreamArch.llada_8b() if llada else DreamArch.dream_7b()
+    name = "LLaDA-8B" if llada else "Dream-7B"
+    n_req, prompt_len, block = max(1, args.concurrent), (4 * 2048 + 64 if llada else 4193), 32
     pages_per_req = -(-prompt_len // 256) + 1
-    model = PagedDreamModel.random_init(DreamArch.dream_7b(), device=device, dtype=torch.bfloat16, num_pages=n_req * pages_per_req + 8, page_size=256)
-    engine = FastDLLMDreamEngine(model, max_model_len=8192, block_length=block, mask_token_id=151666, threshold=0.9, enforce_eager=False)
+    model = PagedDreamModel.random_init(arch, device=device, dtype=torch.bfloat16, num_pages=n_req * pages_per_req + 8, page_size=256)
+    engine = FastDLLMDreamEngine(model, max_model_len=16384, block_length=block, mask_token_id=arch.mask_token_id, threshold=0.9,
+                                 enforce_eager=False)
     gen = torch.Generator().manual_seed(100 + rank)
-    prompts = [torch.randint(0, 151000, (prompt_len,), generator=gen).tolist() for _ in range(n_req)]
+    prompts = [torch.randint(0, 126000, (prompt_len,), generator=gen).tolist() for _ in range(n_req)]
 
     def one_round():
         records = [engine.prefill_to_pd_record(p, max_new_tokens=block) for p in prompts]     # prefix-cache hits after the first round
@@ -483,7 +489,7 @@ def run_decode_batch(args, rank: int, world: int, local_rank: int):
         "metric": "decode_tok_per_s", "value": world * n_req * block / seconds, "unit": "tok/s", "n_gpus": world, "steps": steps,
         "warmup": warmup, "ms_per_step": seconds * 1e3, "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
         "data": "synthetic",
-        "config": {"workload": f"dream7b_decode_batch: {n_req} concurrent requests per GPU, Dream-7B architecture random init, {prompt_len}-token "
+        "config": {"workload": f"{args.workload}: {n_req} concurrent requests per GPU, {name} architecture random init, {prompt_len}-token "
                                f"prompt in pages, one {block}-token block each, threshold 0.9, greedy; {n_steps} shared denoise steps per block",
                    "parallelism": f"dp{world} (replicas over requests, no data-path collective)"},
         "ms_per_denoise_step": seconds * 1e3 / max(1, n_steps), "clocks": clocks,
@@ -753,7 +759,8 @@ def main():
     ap.add_argument("--steps", type=int, default=200)
     ap.add_argument("--warmup", type=int, default=10)
     ap.add_argument("--impl", default="native", choices=["native", "reference"])
-    ap.add_argument("--workload", default="op", choices=["op", "op_mha_decode", "byte_kernels", "dream7b_8k", "dream7b_32k", "dream7b_step", "dream7b_decode_batch"],
+    ap.add_argument("--workload", default="op", choices=["op", "op_mha_decode", "byte_kernels", "dream7b_8k", "dream7b_32k", "dream7b_step", "dream7b_decode_batch",
+                             "llada8b_decode_batch"],
                     help="op (default): BASELINE configs[1], the op-level decode attention; op_mha_decode: the same kernel on an HBM-bound "
                          "MHA shape; the others time whole requests")
     ap.add_argument("--naive", action="store_true", help="dream7b_8k / dream7b_32k on one GPU: also time one request that "
@@ -784,7 +791,7 @@ def main():
             line = run_mha_decode_attention(args, rank, world, local_rank)
         elif args.workload == "byte_kernels":
             line = run_byte_kernels(args, local_rank) if rank == 0 else None
-        elif args.workload == "dream7b_decode_batch":
+        elif args.workload in ("dream7b_decode_batch", "llada8b_decode_batch"):
             line = run_decode_batch(args, rank, world, local_rank)
         elif args.workload == "dream7b_step":
             line = run_step_breakdown(args, local_rank) if rank == 0 else None

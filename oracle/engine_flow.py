@@ -48,8 +48,10 @@ def selection_mask(mode: str, seq_len: int, prefix_len: int, chunk_len: int) -> 
 
 
 def denoise_block(model, past, key_positions: Sequence[int], block_positions: Sequence[int], first_token: int,
-                  last_context_logit: torch.Tensor, *, mask_id: int, threshold: float) -> Tuple[List[int], int]:
-    """:2133-2157 — every step forwards the whole block against `past` (concatenated, not stored)."""
+                  last_context_logit: torch.Tensor, *, mask_id: int, threshold: float, shift: bool = True) -> Tuple[List[int], int]:
+    """:2133-2157 — every step forwards the whole block against `past` (concatenated, not stored). `shift=False`: the
+    un-shifted read-out of the eval class's LLaDA backend (fastdllm_parallelcomp.py:1017-1024); the reference engine has
+    no such model."""
     block = torch.full((len(block_positions),), mask_id, dtype=torch.long)
     block[0] = first_token
     steps = 0
@@ -59,12 +61,12 @@ def denoise_block(model, past, key_positions: Sequence[int], block_positions: Se
             steps += 1
             out = model(block.unsqueeze(0), attention_mask=None, position_ids=pos, past_key_values=past, use_cache=False)
             block, _, _ = O.unmask_step(out.logits[0], block, mask_token_id=mask_id, threshold=threshold,
-                                        last_logit=last_context_logit, softmax_dtype=torch.float32)
+                                        last_logit=last_context_logit if shift else None, shift=shift, softmax_dtype=torch.float32)
     return block.tolist(), steps
 
 
 def prefill_and_decode(model, prompt_ids: Sequence[int], *, block_length: int, mask_id: int, threshold: float,
-                       prompt_positions: Optional[Sequence[int]] = None, keep: Optional[Sequence[int]] = None):
+                       prompt_positions: Optional[Sequence[int]] = None, keep: Optional[Sequence[int]] = None, shift: bool = True):
     """prefill_to_pd_record + decode_from_pd_record. `keep`: ONE ascending index list applied to every layer and KV
     head (post-hoc eviction with head-independent indices); keys keep the rotation of their original position and
     the block moves to max(kept positions) + 1 (:1953-1958).
@@ -77,14 +79,14 @@ def prefill_and_decode(model, prompt_ids: Sequence[int], *, block_length: int, m
     with torch.no_grad():
         out = model(torch.tensor([prompt_ids + [mask_id] * block_length]), attention_mask=None, position_ids=_positions(full_pos),
                     use_cache=True)
-    last = out.logits[0, n - 1]
+    last = out.logits[0, n - 1] if shift else out.logits[0, n]   # un-shifted: the first MASK slot's own row
     first = int(torch.argmax(last))
     idx = torch.arange(n) if keep is None else torch.tensor(list(keep), dtype=torch.long)
     past = [(k[:, idx], v[:, idx]) for k, v in out.past_key_values]
     key_positions = [prompt_positions[i] for i in idx.tolist()]
     block_start = max(key_positions) + 1
     ids, steps = denoise_block(model, past, key_positions, list(range(block_start, block_start + block_length)), first, last,
-                               mask_id=mask_id, threshold=threshold)
+                               mask_id=mask_id, threshold=threshold, shift=shift)
     return dict(first_token=first, last_context_logit=last, token_ids=ids, n_diff_steps=steps, past=past, key_positions=key_positions)
 
 

@@ -534,9 +534,13 @@ class FastDLLMDreamEngine:
                 full_ids = prompt_ids + [self.mask_token_id] * decode_len
                 slots = slots_for(prompt_page_ids, 0, full_prompt_len, self.page_size) + slots_for(block_page_ids, 0, decode_len, self.page_size)
                 # Dream reads token p from logits[p - 1]: the first block token and the "last context logit" are both the
-                # row of the last prompt token, the only row the LM head is run on
+                # row of the last prompt token, the only row the LM head is run on. An un-shifted architecture (LLaDA) reads
+                # token p from logits[p]: the row kept is the first MASK slot's own, which is also what the all-MASK
+                # replace forward of a prefix-cache hit would give for that slot. (The reference engine has no un-shifted
+                # model; this follows its eval class, fastdllm_parallelcomp.py:1017-1024, 2385-2397.)
+                first_row = full_prompt_len - 1 if self.model.arch.logit_shift else full_prompt_len
                 logits, _ = self._forward(full_ids, list(prompt_positions) + prefill_suffix_positions, store_slots=slots,
-                                          logit_rows=[full_prompt_len - 1])
+                                          logit_rows=[first_row])
                 last_context_logit = logits[0].detach()
                 first_token = int(torch.argmax(last_context_logit).item())
                 if keep is not None:
@@ -569,7 +573,7 @@ class FastDLLMDreamEngine:
         remaining = decode_len - 1
         runner = self.model.block_step_runner(block_len=decode_len, positions=block_positions, ctx_page_ids=ctx_page_ids, ctx_len=ctx_len,
                                               mask_token_id=self.mask_token_id, threshold=self.threshold, last_logit=last_context_logit,
-                                              shift=True, softmax_dtype=torch.float32, store_slots=block_slots,
+                                              shift=self.model.arch.logit_shift, softmax_dtype=torch.float32, store_slots=block_slots,
                                               use_graph=not self.config.enforce_eager)
         block = runner.block                          # the step's ids buffer, updated in place by the unmask kernel
         block.fill_(self.mask_token_id)
@@ -642,7 +646,7 @@ class FastDLLMDreamEngine:
                              last_logit=r.last_context_logit, store_slots=slots_for(r.block_page_ids, 0, decode_len, self.page_size))
                         for r in records]
             runner = self.model.batched_step_runner(block_len=decode_len, requests=requests, mask_token_id=self.mask_token_id,
-                                                    threshold=self.threshold, shift=True, softmax_dtype=torch.float32,
+                                                    threshold=self.threshold, shift=self.model.arch.logit_shift, softmax_dtype=torch.float32,
                                                     use_graph=not self.config.enforce_eager)
             for block, r in zip(runner.blocks, records):
                 block.fill_(self.mask_token_id)
@@ -663,6 +667,11 @@ class FastDLLMDreamEngine:
         finally:
             for r in records:
                 self.release_pd_record(r)
+
+    def _require_shifted_logits(self, what: str) -> None:
+        """The selection / chunk-local twins restate Dream's shifted read-out only (the reference engine has no other model)."""
+        if not self.model.arch.logit_shift:
+            raise NotImplementedError(f"{what} is built for architectures with shifted logits (Dream) only")
 
     def release_pd_record(self, record: DreamPrefillRecord) -> None:
         """Release the pages of a record that will not be decoded (reference :2192-2198)."""
@@ -732,6 +741,7 @@ class FastDLLMDreamEngine:
         draft_len = int(max_new_tokens or 0)
         if draft_len <= 0:
             return [], []
+        self._require_shifted_logits("generate_partial_draft_rounds_for_selection")
         prompt_ids = [int(x) for x in prompt_ids]
         p_len = len(prompt_ids)
         if p_len <= 0:
@@ -987,6 +997,7 @@ class FastDLLMDreamEngine:
         if max_new_tokens > self.block_length:
             raise NotImplementedError("FastDLLMDreamEngine chunk-local KV path supports one generation block only. "
                                       f"Got max_new_tokens={max_new_tokens}, block_length={self.block_length}.")
+        self._require_shifted_logits("generate_token_ids_from_chunk_local_kv")
         prefix_ids, prefix_positions = [int(x) for x in prefix_ids], [int(x) for x in prefix_positions]
         query_ids, query_positions = [int(x) for x in query_ids], [int(x) for x in query_positions]
         if len(prefix_ids) != len(prefix_positions):

@@ -94,6 +94,33 @@ def test_pd_split_matches_the_restated_engine(engine, cpu_model):
     assert engine._prefix_cache.evict_one() and engine._prefix_cache.num_free_pages == free0
 
 
+def test_pd_split_with_unshifted_logits(ckpt, cpu_model):
+    """An architecture that reads token p from logits[p] (LLaDA's read-out; same toy weights): the first block token comes
+    from the first MASK slot's own row of the joint prefill, the steps use the un-shifted unmask rule, a prefix-cache hit
+    gives the same record, and the Dream-only selection twins refuse."""
+    import dataclasses
+
+    from oracle import engine_flow as E
+
+    eng = _engine(ckpt, pages=12)
+    eng.model.arch = dataclasses.replace(eng.model.arch, logit_shift=False)
+    prompt = _prompt(500, seed=9)
+    want = E.prefill_and_decode(cpu_model, prompt, block_length=BLOCK, mask_id=MASK, threshold=0.9, shift=False)
+    shifted = E.prefill_and_decode(cpu_model, prompt, block_length=BLOCK, mask_id=MASK, threshold=0.9)
+    assert want["token_ids"] != shifted["token_ids"]          # the two read-outs really differ on this input
+    rec = eng.prefill_to_pd_record(prompt, max_new_tokens=BLOCK)
+    assert rec.first_token_id == want["first_token"]
+    assert torch.allclose(rec.last_context_logit.cpu(), want["last_context_logit"], atol=2e-4)
+    out = eng.decode_from_pd_record(rec, max_new_tokens=BLOCK)
+    assert out.token_ids == want["token_ids"] and out.n_diff_steps == want["n_diff_steps"]
+    again = eng.prefill_to_pd_record(prompt, max_new_tokens=BLOCK)
+    assert again.cached_prefix is not None and again.first_token_id == want["first_token"]
+    both = eng.decode_from_pd_records([again], max_new_tokens=BLOCK)
+    assert both[0].token_ids == want["token_ids"]
+    with pytest.raises(NotImplementedError, match="shifted logits"):
+        eng.generate_partial_draft_rounds_for_selection(prompt, max_new_tokens=4, partial_rounds=1)
+
+
 def test_snapshot_load_and_engine_to_engine_copy(engine, ckpt):
     other = _engine(ckpt, pages=16)
     prompt = _prompt(700, seed=5)
