@@ -189,37 +189,74 @@ def run_native(args, rank: int, world: int, local_rank: int):
     ms_total = start.elapsed_time(stop)
 
     # ---- end to end through the reference-facing op with HOST buffers (e2e) ----
-    pin = {n: host[n].pin_memory() for n in ("q", "k", "v")}
+    # Every step copies its q/k/v rows and block table from pinned host memory, runs the op, and copies the output back to
+    # pinned host memory. The three stages run on three streams over three sets of device buffers, so step i's download,
+    # step i+1's kernel and step i+2's upload overlap (PCIe is full duplex); all of it is inside the timed region.
+    # host rows in the fused [T, Hq + 2 Hkv, D] layout a QKV projection produces: one upload per step; the op takes q, k, v
+    # as strided views of it
+    pin_qkv = torch.cat([host["q"], host["k"], host["v"]], dim=1).contiguous().pin_memory()
     tables_pin = host["tables"].pin_memory()
-    out_host = torch.empty_like(host["q"]).pin_memory()
-    dq, dk, dv = torch.empty_like(dev["q"]), torch.empty_like(dev["k"]), torch.empty_like(dev["v"])
-    dtable = torch.empty_like(dev["tables"][0])
-    h2d = sum(pin[n].numel() * 2 for n in pin) + dtable.numel() * 4
-    d2h = out_host.numel() * 2
+    n_buf = 3
+    bufs = []
+    for _ in range(n_buf):
+        qkv = torch.empty(pin_qkv.shape, dtype=pin_qkv.dtype, device=device)
+        bufs.append(dict(qkv=qkv, q=qkv[:, :HQ], k=qkv[:, HQ:HQ + HKV], v=qkv[:, HQ + HKV:],
+                         table=torch.empty_like(dev["tables"][0]), out=torch.empty_like(dev["q"]),
+                         out_host=torch.empty_like(host["q"]).pin_memory(),
+                         up=torch.cuda.Event(), done=torch.cuda.Event(), down=torch.cuda.Event()))
+    s_up, s_run, s_down = torch.cuda.Stream(device), torch.cuda.Stream(device), torch.cuda.Stream(device)
+    h2d = pin_qkv.numel() * 2 + bufs[0]["table"].numel() * 4
+    d2h = bufs[0]["out_host"].numel() * 2
     e2e_steps = args.steps
 
     def e2e_step(i: int):
-        dq.copy_(pin["q"], non_blocking=True)
-        dk.copy_(pin["k"], non_blocking=True)
-        dv.copy_(pin["v"], non_blocking=True)
-        dtable.copy_(tables_pin[i % N_TABLES], non_blocking=True)
-        ops.diffusion_lm_parallel_flash_decoding(dq, dk, dv, out, "auto", dev["k_cache"], dev["v_cache"], dtable, dev["cu"],
-                                                 dev["seq_lens"], CTX + ROWS, ROWS, 1.0, 1.0, RESP_ROWS, None, None, scale,
+        b = bufs[i % n_buf]
+        torch.cuda.set_stream(s_up)
+        s_up.wait_event(b["down"])            # the buffers' previous output has left the device
+        b["qkv"].copy_(pin_qkv, non_blocking=True)
+        b["table"].copy_(tables_pin[i % N_TABLES], non_blocking=True)
+        b["up"].record(s_up)
+        torch.cuda.set_stream(s_run)
+        s_run.wait_event(b["up"])
+        ops.diffusion_lm_parallel_flash_decoding(b["q"], b["k"], b["v"], b["out"], "auto", dev["k_cache"], dev["v_cache"], b["table"],
+                                                 dev["cu"], dev["seq_lens"], CTX + ROWS, ROWS, 1.0, 1.0, RESP_ROWS, None, None, scale,
                                                  None, True)
-        out_host.copy_(out, non_blocking=True)
+        b["done"].record(s_run)
+        torch.cuda.set_stream(s_down)
+        s_down.wait_event(b["done"])
+        b["out_host"].copy_(b["out"], non_blocking=True)
+        b["down"].record(s_down)
+        torch.cuda.set_stream(stream)
 
+    def join():
+        for st in (s_up, s_run, s_down):
+            stream.wait_stream(st)
+
+    for st in (s_up, s_run, s_down):
+        st.wait_stream(stream)
+    for b in bufs:
+        b["down"].record(s_down)
     for i in range(3):
         e2e_step(i)
+    join()
     torch.cuda.synchronize(device)
     barrier()
     e_start, e_stop = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     e_start.record(stream)
+    for st in (s_up, s_run, s_down):
+        st.wait_stream(stream)
     for i in range(e2e_steps):
         e2e_step(i)
+    join()
     e_stop.record(stream)
     torch.cuda.synchronize(device)
     barrier()
     e2e_ms_total = e_start.elapsed_time(e_stop)
+    # the last step's output, read on the host, must be the kernel's: compare with the device-resident result of the same table
+    step((e2e_steps - 1) % N_TABLES)
+    torch.cuda.synchronize(device)
+    if not torch.equal(bufs[(e2e_steps - 1) % n_buf]["out_host"], out.cpu()):
+        raise RuntimeError("end-to-end output differs from the device-resident run of the same inputs")
     clocks = sampler.stop() if rank == 0 else None
     ops.check_status(device)
 
