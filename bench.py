@@ -49,7 +49,7 @@ FLOPS_PER_STEP = NUM_REQ * 4 * HQ * D * ROWS * (CTX + ROWS)                     
 BYTES_PER_STEP = NUM_REQ * (CTX * 2 * HKV * D * 2 + ROWS * (2 * HQ + 2 * HKV) * D * 2)  # KV pages + q/k/v/out rows
 # dram__bytes_read.sum + dram__bytes_write.sum of one attn_sm100_kernel launch on this workload, from the ncu capture
 # summarised in profiles/attn_sm100_kernel_op_config.md (algorithmic minimum: BYTES_PER_STEP)
-TRAFFIC_BYTES_PER_LAUNCH = 78_066_944
+TRAFFIC_BYTES_PER_LAUNCH = 79_097_088
 WORKLOAD = ("configs[1] op-level paged decode attention: 8 req x (64 query + 32 response rows), 28/4 heads, d128, "
             "page 256, 4 of 32 chunks (4096 ctx tokens) per request via block table, bidirectional, N(0,1) bf16")
 
