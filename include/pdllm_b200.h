@@ -23,7 +23,7 @@
 extern "C" {
 #endif
 
-#define PDLLM_ABI_VERSION 2
+#define PDLLM_ABI_VERSION 3
 
 /* element types of floating-point tensors */
 #define PDLLM_F32 0
@@ -114,8 +114,9 @@ typedef struct pdllm_attn_params {
   const uint8_t* mask;          /* optional bool mask over new rows x new keys, sequence-LOCAL indices */
   int32_t* status;              /* optional device status word */
   void* workspace;              /* split-KV arrival counters + partials; pdllm_attn_workspace_bytes(); 256-byte aligned */
-  void* trace;                  /* optional profiling aid of the tcgen05 kernel: int64 [8 CTAs][64 iterations][16 events]
-                                   of clock64() timestamps, zero-initialised by the caller; NULL (the default) = off */
+  void* trace;                  /* profiling aid of the tcgen05 kernel, read only by a library built with
+                                   -DPDLLM_ENABLE_TRACE (the release build ignores it): int64 [8 CTAs][64 iterations]
+                                   [16 events] of clock64() timestamps, zero-initialised by the caller; NULL = off */
   int64_t workspace_bytes;
   int64_t q_stride, k_stride, v_stride, out_stride; /* row strides, elements */
   int64_t block_table_stride;
@@ -269,12 +270,13 @@ int pdllm_copy_pages(const void* src_cache, const int32_t* src_page_ids, void* d
                      int64_t src_num_pages, int64_t dst_num_pages, int32_t* status, void* stream);
 /* map peer_device's memory into device's address space (idempotent); PDLLM_E_UNSUPPORTED if the GPUs have no peer path */
 int pdllm_enable_peer_access(int device, int peer_device);
-/* per-(KV head) compaction: dst token j of head h := src token keep[h, j]; src and dst page lists may be the
- * same pages (in-place compaction to the front): the kernel stages through `staging`
- * ([keep_count, Hkv, D] elements) so overlapping ranges are safe. */
+/* per-(KV head) compaction: dst token dst_start + j of head h := src token keep[h, j]; src and dst page lists may be
+ * the same pages (in-place compaction to the front): the kernel stages through `staging`
+ * ([keep_count, Hkv, D] elements) so overlapping ranges are safe. src_tokens / dst_tokens: tokens covered by the
+ * two page lists (list length x page_size, or fewer); rows outside them are refused, not written. */
 int pdllm_compact_pages_per_head(void* cache, const int32_t* src_page_ids, const int32_t* dst_page_ids,
                                  const int64_t* keep, int64_t keep_count, int64_t src_tokens,
-                                 int64_t dst_start, int page_size, int num_kv_heads, int head_dim,
+                                 int64_t dst_start, int64_t dst_tokens, int page_size, int num_kv_heads, int head_dim,
                                  int elem_bytes, int64_t num_pages, void* staging, int32_t* status,
                                  void* stream);
 

@@ -270,6 +270,34 @@ def unmask_step(logits: torch.Tensor, block_ids: torch.Tensor, *, mask_token_id:
     return ids, full_conf, x0_full
 
 
+def fixed_step_transfer_counts(masked: int, steps_per_block: int) -> List[int]:
+    """How many slots each step of the fixed-step diffusion sampler transfers (E:fastdllm_parallelcomp.py:2455, 2492-2496):
+    t = linspace(1, 1e-3, steps + 1) in fp32; step i moves int(masks_left * (1 - t[i+1] / t[i])) slots, the last step all
+    that is left; a step that would move none runs no transfer."""
+    timesteps = torch.linspace(1, 1e-3, steps_per_block + 1)
+    out, left = [], int(masked)
+    for step in range(steps_per_block):
+        if left <= 0:
+            break
+        count = int(left * (1 - timesteps[step + 1] / timesteps[step])) if step < steps_per_block - 1 else left
+        out.append(max(0, count))
+        left -= max(0, count)
+    return out
+
+
+def transfer_most_confident(logits: torch.Tensor, block_ids: torch.Tensor, *, mask_token_id: int, count: int,
+                            last_logit: Optional[torch.Tensor] = None, shift: bool = True) -> torch.Tensor:
+    """Fill the `count` most confident masked slots with their arg-max (E:fastdllm_parallelcomp.py:2497-2504 with alg_temp 0,
+    :2548-2552 of the partial draft): confidence = max softmax probability in the logits dtype."""
+    ids = block_ids.clone()
+    _, full_conf, x0_full = unmask_step(logits, ids, mask_token_id=mask_token_id, threshold=2.0, last_logit=last_logit, shift=shift)
+    count = min(int(count), int((ids == mask_token_id).sum()))
+    if count > 0:
+        idx = torch.topk(full_conf.float(), count).indices
+        ids[idx] = x0_full[idx]
+    return ids
+
+
 # --------------------------------------------------------------------------------------------------
 # rows 5-6 / kernels (2a)(2b): self-information score tail and chunk ranking
 # --------------------------------------------------------------------------------------------------

@@ -14,6 +14,7 @@ from ctypes import POINTER, Structure, c_char_p, c_float, c_int, c_int32, c_int6
 PKG_DIR = os.path.dirname(os.path.abspath(__file__))
 LIB_PATH = os.path.join(PKG_DIR, "libpdllm_b200.so")
 
+ABI_VERSION = 3
 # dtype codes
 F32, BF16, F16 = 0, 1, 2
 # cache layouts
@@ -95,7 +96,7 @@ _SIGNATURES = {
     "pdllm_scatter_pages": (c_int, [c_void_p, c_void_p, c_int64, c_int, c_int64, c_int, c_int64, c_void_p, c_void_p, c_void_p]),
     "pdllm_copy_pages": (c_int, [c_void_p, c_void_p, c_void_p, c_void_p, c_int64, c_int64, c_int, c_int64, c_int, c_int64, c_int64, c_void_p, c_void_p]),
     "pdllm_enable_peer_access": (c_int, [c_int, c_int]),
-    "pdllm_compact_pages_per_head": (c_int, [c_void_p, c_void_p, c_void_p, c_void_p, c_int64, c_int64, c_int64, c_int, c_int,
+    "pdllm_compact_pages_per_head": (c_int, [c_void_p, c_void_p, c_void_p, c_void_p, c_int64, c_int64, c_int64, c_int64, c_int, c_int,
                                              c_int, c_int, c_int64, c_void_p, c_void_p, c_void_p]),
     "pdllm_add_rmsnorm": (c_int, [c_void_p, c_void_p, c_void_p, c_void_p, c_int64, c_int, c_int64, c_int64, c_int64, c_float, c_int, c_void_p]),
     "pdllm_rope_inplace": (c_int, [c_void_p, c_void_p, c_void_p, c_int64, c_int, c_int, c_int64, c_int, c_void_p]),
@@ -136,8 +137,8 @@ def load() -> ctypes.CDLL:
             fn = getattr(lib, name)
             fn.restype = restype
             fn.argtypes = argtypes
-        if lib.pdllm_abi_version() != 2:
-            raise ImportError(f"{LIB_PATH} has ABI version {lib.pdllm_abi_version()}, expected 2")
+        if lib.pdllm_abi_version() != ABI_VERSION:
+            raise ImportError(f"{LIB_PATH} has ABI version {lib.pdllm_abi_version()}, expected {ABI_VERSION}")
         _lib = lib
     return _lib
 

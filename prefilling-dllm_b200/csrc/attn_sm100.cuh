@@ -119,7 +119,9 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volati
         const int which = static_cast<int>((smem_u32(bar) & 0x3ff) >> 3);
         const int code = PDLLM_S_WAIT_TIMEOUT | (which << 8) | ((threadIdx.x >> 5) << 16) | (parity << 24);
         report_status(a.status, code);
+#ifdef PDLLM_ENABLE_TRACE
         if (a.trace != nullptr && (threadIdx.x & 31) == 0) a.trace[8 * 64 * 16 - 64 + (threadIdx.x >> 5)] = code;  // per-warp record
+#endif
         return false;
       }
     }
@@ -245,8 +247,13 @@ __host__ __device__ constexpr uint32_t make_idesc(bool bf16, bool b_mn_major, in
          (static_cast<uint32_t>(n >> 3) << 17) | ((kTileM >> 4) << 24);
 }
 
-// Optional timestamps (clock64) of CTA 0..7 for profiling the pipeline: trace[cta][iteration][event].
+// Optional timestamps (clock64) of CTA 0..7 for profiling the pipeline: trace[cta][iteration][event]. Compiled in
+// only with -DPDLLM_ENABLE_TRACE; the release kernel carries no trace code and ignores the pointer.
+#ifdef PDLLM_ENABLE_TRACE
 #define PDLLM_TRACE_ON (a.trace != nullptr)
+#else
+#define PDLLM_TRACE_ON false
+#endif
 constexpr int kTraceEvents = 16;
 constexpr int kTraceIters = 64;
 constexpr int kTraceCtas = 8;

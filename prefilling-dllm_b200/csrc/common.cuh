@@ -120,15 +120,17 @@ struct Vec16<__half> {
 
 inline int dtype_bytes(int dtype) { return dtype == PDLLM_F32 ? 4 : 2; }
 
+// SM count of the CURRENT device (cached per device ordinal; benign race: every writer stores the same value)
 inline int sm_count() {
-  static int cached = 0;
-  if (cached == 0) {
-    int dev = 0;
-    cudaGetDevice(&dev);
-    cudaDeviceGetAttribute(&cached, cudaDevAttrMultiProcessorCount, dev);
-    if (cached <= 0) cached = 148;
+  static int cached[64] = {0};
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return 148;
+  if (cached[dev] == 0) {
+    int n = 0;
+    cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
+    cached[dev] = n > 0 ? n : 148;
   }
-  return cached;
+  return cached[dev];
 }
 
 }  // namespace pdllm

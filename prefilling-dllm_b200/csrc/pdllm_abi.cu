@@ -109,6 +109,11 @@ int pdllm_load_kvcache(const void* k_cache, const void* v_cache, const void* k_n
                        void* k_out, void* v_out, int64_t total_k, int32_t* status, void* stream) {
   if (num_seqs <= 0 || total_k < 0 || page_size <= 0) return fail(PDLLM_E_INVALID, "load_kvcache: bad sizes");
   if (total_k == 0) return 0;
+  if (!k_new || !v_new || !cu_seqlens_q || !cu_seqlens_k || !context_lens || !k_out || !v_out)
+    return fail(PDLLM_E_INVALID, "load_kvcache: null pointer");
+  // the caches and the block table are read only for sequences with a cached context: without pages there is none
+  if ((num_pages > 0 || max_pages > 0) && (!k_cache || !v_cache || !block_table))
+    return fail(PDLLM_E_INVALID, "load_kvcache: null cache or block_table with num_pages=%lld max_pages=%d", (long long)num_pages, max_pages);
   const int64_t row_bytes = static_cast<int64_t>(num_kv_heads) * head_dim * elem_bytes;
   if (row_bytes % 16 != 0 || (new_stride * elem_bytes) % 16 != 0 || !aligned16(k_cache) || !aligned16(v_cache) ||
       !aligned16(k_new) || !aligned16(v_new) || !aligned16(k_out) || !aligned16(v_out))
@@ -210,7 +215,9 @@ static __device__ __align__(256) float g_unmask_static_scratch[(PDLLM_UNMASK_STA
 
 // The array's name is only a host-side handle: the device address has to be looked up, per device, with that device
 // current. Done on the first call for a device and cached.
-static int unmask_static_scratch_ptr(float** out) {
+// `refresh` drops the cached address first: a cudaDeviceReset (or any re-creation of the device's primary context)
+// invalidates it, which shows up as an invalid-value error from the next use.
+static int unmask_static_scratch_ptr(float** out, bool refresh = false) {
   static std::mutex mu;
   static float* cached[64] = {nullptr};
   int dev = 0;
@@ -218,6 +225,7 @@ static int unmask_static_scratch_ptr(float** out) {
   if (e != cudaSuccess) return fail(static_cast<int>(e), "cudaGetDevice: %s", cudaGetErrorString(e));
   if (dev < 0 || dev >= 64) return fail(PDLLM_E_UNSUPPORTED, "unmask_step_static: device ordinal %d not supported", dev);
   std::lock_guard<std::mutex> lock(mu);
+  if (refresh) cached[dev] = nullptr;
   if (cached[dev] == nullptr) {
     void* ptr = nullptr;
     e = cudaGetSymbolAddress(&ptr, g_unmask_static_scratch);
@@ -245,6 +253,12 @@ int pdllm_unmask_step_static(const void* logits, int64_t logits_stride, const vo
   const int64_t words = unmask_ws_words(block_len);
   const int64_t counter_words = block_len + 1;
   cudaError_t e = cudaMemsetAsync(scratch + (words - counter_words), 0, counter_words * 4, as_stream(stream));
+  if (e == cudaErrorInvalidValue || e == cudaErrorInvalidDevicePointer || e == cudaErrorContextIsDestroyed) {
+    // the address cached for this device went stale (its context was reset since): look it up again, once
+    (void)cudaGetLastError();
+    if ((rc = unmask_static_scratch_ptr(&scratch, true)) != 0) return rc;
+    e = cudaMemsetAsync(scratch + (words - counter_words), 0, counter_words * 4, as_stream(stream));
+  }
   if (e != cudaSuccess) return fail(static_cast<int>(e), "cudaMemsetAsync: %s", cudaGetErrorString(e));
   return pdllm_unmask_step(logits, logits_stride, last_logit, dtype, block_len, vocab, shift, block_ids, mask_id, threshold,
                            conf_dtype, out_counts, out_conf, out_x0, scratch, words * 4, stream);
@@ -475,11 +489,15 @@ int pdllm_enable_peer_access(int device, int peer_device) {
 
 int pdllm_compact_pages_per_head(void* cache, const int32_t* src_page_ids, const int32_t* dst_page_ids,
                                  const int64_t* keep, int64_t keep_count, int64_t src_tokens,
-                                 int64_t dst_start, int page_size, int num_kv_heads, int head_dim,
+                                 int64_t dst_start, int64_t dst_tokens, int page_size, int num_kv_heads, int head_dim,
                                  int elem_bytes, int64_t num_pages, void* staging, int32_t* status,
                                  void* stream) {
-  if (keep_count < 0 || page_size <= 0 || num_kv_heads <= 0 || head_dim <= 0) return fail(PDLLM_E_INVALID, "compact_pages_per_head: bad sizes");
+  if (keep_count < 0 || page_size <= 0 || num_kv_heads <= 0 || head_dim <= 0 || dst_start < 0)
+    return fail(PDLLM_E_INVALID, "compact_pages_per_head: bad sizes");
   if (keep_count == 0) return 0;
+  if (dst_start + keep_count > dst_tokens)
+    return fail(PDLLM_E_INVALID, "compact_pages_per_head: rows [%lld, %lld) do not fit the %lld tokens of dst_page_ids",
+                (long long)dst_start, (long long)(dst_start + keep_count), (long long)dst_tokens);
   if (!cache || !src_page_ids || !dst_page_ids || !keep || !staging) return fail(PDLLM_E_INVALID, "compact_pages_per_head: null pointer");
   const int64_t head_bytes = static_cast<int64_t>(head_dim) * elem_bytes;
   if (head_bytes % 16 != 0 || !aligned16(cache) || !aligned16(staging)) return fail(PDLLM_E_UNSUPPORTED, "compact_pages_per_head: head rows must be 16-byte multiples");

@@ -411,6 +411,13 @@ class FastDLLMDreamEngine:
                     done.record(torch.cuda.current_stream(source_engine.device))
                     torch.cuda.current_stream(self.device).wait_event(done)
                 ops.copy_pages(source_engine._layer_pools(), src_ids, self._layer_pools(), dst_ids, n_lists=planes, tokens_per_list=prompt_len)
+                # ... and must not reuse them before this GPU has read them: the copy kernel runs on THIS device's stream, so
+                # a release_pd_record(source) followed by a new prefill on the source would otherwise overwrite pages that are
+                # still being read across NVLink. Later work on the source's current stream is ordered after the copy.
+                if source_engine.device != self.device:
+                    copied = torch.cuda.Event()
+                    copied.record(torch.cuda.current_stream(self.device))
+                    torch.cuda.current_stream(source_engine.device).wait_event(copied)
         except BaseException:
             self._prefix_cache.release_pages(prompt_pages + block_pages)
             raise

@@ -58,7 +58,7 @@ class DreamArch:
 
     @classmethod
     def toy(cls) -> "DreamArch":
-        """BASELINE config 'CPU toy'."""
+        """The CPU-runnable toy: 2 layers, hidden 256, 4 query / 2 KV heads of 64, MLP 688, vocabulary 1024."""
         return cls(vocab_size=1024, hidden_size=256, intermediate_size=688, num_hidden_layers=2, num_attention_heads=4,
                    num_key_value_heads=2, rope_theta=1e6, max_position_embeddings=32768, mask_token_id=1023,
                    bos_token_id=1, eos_token_id=2)

@@ -573,7 +573,7 @@ def compact_pages_per_head(cache: torch.Tensor, src_page_ids, dst_page_ids, keep
     dst_ids = _page_ids_tensor(dst_page_ids, device)
     staging = _workspace(device, "compact", keep_count * hkv * d * cache.element_size())
     check(_lib.load().pdllm_compact_pages_per_head(cache.data_ptr(), src_ids.data_ptr(), dst_ids.data_ptr(), keep.data_ptr(),
-                                                   keep_count, int(src_tokens), int(dst_start), page_size, hkv, d,
+                                                   keep_count, int(src_tokens), int(dst_start), dst_ids.numel() * page_size, page_size, hkv, d,
                                                    cache.element_size(), cache.shape[0], staging.data_ptr(),
                                                    status_word(device).data_ptr(), _stream(device)))
 

@@ -12,8 +12,8 @@ sampling / scoring tails are single fused kernels (`ops.unmask_step`, `ops.self_
 
 Where the reference hands tensors around (`past_key_values`), this class hands a `PagedCache` handle.
 Not built (raise NotImplementedError): sampling with temperature / top-p / top-k, `alg` other than
-"confidence_threshold", score modes other than none / self_information / draft_self_information, avg-pooling and
-non-default head/layer reductions, the LLaDA leave-one-out scorer.
+"confidence_threshold" / "origin", score modes other than none / self_information / draft_self_information, avg-pooling
+and non-default head/layer reductions, the LLaDA leave-one-out scorer.
 """
 
 from __future__ import annotations
@@ -238,8 +238,10 @@ class FastDLLMParallelComp:
             raise ValueError(f"Unsupported token_eviction_granularity: {config.token_eviction_granularity}")
         if config.temperature and config.temperature > 0 or config.top_p is not None or config.top_k is not None:
             raise NotImplementedError("only greedy decoding (temperature 0, no top-p / top-k) is built")
-        if config.alg != "confidence_threshold":
-            raise NotImplementedError(f"alg={config.alg!r} is not built; only 'confidence_threshold'")
+        if config.alg not in {"confidence_threshold", "origin"}:
+            raise NotImplementedError(f"alg={config.alg!r} is not built; only 'confidence_threshold' and 'origin' (max-probability confidence)")
+        if config.alg_temp not in (None, 0, 0.0):
+            raise NotImplementedError("alg_temp > 0 (sampled transfer order) is not built")
         if config.token_score_direction != "query_to_chunk":
             raise NotImplementedError("only token_score_direction='query_to_chunk' is built")
         if float(config.rope_scale_factor or 1.0) > 1.0:
@@ -404,7 +406,7 @@ class FastDLLMParallelComp:
             block = torch.full((draft_len,), mask_id, dtype=torch.long, device=self.device)
             confirmed = torch.zeros(draft_len, dtype=torch.bool, device=self.device)
             if last_logit is not None:
-                block[0] = torch.argmax(last_logit)  # softmax is monotone: the arg-max of the logit
+                block[0] = self._first_block_token(last_logit)
             else:
                 raise ValueError("draft needs at least one context token")
             confirmed[0] = True
@@ -420,20 +422,93 @@ class FastDLLMParallelComp:
         finally:
             cache.release()
 
+    def _fill_most_confident(self, logits: torch.Tensor, block: torch.Tensor, last_logit: Optional[torch.Tensor], count: int) -> int:
+        """Fill the `count` most confident MASK slots of `block` (in place) with their arg-max tokens: the transfer rule of the
+        fixed-step diffusion sampler and of the partial draft (reference :2548-2552, :2497-2504 with alg_temp 0). Confidence
+        and arg-max of every candidate slot come from the unmask kernel run on a scratch copy with a threshold no
+        probability reaches; ties at the cut are as unspecified as torch.topk's in the reference. Returns slots filled."""
+        if count <= 0:
+            return 0
+        scratch = block.clone()
+        counts, conf, x0 = ops.unmask_step(logits, scratch, mask_token_id=self._mask_token_id(), threshold=2.0, last_logit=last_logit,
+                                           shift=self.arch.logit_shift, return_details=True)
+        count = min(int(count), int(counts[0].item()))
+        if count <= 0:
+            return 0
+        idx = torch.topk(conf, count).indices
+        block[idx] = x0[idx]
+        return count
+
+    @torch.inference_mode()
+    def generate_partial_draft_from_cache(self, *, past_key_values: Optional[PagedCache], cache_positions: Sequence[int], query_ids,
+                                          query_rope_start: int, max_new_tokens: int, partial_steps: int) -> Tuple[List[int], int]:
+        """Draft that stops once `partial_steps` slots are filled: slot 0 from the last context logit, then forwards that
+        each fill as many of the most confident slots as are still wanted (reference :2512-2593). Returns (ids, filled)."""
+        draft_len = int(max_new_tokens)
+        if draft_len <= 0:
+            return [], 0
+        if past_key_values is not None:
+            raise NotImplementedError("drafting on top of an existing cache is not needed by the selection path")
+        query_ids = list(query_ids)
+        if not query_ids:
+            raise ValueError("draft needs at least one context token")
+        mask_id = self._mask_token_id()
+        cache = PagedCache(self, len(query_ids) + draft_len)
+        try:
+            q_pos = self._range_positions(query_rope_start, len(query_ids))
+            logits, _ = self._forward_packed([query_ids], [q_pos], causal=False, store_slots=cache.slots(0, len(query_ids)),
+                                             logit_rows=[len(query_ids) - 1])
+            last_logit = logits[0]
+            cache.length = len(query_ids)
+            block_pos = self._range_positions(query_rope_start + len(query_ids), draft_len)
+            block = torch.full((draft_len,), mask_id, dtype=torch.long, device=self.device)
+            target = min(draft_len, max(0, int(partial_steps)))
+            filled = 0
+            if target > 0:
+                block[0] = self._first_block_token(last_logit)
+                filled = 1
+            while filled < target and bool((block == mask_id).any()):
+                logits, _ = self._forward_packed([[0] * draft_len], [block_pos], causal=False, cache=cache, ctx_len=cache.length,
+                                                 ids_tensor=block)
+                done = self._fill_most_confident(logits, block, last_logit, target - filled)
+                if done <= 0:
+                    break
+                filled += done
+            return block.tolist(), filled
+        finally:
+            cache.release()
+
+    def _first_block_token(self, last_logit: torch.Tensor) -> torch.Tensor:
+        if not self.arch.logit_shift:
+            raise NotImplementedError("un-shifted (LLaDA) block initialisation is not built")
+        return torch.argmax(last_logit)   # softmax is monotone: the arg-max of the logit
+
     def _selection_query_ids_with_score_target(self, prefix_ids, scoring_query_ids):
         selection = list(scoring_query_ids)
         score_token_mask: Optional[List[bool]] = None
         cfg = self.config
         if cfg.score_mode == "draft_self_information" and cfg.score_draft_tokens > 0:
-            if cfg.score_draft_partial_rounds is None:
-                raise NotImplementedError("score_draft_partial_rounds=None (full draft generation) is not built; set it (README uses 1)")
-            draft_ids, draft_mask = self.generate_partial_draft_rounds_from_cache(
-                past_key_values=None, cache_positions=[], query_ids=list(prefix_ids) + list(scoring_query_ids), query_rope_start=0,
-                max_new_tokens=int(cfg.score_draft_tokens), partial_rounds=int(cfg.score_draft_partial_rounds))
-            if cfg.score_draft_score_all_slots:
-                score_token_mask = [True] * len(scoring_query_ids) + [True] * len(draft_ids)
+            draft_query = list(prefix_ids) + list(scoring_query_ids)
+            if cfg.score_draft_partial_rounds is not None:
+                draft_ids, draft_mask = self.generate_partial_draft_rounds_from_cache(
+                    past_key_values=None, cache_positions=[], query_ids=draft_query, query_rope_start=0,
+                    max_new_tokens=int(cfg.score_draft_tokens), partial_rounds=int(cfg.score_draft_partial_rounds))
+                if cfg.score_draft_score_all_slots:
+                    score_token_mask = [True] * len(scoring_query_ids) + [True] * len(draft_ids)
+                else:
+                    score_token_mask = [True] * len(scoring_query_ids) + list(draft_mask)
+            elif cfg.score_draft_partial_steps is not None:
+                draft_ids, _ = self.generate_partial_draft_from_cache(
+                    past_key_values=None, cache_positions=[], query_ids=draft_query, query_rope_start=0,
+                    max_new_tokens=int(cfg.score_draft_tokens), partial_steps=int(cfg.score_draft_partial_steps))
+                mask_id = self._mask_token_id()
+                score_token_mask = [True] * len(scoring_query_ids) + [t != mask_id for t in draft_ids]
             else:
-                score_token_mask = [True] * len(scoring_query_ids) + list(draft_mask)
+                # the dataclass default (reference :1828-1837): a complete draft, every query + draft position is a label
+                draft_ids = self.generate_from_cache(
+                    past_key_values=None, cache_positions=[], query_ids=draft_query, query_rope_start=0,
+                    max_new_tokens=int(cfg.score_draft_tokens), diffusion_steps=int(cfg.score_draft_steps or 1),
+                    force_diffusion=bool(cfg.score_draft_fixed_steps))
             selection = list(scoring_query_ids) + draft_ids
         return selection, None, score_token_mask
 
@@ -601,13 +676,17 @@ class FastDLLMParallelComp:
 
     # ------------------------------------------------------------------------------------------------ block denoising
     def _denoise_blocks(self, cache: PagedCache, *, suffix_pos_start: int, last_logit: torch.Tensor,
-                        first_token: Optional[torch.Tensor], tail_in_cache: int, max_new: int) -> List[int]:
+                        first_token: Optional[torch.Tensor], tail_in_cache: int, max_new: int,
+                        fixed_steps_per_block: Optional[int] = None) -> List[int]:
         """Fast-dLLM dual-cache block loop over the paged cache (reference :2932-2998, :2399-2441).
 
         Cache layout while block b is active: [prompt ‖ finished blocks ‖ MASK slots of the later blocks]; the active
         block's rows are the new rows of every forward, so they replace their own slots by construction. After the block
         is committed its K/V take the place of the first later-MASK slots and the later slots are recomputed.
         `tail_in_cache`: later-block MASK slots already stored behind the prompt by the prefill (full_prompt_mask mode).
+        `fixed_steps_per_block`: None = confidence-threshold denoising; an int = the fixed-step diffusion sampler
+        (reference _denoise_block_diffusion :2443-2510): step i of n transfers int(masks * (1 - t[i+1] / t[i])) of the most
+        confident slots, t = linspace(1, 1e-3, n + 1), the last step all that is left.
         """
         mask_id = self._mask_token_id()
         n0 = cache.length - tail_in_cache          # prompt (+ query) tokens
@@ -633,9 +712,7 @@ class FastDLLMParallelComp:
                     self._forward_packed([[mask_id] * (blen + later)], [suffix_pos], causal=False, cache=cache, ctx_len=done,
                                          store_slots=slots, want_logits=False)
                 tail_len = later
-                first = torch.argmax(last_logit) if self.arch.logit_shift else None
-                if first is None:
-                    raise NotImplementedError("un-shifted (LLaDA) block initialisation is not built")
+                first = self._first_block_token(last_logit)
             else:
                 first = first_token
             ctx = done + tail_len
@@ -648,6 +725,18 @@ class FastDLLMParallelComp:
             block[0] = first
             guard = 0
             remaining = blen - 1
+            if fixed_steps_per_block is not None:
+                steps = int(fixed_steps_per_block)
+                timesteps = torch.linspace(1, 1e-3, steps + 1)       # fp32 on the host, the reference's own arithmetic
+                for step in range(steps):
+                    if remaining <= 0:
+                        break
+                    count = int(remaining * (1 - timesteps[step + 1] / timesteps[step])) if step < steps - 1 else remaining
+                    if count <= 0:
+                        continue
+                    logits, _ = self._forward_packed([[0] * blen], [block_pos], causal=False, cache=cache, ctx_len=ctx, ids_tensor=block)
+                    remaining -= self._fill_most_confident(logits, block, last_logit, count)
+                remaining = 0
             while remaining > 0:
                 guard += 1
                 if guard > blen + 8:
@@ -765,11 +854,14 @@ class FastDLLMParallelComp:
     def generate_from_cache(self, *, past_key_values: Optional[PagedCache], cache_positions: Sequence[int], query_ids, query_rope_start: int,
                             max_new_tokens: Optional[int] = None, diffusion_steps=None, force_diffusion: bool = False) -> List[int]:
         """Prefill the query on top of `past_key_values` (a PagedCache) and denoise block by block (reference :2678-2774)."""
-        if force_diffusion:
-            raise NotImplementedError("force_diffusion (fixed-step diffusion) is not built")
         max_new = int(max_new_tokens if max_new_tokens is not None else self.max_new_tokens)
         if max_new <= 0:
             return []
+        fixed_steps = None
+        if force_diffusion or self.config.alg != "confidence_threshold":
+            total_steps = int(diffusion_steps if diffusion_steps is not None else self.diffusion_steps)
+            num_blocks = max(1, math.ceil(max_new / self.block_length))
+            fixed_steps = max(1, math.ceil(total_steps / num_blocks))
         query_ids = list(query_ids)
         own = past_key_values is None
         cache = past_key_values if not own else PagedCache(self, len(query_ids) + max_new + self.model.page_size)
@@ -784,7 +876,7 @@ class FastDLLMParallelComp:
                                              store_slots=cache.slots(base, len(query_ids)), logit_rows=[len(query_ids) - 1])
             cache.length = base + len(query_ids)
             return self._denoise_blocks(cache, suffix_pos_start=query_rope_start + len(query_ids), last_logit=logits[0],
-                                        first_token=None, tail_in_cache=0, max_new=max_new)
+                                        first_token=None, tail_in_cache=0, max_new=max_new, fixed_steps_per_block=fixed_steps)
         finally:
             if own:
                 cache.release()
@@ -885,8 +977,12 @@ class FastDLLMParallelComp:
             else:
                 suffix_start = full_q_start + len(query_ids)
             first = torch.argmax(last_logit) if (with_masks and self.arch.logit_shift) else None
+            fixed_steps = None
+            if cfg.alg != "confidence_threshold":     # reference :2927-2929, :2977-2985
+                fixed_steps = max(1, math.ceil(int(self.diffusion_steps) / max(1, math.ceil(max_new / self.block_length))))
             generated = self._denoise_blocks(cache, suffix_pos_start=suffix_start, last_logit=last_logit, first_token=first,
-                                             tail_in_cache=later0 if with_masks else 0, max_new=max_new)
+                                             tail_in_cache=later0 if with_masks else 0, max_new=max_new,
+                                             fixed_steps_per_block=fixed_steps)
         finally:
             cache.release()
 

@@ -29,7 +29,8 @@ def describe(cls):
 
 def main():
     ap = argparse.ArgumentParser()
-    ap.add_argument("--reference", default="/root/reference")
+    ap.add_argument("--reference", default=os.environ.get("PDLLM_REFERENCE_ROOT"), required="PDLLM_REFERENCE_ROOT" not in os.environ,
+                    help="root of the reference checkout (or set PDLLM_REFERENCE_ROOT)")
     args = ap.parse_args()
     sys.path.insert(0, os.path.join(args.reference, "prefilling_dllm_eval"))
     import fastdllm_parallelcomp as ref

@@ -26,7 +26,8 @@ def literal(node):
 
 def main():
     ap = argparse.ArgumentParser()
-    ap.add_argument("--reference", default="/root/reference")
+    ap.add_argument("--reference", default=os.environ.get("PDLLM_REFERENCE_ROOT"), required="PDLLM_REFERENCE_ROOT" not in os.environ,
+                    help="root of the reference checkout (or set PDLLM_REFERENCE_ROOT)")
     args = ap.parse_args()
     path = os.path.join(args.reference, "prefilling_dllm_engine", "prefilling_dllm", "fastdllm_engine.py")
     tree = ast.parse(open(path).read())

@@ -1,13 +1,14 @@
 """Generates tests/golden/toy_reference.json by running the UNMODIFIED reference class on CPU.
 
-Run where the reference checkout exists:  python tests/golden/make_golden.py [--reference /path/to/reference]
+Run where the reference checkout exists:  python tests/golden/make_golden.py --reference /path/to/reference
+(or set PDLLM_REFERENCE_ROOT)
 It needs only CPU. The reference's model plug-in (Fast-dLLM v1, absent from the reference tree) is supplied by
 oracle/contract_model; everything else — chunking, chunk BOS, draft rounds, self-information scoring, ranking,
 token eviction, position bookkeeping, block denoising — is the reference's own code
 (prefilling_dllm_eval/fastdllm_parallelcomp.py). The JSON it writes is what pins oracle/hotpath.py and the
 GPU path; the GPU box never needs the reference.
 
-Workload = BASELINE config "CPU toy": Dream architecture, 2 layers, hidden 256, 4 query / 2 KV heads, head_dim 64,
+Workload = the CPU-runnable toy: Dream architecture, 2 layers, hidden 256, 4 query / 2 KV heads, head_dim 64,
 MLP 688, vocab 1024, RoPE theta 1e6, fp32, seeded N(0, 0.02) init; 4096 uniform random context ids (seed 0) and a
 32-token query; chunk_size 512 with chunk BOS, topk 4, 4 draft tokens / 1 partial round, block 32, 32 new tokens,
 threshold 0.9, greedy. Token ids: BOS 1, EOS 2, MASK 1023; sampled ids avoid them.
@@ -31,17 +32,24 @@ TOY = dict(vocab_size=1024, hidden_size=256, intermediate_size=688, num_hidden_l
            num_key_value_heads=2, max_position_embeddings=32768, rope_theta=1000000.0, rms_norm_eps=1e-6,
            initializer_range=0.02, mask_token_id=1023, pad_token_id=0, bos_token_id=1, eos_token_id=2)
 BOS, EOS, MASK = 1, 2, 1023
+# The same flow at the head shape the tensor-core attention kernel serves (head_dim 128, GQA group 2): 2 layers, hidden 512,
+# 4 query / 2 KV heads, MLP 1376, vocabulary 4096; MASK is the last id. Run in fp32 and in bf16 by the reference.
+TOY128 = dict(vocab_size=4096, hidden_size=512, intermediate_size=1376, num_hidden_layers=2, num_attention_heads=4,
+              num_key_value_heads=2, max_position_embeddings=32768, rope_theta=1000000.0, rms_norm_eps=1e-6,
+              initializer_range=0.02, mask_token_id=4095, pad_token_id=0, bos_token_id=1, eos_token_id=2)
 
 
-def toy_inputs(context_len=4096, query_len=32, seed=0):
+def toy_inputs(context_len=4096, query_len=32, seed=0, vocab=1024):
     g = torch.Generator().manual_seed(seed)
-    context = torch.randint(3, 1023, (context_len,), generator=g).tolist()
-    query = torch.randint(3, 1023, (query_len,), generator=g).tolist()
+    context = torch.randint(3, vocab - 1, (context_len,), generator=g).tolist()
+    query = torch.randint(3, vocab - 1, (query_len,), generator=g).tolist()
     return context, query
 
 
-def write_toy_checkpoint(path: str, seed: int = 0) -> None:
-    """config.json + seeded-init model.safetensors + a 1024-word tokenizer."""
+def write_toy_checkpoint(path: str, seed: int = 0, config: dict = None) -> None:
+    """config.json + seeded-init model.safetensors + a word-level tokenizer over the vocabulary."""
+    TOY = dict(config or globals()["TOY"])
+    MASK = TOY["mask_token_id"]
     from safetensors.torch import save_file
     from tokenizers import Tokenizer
     from tokenizers.models import WordLevel
@@ -57,7 +65,7 @@ def write_toy_checkpoint(path: str, seed: int = 0) -> None:
     init_weights_(model, seed)
     save_file({k: v.contiguous() for k, v in model.state_dict().items()}, os.path.join(path, "model.safetensors"))
     vocab = {f"t{i}": i for i in range(TOY["vocab_size"])}
-    vocab.pop("t1"), vocab.pop("t2"), vocab.pop("t1023"), vocab.pop("t0")
+    vocab.pop("t1"), vocab.pop("t2"), vocab.pop(f"t{MASK}"), vocab.pop("t0")
     vocab.update({"<pad>": 0, "<bos>": BOS, "<eos>": EOS, "<mask>": MASK})
     tok = Tokenizer(WordLevel(vocab, unk_token="<pad>"))
     tok.pre_tokenizer = Whitespace()
@@ -75,14 +83,14 @@ README_FLAGS = dict(  # the reference README's canonical long-context flags (REA
 )
 
 
-def load_reference(reference_root: str, ckpt: str, **flags):
+def load_reference(reference_root: str, ckpt: str, dtype: str = "float32", **flags):
     eval_dir = os.path.join(reference_root, "prefilling_dllm_eval")
     if eval_dir not in sys.path:
         sys.path.insert(0, eval_dir)
     import fastdllm_parallelcomp as ref  # the reference module, unmodified
 
     runtime = ref.load_fastdllm_parallelcomp(
-        pretrained=ckpt, fastdllm_dream_dir=os.path.join(ROOT, "oracle", "contract_model"), device="cpu", dtype="float32",
+        pretrained=ckpt, fastdllm_dream_dir=os.path.join(ROOT, "oracle", "contract_model"), device="cpu", dtype=dtype,
         trust_remote_code=False, **flags)
     return ref, runtime
 
@@ -96,6 +104,13 @@ def record_run(runtime, context, query, *, capture_steps=True):
     orig_tok_scores = runtime.query_attention_token_scores
     orig_denoise = runtime._denoise_block_confidence_threshold
     orig_fwd_replace = runtime._forward_generation_block_replace
+    orig_selection = runtime._selection_query_ids_with_score_target
+
+    def selection(prefix_ids, scoring_query_ids):
+        ids, count, mask = orig_selection(prefix_ids, scoring_query_ids)
+        rec["selection_query_ids"] = list(ids)
+        rec["score_token_mask"] = None if mask is None else [bool(x) for x in mask]
+        return ids, count, mask
 
     def draft(**kw):
         ids, mask = orig_draft(**kw)
@@ -130,6 +145,7 @@ def record_run(runtime, context, query, *, capture_steps=True):
     runtime._keep_positions_per_layer_per_head_for_chunk = keep_ph
     runtime.query_attention_token_scores = tok_scores
     runtime._forward_generation_block_replace = fwd_replace
+    runtime._selection_query_ids_with_score_target = selection
     try:
         result = runtime.generate(prefix_ids=runtime.bos_ids(), context_ids=context, query_ids=query)
     finally:
@@ -138,6 +154,7 @@ def record_run(runtime, context, query, *, capture_steps=True):
         runtime._keep_positions_per_layer_per_head_for_chunk = orig_keep_ph
         runtime.query_attention_token_scores = orig_tok_scores
         runtime._forward_generation_block_replace = orig_fwd_replace
+        runtime._selection_query_ids_with_score_target = orig_selection
     rec.update(
         sequences=list(result.sequences), selected_chunk_indices=list(result.selected_chunk_indices),
         chunk_scores={str(k): float(v) for k, v in result.chunk_scores.items()}, cache_tokens=result.cache_tokens,
@@ -178,43 +195,77 @@ def cross_check_vendored_dream(reference_root: str, ckpt: str) -> float:
     return float((a - b).abs().max())
 
 
+VARIANTS = {
+    "readme_full_prompt_mask": dict(README_FLAGS),
+    "chunk_query_reuse": dict(README_FLAGS, cache_build_mode="chunk_query", chunk_position_mode="reuse",
+                              query_position_mode="after_reused_window"),
+    "evict_global_cap128": dict(README_FLAGS, token_capacity=128),
+    "evict_per_head_cap128_chunk_query": dict(README_FLAGS, token_capacity=128, token_eviction_granularity="per_head",
+                                              cache_build_mode="chunk_query", chunk_position_mode="reuse",
+                                              query_position_mode="after_reused_window"),
+    "two_blocks": dict(README_FLAGS, max_new_tokens=64),
+    "evict_per_head_cap128_full_prompt_two_blocks": dict(README_FLAGS, token_capacity=128, max_new_tokens=64,
+                                                         token_eviction_granularity="per_head"),
+    "full_prompt_query": dict(README_FLAGS, cache_build_mode="full_prompt_query"),
+    # the config dataclass's own draft defaults: no partial rounds -> a full confidence-threshold draft of 16 tokens,
+    # every query + draft position is a label
+    "draft_dataclass_defaults": dict(README_FLAGS, score_draft_partial_rounds=None, score_draft_tokens=16),
+    "draft_partial_steps": dict(README_FLAGS, score_draft_partial_rounds=None, score_draft_partial_steps=2),
+    "draft_fixed_steps": dict(README_FLAGS, score_draft_partial_rounds=None, score_draft_fixed_steps=True, score_draft_steps=2),
+}
+
+# head_dim-128 toy: the README flow, and the sharded flow's flags (independent chunks, global eviction, two blocks)
+VARIANTS128 = {
+    "readme_full_prompt_mask": dict(README_FLAGS),
+    "chunk_query_evict_global_cap128_two_blocks": dict(README_FLAGS, cache_build_mode="chunk_query", chunk_position_mode="reuse",
+                                                       query_position_mode="after_reused_window", token_capacity=128,
+                                                       max_new_tokens=64),
+    "evict_per_head_cap128_full_prompt": dict(README_FLAGS, token_capacity=128, token_eviction_granularity="per_head"),
+}
+
+
 def main():
     ap = argparse.ArgumentParser()
-    ap.add_argument("--reference", default="/root/reference")
+    ap.add_argument("--reference", default=os.environ.get("PDLLM_REFERENCE_ROOT"), required="PDLLM_REFERENCE_ROOT" not in os.environ,
+                    help="root of the reference checkout (or set PDLLM_REFERENCE_ROOT)")
     ap.add_argument("--out", default=os.path.join(HERE, "toy_reference.json"))
+    ap.add_argument("--out128", default=os.path.join(HERE, "toy128_reference.json"))
+    ap.add_argument("--only", choices=["toy", "toy128"], default=None)
     args = ap.parse_args()
     torch.manual_seed(0)
     torch.set_num_threads(max(1, os.cpu_count() or 1))
-    context, query = toy_inputs()
-    golden = {"config": dict(TOY), "flags": dict(README_FLAGS), "context_seed": 0, "runs": {}}
     with tempfile.TemporaryDirectory() as tmp:
-        ckpt = os.path.join(tmp, "ckpt_toy")
-        write_toy_checkpoint(ckpt)
-        try:
-            golden["vendored_dream_max_abs_logit_diff"] = cross_check_vendored_dream(args.reference, ckpt)
-        except Exception as exc:  # the vendored model depends on the installed transformers version
-            golden["vendored_dream_max_abs_logit_diff"] = None
-            golden["vendored_dream_error"] = f"{type(exc).__name__}: {exc}"
-        variants = {
-            "readme_full_prompt_mask": dict(README_FLAGS),
-            "chunk_query_reuse": dict(README_FLAGS, cache_build_mode="chunk_query", chunk_position_mode="reuse",
-                                      query_position_mode="after_reused_window"),
-            "evict_global_cap128": dict(README_FLAGS, token_capacity=128),
-            "evict_per_head_cap128_chunk_query": dict(README_FLAGS, token_capacity=128, token_eviction_granularity="per_head",
-                                                      cache_build_mode="chunk_query", chunk_position_mode="reuse",
-                                                      query_position_mode="after_reused_window"),
-            "two_blocks": dict(README_FLAGS, max_new_tokens=64),
-            "evict_per_head_cap128_full_prompt_two_blocks": dict(README_FLAGS, token_capacity=128, max_new_tokens=64,
-                                                                 token_eviction_granularity="per_head"),
-            "full_prompt_query": dict(README_FLAGS, cache_build_mode="full_prompt_query"),
-        }
-        for name, flags in variants.items():
-            _, runtime = load_reference(args.reference, ckpt, **flags)
-            golden["runs"][name] = dict(flags=flags, **record_run(runtime, context, query))
-            print(name, golden["runs"][name]["selected_chunk_indices"], golden["runs"][name]["sequences"][:8])
-    with open(args.out, "w") as handle:
-        json.dump(golden, handle)
-    print("wrote", args.out, os.path.getsize(args.out), "bytes")
+        if args.only in (None, "toy"):
+            context, query = toy_inputs()
+            golden = {"config": dict(TOY), "flags": dict(README_FLAGS), "context_seed": 0, "runs": {}}
+            ckpt = os.path.join(tmp, "ckpt_toy")
+            write_toy_checkpoint(ckpt)
+            try:
+                golden["vendored_dream_max_abs_logit_diff"] = cross_check_vendored_dream(args.reference, ckpt)
+            except Exception as exc:  # the vendored model depends on the installed transformers version
+                golden["vendored_dream_max_abs_logit_diff"] = None
+                golden["vendored_dream_error"] = f"{type(exc).__name__}: {exc}"
+            for name, flags in VARIANTS.items():
+                _, runtime = load_reference(args.reference, ckpt, **flags)
+                golden["runs"][name] = dict(flags=flags, **record_run(runtime, context, query))
+                print(name, golden["runs"][name]["selected_chunk_indices"], golden["runs"][name]["sequences"][:8])
+            with open(args.out, "w") as handle:
+                json.dump(golden, handle)
+            print("wrote", args.out, os.path.getsize(args.out), "bytes")
+        if args.only in (None, "toy128"):
+            context, query = toy_inputs(vocab=TOY128["vocab_size"])
+            golden = {"config": dict(TOY128), "flags": dict(README_FLAGS), "context_seed": 0, "runs": {}}
+            ckpt = os.path.join(tmp, "ckpt_toy128")
+            write_toy_checkpoint(ckpt, config=TOY128)
+            for dtype in ("float32", "bfloat16"):
+                for name, flags in VARIANTS128.items():
+                    _, runtime = load_reference(args.reference, ckpt, dtype=dtype, **flags)
+                    key = f"{name}/{dtype}"
+                    golden["runs"][key] = dict(flags=flags, dtype=dtype, **record_run(runtime, context, query))
+                    print(key, golden["runs"][key]["selected_chunk_indices"], golden["runs"][key]["sequences"][:8])
+            with open(args.out128, "w") as handle:
+                json.dump(golden, handle)
+            print("wrote", args.out128, os.path.getsize(args.out128), "bytes")
 
 
 if __name__ == "__main__":

@@ -34,7 +34,7 @@ def test_every_declared_symbol_is_exported(lib):
     for name in declared:
         assert hasattr(handle, name), f"{name} is declared in include/pdllm_b200.h but not exported"
     assert sorted(lib.EXPORTED_SYMBOLS) == declared, "ctypes signature table and header disagree"
-    assert handle.pdllm_abi_version() == 2
+    assert handle.pdllm_abi_version() == lib.ABI_VERSION
 
 
 def test_header_cites_the_reference_for_every_kernel_entry():

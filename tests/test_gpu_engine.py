@@ -296,6 +296,32 @@ def test_engine_to_engine_copy_across_gpus(engine, ckpt):
     engine._prefix_cache.evict_one()
 
 
+@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs two GPUs")
+def test_engine_to_engine_copy_survives_reuse_of_the_source_pages(engine, ckpt):
+    """The copy kernel runs on the destination GPU's stream and returns at once. Releasing the source record and
+    overwriting its pages straight afterwards must not change what the destination received: work enqueued later on the
+    source's stream is ordered after the copy."""
+    other = _engine(ckpt, pages=16, device_start=1)
+    prompt = _prompt(700, seed=31)
+    while engine._prefix_cache.evict_one():
+        pass
+    rec = engine.prefill_to_pd_record(prompt, max_new_tokens=BLOCK)
+    want = engine.snapshot_pd_record_kv(rec)
+    pages = list(rec.prompt_page_ids)
+    remote = other.make_pd_record_from_remote_engine(engine, rec)
+    engine.release_pd_record(rec)
+    while engine._prefix_cache.evict_one():
+        pass
+    with torch.cuda.device(engine.device):
+        engine.model.kv_cache[:, :, pages] = 7.0          # what a new prefill into the recycled pages would do
+    got = other.snapshot_pd_record_kv(remote)
+    for layer in range(2):
+        assert torch.equal(want.k_by_layer[layer].cpu(), got.k_by_layer[layer].cpu())
+        assert torch.equal(want.v_by_layer[layer].cpu(), got.v_by_layer[layer].cpu())
+    other.release_pd_record(remote)
+    assert other._prefix_cache.num_free_pages == 16
+
+
 def test_batched_decode_equals_one_by_one(engine):
     """Three requests with different prompt lengths denoised in shared steps: same ids and step counts as decoding each
     record on its own; every page comes back."""

@@ -348,7 +348,7 @@ def test_attention_tc_uninitialised_pool_tail_is_harmless(ops, cuda_device):
 
 
 def test_attention_op_level_config_full_size(ops, cuda_device):
-    """8 requests, 28/4 heads, d 128, page 256, pool of 32 chunks x 1024 tokens per request,
+    """The op-level decode-attention shape at full size: 8 requests, 28/4 heads, d 128, page 256, pool of 32 chunks x 1024 tokens per request,
     4 chunks picked by a seeded permutation, 64 query + 32 response rows, bidirectional."""
     case = _attention_case(0, num_seqs=8, hq=28, hkv=4, d=128, page=256, chunks_in_pool=32, pages_per_chunk=4, sel_chunks=4,
                            q_lens=[96] * 8, dtype=torch.bfloat16)

@@ -92,10 +92,49 @@ def test_chunking_and_chunk_bos(golden, chunks):
         assert len(chunks[meta["chunk_index"]]) == meta["original_tokens"]
 
 
-def test_partial_draft(golden, draft):
-    for ref in golden["runs"].values():
-        assert draft[0] == ref["draft_ids"]
-        assert draft[1] == ref["draft_confirmed"]
+def test_partial_draft(golden, draft, inputs):
+    _, query = inputs
+    for name, ref in golden["runs"].items():
+        if "draft_ids" in ref:          # variants that draft with score_draft_partial_rounds
+            assert draft[0] == ref["draft_ids"]
+            assert draft[1] == ref["draft_confirmed"]
+    # score_draft_partial_steps=2 stops after the same two slots (reference :2512-2593)
+    steps = golden["runs"]["draft_partial_steps"]
+    assert steps["selection_query_ids"] == query + draft[0] and steps["score_token_mask"] == [True] * len(query) + draft[1]
+
+
+def _draft_block(model, query, n_draft, fill):
+    """Draft of n_draft slots behind [BOS ‖ query] with no context; `fill(logits, block, last_logit)` is the transfer rule."""
+    ctx = [BOS] + query
+    with torch.no_grad():
+        out = model(torch.tensor([ctx]), attention_mask=None, position_ids=_positions(range(len(ctx))), use_cache=True)
+        last_logit = out.logits[0, -1]
+        block = torch.full((n_draft,), MASK, dtype=torch.long)
+        block[0] = int(torch.argmax(last_logit))
+        guard = 0
+        while bool((block == MASK).any()) and guard < n_draft + 8:
+            guard += 1
+            step = model(block.unsqueeze(0), attention_mask=None, position_ids=_positions(range(len(ctx) + n_draft)),
+                         past_key_values=out.past_key_values, use_cache=False)
+            block = fill(step.logits[0], block, last_logit)
+    return block.tolist()
+
+
+def test_draft_paths_of_the_config_defaults(golden, model, inputs):
+    """score_draft_partial_rounds unset (the dataclass default): a complete confidence-threshold draft (reference
+    :1828-1837 → generate_from_cache), or with score_draft_fixed_steps the fixed-step diffusion sampler (:2443-2510)."""
+    _, query = inputs
+    ref = golden["runs"]["draft_dataclass_defaults"]
+    n = ref["flags"]["score_draft_tokens"]
+    ids = _draft_block(model, query, n, lambda lg, blk, last: O.unmask_step(lg, blk, mask_token_id=MASK, threshold=ref["flags"]["threshold"],
+                                                                            last_logit=last)[0])
+    assert ref["selection_query_ids"] == query + ids and ref["score_token_mask"] is None
+    ref = golden["runs"]["draft_fixed_steps"]
+    n, steps = ref["flags"]["score_draft_tokens"], ref["flags"]["score_draft_steps"]
+    counts = iter(c for c in O.fixed_step_transfer_counts(n - 1, steps) if c > 0)
+    ids = _draft_block(model, query, n, lambda lg, blk, last: O.transfer_most_confident(lg, blk, mask_token_id=MASK, count=next(counts),
+                                                                                        last_logit=last))
+    assert ref["selection_query_ids"] == query + ids and ref["score_token_mask"] is None
 
 
 @pytest.fixture(scope="module")
@@ -118,6 +157,8 @@ def chunk_scores(golden, model, inputs, chunks, draft):
 
 def test_chunk_scores_and_selection(golden, chunk_scores):
     for name, ref in golden["runs"].items():
+        if name in ("draft_dataclass_defaults", "draft_fixed_steps"):   # other draft, other labels, other scores
+            continue
         want = [ref["chunk_scores"][str(i)] for i in range(len(chunk_scores))]
         assert max(abs(a - b) for a, b in zip(chunk_scores, want)) < 1e-5, name
         assert O.rank_chunks(chunk_scores, ref["flags"]["topk_chunks"]) == ref["selected_chunk_indices"], name
