@@ -28,6 +28,22 @@ def rel_err(a: torch.Tensor, b: torch.Tensor) -> float:
     return float((a - b).norm() / b.norm().clamp_min(1e-12))
 
 
+def row_rel_err(a: torch.Tensor, b: torch.Tensor) -> float:
+    """Worst (token, head) row: max_r ||a_r - b_r|| / ||b_r||. A few bad rows (a mis-masked last tile, one wrong page) vanish in
+    a norm over the whole output; they cannot hide here. Rows the reference leaves at zero must be zero."""
+    a, b = a.float().cpu(), b.float().cpu()
+    num, den = (a - b).norm(dim=-1), b.norm(dim=-1)
+    zero = den == 0
+    assert float(num[zero].max()) == 0.0 if bool(zero.any()) else True
+    return float((num[~zero] / den[~zero]).max())
+
+
+def assert_attention_close(out: torch.Tensor, ref: torch.Tensor, what=None, tol: float = 1e-2) -> None:
+    assert not torch.isnan(out).any(), what
+    assert rel_err(out, ref) < tol, what
+    assert row_rel_err(out, ref) < tol, what
+
+
 # ----------------------------------------------------------------------------------------------- (5)
 @pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float32])
 def test_store_kvcache_unified(ops, cuda_device, dtype):
@@ -224,7 +240,7 @@ def test_attention_tc_small_single_tile(ops, cuda_device):
                            q_lens=[16], dtype=torch.bfloat16)
     out, used = _run_attention(ops, cuda_device, case, impl="tc", num_splits=1)
     assert used == "tc"
-    assert rel_err(out, _ref_attention(case)) < ATTN_REL_TOL
+    assert_attention_close(out, _ref_attention(case))
 
 
 @pytest.mark.parametrize("num_splits", [1, 3, 0])
@@ -234,7 +250,7 @@ def test_attention_tc_ragged_batch(ops, cuda_device, num_splits):
     out, used = _run_attention(ops, cuda_device, case, impl="tc", num_splits=num_splits)
     assert used == "tc"
     ref = _ref_attention(case)
-    assert rel_err(out, ref) < ATTN_REL_TOL
+    assert_attention_close(out, ref)
     assert float((out.float().cpu() - ref).abs().max()) < 0.05
 
 
@@ -249,8 +265,7 @@ def test_attention_tc_uneven_split_and_fused_merge_ragged(ops, cuda_device):
         out, used = _run_attention(ops, cuda_device, case, impl="tc", **kwargs)
         assert used == "tc"
         ref = _ref_attention(case, **kwargs)
-        assert rel_err(out, ref) < ATTN_REL_TOL, kwargs
-        assert not torch.isnan(out).any(), kwargs
+        assert_attention_close(out, ref, kwargs)
     # twice in a row through the same workspace: the arrival counters must have returned to zero
     again, _ = _run_attention(ops, cuda_device, case, impl="tc")
     first, _ = _run_attention(ops, cuda_device, case, impl="tc")
@@ -267,8 +282,7 @@ def test_attention_tc_masks_and_prefill(ops, cuda_device):
                    dict(causal=True, with_cache=False), dict(with_cache=False), dict(mask=dense, with_cache=False)):
         out, used = _run_attention(ops, cuda_device, case, impl="tc", **kwargs)
         assert used == "tc"
-        assert rel_err(out, _ref_attention(case, **kwargs)) < ATTN_REL_TOL, kwargs
-        assert not torch.isnan(out).any(), kwargs
+        assert_attention_close(out, _ref_attention(case, **kwargs), kwargs)
 
 
 def test_attention_tc_mha_fp16(ops, cuda_device):
@@ -295,8 +309,7 @@ def test_attention_tc_mha_one_query_tile_ragged(ops, cuda_device, num_splits):
         out, used = _run_attention(ops, cuda_device, case, impl="tc", num_splits=num_splits, **kwargs)
         assert used == "tc"
         ref = _ref_attention(case, **kwargs)
-        assert not torch.isnan(out).any(), kwargs
-        assert rel_err(out, ref) < ATTN_REL_TOL, kwargs
+        assert_attention_close(out, ref, kwargs)
     again, _ = _run_attention(ops, cuda_device, case, impl="tc", num_splits=num_splits)
     first, _ = _run_attention(ops, cuda_device, case, impl="tc", num_splits=num_splits)
     assert torch.equal(again, first)
@@ -323,11 +336,33 @@ def test_attention_tc_whole_waves_then_split_tail(ops, cuda_device):
         out, used = _run_attention(ops, cuda_device, case, impl="tc", **kwargs)
         assert used == "tc"
         ref = _ref_attention(case, **kwargs)
-        assert not torch.isnan(out).any(), kwargs
-        assert rel_err(out, ref) < ATTN_REL_TOL, kwargs
+        assert_attention_close(out, ref, kwargs)
     again, _ = _run_attention(ops, cuda_device, case, impl="tc")
     first, _ = _run_attention(ops, cuda_device, case, impl="tc")
     assert torch.equal(again, first)
+
+
+def test_attention_tc_shapes_the_runtime_issues(ops, cuda_device):
+    """The shapes a Dream-7B-sized request really sends to the tensor-core kernel (28 / 4 heads, d 128, bf16):
+    the scoring forward — 8 packed causal rows of 1093 tokens, no cache; the joint prefill — one bidirectional sequence of
+    4193 tokens, no cache (its page write comes after attention); a denoise block — 96 and 32 new rows over a 17-page
+    table whose last page holds 65 tokens. Checked row by row."""
+    scoring = _attention_case(51, num_seqs=8, hq=28, hkv=4, d=128, page=256, chunks_in_pool=1, pages_per_chunk=1, sel_chunks=1,
+                              q_lens=[1093] * 8, dtype=torch.bfloat16)
+    out, used = _run_attention(ops, cuda_device, scoring, impl="auto", causal=True, with_cache=False)
+    assert used == "tc"
+    assert_attention_close(out, _ref_attention(scoring, causal=True, with_cache=False), "causal 8 x 1093")
+    joint = _attention_case(52, num_seqs=1, hq=28, hkv=4, d=128, page=256, chunks_in_pool=1, pages_per_chunk=1, sel_chunks=1,
+                            q_lens=[4193], dtype=torch.bfloat16)
+    out, used = _run_attention(ops, cuda_device, joint, impl="auto", with_cache=False)
+    assert used == "tc"
+    assert_attention_close(out, _ref_attention(joint, with_cache=False), "bidirectional 4193")
+    block = _attention_case(53, num_seqs=2, hq=28, hkv=4, d=128, page=256, chunks_in_pool=17, pages_per_chunk=1, sel_chunks=17,
+                            q_lens=[32, 96], dtype=torch.bfloat16, ctx_tail=256 - 65)
+    assert block["seq_lens"] == [17 * 256 + 32, 16 * 256 + 65 + 96]
+    out, used = _run_attention(ops, cuda_device, block, impl="auto")
+    assert used == "tc"
+    assert_attention_close(out, _ref_attention(block), "decode rows over a ragged 17-page table")
 
 
 def test_attention_tc_uninitialised_pool_tail_is_harmless(ops, cuda_device):
@@ -355,7 +390,7 @@ def test_attention_op_level_config_full_size(ops, cuda_device):
     out, used = _run_attention(ops, cuda_device, case, impl="auto")
     assert used == "tc"
     ref = _ref_attention(case)
-    assert rel_err(out, ref) < ATTN_REL_TOL
+    assert_attention_close(out, ref)
     # the SIMT kernel is an independent on-device witness of the same answer
     out_simt, _ = _run_attention(ops, cuda_device, case, impl="simt")
     assert rel_err(out_simt, ref) < ATTN_REL_TOL

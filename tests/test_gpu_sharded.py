@@ -17,6 +17,8 @@ pytestmark = pytest.mark.gpu
 
 HERE = os.path.dirname(os.path.abspath(__file__))
 ROOT = os.path.dirname(HERE)
+if ROOT not in sys.path:
+    sys.path.insert(0, ROOT)
 
 
 def _free_port():
@@ -25,7 +27,7 @@ def _free_port():
         return s.getsockname()[1]
 
 
-def _rank_main(rank, world, port, ckpt, flags, decode_rank, out):
+def _rank_main(rank, world, port, ckpt, flags, decode_rank, out, substitute=None):
     sys.path.insert(0, ROOT)
     sys.path.insert(0, os.path.join(HERE, "golden"))
     os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
@@ -41,6 +43,17 @@ def _rank_main(rank, world, port, ckpt, flags, decode_rank, out):
 
         rt = load_fastdllm_parallelcomp(pretrained=ckpt, device=f"cuda:{rank}", dtype="float32", **flags)
         context, query = make_golden.toy_inputs()
+        if substitute is not None:
+            # per-head keep lists of the reference, by chunk content: where this library and the CPU reference break an exact
+            # tie at the cut differently, the reference's pick is used so that the rest of the path is held to its ids
+            orig_keep = rt._keep_positions_per_layer_per_head_for_chunk
+
+            def keep_ph(prefix_ids, chunk_ids, query_ids):
+                mine = orig_keep(prefix_ids, chunk_ids, query_ids)
+                theirs = substitute[tuple(chunk_ids)]
+                return [torch.tensor(layer, dtype=t.dtype, device=t.device) for layer, t in zip(theirs, mine)]
+
+            rt._keep_positions_per_layer_per_head_for_chunk = keep_ph
         result = ShardedChunkPrefill(rt).generate(prefix_ids=rt.bos_ids(), context_ids=context, query_ids=query, decode_rank=decode_rank)
         ops.check_status(rt.device)
         leaked = rt.model.num_pages - rt.model.allocator.num_free_pages
@@ -68,22 +81,39 @@ def test_sharded_generate_matches_reference_golden(tmp_path_factory, variant):
     world = 2 if torch.cuda.device_count() >= 2 else 1
     decode_rank = world - 1
     ctx = mp.get_context("spawn")
-    out = ctx.Queue()
-    port = _free_port()
-    procs = [ctx.Process(target=_rank_main, args=(r, world, port, ckpt, ref["flags"], decode_rank, out)) for r in range(world)]
-    for p in procs:
-        p.start()
-    got = out.get(timeout=600)
-    for p in procs:
-        p.join(timeout=120)
-    assert all(p.exitcode == 0 for p in procs), [p.exitcode for p in procs]
+
+    def launch(substitute=None):
+        out = ctx.Queue()
+        port = _free_port()
+        procs = [ctx.Process(target=_rank_main, args=(r, world, port, ckpt, ref["flags"], decode_rank, out, substitute)) for r in range(world)]
+        for p in procs:
+            p.start()
+        got = out.get(timeout=600)
+        for p in procs:
+            p.join(timeout=120)
+        assert all(p.exitcode == 0 for p in procs), [p.exitcode for p in procs]
+        return got
+
+    got = launch()
     assert got["leaked"] == 0
     assert got["selected"] == ref["selected_chunk_indices"]
     assert max(abs(a - ref["chunk_scores"][str(i)]) for i, a in enumerate(got["scores"])) < 1e-4
     assert got["cache_tokens"] == ref["cache_tokens"] and got["removed_tokens"] == ref["removed_tokens"]
     assert got["meta"] == [(m["chunk_index"], m["kept_tokens"], m["cache_start"], m["cache_end"], m["rope_start"]) for m in ref["chunk_meta"]]
     match = sum(int(a == b) for a, b in zip(got["sequences"], ref["sequences"])) / len(ref["sequences"])
+    if match < 0.99 and "keep_positions_per_head" in ref:
+        # Per-head eviction: exact ties at the cut may be broken differently from the CPU reference (tests/test_gpu_runtime.py
+        # checks that every differing pick is such a tie), after which a random-weight toy model drifts. Run again with the
+        # reference's picks among the ties, so that the sharded per-head compaction, hand-off and decode still face the gate.
+        from oracle import hotpath as O
+
+        context, _ = make_golden.toy_inputs()
+        size = ref["flags"]["chunk_size"]
+        chunks = [O.maybe_prepend_bos_to_chunk(c, [1], size) for c in O.split_token_chunks(context, size)]
+        substitute = {tuple(chunks[ci]): lists for ci, lists in zip(ref["selected_chunk_indices"], ref["keep_positions_per_head"])}
+        got = launch(substitute)
+        assert got["leaked"] == 0 and got["selected"] == ref["selected_chunk_indices"]
+        match = sum(int(a == b) for a, b in zip(got["sequences"], ref["sequences"])) / len(ref["sequences"])
+        print(f"{variant}: rerun with the reference's picks among exactly tied scores")
     print(f"{variant}: world {world}, greedy token match {match:.3f}")
-    # per-head eviction: exact ties at the cut may be broken differently from the CPU reference (see test_gpu_runtime),
-    # after which a random-weight toy model drifts; everything up to the keep lists is still exact
-    assert match >= (0.99 if "per_head" not in variant else 0.0)
+    assert match >= 0.99
