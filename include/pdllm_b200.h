@@ -23,7 +23,7 @@
 extern "C" {
 #endif
 
-#define PDLLM_ABI_VERSION 3
+#define PDLLM_ABI_VERSION 4
 
 /* element types of floating-point tensors */
 #define PDLLM_F32 0
@@ -310,6 +310,27 @@ int pdllm_rope_inplace(void* x, const void* cos_tab, const void* sin_tab, int64_
 /* out[t, i] = dtype(silu(gate_up[t, i])) * gate_up[t, inter + i] */
 int pdllm_silu_mul(const void* gate_up, void* out, int64_t n_tokens, int inter, int64_t gu_stride, int64_t out_stride, int dtype,
                    void* stream);
+
+/* ------------------------------------------------------------------------------------------------
+ * Linear layers of the transformer block on the tensor cores: out[m, n] = x[m, k] . weight[n, k]^T (+ bias[n])
+ * replaces QKVParallelLinear / MergedColumnParallelLinear / RowParallelLinear.forward (F.linear)
+ *            prefilling_dllm_engine/prefilling_dllm/layers/linear.py:108-244
+ *          ParallelLMHead.forward                      .../layers/embed_head.py:63-74
+ *          SiluAndMul.forward fused behind gate_up_proj .../layers/activation.py:12-14, models/dream.py:130-136
+ * x: [m, k] rows with stride x_stride, weight: [n, k] rows with stride w_stride (the nn.Linear layout), out: [m, n] rows
+ * with stride out_stride (all in elements); bf16 or fp16, fp32 accumulation, the result rounded once to the dtype.
+ * epilogue PDLLM_EPI_SILU_MUL: the weight rows are INTERLEAVED (row 2i = gate_i, row 2i + 1 = up_i) and
+ *   out[m, i] = dtype(silu(dtype(gate_i))) * dtype(up_i), out is [m, n / 2]; no bias.
+ * Up to 128 rows the weights are streamed once from HBM with the k-blocks dealt evenly over all SMs (stream-K); that
+ * path needs pdllm_linear_workspace_bytes() of workspace whose first 64 KB hold arrival counters: zero-fill it once and
+ * pass workspace_zeroed != 0 (the kernel returns every counter to zero), or pass 0 and a memset is enqueued first.
+ * ---------------------------------------------------------------------------------------------- */
+#define PDLLM_EPI_NONE 0
+#define PDLLM_EPI_SILU_MUL 1
+int64_t pdllm_linear_workspace_bytes(int64_t m, int64_t n, int64_t k);
+int pdllm_linear(const void* x, int64_t x_stride, const void* weight, int64_t w_stride, const void* bias, void* out,
+                 int64_t out_stride, int64_t m, int64_t n, int64_t k, int dtype, int epilogue, void* workspace,
+                 int64_t workspace_bytes, int workspace_zeroed, int32_t* status, void* stream);
 
 #ifdef __cplusplus
 }

@@ -1,0 +1,514 @@
+// Linear layers on the 5th-generation tensor cores (sm_100a): out[M, N] = x[M, K] · W[N, K]^T (+ bias) with an optional
+// fused SiLU(gate)·up epilogue, for the QKV / O / gate-up / down projections and the LM head of the Dream / LLaDA block.
+// bf16 or fp16 operands, fp32 accumulation in TMEM, operands staged by TMA (128-byte swizzle) through a ring of
+// shared-memory stages, one thread issuing tcgen05.mma, four warps draining the accumulator.
+//
+// Both operands are K-major ([rows, K] row-major), so either can be the 128-row "A" side of the instruction:
+//   * few rows (M <= 128: one block of decode rows, a draft, a commit): the WEIGHTS are A. A CTA streams 128 weight rows
+//     x K through shared memory once, the activations are the narrow B side (16..128 columns), the accumulator is
+//     out^T [128 features x M tokens]. The step is bound by reading the weights from HBM, so the (feature tile, k-block)
+//     units are dealt to the CTAs stream-K style: every CTA of the grid (one per SM) gets the same number of 16 KB weight
+//     blocks to stream, whatever N and K are; a feature tile that ends up spread over several CTAs is summed by the CTA
+//     that finishes it last, in CTA order, through fp32 partials in the workspace (an arrival counter per tile; no CTA
+//     ever waits for another).
+//   * many rows (prefill, scoring): the ACTIVATIONS are A: tiles of 128 tokens x 256 (or 128) features, all of K per tile,
+//     tiles dealt round-robin with the token tiles of one weight tile adjacent so that concurrent CTAs share it in L2.
+// The accumulator is double-buffered in TMEM: while the epilogue warps drain tile i, the tensor core works on tile i+1.
+// Every mbarrier wait is bounded; on expiry the CTA raises PDLLM_S_WAIT_TIMEOUT, stops issuing and frees its TMEM.
+#pragma once
+
+#include <type_traits>
+
+#include "attn_sm100.cuh"
+
+namespace pdllm {
+namespace gemm {
+
+using tc::mbar_init; using tc::mbar_expect_tx; using tc::mbar_arrive; using tc::mbar_wait; using tc::smem_u32;
+using tc::fence_barrier_init; using tc::tc_fence_before; using tc::tc_fence_after; using tc::tc_wait_ld;
+using tc::umma_ss; using tc::umma_commit; using tc::desc_kmajor_sw128; using tc::make_idesc;
+
+constexpr int kRowsA = 128;            // rows of the A tile = TMEM lanes
+constexpr int kBlockK = 64;            // elements of K per stage: one 128-byte swizzle row
+constexpr int kThreads = 192;          // warp 0: TMA producer, warp 1: MMA issuer + TMEM owner, warps 2-5: epilogue
+constexpr int kEpiWarp0 = 2;
+constexpr int kEpiThreads = 128;
+constexpr int kSmemBudget = 200 * 1024;
+constexpr int kMaxStages = 12;
+constexpr int64_t kCounterHeaderBytes = 64 * 1024;   // arrival counters of the feature tiles (stream-K), zero between launches
+
+__host__ __device__ constexpr int stage_bytes(int bn) { return kRowsA * kBlockK * 2 + bn * kBlockK * 2; }
+__host__ __device__ constexpr int num_stages(int bn) {
+  return kSmemBudget / stage_bytes(bn) < kMaxStages ? kSmemBudget / stage_bytes(bn) : kMaxStages;
+}
+__host__ __device__ constexpr int smem_bytes(int bn) { return num_stages(bn) * stage_bytes(bn) + 1024 /* align */ + 512 /* barriers */; }
+__host__ __device__ constexpr uint32_t tmem_cols(int bn) { return 2 * bn < 32 ? 32u : static_cast<uint32_t>(2 * bn); }
+
+struct Args {
+  void* out; const void* bias;
+  float* partials;       // stream-K: [2 * grid][bn][128] fp32
+  int* tile_counters;    // stream-K: [feature tiles], zero on entry, zero on exit
+  int32_t* status;
+  long long* trace;      // unused; the shared bounded-wait helper expects the member
+  int64_t out_stride;    // elements
+  int64_t m, n, k;
+  int kb_total;          // k-blocks of 64
+  int m_tiles, n_tiles;  // tiles along tokens / features
+  int64_t units;         // stream-K: n_tiles * kb_total
+  int epilogue;
+};
+
+__device__ __forceinline__ void tma_load_2d(const CUtensorMap* map, uint64_t* bar, void* dst, int c0, int c1) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%3, %4}], [%2];"
+      ::"r"(smem_u32(dst)), "l"(reinterpret_cast<uint64_t>(map)), "r"(smem_u32(bar)), "r"(c0), "r"(c1)
+      : "memory");
+}
+__device__ __forceinline__ void tmem_alloc_cols(uint32_t* dst_smem, uint32_t cols) {
+  asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(dst_smem)), "r"(cols) : "memory");
+  asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+}
+
+// One piece of work of a CTA: k-blocks [kb0, kb1) of the tile at (a_row0, b_row0).
+struct Segment {
+  int a_row0, b_row0;   // first row of the A / B tile in its tensor
+  int kb0, kb1;
+  int tile;             // stream-K: feature tile index (arrival counter); otherwise unused
+  bool partial;         // stream-K: the tile's k-blocks are shared with other CTAs
+};
+
+// Stream-K bookkeeping: unit u = (feature tile, k-block); CTA c owns units [c*U/G, (c+1)*U/G).
+__device__ __forceinline__ int64_t sk_first_unit(int64_t c, int64_t units, int64_t grid) { return c * units / grid; }
+__device__ __forceinline__ int sk_cta_of(int64_t unit, int64_t units, int64_t grid) {
+  return static_cast<int>(((unit + 1) * grid + units - 1) / units - 1);
+}
+
+template <bool kSwap, int kBN>
+struct Schedule {
+  // position in this CTA's list of segments
+  int64_t cursor, end;      // normal: tile index (stride gridDim.x) / number of tiles; stream-K: unit range
+  __device__ __forceinline__ void init(const Args& a) {
+    if (kSwap) {
+      cursor = sk_first_unit(blockIdx.x, a.units, gridDim.x);
+      end = sk_first_unit(static_cast<int64_t>(blockIdx.x) + 1, a.units, gridDim.x);
+    } else {
+      cursor = blockIdx.x;
+      end = static_cast<int64_t>(a.m_tiles) * a.n_tiles;
+    }
+  }
+  __device__ __forceinline__ bool next(const Args& a, Segment& s) {
+    if (cursor >= end) return false;
+    if (kSwap) {
+      const int tile = static_cast<int>(cursor / a.kb_total);
+      const int64_t t0 = static_cast<int64_t>(tile) * a.kb_total;
+      const int64_t stop = end < t0 + a.kb_total ? end : t0 + a.kb_total;
+      s.tile = tile;
+      s.a_row0 = tile * kRowsA;      // weight rows
+      s.b_row0 = 0;                  // all tokens (M <= kBN)
+      s.kb0 = static_cast<int>(cursor - t0);
+      s.kb1 = static_cast<int>(stop - t0);
+      s.partial = !(s.kb0 == 0 && s.kb1 == a.kb_total);
+      cursor = stop;
+    } else {
+      const int mt = static_cast<int>(cursor % a.m_tiles), nt = static_cast<int>(cursor / a.m_tiles);
+      s.tile = static_cast<int>(cursor);
+      s.a_row0 = mt * kRowsA;        // tokens
+      s.b_row0 = nt * kBN;           // weight rows
+      s.kb0 = 0; s.kb1 = a.kb_total;
+      s.partial = false;
+      cursor += gridDim.x;
+    }
+    return true;
+  }
+};
+
+template <typename T>
+__device__ __forceinline__ float round_to(float v) { return to_f32<T>(from_f32<T>(v)); }
+
+// silu(gate) * up with the rounding of the unfused path: the projection output is rounded to T, silu is evaluated in fp32
+// and rounded to T, the product is rounded to T.
+template <typename T>
+__device__ __forceinline__ T silu_mul(float gate_acc, float up_acc) {
+  const float g = round_to<T>(gate_acc), u = round_to<T>(up_acc);
+  const float act = round_to<T>(g / (1.f + expf(-g)));
+  return from_f32<T>(act * u);
+}
+
+template <bool kSwap, int kBN, typename T>
+__global__ void __launch_bounds__(kThreads, 1)
+linear_sm100_kernel(const __grid_constant__ CUtensorMap a_map, const __grid_constant__ CUtensorMap b_map, const Args a) {
+  constexpr int kStages = num_stages(kBN);
+  constexpr int kStageBytes = stage_bytes(kBN);
+  constexpr int kABytes = kRowsA * kBlockK * 2;
+  constexpr bool kBf16 = std::is_same<T, __nv_bfloat16>::value;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + kStages * kStageBytes);
+  uint64_t* full = bars;                    // [kStages] TMA landed
+  uint64_t* empty = bars + kStages;         // [kStages] MMAs that read the stage are done
+  uint64_t* acc_full = bars + 2 * kStages;  // [2] accumulator complete
+  uint64_t* acc_empty = acc_full + 2;       // [2] accumulator drained (4 arrivals: one per epilogue warp)
+  uint64_t* epi_all = acc_empty + 2;        // 128 arrivals: every epilogue thread published its partial
+  uint64_t* epi_go = epi_all + 1;           // 1 arrival: the verdict "this CTA reduces the tile" is in shared memory
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(epi_go + 1);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+  volatile int* reduce_flag = abort_flag + 1;
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+
+  if (warp == 1) {
+    if (lane == 0) {
+      for (int i = 0; i < kStages; ++i) { mbar_init(&full[i], 1); mbar_init(&empty[i], 1); }
+      for (int i = 0; i < 2; ++i) { mbar_init(&acc_full[i], 1); mbar_init(&acc_empty[i], 4); }
+      mbar_init(epi_all, kEpiThreads);
+      mbar_init(epi_go, 1);
+      abort_flag[0] = 0;
+      fence_barrier_init();
+    }
+    __syncwarp();
+    tmem_alloc_cols(tmem_slot, tmem_cols(kBN));
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+
+  Schedule<kSwap, kBN> sched;
+  sched.init(a);
+  Segment seg;
+
+  if (warp == 0) {
+    // =========================== TMA producer ===========================
+    if (lane == 0) {
+      int stage = 0; uint32_t phase = 0;
+      bool ok = true;
+      while (ok && sched.next(a, seg)) {
+        for (int kb = seg.kb0; kb < seg.kb1 && ok; ++kb) {
+          ok = mbar_wait<true>(&empty[stage], phase ^ 1, abort_flag, a);   // a fresh barrier passes the first lap
+          if (!ok) break;
+          uint8_t* sa = smem + stage * kStageBytes;
+          mbar_expect_tx(&full[stage], kStageBytes);
+          tma_load_2d(&a_map, &full[stage], sa, kb * kBlockK, seg.a_row0);
+          tma_load_2d(&b_map, &full[stage], sa + kABytes, kb * kBlockK, seg.b_row0);
+          if (++stage == kStages) { stage = 0; phase ^= 1; }
+        }
+      }
+      if (!ok) {   // the CTA is abandoning its result: give copies in flight a bounded moment to land
+        const long long t0 = clock64();
+        while (clock64() - t0 < 200000) { }
+      }
+    }
+    __syncwarp();
+  } else if (warp == 1) {
+    // =========================== MMA issuer ===========================
+    if (lane == 0) {
+      const uint32_t idesc = make_idesc(kBf16, false, kBN);
+      int stage = 0; uint32_t phase = 0;
+      int n_seg = 0;
+      bool ok = true;
+      while (ok && sched.next(a, seg)) {
+        const int acc = n_seg & 1;
+        const uint32_t acc_phase = (n_seg >> 1) & 1;
+        ++n_seg;
+        ok = mbar_wait<true>(&acc_empty[acc], acc_phase ^ 1, abort_flag, a);
+        if (!ok) break;
+        tc_fence_after();
+        const uint32_t d = tmem_base + static_cast<uint32_t>(acc * kBN);
+        for (int kb = seg.kb0; kb < seg.kb1 && ok; ++kb) {
+          ok = mbar_wait<true>(&full[stage], phase, abort_flag, a);
+          if (!ok) break;
+          tc_fence_after();
+          const uint32_t sa = smem_u32(smem + stage * kStageBytes), sb = sa + kABytes;
+#pragma unroll
+          for (int kk = 0; kk < kBlockK / 16; ++kk) {
+            umma_ss(d, desc_kmajor_sw128(sa + kk * 32), desc_kmajor_sw128(sb + kk * 32), idesc, (kb > seg.kb0 || kk > 0) ? 1u : 0u);
+          }
+          umma_commit(&empty[stage]);
+          if (++stage == kStages) { stage = 0; phase ^= 1; }
+        }
+        if (ok) umma_commit(&acc_full[acc]);
+      }
+    }
+    __syncwarp();
+  } else {
+    // =========================== epilogue: warps 2-5, thread = accumulator row ===========================
+    const int quarter = warp & 3;                       // the TMEM lanes a warp may read: 32 * (warp id mod 4)
+    const int r = quarter * 32 + lane;                  // accumulator row
+    const int et = threadIdx.x - kEpiWarp0 * 32;        // 0..127
+    const uint32_t lane_base = static_cast<uint32_t>(quarter * 32) << 16;
+    T* out = reinterpret_cast<T*>(a.out);
+    const T* bias = reinterpret_cast<const T*>(a.bias);
+    const bool silu = a.epilogue == PDLLM_EPI_SILU_MUL;
+    int n_seg = 0;
+    uint32_t epi_phase = 0;
+    bool ok = true;
+    while (ok && sched.next(a, seg)) {
+      const int acc = n_seg & 1;
+      const uint32_t acc_phase = (n_seg >> 1) & 1;
+      ++n_seg;
+      ok = mbar_wait(&acc_full[acc], acc_phase, abort_flag, a);
+      if (!ok) break;
+      tc_fence_after();
+      const uint32_t t_acc = tmem_base + lane_base + static_cast<uint32_t>(acc * kBN);
+
+      if (kSwap) {
+        // accumulator = out^T: row r = feature n, column j = token j
+        const int64_t n = static_cast<int64_t>(seg.a_row0) + r;
+        const int m_count = static_cast<int>(a.m < kBN ? a.m : kBN);
+        auto emit = [&](int j, float v) {       // one (token, feature) value of the finished tile
+          if (silu) {
+            const float other = __shfl_xor_sync(0xffffffffu, v, 1);
+            if ((lane & 1) == 0 && n + 1 < a.n) out[static_cast<int64_t>(j) * a.out_stride + (n >> 1)] = silu_mul<T>(v, other);
+          } else if (n < a.n) {
+            if (bias != nullptr) v += to_f32<T>(bias[n]);
+            out[static_cast<int64_t>(j) * a.out_stride + n] = from_f32<T>(v);
+          }
+        };
+        if (!seg.partial) {
+#pragma unroll 1
+          for (int c0 = 0; c0 < kBN; c0 += 16) {
+            uint32_t v[16];
+            tc::tmem_ld16(t_acc + c0, v);
+            tc_wait_ld();
+#pragma unroll
+            for (int i = 0; i < 16; ++i) {
+              if (c0 + i < m_count) emit(c0 + i, __uint_as_float(v[i]));      // uniform across the warp
+            }
+          }
+          tc_fence_before();
+          __syncwarp();
+          if (lane == 0) mbar_arrive(&acc_empty[acc]);
+        } else {
+          // publish this CTA's share of the tile; slot 0 = the CTA's first tile, slot 1 = its last
+          const int first_tile = static_cast<int>(sk_first_unit(blockIdx.x, a.units, gridDim.x) / a.kb_total);
+          float* mine = a.partials + (static_cast<int64_t>(blockIdx.x) * 2 + (seg.tile == first_tile ? 0 : 1)) * (kBN * kRowsA);
+#pragma unroll 1
+          for (int c0 = 0; c0 < kBN; c0 += 16) {
+            uint32_t v[16];
+            tc::tmem_ld16(t_acc + c0, v);
+            tc_wait_ld();
+#pragma unroll
+            for (int i = 0; i < 16; ++i) {
+              if (c0 + i < m_count) mine[(c0 + i) * kRowsA + r] = __uint_as_float(v[i]);
+            }
+          }
+          tc_fence_before();
+          __syncwarp();
+          if (lane == 0) mbar_arrive(&acc_empty[acc]);
+          __threadfence();
+          mbar_arrive(epi_all);
+          if (et == 0) {
+            ok = mbar_wait(epi_all, epi_phase, abort_flag, a);
+            if (ok) {
+              const int64_t t0 = static_cast<int64_t>(seg.tile) * a.kb_total;
+              const int parts = sk_cta_of(t0 + a.kb_total - 1, a.units, gridDim.x) - sk_cta_of(t0, a.units, gridDim.x) + 1;
+              const int prev = atomicAdd(&a.tile_counters[seg.tile], 1);
+              const int last = prev == parts - 1 ? 1 : 0;
+              if (last) a.tile_counters[seg.tile] = 0;      // every share has arrived: ready for the next launch
+              reduce_flag[0] = last;
+              mbar_arrive(epi_go);
+            }
+          }
+          ok = mbar_wait(epi_go, epi_phase, abort_flag, a);
+          epi_phase ^= 1;
+          if (!ok) break;
+          if (reduce_flag[0]) {
+            __threadfence();
+            const int64_t t0 = static_cast<int64_t>(seg.tile) * a.kb_total;
+            const int c_first = sk_cta_of(t0, a.units, gridDim.x), c_last = sk_cta_of(t0 + a.kb_total - 1, a.units, gridDim.x);
+#pragma unroll 1
+            for (int j = 0; j < m_count; ++j) {
+              float sum = 0.f;
+              for (int c = c_first; c <= c_last; ++c) {     // fixed order: the result does not depend on who reduces
+                const int c_tile0 = static_cast<int>(sk_first_unit(c, a.units, gridDim.x) / a.kb_total);
+                const float* part = a.partials + (static_cast<int64_t>(c) * 2 + (seg.tile == c_tile0 ? 0 : 1)) * (kBN * kRowsA);
+                sum += __ldcg(part + j * kRowsA + r);
+              }
+              emit(j, sum);
+            }
+          }
+        }
+      } else {
+        // accumulator row r = token, columns = features
+        const int64_t m = static_cast<int64_t>(seg.a_row0) + r;
+        const bool row_ok = m < a.m;
+#pragma unroll 1
+        for (int c0 = 0; c0 < kBN; c0 += 32) {
+          uint32_t v[32];
+          tc::tmem_ld32(t_acc + c0, v);
+          tc_wait_ld();
+          const int64_t n0 = static_cast<int64_t>(seg.b_row0) + c0;
+          if (!row_ok || n0 >= a.n) continue;
+          if (silu) {
+            T* dst = out + m * a.out_stride + (n0 >> 1);
+            if (n0 + 32 <= a.n) {
+              uint32_t packed[8];
+#pragma unroll
+              for (int i = 0; i < 8; ++i) {
+                T lo = silu_mul<T>(__uint_as_float(v[4 * i]), __uint_as_float(v[4 * i + 1]));
+                T hi = silu_mul<T>(__uint_as_float(v[4 * i + 2]), __uint_as_float(v[4 * i + 3]));
+                packed[i] = static_cast<uint32_t>(*reinterpret_cast<uint16_t*>(&lo)) | (static_cast<uint32_t>(*reinterpret_cast<uint16_t*>(&hi)) << 16);
+              }
+              uint4* d4 = reinterpret_cast<uint4*>(dst);
+              d4[0] = make_uint4(packed[0], packed[1], packed[2], packed[3]);
+              d4[1] = make_uint4(packed[4], packed[5], packed[6], packed[7]);
+            } else {
+              for (int i = 0; i < 16 && n0 + 2 * i + 1 < a.n; ++i) dst[i] = silu_mul<T>(__uint_as_float(v[2 * i]), __uint_as_float(v[2 * i + 1]));
+            }
+          } else {
+            T* dst = out + m * a.out_stride + n0;
+            if (n0 + 32 <= a.n) {
+              uint32_t packed[16];
+#pragma unroll
+              for (int i = 0; i < 16; ++i) {
+                float x0 = __uint_as_float(v[2 * i]), x1 = __uint_as_float(v[2 * i + 1]);
+                if (bias != nullptr) { x0 += to_f32<T>(bias[n0 + 2 * i]); x1 += to_f32<T>(bias[n0 + 2 * i + 1]); }
+                T lo = from_f32<T>(x0), hi = from_f32<T>(x1);
+                packed[i] = static_cast<uint32_t>(*reinterpret_cast<uint16_t*>(&lo)) | (static_cast<uint32_t>(*reinterpret_cast<uint16_t*>(&hi)) << 16);
+              }
+              uint4* d4 = reinterpret_cast<uint4*>(dst);
+#pragma unroll
+              for (int i = 0; i < 4; ++i) d4[i] = make_uint4(packed[4 * i], packed[4 * i + 1], packed[4 * i + 2], packed[4 * i + 3]);
+            } else {
+              for (int i = 0; i < 32 && n0 + i < a.n; ++i) {
+                float x = __uint_as_float(v[i]);
+                if (bias != nullptr) x += to_f32<T>(bias[n0 + i]);
+                dst[i] = from_f32<T>(x);
+              }
+            }
+          }
+        }
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&acc_empty[acc]);
+      }
+    }
+  }
+
+  // ---- teardown ----
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tc::tmem_dealloc(tmem_base, tmem_cols(kBN));
+  }
+}
+
+// ---- host side ---------------------------------------------------------------------------------------------
+struct Plan {
+  bool swap;
+  int bn;         // B-tile rows: token tile (swap) or feature tile (normal)
+  int m_tiles, n_tiles, kb_total;
+  int64_t units;  // stream-K units
+  int grid;
+};
+
+inline Plan make_plan(int64_t m, int64_t n, int64_t k) {
+  Plan pl;
+  const int sms = sm_count();
+  pl.kb_total = static_cast<int>((k + kBlockK - 1) / kBlockK);
+  pl.swap = m <= 128;
+  if (pl.swap) {
+    pl.bn = m <= 16 ? 16 : m <= 32 ? 32 : m <= 64 ? 64 : 128;
+    pl.m_tiles = 1;
+    pl.n_tiles = static_cast<int>((n + kRowsA - 1) / kRowsA);
+    pl.units = static_cast<int64_t>(pl.n_tiles) * pl.kb_total;
+    pl.grid = static_cast<int>(pl.units < sms ? pl.units : sms);
+  } else {
+    pl.m_tiles = static_cast<int>((m + kRowsA - 1) / kRowsA);
+    const int64_t tiles256 = static_cast<int64_t>(pl.m_tiles) * ((n + 255) / 256);
+    pl.bn = tiles256 >= sms ? 256 : 128;      // narrower tiles when wide ones would leave SMs without work
+    pl.n_tiles = static_cast<int>((n + pl.bn - 1) / pl.bn);
+    pl.units = 0;
+    const int64_t tiles = static_cast<int64_t>(pl.m_tiles) * pl.n_tiles;
+    pl.grid = static_cast<int>(tiles < sms ? tiles : sms);
+  }
+  if (pl.grid < 1) pl.grid = 1;
+  return pl;
+}
+
+inline int64_t workspace_bytes(int64_t m, int64_t n, int64_t k) {
+  if (m <= 0 || n <= 0) return 0;
+  const Plan pl = make_plan(m, n, k);
+  if (!pl.swap) return 0;
+  // a grid never exceeds the SM count; sized for it so that one workspace serves every layer of a model
+  return kCounterHeaderBytes + static_cast<int64_t>(2) * sm_count() * pl.bn * kRowsA * 4;
+}
+
+template <bool kSwap, int kBN, typename T>
+inline int launch_one(const CUtensorMap& a_map, const CUtensorMap& b_map, const Args& a, int grid, cudaStream_t stream) {
+  auto* fn = linear_sm100_kernel<kSwap, kBN, T>;
+  {
+    static std::mutex mu;
+    static bool done[64] = {false};
+    int dev = 0;
+    cudaGetDevice(&dev);
+    std::lock_guard<std::mutex> lock(mu);
+    if (dev < 0 || dev >= 64 || !done[dev]) {
+      cudaError_t e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, smem_bytes(kBN));
+      if (e != cudaSuccess) return fail(static_cast<int>(e), "cudaFuncSetAttribute(linear): %s", cudaGetErrorString(e));
+      if (dev >= 0 && dev < 64) done[dev] = true;
+    }
+  }
+  fn<<<static_cast<unsigned>(grid), kThreads, smem_bytes(kBN), stream>>>(a_map, b_map, a);
+  return check_launch("linear_sm100_kernel");
+}
+
+template <typename T>
+inline int launch_typed(const Plan& pl, const CUtensorMap& a_map, const CUtensorMap& b_map, const Args& a, cudaStream_t stream) {
+  if (pl.swap) {
+    switch (pl.bn) {
+      case 16: return launch_one<true, 16, T>(a_map, b_map, a, pl.grid, stream);
+      case 32: return launch_one<true, 32, T>(a_map, b_map, a, pl.grid, stream);
+      case 64: return launch_one<true, 64, T>(a_map, b_map, a, pl.grid, stream);
+      default: return launch_one<true, 128, T>(a_map, b_map, a, pl.grid, stream);
+    }
+  }
+  if (pl.bn == 256) return launch_one<false, 256, T>(a_map, b_map, a, pl.grid, stream);
+  return launch_one<false, 128, T>(a_map, b_map, a, pl.grid, stream);
+}
+
+inline int launch(const void* x, int64_t x_stride, const void* w, int64_t w_stride, const void* bias, void* out, int64_t out_stride,
+                  int64_t m, int64_t n, int64_t k, int dtype, int epilogue, void* workspace, int64_t ws_bytes, int workspace_zeroed,
+                  int32_t* status, cudaStream_t stream) {
+  const bool bf16 = dtype == PDLLM_BF16;
+  const Plan pl = make_plan(m, n, k);
+  CUtensorMap x_map, w_map;
+  int rc;
+  {
+    uint64_t dims[2] = {static_cast<uint64_t>(k), static_cast<uint64_t>(m)};
+    uint64_t str[1] = {static_cast<uint64_t>(x_stride) * 2};
+    uint32_t box[2] = {kBlockK, static_cast<uint32_t>(pl.swap ? pl.bn : kRowsA)};
+    if ((rc = tc::encode_map(&x_map, bf16, x, 2, dims, str, box)) != 0) return rc;
+  }
+  {
+    uint64_t dims[2] = {static_cast<uint64_t>(k), static_cast<uint64_t>(n)};
+    uint64_t str[1] = {static_cast<uint64_t>(w_stride) * 2};
+    uint32_t box[2] = {kBlockK, static_cast<uint32_t>(pl.swap ? kRowsA : pl.bn)};
+    if ((rc = tc::encode_map(&w_map, bf16, w, 2, dims, str, box)) != 0) return rc;
+  }
+  Args a;
+  a.out = out; a.bias = bias; a.status = status; a.trace = nullptr;
+  a.out_stride = out_stride; a.m = m; a.n = n; a.k = k;
+  a.kb_total = pl.kb_total; a.m_tiles = pl.m_tiles; a.n_tiles = pl.n_tiles; a.units = pl.units; a.epilogue = epilogue;
+  a.partials = nullptr; a.tile_counters = nullptr;
+  if (pl.swap) {
+    const int64_t need = workspace_bytes(m, n, k);
+    if (workspace == nullptr || ws_bytes < need)
+      return fail(PDLLM_E_WORKSPACE, "linear needs %lld workspace bytes, got %lld", static_cast<long long>(need), static_cast<long long>(ws_bytes));
+    if (static_cast<int64_t>(pl.n_tiles) * 4 > kCounterHeaderBytes)
+      return fail(PDLLM_E_UNSUPPORTED, "linear: %d feature tiles exceed the arrival-counter header", pl.n_tiles);
+    a.tile_counters = reinterpret_cast<int*>(workspace);
+    a.partials = reinterpret_cast<float*>(static_cast<char*>(workspace) + kCounterHeaderBytes);
+    if (!workspace_zeroed) {
+      cudaError_t e = cudaMemsetAsync(a.tile_counters, 0, static_cast<size_t>(pl.n_tiles) * 4, stream);
+      if (e != cudaSuccess) return fail(static_cast<int>(e), "cudaMemsetAsync(linear counters): %s", cudaGetErrorString(e));
+    }
+  }
+  const CUtensorMap& a_map = pl.swap ? w_map : x_map;
+  const CUtensorMap& b_map = pl.swap ? x_map : w_map;
+  return bf16 ? launch_typed<__nv_bfloat16>(pl, a_map, b_map, a, stream) : launch_typed<__half>(pl, a_map, b_map, a, stream);
+}
+
+}  // namespace gemm
+}  // namespace pdllm

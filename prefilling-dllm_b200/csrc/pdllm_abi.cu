@@ -4,6 +4,7 @@
 #include "attn_sm100.cuh"
 #include "common.cuh"
 #include "dense.cuh"
+#include "gemm_sm100.cuh"
 #include "kv_pages.cuh"
 #include "score.cuh"
 
@@ -512,6 +513,33 @@ int pdllm_compact_pages_per_head(void* cache, const int32_t* src_page_ids, const
   compact_scatter_kernel<<<grid, 256, 0, as_stream(stream)>>>(static_cast<uint4*>(cache), dst_page_ids, keep_count, dst_start, page_size,
                                                               per_tok, num_pages, static_cast<const uint4*>(staging), status);
   return check_launch("compact_scatter_kernel");
+}
+
+// ------------------------------------------------------------------------------------------------ linear layers
+int64_t pdllm_linear_workspace_bytes(int64_t m, int64_t n, int64_t k) {
+  if (m < 0 || n < 0 || k < 0) return PDLLM_E_INVALID;
+  return gemm::workspace_bytes(m, n, k);
+}
+
+int pdllm_linear(const void* x, int64_t x_stride, const void* weight, int64_t w_stride, const void* bias, void* out,
+                 int64_t out_stride, int64_t m, int64_t n, int64_t k, int dtype, int epilogue, void* workspace,
+                 int64_t workspace_bytes, int workspace_zeroed, int32_t* status, void* stream) {
+  if (m < 0 || n <= 0 || k <= 0) return fail(PDLLM_E_INVALID, "linear: bad sizes m=%lld n=%lld k=%lld", (long long)m, (long long)n, (long long)k);
+  if (m == 0) return 0;
+  if (!x || !weight || !out) return fail(PDLLM_E_INVALID, "linear: null pointer");
+  if (dtype != PDLLM_BF16 && dtype != PDLLM_F16) return fail(PDLLM_E_UNSUPPORTED, "linear: dtype must be bf16 or fp16 (tensor-core operands)");
+  if (epilogue != PDLLM_EPI_NONE && epilogue != PDLLM_EPI_SILU_MUL) return fail(PDLLM_E_INVALID, "linear: unknown epilogue %d", epilogue);
+  if (epilogue == PDLLM_EPI_SILU_MUL && (bias != nullptr || n % 2 != 0))
+    return fail(PDLLM_E_INVALID, "linear: the SiLU-mul epilogue takes an even number of interleaved (gate, up) rows and no bias");
+  const int64_t out_cols = epilogue == PDLLM_EPI_SILU_MUL ? n / 2 : n;
+  if (k % 8 != 0 || x_stride % 8 != 0 || w_stride % 8 != 0 || x_stride < k || w_stride < k || out_stride < out_cols)
+    return fail(PDLLM_E_UNSUPPORTED, "linear: K and the row strides of x and weight must be multiples of 8 elements (16 bytes)");
+  if (!aligned16(x) || !aligned16(weight)) return fail(PDLLM_E_UNSUPPORTED, "linear: x and weight must be 16-byte aligned");
+  if (m > 128 && (out_stride % 8 != 0 || !aligned16(out) || out_cols % 8 != 0))
+    return fail(PDLLM_E_UNSUPPORTED, "linear: with more than 128 rows, out needs 16-byte aligned rows and a column count that is a multiple of 8");
+  if (m >= (1ll << 31) || n >= (1ll << 31) || k >= (1ll << 31)) return fail(PDLLM_E_UNSUPPORTED, "linear: extent exceeds the tensor-map coordinate range");
+  return gemm::launch(x, x_stride, weight, w_stride, bias, out, out_stride, m, n, k, dtype, epilogue, workspace, workspace_bytes,
+                      workspace_zeroed, status, as_stream(stream));
 }
 
 }  // extern "C"

@@ -1,8 +1,10 @@
 """Dream / LLaDA-architecture transformer over a paged KV pool, GPU only.
 
-The GEMMs (QKV / O / MLP / LM head) and the embedding gather are torch on the current CUDA stream (cuBLAS); everything
-between them — RMSNorm with the residual add, RoPE in place on the fused QKV output, SiLU·mul, KV page writes and
-attention over [selected prefix pages ‖ new rows] — goes through the sm_100a kernels in `ops`: 11 launches per layer. Arithmetic follows the Dream model the
+Every step of a layer goes through the sm_100a kernels in `ops`: the linear layers (QKV with bias, O, gate-up with SiLU·mul
+fused into its epilogue, down, LM head) on the tcgen05 GEMM kernel, RMSNorm with the residual add, RoPE in place on the
+fused QKV output, KV page writes and attention over [selected prefix pages ‖ new rows] — 9 launches per layer (+ the
+split-KV merge for decode shapes). Only the embedding gather is torch. A float32 model (the CPU-parity toy) keeps torch's
+fp32 GEMM: the tensor cores would round its operands to tf32. Arithmetic follows the Dream model the
 reference vendors (prefilling_dllm_eval/model_cache/dream/model_dream.py:117-131 RMSNorm in fp32, :208-264 rotate-half
 RoPE with fp32 tables, :326-329 biased q/k/v, :277-278 SwiGLU, :689-711 pre-norm residual) and the engine's own
 restatement (prefilling_dllm_engine/prefilling_dllm/models/dream.py:26-237). Keys are stored in pages AFTER RoPE, like
@@ -198,6 +200,8 @@ class PagedDreamModel:
         def get(name):
             return state[name].to(device=dev, dtype=dt).contiguous()
 
+        # bf16 / fp16 models run their linear layers on the tcgen05 GEMM kernel; fp32 models on torch's fp32 GEMM
+        self.tensor_core_linear = dtype in (torch.bfloat16, torch.float16)
         self.embed = get("model.embed_tokens.weight")
         self.final_norm = get("model.norm.weight")
         self.lm_head = get("lm_head.weight") if "lm_head.weight" in state else self.embed
@@ -208,10 +212,16 @@ class PagedDreamModel:
             bqkv = None
             if a.attention_bias and (p + "self_attn.q_proj.bias") in state:
                 bqkv = torch.cat([get(p + "self_attn.q_proj.bias"), get(p + "self_attn.k_proj.bias"), get(p + "self_attn.v_proj.bias")], dim=0)
+            gate, up = get(p + "mlp.gate_proj.weight"), get(p + "mlp.up_proj.weight")
+            if self.tensor_core_linear:
+                # rows interleaved (2i = gate_i, 2i + 1 = up_i): the GEMM epilogue then holds each (gate, up) pair together
+                wgu = torch.stack([gate, up], dim=1).reshape(2 * gate.shape[0], gate.shape[1]).contiguous()
+            else:
+                wgu = torch.cat([gate, up], dim=0).contiguous()
+            del gate, up
             self.layers.append(dict(
                 ln1=get(p + "input_layernorm.weight"), ln2=get(p + "post_attention_layernorm.weight"),
-                wqkv=wqkv.contiguous(), bqkv=bqkv, wo=get(p + "self_attn.o_proj.weight"),
-                wgu=torch.cat([get(p + "mlp.gate_proj.weight"), get(p + "mlp.up_proj.weight")], dim=0).contiguous(),
+                wqkv=wqkv.contiguous(), bqkv=bqkv, wo=get(p + "self_attn.o_proj.weight"), wgu=wgu,
                 wd=get(p + "mlp.down_proj.weight")))
         self.inv_freq = (1.0 / (a.rope_theta ** (torch.arange(0, a.head_dim, 2, dtype=torch.int64).float() / a.head_dim))).to(dev)
         # pool [2 (k,v), layers, pages, page_size, Hkv, D] — same shape as the engine's kv_cache (engine/model_runner.py:557-567)
@@ -313,7 +323,7 @@ class PagedDreamModel:
         delta = None                                                     # output of the previous sub-block, not yet added to x
         for li, w in enumerate(self.layers):
             h = ops.add_rmsnorm(x, w["ln1"], eps, delta)                 # x += delta; h = norm(x)
-            qkv = F.linear(h, w["wqkv"], w["bqkv"]).view(total, hq + 2 * hkv, d)
+            qkv = self._linear(h, w["wqkv"], w["bqkv"]).view(total, hq + 2 * hkv, d)
             q, k, v = qkv[:, :hq], qkv[:, hq:hq + hkv], qkv[:, hq + hkv:]   # strided views of one buffer: no copies
             k_cache, v_cache = self.layer_cache(li)
             if slot_mapping is not None and store_unrotated_k:
@@ -332,16 +342,22 @@ class PagedDreamModel:
                                     sm_scale=self.scale, causal=causal, bidirectional=True, mask=new_row_mask)
             if slot_mapping is not None and store_after_attention:
                 ops.store_kvcache_unified_layout(k, v, k_cache, v_cache, slot_mapping, "diffusion_lm")
-            proj = F.linear(attn_out.view(total, hq * d), w["wo"])
+            proj = self._linear(attn_out.view(total, hq * d), w["wo"])
             h = ops.add_rmsnorm(x, w["ln2"], eps, proj)                  # x += attention output; h = norm(x)
-            delta = F.linear(ops.silu_mul(F.linear(h, w["wgu"])), w["wd"])
+            if self.tensor_core_linear:
+                delta = ops.linear(ops.linear(h, w["wgu"], silu_mul_interleaved=True), w["wd"])   # SiLU(gate)·up in the GEMM epilogue
+            else:
+                delta = F.linear(ops.silu_mul(F.linear(h, w["wgu"])), w["wd"])
         if delta is not None:
             x = x + delta
         logits = None
         if want_logits:
             rows = x if logit_rows is None else x.index_select(0, logit_rows)
-            logits = F.linear(ops.add_rmsnorm(rows.contiguous(), self.final_norm, eps), self.lm_head)
+            logits = self._linear(ops.add_rmsnorm(rows.contiguous(), self.final_norm, eps), self.lm_head)
         return logits, captured
+
+    def _linear(self, x: torch.Tensor, weight: torch.Tensor, bias: Optional[torch.Tensor] = None) -> torch.Tensor:
+        return ops.linear(x, weight, bias) if self.tensor_core_linear else F.linear(x, weight, bias)
 
     def rope_rows(self, page_ids, start: int, positions: Sequence[int]) -> None:
         """Rotate the un-rotated K rows `[start, start + len(positions))` of `page_ids` in place, in every layer."""

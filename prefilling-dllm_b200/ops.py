@@ -58,6 +58,8 @@ class _DeviceState(threading.local):
     def __init__(self) -> None:
         self.status: Dict[torch.device, torch.Tensor] = {}
         self.workspaces: Dict[Tuple[torch.device, str], torch.Tensor] = {}
+        self.graph_held: set = set()      # workspaces whose pointer a captured CUDA graph holds
+        self.retired: list = []           # replaced workspaces that such a graph may still use: kept alive
 
 
 _state = _DeviceState()
@@ -82,9 +84,10 @@ def check_status(device: Optional[torch.device] = None, *, reset: bool = True) -
         word.zero_()
     if (code & 0xff) == _lib.S_WAIT_TIMEOUT:
         # an abandoned attention launch may have left split-KV arrival counters behind in the workspace header
-        ws = _state.workspaces.get((torch.device(device), "attn"))
-        if ws is not None:
-            ws[: 64 * 1024].zero_()
+        for key in ("attn", "linear"):
+            ws = _state.workspaces.get((torch.device(device), key))
+            if ws is not None:
+                ws[: 64 * 1024].zero_()
     if code != 0:
         detail = f" (barrier {(code >> 8) & 0xff}, warp {(code >> 16) & 0xff}, parity {(code >> 24) & 1})" if code > 0xff else ""
         raise RuntimeError(f"pdllm_b200 device status {code & 0xff}: {_lib.STATUS_NAMES.get(code & 0xff, 'unknown')}{detail}")
@@ -92,19 +95,30 @@ def check_status(device: Optional[torch.device] = None, *, reset: bool = True) -
 
 
 def _workspace(device: torch.device, key: str, nbytes: int, *, zero: bool = False) -> torch.Tensor:
-    if torch.cuda.is_current_stream_capturing():
-        # A captured launch keeps the pointer it was given. The grow-only buffers below are replaced when a larger shape
-        # comes along, which would leave a graph writing into freed memory: scratch of a captured launch is allocated
-        # inside the capture instead, so it belongs to the graph's own memory pool and lives exactly as long as the graph
-        # (a zero-filled one becomes a memset node that runs on every replay).
+    """Grow-only scratch per (thread, device, key). Launches that share a buffer must be ordered on one stream."""
+    capturing = torch.cuda.is_current_stream_capturing()
+    buf = _state.workspaces.get((device, key))
+    if buf is not None and buf.numel() >= nbytes:
+        if capturing:
+            # A captured launch keeps this pointer for as long as its graph lives: the buffer must never be freed, even
+            # when a larger shape replaces it later (see below). Zero-filled buffers stay valid for the graph because the
+            # kernels return their counters to zero after every launch.
+            _state.graph_held.add((device, key))
+        return buf
+    if capturing:
+        # No buffer of this size exists yet and allocating a long-lived one inside a capture would tie it to the graph's
+        # private pool: give this launch scratch of its own from that pool, which lives exactly as long as the graph
+        # (a zero-filled one becomes a memset node on every replay). A step that ran eagerly once before it was captured
+        # never gets here.
         alloc = max(int(nbytes), 256)
         return torch.zeros(alloc, dtype=torch.uint8, device=device) if zero else torch.empty(alloc, dtype=torch.uint8, device=device)
-    buf = _state.workspaces.get((device, key))
-    if buf is None or buf.numel() < nbytes:
-        alloc = max(int(nbytes), 256)
-        with torch.inference_mode(False):   # kept across calls and cleared in place after a time-out
-            buf = torch.zeros(alloc, dtype=torch.uint8, device=device) if zero else torch.empty(alloc, dtype=torch.uint8, device=device)
-        _state.workspaces[(device, key)] = buf
+    if buf is not None and (device, key) in _state.graph_held:
+        _state.retired.append(buf)          # a captured graph may still launch into it
+        _state.graph_held.discard((device, key))
+    alloc = max(int(nbytes), 256)
+    with torch.inference_mode(False):   # kept across calls and cleared in place after a time-out
+        buf = torch.zeros(alloc, dtype=torch.uint8, device=device) if zero else torch.empty(alloc, dtype=torch.uint8, device=device)
+    _state.workspaces[(device, key)] = buf
     return buf
 
 
@@ -625,6 +639,42 @@ def rope_inplace(x: torch.Tensor, cos: torch.Tensor, sin: torch.Tensor) -> None:
     if cos.shape[0] != t or sin.shape != cos.shape or cos.dtype != x.dtype or sin.dtype != x.dtype or not (cos.is_contiguous() and sin.is_contiguous()):
         raise ValueError("cos / sin must be contiguous [tokens, head_dim] tables in the dtype of x")
     check(_lib.load().pdllm_rope_inplace(x.data_ptr(), cos.data_ptr(), sin.data_ptr(), t, h, d, x.stride(0), dtype_code(x.dtype), _stream(device)))
+
+
+def linear(x: torch.Tensor, weight: torch.Tensor, bias: Optional[torch.Tensor] = None, *, silu_mul_interleaved: bool = False,
+           out: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """`x @ weight.T (+ bias)` on the tcgen05 GEMM kernel: x `[M, K]`, weight `[N, K]` (the nn.Linear layout), bf16 / fp16.
+
+    silu_mul_interleaved: `weight` holds gate and up rows interleaved (row 2i = gate_i, 2i + 1 = up_i) and the result is
+    `silu(gate) * up`, `[M, N / 2]`, with the rounding of the unfused projection -> activation -> product sequence.
+    Takes the place of F.linear in QKVParallelLinear / MergedColumnParallelLinear / RowParallelLinear / ParallelLMHead
+    (prefilling_dllm_engine/prefilling_dllm/layers/linear.py:108-244, layers/embed_head.py:63-74)."""
+    device = _require_cuda(x, weight, bias)
+    if x.dim() != 2 or weight.dim() != 2 or x.shape[1] != weight.shape[1]:
+        raise ValueError(f"linear expects x [M, K] and weight [N, K], got {tuple(x.shape)} and {tuple(weight.shape)}")
+    if x.stride(1) != 1 or weight.stride(1) != 1 or x.dtype != weight.dtype:
+        raise ValueError("x and weight must have contiguous rows and one dtype")
+    m, k = x.shape
+    n = weight.shape[0]
+    if bias is not None and (bias.numel() != n or bias.dtype != x.dtype or not bias.is_contiguous()):
+        raise ValueError("bias must be a contiguous [N] tensor of the dtype of x")
+    cols = n // 2 if silu_mul_interleaved else n
+    if out is None:
+        out = torch.empty((m, cols), dtype=x.dtype, device=device)
+    elif tuple(out.shape) != (m, cols) or out.stride(1) != 1 or out.dtype != x.dtype:
+        raise ValueError("out must be [M, N] (or [M, N / 2] with the fused activation) with contiguous rows")
+    if m == 0:
+        return out
+    lib = _lib.load()
+    need = int(lib.pdllm_linear_workspace_bytes(m, n, k))
+    ws_ptr, ws_bytes = None, 0
+    if need > 0:
+        ws = _workspace(device, "linear", need, zero=True)   # zero-filled at creation; the kernel keeps its counters at zero
+        ws_ptr, ws_bytes = ws.data_ptr(), ws.numel()
+    check(lib.pdllm_linear(x.data_ptr(), x.stride(0), weight.data_ptr(), weight.stride(0), _ptr(bias), out.data_ptr(), out.stride(0),
+                           m, n, k, dtype_code(x.dtype), 1 if silu_mul_interleaved else 0, ws_ptr, ws_bytes, 1,
+                           status_word(device).data_ptr(), _stream(device)))
+    return out
 
 
 def silu_mul(gate_up: torch.Tensor) -> torch.Tensor:

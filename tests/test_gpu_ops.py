@@ -727,3 +727,93 @@ def test_dense_row_ops_match_eager(ops, cuda_device, dtype):
     assert torch.allclose(got.float(), want.float(), **tol)
     if dtype == torch.bfloat16:
         assert (got != want).float().mean() < 0.01
+
+
+# ----------------------------------------------------------------------------------------------- linear layers
+def _linear_reference(x, w, bias, silu):
+    """fp32 on the CPU from the same bf16 / fp16 operands, rounded as the unfused sequence rounds."""
+    acc = x.float() @ w.float().t()
+    if bias is not None:
+        acc = acc + bias.float()
+    if not silu:
+        return acc
+    y = acc.to(x.dtype).float()
+    gate, up = y[:, 0::2], y[:, 1::2]
+    return (torch.nn.functional.silu(gate).to(x.dtype).float() * up)
+
+
+def _assert_within_one_ulp(out, ref32, dtype):
+    """The kernel accumulates in fp32 and rounds once: its result is the rounded reference up to one unit in the last place
+    (different summation order), never more."""
+    out = out.float().cpu()
+    ulp = torch.finfo(dtype).eps * ref32.abs().clamp_min(1e-3)
+    worst = float(((out - ref32).abs() / ulp).max())
+    assert worst <= 1.01, f"{worst:.2f} ulp"
+    exact = float((out == ref32.to(dtype).float()).float().mean())
+    assert exact > 0.97, exact
+
+
+@pytest.mark.parametrize("m", [1, 4, 32, 33, 96, 128])
+def test_linear_few_rows_streams_the_weights(ops, cuda_device, m):
+    """M <= 128: weights on the 128-row side of the instruction, k-blocks dealt over all SMs (stream-K), shares of a feature
+    tile summed through the workspace. Shapes include a K that is not a multiple of 64 and an N that is not a multiple of
+    128; the second call reuses the workspace (the arrival counters must have returned to zero)."""
+    g = torch.Generator().manual_seed(60 + m)
+    for (n, k, with_bias) in ((1024, 512, True), (2752, 1376, False), (4608, 3584, True), (300, 512, False)):
+        x = (torch.randn(m, k, generator=g) * 0.5).bfloat16()
+        w = (torch.randn(n, k, generator=g) * 0.05).bfloat16()
+        b = torch.randn(n, generator=g).bfloat16() if with_bias else None
+        ref = _linear_reference(x, w, b, False)
+        xd, wd, bd = x.to(cuda_device), w.to(cuda_device), None if b is None else b.to(cuda_device)
+        out = ops.linear(xd, wd, bd)
+        again = ops.linear(xd, wd, bd)
+        ops.check_status(cuda_device)
+        _assert_within_one_ulp(out, ref, torch.bfloat16)
+        assert torch.equal(out, again), (m, n, k)
+
+
+@pytest.mark.parametrize("m", [129, 549, 1200])
+def test_linear_many_rows(ops, cuda_device, m):
+    """M > 128: token tiles on the 128-row side, 256- or 128-wide feature tiles, ragged last tiles in M, N and K; fp16 too."""
+    g = torch.Generator().manual_seed(70 + m)
+    for (n, k, with_bias, dtype) in ((1024, 512, True, torch.bfloat16), (2752, 1376, False, torch.bfloat16), (4096, 512, False, torch.float16),
+                                     (37888, 512, False, torch.bfloat16)):
+        x = (torch.randn(m, k, generator=g) * 0.5).to(dtype)
+        w = (torch.randn(n, k, generator=g) * 0.05).to(dtype)
+        b = torch.randn(n, generator=g).to(dtype) if with_bias else None
+        out = ops.linear(x.to(cuda_device), w.to(cuda_device), None if b is None else b.to(cuda_device))
+        ops.check_status(cuda_device)
+        _assert_within_one_ulp(out, _linear_reference(x, w, b, False), dtype)
+
+
+@pytest.mark.parametrize("m", [32, 100, 700])
+def test_linear_fused_silu_mul(ops, cuda_device, m):
+    """Gate and up rows interleaved in the weight, SiLU(gate)·up in the epilogue: equal to projection -> silu_mul kernel."""
+    g = torch.Generator().manual_seed(80 + m)
+    inter, k = 1376, 512
+    x = (torch.randn(m, k, generator=g) * 0.5).bfloat16().to(cuda_device)
+    gate = (torch.randn(inter, k, generator=g) * 0.1).bfloat16().to(cuda_device)
+    up = (torch.randn(inter, k, generator=g) * 0.1).bfloat16().to(cuda_device)
+    fused = ops.linear(x, torch.stack([gate, up], dim=1).reshape(2 * inter, k).contiguous(), silu_mul_interleaved=True)
+    unfused = ops.silu_mul(ops.linear(x, torch.cat([gate, up], dim=0).contiguous()))
+    ops.check_status(cuda_device)
+    assert fused.shape == (m, inter)
+    if m > 128:
+        assert torch.equal(fused, unfused)      # same k order per feature: the same bits
+    else:
+        # stream-K cuts a feature's k range at other points when its row moves to another tile: last-bit differences only
+        diff = (fused.float() - unfused.float()).abs()
+        assert float((diff > 0).float().mean()) < 0.02
+        assert float((diff / (torch.finfo(torch.bfloat16).eps * unfused.float().abs().clamp_min(1e-3))).max()) <= 2.01
+    ref = _linear_reference(x.cpu(), torch.stack([gate, up], dim=1).reshape(2 * inter, k).cpu(), None, True)
+    assert rel_err(fused, ref) < 5e-3
+
+
+def test_linear_rejects_what_it_cannot_run(ops, cuda_device):
+    x = torch.zeros(8, 64, dtype=torch.float32, device=cuda_device)
+    with pytest.raises(NotImplementedError):
+        ops.linear(x, torch.zeros(16, 64, dtype=torch.float32, device=cuda_device))          # fp32: not a tensor-core dtype here
+    xb = torch.zeros(8, 60, dtype=torch.bfloat16, device=cuda_device)
+    with pytest.raises(NotImplementedError):
+        ops.linear(xb, torch.zeros(16, 60, dtype=torch.bfloat16, device=cuda_device))         # K not a multiple of 8
+    assert ops.linear(torch.zeros(0, 64, dtype=torch.bfloat16, device=cuda_device), torch.zeros(16, 64, dtype=torch.bfloat16, device=cuda_device)).shape == (0, 16)
