@@ -46,15 +46,17 @@ __host__ __device__ constexpr uint32_t tmem_cols(int bn) { return 2 * bn < 32 ? 
 
 struct Args {
   void* out; const void* bias;
-  float* partials;       // stream-K: [2 * grid][bn][128] fp32
-  int* tile_counters;    // stream-K: [feature tiles], zero on entry, zero on exit
+  float* partials;       // shared tiles: [2 * grid][bn][128] fp32
+  int* tile_counters;    // shared tiles: arrival counters, zero on entry, zero on exit
   int32_t* status;
   long long* trace;      // unused; the shared bounded-wait helper expects the member
   int64_t out_stride;    // elements
   int64_t m, n, k;
   int kb_total;          // k-blocks of 64
   int m_tiles, n_tiles;  // tiles along tokens / features
-  int64_t units;         // stream-K: n_tiles * kb_total
+  int whole_tiles;       // tiles [0, whole_tiles) run whole, round-robin over the CTAs (always 0 with few rows)
+  int64_t units;         // (tile, k-block) units of the remaining tiles, dealt evenly over the first sk_grid CTAs
+  int sk_grid;           // CTAs that take a share of those units (<= gridDim.x, <= units): each owns at least one unit
   int epilogue;
 };
 
@@ -73,51 +75,56 @@ __device__ __forceinline__ void tmem_alloc_cols(uint32_t* dst_smem, uint32_t col
 struct Segment {
   int a_row0, b_row0;   // first row of the A / B tile in its tensor
   int kb0, kb1;
-  int tile;             // stream-K: feature tile index (arrival counter); otherwise unused
-  bool partial;         // stream-K: the tile's k-blocks are shared with other CTAs
+  int shared_tile;      // index among the shared (stream-K) tiles: arrival counter; -1 for a whole tile
+  bool partial;         // the tile's k-blocks are shared with other CTAs
 };
 
-// Stream-K bookkeeping: unit u = (feature tile, k-block); CTA c owns units [c*U/G, (c+1)*U/G).
+// Stream-K bookkeeping: unit u = (shared tile, k-block); CTA c owns units [c*U/G, (c+1)*U/G).
 __device__ __forceinline__ int64_t sk_first_unit(int64_t c, int64_t units, int64_t grid) { return c * units / grid; }
 __device__ __forceinline__ int sk_cta_of(int64_t unit, int64_t units, int64_t grid) {
   return static_cast<int>(((unit + 1) * grid + units - 1) / units - 1);
 }
 
+// A CTA's list of segments: first its whole tiles (tile = blockIdx + i * grid: concurrent CTAs work on neighbouring tiles,
+// which share a weight tile through L2), then its share of the (tile, k-block) units of the remaining tiles.
 template <bool kSwap, int kBN>
 struct Schedule {
-  // position in this CTA's list of segments
-  int64_t cursor, end;      // normal: tile index (stride gridDim.x) / number of tiles; stream-K: unit range
+  int64_t tile;             // next whole tile
+  int64_t cursor, end;      // unit range of the shared tiles
   __device__ __forceinline__ void init(const Args& a) {
+    tile = blockIdx.x;
+    cursor = end = 0;
+    if (static_cast<int>(blockIdx.x) < a.sk_grid) {
+      cursor = sk_first_unit(blockIdx.x, a.units, a.sk_grid);
+      end = sk_first_unit(static_cast<int64_t>(blockIdx.x) + 1, a.units, a.sk_grid);
+    }
+  }
+  __device__ __forceinline__ void place(const Args& a, int64_t t, Segment& s) const {
     if (kSwap) {
-      cursor = sk_first_unit(blockIdx.x, a.units, gridDim.x);
-      end = sk_first_unit(static_cast<int64_t>(blockIdx.x) + 1, a.units, gridDim.x);
+      s.a_row0 = static_cast<int>(t) * kRowsA;   // weight rows; all tokens (M <= kBN) are the B side
+      s.b_row0 = 0;
     } else {
-      cursor = blockIdx.x;
-      end = static_cast<int64_t>(a.m_tiles) * a.n_tiles;
+      s.a_row0 = static_cast<int>(t % a.m_tiles) * kRowsA;   // tokens, fastest
+      s.b_row0 = static_cast<int>(t / a.m_tiles) * kBN;      // weight rows
     }
   }
   __device__ __forceinline__ bool next(const Args& a, Segment& s) {
-    if (cursor >= end) return false;
-    if (kSwap) {
-      const int tile = static_cast<int>(cursor / a.kb_total);
-      const int64_t t0 = static_cast<int64_t>(tile) * a.kb_total;
-      const int64_t stop = end < t0 + a.kb_total ? end : t0 + a.kb_total;
-      s.tile = tile;
-      s.a_row0 = tile * kRowsA;      // weight rows
-      s.b_row0 = 0;                  // all tokens (M <= kBN)
-      s.kb0 = static_cast<int>(cursor - t0);
-      s.kb1 = static_cast<int>(stop - t0);
-      s.partial = !(s.kb0 == 0 && s.kb1 == a.kb_total);
-      cursor = stop;
-    } else {
-      const int mt = static_cast<int>(cursor % a.m_tiles), nt = static_cast<int>(cursor / a.m_tiles);
-      s.tile = static_cast<int>(cursor);
-      s.a_row0 = mt * kRowsA;        // tokens
-      s.b_row0 = nt * kBN;           // weight rows
-      s.kb0 = 0; s.kb1 = a.kb_total;
-      s.partial = false;
-      cursor += gridDim.x;
+    if (tile < a.whole_tiles) {
+      place(a, tile, s);
+      s.kb0 = 0; s.kb1 = a.kb_total; s.shared_tile = -1; s.partial = false;
+      tile += gridDim.x;
+      return true;
     }
+    if (cursor >= end) return false;
+    const int st = static_cast<int>(cursor / a.kb_total);
+    const int64_t t0 = static_cast<int64_t>(st) * a.kb_total;
+    const int64_t stop = end < t0 + a.kb_total ? end : t0 + a.kb_total;
+    place(a, a.whole_tiles + st, s);
+    s.shared_tile = st;
+    s.kb0 = static_cast<int>(cursor - t0);
+    s.kb1 = static_cast<int>(stop - t0);
+    s.partial = !(s.kb0 == 0 && s.kb1 == a.kb_total);
+    cursor = stop;
     return true;
   }
 };
@@ -133,6 +140,12 @@ __device__ __forceinline__ T silu_mul(float gate_acc, float up_acc) {
   const float act = round_to<T>(g / (1.f + expf(-g)));
   return from_f32<T>(act * u);
 }
+template <typename T>
+__device__ __forceinline__ uint32_t pack2(T lo, T hi) {
+  return static_cast<uint32_t>(*reinterpret_cast<uint16_t*>(&lo)) | (static_cast<uint32_t>(*reinterpret_cast<uint16_t*>(&hi)) << 16);
+}
+
+constexpr int kChunk = 16;   // accumulator columns handled at a time by an epilogue thread
 
 template <bool kSwap, int kBN, typename T>
 __global__ void __launch_bounds__(kThreads, 1)
@@ -239,6 +252,8 @@ linear_sm100_kernel(const __grid_constant__ CUtensorMap a_map, const __grid_cons
     T* out = reinterpret_cast<T*>(a.out);
     const T* bias = reinterpret_cast<const T*>(a.bias);
     const bool silu = a.epilogue == PDLLM_EPI_SILU_MUL;
+    // accumulator columns that carry data: the tokens (few rows: out^T) or the whole feature tile
+    const int n_cols = kSwap ? static_cast<int>(a.m < kBN ? a.m : kBN) : kBN;
     int n_seg = 0;
     uint32_t epi_phase = 0;
     bool ok = true;
@@ -251,136 +266,130 @@ linear_sm100_kernel(const __grid_constant__ CUtensorMap a_map, const __grid_cons
       tc_fence_after();
       const uint32_t t_acc = tmem_base + lane_base + static_cast<uint32_t>(acc * kBN);
 
-      if (kSwap) {
-        // accumulator = out^T: row r = feature n, column j = token j
-        const int64_t n = static_cast<int64_t>(seg.a_row0) + r;
-        const int m_count = static_cast<int>(a.m < kBN ? a.m : kBN);
-        auto emit = [&](int j, float v) {       // one (token, feature) value of the finished tile
-          if (silu) {
-            const float other = __shfl_xor_sync(0xffffffffu, v, 1);
-            if ((lane & 1) == 0 && n + 1 < a.n) out[static_cast<int64_t>(j) * a.out_stride + (n >> 1)] = silu_mul<T>(v, other);
-          } else if (n < a.n) {
-            if (bias != nullptr) v += to_f32<T>(bias[n]);
-            out[static_cast<int64_t>(j) * a.out_stride + n] = from_f32<T>(v);
-          }
-        };
-        if (!seg.partial) {
-#pragma unroll 1
-          for (int c0 = 0; c0 < kBN; c0 += 16) {
-            uint32_t v[16];
-            tc::tmem_ld16(t_acc + c0, v);
-            tc_wait_ld();
+      // Finished values of accumulator columns [c0, c0 + 16) of row r → output.
+      //   few rows:  row r = feature n, column = token: 2-byte stores, a warp covers 32 consecutive features of one token;
+      //   many rows: row r = token, columns = features: 32 contiguous bytes per thread.
+      const int64_t row_id = static_cast<int64_t>(seg.a_row0) + r;     // feature (few rows) or token (many rows)
+      float bias_r = 0.f;
+      if (kSwap && bias != nullptr && row_id < a.n) bias_r = to_f32<T>(bias[row_id]);
+      auto store_chunk = [&](int c0, const float* v) {
+        if (kSwap) {
 #pragma unroll
-            for (int i = 0; i < 16; ++i) {
-              if (c0 + i < m_count) emit(c0 + i, __uint_as_float(v[i]));      // uniform across the warp
+          for (int i = 0; i < kChunk; ++i) {
+            const int j = c0 + i;
+            if (j >= n_cols) break;                       // uniform across the warp
+            if (silu) {
+              const float other = __shfl_xor_sync(0xffffffffu, v[i], 1);
+              if ((lane & 1) == 0 && row_id + 1 < a.n) out[static_cast<int64_t>(j) * a.out_stride + (row_id >> 1)] = silu_mul<T>(v[i], other);
+            } else if (row_id < a.n) {
+              out[static_cast<int64_t>(j) * a.out_stride + row_id] = from_f32<T>(v[i] + bias_r);
             }
           }
-          tc_fence_before();
-          __syncwarp();
-          if (lane == 0) mbar_arrive(&acc_empty[acc]);
         } else {
-          // publish this CTA's share of the tile; slot 0 = the CTA's first tile, slot 1 = its last
-          const int first_tile = static_cast<int>(sk_first_unit(blockIdx.x, a.units, gridDim.x) / a.kb_total);
-          float* mine = a.partials + (static_cast<int64_t>(blockIdx.x) * 2 + (seg.tile == first_tile ? 0 : 1)) * (kBN * kRowsA);
-#pragma unroll 1
-          for (int c0 = 0; c0 < kBN; c0 += 16) {
-            uint32_t v[16];
-            tc::tmem_ld16(t_acc + c0, v);
-            tc_wait_ld();
+          const int64_t n0 = static_cast<int64_t>(seg.b_row0) + c0;
+          if (row_id >= a.m || n0 >= a.n) return;
+          if (silu) {
+            T* dst = out + row_id * a.out_stride + (n0 >> 1);
+            if (n0 + kChunk <= a.n) {
+              uint32_t p[4];
 #pragma unroll
-            for (int i = 0; i < 16; ++i) {
-              if (c0 + i < m_count) mine[(c0 + i) * kRowsA + r] = __uint_as_float(v[i]);
+              for (int i = 0; i < 4; ++i) p[i] = pack2<T>(silu_mul<T>(v[4 * i], v[4 * i + 1]), silu_mul<T>(v[4 * i + 2], v[4 * i + 3]));
+              *reinterpret_cast<uint4*>(dst) = make_uint4(p[0], p[1], p[2], p[3]);
+            } else {
+              for (int i = 0; i < kChunk / 2 && n0 + 2 * i + 1 < a.n; ++i) dst[i] = silu_mul<T>(v[2 * i], v[2 * i + 1]);
             }
-          }
-          tc_fence_before();
-          __syncwarp();
-          if (lane == 0) mbar_arrive(&acc_empty[acc]);
-          __threadfence();
-          mbar_arrive(epi_all);
-          if (et == 0) {
-            ok = mbar_wait(epi_all, epi_phase, abort_flag, a);
-            if (ok) {
-              const int64_t t0 = static_cast<int64_t>(seg.tile) * a.kb_total;
-              const int parts = sk_cta_of(t0 + a.kb_total - 1, a.units, gridDim.x) - sk_cta_of(t0, a.units, gridDim.x) + 1;
-              const int prev = atomicAdd(&a.tile_counters[seg.tile], 1);
-              const int last = prev == parts - 1 ? 1 : 0;
-              if (last) a.tile_counters[seg.tile] = 0;      // every share has arrived: ready for the next launch
-              reduce_flag[0] = last;
-              mbar_arrive(epi_go);
-            }
-          }
-          ok = mbar_wait(epi_go, epi_phase, abort_flag, a);
-          epi_phase ^= 1;
-          if (!ok) break;
-          if (reduce_flag[0]) {
-            __threadfence();
-            const int64_t t0 = static_cast<int64_t>(seg.tile) * a.kb_total;
-            const int c_first = sk_cta_of(t0, a.units, gridDim.x), c_last = sk_cta_of(t0 + a.kb_total - 1, a.units, gridDim.x);
-#pragma unroll 1
-            for (int j = 0; j < m_count; ++j) {
-              float sum = 0.f;
-              for (int c = c_first; c <= c_last; ++c) {     // fixed order: the result does not depend on who reduces
-                const int c_tile0 = static_cast<int>(sk_first_unit(c, a.units, gridDim.x) / a.kb_total);
-                const float* part = a.partials + (static_cast<int64_t>(c) * 2 + (seg.tile == c_tile0 ? 0 : 1)) * (kBN * kRowsA);
-                sum += __ldcg(part + j * kRowsA + r);
+          } else {
+            T* dst = out + row_id * a.out_stride + n0;
+            if (n0 + kChunk <= a.n) {
+              uint32_t p[8];
+#pragma unroll
+              for (int i = 0; i < 8; ++i) {
+                float x0 = v[2 * i], x1 = v[2 * i + 1];
+                if (bias != nullptr) { x0 += to_f32<T>(bias[n0 + 2 * i]); x1 += to_f32<T>(bias[n0 + 2 * i + 1]); }
+                p[i] = pack2<T>(from_f32<T>(x0), from_f32<T>(x1));
               }
-              emit(j, sum);
+              uint4* d4 = reinterpret_cast<uint4*>(dst);
+              d4[0] = make_uint4(p[0], p[1], p[2], p[3]);
+              d4[1] = make_uint4(p[4], p[5], p[6], p[7]);
+            } else {
+              for (int i = 0; i < kChunk && n0 + i < a.n; ++i) dst[i] = from_f32<T>(v[i] + (bias != nullptr ? to_f32<T>(bias[n0 + i]) : 0.f));
             }
           }
         }
-      } else {
-        // accumulator row r = token, columns = features
-        const int64_t m = static_cast<int64_t>(seg.a_row0) + r;
-        const bool row_ok = m < a.m;
+      };
+
+      if (!seg.partial) {
 #pragma unroll 1
-        for (int c0 = 0; c0 < kBN; c0 += 32) {
-          uint32_t v[32];
-          tc::tmem_ld32(t_acc + c0, v);
+        for (int c0 = 0; c0 < n_cols; c0 += kChunk) {
+          uint32_t raw[kChunk];
+          tc::tmem_ld16(t_acc + c0, raw);
           tc_wait_ld();
-          const int64_t n0 = static_cast<int64_t>(seg.b_row0) + c0;
-          if (!row_ok || n0 >= a.n) continue;
-          if (silu) {
-            T* dst = out + m * a.out_stride + (n0 >> 1);
-            if (n0 + 32 <= a.n) {
-              uint32_t packed[8];
+          float v[kChunk];
 #pragma unroll
-              for (int i = 0; i < 8; ++i) {
-                T lo = silu_mul<T>(__uint_as_float(v[4 * i]), __uint_as_float(v[4 * i + 1]));
-                T hi = silu_mul<T>(__uint_as_float(v[4 * i + 2]), __uint_as_float(v[4 * i + 3]));
-                packed[i] = static_cast<uint32_t>(*reinterpret_cast<uint16_t*>(&lo)) | (static_cast<uint32_t>(*reinterpret_cast<uint16_t*>(&hi)) << 16);
-              }
-              uint4* d4 = reinterpret_cast<uint4*>(dst);
-              d4[0] = make_uint4(packed[0], packed[1], packed[2], packed[3]);
-              d4[1] = make_uint4(packed[4], packed[5], packed[6], packed[7]);
-            } else {
-              for (int i = 0; i < 16 && n0 + 2 * i + 1 < a.n; ++i) dst[i] = silu_mul<T>(__uint_as_float(v[2 * i]), __uint_as_float(v[2 * i + 1]));
-            }
-          } else {
-            T* dst = out + m * a.out_stride + n0;
-            if (n0 + 32 <= a.n) {
-              uint32_t packed[16];
+          for (int i = 0; i < kChunk; ++i) v[i] = __uint_as_float(raw[i]);
+          store_chunk(c0, v);
+        }
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&acc_empty[acc]);
+      } else {
+        // This CTA holds only some k-blocks of the tile: publish its share as fp32 [column][128 rows]; slot 0 = the first
+        // shared tile of the CTA's unit range, slot 1 = its last.
+        const int first_st = static_cast<int>(sk_first_unit(blockIdx.x, a.units, a.sk_grid) / a.kb_total);
+        float* mine = a.partials + (static_cast<int64_t>(blockIdx.x) * 2 + (seg.shared_tile == first_st ? 0 : 1)) * (kBN * kRowsA) + r;
+#pragma unroll 1
+        for (int c0 = 0; c0 < n_cols; c0 += kChunk) {
+          uint32_t raw[kChunk];
+          tc::tmem_ld16(t_acc + c0, raw);
+          tc_wait_ld();
 #pragma unroll
-              for (int i = 0; i < 16; ++i) {
-                float x0 = __uint_as_float(v[2 * i]), x1 = __uint_as_float(v[2 * i + 1]);
-                if (bias != nullptr) { x0 += to_f32<T>(bias[n0 + 2 * i]); x1 += to_f32<T>(bias[n0 + 2 * i + 1]); }
-                T lo = from_f32<T>(x0), hi = from_f32<T>(x1);
-                packed[i] = static_cast<uint32_t>(*reinterpret_cast<uint16_t*>(&lo)) | (static_cast<uint32_t>(*reinterpret_cast<uint16_t*>(&hi)) << 16);
-              }
-              uint4* d4 = reinterpret_cast<uint4*>(dst);
-#pragma unroll
-              for (int i = 0; i < 4; ++i) d4[i] = make_uint4(packed[4 * i], packed[4 * i + 1], packed[4 * i + 2], packed[4 * i + 3]);
-            } else {
-              for (int i = 0; i < 32 && n0 + i < a.n; ++i) {
-                float x = __uint_as_float(v[i]);
-                if (bias != nullptr) x += to_f32<T>(bias[n0 + i]);
-                dst[i] = from_f32<T>(x);
-              }
-            }
+          for (int i = 0; i < kChunk; ++i) {
+            if (c0 + i < n_cols) mine[(c0 + i) * kRowsA] = __uint_as_float(raw[i]);
           }
         }
         tc_fence_before();
         __syncwarp();
         if (lane == 0) mbar_arrive(&acc_empty[acc]);
+        __threadfence();
+        mbar_arrive(epi_all);
+        const int64_t t0 = static_cast<int64_t>(seg.shared_tile) * a.kb_total;
+        if (et == 0) {
+          ok = mbar_wait(epi_all, epi_phase, abort_flag, a);
+          if (ok) {
+            const int parts = sk_cta_of(t0 + a.kb_total - 1, a.units, a.sk_grid) - sk_cta_of(t0, a.units, a.sk_grid) + 1;
+            const int prev = atomicAdd(&a.tile_counters[seg.shared_tile], 1);
+            const int last = prev == parts - 1 ? 1 : 0;
+            if (last) a.tile_counters[seg.shared_tile] = 0;      // every share has arrived: ready for the next launch
+            reduce_flag[0] = last;
+            mbar_arrive(epi_go);
+          }
+        }
+        ok = mbar_wait(epi_go, epi_phase, abort_flag, a);
+        epi_phase ^= 1;
+        if (!ok) break;
+        if (reduce_flag[0]) {
+          __threadfence();
+          // Shares are added in CTA order c_first..c_last, whoever reduces. Every CTA after the first starts inside this
+          // tile, so the tile is its first (slot 0); for the first CTA that holds only when its range starts exactly here.
+          const int c_first = sk_cta_of(t0, a.units, a.sk_grid), c_last = sk_cta_of(t0 + a.kb_total - 1, a.units, a.sk_grid);
+          const int first_slot = sk_first_unit(c_first, a.units, a.sk_grid) == t0 ? 0 : 1;
+#pragma unroll 1
+          for (int c0 = 0; c0 < n_cols; c0 += kChunk) {
+            float sum[kChunk];
+#pragma unroll
+            for (int i = 0; i < kChunk; ++i) sum[i] = 0.f;
+#pragma unroll 1
+            for (int c = c_first; c <= c_last; ++c) {
+              const float* part = a.partials + (static_cast<int64_t>(c) * 2 + (c == c_first ? first_slot : 0)) * (kBN * kRowsA) + c0 * kRowsA + r;
+              float v[kChunk];
+#pragma unroll
+              for (int i = 0; i < kChunk; ++i) v[i] = (c0 + i < n_cols) ? __ldcg(part + i * kRowsA) : 0.f;
+#pragma unroll
+              for (int i = 0; i < kChunk; ++i) sum[i] += v[i];
+            }
+            store_chunk(c0, sum);
+          }
+        }
       }
     }
   }
@@ -397,9 +406,12 @@ linear_sm100_kernel(const __grid_constant__ CUtensorMap a_map, const __grid_cons
 // ---- host side ---------------------------------------------------------------------------------------------
 struct Plan {
   bool swap;
-  int bn;         // B-tile rows: token tile (swap) or feature tile (normal)
+  int bn;         // B-tile rows: token tile (few rows) or feature tile (many rows)
   int m_tiles, n_tiles, kb_total;
-  int64_t units;  // stream-K units
+  int whole_tiles;   // tiles that run whole, round-robin
+  int shared_tiles;  // tiles whose k-blocks are dealt over all CTAs
+  int64_t units;     // shared_tiles * kb_total
+  int sk_grid;       // CTAs that share those units
   int grid;
 };
 
@@ -408,29 +420,45 @@ inline Plan make_plan(int64_t m, int64_t n, int64_t k) {
   const int sms = sm_count();
   pl.kb_total = static_cast<int>((k + kBlockK - 1) / kBlockK);
   pl.swap = m <= 128;
+  int64_t tiles, sk_ctas = 0;
   if (pl.swap) {
+    // bound by streaming the weights: every k-block of every feature tile is a unit, all dealt evenly
     pl.bn = m <= 16 ? 16 : m <= 32 ? 32 : m <= 64 ? 64 : 128;
     pl.m_tiles = 1;
     pl.n_tiles = static_cast<int>((n + kRowsA - 1) / kRowsA);
-    pl.units = static_cast<int64_t>(pl.n_tiles) * pl.kb_total;
-    pl.grid = static_cast<int>(pl.units < sms ? pl.units : sms);
+    tiles = pl.n_tiles;
+    pl.whole_tiles = 0;
   } else {
     pl.m_tiles = static_cast<int>((m + kRowsA - 1) / kRowsA);
     const int64_t tiles256 = static_cast<int64_t>(pl.m_tiles) * ((n + 255) / 256);
     pl.bn = tiles256 >= sms ? 256 : 128;      // narrower tiles when wide ones would leave SMs without work
     pl.n_tiles = static_cast<int>((n + pl.bn - 1) / pl.bn);
-    pl.units = 0;
-    const int64_t tiles = static_cast<int64_t>(pl.m_tiles) * pl.n_tiles;
-    pl.grid = static_cast<int>(tiles < sms ? tiles : sms);
+    tiles = static_cast<int64_t>(pl.m_tiles) * pl.n_tiles;
+    // Full waves of whole tiles. A last wave that fills less than three quarters of the SMs is cut along K instead: each of
+    // its tiles goes to `parts` CTAs (at least 8 k-blocks each), so the tail of the kernel is a fraction of a tile long.
+    pl.whole_tiles = static_cast<int>(tiles);
+    const int64_t rest = tiles % sms;
+    if (rest > 0 && rest * 4 < static_cast<int64_t>(sms) * 3) {
+      int64_t parts = sms / rest;
+      if (parts > pl.kb_total / 8) parts = pl.kb_total / 8;
+      if (parts >= 2) {
+        pl.whole_tiles = static_cast<int>(tiles - rest);
+        sk_ctas = rest * parts;
+      }
+    }
   }
-  if (pl.grid < 1) pl.grid = 1;
+  pl.shared_tiles = static_cast<int>(tiles - pl.whole_tiles);
+  pl.units = static_cast<int64_t>(pl.shared_tiles) * pl.kb_total;
+  if (pl.swap) sk_ctas = pl.units < sms ? pl.units : sms;
+  pl.sk_grid = static_cast<int>(sk_ctas);
+  int64_t grid = pl.whole_tiles >= sms ? sms : (pl.whole_tiles > sk_ctas ? pl.whole_tiles : sk_ctas);
+  pl.grid = static_cast<int>(grid < 1 ? 1 : grid);
   return pl;
 }
 
 inline int64_t workspace_bytes(int64_t m, int64_t n, int64_t k) {
   if (m <= 0 || n <= 0) return 0;
   const Plan pl = make_plan(m, n, k);
-  if (!pl.swap) return 0;
   // a grid never exceeds the SM count; sized for it so that one workspace serves every layer of a model
   return kCounterHeaderBytes + static_cast<int64_t>(2) * sm_count() * pl.bn * kRowsA * 4;
 }
@@ -490,18 +518,19 @@ inline int launch(const void* x, int64_t x_stride, const void* w, int64_t w_stri
   Args a;
   a.out = out; a.bias = bias; a.status = status; a.trace = nullptr;
   a.out_stride = out_stride; a.m = m; a.n = n; a.k = k;
-  a.kb_total = pl.kb_total; a.m_tiles = pl.m_tiles; a.n_tiles = pl.n_tiles; a.units = pl.units; a.epilogue = epilogue;
+  a.kb_total = pl.kb_total; a.m_tiles = pl.m_tiles; a.n_tiles = pl.n_tiles; a.whole_tiles = pl.whole_tiles; a.units = pl.units; a.sk_grid = pl.sk_grid;
+  a.epilogue = epilogue;
   a.partials = nullptr; a.tile_counters = nullptr;
-  if (pl.swap) {
+  if (pl.shared_tiles > 0) {
     const int64_t need = workspace_bytes(m, n, k);
     if (workspace == nullptr || ws_bytes < need)
       return fail(PDLLM_E_WORKSPACE, "linear needs %lld workspace bytes, got %lld", static_cast<long long>(need), static_cast<long long>(ws_bytes));
-    if (static_cast<int64_t>(pl.n_tiles) * 4 > kCounterHeaderBytes)
-      return fail(PDLLM_E_UNSUPPORTED, "linear: %d feature tiles exceed the arrival-counter header", pl.n_tiles);
+    if (static_cast<int64_t>(pl.shared_tiles) * 4 > kCounterHeaderBytes)
+      return fail(PDLLM_E_UNSUPPORTED, "linear: %d shared tiles exceed the arrival-counter header", pl.shared_tiles);
     a.tile_counters = reinterpret_cast<int*>(workspace);
     a.partials = reinterpret_cast<float*>(static_cast<char*>(workspace) + kCounterHeaderBytes);
     if (!workspace_zeroed) {
-      cudaError_t e = cudaMemsetAsync(a.tile_counters, 0, static_cast<size_t>(pl.n_tiles) * 4, stream);
+      cudaError_t e = cudaMemsetAsync(a.tile_counters, 0, static_cast<size_t>(pl.shared_tiles) * 4, stream);
       if (e != cudaSuccess) return fail(static_cast<int>(e), "cudaMemsetAsync(linear counters): %s", cudaGetErrorString(e));
     }
   }

