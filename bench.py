@@ -1,20 +1,36 @@
 #!/usr/bin/env python3
-"""Benchmark of the hot path: op-level non-contiguous paged decode attention.
+"""Benchmark of the Prefilling-dLLM long-context hot path on B200.
 
-    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl native|reference]
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl native|reference] [--workload request|...]
     python -m torch.distributed.run --nnodes=1 --nproc-per-node N --master-addr 127.0.0.1 --master-port P \
         bench.py --gpus N --steps K --warmup W
 
-One step = one attention pass over one batch: 8 requests per GPU, each with 64 query + 32 response rows attending
-4 selected chunks (16 pages of 256 tokens, any physical order, no gather) plus the bidirectional new rows;
-28 query / 4 KV heads, head_dim 128, bf16. Decode is data-parallel over requests, so every rank runs its own batch
-(weak scaling, no data-path collective). Prints ONE JSON line on rank 0.
+Default workload `request`. One step = ONE REQUEST through `FastDLLMParallelComp.generate`: Dream-7B architecture (28 layers,
+hidden 3584, 28 / 4 heads of 128, MLP 18944, vocabulary 152064, random init, bf16), an 8192-token random prefix and a 64-token
+query as host token-id lists in, 32 generated token ids as a host list out; chunk 1024 with chunk BOS, draft-self-information
+scoring of the 8 chunks in one packed causal forward, top-4, one joint bidirectional prefill, confidence-threshold block
+denoising (threshold 0.9, greedy). With N GPUs every rank serves its own request (decode is data-parallel over requests, no
+data-path collective): weak scaling.
 
-Timing: CUDA events on the launching stream, max over ranks. Consecutive steps use different block tables that
-together cover the whole 537 MB pool, so a step never finds its pages in the 126 MB L2.
-`--impl reference` times the CPU restatement of the reference's own path (oracle/, all host threads) on a bounded
-sample of the same workload; it is the only place the product bench executes the oracle, and only as the thing
-being compared against.
+The ONE JSON line rank 0 prints:
+  metric / value   decode tokens per second: generated tokens of all ranks / device time of the block-denoising phase (its
+                   inputs, the KV pages, are resident in HBM when it starts), max over ranks
+  ms_per_step      latency of one whole request, CUDA events, max over ranks
+  e2e              tokens per second of the whole request (host ids in, host ids out), and that latency
+  phases_ms        draft / scoring / prefill / decode split of one request (CUDA events at the phase boundaries)
+  kernel_share     one denoise step by kernel group, each group replayed as a CUDA graph of its own
+  roofline         the dominant kernel of the denoise step, the weight-streaming GEMM: algorithmic bytes / measured time
+  ops              op-level measurements: the paged decode attention on the 8-request op shape and on MHA decode heads, the
+                   attention kernel on the two prefill shapes of this request, the GEMM kernel next to cuBLAS
+  request_32k      the 32768-token request (32 chunks, top-8, token_capacity 256, 64 new tokens) with chunk scoring and chunk
+                   prefill SHARDED over the N ranks: score all-gather, kept-KV hand-off to the decode rank, bytes moved
+  cpu_baseline     the reference's own class on the CPU toy, on this machine's host cores (N = 1 only), next to
+  toy_same_config  this runtime on the same toy
+
+`--impl reference` times that CPU run alone and prints it with "impl": "reference".
+Consecutive requests differ in nothing but time: weights (15 GB) and KV pages are far larger than the 126 MB L2 and are
+streamed again by every forward, so no step finds its inputs cached. LongBench-style data, checkpoints and tokenizers are
+absent: inputs are seeded uniform random token ids of the same shapes.
 """
 
 from __future__ import annotations
@@ -34,7 +50,7 @@ if ROOT not in sys.path:
 
 import torch  # noqa: E402
 
-# ---- workload: BASELINE.json configs[1] ------------------------------------------------------------------
+# ---- op-level workload: 8 requests x (64 query + 32 response rows) over 4 of 32 cached chunks -------------------------------
 NUM_REQ = 8
 HQ, HKV, D = 28, 4, 128
 PAGE = 256
@@ -50,8 +66,8 @@ BYTES_PER_STEP = NUM_REQ * (CTX * 2 * HKV * D * 2 + ROWS * (2 * HQ + 2 * HKV) * 
 # dram__bytes_read.sum + dram__bytes_write.sum of one attn_sm100_kernel launch on this workload, from the ncu capture
 # summarised in profiles/attn_sm100_kernel_op_config.md (algorithmic minimum: BYTES_PER_STEP)
 TRAFFIC_BYTES_PER_LAUNCH = 79_097_088
-WORKLOAD = ("configs[1] op-level paged decode attention: 8 req x (64 query + 32 response rows), 28/4 heads, d128, "
-            "page 256, 4 of 32 chunks (4096 ctx tokens) per request via block table, bidirectional, N(0,1) bf16")
+OP_WORKLOAD = ("op-level paged decode attention: 8 req x (64 query + 32 response rows), 28/4 heads, d128, "
+               "page 256, 4 of 32 chunks (4096 ctx tokens) per request via block table, bidirectional, N(0,1) bf16")
 
 
 def load_peaks():
@@ -59,8 +75,42 @@ def load_peaks():
     if os.path.exists(path):
         with open(path) as handle:
             data = json.load(handle)
-        return dict(hbm=float(data["hbm_gbs"]), tflops=float(data["bf16_tflops"]), source="measured")
-    return dict(hbm=6650.0, tflops=1590.0, source="fallback")
+        return dict(hbm=float(data["hbm_gbs"]), tflops=float(data["bf16_tflops"]), tflops_sustained=float(data.get("bf16_tflops_sustained", data["bf16_tflops"])),
+                    source="measured")
+    return dict(hbm=6650.0, tflops=1590.0, tflops_sustained=1400.0, source="fallback")
+
+
+def timed_launches(fn, n_sets: int, launches: int, device):
+    """Average duration (us) of `fn(i)` over >= `launches` back-to-back launches, CUDA events on the current stream."""
+    for i in range(max(3, n_sets)):
+        fn(i)
+    torch.cuda.synchronize(device)
+    start, stop = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    stream = torch.cuda.current_stream(device)
+    start.record(stream)
+    for i in range(launches):
+        fn(i)
+    stop.record(stream)
+    torch.cuda.synchronize(device)
+    return start.elapsed_time(stop) / launches * 1e3
+
+
+def timed_graph(fn, device, replays: int = 10):
+    """ms of one execution of `fn()` replayed as a CUDA graph (no Python between its launches)."""
+    fn()
+    torch.cuda.synchronize(device)
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph, stream=torch.cuda.Stream(device=device)):
+        fn()
+    for _ in range(3):
+        graph.replay()
+    start, stop = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    start.record()
+    for _ in range(replays):
+        graph.replay()
+    stop.record()
+    torch.cuda.synchronize(device)
+    return start.elapsed_time(stop) / replays
 
 
 class ClockSampler:
@@ -117,6 +167,7 @@ class ClockSampler:
         return dict(sm_mhz=sm[len(sm) // 2] if sm else None, sm_max_mhz=sm_max, reasons=sorted(reasons), samples=len(sm))
 
 
+
 def build_batch(seed: int, device: torch.device):
     """Seeded synthetic batch of the op-level config. The pool is N(0,1) bf16; block tables come from seeded
     permutations; N_TABLES tables per request pick disjoint chunk sets so that rotating them sweeps the pool."""
@@ -145,55 +196,38 @@ def build_batch(seed: int, device: torch.device):
     return host, dev
 
 
-def run_native(args, rank: int, world: int, local_rank: int):
+
+def op_decode_attention(steps: int, warmup: int, rank: int, world: int, device: torch.device, *, with_e2e: bool = True):
+    """The op-level decode attention shape: device-resident launches, and the reference-facing op with HOST buffers (every
+    step copies q/k/v rows and the block table from pinned host memory and the output back, three streams over three
+    buffer sets so that consecutive steps overlap on the full-duplex link). Returns a sub-record."""
     from prefilling_dllm_b200 import ops
 
-    device = torch.device("cuda", local_rank)
-    torch.cuda.set_device(device)
     host, dev = build_batch(1000 + rank, device)
     out = torch.empty_like(dev["q"])
     scale = 1.0 / math.sqrt(D)
     stream = torch.cuda.current_stream(device)
+    steps = max(int(steps), 200)
 
     def step(i: int):
         ops.paged_attention(dev["q"], dev["k"], dev["v"], out, cu_seqlens_q=dev["cu"], max_query_len=ROWS,
                             key_cache=dev["k_cache"], value_cache=dev["v_cache"], block_table=dev["tables"][i % N_TABLES],
                             seq_lens=dev["seq_lens"], max_seq_len=CTX + ROWS, sm_scale=scale, bidirectional=True)
 
-    for i in range(max(3, args.warmup)):
-        step(i)
-    torch.cuda.synchronize(device)
+    us = timed_launches(step, N_TABLES, steps, device)
     ops.check_status(device)
-    # launches per step: the attention kernel (split-KV partials are merged inside it by the last CTA of a tile pair;
-    # the 4-byte-per-pair arrival counters are cleared by a memset node, not a kernel)
-    launches_per_step = 1
-
-    def barrier():
-        if world > 1:
-            torch.distributed.barrier()
-
-    sampler = ClockSampler(local_rank)
-    if rank == 0:
-        sampler.start()
-
-    # ---- device-resident timing (value) ----
-    barrier()
-    torch.cuda.synchronize(device)
-    start, stop = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    start.record(stream)
-    for i in range(args.steps):
-        step(i)
-    stop.record(stream)
-    torch.cuda.synchronize(device)
-    barrier()
-    ms_total = start.elapsed_time(stop)
-
-    # ---- end to end through the reference-facing op with HOST buffers (e2e) ----
-    # Every step copies its q/k/v rows and block table from pinned host memory, runs the op, and copies the output back to
-    # pinned host memory. The three stages run on three streams over three sets of device buffers, so step i's download,
-    # step i+1's kernel and step i+2's upload overlap (PCIe is full duplex); all of it is inside the timed region.
-    # host rows in the fused [T, Hq + 2 Hkv, D] layout a QKV projection produces: one upload per step; the op takes q, k, v
-    # as strided views of it
+    peaks = load_peaks()
+    record = {
+        "workload": OP_WORKLOAD, "launches": steps, "us_per_launch": us, "tok_per_s": NUM_REQ * ROWS / (us * 1e-6),
+        "l2": f"{N_TABLES} disjoint block tables rotate over a 537 MB K/V pool (> 126 MB L2) between launches",
+        "roofline": {"bound": "tensor", "achieved": FLOPS_PER_STEP / (us * 1e-6) / 1e12, "peak": peaks["tflops"], "unit": "TFLOP/s",
+                     "frac": FLOPS_PER_STEP / (us * 1e-6) / 1e12 / peaks["tflops"], "traffic": TRAFFIC_BYTES_PER_LAUNCH,
+                     "peak_source": peaks["source"] + " (burst bf16 GEMM)", "flops_per_launch": FLOPS_PER_STEP,
+                     "hbm": {"achieved": BYTES_PER_STEP / (us * 1e-6) / 1e9, "peak": peaks["hbm"], "unit": "GB/s",
+                             "frac": BYTES_PER_STEP / (us * 1e-6) / 1e9 / peaks["hbm"], "bytes_per_launch": BYTES_PER_STEP}},
+    }
+    if not with_e2e:
+        return record
     pin_qkv = torch.cat([host["q"], host["k"], host["v"]], dim=1).contiguous().pin_memory()
     tables_pin = host["tables"].pin_memory()
     n_buf = 3
@@ -207,7 +241,7 @@ def run_native(args, rank: int, world: int, local_rank: int):
     s_up, s_run, s_down = torch.cuda.Stream(device), torch.cuda.Stream(device), torch.cuda.Stream(device)
     h2d = pin_qkv.numel() * 2 + bufs[0]["table"].numel() * 4
     d2h = bufs[0]["out_host"].numel() * 2
-    e2e_steps = args.steps
+    e2e_steps = min(steps, 200)
 
     def e2e_step(i: int):
         b = bufs[i % n_buf]
@@ -240,7 +274,6 @@ def run_native(args, rank: int, world: int, local_rank: int):
         e2e_step(i)
     join()
     torch.cuda.synchronize(device)
-    barrier()
     e_start, e_stop = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     e_start.record(stream)
     for st in (s_up, s_run, s_down):
@@ -250,223 +283,584 @@ def run_native(args, rank: int, world: int, local_rank: int):
     join()
     e_stop.record(stream)
     torch.cuda.synchronize(device)
-    barrier()
-    e2e_ms_total = e_start.elapsed_time(e_stop)
+    e2e_us = e_start.elapsed_time(e_stop) / e2e_steps * 1e3
     # the last step's output, read on the host, must be the kernel's: compare with the device-resident result of the same table
     step((e2e_steps - 1) % N_TABLES)
     torch.cuda.synchronize(device)
     if not torch.equal(bufs[(e2e_steps - 1) % n_buf]["out_host"], out.cpu()):
         raise RuntimeError("end-to-end output differs from the device-resident run of the same inputs")
+    ops.check_status(device)
+    record["host_buffers"] = {"us_per_step": e2e_us, "tok_per_s": NUM_REQ * ROWS / (e2e_us * 1e-6), "h2d_bytes_per_step": h2d,
+                              "d2h_bytes_per_step": d2h}
+    return record
+
+
+def op_mha_decode(n_req: int, steps: int, rank: int, device: torch.device):
+    """The HBM-bound side of the decode-attention kernel: LLaDA-8B-shaped heads (32 query = 32 KV heads, d128, bf16), `n_req`
+    requests, each one 32-row block over 8256 cached tokens through a block table of pages in random physical order. One
+    launch = one layer of one denoise step; the K/V pool (2 x 1.1 GB at 16 requests) is far larger than L2."""
+    from prefilling_dllm_b200 import ops
+
+    rows, ctx, heads, page = 32, 4 * 2048 + 64, 32, 256
+    pages_per = -(-ctx // page)
+    g = torch.Generator(device=device).manual_seed(2000 + rank)
+    k_cache = torch.randn(n_req * pages_per, page, heads, D, device=device, dtype=torch.bfloat16, generator=g)
+    v_cache = torch.randn(n_req * pages_per, page, heads, D, device=device, dtype=torch.bfloat16, generator=g)
+    table = torch.randperm(n_req * pages_per, device=device, generator=g).to(torch.int32).view(n_req, pages_per).contiguous()
+    qkv = torch.randn(n_req * rows, 3 * heads, D, device=device, dtype=torch.bfloat16, generator=g)
+    q, k, v = qkv[:, :heads], qkv[:, heads:2 * heads], qkv[:, 2 * heads:]
+    out = torch.empty(n_req * rows, heads, D, device=device, dtype=torch.bfloat16)
+    cu = (torch.arange(n_req + 1, device=device) * rows).to(torch.int32)
+    seq_lens = torch.full((n_req,), ctx + rows, dtype=torch.int32, device=device)
+    used = []
+
+    def step(i):
+        used.append(ops.paged_attention(q, k, v, out, cu_seqlens_q=cu, max_query_len=rows, key_cache=k_cache, value_cache=v_cache,
+                                        block_table=table, seq_lens=seq_lens, max_seq_len=pages_per * page + rows, sm_scale=D ** -0.5,
+                                        bidirectional=True))
+
+    us = timed_launches(step, 1, max(50, min(steps, 200)), device)
+    ops.check_status(device)
+    if used[-1] != "tc":
+        raise RuntimeError(f"expected the tcgen05 attention kernel, ran {used[-1]}")
+    nbytes = n_req * (ctx * 2 * heads * D * 2 + rows * 4 * heads * D * 2)     # K/V pages once + q, k, v, out rows
+    peaks = load_peaks()
+    gbs = nbytes / us / 1e3
+    return {"workload": f"{n_req} req x 32 response rows, 32/32 heads (LLaDA-8B shape), d128, page 256, {ctx} cached tokens per request "
+                        "via block table (random page order), bidirectional, N(0,1) bf16",
+            "us_per_launch": us, "tok_per_s": n_req * rows / (us * 1e-6),
+            "roofline": {"bound": "hbm", "achieved": gbs, "peak": peaks["hbm"], "unit": "GB/s", "frac": gbs / peaks["hbm"],
+                         # dram bytes of one launch at 16 requests, from the ncu capture in profiles/attn_sm100_kernel_mha_decode.md
+                         "traffic": 2_208_000_000 if n_req == 16 else None, "peak_source": peaks["source"], "bytes_per_launch": nbytes}}
+
+
+def op_prefill_attention(device: torch.device, steps: int):
+    """The attention kernel on the two prefill shapes of the 8K request (28 / 4 heads, d128, bf16, no cached context):
+    scoring = 8 packed causal rows of 1093 tokens; joint prefill = one bidirectional sequence of 4193 tokens. Tensor-bound:
+    FLOPs = 4 Hq D x visible (row, key) pairs. Inputs (19 / 36 MB per launch incl. output) rotate over 8 sets (> L2)."""
+    from prefilling_dllm_b200 import ops
+
+    peaks = load_peaks()
+    g = torch.Generator(device=device).manual_seed(3000)
+    out_rec = {}
+    for name, lens, causal in (("scoring_causal_8x1093", [1093] * 8, True), ("joint_bidirectional_4193", [4193], False)):
+        total = sum(lens)
+        sets = [torch.randn(total, HQ + 2 * HKV, D, device=device, dtype=torch.bfloat16, generator=g) for _ in range(8)]
+        out = torch.empty(total, HQ, D, device=device, dtype=torch.bfloat16)
+        cu = torch.tensor([0] + [sum(lens[:i + 1]) for i in range(len(lens))], dtype=torch.int32, device=device)
+        used = []
+
+        def step(i):
+            qkv = sets[i % 8]
+            used.append(ops.paged_attention(qkv[:, :HQ], qkv[:, HQ:HQ + HKV], qkv[:, HQ + HKV:], out, cu_seqlens_q=cu, max_query_len=max(lens),
+                                            sm_scale=D ** -0.5, causal=causal, bidirectional=True))
+
+        us = timed_launches(step, 8, max(20, min(steps, 100)), device)
+        ops.check_status(device)
+        pairs = sum(n * (n + 1) // 2 if causal else n * n for n in lens)
+        flops = 4 * HQ * D * pairs
+        nbytes = total * (2 * HQ + 2 * HKV) * D * 2
+        tf = flops / us / 1e6
+        out_rec[name] = {"kernel": used[-1], "us_per_launch": us, "flops_per_launch": flops, "bytes_per_launch": nbytes,
+                         "roofline": {"bound": "tensor", "achieved": tf, "peak": peaks["tflops"], "unit": "TFLOP/s", "frac": tf / peaks["tflops"],
+                                      "peak_source": peaks["source"] + " (burst bf16 GEMM)", "traffic": None}}
+        del sets
+    return out_rec
+
+
+def op_linear(device: torch.device, steps: int):
+    """The GEMM kernel on the linear-layer shapes of the 8K request, next to cuBLAS (torch.matmul) on the same operands:
+    32 block rows (weight streaming: GB/s of weight bytes against the HBM peak) and the 8744 scoring rows (TFLOP/s against the
+    bf16 peak). Weights rotate over several copies (> L2); launches replayed as CUDA graphs of 8."""
+    from prefilling_dllm_b200 import ops
+
+    peaks = load_peaks()
+    g = torch.Generator(device=device).manual_seed(4000)
+    rec = {}
+    shapes = [("qkv", 4608, 3584), ("o", 3584, 3584), ("gate_up", 37888, 3584), ("down", 3584, 18944), ("lm_head", 152064, 3584)]
+    for m in (32, 8744):
+        for name, n, k in shapes:
+            if m > 128 and name == "lm_head":
+                continue
+            copies = max(2, min(8, int(300e6 // (n * k * 2)) + 1))
+            ws = [torch.randn(n, k, device=device, dtype=torch.bfloat16, generator=g) * 0.02 for _ in range(copies)]
+            x = torch.randn(m, k, device=device, dtype=torch.bfloat16, generator=g)
+            out = torch.empty(m, n, device=device, dtype=torch.bfloat16)
+            calls = 8
+            t_mine = timed_graph(lambda: [ops.linear(x, ws[i % copies], out=out) for i in range(calls)], device, replays=max(3, min(steps, 10))) / calls * 1e3
+            t_lib = timed_graph(lambda: [torch.matmul(x, ws[i % copies].t(), out=out) for i in range(calls)], device, replays=max(3, min(steps, 10))) / calls * 1e3
+            ops.check_status(device)
+            nbytes = (n * k + m * k + m * n) * 2
+            flops = 2 * m * n * k
+            entry = {"m": m, "n": n, "k": k, "us": t_mine, "cublas_us": t_lib}
+            if m <= 128:
+                entry["roofline"] = {"bound": "hbm", "achieved": nbytes / t_mine / 1e3, "peak": peaks["hbm"], "unit": "GB/s",
+                                     "frac": nbytes / t_mine / 1e3 / peaks["hbm"], "bytes_per_launch": nbytes}
+            else:
+                entry["roofline"] = {"bound": "tensor", "achieved": flops / t_mine / 1e6, "peak": peaks["tflops_sustained"], "unit": "TFLOP/s",
+                                     "frac": flops / t_mine / 1e6 / peaks["tflops_sustained"], "flops_per_launch": flops,
+                                     "peak_source": peaks["source"] + " (sustained bf16 GEMM: timed back to back)"}
+            rec[f"{name}_m{m}"] = entry
+            del ws
+    return rec
+
+
+def reference_triton_on_this_gpu(device: torch.device):
+    """The reference's own Triton kernels (staged unmodified under oracle/_ref/ops by oracle/build_ref.py), timed on this GPU on
+    the same inputs as the library's kernels: 5 warm-ups, 20 timed launches, CUDA events (the protocol of the reference's
+    examples/bench_unified_vs_distinct.py). A same-box baseline; nothing of it runs in the product path."""
+    from oracle import build_ref
+    from prefilling_dllm_b200 import ops
+
+    try:
+        ref = build_ref.load_engine_ops()
+    except Exception as exc:
+        return {"unavailable": f"{type(exc).__name__}: {exc}"}
+    rec = {"vllm_stand_in": bool(ref.stubbed_vllm)}
+    host, dev = build_batch(1000, device)
+    scale = 1.0 / math.sqrt(D)
+
+    def timed(fn):
+        for _ in range(5):
+            fn()
+        torch.cuda.synchronize(device)
+        start, stop = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        start.record()
+        for _ in range(20):
+            fn()
+        stop.record()
+        torch.cuda.synchronize(device)
+        return start.elapsed_time(stop) / 20 * 1e3
+
+    try:
+        # decode attention on the op shape: the reference reads the vLLM-style distinct layout
+        pages, page, hkv, d = dev["k_cache"].shape
+        kd = dev["k_cache"].view(pages, page, hkv, d // 8, 8).permute(0, 2, 3, 1, 4).contiguous()
+        vd = dev["v_cache"].permute(0, 2, 3, 1).contiguous()
+        mask = torch.ones(ROWS, ROWS, dtype=torch.bool, device=device)
+        out_ref, out_mine = torch.empty_like(dev["q"]), torch.empty_like(dev["q"])
+        table = dev["tables"][0]
+        us_ref = timed(lambda: ref.chunked_prefill_paged_decode(dev["q"], dev["k"], dev["v"], out_ref, "auto", kd, vd, table, dev["cu"], dev["seq_lens"],
+                                                                CTX + ROWS, ROWS, 1.0, 1.0, diffusion_blk_sz=32, sm_scale=scale, mask=mask, bidirectional=True))
+        us_mine = timed(lambda: ops.diffusion_lm_parallel_flash_decoding(dev["q"], dev["k"], dev["v"], out_mine, "auto", dev["k_cache"], dev["v_cache"], table,
+                                                                         dev["cu"], dev["seq_lens"], CTX + ROWS, ROWS, 1.0, 1.0, 32, None, None, scale, None, True))
+        err = float((out_mine.float() - out_ref.float()).norm() / out_ref.float().norm())
+        rec["decode_attention_op_shape"] = {"reference_triton_us": us_ref, "library_us": us_mine, "speedup": us_ref / us_mine, "rel_diff": err,
+                                            "note": "one block table (pages stay L2-resident across the 20 launches of either side)"}
+        del kd, vd
+        # page write of 4193 rows (K and V)
+        n_tok = 4193
+        kv = torch.randn(n_tok, 2 * HKV, D, device=device, dtype=torch.bfloat16)
+        slots = torch.randperm(pages * page, device=device)[:n_tok].to(torch.int32)
+        kc, vc = torch.zeros_like(dev["k_cache"][:64]), torch.zeros_like(dev["v_cache"][:64])
+        slots64 = (slots % (64 * page)).to(torch.int32)
+        us_ref = timed(lambda: ref.store_kvcache_unified_layout(kv[:, :HKV], kv[:, HKV:], kc, vc, slots64, "diffusion_lm"))
+        us_mine = timed(lambda: ops.store_kvcache_unified_layout(kv[:, :HKV], kv[:, HKV:], kc, vc, slots64, "diffusion_lm"))
+        rec["page_write_4193_rows"] = {"reference_triton_us": us_ref, "library_us": us_mine, "speedup": us_ref / us_mine}
+        # eviction scorer of one (chunk, layer)
+        length = 1 + 1024 + 8
+        q = torch.randn(length, HQ, D, device=device, dtype=torch.bfloat16)
+        k = torch.randn(length, HKV, D, device=device, dtype=torch.bfloat16)
+        kw = dict(prefix_len=1, chunk_len=1024, query_len=8, scale=scale, reduce_mode="sum", attention_mask="causal")
+        us_ref = timed(lambda: ref.query_to_chunk_attention_scores(q, k, **kw))
+        us_mine = timed(lambda: ops.query_to_chunk_attention_scores(q, k, **kw))
+        rec["eviction_scorer_chunk_1024"] = {"reference_triton_us": us_ref, "library_us": us_mine, "speedup": us_ref / us_mine}
+        ops.check_status(device)
+    except Exception as exc:   # a reference kernel that does not run on this GPU / Triton version: record it, time nothing more
+        rec["error"] = f"{type(exc).__name__}: {str(exc)[:300]}"
+    return rec
+
+
+# ---- whole requests ---------------------------------------------------------------------------------------------------------
+README_FLAGS = dict(score_mode="draft_self_information", score_draft_tokens=4, score_draft_partial_rounds=1, score_context_mode="single_chunk",
+                    score_attention_mask="causal", score_batch_size=8, block_length=32, threshold=0.9, temperature=0.0)
+
+
+class PhaseTimer:
+    """CUDA-event pairs around bound methods of a runtime: where one request spends its device time."""
+
+    def __init__(self, device):
+        self.device = device
+        self.spans = []
+        self.undo = []
+
+    def wrap(self, obj, attr: str, name: str):
+        inner = getattr(obj, attr)
+
+        def timed(*a, **k):
+            start, stop = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            start.record()
+            try:
+                return inner(*a, **k)
+            finally:
+                stop.record()
+                self.spans.append((name, start, stop))
+
+        setattr(obj, attr, timed)
+        self.undo.append((obj, attr, inner))
+
+    def restore(self):
+        for obj, attr, inner in self.undo:
+            setattr(obj, attr, inner)
+        self.undo = []
+
+    def totals_ms(self):
+        torch.cuda.synchronize(self.device)
+        out = {}
+        for name, start, stop in self.spans:
+            out[name] = out.get(name, 0.0) + start.elapsed_time(stop)
+        self.spans = []
+        return out
+
+
+def denoise_step_breakdown(model, rows: int, ctx: int, device):
+    """One denoise step of `rows` block rows over `ctx` cached tokens, by kernel group; every group is captured in a CUDA graph
+    of its own with the model's real weights (15 GB, streamed from HBM by every replay) and timed by CUDA events."""
+    from prefilling_dllm_b200 import ops
+
+    a = model.arch
+    hq, hkv, d, hidden, inter = a.num_attention_heads, a.num_key_value_heads, a.head_dim, a.hidden_size, a.intermediate_size
+    dt = model.dtype
+    h = torch.randn(rows, hidden, device=device, dtype=dt)
+    hi = torch.randn(rows, inter, device=device, dtype=dt)
+    attn = torch.randn(rows, hq * d, device=device, dtype=dt)
+    qkv = torch.randn(rows, hq + 2 * hkv, d, device=device, dtype=dt)
+    logits = torch.randn(1, rows, a.vocab_size, device=device, dtype=dt)
+    block = torch.full((1, rows), a.mask_token_id, dtype=torch.int64, device=device)
+    last = torch.randn(1, a.vocab_size, device=device, dtype=dt)
+    cos, sin = model._rope_tables(torch.arange(rows, device=device) + ctx)
+    n_pages = -(-ctx // model.page_size)
+    table = torch.arange(4 * -(-n_pages // 4), dtype=torch.int32, device=device).view(1, -1) % model.num_pages
+    seq_lens = torch.tensor([ctx + rows], dtype=torch.int32, device=device)
+    cu = torch.tensor([0, rows], dtype=torch.int32, device=device)
+    out = torch.empty(rows, hq, d, device=device, dtype=dt)
+    slots = torch.full((rows,), -1, dtype=torch.int32, device=device)
+    layers = a.num_hidden_layers
+
+    def linears():
+        for w in model.layers:
+            ops.linear(h, w["wqkv"], w["bqkv"]); ops.linear(attn, w["wo"]); ops.linear(h, w["wgu"], silu_mul_interleaved=True); ops.linear(hi, w["wd"])
+        ops.linear(h, model.lm_head)
+
+    def row_ops():
+        for li in range(layers):
+            kc, vc = model.layer_cache(li)
+            ops.add_rmsnorm(h, model.layers[li]["ln1"], a.rms_norm_eps, h)
+            ops.rope_inplace(qkv[:, : hq + hkv], cos.reshape(-1, d), sin.reshape(-1, d))
+            ops.store_kvcache_unified_layout(qkv[:, hq:hq + hkv], qkv[:, hq + hkv:], kc, vc, slots, "diffusion_lm")
+            ops.add_rmsnorm(h, model.layers[li]["ln2"], a.rms_norm_eps, h)
+        ops.add_rmsnorm(h, model.final_norm, a.rms_norm_eps)
+
+    def attention():
+        for li in range(layers):
+            kc, vc = model.layer_cache(li)
+            ops.paged_attention(qkv[:, :hq], qkv[:, hq:hq + hkv], qkv[:, hq + hkv:], out, cu_seqlens_q=cu, max_query_len=rows, key_cache=kc,
+                                value_cache=vc, block_table=table, seq_lens=seq_lens, max_seq_len=table.shape[1] * model.page_size + rows,
+                                sm_scale=d ** -0.5)
+
+    def unmask():
+        ops.unmask_step_batched(logits, block, mask_token_id=a.mask_token_id, threshold=0.9, last_logit=last, shift=a.logit_shift)
+
+    t_lin, t_rows, t_attn, t_unm = (timed_graph(f, device) for f in (linears, row_ops, attention, unmask))
+    ops.check_status(device)
+    n_linear = 4 * layers + 1
+    weight_bytes = (sum(w[k].numel() for w in model.layers for k in ("wqkv", "wo", "wgu", "wd")) + model.lm_head.numel()) * 2
+    act_bytes = layers * rows * (hidden + (hq + 2 * hkv) * d + hq * d + hidden + hidden + inter + inter + hidden) * 2 + rows * (hidden + a.vocab_size) * 2
+    kv_bytes = layers * (ctx * 2 * hkv * d * 2 + rows * (2 * hq + 2 * hkv) * d * 2)
+    total = t_lin + t_rows + t_attn + t_unm
+    return {
+        "rows": rows, "cached_tokens": ctx, "sum_of_groups_ms": total,
+        "groups_ms": {"linear_sm100_kernel": t_lin, "attention (+ split-KV merge)": t_attn, "rmsnorm / rope / page write": t_rows, "unmask_kernel": t_unm},
+        "share": {"linear_sm100_kernel": t_lin / total, "attention": t_attn / total, "row_ops": t_rows / total, "unmask": t_unm / total},
+        "launches": {"linear_sm100_kernel": n_linear, "attention": layers, "row_ops": 4 * layers + 1, "unmask": 1},
+        "linear_bytes": weight_bytes + act_bytes, "linear_ms": t_lin, "linear_launches": n_linear,
+        "attention_kv_gbs": kv_bytes / (t_attn * 1e-3) / 1e9,
+    }
+
+
+def build_dream7b(device):
+    from prefilling_dllm_b200.model import DreamArch, PagedDreamModel
+
+    return PagedDreamModel.random_init(DreamArch.dream_7b(), device=device, dtype=torch.bfloat16, num_pages=192, page_size=256, seed=0)
+
+
+def make_runtime(model, *, long_ctx: bool):
+    from prefilling_dllm_b200.parallelcomp import FastDLLMParallelComp, FastDLLMParallelCompConfig
+
+    cfg = FastDLLMParallelCompConfig(
+        fastdllm_dream_dir="", pretrained="", device="cuda", dtype="bfloat16", chunk_size=1024, topk_chunks=8 if long_ctx else 4,
+        max_new_tokens=64 if long_ctx else 32,
+        cache_build_mode="chunk_query" if long_ctx else "full_prompt_mask",
+        chunk_position_mode="reuse" if long_ctx else "continuous",
+        query_position_mode="after_reused_window" if long_ctx else "after_selected_chunks",
+        token_capacity=256 if long_ctx else 0, **README_FLAGS)
+    return FastDLLMParallelComp(cfg, model=model)
+
+
+def timed_requests(request, steps: int, warmup: int, device, barrier):
+    """(ms per request, result of the last one): CUDA events around `steps` back-to-back calls after `warmup` untimed ones."""
+    for _ in range(warmup):
+        request()
+    barrier()
+    start, stop = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    start.record()
+    result = None
+    for _ in range(steps):
+        result = request()
+    stop.record()
+    barrier()
+    return start.elapsed_time(stop) / steps, result
+
+
+def run_request(args, rank: int, world: int, local_rank: int):
+    from prefilling_dllm_b200 import ops
+    from prefilling_dllm_b200 import sharded as sharded_mod
+    from prefilling_dllm_b200.sharded import ShardedChunkPrefill
+
+    device = torch.device("cuda", local_rank)
+    torch.cuda.set_device(device)
+    dist = torch.distributed
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+        torch.cuda.synchronize(device)
+
+    def max_over_ranks(values):
+        t = torch.tensor(values, dtype=torch.float64, device=device)
+        if world > 1:
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return [float(v) for v in t]
+
+    model = build_dream7b(device)
+    steps, warmup = max(1, args.steps), max(3, args.warmup)
+
+    # ---------------- the 8K request: one per rank ----------------
+    rt = make_runtime(model, long_ctx=False)
+    gen = torch.Generator().manual_seed(rank)
+    context = torch.randint(0, 151000, (8192,), generator=gen).tolist()
+    query = torch.randint(0, 151000, (64,), generator=gen).tolist()
+    new_tokens = rt.max_new_tokens
+    timer = PhaseTimer(device)
+    timer.wrap(rt, "_selection_query_ids_with_score_target", "draft")
+    timer.wrap(rt, "score_chunks_self_information_batched", "scoring")
+    timer.wrap(rt, "_denoise_blocks", "decode")
+
+    def request():
+        return rt.generate(prefix_ids=rt.bos_ids(), context_ids=context, query_ids=query)
+
+    for _ in range(warmup):
+        request()
+    ops.check_status(device)
+    timer.totals_ms()
+    sampler = ClockSampler(local_rank)
+    if rank == 0:
+        sampler.start()
+    calls_before = ops.C_ABI_CALLS
+    ms_request, result = timed_requests(request, steps, 0, device, barrier)
+    launches = ops.C_ABI_CALLS - calls_before
+    phases = {k: v / steps for k, v in timer.totals_ms().items()}
+    timer.restore()
     clocks = sampler.stop() if rank == 0 else None
     ops.check_status(device)
+    phases["prefill"] = ms_request - sum(phases.values())     # the joint prefill and everything between the wrapped phases
+    ms_request, decode_ms = max_over_ranks([ms_request, phases["decode"]])
+    denoise_steps = new_tokens - 1                             # random-init weights never reach the threshold: one token per step
 
-    if world > 1:
-        t = torch.tensor([ms_total, e2e_ms_total], dtype=torch.float64, device=device)
-        torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
-        ms_total, e2e_ms_total = float(t[0]), float(t[1])
-    if rank != 0:
-        return None
+    line = None
+    if rank == 0:
+        peaks = load_peaks()
+        line = {
+            "metric": "decode_tok_per_s", "value": world * new_tokens / (decode_ms * 1e-3), "unit": "tok/s", "n_gpus": world, "steps": steps,
+            "warmup": warmup, "ms_per_step": ms_request, "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
+            "data": "synthetic",
+            "config": {"workload": "Dream-7B architecture (random init), 8192-token random prefix + 64-token query, chunk 1024 with chunk BOS, "
+                                   "draft-self-information scoring at batch 8, top-4, joint full_prompt_mask prefill, block 32, 32 new tokens, "
+                                   "threshold 0.9, greedy; one request per step and per GPU through FastDLLMParallelComp.generate",
+                       "parallelism": f"dp{world} (one request per rank, no data-path collective)",
+                       "l2": "15 GB of weights and the KV pages are streamed again by every forward (> 126 MB L2)"},
+            "e2e": {"value": world * new_tokens / (ms_request * 1e-3), "unit": "tok/s", "request_latency_ms": ms_request,
+                    "h2d_bytes_per_step": (len(context) + len(query) + 1) * 8 * 2, "d2h_bytes_per_step": new_tokens * 8 + denoise_steps * 4,
+                    "what": "host token-id lists in (ids and RoPE positions uploaded), generated ids out as a host list; one 4-byte count read per denoise step"},
+            "phases_ms": phases, "denoise_steps": denoise_steps, "ms_per_denoise_step": phases["decode"] / (denoise_steps + 1),
+            "selected_chunks": list(result.selected_chunk_indices),
+            "gpu_launches": launches, "clocks": clocks,
+        }
 
-    ms_per_step = ms_total / args.steps
-    tokens_per_step = world * NUM_REQ * ROWS
-    value = tokens_per_step / (ms_per_step * 1e-3)
-    e2e_value = tokens_per_step / (e2e_ms_total / e2e_steps * 1e-3)
-    peaks = load_peaks()
-    achieved_tf = FLOPS_PER_STEP / (ms_per_step * 1e-3) / 1e12
-    achieved_gb = BYTES_PER_STEP / (ms_per_step * 1e-3) / 1e9
-    traffic = TRAFFIC_BYTES_PER_LAUNCH
-    line = {
-        "metric": "decode_attention_tok_per_s", "value": value, "unit": "tok/s", "n_gpus": world, "steps": args.steps,
-        "warmup": max(3, args.warmup), "ms_per_step": ms_per_step, "higher_is_better": True, "scaling": "weak",
-        "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
-        "config": {"workload": WORKLOAD, "requests_per_gpu": NUM_REQ, "rows_per_request": ROWS, "ctx_tokens": CTX,
-                   "parallelism": f"dp{world} (replicas over requests, no data-path collective)",
-                   "l2": f"{N_TABLES} disjoint block tables rotate over a 537 MB K/V pool (> 126 MB L2) between steps"},
-        "roofline": {"bound": "tensor", "achieved": achieved_tf, "peak": peaks["tflops"], "unit": "TFLOP/s",
-                     "frac": achieved_tf / peaks["tflops"], "traffic": traffic, "peak_source": peaks["source"] + " (burst bf16 GEMM)",
-                     "flops_per_launch": FLOPS_PER_STEP, "hbm": {"achieved": achieved_gb, "peak": peaks["hbm"], "unit": "GB/s",
-                                                                "frac": achieved_gb / peaks["hbm"], "bytes_per_launch": BYTES_PER_STEP}},
-        "e2e": {"value": e2e_value, "unit": "tok/s", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
-                "ms_per_step": e2e_ms_total / e2e_steps},
-        "gpu_launches": launches_per_step * args.steps,
-        "clocks": clocks,
-    }
-    if world == 1:
-        line["cpu_baseline"] = cpu_baseline(sample_requests=2)
+    # ---------------- kernel shares of one denoise step + roofline of the dominant kernel (rank 0) ----------------
+    if rank == 0:
+        br = denoise_step_breakdown(model, 32, 4161, device)
+        line["kernel_share"] = {"groups_ms": br["groups_ms"], "share": br["share"], "launches": br["launches"], "sum_of_groups_ms": br["sum_of_groups_ms"],
+                                "measured_step_ms": line["ms_per_denoise_step"]}
+        gbs = br["linear_bytes"] / (br["linear_ms"] * 1e-3) / 1e9
+        line["roofline"] = {
+            "kernel": "linear_sm100_kernel, the linear layers of one denoise step (32 rows): 4 per layer + LM head",
+            "bound": "hbm", "achieved": gbs, "peak": peaks["hbm"], "unit": "GB/s", "frac": gbs / peaks["hbm"],
+            "bytes_per_launch": br["linear_bytes"] / br["linear_launches"], "us_per_launch": br["linear_ms"] * 1e3 / br["linear_launches"],
+            "launches_timed": br["linear_launches"], "traffic": LINEAR_TRAFFIC_BYTES_PER_LAUNCH, "peak_source": peaks["source"] + " (copy bandwidth)"}
+    barrier()
+
+    # ---------------- the 32K request, chunks sharded over the ranks ----------------
+    rt32 = make_runtime(model, long_ctx=True)
+    gen = torch.Generator().manual_seed(32768)
+    context32 = torch.randint(0, 151000, (32768,), generator=gen).tolist()
+    query32 = torch.randint(0, 151000, (64,), generator=gen).tolist()
+    sharded = ShardedChunkPrefill(rt32) if world > 1 else None
+    timer = PhaseTimer(device)
+    timer.wrap(rt32, "_selection_query_ids_with_score_target", "draft")
+    timer.wrap(rt32, "score_chunks_self_information_batched", "scoring")
+    timer.wrap(rt32, "_denoise_blocks", "decode")
+    timer.wrap(rt32, "_prefill_one_chunk", "chunk_eviction_and_prefill")
+    moved = {"all_gather_bytes": 0, "kv_bytes_received": 0}
+    if sharded is not None:
+        timer.wrap(sharded_mod, "all_gather_chunk_scores", "score_all_gather")
+        timer.wrap(sharded_mod, "exchange_chunk_kv", "kv_hand_off")
+        inner_exchange = sharded_mod.exchange_chunk_kv
+
+        def counting_exchange(*a, **k):
+            got_kv, got_pos = inner_exchange(*a, **k)
+            owned = {t.chunk_index for t in a[0] if t.src_rank == k["decode_rank"]}
+            moved["kv_bytes_received"] = sum(v.numel() * v.element_size() for ci, v in got_kv.items() if ci not in owned)
+            return got_kv, got_pos
+
+        sharded_mod.exchange_chunk_kv = counting_exchange
+        moved["all_gather_bytes"] = 4 * world * math.ceil(32 / world)
+
+    def request32():
+        if sharded is not None:
+            return sharded.generate(prefix_ids=rt32.bos_ids(), context_ids=context32, query_ids=query32, decode_rank=0)
+        return rt32.generate(prefix_ids=rt32.bos_ids(), context_ids=context32, query_ids=query32)
+
+    n32 = max(2, min(steps, 3))
+    for _ in range(2):
+        request32()
+    timer.totals_ms()
+    ms32, res32 = timed_requests(request32, n32, 0, device, barrier)
+    ph32 = {k: v / n32 for k, v in timer.totals_ms().items()}
+    timer.restore()
+    if sharded is not None:
+        sharded_mod.exchange_chunk_kv = inner_exchange
+    ops.check_status(device)
+    (ms32,) = max_over_ranks([ms32])
+    ph_max = max_over_ranks([ph32.get(k, 0.0) for k in ("draft", "scoring", "chunk_eviction_and_prefill", "score_all_gather", "kv_hand_off", "decode")])
+    same_selection = None
+    if world > 1 and rank == 0:
+        # the sharded selection must be the single-GPU selection: rank 0 scores all 32 chunks itself and compares
+        chunks, single, _, _, _ = rt32._prepare_candidate_chunks(prefix_ids=rt32.bos_ids(), context_ids=context32, scoring_query_ids=query32)
+        same_selection = list(single) == list(res32.selected_chunk_indices)
+    barrier()
+    if rank == 0:
+        names = ("draft", "scoring", "chunk_eviction_and_prefill", "score_all_gather", "kv_hand_off", "decode")
+        line["request_32k"] = {
+            "workload": "Dream-7B architecture, 32768-token random prefix (32 chunks of 1024) + 64-token query, top-8, token_capacity 256, "
+                        "chunk_query cache mode, 64 new tokens (2 blocks); " + (f"chunk scoring and chunk prefill sharded over {world} ranks, decode on rank 0"
+                                                                                 if world > 1 else "one GPU"),
+            "scaling": "strong", "request_latency_ms": ms32, "requests_timed": n32, "decode_tok_per_s": 64 / (ph_max[5] * 1e-3),
+            "phases_ms_max_over_ranks": dict(zip(names, ph_max)), "selected_chunks": list(res32.selected_chunk_indices),
+            "selection_equals_single_gpu": same_selection, "score_all_gather_bytes": moved["all_gather_bytes"],
+            "kv_bytes_received_by_decode_rank": moved["kv_bytes_received"],
+        }
+
+    # ---------------- op-level records ----------------
+    del rt, rt32
+    op_main = op_decode_attention(200, 3, rank, world, device, with_e2e=(rank == 0))
+    if rank == 0:
+        del model
+        torch.cuda.empty_cache()
+        line["ops"] = {"decode_attention_8_requests": op_main, "mha_decode_16_requests": op_mha_decode(16, 100, rank, device),
+                       "prefill_attention": op_prefill_attention(device, 50), "linear": op_linear(device, 5),
+                       "reference_triton_same_gpu": reference_triton_on_this_gpu(device)}
+        if world == 1:
+            line["cpu_baseline"], line["toy_same_config"] = cpu_toy_baseline(), gpu_toy_same_config(device)
+    barrier()
     return line
 
 
-def cpu_baseline(sample_requests: int, repeats: int = 1):
-    """The CPU restatement of the reference path, timed on the host cores over a bounded sample of the batch."""
-    from oracle import hotpath as oracle
+# dram__bytes_read.sum + dram__bytes_write.sum per linear_sm100_kernel launch of the denoise step (ncu, profiles/); None until captured
+LINEAR_TRAFFIC_BYTES_PER_LAUNCH = None
+
+# ---- the reference's CPU path on the toy, and this runtime on the same toy ----------------------------------------------------
+def _toy_setup(tmp):
+    sys.path.insert(0, os.path.join(ROOT, "tests", "golden"))
+    import make_golden
+
+    ckpt = os.path.join(tmp, "ckpt_toy")
+    make_golden.write_toy_checkpoint(ckpt)
+    context, query = make_golden.toy_inputs()
+    return ckpt, context, query, dict(make_golden.README_FLAGS)
+
+
+TOY_WORKLOAD = ("CPU toy: Dream architecture, 2 layers, hidden 256, 4/2 heads of 64, MLP 688, vocabulary 1024, fp32, seeded init; 4096 random "
+                "context ids + 32-token query, chunk 512 with chunk BOS, top-4, 4 draft tokens / 1 round, block 32, 32 new tokens, threshold 0.9")
+
+
+def cpu_toy_baseline(repeats: int = 3):
+    """One toy request on the host cores: the reference's own class when it is staged under oracle/_ref, else the chained CPU
+    restatement. A bounded sample by construction: the toy is the only configuration the reference can run on a CPU in seconds."""
+    import tempfile
+
+    from oracle import build_ref, toy_request
 
     cores = os.cpu_count() or 1
     torch.set_num_threads(cores)
-    host, _ = build_batch(1000, torch.device("cpu"))
-    rows = sample_requests * ROWS
-    args = dict(cu_seqlens_q=host["cu"][: sample_requests + 1].tolist(), k_cache=host["k_cache"], v_cache=host["v_cache"],
-                block_table=host["tables"][0][:sample_requests], seq_lens=host["seq_lens"][:sample_requests].tolist(),
-                sm_scale=1.0 / math.sqrt(D), bidirectional=True)
-    warm = dict(args, cu_seqlens_q=[0, ROWS], block_table=host["tables"][0][:1], seq_lens=[CTX + ROWS])
-    oracle.paged_attention(host["q"][:ROWS], host["k"][:ROWS], host["v"][:ROWS], **warm)  # warm-up: one request
-    t0 = time.perf_counter()
-    for _ in range(repeats):
-        oracle.paged_attention(host["q"][:rows], host["k"][:rows], host["v"][:rows], **args)
-    dt = (time.perf_counter() - t0) / repeats
-    return {"value": rows / dt, "unit": "tok/s", "cores": cores, "kind": "port",
-            "sample": f"{sample_requests} of the batch's {NUM_REQ} requests ({rows} rows), fp32 torch on CPU, {dt:.2f} s"}
+    with tempfile.TemporaryDirectory() as tmp:
+        ckpt, context, query, flags = _toy_setup(tmp)
+        try:
+            toy_request.run_reference_class(ckpt, context, query, flags)        # warm-up
+            got = toy_request.run_reference_class(ckpt, context, query, flags, repeats=repeats)
+            kind = "reference"
+        except build_ref.RefUnavailable:
+            from oracle.contract_model.model.modeling_dream import DreamModel
+
+            model = DreamModel.from_pretrained(ckpt).eval()
+            toy_request.run_port(model, context, query, flags)
+            got = toy_request.run_port(model, context, query, flags)
+            kind = "port"
+    return {"value": got["decode_tok_per_s"], "unit": "tok/s", "cores": cores, "kind": kind,
+            "sample": f"{TOY_WORKLOAD}; whole request {got['seconds']['total']:.2f} s, decode phase {got['seconds']['decode']:.2f} s",
+            "request_latency_ms": got["seconds"]["total"] * 1e3, "phases_ms": {k: v * 1e3 for k, v in got["seconds"].items() if k != "total"},
+            "sequences": got["sequences"], "selected_chunks": got["selected"]}
+
+
+def gpu_toy_same_config(device):
+    """This runtime on the same toy, fp32, so that the CPU figure has a same-configuration counterpart."""
+    import tempfile
+
+    from prefilling_dllm_b200.parallelcomp import load_fastdllm_parallelcomp
+
+    with tempfile.TemporaryDirectory() as tmp:
+        ckpt, context, query, flags = _toy_setup(tmp)
+        rt = load_fastdllm_parallelcomp(pretrained=ckpt, device=str(device), dtype="float32", **flags)
+        timer = PhaseTimer(device)
+        timer.wrap(rt, "_denoise_blocks", "decode")
+
+        def request():
+            return rt.generate(prefix_ids=rt.bos_ids(), context_ids=context, query_ids=query)
+
+        for _ in range(3):
+            request()
+        timer.totals_ms()
+        ms, result = timed_requests(request, 5, 0, device, lambda: torch.cuda.synchronize(device))
+        decode_ms = timer.totals_ms()["decode"] / 5
+        timer.restore()
+    return {"workload": TOY_WORKLOAD, "value": len(result.sequences) / (decode_ms * 1e-3), "unit": "tok/s", "request_latency_ms": ms,
+            "decode_ms": decode_ms, "sequences": list(result.sequences), "selected_chunks": list(result.selected_chunk_indices)}
 
 
 def run_reference(args, rank: int, world: int):
     if rank != 0:
         return None
-    steps = max(1, args.steps)
-    warm = max(0, args.warmup)
-    # every step is the same bounded sample; keep the whole run within a few minutes
-    per = 1
-    for _ in range(min(warm, 1)):
-        cpu_baseline(sample_requests=per)
+    steps = max(1, min(args.steps, 5))
     t0 = time.perf_counter()
-    results = [cpu_baseline(sample_requests=per) for _ in range(min(steps, 5))]
+    base = cpu_toy_baseline(repeats=steps)
     wall = time.perf_counter() - t0
-    value = sum(r["value"] for r in results) / len(results)
-    base = results[-1]
-    base["value"] = value
     return {
-        "impl": "reference", "metric": "decode_attention_tok_per_s", "value": value, "unit": "tok/s", "n_gpus": world,
-        "steps": len(results), "warmup": min(warm, 1), "ms_per_step": wall / len(results) * 1e3, "higher_is_better": True,
-        "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
-        "config": {"workload": WORKLOAD, "sample": base["sample"]},
-        "cpu_baseline": base,
-        "e2e": {"value": value, "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+        "impl": "reference", "metric": "decode_tok_per_s", "value": base["value"], "unit": "tok/s", "n_gpus": world, "steps": steps, "warmup": 1,
+        "ms_per_step": base["request_latency_ms"], "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+        "data": "synthetic", "config": {"workload": TOY_WORKLOAD, "note": "the one configuration the reference's CPU path finishes in seconds; "
+                                       "the native arm reports this runtime on the same toy as toy_same_config", "wall_s": wall},
+        "cpu_baseline": base, "e2e": {"value": 32 / (base["request_latency_ms"] * 1e-3), "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
-
-
-def run_request(args, rank: int, world: int, local_rank: int):
-    """End-to-end request latency and decode rate of the whole hot path at BASELINE configs[2] / configs[3] shapes:
-    Dream-7B architecture (random init, bf16), random prefix + 64-token query through the eval-class runtime.
-
-    dream7b_8k : 8192-token prefix, chunk 1024, top-4, joint full_prompt_mask prefill, 32 new tokens, ONE GPU per replica
-                 (with --gpus N every rank serves its own request: weak scaling, no collective).
-    dream7b_32k: 32768-token prefix, 32 chunks, top-8, token_capacity 256, chunk_query mode, 64 new tokens; chunk scoring
-                 and chunk prefill sharded over the N ranks (score all-gather, KV hand-off to the decode rank)."""
-    from prefilling_dllm_b200 import ops
-    from prefilling_dllm_b200.model import DreamArch, PagedDreamModel
-    from prefilling_dllm_b200.parallelcomp import FastDLLMParallelComp, FastDLLMParallelCompConfig
-    from prefilling_dllm_b200.sharded import ShardedChunkPrefill
-
-    device = torch.device("cuda", local_rank)
-    torch.cuda.set_device(device)
-    long_ctx = args.workload == "dream7b_32k"
-    prefix_len, topk, new_tokens = (32768, 8, 64) if long_ctx else (8192, 4, 32)
-    model = PagedDreamModel.random_init(DreamArch.dream_7b(), device=device, dtype=torch.bfloat16, num_pages=160, page_size=256, seed=0)
-    cfg = FastDLLMParallelCompConfig(
-        fastdllm_dream_dir="", pretrained="", device="cuda", dtype="bfloat16", chunk_size=1024, topk_chunks=topk,
-        score_mode="draft_self_information", score_draft_tokens=4, score_draft_partial_rounds=1, score_context_mode="single_chunk",
-        score_attention_mask="causal", score_batch_size=8, block_length=32, max_new_tokens=new_tokens, threshold=0.9, temperature=0.0,
-        cache_build_mode="chunk_query" if long_ctx else "full_prompt_mask",
-        chunk_position_mode="reuse" if long_ctx else "continuous",
-        query_position_mode="after_reused_window" if long_ctx else "after_selected_chunks",
-        token_capacity=256 if long_ctx else 0)
-    rt = FastDLLMParallelComp(cfg, model=model)
-    sharded = ShardedChunkPrefill(rt) if (long_ctx and world > 1) else None
-    gen = torch.Generator().manual_seed(0 if long_ctx else rank)
-    context = torch.randint(0, 151000, (prefix_len,), generator=gen).tolist()
-    query = torch.randint(0, 151000, (64,), generator=gen).tolist()
-
-    def request():
-        if sharded is not None:
-            return sharded.generate(prefix_ids=rt.bos_ids(), context_ids=context, query_ids=query, decode_rank=0)
-        return rt.generate(prefix_ids=rt.bos_ids(), context_ids=context, query_ids=query)
-
-    def barrier():
-        if world > 1:
-            torch.distributed.barrier()
-        torch.cuda.synchronize(device)
-
-    steps, warmup = max(1, min(args.steps, 20)), max(3, min(args.warmup, 5))
-    for _ in range(warmup):
-        request()
-    ops.check_status(device)
-    sampler = ClockSampler(local_rank)
-    if rank == 0:
-        sampler.start()
-    decode_s0 = rt.total_generation_time
-    phase = {"decode": 0.0}
-    inner = rt._denoise_blocks
-
-    def timed_denoise(*a, **k):
-        torch.cuda.synchronize(device)
-        t0 = time.perf_counter()
-        out = inner(*a, **k)
-        torch.cuda.synchronize(device)
-        phase["decode"] += time.perf_counter() - t0
-        return out
-
-    rt._denoise_blocks = timed_denoise
-    barrier()
-    start, stop = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    start.record()
-    for _ in range(steps):
-        request()
-    stop.record()
-    barrier()
-    ms = torch.tensor([start.elapsed_time(stop) / steps], device=device)
-    dec = torch.tensor([phase["decode"] / steps], device=device)
-    if world > 1:
-        torch.distributed.all_reduce(ms, op=torch.distributed.ReduceOp.MAX)
-        torch.distributed.all_reduce(dec, op=torch.distributed.ReduceOp.MAX)
-    clocks = sampler.stop() if rank == 0 else None
-    ops.check_status(device)
-    if rank != 0:
-        return None
-    ms_per_request, decode_s = float(ms.item()), float(dec.item())
-    requests_in_flight = 1 if long_ctx else world
-    naive = None
-    if args.naive and world == 1:
-        # What the path avoids (the comparison the reference's README quotes): no selection, no cache — every denoise
-        # step re-encodes [BOS ‖ context ‖ query ‖ generated ‖ block] bidirectionally on the same model and kernels; the LM
-        # head runs on the block's 32 (shifted) rows only. One request, CUDA-event timed.
-        mask_id = rt._mask_token_id()
-        prompt = list(rt.bos_ids()) + context + query
-        torch.cuda.synchronize(device)
-        n_start, n_stop = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        n_start.record()
-        done, n_steps = [], 0
-        with torch.inference_mode():
-            while len(done) < new_tokens:
-                blen = min(32, new_tokens - len(done))
-                block = torch.full((blen,), mask_id, dtype=torch.int64, device=device)
-                base = len(prompt) + len(done)
-                while bool((block == mask_id).any()):
-                    ids = torch.cat([rt.model.ids_tensor(prompt + done), block])
-                    rows = list(range(base - 1, base + blen - 1))
-                    logits, _ = rt._forward_packed([[0] * (base + blen)], [list(range(base + blen))], causal=False, ids_tensor=ids,
-                                                   logit_rows=rows)
-                    ops.unmask_step(logits, block, mask_token_id=mask_id, threshold=0.9, shift=False)
-                    n_steps += 1
-                done += block.tolist()
-        n_stop.record()
-        torch.cuda.synchronize(device)
-        ops.check_status(device)
-        naive_ms = n_start.elapsed_time(n_stop)
-        naive = {"ms_per_request": naive_ms, "denoise_steps": n_steps, "rows_per_step": len(prompt) + new_tokens,
-                 "speedup_of_this_path": naive_ms / ms_per_request}
-    return {
-        "metric": "request_latency_ms", "value": ms_per_request, "unit": "ms", "n_gpus": world, "steps": steps, "warmup": warmup,
-        "ms_per_step": ms_per_request, "higher_is_better": False, "scaling": "strong" if long_ctx else "weak", "vs_baseline": None,
-        "dtype": "bf16", "data": "synthetic",
-        "config": {"workload": f"{args.workload}: Dream-7B architecture, random init, {prefix_len}-token random prefix + 64-token query, "
-                               f"chunk 1024, top-{topk}, block 32, {new_tokens} new tokens, threshold 0.9, greedy, "
-                               + ("token_capacity 256, chunk_query, chunks sharded over the ranks" if long_ctx else "full_prompt_mask"),
-                   "parallelism": (f"chunks over {world} ranks, decode on rank 0" if long_ctx else f"dp{world} (one request per rank)")},
-        "decode_tok_per_s": requests_in_flight * new_tokens / decode_s if decode_s > 0 else None,
-        "decode_ms_per_request": decode_s * 1e3,
-        "requests_per_s": requests_in_flight * 1e3 / ms_per_request,
-        "full_reencode_every_step": naive,
-        "clocks": clocks,
-    }
-
 
 def run_decode_batch(args, rank: int, world: int, local_rank: int):
     """Decode throughput of the PD engine facade with `--concurrent` requests per GPU sharing every denoise step:
@@ -479,7 +873,7 @@ def run_decode_batch(args, rank: int, world: int, local_rank: int):
 
     device = torch.device("cuda", local_rank)
     torch.cuda.set_device(device)
-    # llada8b_decode_batch: the decode side of BASELINE configs[4] — LLaDA-8B architecture (32 MHA heads, un-shifted logits),
+    # llada8b_decode_batch: LLaDA-8B architecture (32 MHA heads, un-shifted logits, 16 concurrent requests),
     # each request 4 selected chunks of 2048 tokens + a 64-token query in pages
     llada = args.workload == "llada8b_decode_batch"
     arch = DreamArch.llada_8b() if llada else DreamArch.dream_7b()
@@ -533,86 +927,9 @@ def run_decode_batch(args, rank: int, world: int, local_rank: int):
     }
 
 
-def run_mha_decode_attention(args, rank: int, world: int, local_rank: int):
-    """The HBM-bound side of the decode-attention kernel: LLaDA-8B-shaped heads (32 query = 32 KV heads, d128, bf16),
-    `--concurrent` requests per GPU (default 16), each one 32-row response block attending 8256 cached tokens (4 selected
-    chunks of 2048 + a 64-token query) through a block table of pages in random physical order. One attention launch
-    per step = one layer of one denoise step. The K/V pool (2 x 1.1 GB at 16 requests) is far larger than L2.
-    Replicas over GPUs (every rank its own requests, no collective)."""
-    from prefilling_dllm_b200 import ops
-
-    device = torch.device("cuda", local_rank)
-    torch.cuda.set_device(device)
-    n_req, rows, ctx, heads, page = max(1, args.concurrent), 32, 4 * 2048 + 64, 32, 256
-    pages_per = -(-ctx // page)
-    g = torch.Generator(device=device).manual_seed(2000 + rank)
-    k_cache = torch.randn(n_req * pages_per, page, heads, D, device=device, dtype=torch.bfloat16, generator=g)
-    v_cache = torch.randn(n_req * pages_per, page, heads, D, device=device, dtype=torch.bfloat16, generator=g)
-    table = torch.randperm(n_req * pages_per, device=device, generator=g).to(torch.int32).view(n_req, pages_per).contiguous()
-    qkv = torch.randn(n_req * rows, 3 * heads, D, device=device, dtype=torch.bfloat16, generator=g)
-    q, k, v = qkv[:, :heads], qkv[:, heads:2 * heads], qkv[:, 2 * heads:]
-    out = torch.empty(n_req * rows, heads, D, device=device, dtype=torch.bfloat16)
-    cu = (torch.arange(n_req + 1, device=device) * rows).to(torch.int32)
-    seq_lens = torch.full((n_req,), ctx + rows, dtype=torch.int32, device=device)
-    scale = 1.0 / math.sqrt(D)
-    stream = torch.cuda.current_stream(device)
-
-    def step():
-        return ops.paged_attention(q, k, v, out, cu_seqlens_q=cu, max_query_len=rows, key_cache=k_cache, value_cache=v_cache,
-                                   block_table=table, seq_lens=seq_lens, max_seq_len=pages_per * page + rows, sm_scale=scale,
-                                   bidirectional=True)
-
-    warmup = max(3, args.warmup)
-    for _ in range(warmup):
-        used = step()
-    torch.cuda.synchronize(device)
-    ops.check_status(device)
-    if used != "tc":
-        raise RuntimeError(f"expected the tcgen05 attention kernel, ran {used}")
-    sampler = ClockSampler(local_rank)
-    if rank == 0:
-        sampler.start()
-    if world > 1:
-        torch.distributed.barrier()
-    torch.cuda.synchronize(device)
-    start, stop = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    start.record(stream)
-    for _ in range(args.steps):
-        step()
-    stop.record(stream)
-    torch.cuda.synchronize(device)
-    ms = torch.tensor([start.elapsed_time(stop) / args.steps], dtype=torch.float64, device=device)
-    if world > 1:
-        torch.distributed.all_reduce(ms, op=torch.distributed.ReduceOp.MAX)
-    clocks = sampler.stop() if rank == 0 else None
-    ops.check_status(device)
-    if rank != 0:
-        return None
-    ms_per_step = float(ms.item())
-    bytes_per_launch = n_req * (ctx * 2 * heads * D * 2 + rows * 4 * heads * D * 2)     # K/V pages once + q, k, v, out rows
-    flops_per_launch = n_req * 4 * heads * D * rows * (ctx + rows)
-    peaks = load_peaks()
-    gbs = bytes_per_launch / (ms_per_step * 1e-3) / 1e9
-    return {
-        "metric": "decode_attention_tok_per_s", "value": world * n_req * rows / (ms_per_step * 1e-3), "unit": "tok/s", "n_gpus": world,
-        "steps": args.steps, "warmup": warmup, "ms_per_step": ms_per_step, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
-        "dtype": "bf16", "data": "synthetic",
-        "config": {"workload": f"op_mha_decode: {n_req} req x 32 response rows, 32/32 heads (LLaDA-8B shape), d128, page 256, {ctx} cached "
-                               "tokens per request via block table (random page order), bidirectional, N(0,1) bf16",
-                   "parallelism": f"dp{world} (replicas over requests, no data-path collective)",
-                   "l2": "K/V pool of 2 x %.2f GB read once per step (> 126 MB L2)" % (k_cache.numel() * 2 / 1e9)},
-        "roofline": {"bound": "hbm", "achieved": gbs, "peak": peaks["hbm"], "unit": "GB/s", "frac": gbs / peaks["hbm"],
-                     # dram bytes of one launch at 16 requests from the ncu capture summarised in
-                     # profiles/attn_sm100_kernel_mha_decode.md; other request counts were not captured
-                     "traffic": 2_208_000_000 if n_req == 16 else None,
-                     "peak_source": peaks["source"], "bytes_per_launch": bytes_per_launch,
-                     "tensor": {"achieved": flops_per_launch / (ms_per_step * 1e-3) / 1e12, "unit": "TFLOP/s"}},
-        "gpu_launches": args.steps, "clocks": clocks,
-    }
-
 
 def run_byte_kernels(args, local_rank: int):
-    """Achieved HBM rate of each byte-moving kernel of the path at the shapes of BASELINE's Dream-7B configs, one GPU.
+    """Achieved HBM rate of each byte-moving kernel of the path at Dream-7B request shapes, one GPU.
     Every kernel runs over several independent input sets in turn, together larger than L2 (so no launch finds its input
     in the 126 MB L2), as a replayed CUDA graph of 16 launches, CUDA-event timed; bytes are the algorithmic ones (inputs read once + outputs written once)."""
     from prefilling_dllm_b200 import ops
@@ -715,94 +1032,42 @@ def run_byte_kernels(args, local_rank: int):
     }
 
 
-def run_step_breakdown(args, local_rank: int):
-    """Where one denoise step of Dream-7B (32 block rows against 4161 cached tokens, bf16) spends its time: each group
-    of launches captured in a CUDA graph of its own and replayed, CUDA-event timed. One GPU."""
-    import torch.nn.functional as F
 
-    from prefilling_dllm_b200 import ops
-    from prefilling_dllm_b200.model import DreamArch, PagedDreamModel
-
+def run_op(args, rank: int, world: int, local_rank: int):
+    """`--workload op`: the op-level decode attention alone, one replica per rank (weak scaling, no collective)."""
     device = torch.device("cuda", local_rank)
     torch.cuda.set_device(device)
-    arch = DreamArch.dream_7b()
-    m = PagedDreamModel.random_init(arch, device=device, dtype=torch.bfloat16, num_pages=64, page_size=256)
-    rows, ctx = 32, 4161
-    hq, hkv, d, hidden, inter = arch.num_attention_heads, arch.num_key_value_heads, arch.head_dim, arch.hidden_size, arch.intermediate_size
-    h = torch.randn(rows, hidden, device=device, dtype=torch.bfloat16)
-    hi = torch.randn(rows, inter, device=device, dtype=torch.bfloat16)
-    gu = torch.randn(rows, 2 * inter, device=device, dtype=torch.bfloat16)
-    qkv = torch.randn(rows, hq + 2 * hkv, d, device=device, dtype=torch.bfloat16)
-    cos, sin = m._rope_tables(torch.arange(rows, device=device) + ctx)
-    n_pages = -(-ctx // 256)
-    table = torch.arange(4 * -(-n_pages // 4), dtype=torch.int32, device=device).view(1, -1)
-    seq_lens = torch.tensor([ctx + rows], dtype=torch.int32, device=device)
-    cu = torch.tensor([0, rows], dtype=torch.int32, device=device)
-    out = torch.empty(rows, hq, d, device=device, dtype=torch.bfloat16)
-    kc, vc = m.layer_cache(0)
-    layers = arch.num_hidden_layers
-
-    def gemms():
-        for w in m.layers:
-            F.linear(h, w["wqkv"], w["bqkv"]); F.linear(h, w["wo"]); F.linear(h, w["wgu"]); F.linear(hi, w["wd"])
-        F.linear(h, m.lm_head)
-
-    def row_ops():
-        for _ in range(layers):
-            ops.add_rmsnorm(h, m.layers[0]["ln1"], 1e-6, h)
-            ops.rope_inplace(qkv[:, : hq + hkv], cos.reshape(-1, d), sin.reshape(-1, d))
-            ops.add_rmsnorm(h, m.layers[0]["ln2"], 1e-6, h)
-            ops.silu_mul(gu)
-
-    def attention():
-        for _ in range(layers):
-            ops.paged_attention(qkv[:, :hq], qkv[:, hq:hq + hkv], qkv[:, hq + hkv:], out, cu_seqlens_q=cu, max_query_len=rows, key_cache=kc,
-                                value_cache=vc, block_table=table, seq_lens=seq_lens, max_seq_len=table.shape[1] * 256 + rows, sm_scale=d ** -0.5)
-
-    def timed(fn):
-        fn()
-        torch.cuda.synchronize(device)
-        graph = torch.cuda.CUDAGraph()
-        with torch.cuda.graph(graph, stream=torch.cuda.Stream(device=device)):
-            fn()
-        for _ in range(3):
-            graph.replay()
-        start, stop = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        start.record()
-        for _ in range(max(5, min(args.steps, 20))):
-            graph.replay()
-        stop.record()
-        torch.cuda.synchronize(device)
-        return start.elapsed_time(stop) / max(5, min(args.steps, 20))
-
-    t_gemm, t_rows, t_attn = timed(gemms), timed(row_ops), timed(attention)
-    ops.check_status(device)
-    weight_bytes = (sum(w[k].numel() for w in m.layers for k in ("wqkv", "wo", "wgu", "wd")) + m.lm_head.numel()) * 2
-    kv_bytes = layers * (ctx * 2 * hkv * d * 2 + rows * (2 * hq + 2 * hkv) * d * 2)
-    peaks = load_peaks()
-    return {
-        "metric": "denoise_step_ms", "value": t_gemm + t_rows + t_attn, "unit": "ms", "n_gpus": 1, "higher_is_better": False,
-        "dtype": "bf16", "data": "synthetic",
-        "config": {"workload": "dream7b_step: one denoise step of Dream-7B, 32 block rows, 4161 cached tokens, groups replayed as CUDA graphs"},
-        "breakdown_ms": {"cublas_gemms": t_gemm, "row_ops_4_per_layer": t_rows, "attention_28_layers": t_attn},
-        "gemm_weight_gbs": weight_bytes / (t_gemm * 1e-3) / 1e9, "attention_kv_gbs": kv_bytes / (t_attn * 1e-3) / 1e9,
-        "hbm_peak_gbs": peaks["hbm"], "peak_source": peaks["source"],
-    }
+    sampler = ClockSampler(local_rank)
+    if rank == 0:
+        sampler.start()
+    rec = op_decode_attention(args.steps, args.warmup, rank, world, device)
+    t = torch.tensor([rec["us_per_launch"], rec["host_buffers"]["us_per_step"]], dtype=torch.float64, device=device)
+    if world > 1:
+        torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
+    clocks = sampler.stop() if rank == 0 else None
+    if rank != 0:
+        return None
+    us, e2e_us = float(t[0]), float(t[1])
+    return {"metric": "decode_attention_tok_per_s", "value": world * NUM_REQ * ROWS / (us * 1e-6), "unit": "tok/s", "n_gpus": world,
+            "steps": rec["launches"], "warmup": max(3, args.warmup), "ms_per_step": us * 1e-3, "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+            "config": {"workload": OP_WORKLOAD, "parallelism": f"dp{world} (replicas over requests, no data-path collective)", "l2": rec["l2"]},
+            "roofline": rec["roofline"],
+            "e2e": {"value": world * NUM_REQ * ROWS / (e2e_us * 1e-6), "unit": "tok/s", "h2d_bytes_per_step": rec["host_buffers"]["h2d_bytes_per_step"],
+                    "d2h_bytes_per_step": rec["host_buffers"]["d2h_bytes_per_step"], "ms_per_step": e2e_us * 1e-3},
+            "gpu_launches": rec["launches"], "clocks": clocks}
 
 
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=200)
-    ap.add_argument("--warmup", type=int, default=10)
+    ap.add_argument("--steps", type=int, default=10)
+    ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="native", choices=["native", "reference"])
-    ap.add_argument("--workload", default="op", choices=["op", "op_mha_decode", "byte_kernels", "dream7b_8k", "dream7b_32k", "dream7b_step", "dream7b_decode_batch",
-                             "llada8b_decode_batch"],
-                    help="op (default): BASELINE configs[1], the op-level decode attention; op_mha_decode: the same kernel on an HBM-bound "
-                         "MHA shape; the others time whole requests")
-    ap.add_argument("--naive", action="store_true", help="dream7b_8k / dream7b_32k on one GPU: also time one request that "
-                    "re-encodes the full context at every denoise step")
-    ap.add_argument("--concurrent", type=int, default=16, help="requests per GPU that share a denoise step (dream7b_decode_batch)")
+    ap.add_argument("--workload", default="request",
+                    choices=["request", "op", "op_mha_decode", "op_prefill", "linear", "byte_kernels", "dream7b_decode_batch", "llada8b_decode_batch"],
+                    help="request (default): the 8K request per GPU + the sharded 32K request + op-level records; the others run one piece alone")
+    ap.add_argument("--concurrent", type=int, default=16, help="requests per GPU that share a denoise step (decode_batch workloads, op_mha_decode)")
     args = ap.parse_args()
 
     rank = int(os.environ.get("RANK", "0"))
@@ -822,18 +1087,22 @@ def main():
         torch.cuda.set_device(local_rank)
         torch.distributed.init_process_group("nccl", device_id=torch.device("cuda", local_rank))
     try:
-        if args.workload == "op":
-            line = run_native(args, rank, world, local_rank)
+        device = torch.device("cuda", local_rank)
+        torch.cuda.set_device(device)
+        if args.workload == "request":
+            line = run_request(args, rank, world, local_rank)
+        elif args.workload == "op":
+            line = run_op(args, rank, world, local_rank)
         elif args.workload == "op_mha_decode":
-            line = run_mha_decode_attention(args, rank, world, local_rank)
+            line = op_mha_decode(max(1, args.concurrent), args.steps, rank, device) if rank == 0 else None
+        elif args.workload == "op_prefill":
+            line = op_prefill_attention(device, args.steps) if rank == 0 else None
+        elif args.workload == "linear":
+            line = op_linear(device, args.steps) if rank == 0 else None
         elif args.workload == "byte_kernels":
             line = run_byte_kernels(args, local_rank) if rank == 0 else None
-        elif args.workload in ("dream7b_decode_batch", "llada8b_decode_batch"):
-            line = run_decode_batch(args, rank, world, local_rank)
-        elif args.workload == "dream7b_step":
-            line = run_step_breakdown(args, local_rank) if rank == 0 else None
         else:
-            line = run_request(args, rank, world, local_rank)
+            line = run_decode_batch(args, rank, world, local_rank)
         if line is not None:
             print(json.dumps(line), flush=True)
     finally:

@@ -197,7 +197,7 @@ linear_sm100_kernel(const __grid_constant__ CUtensorMap a_map, const __grid_cons
       bool ok = true;
       while (ok && sched.next(a, seg)) {
         for (int kb = seg.kb0; kb < seg.kb1 && ok; ++kb) {
-          ok = mbar_wait<true>(&empty[stage], phase ^ 1, abort_flag, a);   // a fresh barrier passes the first lap
+          ok = mbar_wait(&empty[stage], phase ^ 1, abort_flag, a);   // a fresh barrier passes the first lap
           if (!ok) break;
           uint8_t* sa = smem + stage * kStageBytes;
           mbar_expect_tx(&full[stage], kStageBytes);
@@ -223,12 +223,12 @@ linear_sm100_kernel(const __grid_constant__ CUtensorMap a_map, const __grid_cons
         const int acc = n_seg & 1;
         const uint32_t acc_phase = (n_seg >> 1) & 1;
         ++n_seg;
-        ok = mbar_wait<true>(&acc_empty[acc], acc_phase ^ 1, abort_flag, a);
+        ok = mbar_wait(&acc_empty[acc], acc_phase ^ 1, abort_flag, a);
         if (!ok) break;
         tc_fence_after();
         const uint32_t d = tmem_base + static_cast<uint32_t>(acc * kBN);
         for (int kb = seg.kb0; kb < seg.kb1 && ok; ++kb) {
-          ok = mbar_wait<true>(&full[stage], phase, abort_flag, a);
+          ok = mbar_wait(&full[stage], phase, abort_flag, a);
           if (!ok) break;
           tc_fence_after();
           const uint32_t sa = smem_u32(smem + stage * kStageBytes), sb = sa + kABytes;

@@ -408,6 +408,7 @@ class _StepGraph:
         self.graph: Optional[torch.cuda.CUDAGraph] = None
         self.left: Optional[torch.Tensor] = None      # [batch] MASK slots left after the captured step
         self.eager_steps = 0
+        self.calls_per_step = 0                       # C-ABI calls the captured step makes (for launch accounting)
 
 
 class BlockStepRunner:
@@ -496,14 +497,18 @@ class BlockStepRunner:
                     gc_was_on = gc.isenabled()
                     gc.collect()
                     gc.disable()
+                    calls_before = ops.C_ABI_CALLS
                     try:
                         with torch.cuda.graph(graph, stream=torch.cuda.Stream(device=self.m.device)):
                             e.left = self._step()
                     finally:
+                        e.calls_per_step = ops.C_ABI_CALLS - calls_before
+                        ops.C_ABI_CALLS = calls_before      # capturing records the launches without running them
                         if gc_was_on:
                             gc.enable()
                     e.graph = graph                  # capturing records the launches without running them
                 e.graph.replay()
+                ops.C_ABI_CALLS += e.calls_per_step
                 left = e.left
             self.remaining = left.tolist()           # the one host read of a step
             return int(sum(self.remaining))

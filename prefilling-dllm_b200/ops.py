@@ -16,7 +16,18 @@ from typing import Dict, Optional, Tuple
 import torch
 
 from . import _lib
-from ._lib import AttnParams, check
+from ._lib import AttnParams
+
+# Calls made into the C-ABI (every one enqueues at least one kernel); a replayed CUDA graph adds the calls it captured.
+# Read by benchmarks that report how many launches a timed region made.
+C_ABI_CALLS = 0
+
+
+def check(code: int) -> None:
+    global C_ABI_CALLS
+    C_ABI_CALLS += 1
+    _lib.check(code)
+
 
 _DTYPE_CODE = {torch.float32: _lib.F32, torch.bfloat16: _lib.BF16, torch.float16: _lib.F16}
 

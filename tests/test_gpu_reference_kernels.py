@@ -1,0 +1,184 @@
+"""The reference's own Triton kernels, run on this GPU, against this library's kernels and the CPU oracle.
+
+oracle/build_ref.py stages the four op files of the reference engine (prefix_prefill, chunked_prefill_decoding_unified_kernel,
+kv_cache_kernels, triton_eviction_scorer) under oracle/_ref/ops, unmodified. Where they are staged and import (Triton on a GPU
+machine), the same seeded inputs go through (a) the reference kernel, (b) the C-ABI kernel of this library, (c) the CPU
+restatement in oracle/hotpath.py. (a) vs (c) pins the op-level oracle to the reference's code instead of to a reading of it;
+(a) vs (b) is the drop-in claim itself. Page writes and the KV gather must be bit-exact; attention (bf16) within 1e-2
+relative, row by row; the eviction scorer (fp32 reductions) within 1e-3.
+"""
+
+import math
+import types
+
+import pytest
+import torch
+
+from oracle import hotpath as oracle
+
+pytestmark = pytest.mark.gpu
+
+
+@pytest.fixture(scope="module")
+def ref_ops(cuda_device):
+    from oracle import build_ref
+
+    try:
+        return build_ref.load_engine_ops()
+    except build_ref.RefUnavailable as exc:
+        pytest.skip(str(exc))
+    except Exception as exc:  # a third-party import of the reference files failed on this image: say which
+        pytest.skip(f"the reference op files do not import here: {type(exc).__name__}: {exc}")
+
+
+@pytest.fixture(scope="module")
+def ops(cuda_device):
+    from prefilling_dllm_b200 import ops as _ops
+
+    return _ops
+
+
+def _row_rel(a, b):
+    a, b = a.float().cpu(), b.float().cpu()
+    num, den = (a - b).norm(dim=-1), b.norm(dim=-1).clamp_min(1e-12)
+    return float((num / den).max())
+
+
+def _to_distinct(k_cache, v_cache, x=8):
+    pages, page, hkv, d = k_cache.shape
+    kd = k_cache.view(pages, page, hkv, d // x, x).permute(0, 2, 3, 1, 4).contiguous()
+    vd = v_cache.permute(0, 2, 3, 1).contiguous()
+    return kd, vd
+
+
+def _decode_case(seed, num_seqs, q_lens, ctx_lens, pages_per_seq, hq=28, hkv=4, d=128, page=256):
+    g = torch.Generator().manual_seed(seed)
+    num_pages = num_seqs * pages_per_seq + 3
+    k_cache = torch.randn(num_pages, page, hkv, d, generator=g).bfloat16()
+    v_cache = torch.randn(num_pages, page, hkv, d, generator=g).bfloat16()
+    perm = torch.randperm(num_pages, generator=g)[: num_seqs * pages_per_seq].view(num_seqs, pages_per_seq).to(torch.int32)
+    cu = [0]
+    for n in q_lens:
+        cu.append(cu[-1] + n)
+    t = cu[-1]
+    q = torch.randn(t, hq, d, generator=g).bfloat16()
+    k = torch.randn(t, hkv, d, generator=g).bfloat16()
+    v = torch.randn(t, hkv, d, generator=g).bfloat16()
+    seq_lens = [c + n for c, n in zip(ctx_lens, q_lens)]
+    return dict(q=q, k=k, v=v, k_cache=k_cache, v_cache=v_cache, bt=perm, cu=cu, seq_lens=seq_lens)
+
+
+@pytest.mark.parametrize("shape", ["op_config", "reference_example"])
+@pytest.mark.parametrize("bidirectional", [True, False])
+def test_decode_attention_three_ways(ref_ops, ops, cuda_device, shape, bidirectional):
+    """chunked_prefill_paged_decode -> context_attention_fwd -> _fwd_kernel_d2f (reference) vs pdllm_paged_attention vs the
+    oracle. op_config: 8 requests x 96 new rows over 16 pages each; reference_example: the ragged shapes of the reference's
+    own kernel example (20 sequences of 64 new rows, 81-120 cached tokens in one page each)."""
+    if shape == "op_config":
+        case = _decode_case(1, 8, [96] * 8, [4096] * 8, 16)
+    else:
+        ctx = [119, 110, 81, 114, 112, 119, 110, 81, 114, 112, 119, 110, 81, 114, 112, 120, 111, 82, 115, 113]
+        case = _decode_case(2, 20, [64] * 20, ctx, 1)
+    dev = cuda_device
+    q, k, v = (case[n].to(dev) for n in ("q", "k", "v"))
+    kd, vd = _to_distinct(case["k_cache"].to(dev), case["v_cache"].to(dev))
+    bt = case["bt"].to(dev)
+    cu = torch.tensor(case["cu"], dtype=torch.int32, device=dev)
+    seq_lens = torch.tensor(case["seq_lens"], dtype=torch.int32, device=dev)
+    max_q = max(b - a for a, b in zip(case["cu"], case["cu"][1:]))
+    mask = torch.ones(max_q, max_q, dtype=torch.bool, device=dev)
+    scale = 1.0 / math.sqrt(128)
+    theirs = torch.zeros_like(q)
+    ref_ops.chunked_prefill_paged_decode(q, k, v, theirs, "auto", kd, vd, bt, cu, seq_lens, max(case["seq_lens"]), max_q, 1.0, 1.0,
+                                         diffusion_blk_sz=32, sm_scale=scale, mask=mask, bidirectional=bidirectional)
+    mine = torch.zeros_like(q)
+    ops.diffusion_lm_parallel_flash_decoding(q, k, v, mine, "auto", case["k_cache"].to(dev), case["v_cache"].to(dev), bt, cu, seq_lens,
+                                             max(case["seq_lens"]), max_q, 1.0, 1.0, 32, None, None, scale, mask, bidirectional)
+    torch.cuda.synchronize(dev)
+    ops.check_status(dev)
+    cpu = oracle.paged_attention(case["q"], case["k"], case["v"], cu_seqlens_q=case["cu"], k_cache=case["k_cache"], v_cache=case["v_cache"],
+                                 block_table=case["bt"], seq_lens=case["seq_lens"], sm_scale=scale, mask=mask.cpu(), bidirectional=bidirectional,
+                                 diffusion_blk=32)
+    print(f"{shape} bidirectional={bidirectional}: row-wise rel err  reference vs oracle {_row_rel(theirs, cpu):.2e}, "
+          f"library vs oracle {_row_rel(mine, cpu):.2e}, library vs reference {_row_rel(mine, theirs):.2e}")
+    assert _row_rel(theirs, cpu) < 1e-2, "the CPU oracle disagrees with the reference's own kernel"
+    assert _row_rel(mine, cpu) < 1e-2
+    assert _row_rel(mine, theirs) < 1e-2
+
+
+def test_page_write_bit_exact(ref_ops, ops, cuda_device):
+    g = torch.Generator().manual_seed(3)
+    n, hkv, d, pages, page, x = 500, 4, 128, 6, 256, 8
+    dev = cuda_device
+    key = torch.randn(n, hkv, d, generator=g).bfloat16().to(dev)
+    value = torch.randn(n, hkv, d, generator=g).bfloat16().to(dev)
+    slots = torch.randperm(pages * page, generator=g)[:n].to(torch.int32)
+    slots[::9] = -1
+    slots = slots.to(dev)
+    for layout in ("unified", "distinct"):
+        if layout == "unified":
+            shape_k = shape_v = (pages, page, hkv, d)
+            theirs_fn, mine_fn = ref_ops.store_kvcache_unified_layout, ops.store_kvcache_unified_layout
+        else:
+            shape_k, shape_v = (pages, hkv, d // x, page, x), (pages, hkv, d, page)
+            theirs_fn, mine_fn = ref_ops.store_kvcache_distinct_layout, ops.store_kvcache_distinct_layout
+        ka, va = torch.zeros(shape_k, dtype=torch.bfloat16, device=dev), torch.zeros(shape_v, dtype=torch.bfloat16, device=dev)
+        kb, vb = torch.zeros_like(ka), torch.zeros_like(va)
+        theirs_fn(key, value, ka, va, slots, "diffusion_lm")
+        mine_fn(key, value, kb, vb, slots, "diffusion_lm")
+        torch.cuda.synchronize(dev)
+        ops.check_status(dev)
+        assert torch.equal(ka, kb) and torch.equal(va, vb), layout
+        if layout == "unified":
+            kc, vc = torch.zeros(shape_k, dtype=torch.bfloat16), torch.zeros(shape_v, dtype=torch.bfloat16)
+            oracle.store_kvcache_unified(key.cpu(), value.cpu(), kc, vc, slots.cpu())
+            assert torch.equal(ka.cpu(), kc) and torch.equal(va.cpu(), vc)
+
+
+def test_kv_gather_bit_exact(ref_ops, ops, cuda_device):
+    """load_kvcache: the gather the reference runs per layer per step (attention_v4.py:380). The reference decorates the host
+    function itself with @triton.jit; the plain function underneath is what is called here."""
+    g = torch.Generator().manual_seed(4)
+    dev = cuda_device
+    hkv, d, page, pages = 4, 128, 256, 12
+    ctx_lens, new_lens = [300, 512, 77], [32, 64, 32]
+    k_cache = torch.randn(pages, page, hkv, d, generator=g).bfloat16()
+    v_cache = torch.randn(pages, page, hkv, d, generator=g).bfloat16()
+    bt = torch.tensor([[7, 2, 0], [5, 11, 0], [3, 0, 0]], dtype=torch.int32)
+    cu_q, cu_k = [0], [0]
+    for c, n in zip(ctx_lens, new_lens):
+        cu_q.append(cu_q[-1] + n)
+        cu_k.append(cu_k[-1] + c + n)
+    k_new = torch.randn(cu_q[-1], hkv, d, generator=g).bfloat16()
+    v_new = torch.randn(cu_q[-1], hkv, d, generator=g).bfloat16()
+    ctx = types.SimpleNamespace(
+        block_tables=bt.to(dev), context_lens=torch.tensor(ctx_lens, dtype=torch.int32, device=dev),
+        seq_lens_ts=torch.tensor(new_lens, dtype=torch.int32, device=dev), cu_seqlens_q=torch.tensor(cu_q, dtype=torch.int32, device=dev),
+        cu_seqlens_k=torch.tensor(cu_k, dtype=torch.int32, device=dev), seqs=[types.SimpleNamespace(diffusion_block_size=32)])
+    k_theirs, v_theirs = ref_ops.load_kvcache(k_cache.to(dev), v_cache.to(dev), ctx, k_new.to(dev), v_new.to(dev))
+    k_mine, v_mine = ops.load_kvcache(k_cache.to(dev), v_cache.to(dev), ctx, k_new.to(dev), v_new.to(dev))
+    torch.cuda.synchronize(dev)
+    ops.check_status(dev)
+    k_cpu, v_cpu = oracle.load_kvcache(k_cache, v_cache, bt, ctx_lens, cu_q, k_new, v_new)
+    assert torch.equal(k_theirs.cpu(), k_cpu) and torch.equal(v_theirs.cpu(), v_cpu), "the CPU oracle disagrees with the reference's gather"
+    assert torch.equal(k_mine, k_theirs) and torch.equal(v_mine, v_theirs)
+
+
+@pytest.mark.parametrize("mask_mode", ["causal", "full"])
+def test_eviction_scorer_three_ways(ref_ops, ops, cuda_device, mask_mode):
+    g = torch.Generator().manual_seed(5)
+    dev = cuda_device
+    prefix, chunk, window, hq, hkv, d = 1, 1024, 8, 28, 4, 128
+    length = prefix + chunk + window
+    q = torch.randn(length, hq, d, generator=g).bfloat16()
+    k = torch.randn(length, hkv, d, generator=g).bfloat16()
+    kw = dict(prefix_len=prefix, chunk_len=chunk, query_len=window, scale=d ** -0.5, reduce_mode="sum", attention_mask=mask_mode)
+    theirs = ref_ops.query_to_chunk_attention_scores(q.to(dev), k.to(dev), **kw)
+    mine = ops.query_to_chunk_attention_scores(q.to(dev), k.to(dev), **kw)
+    torch.cuda.synchronize(dev)
+    cpu = oracle.query_to_chunk_scores(q, k, prefix_len=prefix, chunk_len=chunk, query_len=window, scale=d ** -0.5, reduce_mode="sum",
+                                       causal=mask_mode == "causal")
+    rel = lambda a, b: float((a.float().cpu() - b.float().cpu()).norm() / b.float().cpu().norm())
+    print(f"scorer {mask_mode}: reference vs oracle {rel(theirs, cpu):.2e}, library vs reference {rel(mine, theirs):.2e}")
+    assert rel(theirs, cpu) < 1e-3, "the CPU oracle disagrees with the reference's scorer"
+    assert rel(mine, theirs) < 1e-3 and rel(mine, cpu) < 1e-3

@@ -256,3 +256,23 @@ def test_block_denoising(golden, model, inputs, chunks, variant):
     assert generated == ref["sequences"]
     # the golden list also holds the 4-slot draft round, which goes through the same forward helper
     assert states == [s for s in ref["block_states_before_each_forward"] if len(s) == blen]
+
+
+def test_whole_request_port_and_staged_reference_class(golden, model, inputs, tmp_path):
+    """The chained CPU restatement of a whole README-flags request reproduces the golden ids and selection; when the
+    reference's own class is staged under oracle/_ref it is run as well (it is what produced the golden)."""
+    from oracle import build_ref, toy_request
+
+    context, query = inputs
+    ref = golden["runs"]["readme_full_prompt_mask"]
+    got = toy_request.run_port(model, context, query, ref["flags"], bos=BOS, mask_id=MASK)
+    assert got["sequences"] == ref["sequences"] and got["selected"] == ref["selected_chunk_indices"]
+    assert max(abs(a - ref["chunk_scores"][str(i)]) for i, a in enumerate(got["scores"])) < 1e-5
+    if not build_ref.staged():
+        pytest.skip("oracle/_ref not staged on this machine (oracle/build_ref.py)")
+    import make_golden
+
+    ckpt = str(tmp_path / "ckpt")
+    make_golden.write_toy_checkpoint(ckpt)
+    theirs = toy_request.run_reference_class(ckpt, context, query, ref["flags"])
+    assert theirs["sequences"] == ref["sequences"] and theirs["selected"] == ref["selected_chunk_indices"]
