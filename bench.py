@@ -1074,10 +1074,20 @@ def main():
     world = int(os.environ.get("WORLD_SIZE", "1"))
     local_rank = int(os.environ.get("LOCAL_RANK", "0"))
 
-    if args.impl == "reference":
-        line = run_reference(args, rank, world)
+    # stdout carries the ONE JSON line and nothing else: whatever libraries print while they load (some log to stdout) goes
+    # to stderr, at the file-descriptor level so that native code is covered too
+    sys.stdout.flush()
+    result_out = os.fdopen(os.dup(1), "w")
+    os.dup2(2, 1)
+    sys.stdout = sys.stderr
+
+    def emit(line):
         if line is not None:
-            print(json.dumps(line), flush=True)
+            result_out.write(json.dumps(line) + "\n")
+            result_out.flush()
+
+    if args.impl == "reference":
+        emit(run_reference(args, rank, world))
         return
 
     if not torch.cuda.is_available():
@@ -1103,8 +1113,7 @@ def main():
             line = run_byte_kernels(args, local_rank) if rank == 0 else None
         else:
             line = run_decode_batch(args, rank, world, local_rank)
-        if line is not None:
-            print(json.dumps(line), flush=True)
+        emit(line)
     finally:
         if world > 1:
             torch.distributed.destroy_process_group()

@@ -89,8 +89,21 @@ def test_decode_attention_three_ways(ref_ops, ops, cuda_device, shape, bidirecti
     mask = torch.ones(max_q, max_q, dtype=torch.bool, device=dev)
     scale = 1.0 / math.sqrt(128)
     theirs = torch.zeros_like(q)
-    ref_ops.chunked_prefill_paged_decode(q, k, v, theirs, "auto", kd, vd, bt, cu, seq_lens, max(case["seq_lens"]), max_q, 1.0, 1.0,
-                                         diffusion_blk_sz=32, sm_scale=scale, mask=mask, bidirectional=bidirectional)
+    try:
+        ref_ops.chunked_prefill_paged_decode(q, k, v, theirs, "auto", kd, vd, bt, cu, seq_lens, max(case["seq_lens"]), max_q, 1.0, 1.0,
+                                             diffusion_blk_sz=32, sm_scale=scale, mask=mask, bidirectional=bidirectional)
+    except Exception as exc:
+        # The reference launches _fwd_kernel_d2f with fixed tile sizes; where this GPU's Triton cannot compile it (on sm_100
+        # Triton 3.6 maps its dots to tensor memory and asks for 1024 of the 512 columns) the reference kernel has no result to
+        # compare with: the library is still held to the oracle, and the skip message carries the compiler's own words.
+        mine = torch.zeros_like(q)
+        ops.diffusion_lm_parallel_flash_decoding(q, k, v, mine, "auto", case["k_cache"].to(dev), case["v_cache"].to(dev), bt, cu, seq_lens,
+                                                 max(case["seq_lens"]), max_q, 1.0, 1.0, 32, None, None, scale, mask, bidirectional)
+        cpu = oracle.paged_attention(case["q"], case["k"], case["v"], cu_seqlens_q=case["cu"], k_cache=case["k_cache"], v_cache=case["v_cache"],
+                                     block_table=case["bt"], seq_lens=case["seq_lens"], sm_scale=scale, mask=mask.cpu(), bidirectional=bidirectional,
+                                     diffusion_blk=32)
+        assert _row_rel(mine, cpu) < 1e-2
+        pytest.skip(f"the reference's decode-attention kernel does not run on this GPU: {type(exc).__name__}: {str(exc)[:200]}")
     mine = torch.zeros_like(q)
     ops.diffusion_lm_parallel_flash_decoding(q, k, v, mine, "auto", case["k_cache"].to(dev), case["v_cache"].to(dev), bt, cu, seq_lens,
                                              max(case["seq_lens"]), max_q, 1.0, 1.0, 32, None, None, scale, mask, bidirectional)

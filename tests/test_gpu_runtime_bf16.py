@@ -224,5 +224,5 @@ def test_bfloat16_run_on_the_tensor_core_kernel(golden, ckpt, variant):
     worst = max((s["gap"] / s["tol"] for s in flips), default=0.0)
     print(f"{variant}/bfloat16: {swaps} near-tie swaps in keep lists; {same}/{len(steps)} denoise steps transfer the reference's "
           f"(slot, token); the other {len(flips)} differ by at most {worst:.2f} x the tolerance of three bf16 ulps of the deciding logit")
-    assert all(s["gap"] <= s["tol"] for s in flips), [(s["step"], s["mine"], s["theirs"], s["gap"], s["tol"]) for s in flips]
+    assert all(s["gap"] <= s["tol"] for s in flips), [(s["step"], s["mine"], s["theirs"], s["gap"], s["tol"]) for s in flips if s["gap"] > s["tol"]]
     assert same / len(steps) >= 0.25
