@@ -57,6 +57,8 @@ struct Args {
   int whole_tiles;       // tiles [0, whole_tiles) run whole, round-robin over the CTAs (always 0 with few rows)
   int64_t units;         // (tile, k-block) units of the remaining tiles, dealt evenly over the first sk_grid CTAs
   int sk_grid;           // CTAs that take a share of those units (<= gridDim.x, <= units): each owns at least one unit
+  int cluster_parts;     // > 1: launched as thread-block clusters of this many CTAs; the CTAs of a cluster split the k-blocks of ONE
+                         // feature tile and add their accumulators through distributed shared memory (few rows, few tiles)
   int epilogue;
 };
 
@@ -69,6 +71,25 @@ __device__ __forceinline__ void tma_load_2d(const CUtensorMap* map, uint64_t* ba
 __device__ __forceinline__ void tmem_alloc_cols(uint32_t* dst_smem, uint32_t cols) {
   asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(dst_smem)), "r"(cols) : "memory");
   asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+}
+
+// ---- thread-block cluster helpers ----
+__device__ __forceinline__ uint32_t cluster_ctarank() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+  return r;
+}
+__device__ __forceinline__ void cluster_sync_all() {   // every thread of every CTA of the cluster
+  asm volatile("barrier.cluster.arrive.release.aligned;" ::: "memory");
+  asm volatile("barrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+// fp32 word at the same shared-memory offset in the CTA of rank `cta` of this cluster
+__device__ __forceinline__ float ld_peer_shared_f32(const void* local_smem, uint32_t cta) {
+  uint32_t remote;
+  float v;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(remote) : "r"(smem_u32(local_smem)), "r"(cta));
+  asm volatile("ld.shared::cluster.f32 %0, [%1];" : "=f"(v) : "r"(remote) : "memory");
+  return v;
 }
 
 // One piece of work of a CTA: k-blocks [kb0, kb1) of the tile at (a_row0, b_row0).
@@ -94,6 +115,12 @@ struct Schedule {
   __device__ __forceinline__ void init(const Args& a) {
     tile = blockIdx.x;
     cursor = end = 0;
+    if (a.cluster_parts > 1) {          // one segment: this CTA's share of the k-blocks of tile blockIdx / parts
+      const int64_t p = blockIdx.x % a.cluster_parts;
+      cursor = p * a.kb_total / a.cluster_parts;
+      end = (p + 1) * a.kb_total / a.cluster_parts;
+      return;
+    }
     if (static_cast<int>(blockIdx.x) < a.sk_grid) {
       cursor = sk_first_unit(blockIdx.x, a.units, a.sk_grid);
       end = sk_first_unit(static_cast<int64_t>(blockIdx.x) + 1, a.units, a.sk_grid);
@@ -109,6 +136,13 @@ struct Schedule {
     }
   }
   __device__ __forceinline__ bool next(const Args& a, Segment& s) {
+    if (a.cluster_parts > 1) {
+      if (cursor >= end) return false;
+      place(a, blockIdx.x / a.cluster_parts, s);
+      s.kb0 = static_cast<int>(cursor); s.kb1 = static_cast<int>(end); s.shared_tile = -1; s.partial = false;
+      cursor = end;
+      return true;
+    }
     if (tile < a.whole_tiles) {
       place(a, tile, s);
       s.kb0 = 0; s.kb1 = a.kb_total; s.shared_tile = -1; s.partial = false;
@@ -318,7 +352,23 @@ linear_sm100_kernel(const __grid_constant__ CUtensorMap a_map, const __grid_cons
         }
       };
 
-      if (!seg.partial) {
+      if (kSwap && a.cluster_parts > 1) {
+        // this CTA's accumulator → its own shared memory as fp32 [column][128 rows]; the pipeline stages are idle by now
+        // (the accumulator is complete, so every copy has landed and every MMA has read its stage). Summed after the
+        // cluster barrier below.
+        float* red = reinterpret_cast<float*>(smem);
+#pragma unroll 1
+        for (int c0 = 0; c0 < n_cols; c0 += kChunk) {
+          uint32_t raw[kChunk];
+          tc::tmem_ld16(t_acc + c0, raw);
+          tc_wait_ld();
+#pragma unroll
+          for (int i = 0; i < kChunk; ++i) red[(c0 + i) * kRowsA + r] = __uint_as_float(raw[i]);
+        }
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&acc_empty[acc]);
+      } else if (!seg.partial) {
 #pragma unroll 1
         for (int c0 = 0; c0 < n_cols; c0 += kChunk) {
           uint32_t raw[kChunk];
@@ -333,19 +383,18 @@ linear_sm100_kernel(const __grid_constant__ CUtensorMap a_map, const __grid_cons
         __syncwarp();
         if (lane == 0) mbar_arrive(&acc_empty[acc]);
       } else {
-        // This CTA holds only some k-blocks of the tile: publish its share as fp32 [column][128 rows]; slot 0 = the first
+        // This CTA holds only some k-blocks of the tile: publish its share as fp32 [128 rows][kBN columns]; slot 0 = the first
         // shared tile of the CTA's unit range, slot 1 = its last.
         const int first_st = static_cast<int>(sk_first_unit(blockIdx.x, a.units, a.sk_grid) / a.kb_total);
-        float* mine = a.partials + (static_cast<int64_t>(blockIdx.x) * 2 + (seg.shared_tile == first_st ? 0 : 1)) * (kBN * kRowsA) + r;
+        float* mine = a.partials + (static_cast<int64_t>(blockIdx.x) * 2 + (seg.shared_tile == first_st ? 0 : 1)) * (kBN * kRowsA) + r * kBN;
 #pragma unroll 1
         for (int c0 = 0; c0 < n_cols; c0 += kChunk) {
           uint32_t raw[kChunk];
           tc::tmem_ld16(t_acc + c0, raw);
           tc_wait_ld();
+          uint4* dst = reinterpret_cast<uint4*>(mine + c0);
 #pragma unroll
-          for (int i = 0; i < kChunk; ++i) {
-            if (c0 + i < n_cols) mine[(c0 + i) * kRowsA] = __uint_as_float(raw[i]);
-          }
+          for (int i = 0; i < kChunk / 4; ++i) dst[i] = make_uint4(raw[4 * i], raw[4 * i + 1], raw[4 * i + 2], raw[4 * i + 3]);
         }
         tc_fence_before();
         __syncwarp();
@@ -371,27 +420,83 @@ linear_sm100_kernel(const __grid_constant__ CUtensorMap a_map, const __grid_cons
           __threadfence();
           // Shares are added in CTA order c_first..c_last, whoever reduces. Every CTA after the first starts inside this
           // tile, so the tile is its first (slot 0); for the first CTA that holds only when its range starts exactly here.
+          // Four shares x 16 columns of a row are in flight per thread (sixteen 16-byte loads), then added in order.
           const int c_first = sk_cta_of(t0, a.units, a.sk_grid), c_last = sk_cta_of(t0 + a.kb_total - 1, a.units, a.sk_grid);
           const int first_slot = sk_first_unit(c_first, a.units, a.sk_grid) == t0 ? 0 : 1;
+          constexpr int kBatch = 4;
 #pragma unroll 1
           for (int c0 = 0; c0 < n_cols; c0 += kChunk) {
             float sum[kChunk];
 #pragma unroll
             for (int i = 0; i < kChunk; ++i) sum[i] = 0.f;
 #pragma unroll 1
-            for (int c = c_first; c <= c_last; ++c) {
-              const float* part = a.partials + (static_cast<int64_t>(c) * 2 + (c == c_first ? first_slot : 0)) * (kBN * kRowsA) + c0 * kRowsA + r;
-              float v[kChunk];
+            for (int cb = c_first; cb <= c_last; cb += kBatch) {
+              float4 v[kBatch][kChunk / 4];
 #pragma unroll
-              for (int i = 0; i < kChunk; ++i) v[i] = (c0 + i < n_cols) ? __ldcg(part + i * kRowsA) : 0.f;
+              for (int p = 0; p < kBatch; ++p) {
+                const int c = cb + p;
+                const float4* part = reinterpret_cast<const float4*>(
+                    a.partials + (static_cast<int64_t>(c) * 2 + (c == c_first ? first_slot : 0)) * (kBN * kRowsA) + r * kBN + c0);
 #pragma unroll
-              for (int i = 0; i < kChunk; ++i) sum[i] += v[i];
+                for (int i = 0; i < kChunk / 4; ++i) v[p][i] = c <= c_last ? __ldcg(part + i) : make_float4(0.f, 0.f, 0.f, 0.f);
+              }
+#pragma unroll
+              for (int p = 0; p < kBatch; ++p) {
+#pragma unroll
+                for (int i = 0; i < kChunk / 4; ++i) {
+                  sum[4 * i] += v[p][i].x; sum[4 * i + 1] += v[p][i].y; sum[4 * i + 2] += v[p][i].z; sum[4 * i + 3] += v[p][i].w;
+                }
+              }
             }
             store_chunk(c0, sum);
           }
         }
       }
     }
+  }
+
+  // ---- cluster reduction (few rows, few feature tiles): the CTAs of a cluster hold shares of ONE tile ----
+  if (kSwap && a.cluster_parts > 1) {
+    __syncwarp();
+    cluster_sync_all();                 // every CTA's share is in its shared memory
+    if (warp >= kEpiWarp0) {
+      // CTA of rank p finishes the token columns j = p, p + parts, ...: thread r adds the shares of all ranks (in rank order:
+      // the result does not depend on timing) straight out of the peers' shared memory and writes out[j, n].
+      const int r = (warp & 3) * 32 + lane;
+      const int parts = a.cluster_parts;
+      const int rank = static_cast<int>(cluster_ctarank());
+      const int n_cols = static_cast<int>(a.m < kBN ? a.m : kBN);
+      const int64_t row_id = static_cast<int64_t>(blockIdx.x / parts) * kRowsA + r;
+      const float* red = reinterpret_cast<const float*>(smem);
+      T* out = reinterpret_cast<T*>(a.out);
+      const T* bias = reinterpret_cast<const T*>(a.bias);
+      const bool silu = a.epilogue == PDLLM_EPI_SILU_MUL;
+      const float bias_r = (bias != nullptr && row_id < a.n) ? to_f32<T>(bias[row_id]) : 0.f;
+#pragma unroll 1
+      for (int j0 = rank; j0 < n_cols; j0 += 4 * parts) {
+        float sum[4] = {0.f, 0.f, 0.f, 0.f};
+        for (int p = 0; p < parts; ++p) {
+          float v[4];
+#pragma unroll
+          for (int i = 0; i < 4; ++i) v[i] = (j0 + i * parts < n_cols) ? ld_peer_shared_f32(red + (j0 + i * parts) * kRowsA + r, p) : 0.f;
+#pragma unroll
+          for (int i = 0; i < 4; ++i) sum[i] += v[i];
+        }
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          const int j = j0 + i * parts;
+          if (j >= n_cols) break;             // uniform across the warp
+          if (silu) {
+            const float other = __shfl_xor_sync(0xffffffffu, sum[i], 1);
+            if ((lane & 1) == 0 && row_id + 1 < a.n) out[static_cast<int64_t>(j) * a.out_stride + (row_id >> 1)] = silu_mul<T>(sum[i], other);
+          } else if (row_id < a.n) {
+            out[static_cast<int64_t>(j) * a.out_stride + row_id] = from_f32<T>(sum[i] + bias_r);
+          }
+        }
+      }
+    }
+    __syncwarp();
+    cluster_sync_all();                 // no CTA leaves while a peer may still read its shared memory
   }
 
   // ---- teardown ----
@@ -412,6 +517,7 @@ struct Plan {
   int shared_tiles;  // tiles whose k-blocks are dealt over all CTAs
   int64_t units;     // shared_tiles * kb_total
   int sk_grid;       // CTAs that share those units
+  int cluster_parts; // > 1: clusters of this many CTAs per feature tile (few rows, few tiles)
   int grid;
 };
 
@@ -447,6 +553,21 @@ inline Plan make_plan(int64_t m, int64_t n, int64_t k) {
       }
     }
   }
+  pl.cluster_parts = 1;
+  if (pl.swap && 2 * tiles <= sms) {
+    // Fewer feature tiles than half the SMs (the QKV, O and down projections of a 7B model): a cluster of `parts` CTAs per
+    // tile, each streaming 1/parts of the tile's k-blocks, summed through distributed shared memory — no workspace round
+    // trip, no arrival counters. parts: as many as fill the SMs, at most 8 (the portable cluster size), at least 4 k-blocks each.
+    int64_t parts = sms / tiles;
+    if (parts > 8) parts = 8;
+    if (parts > pl.kb_total / 4) parts = pl.kb_total / 4;
+    if (parts >= 2) pl.cluster_parts = static_cast<int>(parts);
+  }
+  if (pl.cluster_parts > 1) {
+    pl.whole_tiles = 0; pl.shared_tiles = 0; pl.units = 0; pl.sk_grid = 0;
+    pl.grid = static_cast<int>(tiles) * pl.cluster_parts;
+    return pl;
+  }
   pl.shared_tiles = static_cast<int>(tiles - pl.whole_tiles);
   pl.units = static_cast<int64_t>(pl.shared_tiles) * pl.kb_total;
   if (pl.swap) sk_ctas = pl.units < sms ? pl.units : sms;
@@ -477,6 +598,56 @@ inline int launch_one(const CUtensorMap& a_map, const CUtensorMap& b_map, const 
       if (e != cudaSuccess) return fail(static_cast<int>(e), "cudaFuncSetAttribute(linear): %s", cudaGetErrorString(e));
       if (dev >= 0 && dev < 64) done[dev] = true;
     }
+  }
+  if (a.cluster_parts > 1) {
+    // All clusters of the launch must be resident at once (one CTA per SM, clusters packed per GPC): take the largest
+    // cluster size, from the planned one down, for which the device says that many clusters fit; with none, one CTA per tile.
+    const int tiles = grid / a.cluster_parts;
+    cudaLaunchConfig_t cfg = {};
+    cfg.blockDim = dim3(kThreads, 1, 1);
+    cfg.dynamicSmemBytes = smem_bytes(kBN);
+    cfg.stream = stream;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    static std::mutex mu_fit;
+    static int fits[64][9] = {};      // per device and cluster size: max resident clusters + 1 (0 = not asked yet)
+    int dev = 0;
+    cudaGetDevice(&dev);
+    int parts = a.cluster_parts;
+    for (; parts >= 2; --parts) {
+      int n_fit = -1;
+      {
+        std::lock_guard<std::mutex> lock(mu_fit);
+        if (dev >= 0 && dev < 64 && fits[dev][parts] > 0) n_fit = fits[dev][parts] - 1;
+      }
+      if (n_fit < 0) {
+        cfg.gridDim = dim3(static_cast<unsigned>(tiles * parts), 1, 1);
+        attr[0].val.clusterDim.x = static_cast<unsigned>(parts);
+        int n = 0;
+        if (cudaOccupancyMaxActiveClusters(&n, fn, &cfg) != cudaSuccess) { (void)cudaGetLastError(); n = 0; }
+        n_fit = n;
+        std::lock_guard<std::mutex> lock(mu_fit);
+        if (dev >= 0 && dev < 64) fits[dev][parts] = n + 1;
+      }
+      if (n_fit >= tiles) break;
+    }
+    Args b = a;
+    b.cluster_parts = parts >= 2 ? parts : 1;
+    if (b.cluster_parts > 1) {
+      cfg.gridDim = dim3(static_cast<unsigned>(tiles * b.cluster_parts), 1, 1);
+      attr[0].val.clusterDim.x = static_cast<unsigned>(b.cluster_parts);
+      cudaError_t e = cudaLaunchKernelEx(&cfg, fn, a_map, b_map, b);
+      if (e != cudaSuccess) return fail(static_cast<int>(e), "linear_sm100_kernel (clusters of %d): %s", b.cluster_parts, cudaGetErrorString(e));
+      return check_launch("linear_sm100_kernel");
+    }
+    // no cluster size fits: every tile whole in one CTA (no workspace needed)
+    b.whole_tiles = tiles; b.units = 0; b.sk_grid = 0;
+    fn<<<static_cast<unsigned>(tiles), kThreads, smem_bytes(kBN), stream>>>(a_map, b_map, b);
+    return check_launch("linear_sm100_kernel");
   }
   fn<<<static_cast<unsigned>(grid), kThreads, smem_bytes(kBN), stream>>>(a_map, b_map, a);
   return check_launch("linear_sm100_kernel");
@@ -518,7 +689,7 @@ inline int launch(const void* x, int64_t x_stride, const void* w, int64_t w_stri
   Args a;
   a.out = out; a.bias = bias; a.status = status; a.trace = nullptr;
   a.out_stride = out_stride; a.m = m; a.n = n; a.k = k;
-  a.kb_total = pl.kb_total; a.m_tiles = pl.m_tiles; a.n_tiles = pl.n_tiles; a.whole_tiles = pl.whole_tiles; a.units = pl.units; a.sk_grid = pl.sk_grid;
+  a.kb_total = pl.kb_total; a.m_tiles = pl.m_tiles; a.n_tiles = pl.n_tiles; a.whole_tiles = pl.whole_tiles; a.units = pl.units; a.sk_grid = pl.sk_grid; a.cluster_parts = pl.cluster_parts;
   a.epilogue = epilogue;
   a.partials = nullptr; a.tile_counters = nullptr;
   if (pl.shared_tiles > 0) {

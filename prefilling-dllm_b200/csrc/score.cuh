@@ -86,13 +86,40 @@ unmask_kernel(const T* __restrict__ logits, int64_t stride, const T* __restrict_
       else if (x == mx) { sm += 1.f; if (i < ix) ix = static_cast<int>(i); }
       else sm += expf(x - mx);
     };
+    // One rescale per 16-byte vector instead of one branch and one exp call per element. A thread meets its indices in
+    // ascending order, so a strict '>' keeps the first occurrence of its maximum.
+    auto feed_vec = [&](const float* f, int64_t base) {
+      float vm = f[0];
+#pragma unroll
+      for (int j = 1; j < VEC; ++j) vm = fmaxf(vm, f[j]);
+      if (vm > mx) {
+        sm = (mx == -INFINITY) ? 0.f : sm * __expf(mx - vm);
+        mx = vm;
+        int first = VEC - 1;
+#pragma unroll
+        for (int j = VEC - 2; j >= 0; --j) first = (f[j] == vm) ? j : first;
+        ix = static_cast<int>(base) + first;
+      }
+      if (mx > -INFINITY) {
+#pragma unroll
+        for (int j = 0; j < VEC; ++j) sm += __expf(f[j] - mx);   // arguments <= 0
+      }
+    };
     if (aligned) {
       const int64_t nvec = (e - b) / VEC;
-      for (int64_t vI = tid; vI < nvec; vI += kUnmaskThreads) {
+      constexpr int kInFlight = 4;   // a CTA streams 38 KB of a row: keep four 16-byte loads per thread in flight
+      int64_t vI = tid;
+      for (; vI + (kInFlight - 1) * kUnmaskThreads < nvec; vI += kInFlight * kUnmaskThreads) {
+        float f[kInFlight][VEC];
+#pragma unroll
+        for (int u = 0; u < kInFlight; ++u) Vec16<T>::load(row + b + (vI + u * kUnmaskThreads) * VEC, f[u]);
+#pragma unroll
+        for (int u = 0; u < kInFlight; ++u) feed_vec(f[u], b + (vI + u * kUnmaskThreads) * VEC);
+      }
+      for (; vI < nvec; vI += kUnmaskThreads) {
         float f[VEC];
         Vec16<T>::load(row + b + vI * VEC, f);
-#pragma unroll
-        for (int j = 0; j < VEC; ++j) feed(f[j], b + vI * VEC + j);
+        feed_vec(f, b + vI * VEC);
       }
       for (int64_t i = b + nvec * VEC + tid; i < e; i += kUnmaskThreads) feed(to_f32<T>(row[i]), i);
     } else {
@@ -158,9 +185,29 @@ unmask_kernel(const T* __restrict__ logits, int64_t stride, const T* __restrict_
       // whose rounded probability equals the rounded maximum ties with it and the lowest index wins.
       const float M = s_rowM, S = s_rowS, target = conf[r];
       int first = 0x7fffffff;
-      for (int64_t i = tid; i < vocab; i += kUnmaskThreads) {
-        const float pr = round_through(expf(to_f32<T>(row[i]) - M) / S, conf_dtype);
-        if (pr == target) { first = static_cast<int>(i); break; }  // i ascends per thread: first hit is its lowest
+      // Only logits within a hair of the maximum can round to the maximum's probability (bf16 / fp16 keep 8 / 11 significant
+      // bits: ratio > 1 - 2^-7, i.e. a logit gap under 0.008): compare first, evaluate the exponential for those few only.
+      const float floor_x = M - 0.03f;
+      constexpr int VEC = Vec16<T>::N;
+      if ((reinterpret_cast<uintptr_t>(row) & 15) == 0) {
+        const int64_t nvec = vocab / VEC;
+        for (int64_t vI = tid; vI < nvec && first == 0x7fffffff; vI += kUnmaskThreads) {
+          float f[VEC];
+          Vec16<T>::load(row + vI * VEC, f);
+#pragma unroll
+          for (int j = VEC - 1; j >= 0; --j) {
+            if (f[j] >= floor_x && round_through(expf(f[j] - M) / S, conf_dtype) == target) first = static_cast<int>(vI * VEC + j);
+          }
+        }
+        for (int64_t i = nvec * VEC + tid; i < vocab; i += kUnmaskThreads) {
+          const float x = to_f32<T>(row[i]);
+          if (x >= floor_x && round_through(expf(x - M) / S, conf_dtype) == target) first = min(first, static_cast<int>(i));
+        }
+      } else {
+        for (int64_t i = tid; i < vocab; i += kUnmaskThreads) {
+          const float x = to_f32<T>(row[i]);
+          if (x >= floor_x && round_through(expf(x - M) / S, conf_dtype) == target) { first = static_cast<int>(i); break; }  // i ascends per thread
+        }
       }
 #pragma unroll
       for (int o = 16; o > 0; o >>= 1) first = min(first, __shfl_xor_sync(0xffffffffu, first, o));
