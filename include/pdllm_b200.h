@@ -144,6 +144,10 @@ int64_t pdllm_attn_workspace_bytes(const pdllm_attn_params* p);
 int pdllm_paged_attention(const pdllm_attn_params* p, void* stream);
 /* which kernel pdllm_paged_attention would run for p: PDLLM_ATTN_SIMT or PDLLM_ATTN_TC (<0 = error) */
 int pdllm_attn_select_impl(const pdllm_attn_params* p);
+/* 1 when the tcgen05 path would take its few-rows form for p (one query tile per CTA, the KV splits of a (sequence, KV head,
+ * query tile) merged inside a thread-block cluster through distributed shared memory: a block of decode rows of one or a few
+ * requests, the shape of attention_v4.py:375-397 per layer per denoise step), 0 when the twin-tile form, <0 = error */
+int pdllm_attn_uses_cluster_kernel(const pdllm_attn_params* p);
 
 /* ------------------------------------------------------------------------------------------------
  * (4) confidence-threshold unmask step

@@ -77,6 +77,7 @@ _SIGNATURES = {
     "pdllm_attn_workspace_bytes": (c_int64, [POINTER(AttnParams)]),
     "pdllm_paged_attention": (c_int, [POINTER(AttnParams), c_void_p]),
     "pdllm_attn_select_impl": (c_int, [POINTER(AttnParams)]),
+    "pdllm_attn_uses_cluster_kernel": (c_int, [POINTER(AttnParams)]),
     "pdllm_unmask_workspace_bytes": (c_int64, [c_int]),
     "pdllm_unmask_step": (c_int, [c_void_p, c_int64, c_void_p, c_int, c_int, c_int64, c_int, c_void_p, c_int64, c_float,
                                   c_int, c_void_p, c_void_p, c_void_p, c_void_p, c_int64, c_void_p]),

@@ -1,6 +1,7 @@
 // extern "C" surface of libpdllm_b200.so: argument validation and kernel launches.
 // Declarations and the reference op each entry replaces: include/pdllm_b200.h.
 #include "attn_simt.cuh"
+#include "attn_decode_sm100.cuh"
 #include "attn_sm100.cuh"
 #include "common.cuh"
 #include "dense.cuh"
@@ -8,6 +9,7 @@
 #include "kv_pages.cuh"
 #include "score.cuh"
 
+#include <cstdlib>
 #include <mutex>
 
 using namespace pdllm;
@@ -158,10 +160,17 @@ int pdllm_attn_select_impl(const pdllm_attn_params* p) {
   return ok ? PDLLM_ATTN_TC : PDLLM_ATTN_SIMT;
 }
 
+int pdllm_attn_uses_cluster_kernel(const pdllm_attn_params* p) {
+  const int impl = pdllm_attn_select_impl(p);
+  if (impl < 0) return impl;
+  return (impl == PDLLM_ATTN_TC && dec::make_plan(p).use && !getenv("PDLLM_NO_DECODE_KERNEL")) ? 1 : 0;
+}
+
 int64_t pdllm_attn_workspace_bytes(const pdllm_attn_params* p) {
   int impl = pdllm_attn_select_impl(p);
   if (impl < 0) return impl;
   if (impl != PDLLM_ATTN_TC) return 0;
+  if (dec::make_plan(p).use && !getenv("PDLLM_NO_DECODE_KERNEL")) return 0;   // the few-rows kernel merges its splits in shared memory
   return tc::workspace_bytes(p);
 }
 
@@ -170,7 +179,18 @@ int pdllm_paged_attention(const pdllm_attn_params* p, void* stream) {
   if (v <= 0) return v;
   int impl = pdllm_attn_select_impl(p);
   if (impl < 0) return impl;
-  if (impl == PDLLM_ATTN_TC) return tc::launch(p, as_stream(stream));
+  if (impl == PDLLM_ATTN_TC) {
+    // few (sequence, KV head, query tile) units: one query tile per CTA, splits merged inside a thread-block cluster
+    const dec::Plan dp = dec::make_plan(p);
+    if (dp.use && p->total_q > 0 && !getenv("PDLLM_NO_DECODE_KERNEL")) {
+      const int rc = dec::launch(p, dp, as_stream(stream));
+      if (rc != PDLLM_E_UNSUPPORTED) return rc;
+      // no cluster size fits on this device: the twin-tile kernel needs its split-KV workspace
+      if (tc::workspace_bytes(p) > 0 && (p->workspace == nullptr || p->workspace_bytes < tc::workspace_bytes(p)))
+        return fail(PDLLM_E_WORKSPACE, "attention: %lld workspace bytes needed", static_cast<long long>(tc::workspace_bytes(p)));
+    }
+    return tc::launch(p, as_stream(stream));
+  }
   return launch_attn_simt(p, as_stream(stream));
 }
 

@@ -219,6 +219,7 @@ def load_kvcache(k_cache: torch.Tensor, v_cache: torch.Tensor, context, k_new: t
 # (3)+(1) attention
 # ---------------------------------------------------------------------------------------------------
 _IMPL_CODE = {"auto": _lib.ATTN_AUTO, "simt": _lib.ATTN_SIMT, "tc": _lib.ATTN_TC}
+LAST_ATTENTION_USED_CLUSTERS = False   # whether the latest "tc" call took the few-rows form (clusters merge the KV splits)
 
 
 def paged_attention(query: torch.Tensor, key: torch.Tensor, value: torch.Tensor, output: torch.Tensor, *,
@@ -311,6 +312,8 @@ def paged_attention(query: torch.Tensor, key: torch.Tensor, value: torch.Tensor,
         # zero-filled when it is created; the kernel keeps its arrival counters at zero between launches
         ws = _workspace(device, "attn", int(need), zero=True)
         p.workspace, p.workspace_bytes, p.workspace_zeroed = ws.data_ptr(), ws.numel(), 1
+    global LAST_ATTENTION_USED_CLUSTERS
+    LAST_ATTENTION_USED_CLUSTERS = chosen == _lib.ATTN_TC and lib.pdllm_attn_uses_cluster_kernel(ctypes.byref(p)) == 1
     check(lib.pdllm_paged_attention(ctypes.byref(p), _stream(device)))
     return "tc" if chosen == _lib.ATTN_TC else "simt"
 

@@ -55,8 +55,14 @@ def test_forced_splits_are_honoured(lib):
     assert _partials(lib, 2, 28, 4, 36, 4096 + 36, num_splits=3) == 2 * 4 * 2 * 3
 
 
-def test_few_units_split_to_fill_the_sms(lib):
-    # one request, one block of 32 rows (two query tiles, 4 units): the cost model settles between 8 and 16 splits
+def test_few_units_go_to_the_cluster_kernel(lib, monkeypatch):
+    # one request, one block of 32 rows (two query tiles x 4 KV heads = 8 units): the few-rows kernel merges its KV splits
+    # inside thread-block clusters and needs no workspace ...
+    assert _partials(lib, 1, 28, 4, 32, 4161 + 32) == 0
+    # ... a forced split count keeps the shape on the twin-tile kernel, which merges through partials in the workspace
+    assert _partials(lib, 1, 28, 4, 32, 4161 + 32, num_splits=12) == 1 * 4 * 2 * 12
+    # ... and with the few-rows kernel switched off its cost model settles between 8 and 16 splits
+    monkeypatch.setenv("PDLLM_NO_DECODE_KERNEL", "1")
     n = _partials(lib, 1, 28, 4, 32, 4161 + 32)
     assert n % 8 == 0 and 8 <= n // 8 <= 16
 

@@ -365,6 +365,42 @@ def test_attention_tc_shapes_the_runtime_issues(ops, cuda_device):
     assert_attention_close(out, _ref_attention(block), "decode rows over a ragged 17-page table")
 
 
+def test_attention_few_rows_cluster_kernel(ops, cuda_device):
+    """A block of decode rows of one or a few requests: one query tile per CTA, the KV splits of a (sequence, KV head, query
+    tile) merged inside a thread-block cluster through distributed shared memory. Ragged query lengths and contexts (a last
+    page of 65 tokens, splits that get nothing), GQA 7 and MHA, every mask rule, poisoned page tails; checked row by row
+    against the oracle and, bit for bit, against a second launch."""
+    g = torch.Generator().manual_seed(9)
+    dense = torch.rand(64, 64, generator=g) > 0.4
+    dense[3, :] = False
+    shapes = [
+        dict(num_seqs=1, hq=28, hkv=4, q_lens=[32], sel_chunks=17, ctx_tail=0),                     # one request's denoise step
+        dict(num_seqs=2, hq=28, hkv=4, q_lens=[32, 32], sel_chunks=17, ctx_tail=256 - 65),          # the second ends in a 65-token page
+        dict(num_seqs=3, hq=28, hkv=4, q_lens=[32, 7, 20], sel_chunks=5, ctx_tail=100),
+        dict(num_seqs=2, hq=8, hkv=8, q_lens=[32, 64], sel_chunks=3, ctx_tail=250),                 # MHA: 32 and 64 rows per tile
+        dict(num_seqs=1, hq=28, hkv=4, q_lens=[4], sel_chunks=2, ctx_tail=0),                       # a draft round
+    ]
+    for i, sh in enumerate(shapes):
+        case = _attention_case(60 + i, num_seqs=sh["num_seqs"], hq=sh["hq"], hkv=sh["hkv"], d=128, page=256, chunks_in_pool=sh["sel_chunks"],
+                               pages_per_chunk=1, sel_chunks=sh["sel_chunks"], q_lens=sh["q_lens"], dtype=torch.bfloat16, ctx_tail=sh["ctx_tail"])
+        # rows of every page past what any sequence reads hold NaN bit patterns: they must not leak through masked keys
+        for s_idx in range(sh["num_seqs"]):
+            ctx = case["seq_lens"][s_idx] - sh["q_lens"][s_idx]
+            last_page, used = int(case["bt"][s_idx, (ctx - 1) // 256]), (ctx - 1) % 256 + 1
+            if used < 256:
+                case["k_cache"][last_page, used:] = float("nan")
+                case["v_cache"][last_page, used:] = float("nan")
+        for kwargs in (dict(), dict(bidirectional=False), dict(causal=True), dict(mask=dense, bidirectional=True)):
+            if "mask" in kwargs and max(sh["q_lens"]) > 64:
+                continue
+            out, used = _run_attention(ops, cuda_device, case, impl="auto", **kwargs)
+            assert used == "tc" and ops.LAST_ATTENTION_USED_CLUSTERS, (sh, kwargs)
+            clean = dict(case, k_cache=torch.nan_to_num(case["k_cache"]), v_cache=torch.nan_to_num(case["v_cache"]))
+            assert_attention_close(out, _ref_attention(clean, **kwargs), (sh, kwargs))
+            again, _ = _run_attention(ops, cuda_device, case, impl="auto", **kwargs)
+            assert torch.equal(out, again), (sh, kwargs)
+
+
 def test_attention_tc_uninitialised_pool_tail_is_harmless(ops, cuda_device):
     # rows of a page past the context length may hold NaN bit patterns; they must not leak into the output
     case = _attention_case(24, num_seqs=2, hq=28, hkv=4, d=128, page=256, chunks_in_pool=2, pages_per_chunk=1, sel_chunks=1,
