@@ -7,13 +7,15 @@
 //   * a CTA owns ONE GQA-packed query tile (<= 128 rows = tokens x heads of a KV group) and a contiguous range of 128-key
 //     tiles: Q·K^T (128 x 128) -> softmax -> P·V per tile, S double-buffered in TMEM so the next Q·K^T overlaps the softmax;
 //   * the splits of one (sequence, KV head, query tile) form a THREAD-BLOCK CLUSTER (up to 16 CTAs, as many as the device
-//     keeps resident). Every CTA leaves its unnormalised O, row maxima and row sums in its own shared memory; after a
-//     cluster barrier each CTA merges a slice of the head dimension straight out of its peers' shared memory and writes the
-//     final rows. No partials in HBM, no second launch, no arrival counters.
+//     keeps resident), so they are co-scheduled and may meet at a hardware barrier. Every CTA writes its unnormalised O, row
+//     maxima and row sums (fp32) to a workspace that stays in L2; after ONE cluster barrier each CTA merges a slice of the
+//     head dimension over all shares and writes the final rows. The merge is spread over all CTAs of the unit, there is no
+//     second launch and no arrival counter. (Reading the shares straight out of the peers' shared memory was measured
+//     slower: 7 us of distributed-shared-memory loads against 2 us through L2 for 10 shares of 64 KB.)
 // Operands come by TMA out of the paged pool exactly as in the twin-tile kernel (page id = a tensor-map coordinate, no
 // gather); masks follow the same rules (context always visible; new keys block-causal / bidirectional / dense mask / causal).
 // Roles: warp 0 TMA producer, warp 1 MMA issuer + TMEM owner, warps 2-5 softmax + epilogue (thread = tile row = TMEM lane).
-// Every mbarrier wait is bounded; nobody leaves before the cluster barriers, so a CTA that gave up cannot strand its peers.
+// Every mbarrier wait is bounded; nobody leaves before the cluster barrier, so a CTA that gave up cannot strand its peers.
 #pragma once
 
 #include "attn_sm100.cuh"
@@ -37,12 +39,22 @@ constexpr int kSmemQ = 0;
 constexpr int kSmemK = kQBytes;
 constexpr int kSmemV = kSmemK + kRing * kKvBytes;
 constexpr int kSmemBar = kSmemV + kRing * kKvBytes;  // 160 KB
-constexpr int kSmemMl = kSmemBar + 256;              // (m, l) of this CTA's rows: [2][128] fp32
-constexpr int kSmemBytes = kSmemMl + 1024 + 1024;    // + slack to align the base to 1024 B
+constexpr int kSmemBytes = kSmemBar + 256 + 1024;    // + slack to align the base to 1024 B
 constexpr uint32_t kTmemCols = 512;
 constexpr uint32_t kColS = 0;                        // S_0, S_1: 128 fp32 columns each; P (bf16 pairs) aliases the first 64
 constexpr uint32_t kColO = 256;                      // O: 128 columns
 constexpr int kMaxCluster = 16;
+// A CTA's fp32 O share is laid out [column group of 4][128 rows][4]: the 16-byte accesses of a warp (32 consecutive rows, one
+// column group) cover 512 contiguous bytes, for the writer and for the merging readers alike.
+constexpr int kPartStride = kHeadDim;
+constexpr int64_t kShareFloats = static_cast<int64_t>(kTileM) * kPartStride + 2 * kTileM;   // O + (m, l) of one CTA
+
+// Optional timeline of the first CTA (only with -DPDLLM_ENABLE_TRACE): trace[event] = %globaltimer in nanoseconds.
+#ifdef PDLLM_ENABLE_TRACE
+#define PDLLM_DEC_TRACE(ev) do { if (a.trace != nullptr && blockIdx.x == 0 && (ev) < 64) { long long t_; asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t_)); a.trace[(ev)] = t_; } } while (0)
+#else
+#define PDLLM_DEC_TRACE(ev) do { } while (0)
+#endif
 
 // barrier indices
 constexpr int kQFull = 0, kKFull = 1, kVFull = 3, kKFree = 5, kVFree = 7, kSFull = 9, kPFull = 11, kPvDone = 13, kNumBars = 15;
@@ -51,7 +63,8 @@ struct Args {
   void* out;
   const int32_t* block_table; const int32_t* cu_seqlens_q; const int32_t* seq_lens;
   const uint8_t* mask; int32_t* status;
-  long long* trace;    // unused; the shared bounded-wait helper expects the member
+  long long* trace;    // timeline of CTA 0 in a build with PDLLM_ENABLE_TRACE, else unused
+  float* shares;       // [CTA][128 rows][kPartStride] fp32 O, then [CTA][2][128] (m, l)
   int64_t out_stride, block_table_stride, mask_stride_m, mask_stride_n, num_pages;
   int num_seqs, max_pages, num_kv_heads, group, tpt, q_tiles, splits;
   int page_size, has_cache, mask_mode, bidirectional, block_m;
@@ -69,10 +82,11 @@ attn_decode_sm100_kernel(const __grid_constant__ CUtensorMap q_map, const __grid
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + kSmemBar + 128);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + kSmemBar + 136);
   volatile int* tile_flags = reinterpret_cast<volatile int*>(smem + kSmemBar + 144);   // [4]: page of tile (it & 3) was unreadable
-  float* ml = reinterpret_cast<float*>(smem + kSmemMl);
-  float* part_o = reinterpret_cast<float*>(smem + kSmemK);   // after the main loop: fp32 O as [d][128 rows], 64 KB over the K ring
+  float* part_o = a.shares + static_cast<int64_t>(blockIdx.x) * kShareFloats;     // this CTA's share: O [128 rows][128], then (m, l)
+  float* ml = part_o + kTileM * kPartStride;
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  if (threadIdx.x == 64) PDLLM_DEC_TRACE(0);
 
   // ---- work unit: (sequence, KV head, query tile) x split; the splits of a unit are the CTAs of one cluster ----
   const int split = static_cast<int>(blockIdx.x) % a.splits;
@@ -100,52 +114,60 @@ attn_decode_sm100_kernel(const __grid_constant__ CUtensorMap q_map, const __grid
   const int t_end = min(total_tiles, t_begin + per_split);
   const int n_iter = n_tok > 0 ? t_end - t_begin : 0;
 
-  // ---- set-up ----
-  if (warp == 1) {
+  // ---- set-up: warp 0 initialises the barriers and starts the first copies at once, warp 1 allocates TMEM meanwhile ----
+  // one K or V tile of key tile `it` → its ring slot (the caller has made sure the slot is free)
+  auto load_kv = [&](int it, int is_v) {
+    const int slot = it & 1;
+    const TileInfo ti = tile_info(t_begin + it, n_ctx_tiles, ctx_len, new_end);
+    uint64_t* bar = &bars[(is_v ? kVFull : kKFull) + slot];
+    uint8_t* dst = smem + (is_v ? kSmemV : kSmemK) + slot * kKvBytes;
+    mbar_expect_tx(bar, kKvBytes);
+    if (ti.is_ctx) {
+      const int pidx = ti.key0 / a.page_size;
+      const int off = ti.key0 - pidx * a.page_size;
+      int page = (pidx < a.max_pages) ? a.block_table[seq * a.block_table_stride + pidx] : -1;
+      const bool bad = page < 0 || page >= a.num_pages;
+      if (bad) { report_status(a.status, PDLLM_S_BAD_PAGE); page = 0; }   // keep the copy in bounds; the softmax warps hide the tile
+      if (!is_v) tile_flags[it & 3] = bad ? 1 : 0;   // reaches the softmax warps through K-full -> S-full; the producer runs at most 3 tiles ahead
+      tc::tma_load_5d(is_v ? &vc_map : &kc_map, bar, dst, 0, off, 0, kvh, page);
+    } else {
+      if (!is_v) tile_flags[it & 3] = 0;
+      tc::tma_load_4d(is_v ? &vn_map : &kn_map, bar, dst, 0, q_start + ti.key0, 0, kvh);
+    }
+  };
+  if (warp == 0) {
     if (lane == 0) {
       for (int i = 0; i < kNumBars; ++i) mbar_init(&bars[i], (i >= kPFull && i < kPFull + 2) ? 128u : 1u);
       abort_flag[0] = 0;
       fence_barrier_init();
+      if (n_iter > 0) {
+        mbar_expect_tx(&bars[kQFull], 2u * 64u * 2u * static_cast<uint32_t>(G * a.tpt));
+        tc::tma_load_3d(&q_map, &bars[kQFull], smem + kSmemQ, 0, kvh * G, q_start + tok0);
+        tc::tma_load_3d(&q_map, &bars[kQFull], smem + kSmemQ + kQBytes / 2, 64, kvh * G, q_start + tok0);
+        for (int it = 0; it < n_iter && it < kRing; ++it) { load_kv(it, 0); load_kv(it, 1); }   // both ring slots are free at the start
+      }
     }
     __syncwarp();
+  } else if (warp == 1) {
     gemm::tmem_alloc_cols(tmem_slot, kTmemCols);
   }
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
+  if (threadIdx.x == 64) PDLLM_DEC_TRACE(1);
 
   if (n_iter > 0) {
     if (warp == 0) {
-      // =========================== TMA producer ===========================
+      // =========================== TMA producer: tiles 2.. as their ring slots come free ===========================
       if (lane == 0) {
-        mbar_expect_tx(&bars[kQFull], 2u * 64u * 2u * static_cast<uint32_t>(G * a.tpt));
-        tc::tma_load_3d(&q_map, &bars[kQFull], smem + kSmemQ, 0, kvh * G, q_start + tok0);
-        tc::tma_load_3d(&q_map, &bars[kQFull], smem + kSmemQ + kQBytes / 2, 64, kvh * G, q_start + tok0);
         bool ok = true;
-        for (int it = 0; it < n_iter && ok; ++it) {
+        for (int it = kRing; it < n_iter && ok; ++it) {
           const int slot = it & 1;
           const uint32_t use = (it >> 1) & 1;
-          const TileInfo ti = tile_info(t_begin + it, n_ctx_tiles, ctx_len, new_end);
-          int page = 0, off = 0;
-          if (ti.is_ctx) {
-            const int pidx = ti.key0 / a.page_size;
-            off = ti.key0 - pidx * a.page_size;
-            page = (pidx < a.max_pages) ? a.block_table[seq * a.block_table_stride + pidx] : -1;
-            const bool bad = page < 0 || page >= a.num_pages;
-            if (bad) { report_status(a.status, PDLLM_S_BAD_PAGE); page = 0; }
-            tile_flags[it & 3] = bad ? 1 : 0;   // reaches the softmax warps through K-full -> S-full; the producer runs at most 3 tiles ahead
-          } else {
-            tile_flags[it & 3] = 0;
-          }
           for (int is_v = 0; is_v < 2 && ok; ++is_v) {
-            ok = mbar_wait(&bars[(is_v ? kVFree : kKFree) + slot], use ^ 1, abort_flag, a);   // a fresh barrier passes the first lap
-            if (!ok) break;
-            uint64_t* bar = &bars[(is_v ? kVFull : kKFull) + slot];
-            uint8_t* dst = smem + (is_v ? kSmemV : kSmemK) + slot * kKvBytes;
-            mbar_expect_tx(bar, kKvBytes);
-            if (ti.is_ctx) tc::tma_load_5d(is_v ? &vc_map : &kc_map, bar, dst, 0, off, 0, kvh, page);
-            else tc::tma_load_4d(is_v ? &vn_map : &kn_map, bar, dst, 0, q_start + ti.key0, 0, kvh);
+            ok = mbar_wait(&bars[(is_v ? kVFree : kKFree) + slot], use ^ 1, abort_flag, a);   // the MMAs on tile it - 2 are done
+            if (ok) load_kv(it, is_v);
           }
         }
         if (!ok) {   // abandoning: let copies in flight land (bounded)
@@ -176,6 +198,7 @@ attn_decode_sm100_kernel(const __grid_constant__ CUtensorMap q_map, const __grid
           }
           umma_commit(&bars[kSFull + slot]);
           umma_commit(&bars[kKFree + slot]);
+          PDLLM_DEC_TRACE(10 + 4 * it);
         }
         __syncwarp();
         return true;
@@ -209,6 +232,7 @@ attn_decode_sm100_kernel(const __grid_constant__ CUtensorMap q_map, const __grid
           }
           umma_commit(&bars[kPvDone + slot]);
           umma_commit(&bars[kVFree + slot]);
+          PDLLM_DEC_TRACE(11 + 4 * it);
         }
         __syncwarp();
       }
@@ -240,6 +264,7 @@ attn_decode_sm100_kernel(const __grid_constant__ CUtensorMap q_map, const __grid
         ok = mbar_wait(&bars[kSFull + slot], use, abort_flag, a);
         if (!ok) break;
         tc_fence_after();
+        if (threadIdx.x == 64) PDLLM_DEC_TRACE(8 + 4 * it);
         const uint32_t tS = tmem_base + lane_base + kColS + slot * kTileN;
 #pragma unroll
         for (int b = 0; b < 2; ++b) {
@@ -321,9 +346,11 @@ attn_decode_sm100_kernel(const __grid_constant__ CUtensorMap q_map, const __grid
         tc_wait_st();
         tc_fence_before();
         mbar_arrive(&bars[kPFull + slot]);
+        if (threadIdx.x == 64) PDLLM_DEC_TRACE(9 + 4 * it);
       }
       // ---- this CTA's result: O (unnormalised, relative to m_ref), m_ref, l_run ----
       if (ok) ok = mbar_wait(&bars[kPvDone + ((n_iter - 1) & 1)], ((n_iter - 1) >> 1) & 1, abort_flag, a);
+      if (threadIdx.x == 64) PDLLM_DEC_TRACE(2);
       if (ok) {
         tc_fence_after();
         if (a.splits == 1) {
@@ -356,7 +383,8 @@ attn_decode_sm100_kernel(const __grid_constant__ CUtensorMap q_map, const __grid
             tc::tmem_ld32(tO + c * 32, o);
             tc_wait_ld();
 #pragma unroll
-            for (int j = 0; j < 32; ++j) part_o[(c * 32 + j) * kTileM + r] = __uint_as_float(o[j]);
+            for (int j = 0; j < 8; ++j)
+              *reinterpret_cast<uint4*>(part_o + (static_cast<int64_t>(c * 8 + j) * kTileM + r) * 4) = make_uint4(o[4 * j], o[4 * j + 1], o[4 * j + 2], o[4 * j + 3]);
           }
           ml[r] = m_ref;
           ml[kTileM + r] = l_run;
@@ -373,8 +401,11 @@ attn_decode_sm100_kernel(const __grid_constant__ CUtensorMap q_map, const __grid
 
   // ---- merge across the cluster: CTA of rank p finishes a slice of the head dimension for every row ----
   if (a.splits > 1) {
+    __threadfence();                    // this CTA's share is visible device-wide before it arrives
     __syncwarp();
+    if (threadIdx.x == 64) PDLLM_DEC_TRACE(3);
     gemm::cluster_sync_all();
+    if (threadIdx.x == 64) PDLLM_DEC_TRACE(4);
     if (warp >= kSoftmaxWarp0 && n_tok > 0) {
       const int r = (warp & 3) * 32 + lane;
       const int tok_local = r / G;
@@ -384,45 +415,81 @@ attn_decode_sm100_kernel(const __grid_constant__ CUtensorMap q_map, const __grid
         const int cols = (kHeadDim / 8 + S - 1) / S * 8;          // a multiple of 8 columns (16 bytes of output) per rank
         const int d0 = rank * cols, d1 = min(kHeadDim, d0 + cols);
         if (d0 < d1) {
-          float w[kMaxCluster];
+          const float* unit_shares = a.shares + static_cast<int64_t>(blockIdx.x - rank) * kShareFloats;   // share of rank 0 of this cluster
+          // all loads of a batch are issued before the first value is used
+          float w[kMaxCluster], lsum[kMaxCluster];
+#pragma unroll
+          for (int p = 0; p < kMaxCluster; ++p) {
+            const float* pml = unit_shares + p * kShareFloats + kTileM * kPartStride;
+            w[p] = p < S ? __ldcg(pml + r) : -INFINITY;
+            lsum[p] = p < S ? __ldcg(pml + kTileM + r) : 0.f;
+          }
           float M = -INFINITY;
-          for (int p = 0; p < S; ++p) { w[p] = gemm::ld_peer_shared_f32(ml + r, p); M = fmaxf(M, w[p]); }
+#pragma unroll
+          for (int p = 0; p < kMaxCluster; ++p) M = fmaxf(M, w[p]);
           float denom = 0.f;
-          for (int p = 0; p < S; ++p) {
-            const float lp = gemm::ld_peer_shared_f32(ml + kTileM + r, p);
+#pragma unroll
+          for (int p = 0; p < kMaxCluster; ++p) {
             w[p] = (w[p] == -INFINITY) ? 0.f : exp2f(w[p] - M);
-            denom += w[p] * lp;
+            denom += w[p] * lsum[p];
           }
           const float inv = denom > 0.f ? 1.f / denom : 0.f;
           const int head_local = r - tok_local * G;
           uint8_t* out_row = reinterpret_cast<uint8_t*>(a.out) +
                              ((static_cast<int64_t>(q_start + tok0 + tok_local)) * a.out_stride + static_cast<int64_t>(kvh * G + head_local) * kHeadDim) * 2;
+          // Every share's slice of this row is requested before the first value is used: one L2 round trip per batch of 8
+          // shares instead of one per share. kCols4 16-byte loads per share: 2 when a cluster of 16 leaves 8 columns per
+          // rank, 4 for clusters of 8 to 15, 8 below.
+          auto merge_cols = [&](auto kCols4Tag, int d0) {          // columns [d0, min(d1, d0 + 4 kCols4))
+            constexpr int kCols4 = decltype(kCols4Tag)::value;
+            float acc[4 * kCols4];
+#pragma unroll
+            for (int j = 0; j < 4 * kCols4; ++j) acc[j] = 0.f;
+            const float* first = unit_shares + (static_cast<int64_t>(d0 / 4) * kTileM + r) * 4;
+            constexpr int kBatch = kCols4 >= 8 ? 4 : 8;
 #pragma unroll 1
-          for (int d = d0; d < d1; d += 8) {
-            float acc[8];
+            for (int pb = 0; pb < S; pb += kBatch) {                // rank order: the result does not depend on timing
+              float4 v[kBatch][kCols4];
 #pragma unroll
-            for (int j = 0; j < 8; ++j) acc[j] = 0.f;
-            for (int p = 0; p < S; ++p) {               // rank order: the result does not depend on timing
-              if (w[p] == 0.f) continue;                // a neutral share has no O behind it
-              float v[8];
+              for (int q = 0; q < kBatch; ++q) {
+                const int p = pb + q;
+                const bool live = p < S && w[p] != 0.f;             // a neutral share has no O behind it
+                const float4* src = reinterpret_cast<const float4*>(first + p * kShareFloats);
 #pragma unroll
-              for (int j = 0; j < 8; ++j) v[j] = gemm::ld_peer_shared_f32(part_o + (d + j) * kTileM + r, p);
+                for (int c = 0; c < kCols4; ++c) v[q][c] = (live && d0 + 4 * c < d1) ? __ldcg(src + c * kTileM) : make_float4(0.f, 0.f, 0.f, 0.f);
+              }
 #pragma unroll
-              for (int j = 0; j < 8; ++j) acc[j] = fmaf(w[p], v[j], acc[j]);
+              for (int q = 0; q < kBatch; ++q) {
+                const float wp = (pb + q) < S ? w[pb + q] : 0.f;
+#pragma unroll
+                for (int c = 0; c < kCols4; ++c) {
+                  acc[4 * c] = fmaf(wp, v[q][c].x, acc[4 * c]); acc[4 * c + 1] = fmaf(wp, v[q][c].y, acc[4 * c + 1]);
+                  acc[4 * c + 2] = fmaf(wp, v[q][c].z, acc[4 * c + 2]); acc[4 * c + 3] = fmaf(wp, v[q][c].w, acc[4 * c + 3]);
+                }
+              }
             }
-            uint32_t pk[4];
 #pragma unroll
-            for (int j = 0; j < 8; j += 2) {
-              if (kBf16) { __nv_bfloat162 h = __floats2bfloat162_rn(acc[j] * inv, acc[j + 1] * inv); pk[j >> 1] = *reinterpret_cast<uint32_t*>(&h); }
-              else { __half2 h = __floats2half2_rn(acc[j] * inv, acc[j + 1] * inv); pk[j >> 1] = *reinterpret_cast<uint32_t*>(&h); }
+            for (int c = 0; c < kCols4; c += 2) {
+              if (d0 + 4 * c >= d1) break;
+              uint32_t pk[4];
+#pragma unroll
+              for (int j = 0; j < 8; j += 2) {
+                const float x0 = acc[4 * c + j] * inv, x1 = acc[4 * c + j + 1] * inv;
+                if (kBf16) { __nv_bfloat162 h = __floats2bfloat162_rn(x0, x1); pk[j >> 1] = *reinterpret_cast<uint32_t*>(&h); }
+                else { __half2 h = __floats2half2_rn(x0, x1); pk[j >> 1] = *reinterpret_cast<uint32_t*>(&h); }
+              }
+              *reinterpret_cast<uint4*>(out_row + (d0 + 4 * c) * 2) = make_uint4(pk[0], pk[1], pk[2], pk[3]);
             }
-            *reinterpret_cast<uint4*>(out_row + d * 2) = make_uint4(pk[0], pk[1], pk[2], pk[3]);
+          };
+          if (cols <= 8) merge_cols(std::integral_constant<int, 2>(), d0);
+          else if (cols <= 16) merge_cols(std::integral_constant<int, 4>(), d0);
+          else {
+            for (int dd = d0; dd < d1; dd += 32) merge_cols(std::integral_constant<int, 8>(), dd);   // clusters of 2 to 7
           }
         }
       }
     }
-    __syncwarp();
-    gemm::cluster_sync_all();       // no CTA leaves while a peer may still read its shared memory
+    if (threadIdx.x == 64) PDLLM_DEC_TRACE(5);
   }
 
   // ---- teardown ----
@@ -460,7 +527,14 @@ inline Plan make_plan(const pdllm_attn_params* p) {
   return pl;
 }
 
+// one share per CTA of the largest grid the plan may launch
+// (behind the header of arrival counters that the twin-tile kernel keeps zeroed at the start of the same workspace)
+inline int64_t workspace_bytes(const Plan& pl) { return tc::kCounterHeaderBytes + pl.units * pl.splits * kShareFloats * 4; }
+
 inline int launch(const pdllm_attn_params* p, const Plan& pl, cudaStream_t stream) {
+  if (p->workspace == nullptr || p->workspace_bytes < workspace_bytes(pl))
+    return fail(PDLLM_E_WORKSPACE, "attention (few rows) needs %lld workspace bytes, got %lld", static_cast<long long>(workspace_bytes(pl)),
+                static_cast<long long>(p->workspace_bytes));
   const bool bf16 = p->dtype == PDLLM_BF16;
   const bool has_cache = p->kv_layout == PDLLM_KV_UNIFIED && p->k_cache != nullptr && p->num_pages > 0;
   CUtensorMap q_map, kn_map, vn_map, kc_map, vc_map;
@@ -492,7 +566,8 @@ inline int launch(const pdllm_attn_params* p, const Plan& pl, cudaStream_t strea
   }
   Args a;
   a.out = p->out; a.block_table = p->block_table; a.cu_seqlens_q = p->cu_seqlens_q; a.seq_lens = p->seq_lens;
-  a.mask = p->mask; a.status = p->status; a.trace = nullptr;
+  a.mask = p->mask; a.status = p->status; a.trace = reinterpret_cast<long long*>(p->trace);
+  a.shares = reinterpret_cast<float*>(static_cast<char*>(p->workspace) + tc::kCounterHeaderBytes);
   a.out_stride = p->out_stride; a.block_table_stride = p->block_table_stride;
   a.mask_stride_m = p->mask_stride_m; a.mask_stride_n = p->mask_stride_n; a.num_pages = has_cache ? p->num_pages : 0;
   a.num_seqs = p->num_seqs; a.max_pages = p->max_pages; a.num_kv_heads = p->num_kv_heads;

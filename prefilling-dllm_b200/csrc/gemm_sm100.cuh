@@ -474,13 +474,19 @@ linear_sm100_kernel(const __grid_constant__ CUtensorMap a_map, const __grid_cons
       const float bias_r = (bias != nullptr && row_id < a.n) ? to_f32<T>(bias[row_id]) : 0.f;
 #pragma unroll 1
       for (int j0 = rank; j0 < n_cols; j0 += 4 * parts) {
+        // 4 columns x up to 8 ranks: every load is issued before the first value is used (a load from a peer's shared
+        // memory takes a few hundred cycles)
+        float v[8][4];
+#pragma unroll
+        for (int p = 0; p < 8; ++p) {
+#pragma unroll
+          for (int i = 0; i < 4; ++i) v[p][i] = (p < parts && j0 + i * parts < n_cols) ? ld_peer_shared_f32(red + (j0 + i * parts) * kRowsA + r, p) : 0.f;
+        }
         float sum[4] = {0.f, 0.f, 0.f, 0.f};
-        for (int p = 0; p < parts; ++p) {
-          float v[4];
 #pragma unroll
-          for (int i = 0; i < 4; ++i) v[i] = (j0 + i * parts < n_cols) ? ld_peer_shared_f32(red + (j0 + i * parts) * kRowsA + r, p) : 0.f;
+        for (int p = 0; p < 8; ++p) {          // rank order: the result does not depend on timing
 #pragma unroll
-          for (int i = 0; i < 4; ++i) sum[i] += v[i];
+          for (int i = 0; i < 4; ++i) sum[i] += v[p][i];
         }
 #pragma unroll
         for (int i = 0; i < 4; ++i) {

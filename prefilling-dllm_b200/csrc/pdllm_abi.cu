@@ -170,7 +170,13 @@ int64_t pdllm_attn_workspace_bytes(const pdllm_attn_params* p) {
   int impl = pdllm_attn_select_impl(p);
   if (impl < 0) return impl;
   if (impl != PDLLM_ATTN_TC) return 0;
-  if (dec::make_plan(p).use && !getenv("PDLLM_NO_DECODE_KERNEL")) return 0;   // the few-rows kernel merges its splits in shared memory
+  if (!getenv("PDLLM_NO_DECODE_KERNEL")) {
+    const dec::Plan dp = dec::make_plan(p);
+    if (dp.use) {     // enough for either form, should no cluster size fit on the device
+      const int64_t a = dec::workspace_bytes(dp), b = tc::workspace_bytes(p);
+      return a > b ? a : b;
+    }
+  }
   return tc::workspace_bytes(p);
 }
 
@@ -184,10 +190,7 @@ int pdllm_paged_attention(const pdllm_attn_params* p, void* stream) {
     const dec::Plan dp = dec::make_plan(p);
     if (dp.use && p->total_q > 0 && !getenv("PDLLM_NO_DECODE_KERNEL")) {
       const int rc = dec::launch(p, dp, as_stream(stream));
-      if (rc != PDLLM_E_UNSUPPORTED) return rc;
-      // no cluster size fits on this device: the twin-tile kernel needs its split-KV workspace
-      if (tc::workspace_bytes(p) > 0 && (p->workspace == nullptr || p->workspace_bytes < tc::workspace_bytes(p)))
-        return fail(PDLLM_E_WORKSPACE, "attention: %lld workspace bytes needed", static_cast<long long>(tc::workspace_bytes(p)));
+      if (rc != PDLLM_E_UNSUPPORTED) return rc;      // else: no cluster size fits on this device
     }
     return tc::launch(p, as_stream(stream));
   }

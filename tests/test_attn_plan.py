@@ -56,9 +56,9 @@ def test_forced_splits_are_honoured(lib):
 
 
 def test_few_units_go_to_the_cluster_kernel(lib, monkeypatch):
-    # one request, one block of 32 rows (two query tiles x 4 KV heads = 8 units): the few-rows kernel merges its KV splits
-    # inside thread-block clusters and needs no workspace ...
-    assert _partials(lib, 1, 28, 4, 32, 4161 + 32) == 0
+    # one request, one block of 32 rows (two query tiles x 4 KV heads = 8 units): the few-rows kernel cuts every unit into a
+    # cluster of up to 16 CTAs, each leaving one share (O, m, l of one query tile) in the workspace ...
+    assert _partials(lib, 1, 28, 4, 32, 4161 + 32) == 8 * 16
     # ... a forced split count keeps the shape on the twin-tile kernel, which merges through partials in the workspace
     assert _partials(lib, 1, 28, 4, 32, 4161 + 32, num_splits=12) == 1 * 4 * 2 * 12
     # ... and with the few-rows kernel switched off its cost model settles between 8 and 16 splits
