@@ -29,7 +29,7 @@ from typing import Dict, Iterable, List, Optional, Sequence, Tuple
 import torch
 
 from . import ops
-from .model import CachedPrefix, DreamArch, PageAllocator, PagedDreamModel, slots_for
+from .model import CachedPrefix, DreamArch, PageAllocator, PagedDreamModel, denoise_blocks, slots_for
 
 _OFF = {"none", "off", "0", ""}
 
@@ -104,6 +104,18 @@ class _EngineConfig:
     kvcache_block_size: int
     model_name: str = "dream"
     model_type: str = "diffusion_lm"
+
+
+class _TokenRun:
+    """A run of tokens laid over a page list: what the block loop needs to know about a cache."""
+
+    def __init__(self, page_ids: Sequence[int], length: int, page_size: int):
+        self.page_ids, self.length, self.page_size = list(page_ids), int(length), int(page_size)
+
+    def slots(self, start: int, n: int) -> List[int]:
+        if start + n > len(self.page_ids) * self.page_size:
+            raise RuntimeError("token run overflows its pages")
+        return slots_for(self.page_ids, start, n, self.page_size)
 
 
 class FastDLLMDreamEngine:
@@ -181,7 +193,7 @@ class FastDLLMDreamEngine:
     # ------------------------------------------------------------------------------------------------ forwards
     def _forward(self, ids, positions: Sequence[int], *, ctx_page_ids: Optional[Sequence[int]] = None, ctx_len: int = 0,
                  store_slots: Optional[Sequence[int]] = None, causal: bool = False, mask: Optional[torch.Tensor] = None,
-                 logit_rows: Optional[Sequence[int]] = None, want_logits: bool = True, capture_layers=None):
+                 logit_rows: Optional[Sequence[int]] = None, want_logits: bool = True, capture_layers=None, on_layer_stored=None):
         """One sequence of new rows at `positions`, seeing the first `ctx_len` tokens held by `ctx_page_ids`."""
         m = self.model
         ids_t = ids if isinstance(ids, torch.Tensor) else m.ids_tensor(ids)
@@ -195,7 +207,7 @@ class FastDLLMDreamEngine:
             return m.forward(ids_t, torch.tensor(list(positions), dtype=torch.long, device=m.device), cu_seqlens=m.i32([0, n]),
                              max_query_len=n, slot_mapping=None if store_slots is None else m.i32(list(store_slots)),
                              causal=causal, new_row_mask=mask, logit_rows=None if logit_rows is None else m.ids_tensor(logit_rows),
-                             want_logits=want_logits, capture_qk_layers=capture_layers, **kwargs)
+                             want_logits=want_logits, capture_qk_layers=capture_layers, on_layer_stored=on_layer_stored, **kwargs)
 
     def _selection_mask(self, mode: str, *, seq_len: int, prefix_len: int, chunk_len: int, query_len: int):
         """(causal flag, dense mask or None) for a selection forward (reference _selection_prefill_mask :930-953)."""
@@ -463,21 +475,25 @@ class FastDLLMDreamEngine:
                              prefill_delta_left: int = 7, prefill_delta_right: int = 0, prefill_delta_direction: str = "left",
                              prefill_delta_scale: float = 1.0, prefill_delta_debug: bool = False,
                              prefill_delta_selection_mode: str = "none", prefill_delta_selection_scale: float = 1.0,
-                             prefill_selection_dense_outputs: Optional[dict] = None) -> DreamPrefillRecord:
-        """Prefill `[prompt ‖ MASK x block_length]` bidirectionally into pages and return the decode-ready boundary state
-        (reference :1879-2108). With keep indices the prompt KV is compacted per layer and KV head after the prefill
+                             prefill_selection_dense_outputs: Optional[dict] = None, kv_stream=None) -> DreamPrefillRecord:
+        """Prefill `[prompt ‖ MASK x block_length]` (or `MASK x max_new_tokens` for several blocks) bidirectionally into pages
+        and return the decode-ready boundary state (reference :1879-2108). With keep indices the prompt KV is compacted per layer and KV head after the prefill
         ("compacted_posthoc_eviction"); without them the whole prompt is registered in the prefix cache and reused by
-        the next request with the same prompt ids."""
+        the next request with the same prompt ids.
+        `kv_stream` (not in the reference): a `pd_wire.KVStreamWriter`; the prompt KV is then sent layer group by layer group
+        WHILE the prefill runs (full-dense records only)."""
         if max_new_tokens <= 0:
             raise ValueError("prefill_to_pd_record requires max_new_tokens > 0")
-        if max_new_tokens > self.block_length:
-            raise NotImplementedError("The first FastDLLMDreamEngine version supports one generation block only. "
-                                      f"Got max_new_tokens={max_new_tokens}, block_length={self.block_length}.")
+        if kv_stream is not None and prompt_keep_indices_per_layer_per_head is not None:
+            raise ValueError("kv_stream carries full_dense records only: per-head eviction rewrites the pages after the prefill")
         prompt_ids = [int(x) for x in prompt_ids]
         prompt_positions = list(range(len(prompt_ids))) if prompt_positions is None else [int(x) for x in prompt_positions]
         if len(prompt_ids) != len(prompt_positions):
             raise ValueError(f"prompt_ids/prompt_positions length mismatch: {len(prompt_ids)} vs {len(prompt_positions)}")
-        decode_len = self.block_length
+        # One block: the reference's record, MASK slots padded to the block length. More than one block (the reference stops
+        # here with NotImplementedError, fastdllm_engine.py:1911-1915): the record carries max_new_tokens MASK slots, all of
+        # them in the joint prefill, as the eval class's full_prompt_mask flow does (fastdllm_parallelcomp.py:2896-2912).
+        decode_len = self.block_length if max_new_tokens <= self.block_length else int(max_new_tokens)
         has_keep = prompt_keep_indices_per_layer_per_head is not None
         self._reject_unbuilt_modes(prefill_sparse_mode=prefill_sparse_mode, prefill_delta_mode=prefill_delta_mode,
                                    prefill_delta_selection_mode=prefill_delta_selection_mode,
@@ -511,12 +527,21 @@ class FastDLLMDreamEngine:
         n_prompt_pages = math.ceil(full_prompt_len / self.page_size)
         n_block_pages = math.ceil(decode_len / self.page_size)
         use_prefix_cache = keep is None
-        cached = self._prefix_cache.lookup_prefix(prompt_ids) if use_prefix_cache else None
+        # the prompt KV of a joint prefill depends on how many MASK slots it saw: records of several blocks get entries of
+        # their own in the prefix cache
+        cache_key = prompt_ids if decode_len == self.block_length else prompt_ids + [-decode_len]
+        cached = self._prefix_cache.lookup_prefix(cache_key) if use_prefix_cache else None
         owns_prompt_pages = False
+        stream_header = dict(prompt_ids=prompt_ids, prompt_positions=prompt_positions, suffix_positions=suffix_positions,
+                             full_prompt_len=full_prompt_len, decode_len=decode_len, kv_mode=kv_mode) if kv_stream is not None else None
         if cached is not None:
             prompt_page_ids = cached.page_ids
             cached.ref_count += 1
             last_context_logit = cached.last_context_logit
+            if kv_stream is not None:        # nothing is computed on a prefix-cache hit: the pages are final already
+                kv_stream.begin(prompt_page_ids=prompt_page_ids, prompt_len=prompt_len, header=stream_header)
+                for layer in range(self.model.arch.num_hidden_layers):
+                    kv_stream.on_layer_stored(layer)
             try:
                 self._prefix_cache.ensure_free(n_block_pages)
                 block_page_ids = self._prefix_cache.allocate_pages(n_block_pages)
@@ -546,8 +571,10 @@ class FastDLLMDreamEngine:
                 # replace forward of a prefix-cache hit would give for that slot. (The reference engine has no un-shifted
                 # model; this follows its eval class, fastdllm_parallelcomp.py:1017-1024, 2385-2397.)
                 first_row = full_prompt_len - 1 if self.model.arch.logit_shift else full_prompt_len
+                if kv_stream is not None:
+                    kv_stream.begin(prompt_page_ids=prompt_page_ids, prompt_len=prompt_len, header=stream_header)
                 logits, _ = self._forward(full_ids, list(prompt_positions) + prefill_suffix_positions, store_slots=slots,
-                                          logit_rows=[first_row])
+                                          logit_rows=[first_row], on_layer_stored=None if kv_stream is None else kv_stream.on_layer_stored)
                 last_context_logit = logits[0].detach()
                 first_token = int(torch.argmax(last_context_logit).item())
                 if keep is not None:
@@ -562,12 +589,15 @@ class FastDLLMDreamEngine:
                 self._prefix_cache.release_pages(prompt_page_ids)
                 raise
             if use_prefix_cache:
-                self._prefix_cache.register_prefix(prompt_ids, prompt_page_ids, prompt_len, last_context_logit)
-        return DreamPrefillRecord(
+                self._prefix_cache.register_prefix(cache_key, prompt_page_ids, prompt_len, last_context_logit)
+        record = DreamPrefillRecord(
             prompt_ids=prompt_ids, prompt_positions=prompt_positions, suffix_positions=suffix_positions, prompt_len=prompt_len,
             full_prompt_len=full_prompt_len, decode_len=decode_len, prompt_page_ids=prompt_page_ids, block_page_ids=block_page_ids,
             first_token_id=first_token, last_context_logit=last_context_logit, decode_delta_state=None,
             owns_prompt_pages=owns_prompt_pages, cached_prefix=cached, kv_mode=kv_mode)
+        if kv_stream is not None:
+            kv_stream.finish(record)
+        return record
 
     # ------------------------------------------------------------------------------------------------ decode half
     def _denoise_block(self, *, ctx_page_ids: Sequence[int], ctx_len: int, block_slots: Sequence[int], block_positions: Sequence[int],
@@ -618,6 +648,8 @@ class FastDLLMDreamEngine:
             return FastDLLMEngineOutput(text="", token_ids=[], n_diff_steps=0)
         if max_new_tokens > record.decode_len:
             raise ValueError(f"max_new_tokens={max_new_tokens} exceeds record decode_len={record.decode_len}.")
+        if record.decode_len > self.block_length:
+            return self._decode_blocks(record, max_new_tokens, stop_token_ids)
         try:
             block, n_steps = self._denoise_block(
                 ctx_page_ids=record.prompt_page_ids, ctx_len=record.prompt_len,
@@ -627,6 +659,51 @@ class FastDLLMDreamEngine:
             ops.check_status(self.device)
             return self._finish(block, max_new_tokens, stop_token_ids, n_steps)
         finally:
+            self.release_pd_record(record)
+
+    def _decode_blocks(self, record: DreamPrefillRecord, max_new_tokens: int, stop_token_ids) -> FastDLLMEngineOutput:
+        """Several generation blocks on a record (beyond the reference engine, whose first version stops at one block:
+        fastdllm_engine.py:1911-1915, 2286-2290). The block loop is the eval class's dual cache (fastdllm_parallelcomp.py
+        :2932-2998) with the engine's fp32 softmax: every block starts by forwarding all remaining MASK slots against
+        [prompt ‖ finished blocks], the active block's rows replace their slots at every step and see the later MASK slots,
+        a commit forward stores the finished block. Only the prompt KV crosses the prefill/decode boundary: the MASK slots
+        are recomputed here, so a record that came from a snapshot or from another engine decodes the same way.
+        The loop needs [prompt ‖ suffix] as ONE run of tokens over a page list. The suffix continues in the prompt's last
+        page when the record owns its prompt pages; when they belong to the shared prefix cache (other requests read them, and
+        may append their own suffix) the partially filled last page is first copied into a private one."""
+        page = self.page_size
+        n_full, rem = divmod(int(record.prompt_len), page)
+        extra: List[int] = []
+        try:
+            if rem == 0:
+                pages = list(record.prompt_page_ids[:n_full]) + list(record.block_page_ids)
+            elif record.owns_prompt_pages:
+                pages = list(record.prompt_page_ids[:n_full + 1]) + list(record.block_page_ids)
+            else:
+                private = list(record.block_page_ids)
+                need = math.ceil((rem + record.decode_len) / page)
+                if need > len(private):
+                    self._prefix_cache.ensure_free(need - len(private))
+                    extra = self._prefix_cache.allocate_pages(need - len(private))
+                    private += extra
+                planes = 2 * int(self.model.kv_cache.shape[1])
+                ops.copy_pages(self._layer_pools(), self._all_layer_page_ids([record.prompt_page_ids[n_full]]), self._layer_pools(),
+                               self._all_layer_page_ids([private[0]]), n_lists=planes, tokens_per_list=rem)
+                pages = list(record.prompt_page_ids[:n_full]) + private
+            if len(pages) * page < record.prompt_len + record.decode_len:
+                raise RuntimeError("record holds too few pages for its prompt and MASK slots")
+            view = _TokenRun(pages, int(record.prompt_len), page)
+            steps: List[int] = []
+            generated = denoise_blocks(self.model, view, suffix_pos_start=int(record.suffix_positions[0]), last_logit=record.last_context_logit,
+                                       first_token=None, tail_in_cache=0, max_new=int(max_new_tokens), block_length=self.block_length,
+                                       mask_id=self.mask_token_id, threshold=self.threshold, softmax_dtype=torch.float32,
+                                       use_graph=not self.config.enforce_eager, steps_out=steps)
+            ops.check_status(self.device)
+            block = torch.tensor(generated, dtype=torch.long)
+            return self._finish(block, max_new_tokens, stop_token_ids, sum(steps))
+        finally:
+            if extra:
+                self._prefix_cache.release_pages(extra)
             self.release_pd_record(record)
 
     @_on_device
@@ -647,6 +724,8 @@ class FastDLLMDreamEngine:
             for r in records:
                 if r.decode_len != decode_len:
                     raise ValueError("records of one batch must share decode_len")
+                if r.decode_len > self.block_length:
+                    raise NotImplementedError("shared denoise steps serve one-block records; decode records with several blocks one by one")
                 if max_new_tokens > r.decode_len:
                     raise ValueError(f"max_new_tokens={max_new_tokens} exceeds record decode_len={r.decode_len}.")
             requests = [dict(positions=r.suffix_positions, ctx_page_ids=r.prompt_page_ids, ctx_len=r.prompt_len,

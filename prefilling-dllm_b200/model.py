@@ -291,7 +291,7 @@ class PagedDreamModel:
                 seq_lens: Optional[torch.Tensor] = None, max_seq_len: int = 0, causal: bool = False,
                 logit_rows: Optional[torch.Tensor] = None, want_logits: bool = True,
                 capture_qk_layers: Optional[Sequence[int]] = None, store_after_attention: bool = False,
-                store_unrotated_k: bool = False, new_row_mask: Optional[torch.Tensor] = None):
+                store_unrotated_k: bool = False, new_row_mask: Optional[torch.Tensor] = None, on_layer_stored=None):
         """Packed forward of `ids` [T] (several sequences delimited by cu_seqlens) at RoPE `positions` [T].
 
         slot_mapping [T] int32 (optional): where each row's K/V goes in the pool (-1 = do not store).
@@ -306,6 +306,8 @@ class PagedDreamModel:
         causal: scoring mask (row sees itself and earlier rows); otherwise rows see each other bidirectionally.
         logit_rows: indices of the rows whose logits are wanted (LM head runs on those rows only).
         capture_qk_layers: layers whose rotated (q, k) are returned for the eviction scorer.
+        on_layer_stored: callable(layer index), invoked right after a layer's K/V rows were written to pages (their final
+        values in a forward that stores before attention): lets a transfer of layer l overlap the compute of layer l + 1.
         Returns (logits or None, {layer: (q, k)}).
         """
         a = self.arch
@@ -342,6 +344,8 @@ class PagedDreamModel:
                                     sm_scale=self.scale, causal=causal, bidirectional=True, mask=new_row_mask)
             if slot_mapping is not None and store_after_attention:
                 ops.store_kvcache_unified_layout(k, v, k_cache, v_cache, slot_mapping, "diffusion_lm")
+            if on_layer_stored is not None and slot_mapping is not None:
+                on_layer_stored(li)
             proj = self._linear(attn_out.view(total, hq * d), w["wo"])
             h = ops.add_rmsnorm(x, w["ln2"], eps, proj)                  # x += attention output; h = norm(x)
             if self.tensor_core_linear:
@@ -391,6 +395,103 @@ class PagedDreamModel:
     def i32(self, values: Sequence[int]) -> torch.Tensor:
         return torch.tensor(list(values), dtype=torch.int32, device=self.device)
 
+
+
+def denoise_blocks(model: "PagedDreamModel", cache, *, suffix_pos_start: int, last_logit: torch.Tensor, first_token, tail_in_cache: int,
+                   max_new: int, block_length: int, mask_id: int, threshold: float, softmax_dtype: Optional[torch.dtype], use_graph: bool,
+                   fixed_steps_per_block: Optional[int] = None, fill_most_confident=None, steps_out: Optional[List[int]] = None) -> List[int]:
+    """Fast-dLLM dual-cache block loop over a paged cache (reference eval class prefilling_dllm_eval/fastdllm_parallelcomp.py
+    :2932-2998, :2399-2441), shared by the eval-class runtime and the engine's multi-block decode.
+
+    `cache`: a handle with `page_ids`, `length` (valid tokens: prompt, finished blocks and `tail_in_cache` later-block MASK
+    slots; updated here) and `slots(start, n)`. Layout while block b is active: [prompt ‖ finished blocks ‖ MASK slots of the
+    later blocks]; the active block's rows are the new rows of every forward, so they replace their own slots by
+    construction. After the block is committed its K/V take the place of the first later-MASK slots and the later slots are
+    recomputed by the next block's suffix initialisation (reference :2368-2397).
+    `first_token`: the first token of block 0 when the prefill already produced it together with the later-MASK slots
+    (full_prompt_mask mode); None = every block starts with a suffix initialisation.
+    `softmax_dtype`: None = probabilities in the model dtype (eval class), torch.float32 = the engine's rule.
+    `fixed_steps_per_block`: None = confidence-threshold denoising; an int = the fixed-step diffusion sampler (reference
+    _denoise_block_diffusion :2443-2510): step i of n transfers int(masks * (1 - t[i+1] / t[i])) of the most confident slots
+    through `fill_most_confident(logits, block, last_logit, count)`, t = linspace(1, 1e-3, n + 1), the last step all that is left.
+    `steps_out`: when given, the number of denoise forwards of every block is appended."""
+    import math
+
+    arch = model.arch
+    dev = model.device
+
+    def forward(ids_t, positions, ctx_len, *, store_slots=None, logit_rows=None, want_logits=True, store_after_attention=False):
+        n = int(ids_t.numel())
+        kwargs = {}
+        if ctx_len > 0:
+            kwargs = dict(block_table=model.i32(cache.page_ids).view(1, -1), seq_lens=model.i32([ctx_len + n]), max_seq_len=ctx_len + n)
+        return model.forward(ids_t, torch.tensor(list(positions), dtype=torch.long, device=dev), cu_seqlens=model.i32([0, n]), max_query_len=n,
+                             slot_mapping=None if store_slots is None else model.i32(store_slots), causal=False,
+                             logit_rows=None if logit_rows is None else model.ids_tensor(logit_rows), want_logits=want_logits,
+                             store_after_attention=store_after_attention, **kwargs)
+
+    n0 = cache.length - tail_in_cache          # prompt (+ query) tokens
+    num_blocks = max(1, math.ceil(max_new / block_length))
+    generated: List[int] = []
+    tail_len = tail_in_cache
+    for b in range(num_blocks):
+        start = b * block_length
+        blen = min(block_length, max_new - start)
+        if blen <= 0:
+            break
+        done = n0 + start                       # prompt + finished blocks
+        block_pos = list(range(suffix_pos_start + start, suffix_pos_start + start + blen))
+        later = max_new - start - blen          # MASK slots of the blocks after this one
+        if first_token is None or b > 0:
+            # suffix initialisation: forward all remaining MASKs against prompt + finished blocks; the later blocks' K/V go
+            # behind the finished ones, the active block's rows are not stored
+            if later > 0:
+                suffix_pos = list(range(suffix_pos_start + start, suffix_pos_start + start + blen + later))
+                slots = [-1] * blen + cache.slots(done, later)
+                forward(torch.full((blen + later,), mask_id, dtype=torch.long, device=dev), suffix_pos, done, store_slots=slots, want_logits=False)
+            tail_len = later
+            if not arch.logit_shift:
+                raise NotImplementedError("un-shifted (LLaDA) block initialisation is not built")
+            first = torch.argmax(last_logit)    # softmax is monotone: the arg-max of the logit
+        else:
+            first = first_token
+        ctx = done + tail_len
+        runner = model.block_step_runner(block_len=blen, positions=block_pos, ctx_page_ids=cache.page_ids, ctx_len=ctx, mask_token_id=mask_id,
+                                         threshold=float(threshold), last_logit=last_logit, shift=arch.logit_shift, softmax_dtype=softmax_dtype,
+                                         use_graph=bool(use_graph))
+        block = runner.block                      # the step's ids buffer, updated in place by the unmask kernel
+        block.fill_(mask_id)
+        block[0] = first
+        guard = 0
+        remaining = blen - 1
+        if fixed_steps_per_block is not None:
+            steps = int(fixed_steps_per_block)
+            timesteps = torch.linspace(1, 1e-3, steps + 1)       # fp32 on the host, the reference's own arithmetic
+            for step in range(steps):
+                if remaining <= 0:
+                    break
+                count = int(remaining * (1 - timesteps[step + 1] / timesteps[step])) if step < steps - 1 else remaining
+                if count <= 0:
+                    continue
+                logits, _ = forward(block, block_pos, ctx)
+                remaining -= fill_most_confident(logits, block, last_logit, count)
+                guard += 1
+            remaining = 0
+        while remaining > 0:
+            guard += 1
+            if guard > blen + 8:
+                break
+            remaining = runner.run()   # forward + unmask kernel (a CUDA graph replay from the third step on); one host read
+        if steps_out is not None:
+            steps_out.append(guard)
+        generated.extend(block.tolist())
+        # commit forward: the finished block's K/V take the first slots behind prompt + finished; its last logit is the next
+        # block's "last context logit". The store comes after attention so the later-MASK slots are still seen.
+        logits, _ = forward(block, block_pos, ctx, store_slots=cache.slots(done, blen), logit_rows=[blen - 1], store_after_attention=True)
+        last_logit = logits[0]
+        cache.length = done + blen
+        tail_len = 0
+    return generated[:max_new]
 
 
 class _StepGraph:

@@ -27,7 +27,7 @@ from typing import Dict, List, Optional, Sequence, Tuple
 import torch
 
 from . import ops
-from .model import DreamArch, PagedDreamModel, slots_for
+from .model import DreamArch, PagedDreamModel, denoise_blocks, slots_for
 
 
 @dataclass
@@ -678,79 +678,14 @@ class FastDLLMParallelComp:
     def _denoise_blocks(self, cache: PagedCache, *, suffix_pos_start: int, last_logit: torch.Tensor,
                         first_token: Optional[torch.Tensor], tail_in_cache: int, max_new: int,
                         fixed_steps_per_block: Optional[int] = None) -> List[int]:
-        """Fast-dLLM dual-cache block loop over the paged cache (reference :2932-2998, :2399-2441).
-
-        Cache layout while block b is active: [prompt ‖ finished blocks ‖ MASK slots of the later blocks]; the active
-        block's rows are the new rows of every forward, so they replace their own slots by construction. After the block
-        is committed its K/V take the place of the first later-MASK slots and the later slots are recomputed.
-        `tail_in_cache`: later-block MASK slots already stored behind the prompt by the prefill (full_prompt_mask mode).
-        `fixed_steps_per_block`: None = confidence-threshold denoising; an int = the fixed-step diffusion sampler
-        (reference _denoise_block_diffusion :2443-2510): step i of n transfers int(masks * (1 - t[i+1] / t[i])) of the most
-        confident slots, t = linspace(1, 1e-3, n + 1), the last step all that is left.
-        """
-        mask_id = self._mask_token_id()
-        n0 = cache.length - tail_in_cache          # prompt (+ query) tokens
-        num_blocks = max(1, math.ceil(max_new / self.block_length))
-        generated: List[int] = []
-        tail_len = tail_in_cache
-        for b in range(num_blocks):
-            start = b * self.block_length
-            blen = min(self.block_length, max_new - start)
-            if blen <= 0:
-                break
-            if self.config.generation_position_mode != "after_query":
-                raise ValueError(f"Unsupported generation_position_mode: {self.config.generation_position_mode}")
-            done = n0 + start                       # prompt + finished blocks
-            block_pos = self._range_positions(suffix_pos_start + start, blen)
-            later = max_new - start - blen          # MASK slots of the blocks after this one
-            if first_token is None or b > 0:
-                # suffix initialisation (reference :2368-2397): forward all remaining MASKs against prompt+finished; the
-                # later blocks' K/V go behind the finished ones, the active block's rows are not stored
-                if later > 0:
-                    suffix_pos = self._range_positions(suffix_pos_start + start, blen + later)
-                    slots = [-1] * blen + cache.slots(done, later)
-                    self._forward_packed([[mask_id] * (blen + later)], [suffix_pos], causal=False, cache=cache, ctx_len=done,
-                                         store_slots=slots, want_logits=False)
-                tail_len = later
-                first = self._first_block_token(last_logit)
-            else:
-                first = first_token
-            ctx = done + tail_len
-            runner = self.model.block_step_runner(block_len=blen, positions=block_pos, ctx_page_ids=cache.page_ids, ctx_len=ctx,
-                                                  mask_token_id=mask_id, threshold=float(self.config.threshold), last_logit=last_logit,
-                                                  shift=self.arch.logit_shift, softmax_dtype=None,
-                                                  use_graph=bool(self.config.decode_cuda_graph))
-            block = runner.block                      # the step's ids buffer, updated in place by the unmask kernel
-            block.fill_(mask_id)
-            block[0] = first
-            guard = 0
-            remaining = blen - 1
-            if fixed_steps_per_block is not None:
-                steps = int(fixed_steps_per_block)
-                timesteps = torch.linspace(1, 1e-3, steps + 1)       # fp32 on the host, the reference's own arithmetic
-                for step in range(steps):
-                    if remaining <= 0:
-                        break
-                    count = int(remaining * (1 - timesteps[step + 1] / timesteps[step])) if step < steps - 1 else remaining
-                    if count <= 0:
-                        continue
-                    logits, _ = self._forward_packed([[0] * blen], [block_pos], causal=False, cache=cache, ctx_len=ctx, ids_tensor=block)
-                    remaining -= self._fill_most_confident(logits, block, last_logit, count)
-                remaining = 0
-            while remaining > 0:
-                guard += 1
-                if guard > blen + 8:
-                    break
-                remaining = runner.run()   # forward + unmask kernel (a CUDA graph replay from the third step on); one host read
-            generated.extend(block.tolist())
-            # commit forward: the finished block's K/V take the first slots behind prompt+finished; its last logit is the
-            # next block's "last context logit". The store comes after attention so the later-MASK slots are still seen.
-            logits, _ = self._forward_packed([[0] * blen], [block_pos], causal=False, cache=cache, ctx_len=ctx, ids_tensor=block,
-                                             store_slots=cache.slots(done, blen), logit_rows=[blen - 1], store_after_attention=True)
-            last_logit = logits[0]
-            cache.length = done + blen
-            tail_len = 0
-        return generated[:max_new]
+        """Fast-dLLM dual-cache block loop over the paged cache (reference :2932-2998, :2399-2441): `model.denoise_blocks`
+        with this runtime's settings — softmax in the model dtype, as the eval class computes it."""
+        if self.config.generation_position_mode != "after_query":
+            raise ValueError(f"Unsupported generation_position_mode: {self.config.generation_position_mode}")
+        return denoise_blocks(self.model, cache, suffix_pos_start=suffix_pos_start, last_logit=last_logit, first_token=first_token,
+                              tail_in_cache=tail_in_cache, max_new=max_new, block_length=self.block_length, mask_id=self._mask_token_id(),
+                              threshold=float(self.config.threshold), softmax_dtype=None, use_graph=bool(self.config.decode_cuda_graph),
+                              fixed_steps_per_block=fixed_steps_per_block, fill_most_confident=self._fill_most_confident)
 
     # ------------------------------------------------------------------------------------------------ chunk-local caches
     def _prefill_one_chunk(self, cache: "PagedCache", dst: int, prefix_ids, chunk, order: int, ci: int, evict_q, window_q):

@@ -192,8 +192,10 @@ def test_rejections(engine):
     prompt = _prompt(64)
     with pytest.raises(ValueError):
         engine.prefill_to_pd_record(prompt, max_new_tokens=0)
-    with pytest.raises(NotImplementedError, match="one generation block"):
-        engine.prefill_to_pd_record(prompt, max_new_tokens=BLOCK + 1)
+    with pytest.raises(NotImplementedError, match="one generation block"):       # the chunk-local path keeps the reference's limit
+        engine.generate_token_ids_from_chunk_local_kv(prefix_ids=[BOS], prefix_positions=[0], chunk_ids_list=[], chunk_positions_list=[],
+                                                      chunk_keep_indices_per_layer_per_head=[], query_ids=prompt, query_positions=list(range(1, 65)),
+                                                      local_query_ids=prompt[-8:], max_new_tokens=BLOCK + 1)
     with pytest.raises(ValueError, match="Unsupported prefill_sparse_mode"):
         engine.prefill_to_pd_record(prompt, max_new_tokens=8, prefill_sparse_mode="banded")
     with pytest.raises(ValueError, match="requires prompt_keep_indices"):
@@ -273,6 +275,101 @@ def test_chunk_local_kv_generate(engine, cpu_model):
     assert engine._prefix_cache.num_free_pages == free0
     with pytest.raises(ValueError, match="keep-indices list length mismatch"):
         engine.generate_token_ids_from_chunk_local_kv(chunk_keep_indices_per_layer_per_head=nested[:1], max_new_tokens=BLOCK, **kw)
+
+
+def test_two_blocks_on_the_engine_reproduce_the_reference_eval_golden(engine, ckpt):
+    """max_new_tokens = 2 x block_length on the PD engine (the reference engine stops at one block; the block loop follows its
+    eval class). The eval class's golden run `two_blocks` is exactly this flow on [BOS ‖ selected chunks ‖ query] — a joint
+    prefill with all 64 MASK slots, then the dual-cache loop — and in float32 the engine's fp32 softmax is the eval class's:
+    the ids must come out the same. Checked through the explicit boundary, through a KV snapshot loaded into a second
+    engine, and on a prefix-cache hit (where the partially filled last prompt page is copied before the suffix is appended)."""
+    import json
+    import os
+
+    import make_golden
+    from oracle import hotpath as O
+
+    with open(os.path.join(os.path.dirname(os.path.abspath(__file__)), "golden", "toy_reference.json")) as handle:
+        ref = json.load(handle)["runs"]["two_blocks"]
+    context, query = make_golden.toy_inputs()
+    size = ref["flags"]["chunk_size"]
+    chunks = [O.maybe_prepend_bos_to_chunk(c, [BOS], size) for c in O.split_token_chunks(context, size)]
+    prompt = [BOS] + [t for ci in ref["selected_chunk_indices"] for t in chunks[ci]] + query
+    while engine._prefix_cache.evict_one():
+        pass
+    free0 = engine._prefix_cache.num_free_pages
+    rec = engine.prefill_to_pd_record(prompt, max_new_tokens=64)
+    assert rec.decode_len == 64 and rec.prompt_len == len(prompt) and rec.suffix_positions == list(range(len(prompt), len(prompt) + 64))
+    snap = engine.snapshot_pd_record_kv(rec)
+    out = engine.decode_from_pd_record(rec, max_new_tokens=64)
+    match = sum(int(a == b) for a, b in zip(out.token_ids, ref["sequences"])) / 64
+    print(f"engine, two blocks: greedy token match with the reference eval class {match:.3f}, {out.n_diff_steps} denoise forwards")
+    assert len(out.token_ids) == 64 and match >= 0.99
+    # a second engine gets only the prompt KV (snapshot) and recomputes the MASK slots itself
+    other = _engine(ckpt, pages=16)
+    moved = other.make_pd_record_from_kv_snapshot(rec, snap)
+    assert other.decode_from_pd_record(moved, max_new_tokens=64).token_ids == out.token_ids
+    assert other._prefix_cache.num_free_pages == 16
+    # prefix-cache hit: the shared prompt pages end mid-page, the suffix goes behind a private copy of that page
+    again = engine.prefill_to_pd_record(prompt, max_new_tokens=64)
+    assert again.cached_prefix is not None and not again.owns_prompt_pages and len(prompt) % 256 != 0
+    assert engine.decode_from_pd_record(again, max_new_tokens=64).token_ids == out.token_ids
+    one_block = engine.prefill_to_pd_record(prompt, max_new_tokens=BLOCK)       # another entry: the prompt KV saw 32 MASK slots
+    assert one_block.cached_prefix is None
+    engine.release_pd_record(one_block)
+    from prefilling_dllm_b200 import ops
+
+    ops.check_status(engine.device)
+    while engine._prefix_cache.evict_one():
+        pass
+    assert engine._prefix_cache.num_free_pages == free0
+
+
+@pytest.mark.parametrize("layers_per_message", [1, 4])
+def test_kv_streamed_during_the_prefill(engine, ckpt, layers_per_message):
+    """The prompt KV leaves the prefill engine as wire messages while the prefill runs (a group of layers per message,
+    gathered on a side stream after that group's page writes) and lands in a second engine's pages group by group: same KV
+    bits and same ids as decoding where the prefill ran; a prefix-cache hit streams the cached pages; a serialised
+    whole snapshot carries the same payload."""
+    from prefilling_dllm_b200 import ops, pd_wire
+
+    other = _engine(ckpt, pages=16)
+    prompt = _prompt(700, seed=41)
+    while engine._prefix_cache.evict_one():
+        pass
+    for attempt in ("computed", "prefix-cache hit"):
+        messages = []
+        writer = pd_wire.KVStreamWriter(engine, messages.append, layers_per_message=layers_per_message)
+        rec = engine.prefill_to_pd_record(prompt, max_new_tokens=BLOCK, kv_stream=writer)
+        assert (rec.cached_prefix is not None) == (attempt == "prefix-cache hit")
+        kinds = [pd_wire.unpack_message(m)[0] for m in messages]
+        n_groups = -(-2 // layers_per_message)
+        assert kinds == [pd_wire.TYPE_HEADER] + [pd_wire.TYPE_LAYERS] * n_groups + [pd_wire.TYPE_TRAILER], attempt
+        assert writer.bytes_sent == sum(len(m) for m in messages) > 2 * 2 * 700 * 2 * 64 * 4
+        reader = pd_wire.KVStreamReader(other)
+        for m in messages:
+            reader.feed(m)
+        moved = reader.record
+        assert moved is not None and moved.owns_prompt_pages and moved.prompt_len == 700 and moved.first_token_id == rec.first_token_id
+        a, b = engine.snapshot_pd_record_kv(rec), other.snapshot_pd_record_kv(moved)
+        for layer in range(2):
+            assert torch.equal(a.k_by_layer[layer], b.k_by_layer[layer]) and torch.equal(a.v_by_layer[layer], b.v_by_layer[layer]), attempt
+        assert torch.equal(moved.last_context_logit.cpu(), rec.last_context_logit.cpu())
+        whole = pd_wire.snapshot_from_bytes(pd_wire.snapshot_to_bytes(a))
+        assert torch.equal(whole.k_by_layer[1], b.k_by_layer[1]) and whole.prompt_len == 700
+        ids = engine.decode_from_pd_record(rec, max_new_tokens=BLOCK).token_ids
+        assert other.decode_from_pd_record(moved, max_new_tokens=BLOCK).token_ids == ids
+        assert other._prefix_cache.num_free_pages == 16
+    # a stream that skips a group is refused and the pages it held are returned
+    reader = pd_wire.KVStreamReader(other)
+    reader.feed(messages[0])
+    with pytest.raises(ValueError, match="PD KV stream"):
+        reader.feed(messages[-1] if layers_per_message == 4 and False else pd_wire.pack_message(pd_wire.TYPE_LAYERS, dict(first_layer=1, count=1), b""))
+    assert other._prefix_cache.num_free_pages == 16
+    ops.check_status(engine.device)
+    ops.check_status(other.device)
+    while engine._prefix_cache.evict_one():
+        pass
 
 
 @pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs two GPUs")
