@@ -334,6 +334,39 @@ def op_mha_decode(n_req: int, steps: int, rank: int, device: torch.device):
                          "traffic": 2_208_000_000 if n_req == 16 else None, "peak_source": peaks["source"], "bytes_per_launch": nbytes}}
 
 
+def op_decode_rows(device: torch.device, steps: int):
+    """The attention launch of ONE request's denoise step: 32 block rows x 28 / 4 heads over 4161 cached tokens in 17 pages (random
+    physical order) plus the block itself. HBM-bound in principle (8.8 MB of K/V, 1.3 us at the copy peak); in practice bound by
+    the length of one CTA's dependent chain and the merge of the KV splits. Page sets rotate over a 335 MB pool (> L2)."""
+    from prefilling_dllm_b200 import ops
+
+    rows, ctx, pages_per, pool_pages = 32, 4161, 17, 640
+    g = torch.Generator(device=device).manual_seed(5000)
+    k_cache = torch.randn(pool_pages, PAGE, HKV, D, device=device, dtype=torch.bfloat16, generator=g)
+    v_cache = torch.randn(pool_pages, PAGE, HKV, D, device=device, dtype=torch.bfloat16, generator=g)
+    tables = torch.randperm(pool_pages, device=device, generator=g)[: 32 * pages_per].to(torch.int32).view(32, 1, pages_per)
+    qkv = torch.randn(rows, HQ + 2 * HKV, D, device=device, dtype=torch.bfloat16, generator=g)
+    out = torch.empty(rows, HQ, D, device=device, dtype=torch.bfloat16)
+    cu = torch.tensor([0, rows], dtype=torch.int32, device=device)
+    seq_lens = torch.tensor([ctx + rows], dtype=torch.int32, device=device)
+
+    def step(i):
+        ops.paged_attention(qkv[:, :HQ], qkv[:, HQ:HQ + HKV], qkv[:, HQ + HKV:], out, cu_seqlens_q=cu, max_query_len=rows, key_cache=k_cache,
+                            value_cache=v_cache, block_table=tables[i % 32], seq_lens=seq_lens, max_seq_len=pages_per * PAGE + rows, sm_scale=D ** -0.5)
+
+    step(0)
+    used_clusters = bool(ops.LAST_ATTENTION_USED_CLUSTERS)
+    us = timed_graph(lambda: [step(i) for i in range(32)], device, replays=max(3, min(steps, 10))) / 32 * 1e3
+    ops.check_status(device)
+    nbytes = ctx * 2 * HKV * D * 2 + rows * (2 * HQ + 2 * HKV) * D * 2
+    peaks = load_peaks()
+    return {"workload": "1 request x 32 block rows, 28/4 heads, d128, 4161 cached tokens in 17 pages + the block, bidirectional, bf16; launches replayed "
+                        "as a CUDA graph of 32 over rotating page sets",
+            "kernel": "attn_decode_sm100_kernel (KV splits of a unit = one thread-block cluster)" if used_clusters else "attn_sm100_kernel + attn_combine_kernel",
+            "us_per_launch": us, "roofline": {"bound": "hbm", "achieved": nbytes / us / 1e3, "peak": peaks["hbm"], "unit": "GB/s",
+                                              "frac": nbytes / us / 1e3 / peaks["hbm"], "bytes_per_launch": nbytes, "traffic": None}}
+
+
 def op_prefill_attention(device: torch.device, steps: int):
     """The attention kernel on the two prefill shapes of the 8K request (28 / 4 heads, d128, bf16, no cached context):
     scoring = 8 packed causal rows of 1093 tokens; joint prefill = one bidirectional sequence of 4193 tokens. Tensor-bound:
@@ -368,7 +401,7 @@ def op_prefill_attention(device: torch.device, steps: int):
     return out_rec
 
 
-def op_linear(device: torch.device, steps: int):
+def op_linear(device: torch.device, steps: int, only: str = ""):
     """The GEMM kernel on the linear-layer shapes of the 8K request, next to cuBLAS (torch.matmul) on the same operands:
     32 block rows (weight streaming: GB/s of weight bytes against the HBM peak) and the 8744 scoring rows (TFLOP/s against the
     bf16 peak). Weights rotate over several copies (> L2); launches replayed as CUDA graphs of 8."""
@@ -380,7 +413,7 @@ def op_linear(device: torch.device, steps: int):
     shapes = [("qkv", 4608, 3584), ("o", 3584, 3584), ("gate_up", 37888, 3584), ("down", 3584, 18944), ("lm_head", 152064, 3584)]
     for m in (32, 8744):
         for name, n, k in shapes:
-            if m > 128 and name == "lm_head":
+            if (m > 128 and name == "lm_head") or (only and only != f"{name}_m{m}"):
                 continue
             copies = max(2, min(8, int(300e6 // (n * k * 2)) + 1))
             ws = [torch.randn(n, k, device=device, dtype=torch.bfloat16, generator=g) * 0.02 for _ in range(copies)]
@@ -612,6 +645,26 @@ def timed_requests(request, steps: int, warmup: int, device, barrier):
     return start.elapsed_time(stop) / steps, result
 
 
+def run_request_once(local_rank: int):
+    """ONE cold 8K request and nothing else: the command a profiler's launch list is taken from (every kernel of a request, a
+    few ten thousand launches, no warm-up to skip)."""
+    from prefilling_dllm_b200 import ops
+
+    device = torch.device("cuda", local_rank)
+    model = build_dream7b(device)
+    rt = make_runtime(model, long_ctx=False)
+    gen = torch.Generator().manual_seed(0)
+    context = torch.randint(0, 151000, (8192,), generator=gen).tolist()
+    query = torch.randint(0, 151000, (64,), generator=gen).tolist()
+    torch.cuda.synchronize(device)
+    t0 = time.perf_counter()
+    result = rt.generate(prefix_ids=rt.bos_ids(), context_ids=context, query_ids=query)
+    torch.cuda.synchronize(device)
+    ops.check_status(device)
+    return {"workload": "one cold 8K request (Dream-7B architecture, random init)", "wall_ms": (time.perf_counter() - t0) * 1e3,
+            "selected_chunks": list(result.selected_chunk_indices), "c_abi_calls": ops.C_ABI_CALLS}
+
+
 def run_request(args, rank: int, world: int, local_rank: int):
     from prefilling_dllm_b200 import ops
     from prefilling_dllm_b200 import sharded as sharded_mod
@@ -767,7 +820,8 @@ def run_request(args, rank: int, world: int, local_rank: int):
     if rank == 0:
         del model
         torch.cuda.empty_cache()
-        line["ops"] = {"decode_attention_8_requests": op_main, "mha_decode_16_requests": op_mha_decode(16, 100, rank, device),
+        line["ops"] = {"decode_attention_8_requests": op_main, "decode_attention_1_request_32_rows": op_decode_rows(device, 5),
+                       "mha_decode_16_requests": op_mha_decode(16, 100, rank, device),
                        "prefill_attention": op_prefill_attention(device, 50), "linear": op_linear(device, 5),
                        "reference_triton_same_gpu": reference_triton_on_this_gpu(device)}
         if world == 1:
@@ -1065,8 +1119,10 @@ def main():
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="native", choices=["native", "reference"])
     ap.add_argument("--workload", default="request",
-                    choices=["request", "op", "op_mha_decode", "op_prefill", "linear", "byte_kernels", "dream7b_decode_batch", "llada8b_decode_batch"],
+                    choices=["request", "request_once", "op", "op_mha_decode", "op_decode_rows", "op_prefill", "linear", "byte_kernels", "dream7b_decode_batch",
+                             "llada8b_decode_batch"],
                     help="request (default): the 8K request per GPU + the sharded 32K request + op-level records; the others run one piece alone")
+    ap.add_argument("--shape", default="", help="--workload linear: run one shape only, e.g. gate_up_m32 (for a profiler capture)")
     ap.add_argument("--concurrent", type=int, default=16, help="requests per GPU that share a denoise step (decode_batch workloads, op_mha_decode)")
     args = ap.parse_args()
 
@@ -1108,7 +1164,11 @@ def main():
         elif args.workload == "op_prefill":
             line = op_prefill_attention(device, args.steps) if rank == 0 else None
         elif args.workload == "linear":
-            line = op_linear(device, args.steps) if rank == 0 else None
+            line = op_linear(device, args.steps, args.shape) if rank == 0 else None
+        elif args.workload == "op_decode_rows":
+            line = op_decode_rows(device, args.steps) if rank == 0 else None
+        elif args.workload == "request_once":
+            line = run_request_once(local_rank) if rank == 0 else None
         elif args.workload == "byte_kernels":
             line = run_byte_kernels(args, local_rank) if rank == 0 else None
         else:

@@ -284,6 +284,21 @@ class PagedDreamModel:
     def layer_cache(self, layer: int) -> Tuple[torch.Tensor, torch.Tensor]:
         return self.kv_cache[0, layer], self.kv_cache[1, layer]
 
+    def plane_pools(self) -> Tuple[torch.Tensor, torch.Tensor]:
+        """(K pool, V pool) of ALL layers, each seen as one unified cache of layers * pages pages: one slot mapping or page list
+        then addresses every layer at once (slot of token t of layer l: (l * pages + page_id) * page_size + offset)."""
+        kv = self.kv_cache
+        shape = (kv.shape[1] * kv.shape[2], kv.shape[3], kv.shape[4], kv.shape[5])
+        return kv[0].view(shape), kv[1].view(shape)
+
+    def all_layer_slots(self, page_ids: Sequence[int], start: int, n: int) -> torch.Tensor:
+        """int32 [n * layers] slots in `plane_pools()` of cache tokens [start, start + n) laid over `page_ids`, token-major
+        (row index = token * layers + layer)."""
+        base = torch.tensor(slots_for(page_ids, start, n, self.page_size), dtype=torch.int64, device=self.device)
+        layers = self.arch.num_hidden_layers
+        offs = torch.arange(layers, dtype=torch.int64, device=self.device) * (self.num_pages * self.page_size)
+        return (base.view(-1, 1) + offs.view(1, -1)).reshape(-1).to(torch.int32)
+
     # ---- forward ----
     @torch.inference_mode()
     def forward(self, ids: torch.Tensor, positions: torch.Tensor, *, cu_seqlens: torch.Tensor, max_query_len: int,

@@ -9,9 +9,11 @@ make every chunk's work depend only on `[prefix ‖ chunk ‖ query ‖ draft]`,
      same selection (no second collective);
   4. the owner of each selected chunk evicts and prefills it locally, which needs the selection only for the chunk's
      RoPE start in `continuous` position mode;
-  5. the owners send the kept KV rows of all layers (one contiguous `[2, layers, kept, Hkv, D]` payload per chunk, plus
-     the kept RoPE positions) to the decode rank with grouped point-to-point operations; the decode rank lays them
-     behind its prefix KV in selected-index order, prefills the query and denoises.
+  5. the owners send the kept KV rows of all layers (one contiguous `[kept, layers, 2, Hkv, D]` payload per chunk — ONE gather
+     launch over the pool seen as `2 * layers * pages` pages — plus the kept RoPE positions) to the decode rank with grouped
+     point-to-point operations. The decode rank receives every payload straight into its slice of one buffer and writes
+     all layers of all chunks into its own page pool with ONE page-write launch (a slot mapping over every layer), in
+     selected-index order behind its prefix KV; then it prefills the query and denoises.
 
 Decode itself is data-parallel over requests (different requests use different decode ranks); there is no tensor
 parallelism. The planning and exchange helpers work on CPU tensors over `gloo` as well, which is how the host logic is
@@ -22,7 +24,7 @@ from __future__ import annotations
 
 import math
 from dataclasses import dataclass
-from typing import Callable, Dict, List, Sequence, Tuple
+from typing import Callable, Dict, List, Optional, Sequence, Tuple
 
 import torch
 import torch.distributed as dist
@@ -103,20 +105,27 @@ def plan_kv_transfers(selected: Sequence[int], kept_tokens: Dict[int, int], plan
 
 def exchange_chunk_kv(transfers: Sequence[KVTransfer], *, rank: int, decode_rank: int, payloads: Dict[int, torch.Tensor],
                       positions: Dict[int, torch.Tensor], payload_shape: Callable[[int], Tuple[int, ...]], dtype: torch.dtype,
-                      device, group=None) -> Tuple[Dict[int, torch.Tensor], Dict[int, torch.Tensor]]:
+                      device, group=None, recv_into: Optional[Dict[int, torch.Tensor]] = None
+                      ) -> Tuple[Dict[int, torch.Tensor], Dict[int, torch.Tensor]]:
     """Move every selected chunk's kept KV and kept RoPE positions from its owner to `decode_rank`.
 
     payloads[ci]: contiguous KV of chunk ci on its owner, shape `payload_shape(kept)`; positions[ci]: int64 [kept].
     All sends and receives of one request are posted as ONE grouped batch (NCCL: a single ncclGroup of send/recv pairs
     over NVLink). Returns, on the decode rank, (payload by chunk, positions by chunk) for every selected chunk — its own
-    chunks are passed through without a copy — and empty dicts elsewhere."""
+    chunks are passed through without a copy — and empty dicts elsewhere. `recv_into[ci]` (decode rank, optional): a contiguous
+    tensor of the payload's shape that chunk ci is received into (a slice of the caller's buffer) instead of a fresh one; the
+    decode rank's own chunks are copied into theirs."""
     ops: List[dist.P2POp] = []
     got_kv: Dict[int, torch.Tensor] = {}
     got_pos: Dict[int, torch.Tensor] = {}
     for t in transfers:
         if t.src_rank == decode_rank:
             if rank == decode_rank:
-                got_kv[t.chunk_index], got_pos[t.chunk_index] = payloads[t.chunk_index], positions[t.chunk_index]
+                kv = payloads[t.chunk_index]
+                if recv_into is not None and t.chunk_index in recv_into:
+                    recv_into[t.chunk_index].copy_(kv)
+                    kv = recv_into[t.chunk_index]
+                got_kv[t.chunk_index], got_pos[t.chunk_index] = kv, positions[t.chunk_index]
             continue
         if rank == t.src_rank:
             kv, pos = payloads[t.chunk_index].contiguous(), positions[t.chunk_index].to(torch.int64).contiguous()
@@ -125,7 +134,9 @@ def exchange_chunk_kv(transfers: Sequence[KVTransfer], *, rank: int, decode_rank
             ops.append(dist.P2POp(dist.isend, kv, decode_rank, group=group))
             ops.append(dist.P2POp(dist.isend, pos, decode_rank, group=group))
         elif rank == decode_rank:
-            kv = torch.empty(payload_shape(t.kept_tokens), dtype=dtype, device=device)
+            kv = recv_into[t.chunk_index] if recv_into is not None and t.chunk_index in recv_into else torch.empty(payload_shape(t.kept_tokens), dtype=dtype, device=device)
+            if tuple(kv.shape) != tuple(payload_shape(t.kept_tokens)) or not kv.is_contiguous():
+                raise ValueError(f"chunk {t.chunk_index}: receive buffer {tuple(kv.shape)} does not match the plan")
             pos = torch.empty((t.kept_tokens,), dtype=torch.int64, device=device)
             got_kv[t.chunk_index], got_pos[t.chunk_index] = kv, pos
             ops.append(dist.P2POp(dist.irecv, kv, t.src_rank, group=group))
@@ -153,19 +164,26 @@ class ShardedChunkPrefill:
 
     def _payload_shape(self, kept: int) -> Tuple[int, ...]:
         a = self.rt.arch
-        return (2, a.num_hidden_layers, int(kept), a.num_key_value_heads, a.head_dim)
+        return (int(kept), a.num_hidden_layers, 2, a.num_key_value_heads, a.head_dim)
 
     def _gather_rows(self, cache, start: int, n: int) -> torch.Tensor:
-        """[2, layers, n, Hkv, D] copy of cache tokens [start, start + n) of every layer."""
+        """[n, layers, 2 (K, V), Hkv, D] copy of cache tokens [start, start + n) of every layer: one gather launch over the
+        pages that hold them in all (K|V, layer) planes, one strided copy into the payload layout."""
         from . import ops
 
         m = self.rt.model
-        out = torch.empty(self._payload_shape(n), dtype=m.dtype, device=m.device)
-        if n:
-            for layer in range(m.arch.num_hidden_layers):
-                for plane, pool in enumerate(m.layer_cache(layer)):
-                    out[plane, layer] = ops.gather_pages(pool, cache.page_ids, start + n)[start:]
-        return out
+        if n <= 0:
+            return torch.empty(self._payload_shape(0), dtype=m.dtype, device=m.device)
+        page, layers, pages = m.page_size, m.arch.num_hidden_layers, m.num_pages
+        p0, p1 = start // page, (start + n - 1) // page
+        base = torch.tensor(cache.page_ids[p0:p1 + 1], dtype=torch.int32, device=m.device)
+        planes = torch.arange(2 * layers, dtype=torch.int32, device=m.device) * pages
+        ids = (planes.view(-1, 1) + base.view(1, -1)).reshape(-1).contiguous()
+        kv = m.kv_cache
+        pool = kv.view(2 * layers * pages, kv.shape[3], kv.shape[4], kv.shape[5])
+        dense = ops.gather_pages(pool, ids, int(ids.numel()) * page).view(2, layers, (p1 - p0 + 1) * page, kv.shape[4], kv.shape[5])
+        off = start - p0 * page
+        return dense[:, :, off:off + n].permute(2, 1, 0, 3, 4).contiguous()
 
     @torch.inference_mode()
     def generate(self, *, prefix_ids, context_ids, query_ids, scoring_query_ids=None, decode_rank: int = 0):
@@ -217,8 +235,17 @@ class ShardedChunkPrefill:
                 scratch.release()
         # 5: hand-off to the decode rank
         transfers = plan_kv_transfers(selected, kept_tokens, plan)
+        recv_into = None
+        if self.rank == decode_rank and selected:
+            # every chunk's payload lands in its slice of one [sum kept, layers, 2, Hkv, D] buffer, in selected order
+            landing = torch.empty(self._payload_shape(sum(kept_tokens[ci] for ci in selected)), dtype=rt.model.dtype, device=rt.device)
+            recv_into, off = {}, 0
+            for ci in selected:
+                recv_into[ci] = landing[off:off + kept_tokens[ci]]
+                off += kept_tokens[ci]
         got_kv, got_pos = exchange_chunk_kv(transfers, rank=self.rank, decode_rank=decode_rank, payloads=payloads, positions=positions,
-                                            payload_shape=self._payload_shape, dtype=rt.model.dtype, device=rt.device, group=self.group)
+                                            payload_shape=self._payload_shape, dtype=rt.model.dtype, device=rt.device, group=self.group,
+                                            recv_into=recv_into)
         ops.check_status(rt.device)
         if self.rank != decode_rank:
             return None
@@ -232,12 +259,14 @@ class ShardedChunkPrefill:
                 cache_positions.extend(rt._range_positions(0, p_len))
             meta = []
             if selected:
-                joined = torch.cat([got_kv[ci] for ci in selected], dim=2)            # [2, layers, sum kept, Hkv, D]
-                slot_t = rt.model.i32(cache.slots(p_len, joined.shape[2]))
-                for layer in range(rt.arch.num_hidden_layers):
-                    k_pool, v_pool = rt.model.layer_cache(layer)
-                    ops.store_kvcache_unified_layout(joined[0, layer].contiguous(), joined[1, layer].contiguous(), k_pool, v_pool, slot_t,
-                                                     "diffusion_lm")
+                # ONE page write for every layer of every chunk: rows (token, layer) of the landing buffer, K and V side by
+                # side, go to the slots of that token in that layer's planes of the pool
+                a = rt.arch
+                rows = landing.view(landing.shape[0] * a.num_hidden_layers, 2, a.num_key_value_heads, a.head_dim)
+                k_pool, v_pool = rt.model.plane_pools()
+                cache.slots(p_len, landing.shape[0])                                   # capacity check
+                ops.store_kvcache_unified_layout(rows[:, 0], rows[:, 1], k_pool, v_pool,
+                                                 rt.model.all_layer_slots(cache.page_ids, p_len, landing.shape[0]), "diffusion_lm")
             for order, ci in enumerate(selected):
                 kept, dst = kept_tokens[ci], cache.length
                 c_start = rt._chunk_rope_start(p_len, order, ci)
