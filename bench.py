@@ -665,6 +665,53 @@ def run_request_once(local_rank: int):
             "selected_chunks": list(result.selected_chunk_indices), "c_abi_calls": ops.C_ABI_CALLS}
 
 
+def run_full_reencode(args, local_rank: int):
+    """`--workload full_reencode --ctx 8192|32768`: what the path avoids, the comparison the reference's README quotes. No selection and
+    no cache: every denoise step forwards [BOS, context, query, generated, block] bidirectionally on the same model and kernels, the
+    LM head on the block's (shifted) rows only. One request, CUDA events, next to the same request through the path."""
+    from prefilling_dllm_b200 import ops
+
+    device = torch.device("cuda", local_rank)
+    torch.cuda.set_device(device)
+    long_ctx = args.ctx > 8192
+    model = build_dream7b(device)
+    rt = make_runtime(model, long_ctx=long_ctx)
+    gen = torch.Generator().manual_seed(args.ctx)
+    context = torch.randint(0, 151000, (args.ctx,), generator=gen).tolist()
+    query = torch.randint(0, 151000, (64,), generator=gen).tolist()
+    new_tokens = rt.max_new_tokens
+    path_ms, _ = timed_requests(lambda: rt.generate(prefix_ids=rt.bos_ids(), context_ids=context, query_ids=query), max(1, min(args.steps, 3)),
+                                max(3, args.warmup), device, lambda: torch.cuda.synchronize(device))
+    mask_id = rt._mask_token_id()
+    prompt = list(rt.bos_ids()) + context + query
+    torch.cuda.synchronize(device)
+    start, stop = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    start.record()
+    done, n_steps = [], 0
+    with torch.inference_mode():
+        while len(done) < new_tokens:
+            blen = min(32, new_tokens - len(done))
+            block = torch.full((blen,), mask_id, dtype=torch.int64, device=device)
+            base = len(prompt) + len(done)
+            while bool((block == mask_id).any()):
+                ids = torch.cat([rt.model.ids_tensor(prompt + done), block])
+                logits, _ = rt._forward_packed([[0] * (base + blen)], [list(range(base + blen))], causal=False, ids_tensor=ids,
+                                               logit_rows=list(range(base - 1, base + blen - 1)))
+                ops.unmask_step(logits, block, mask_token_id=mask_id, threshold=0.9, shift=False)
+                n_steps += 1
+            done += block.tolist()
+    stop.record()
+    torch.cuda.synchronize(device)
+    ops.check_status(device)
+    naive_ms = start.elapsed_time(stop)
+    return {"metric": "request_latency_ms", "value": path_ms, "unit": "ms", "n_gpus": 1, "steps": 1, "warmup": max(3, args.warmup),
+            "higher_is_better": False, "dtype": "bf16", "data": "synthetic",
+            "config": {"workload": f"Dream-7B architecture (random init), {args.ctx}-token random prefix + 64-token query, {new_tokens} new tokens, "
+                                   "block 32, threshold 0.9: the path against re-encoding the full context at every denoise step"},
+            "full_reencode_every_step": {"ms_per_request": naive_ms, "denoise_steps": n_steps, "rows_per_step": len(prompt) + new_tokens,
+                                         "speedup_of_this_path": naive_ms / path_ms}}
+
+
 def run_request(args, rank: int, world: int, local_rank: int):
     from prefilling_dllm_b200 import ops
     from prefilling_dllm_b200 import sharded as sharded_mod
@@ -750,7 +797,11 @@ def run_request(args, rank: int, world: int, local_rank: int):
             "kernel": "linear_sm100_kernel, the linear layers of one denoise step (32 rows): 4 per layer + LM head",
             "bound": "hbm", "achieved": gbs, "peak": peaks["hbm"], "unit": "GB/s", "frac": gbs / peaks["hbm"],
             "bytes_per_launch": br["linear_bytes"] / br["linear_launches"], "us_per_launch": br["linear_ms"] * 1e3 / br["linear_launches"],
-            "launches_timed": br["linear_launches"], "traffic": LINEAR_TRAFFIC_BYTES_PER_LAUNCH, "peak_source": peaks["source"] + " (copy bandwidth)"}
+            "launches_timed": br["linear_launches"],
+            "traffic": LINEAR_TRAFFIC_OVER_ALGORITHMIC * br["linear_bytes"] / br["linear_launches"],
+            "traffic_note": "DRAM bytes of the captured gate/up launch (272.1 MB read + 4.5 MB written for 273.0 MB algorithmic) scaled to the "
+                            "step's average launch; every launch of the step streams its weight matrix exactly once the same way",
+            "peak_source": peaks["source"] + " (copy bandwidth)"}
     barrier()
 
     # ---------------- the 32K request, chunks sharded over the ranks ----------------
@@ -830,8 +881,9 @@ def run_request(args, rank: int, world: int, local_rank: int):
     return line
 
 
-# dram__bytes_read.sum + dram__bytes_write.sum per linear_sm100_kernel launch of the denoise step (ncu, profiles/); None until captured
-LINEAR_TRAFFIC_BYTES_PER_LAUNCH = None
+# (dram__bytes_read.sum + dram__bytes_write.sum) / algorithmic bytes of one linear_sm100_kernel launch at 32 rows: the ncu capture of the
+# gate/up projection (profiles/linear_sm100_kernel_gate_up_32_rows.md) read 272.1 MB and wrote 4.5 MB for 273.0 MB of weights, rows and outputs
+LINEAR_TRAFFIC_OVER_ALGORITHMIC = 276.6 / 273.0
 
 # ---- the reference's CPU path on the toy, and this runtime on the same toy ----------------------------------------------------
 def _toy_setup(tmp):
@@ -1119,10 +1171,11 @@ def main():
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="native", choices=["native", "reference"])
     ap.add_argument("--workload", default="request",
-                    choices=["request", "request_once", "op", "op_mha_decode", "op_decode_rows", "op_prefill", "linear", "byte_kernels", "dream7b_decode_batch",
+                    choices=["request", "request_once", "full_reencode", "op", "op_mha_decode", "op_decode_rows", "op_prefill", "linear", "byte_kernels", "dream7b_decode_batch",
                              "llada8b_decode_batch"],
                     help="request (default): the 8K request per GPU + the sharded 32K request + op-level records; the others run one piece alone")
     ap.add_argument("--shape", default="", help="--workload linear: run one shape only, e.g. gate_up_m32 (for a profiler capture)")
+    ap.add_argument("--ctx", type=int, default=8192, help="--workload full_reencode: context length (8192 or 32768)")
     ap.add_argument("--concurrent", type=int, default=16, help="requests per GPU that share a denoise step (decode_batch workloads, op_mha_decode)")
     args = ap.parse_args()
 
@@ -1167,6 +1220,8 @@ def main():
             line = op_linear(device, args.steps, args.shape) if rank == 0 else None
         elif args.workload == "op_decode_rows":
             line = op_decode_rows(device, args.steps) if rank == 0 else None
+        elif args.workload == "full_reencode":
+            line = run_full_reencode(args, local_rank) if rank == 0 else None
         elif args.workload == "request_once":
             line = run_request_once(local_rank) if rank == 0 else None
         elif args.workload == "byte_kernels":
