@@ -88,6 +88,21 @@ attn_decode_sm100_kernel(const __grid_constant__ CUtensorMap q_map, const __grid
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   if (threadIdx.x == 64) PDLLM_DEC_TRACE(0);
 
+  // ---- on-chip set-up first: it may run while the previous kernel of the stream is still finishing. Nothing global (the
+  // sequence tables, the rows the projections just wrote, the workspace) is touched before grid_dependency_wait().
+  if (warp == 0) {
+    if (lane == 0) {
+      for (int i = 0; i < kNumBars; ++i) mbar_init(&bars[i], (i >= kPFull && i < kPFull + 2) ? 128u : 1u);
+      abort_flag[0] = 0;
+      fence_barrier_init();
+    }
+    __syncwarp();
+  } else if (warp == 1) {
+    gemm::tmem_alloc_cols(tmem_slot, kTmemCols);
+  }
+  grid_dependency_wait();
+  grid_launch_dependents();
+
   // ---- work unit: (sequence, KV head, query tile) x split; the splits of a unit are the CTAs of one cluster ----
   const int split = static_cast<int>(blockIdx.x) % a.splits;
   int u = static_cast<int>(blockIdx.x) / a.splits;
@@ -114,7 +129,7 @@ attn_decode_sm100_kernel(const __grid_constant__ CUtensorMap q_map, const __grid
   const int t_end = min(total_tiles, t_begin + per_split);
   const int n_iter = n_tok > 0 ? t_end - t_begin : 0;
 
-  // ---- set-up: warp 0 initialises the barriers and starts the first copies at once, warp 1 allocates TMEM meanwhile ----
+  // ---- the first copies start at once (warp 0) ----
   // one K or V tile of key tile `it` → its ring slot (the caller has made sure the slot is free)
   auto load_kv = [&](int it, int is_v) {
     const int slot = it & 1;
@@ -137,9 +152,6 @@ attn_decode_sm100_kernel(const __grid_constant__ CUtensorMap q_map, const __grid
   };
   if (warp == 0) {
     if (lane == 0) {
-      for (int i = 0; i < kNumBars; ++i) mbar_init(&bars[i], (i >= kPFull && i < kPFull + 2) ? 128u : 1u);
-      abort_flag[0] = 0;
-      fence_barrier_init();
       if (n_iter > 0) {
         mbar_expect_tx(&bars[kQFull], 2u * 64u * 2u * static_cast<uint32_t>(G * a.tpt));
         tc::tma_load_3d(&q_map, &bars[kQFull], smem + kSmemQ, 0, kvh * G, q_start + tok0);
@@ -148,8 +160,6 @@ attn_decode_sm100_kernel(const __grid_constant__ CUtensorMap q_map, const __grid
       }
     }
     __syncwarp();
-  } else if (warp == 1) {
-    gemm::tmem_alloc_cols(tmem_slot, kTmemCols);
   }
   tc_fence_before();
   __syncthreads();
@@ -598,10 +608,12 @@ inline int launch(const pdllm_attn_params* p, const Plan& pl, cudaStream_t strea
   cfg.blockDim = dim3(kThreads, 1, 1);
   cfg.dynamicSmemBytes = kSmemBytes;
   cfg.stream = stream;
-  cudaLaunchAttribute attr[1];
+  cudaLaunchAttribute attr[2];
   attr[0].id = cudaLaunchAttributeClusterDimension;
   attr[0].val.clusterDim.y = 1;
   attr[0].val.clusterDim.z = 1;
+  attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;   // see launch_dependent(): start ahead of the predecessor's end
+  attr[1].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
   // every cluster of the launch should be resident at once: the largest cluster size, from the planned one down, that fits
@@ -627,6 +639,7 @@ inline int launch(const pdllm_attn_params* p, const Plan& pl, cudaStream_t strea
   a.splits = splits;
   cfg.gridDim = dim3(static_cast<unsigned>(pl.units * splits), 1, 1);
   attr[0].val.clusterDim.x = static_cast<unsigned>(splits);
+  cfg.numAttrs = dependent_launch_enabled() ? 2 : 1;
   cudaError_t e = cudaLaunchKernelEx(&cfg, fn, q_map, kn_map, vn_map, kc_map, vc_map, a);
   if (e != cudaSuccess) return fail(static_cast<int>(e), "attn_decode_sm100_kernel (clusters of %d): %s", splits, cudaGetErrorString(e));
   return check_launch("attn_decode_sm100_kernel");

@@ -378,6 +378,8 @@ attn_sm100_kernel(const __grid_constant__ CUtensorMap q_map, const __grid_consta
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
+  grid_dependency_wait();     // launched ahead of its predecessor's end: nothing global is touched before this
+  grid_launch_dependents();
 
   // ---- decode the work unit: (sequence, KV head, pair of query tiles, KV split) ----
   // Unsplit units come first in launch order, then the split ones with the split as the slowest index: all first
@@ -1103,8 +1105,8 @@ inline int launch(const pdllm_attn_params* p, cudaStream_t stream) {
     }
   }
 
-  if (bf16) attn_sm100_kernel<true><<<static_cast<unsigned>(pl.ctas), kThreads, kSmemBytes, stream>>>(q_map, kn_map, vn_map, kc_map, vc_map, a);
-  else attn_sm100_kernel<false><<<static_cast<unsigned>(pl.ctas), kThreads, kSmemBytes, stream>>>(q_map, kn_map, vn_map, kc_map, vc_map, a);
+  if (bf16) (void)launch_dependent(attn_sm100_kernel<true>, dim3(static_cast<unsigned>(pl.ctas)), dim3(kThreads), kSmemBytes, stream, q_map, kn_map, vn_map, kc_map, vc_map, a);
+  else (void)launch_dependent(attn_sm100_kernel<false>, dim3(static_cast<unsigned>(pl.ctas)), dim3(kThreads), kSmemBytes, stream, q_map, kn_map, vn_map, kc_map, vc_map, a);
   if ((rc = check_launch("attn_sm100_kernel")) != 0) return rc;
   if (pl.num_splits > 1 && !pl.fused_merge) {
     attn_combine_kernel<<<static_cast<unsigned>(pl.tiles * (kHeadDim / kCombineCols)), kTileM, 0, stream>>>(a);

@@ -8,7 +8,9 @@
 
 #include <cstdarg>
 #include <cstdio>
+#include <cstdlib>
 #include <string>
+#include <utility>
 
 #include "../../include/pdllm_b200.h"
 
@@ -117,6 +119,43 @@ struct Vec16<__half> {
     }
   }
 };
+
+// ---- programmatic dependent launch ----------------------------------------------------------------------------------
+// The kernels of a forward run back to back on one stream, each a few microseconds long at decode shapes, so the gap between
+// a kernel's last CTA and the next kernel's first instruction is a visible share of a step. A kernel launched with the
+// programmatic-serialization attribute may be scheduled while its predecessor still runs; it does its on-chip set-up
+// (barriers, TMEM allocation, descriptor prefetch), then calls grid_dependency_wait(), which returns once the predecessor
+// has completed and its writes are visible, and only then touches global memory. Directly after its own wait it calls
+// grid_launch_dependents(), so at most one successor runs ahead. Both calls are no-ops in a kernel launched the plain way,
+// and a successor of a kernel that never signals simply starts when that kernel has finished.
+__device__ __forceinline__ void grid_dependency_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void grid_launch_dependents() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+
+// PDLLM_NO_PDL=1 launches every kernel the plain way (for A/B timing)
+inline bool dependent_launch_enabled() {
+  static const bool on = [] {
+    const char* v = std::getenv("PDLLM_NO_PDL");
+    return !(v != nullptr && v[0] != '\0' && v[0] != '0');
+  }();
+  return on;
+}
+
+// Launch `kernel` on `stream`, overlapping its start with the tail of the kernel before it (see above). The kernel must call
+// grid_dependency_wait() before its first access to global memory.
+template <typename... KArgs, typename... Args>
+inline cudaError_t launch_dependent(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t stream, Args&&... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = dependent_launch_enabled() ? 1 : 0;
+  return cudaLaunchKernelEx(&cfg, kernel, static_cast<KArgs>(std::forward<Args>(args))...);
+}
 
 inline int dtype_bytes(int dtype) { return dtype == PDLLM_F32 ? 4 : 2; }
 

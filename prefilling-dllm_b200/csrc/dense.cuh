@@ -18,6 +18,8 @@ template <typename T>
 __global__ void add_rmsnorm_kernel(T* __restrict__ x, const T* __restrict__ delta, const T* __restrict__ weight,
                                    T* __restrict__ out, int hidden, int64_t x_stride, int64_t delta_stride,
                                    int64_t out_stride, float eps) {
+  grid_dependency_wait();     // launched ahead of its predecessor's end: nothing global is touched before this
+  grid_launch_dependents();
   const int64_t row = blockIdx.x;
   T* xr = x + row * x_stride;
   const T* dr = delta ? delta + row * delta_stride : nullptr;
@@ -54,6 +56,8 @@ __global__ void add_rmsnorm_kernel(T* __restrict__ x, const T* __restrict__ delt
 template <typename T>
 __global__ void rope_inplace_kernel(T* __restrict__ x, const T* __restrict__ cos_tab, const T* __restrict__ sin_tab,
                                     int64_t n_tokens, int num_heads, int head_dim, int64_t row_stride) {
+  grid_dependency_wait();     // launched ahead of its predecessor's end: nothing global is touched before this
+  grid_launch_dependents();
   const int half = head_dim / 2;
   const int64_t per_tok = static_cast<int64_t>(num_heads) * half;
   const int64_t total = n_tokens * per_tok;

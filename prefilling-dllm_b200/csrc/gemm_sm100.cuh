@@ -219,6 +219,9 @@ linear_sm100_kernel(const __grid_constant__ CUtensorMap a_map, const __grid_cons
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
+  // barriers and TMEM are set up; from here on the kernel reads what its predecessor wrote
+  grid_dependency_wait();
+  grid_launch_dependents();
 
   Schedule<kSwap, kBN> sched;
   sched.init(a);
@@ -613,10 +616,12 @@ inline int launch_one(const CUtensorMap& a_map, const CUtensorMap& b_map, const 
     cfg.blockDim = dim3(kThreads, 1, 1);
     cfg.dynamicSmemBytes = smem_bytes(kBN);
     cfg.stream = stream;
-    cudaLaunchAttribute attr[1];
+    cudaLaunchAttribute attr[2];
     attr[0].id = cudaLaunchAttributeClusterDimension;
     attr[0].val.clusterDim.y = 1;
     attr[0].val.clusterDim.z = 1;
+    attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;   // see launch_dependent(): start ahead of the predecessor's end
+    attr[1].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = attr;
     cfg.numAttrs = 1;
     static std::mutex mu_fit;
@@ -646,16 +651,17 @@ inline int launch_one(const CUtensorMap& a_map, const CUtensorMap& b_map, const 
     if (b.cluster_parts > 1) {
       cfg.gridDim = dim3(static_cast<unsigned>(tiles * b.cluster_parts), 1, 1);
       attr[0].val.clusterDim.x = static_cast<unsigned>(b.cluster_parts);
+      cfg.numAttrs = dependent_launch_enabled() ? 2 : 1;
       cudaError_t e = cudaLaunchKernelEx(&cfg, fn, a_map, b_map, b);
       if (e != cudaSuccess) return fail(static_cast<int>(e), "linear_sm100_kernel (clusters of %d): %s", b.cluster_parts, cudaGetErrorString(e));
       return check_launch("linear_sm100_kernel");
     }
     // no cluster size fits: every tile whole in one CTA (no workspace needed)
     b.whole_tiles = tiles; b.units = 0; b.sk_grid = 0;
-    fn<<<static_cast<unsigned>(tiles), kThreads, smem_bytes(kBN), stream>>>(a_map, b_map, b);
+    (void)launch_dependent(fn, dim3(static_cast<unsigned>(tiles)), dim3(kThreads), smem_bytes(kBN), stream, a_map, b_map, b);
     return check_launch("linear_sm100_kernel");
   }
-  fn<<<static_cast<unsigned>(grid), kThreads, smem_bytes(kBN), stream>>>(a_map, b_map, a);
+  (void)launch_dependent(fn, dim3(static_cast<unsigned>(grid)), dim3(kThreads), smem_bytes(kBN), stream, a_map, b_map, a);
   return check_launch("linear_sm100_kernel");
 }
 

@@ -15,6 +15,8 @@ __global__ void store_unified_vec16_kernel(const uint4* __restrict__ key, const 
                                            const int32_t* __restrict__ slot_mapping, int64_t n_tokens,
                                            int segs_per_row, int64_t key_stride_v, int64_t value_stride_v,
                                            int64_t num_slots, int32_t* status) {
+  grid_dependency_wait();     // launched ahead of its predecessor's end: nothing global is touched before this
+  grid_launch_dependents();
   int64_t idx = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
   int64_t total = n_tokens * segs_per_row;
   for (; idx < total; idx += static_cast<int64_t>(gridDim.x) * blockDim.x) {

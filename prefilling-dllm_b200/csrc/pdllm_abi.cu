@@ -61,7 +61,7 @@ int pdllm_store_kvcache_unified(const void* key, const void* value, void* k_cach
   if (vec) {
     const int segs = static_cast<int>(row_bytes / 16);
     const int threads = 256;
-    store_unified_vec16_kernel<<<grid_for(n_tokens * segs, threads), threads, 0, as_stream(stream)>>>(
+    (void)launch_dependent(store_unified_vec16_kernel, dim3(grid_for(n_tokens * segs, threads)), dim3(threads), 0, as_stream(stream),
         static_cast<const uint4*>(key), static_cast<const uint4*>(value), static_cast<uint4*>(k_cache), static_cast<uint4*>(v_cache),
         slot_mapping, n_tokens, segs, key_stride * elem_bytes / 16, value_stride * elem_bytes / 16, num_slots, status);
   } else {
@@ -226,7 +226,7 @@ int pdllm_unmask_step_batched(const void* logits, int64_t logits_stride, int64_t
   dim3 grid(kUnmaskChunks, block_len, batch);
   return dispatch_dtype(dtype, [&](auto* tag) -> int {
     using T = std::remove_pointer_t<decltype(tag)>;
-    unmask_kernel<T><<<grid, kUnmaskThreads, 0, as_stream(stream)>>>(
+    (void)launch_dependent(unmask_kernel<T>, grid, dim3(kUnmaskThreads), 0, as_stream(stream),
         static_cast<const T*>(logits), logits_stride, static_cast<const T*>(last_logit), block_len, vocab, shift, block_ids, mask_id,
         threshold, conf_dtype, out_counts, out_conf, out_x0, static_cast<float*>(workspace), batch_stride, last_stride);
     return check_launch("unmask_kernel");
@@ -426,7 +426,7 @@ int pdllm_add_rmsnorm(void* x, const void* delta, const void* weight, void* out,
   if (!x || !weight || !out) return fail(PDLLM_E_INVALID, "add_rmsnorm: null pointer");
   const int threads = hidden >= 2048 ? 512 : 256;
   PDLLM_DISPATCH_DTYPE(dtype, "add_rmsnorm",
-                       add_rmsnorm_kernel<T><<<static_cast<unsigned>(n_tokens), threads, 0, as_stream(stream)>>>(
+                       (void)launch_dependent(add_rmsnorm_kernel<T>, dim3(static_cast<unsigned>(n_tokens)), dim3(threads), 0, as_stream(stream),
                            static_cast<T*>(x), static_cast<const T*>(delta), static_cast<const T*>(weight), static_cast<T*>(out), hidden,
                            x_stride, delta_stride, out_stride, eps));
   return check_launch("add_rmsnorm");
@@ -439,7 +439,7 @@ int pdllm_rope_inplace(void* x, const void* cos_tab, const void* sin_tab, int64_
   if (!x || !cos_tab || !sin_tab) return fail(PDLLM_E_INVALID, "rope_inplace: null pointer");
   const int grid = grid_for(n_tokens * num_heads * (head_dim / 2), 256);
   PDLLM_DISPATCH_DTYPE(dtype, "rope_inplace",
-                       rope_inplace_kernel<T><<<grid, 256, 0, as_stream(stream)>>>(static_cast<T*>(x), static_cast<const T*>(cos_tab),
+                       (void)launch_dependent(rope_inplace_kernel<T>, dim3(grid), dim3(256), 0, as_stream(stream), static_cast<T*>(x), static_cast<const T*>(cos_tab),
                                                                                    static_cast<const T*>(sin_tab), n_tokens, num_heads,
                                                                                    head_dim, row_stride));
   return check_launch("rope_inplace");

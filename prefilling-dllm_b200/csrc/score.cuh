@@ -41,6 +41,8 @@ unmask_kernel(const T* __restrict__ logits, int64_t stride, const T* __restrict_
               int64_t vocab, int shift, int64_t* __restrict__ block_ids, int64_t mask_id, float threshold,
               int conf_dtype, int32_t* __restrict__ out_counts, float* __restrict__ out_conf,
               int64_t* __restrict__ out_x0, float* __restrict__ ws, int64_t batch_stride, int64_t last_stride) {
+  grid_dependency_wait();     // launched ahead of its predecessor's end: nothing global is touched before this
+  grid_launch_dependents();
   // blockIdx.z: one block of slots per request, each with its own logits rows, ids, outputs and scratch
   {
     const int64_t z = blockIdx.z;

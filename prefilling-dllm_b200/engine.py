@@ -29,7 +29,7 @@ from typing import Dict, Iterable, List, Optional, Sequence, Tuple
 import torch
 
 from . import ops
-from .model import CachedPrefix, DreamArch, PageAllocator, PagedDreamModel, denoise_blocks, slots_for
+from .model import denoise_blocks_batched, CachedPrefix, DreamArch, PageAllocator, PagedDreamModel, denoise_blocks, slots_for
 
 _OFF = {"none", "off", "0", ""}
 
@@ -661,6 +661,33 @@ class FastDLLMDreamEngine:
         finally:
             self.release_pd_record(record)
 
+    def _token_run(self, record: DreamPrefillRecord, extra: List[int]) -> _TokenRun:
+        """[prompt ‖ suffix] of a record as ONE run of tokens over a page list. The suffix continues in the prompt's last page
+        when the record owns its prompt pages; when they belong to the shared prefix cache (other requests read them, and may
+        append their own suffix) the partially filled last page is first copied into a private one. Pages allocated here are
+        appended to `extra` for the caller to release."""
+        page = self.page_size
+        n_full, rem = divmod(int(record.prompt_len), page)
+        if rem == 0:
+            pages = list(record.prompt_page_ids[:n_full]) + list(record.block_page_ids)
+        elif record.owns_prompt_pages:
+            pages = list(record.prompt_page_ids[:n_full + 1]) + list(record.block_page_ids)
+        else:
+            private = list(record.block_page_ids)
+            need = math.ceil((rem + record.decode_len) / page)
+            if need > len(private):
+                self._prefix_cache.ensure_free(need - len(private))
+                more = self._prefix_cache.allocate_pages(need - len(private))
+                extra += more
+                private += more
+            planes = 2 * int(self.model.kv_cache.shape[1])
+            ops.copy_pages(self._layer_pools(), self._all_layer_page_ids([record.prompt_page_ids[n_full]]), self._layer_pools(),
+                           self._all_layer_page_ids([private[0]]), n_lists=planes, tokens_per_list=rem)
+            pages = list(record.prompt_page_ids[:n_full]) + private
+        if len(pages) * page < record.prompt_len + record.decode_len:
+            raise RuntimeError("record holds too few pages for its prompt and MASK slots")
+        return _TokenRun(pages, int(record.prompt_len), page)
+
     def _decode_blocks(self, record: DreamPrefillRecord, max_new_tokens: int, stop_token_ids) -> FastDLLMEngineOutput:
         """Several generation blocks on a record (beyond the reference engine, whose first version stops at one block:
         fastdllm_engine.py:1911-1915, 2286-2290). The block loop is the eval class's dual cache (fastdllm_parallelcomp.py
@@ -671,28 +698,9 @@ class FastDLLMDreamEngine:
         The loop needs [prompt ‖ suffix] as ONE run of tokens over a page list. The suffix continues in the prompt's last
         page when the record owns its prompt pages; when they belong to the shared prefix cache (other requests read them, and
         may append their own suffix) the partially filled last page is first copied into a private one."""
-        page = self.page_size
-        n_full, rem = divmod(int(record.prompt_len), page)
         extra: List[int] = []
         try:
-            if rem == 0:
-                pages = list(record.prompt_page_ids[:n_full]) + list(record.block_page_ids)
-            elif record.owns_prompt_pages:
-                pages = list(record.prompt_page_ids[:n_full + 1]) + list(record.block_page_ids)
-            else:
-                private = list(record.block_page_ids)
-                need = math.ceil((rem + record.decode_len) / page)
-                if need > len(private):
-                    self._prefix_cache.ensure_free(need - len(private))
-                    extra = self._prefix_cache.allocate_pages(need - len(private))
-                    private += extra
-                planes = 2 * int(self.model.kv_cache.shape[1])
-                ops.copy_pages(self._layer_pools(), self._all_layer_page_ids([record.prompt_page_ids[n_full]]), self._layer_pools(),
-                               self._all_layer_page_ids([private[0]]), n_lists=planes, tokens_per_list=rem)
-                pages = list(record.prompt_page_ids[:n_full]) + private
-            if len(pages) * page < record.prompt_len + record.decode_len:
-                raise RuntimeError("record holds too few pages for its prompt and MASK slots")
-            view = _TokenRun(pages, int(record.prompt_len), page)
+            view = self._token_run(record, extra)
             steps: List[int] = []
             generated = denoise_blocks(self.model, view, suffix_pos_start=int(record.suffix_positions[0]), last_logit=record.last_context_logit,
                                        first_token=None, tail_in_cache=0, max_new=int(max_new_tokens), block_length=self.block_length,
@@ -724,10 +732,10 @@ class FastDLLMDreamEngine:
             for r in records:
                 if r.decode_len != decode_len:
                     raise ValueError("records of one batch must share decode_len")
-                if r.decode_len > self.block_length:
-                    raise NotImplementedError("shared denoise steps serve one-block records; decode records with several blocks one by one")
                 if max_new_tokens > r.decode_len:
                     raise ValueError(f"max_new_tokens={max_new_tokens} exceeds record decode_len={r.decode_len}.")
+            if decode_len > self.block_length:
+                return self._decode_blocks_shared(records, int(max_new_tokens), stop_token_ids)
             requests = [dict(positions=r.suffix_positions, ctx_page_ids=r.prompt_page_ids, ctx_len=r.prompt_len,
                              last_logit=r.last_context_logit, store_slots=slots_for(r.block_page_ids, 0, decode_len, self.page_size))
                         for r in records]
@@ -753,6 +761,23 @@ class FastDLLMDreamEngine:
         finally:
             for r in records:
                 self.release_pd_record(r)
+
+    def _decode_blocks_shared(self, records: List[DreamPrefillRecord], max_new_tokens: int, stop_token_ids) -> List[FastDLLMEngineOutput]:
+        """Records of several blocks in shared steps: the dual-cache block loop of `_decode_blocks`, every forward of it packed over
+        the records (`model.denoise_blocks_batched`). The caller releases the records."""
+        extra: List[int] = []
+        try:
+            views = [self._token_run(r, extra) for r in records]
+            steps: List[List[int]] = [[] for _ in records]
+            generated = denoise_blocks_batched(self.model, views, suffix_pos_starts=[int(r.suffix_positions[0]) for r in records],
+                                               last_logits=[r.last_context_logit for r in records], max_new=max_new_tokens,
+                                               block_length=self.block_length, mask_id=self.mask_token_id, threshold=self.threshold,
+                                               softmax_dtype=torch.float32, use_graph=not self.config.enforce_eager, steps_out=steps)
+            ops.check_status(self.device)
+            return [self._finish(torch.tensor(g, dtype=torch.long), max_new_tokens, stop_token_ids, sum(st)) for g, st in zip(generated, steps)]
+        finally:
+            if extra:
+                self._prefix_cache.release_pages(extra)
 
     def _require_shifted_logits(self, what: str) -> None:
         """The selection / chunk-local twins restate Dream's shifted read-out only (the reference engine has no other model)."""

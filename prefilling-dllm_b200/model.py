@@ -414,7 +414,8 @@ class PagedDreamModel:
 
 def denoise_blocks(model: "PagedDreamModel", cache, *, suffix_pos_start: int, last_logit: torch.Tensor, first_token, tail_in_cache: int,
                    max_new: int, block_length: int, mask_id: int, threshold: float, softmax_dtype: Optional[torch.dtype], use_graph: bool,
-                   fixed_steps_per_block: Optional[int] = None, fill_most_confident=None, steps_out: Optional[List[int]] = None) -> List[int]:
+                   fixed_steps_per_block: Optional[int] = None, fill_most_confident=None, steps_out: Optional[List[int]] = None,
+                   pick_first_token=None, threshold_step=None) -> List[int]:
     """Fast-dLLM dual-cache block loop over a paged cache (reference eval class prefilling_dllm_eval/fastdllm_parallelcomp.py
     :2932-2998, :2399-2441), shared by the eval-class runtime and the engine's multi-block decode.
 
@@ -429,7 +430,10 @@ def denoise_blocks(model: "PagedDreamModel", cache, *, suffix_pos_start: int, la
     `fixed_steps_per_block`: None = confidence-threshold denoising; an int = the fixed-step diffusion sampler (reference
     _denoise_block_diffusion :2443-2510): step i of n transfers int(masks * (1 - t[i+1] / t[i])) of the most confident slots
     through `fill_most_confident(logits, block, last_logit, count)`, t = linspace(1, 1e-3, n + 1), the last step all that is left.
-    `steps_out`: when given, the number of denoise forwards of every block is appended."""
+    `steps_out`: when given, the number of denoise forwards of every block is appended.
+    `pick_first_token(last_logit) -> 0-d tensor`: the first token of a block (default: arg-max, which is what any greedy sampler
+    returns). `threshold_step(logits, block, last_logit) -> MASK slots left`: replaces the fused forward + unmask step of the
+    confidence-threshold loop by an eager forward followed by this callable (samplers that the unmask kernel does not cover)."""
     import math
 
     arch = model.arch
@@ -467,7 +471,8 @@ def denoise_blocks(model: "PagedDreamModel", cache, *, suffix_pos_start: int, la
             tail_len = later
             if not arch.logit_shift:
                 raise NotImplementedError("un-shifted (LLaDA) block initialisation is not built")
-            first = torch.argmax(last_logit)    # softmax is monotone: the arg-max of the logit
+            # softmax is monotone: a greedy sampler's first token is the arg-max of the logit
+            first = torch.argmax(last_logit) if pick_first_token is None else pick_first_token(last_logit)
         else:
             first = first_token
         ctx = done + tail_len
@@ -496,6 +501,10 @@ def denoise_blocks(model: "PagedDreamModel", cache, *, suffix_pos_start: int, la
             guard += 1
             if guard > blen + 8:
                 break
+            if threshold_step is not None:
+                logits, _ = forward(block, block_pos, ctx)
+                remaining = int(threshold_step(logits, block, last_logit))
+                continue
             remaining = runner.run()   # forward + unmask kernel (a CUDA graph replay from the third step on); one host read
         if steps_out is not None:
             steps_out.append(guard)
@@ -507,6 +516,87 @@ def denoise_blocks(model: "PagedDreamModel", cache, *, suffix_pos_start: int, la
         cache.length = done + blen
         tail_len = 0
     return generated[:max_new]
+
+
+def denoise_blocks_batched(model: "PagedDreamModel", caches, *, suffix_pos_starts: Sequence[int], last_logits: Sequence[torch.Tensor],
+                           max_new: int, block_length: int, mask_id: int, threshold: float, softmax_dtype: Optional[torch.dtype],
+                           use_graph: bool, steps_out: Optional[List[List[int]]] = None) -> List[List[int]]:
+    """`denoise_blocks` for several requests whose blocks share every forward: the suffix initialisation, each denoise step and
+    the commit of block b run once for all requests (rows packed, every request against its own page list and context
+    length), so a step reads the model's weights once whatever the number of requests. Confidence-threshold rule only; every
+    request generates `max_new` tokens in blocks of `block_length`. `caches[i]`: as in `denoise_blocks` (updated in place).
+    Same ids per request as `denoise_blocks` on that request alone. `steps_out[i]`: forwards each block of request i needed."""
+    import math
+
+    arch, dev, n_req = model.arch, model.device, len(caches)
+    if not arch.logit_shift:
+        raise NotImplementedError("un-shifted (LLaDA) block initialisation is not built")
+    page = model.page_size
+
+    def packed_forward(ids_rows, pos_rows, ctx_lens, *, slot_rows=None, logit_rows=None, want_logits=True, store_after_attention=False):
+        lens = [len(p) for p in pos_rows]
+        cu = [0]
+        for n in lens:
+            cu.append(cu[-1] + n)
+        width = max(len(c.page_ids) for c in caches)
+        table = torch.zeros((n_req, width), dtype=torch.int32, device=dev)
+        for i, c in enumerate(caches):
+            table[i, :len(c.page_ids)] = model.i32(c.page_ids)
+        slots = None if slot_rows is None else model.i32([s for row in slot_rows for s in row])
+        return model.forward(torch.cat(ids_rows), torch.tensor([p for row in pos_rows for p in row], dtype=torch.long, device=dev),
+                             cu_seqlens=model.i32(cu), max_query_len=max(lens), slot_mapping=slots, causal=False,
+                             logit_rows=None if logit_rows is None else model.ids_tensor(logit_rows), want_logits=want_logits,
+                             store_after_attention=store_after_attention, block_table=table,
+                             seq_lens=model.i32([c + n for c, n in zip(ctx_lens, lens)]), max_seq_len=max(ctx_lens) + max(lens))
+
+    prompt_lens = [int(c.length) for c in caches]
+    last_logits = list(last_logits)
+    generated: List[List[int]] = [[] for _ in range(n_req)]
+    num_blocks = max(1, math.ceil(max_new / block_length))
+    for b in range(num_blocks):
+        start = b * block_length
+        blen = min(block_length, max_new - start)
+        if blen <= 0:
+            break
+        later = max_new - start - blen
+        done = [n0 + start for n0 in prompt_lens]
+        block_pos = [list(range(s0 + start, s0 + start + blen)) for s0 in suffix_pos_starts]
+        if later > 0:
+            masks = torch.full((blen + later,), mask_id, dtype=torch.long, device=dev)
+            packed_forward([masks] * n_req, [list(range(s0 + start, s0 + start + blen + later)) for s0 in suffix_pos_starts], done,
+                           slot_rows=[[-1] * blen + c.slots(d, later) for c, d in zip(caches, done)], want_logits=False)
+        requests = [dict(positions=block_pos[i], ctx_page_ids=caches[i].page_ids, ctx_len=done[i] + later, last_logit=last_logits[i])
+                    for i in range(n_req)]
+        runner = model.batched_step_runner(block_len=blen, requests=requests, mask_token_id=mask_id, threshold=float(threshold),
+                                           shift=True, softmax_dtype=softmax_dtype, use_graph=bool(use_graph))
+        for i, block in enumerate(runner.blocks):
+            block.fill_(mask_id)
+            block[0] = torch.argmax(last_logits[i])
+        left, step, needed = [blen - 1] * n_req, 0, [0] * n_req
+        while any(x > 0 for x in left):
+            step += 1
+            if step > blen + 8:
+                raise RuntimeError("denoising did not converge: every step must unmask at least one slot")
+            runner.run()
+            for i, (before, after) in enumerate(zip(left, runner.remaining)):
+                if before > 0 and after == 0:
+                    needed[i] = step
+            left = list(runner.remaining)
+        if steps_out is not None:
+            for i in range(n_req):
+                steps_out[i].append(needed[i])
+        for i, block in enumerate(runner.blocks):
+            generated[i].extend(block.tolist())
+        # commit: the finished blocks' K/V take the first slots behind prompt + finished blocks (stored after attention, which
+        # still reads the later-MASK slots there); the last row's logit is the next block's last-context logit
+        ctx = [d + later for d in done]
+        logits, _ = packed_forward([blk.clone() for blk in runner.blocks], block_pos, ctx,
+                                   slot_rows=[c.slots(d, blen) for c, d in zip(caches, done)],
+                                   logit_rows=[i * blen + blen - 1 for i in range(n_req)], store_after_attention=True)
+        last_logits = [logits[i] for i in range(n_req)]
+        for c, d in zip(caches, done):
+            c.length = d + blen
+    return [g[:max_new] for g in generated]
 
 
 class _StepGraph:
@@ -525,6 +615,7 @@ class _StepGraph:
         self.left: Optional[torch.Tensor] = None      # [batch] MASK slots left after the captured step
         self.eager_steps = 0
         self.calls_per_step = 0                       # C-ABI calls the captured step makes (for launch accounting)
+        self.host_counts: Optional[torch.Tensor] = None   # pinned [2, batch]: where the counts of the last two replays land
 
 
 class BlockStepRunner:
@@ -572,6 +663,10 @@ class BlockStepRunner:
         self.blocks = [entry.block[i * n:(i + 1) * n] for i in range(batch)]
         self.block = self.blocks[0]
         self.remaining = [n] * batch
+        self._known = [n] * batch            # MASK slots per request after the last step whose counts were read
+        self._most_filled = 1                # most slots any step of this block has filled in one request
+        self._pending: List[Tuple[torch.cuda.Event, int]] = []   # replays enqueued whose counts were not read yet
+        self._slot = 0
         dev = model.device
         entry.positions.copy_(torch.tensor([p for r in requests for p in r["positions"]], dtype=torch.long, device=dev))
         entry.table.zero_()
@@ -623,8 +718,38 @@ class BlockStepRunner:
                         if gc_was_on:
                             gc.enable()
                     e.graph = graph                  # capturing records the launches without running them
-                e.graph.replay()
-                ops.C_ABI_CALLS += e.calls_per_step
-                left = e.left
+                return self._run_replayed()
             self.remaining = left.tolist()           # the one host read of a step
+            self._known = list(self.remaining)
             return int(sum(self.remaining))
+
+    def _enqueue_replay(self) -> None:
+        """Replay the step and copy its MASK counts to pinned host memory behind it, without waiting."""
+        e = self.e
+        e.graph.replay()
+        ops.C_ABI_CALLS += e.calls_per_step
+        if e.host_counts is None:
+            e.host_counts = torch.empty((2,) + tuple(e.left.shape), dtype=e.left.dtype, pin_memory=True)
+        slot = self._slot
+        self._slot ^= 1
+        e.host_counts[slot].copy_(e.left, non_blocking=True)
+        done = torch.cuda.Event()
+        done.record()
+        self._pending.append((done, slot))
+
+    def _run_replayed(self) -> int:
+        """A replayed step, with the NEXT step already enqueued behind it when the block cannot finish in this one: launching a
+        graph of a few hundred nodes and turning the host around take a fraction of a millisecond per step, during which the
+        GPU would idle. A step on a block without MASK slots changes nothing, so a step enqueued in vain costs time only; it is
+        enqueued only while more slots are left than four times the most any step of this block has filled."""
+        e = self.e
+        if not self._pending:
+            self._enqueue_replay()
+        if len(self._pending) < 2 and max(self._known) > 4 * self._most_filled:
+            self._enqueue_replay()
+        done, slot = self._pending.pop(0)
+        done.synchronize()
+        new = e.host_counts[slot].tolist()
+        self._most_filled = max([self._most_filled] + [b - a for b, a in zip(self._known, new)])
+        self._known = self.remaining = new
+        return int(sum(new))

@@ -11,9 +11,11 @@ slot mapping of the page write, every model call is a packed var-len forward ove
 sampling / scoring tails are single fused kernels (`ops.unmask_step`, `ops.self_information_scores`, ...).
 
 Where the reference hands tensors around (`past_key_values`), this class hands a `PagedCache` handle.
-Not built (raise NotImplementedError): sampling with temperature / top-p / top-k, `alg` other than
-"confidence_threshold" / "origin", score modes other than none / self_information / draft_self_information, avg-pooling
-and non-default head/layer reductions, the LLaDA leave-one-out scorer.
+The default flags run on the fused kernels. Flags off the default path — sampling with temperature / top-p / top-k, the
+`topk_margin` / `entropy` confidence rules, `alg_temp`, avg-pooling and the other head / layer reductions, the chunk→query score
+direction, the `attention` / `next_block_logits` / per-chunk-draft score modes — reuse the same forwards and finish with a few
+device-side torch ops on [rows, vocab] or [heads, chunk] tensors instead of a fused tail.
+Not built (raise NotImplementedError): YaRN RoPE scaling, the LLaDA leave-one-out scorer.
 """
 
 from __future__ import annotations
@@ -163,6 +165,41 @@ def split_token_chunks(token_ids: Sequence[int], chunk_size: int, split_from_tai
     return out
 
 
+def sample_tokens(logits: torch.Tensor, temperature: float = 0.0, top_p: Optional[float] = None, top_k: Optional[int] = None,
+                  margin_confidence: bool = False, neg_entropy: bool = False, generator: Optional[torch.Generator] = None):
+    """(confidence, token) per row of `logits` [rows, vocab] — the reference's sampler (fastdllm_parallelcomp.py:183-233) on the
+    device the logits live on. Order of the filters as there: temperature, nucleus (keep the smallest prefix of the sorted
+    distribution whose mass exceeds top_p, the first token always), top-k (drop what is below the k-th largest), softmax in the
+    logits' dtype; greedy arg-max at temperature 0, otherwise one categorical draw (from `generator` when given).
+    Confidence: the chosen token's probability, or top-1 minus top-2 probability, or the negative entropy sum p*log(p + 1e-10)."""
+    if temperature and temperature > 0:
+        logits = logits / temperature
+    floor = torch.finfo(logits.dtype).min
+    if top_p is not None and top_p < 1:
+        ordered, order = torch.sort(logits, dim=-1, descending=True)
+        mass = torch.cumsum(torch.softmax(ordered, dim=-1), dim=-1)
+        drop_sorted = mass > top_p
+        drop_sorted = torch.cat([torch.zeros_like(drop_sorted[..., :1]), drop_sorted[..., :-1]], dim=-1)   # shift right: keep the crossing token
+        drop = torch.zeros_like(drop_sorted).scatter(-1, order, drop_sorted)
+        logits = logits.masked_fill(drop, floor)
+    if top_k is not None:
+        kth = torch.topk(logits, min(int(top_k), logits.size(-1)), dim=-1).values[..., -1:]
+        logits = logits.masked_fill(logits < kth, floor)
+    probs = torch.softmax(logits, dim=-1)
+    if temperature and temperature > 0:
+        flat = probs.reshape(-1, probs.size(-1)).float()
+        token = torch.multinomial(flat, 1, generator=generator).reshape(probs.shape[:-1])
+        confidence = torch.gather(probs, -1, token.unsqueeze(-1)).squeeze(-1)
+    else:
+        confidence, token = probs.max(dim=-1)
+    if margin_confidence:
+        top2 = torch.topk(probs, 2, dim=-1).values
+        confidence = top2[..., 0] - top2[..., 1]
+    if neg_entropy:
+        confidence = torch.sum(probs * torch.log(probs + 1e-10), dim=-1)
+    return confidence, token
+
+
 class PagedCache:
     """Handle to a request's KV in the paged pool: logical token order → pages, plus the RoPE position of each token."""
 
@@ -236,14 +273,8 @@ class FastDLLMParallelComp:
             raise ValueError(f"Unsupported token_score_keep: {config.token_score_keep}")
         if config.token_eviction_granularity not in {"global", "per_head"}:
             raise ValueError(f"Unsupported token_eviction_granularity: {config.token_eviction_granularity}")
-        if config.temperature and config.temperature > 0 or config.top_p is not None or config.top_k is not None:
-            raise NotImplementedError("only greedy decoding (temperature 0, no top-p / top-k) is built")
-        if config.alg not in {"confidence_threshold", "origin"}:
-            raise NotImplementedError(f"alg={config.alg!r} is not built; only 'confidence_threshold' and 'origin' (max-probability confidence)")
-        if config.alg_temp not in (None, 0, 0.0):
-            raise NotImplementedError("alg_temp > 0 (sampled transfer order) is not built")
-        if config.token_score_direction != "query_to_chunk":
-            raise NotImplementedError("only token_score_direction='query_to_chunk' is built")
+        # one generator per runtime for the sampled paths (temperature > 0, alg_temp > 0); seed it with `manual_seed`
+        self.sampling_generator: Optional[torch.Generator] = None
         if float(config.rope_scale_factor or 1.0) > 1.0:
             raise NotImplementedError("RoPE (YaRN) scaling is not built")
 
@@ -344,23 +375,37 @@ class FastDLLMParallelComp:
         raise ValueError(f"Unsupported attention layer mode: {layer_mode}")
 
     @staticmethod
-    def _mask_is_causal(mode: str) -> bool:
+    def _mask_kind(mode: str) -> str:
+        """"full" | "causal" | "query_to_chunk" (reference _attention_mask :982-1005)."""
         mode = (mode or "full").lower()
         if mode in {"full", "none"}:
-            return False
-        if mode == "causal":
-            return True
-        if mode == "query_to_chunk":
-            raise NotImplementedError("attention mask 'query_to_chunk' is not built")
+            return "full"
+        if mode in {"causal", "query_to_chunk"}:
+            return mode
         raise ValueError(f"Unsupported attention mask mode: {mode}")
+
+    def _mask_args(self, mode: str, *, rows_before_chunk: int, chunk_len: int, query_len: int) -> dict:
+        """Keyword arguments of `_forward_packed` that realise a reference mask over the NEW rows [.. ‖ chunk ‖ query] of every
+        packed sequence. "query_to_chunk" (reference _query_to_chunk_mask :963-980): everything is visible except that the
+        chunk's rows do not see the query's keys — a dense bool mask with sequence-local indices, shared by the sequences."""
+        kind = self._mask_kind(mode)
+        if kind == "causal":
+            return dict(causal=True)
+        if kind == "full" or query_len <= 0 or chunk_len <= 0:
+            return dict(causal=False)
+        rows = rows_before_chunk + chunk_len + query_len
+        visible = torch.ones((rows, rows), dtype=torch.bool, device=self.device)
+        visible[rows_before_chunk:rows_before_chunk + chunk_len, rows_before_chunk + chunk_len:] = False
+        return dict(causal=False, row_mask=visible)
 
     # ------------------------------------------------------------------------------------------------ model calls
     def _forward_packed(self, seqs_ids: Sequence[Sequence[int]], seqs_positions: Sequence[Sequence[int]], *, causal: bool,
                         cache: Optional[PagedCache] = None, ctx_len: int = 0, store_slots: Optional[Sequence[int]] = None,
                         logit_rows: Optional[Sequence[int]] = None, want_logits: bool = True, capture_layers=None,
                         ids_tensor: Optional[torch.Tensor] = None, store_after_attention: bool = False,
-                        store_unrotated_k: bool = False):
-        """One packed forward over several sequences; every sequence sees the first `ctx_len` tokens of `cache`."""
+                        store_unrotated_k: bool = False, row_mask: Optional[torch.Tensor] = None):
+        """One packed forward over several sequences; every sequence sees the first `ctx_len` tokens of `cache`. `row_mask`:
+        bool [rows, rows] visibility among the new rows, the same for every sequence (all of one length then)."""
         m = self.model
         flat_pos = [p for seq in seqs_positions for p in seq]
         if ids_tensor is None:
@@ -377,7 +422,7 @@ class FastDLLMParallelComp:
                          max_query_len=max(lens), slot_mapping=None if store_slots is None else m.i32(store_slots),
                          causal=causal, logit_rows=None if logit_rows is None else m.ids_tensor(logit_rows),
                          want_logits=want_logits, capture_qk_layers=capture_layers, store_after_attention=store_after_attention,
-                         store_unrotated_k=store_unrotated_k, **kwargs)
+                         store_unrotated_k=store_unrotated_k, new_row_mask=row_mask, **kwargs)
 
     # ------------------------------------------------------------------------------------------------ draft
     @torch.inference_mode()
@@ -415,28 +460,90 @@ class FastDLLMParallelComp:
                 logits, _ = self._forward_packed([[0] * draft_len], [block_pos], causal=False, cache=cache, ctx_len=cache.length,
                                                  ids_tensor=block)
                 # only the top-1 slot is transferred in a draft round: a threshold above any probability
-                ops.unmask_step(logits, block, mask_token_id=mask_id, threshold=2.0, last_logit=last_logit,
-                                shift=self.arch.logit_shift)
+                if self._custom_sampling():
+                    self._fill_most_confident(logits, block, last_logit, 1)
+                else:
+                    ops.unmask_step(logits, block, mask_token_id=mask_id, threshold=2.0, last_logit=last_logit,
+                                    shift=self.arch.logit_shift)
                 confirmed |= block != before
             return block.tolist(), confirmed.tolist()
         finally:
             cache.release()
 
-    def _fill_most_confident(self, logits: torch.Tensor, block: torch.Tensor, last_logit: Optional[torch.Tensor], count: int) -> int:
-        """Fill the `count` most confident MASK slots of `block` (in place) with their arg-max tokens: the transfer rule of the
-        fixed-step diffusion sampler and of the partial draft (reference :2548-2552, :2497-2504 with alg_temp 0). Confidence
-        and arg-max of every candidate slot come from the unmask kernel run on a scratch copy with a threshold no
-        probability reaches; ties at the cut are as unspecified as torch.topk's in the reference. Returns slots filled."""
+    # ---- samplers off the fused path -----------------------------------------------------------------------------------
+    def manual_seed(self, seed: int) -> None:
+        """Seed the draws of the sampled paths (temperature > 0, alg_temp > 0)."""
+        self.sampling_generator = torch.Generator(device=self.device)
+        self.sampling_generator.manual_seed(int(seed))
+
+    def _custom_sampling(self) -> bool:
+        cfg = self.config
+        return bool((cfg.temperature and cfg.temperature > 0) or cfg.top_p is not None or cfg.top_k is not None)
+
+    def _slot_candidates(self, logits: torch.Tensor, block: torch.Tensor, last_logit: Optional[torch.Tensor], alg: str):
+        """(is-MASK [n], confidence [masked], token [masked]) of one denoise forward under the configured sampler; `alg` picks the
+        confidence (reference :2469-2493: max probability for origin / confidence_threshold, top-1 minus top-2 for topk_margin,
+        negative entropy for anything else)."""
+        cfg = self.config
+        mask_index = block == self._mask_token_id()
+        if self.arch.logit_shift:
+            first = logits[:1] if last_logit is None else last_logit.reshape(1, -1)
+            logits = torch.cat([first, logits[:-1]], dim=0)
+        conf, tok = sample_tokens(logits[mask_index], temperature=float(cfg.temperature or 0.0), top_p=cfg.top_p, top_k=cfg.top_k,
+                                  margin_confidence=alg == "topk_margin",
+                                  neg_entropy=alg not in {"origin", "confidence_threshold", "topk_margin"}, generator=self.sampling_generator)
+        return mask_index, conf, tok
+
+    def _pick_first_token(self, last_logit: torch.Tensor) -> torch.Tensor:
+        cfg = self.config
+        return sample_tokens(last_logit.reshape(1, -1), temperature=float(cfg.temperature or 0.0), top_p=cfg.top_p, top_k=cfg.top_k,
+                             generator=self.sampling_generator)[1][0]
+
+    def _threshold_step_sampled(self, logits: torch.Tensor, block: torch.Tensor, last_logit: Optional[torch.Tensor]) -> int:
+        """The confidence-threshold accept rule (reference :2414-2440) over `_slot_candidates`: the most confident MASK slot
+        always, every other one whose confidence reaches the threshold. Returns the MASK slots left."""
+        mask_index, conf, tok = self._slot_candidates(logits, block, last_logit, "confidence_threshold")
+        n = int(conf.numel())
+        if n == 0:
+            return 0
+        accept = conf >= float(self.config.threshold)
+        accept[torch.argmax(conf)] = True
+        slots = torch.nonzero(mask_index).reshape(-1)
+        block[slots[accept]] = tok[accept]
+        return n - int(accept.sum().item())
+
+    def _fill_most_confident(self, logits: torch.Tensor, block: torch.Tensor, last_logit: Optional[torch.Tensor], count: int,
+                             alg: str = "origin") -> int:
+        """Fill `count` MASK slots of `block` (in place): the transfer rule of the fixed-step diffusion sampler and of the partial
+        draft (reference :2548-2552, :2497-2510). With the default sampler (greedy, max-probability confidence, alg_temp 0)
+        confidence and arg-max of every candidate slot come from the unmask kernel run on a scratch copy with a threshold no
+        probability reaches, and the `count` most confident are taken; ties at the cut are as unspecified as torch.topk's in
+        the reference. Otherwise the candidates come from `_slot_candidates` and, with alg_temp > 0, the slots are drawn
+        without replacement from softmax(confidence / alg_temp). Returns slots filled."""
         if count <= 0:
             return 0
-        scratch = block.clone()
-        counts, conf, x0 = ops.unmask_step(logits, scratch, mask_token_id=self._mask_token_id(), threshold=2.0, last_logit=last_logit,
-                                           shift=self.arch.logit_shift, return_details=True)
-        count = min(int(count), int(counts[0].item()))
+        cfg = self.config
+        alg_temp = float(cfg.alg_temp or 0.0)
+        if not self._custom_sampling() and alg in {"origin", "confidence_threshold"} and alg_temp == 0.0:
+            scratch = block.clone()
+            counts, conf, x0 = ops.unmask_step(logits, scratch, mask_token_id=self._mask_token_id(), threshold=2.0, last_logit=last_logit,
+                                               shift=self.arch.logit_shift, return_details=True)
+            count = min(int(count), int(counts[0].item()))
+            if count <= 0:
+                return 0
+            idx = torch.topk(conf, count).indices
+            block[idx] = x0[idx]
+            return count
+        mask_index, conf, tok = self._slot_candidates(logits, block, last_logit, alg)
+        count = min(int(count), int(conf.numel()))
         if count <= 0:
             return 0
-        idx = torch.topk(conf, count).indices
-        block[idx] = x0[idx]
+        if alg_temp == 0.0:
+            pick = torch.topk(conf, count).indices
+        else:
+            pick = torch.multinomial(torch.softmax(conf.float() / alg_temp, dim=-1), count, generator=self.sampling_generator)
+        slots = torch.nonzero(mask_index).reshape(-1)
+        block[slots[pick]] = tok[pick]
         return count
 
     @torch.inference_mode()
@@ -481,6 +588,8 @@ class FastDLLMParallelComp:
     def _first_block_token(self, last_logit: torch.Tensor) -> torch.Tensor:
         if not self.arch.logit_shift:
             raise NotImplementedError("un-shifted (LLaDA) block initialisation is not built")
+        if self._custom_sampling():
+            return self._pick_first_token(last_logit)
         return torch.argmax(last_logit)   # softmax is monotone: the arg-max of the logit
 
     def _selection_query_ids_with_score_target(self, prefix_ids, scoring_query_ids):
@@ -519,9 +628,7 @@ class FastDLLMParallelComp:
         """mean log p(label | prefix, chunk, earlier query) per chunk (reference :1314-1423): causal forward of
         [prefix‖chunk‖query‖draft] rows batched by chunk length, LM head on the label rows only, fused fp32 tail."""
         cfg = self.config
-        if score_token_count is not None:
-            raise NotImplementedError("score_token_count is not built")
-        if score_token_mask is None:
+        if score_token_count is None and score_token_mask is None:
             query_ids = self._window_query(query_ids, cfg.score_query_window)
         query_ids, prefix_ids = list(query_ids), list(prefix_ids)
         if not query_ids:
@@ -535,7 +642,6 @@ class FastDLLMParallelComp:
                 scores[idx] = float("-inf")
             else:
                 groups.setdefault(len(chunk), []).append((idx, chunk))
-        causal = self._mask_is_causal(cfg.score_attention_mask)
         batch_size = max(1, int(cfg.score_batch_size or 1))
         for c_len, group in groups.items():
             if score_token_mask is not None:
@@ -543,9 +649,11 @@ class FastDLLMParallelComp:
                     scores.update({idx: float("-inf") for idx, _ in group})
                     continue
                 local = [i for i, keep in enumerate(score_token_mask) if keep]
-            else:
+            elif score_token_count is None:
                 window = min(q_len, cfg.score_query_window or q_len)
                 local = list(range(q_len - window, q_len))
+            else:
+                local = list(range(min(q_len, max(0, int(score_token_count)))))    # the FIRST tokens of the query
             if not local:
                 scores.update({idx: float("-inf") for idx, _ in group})
                 continue
@@ -556,15 +664,72 @@ class FastDLLMParallelComp:
             labels = self.model.ids_tensor([query_ids[i] for i in local])
             row_len = p_len + c_len + q_len
             positions = list(range(row_len))
+            mask_args = self._mask_args(cfg.score_attention_mask, rows_before_chunk=p_len, chunk_len=c_len, query_len=q_len)
             for off in range(0, len(group), batch_size):
                 batch = group[off:off + batch_size]
                 rows = [prefix_ids + chunk + query_ids for _, chunk in batch]
                 logit_rows = [b * row_len + (p - 1) for b in range(len(batch)) for p in label_pos]  # label p reads logits[p-1]
-                logits, _ = self._forward_packed(rows, [positions] * len(batch), causal=causal, logit_rows=logit_rows)
+                logits, _ = self._forward_packed(rows, [positions] * len(batch), logit_rows=logit_rows, **mask_args)
                 vals = ops.self_information_scores(logits, labels, len(batch)).tolist()
                 for (idx, _), v in zip(batch, vals):
                     scores[idx] = v if math.isfinite(v) else float("-inf")
         return scores
+
+    def score_chunk_self_information(self, prefix_ids, chunk_ids, query_ids, score_token_count=None, score_token_mask=None) -> float:
+        """One chunk's score (reference :1258-1312): the batched scorer on a batch of one."""
+        return self.score_chunks_self_information_batched(prefix_ids, [list(chunk_ids)], query_ids, score_token_count=score_token_count,
+                                                          score_token_mask=score_token_mask).get(0, float("-inf"))
+
+    @torch.inference_mode()
+    def score_chunk_self_information_joint_chunks(self, prefix_ids, candidate_chunks, target_index: int, query_ids,
+                                                  score_token_count=None, score_token_mask=None) -> float:
+        """Score chunk `target_index` with every other chunk in front of it in the same forward: rows
+        [prefix ‖ other chunks in order ‖ target chunk ‖ query], labels as in the single-chunk score (reference :1425-1505)."""
+        cfg = self.config
+        if score_token_count is None and score_token_mask is None:
+            query_ids = self._window_query(query_ids, cfg.score_query_window)
+        query_ids, prefix_ids = list(query_ids), list(prefix_ids)
+        if not candidate_chunks or not query_ids or not 0 <= target_index < len(candidate_chunks):
+            return float("-inf")
+        target = list(candidate_chunks[target_index])
+        if not target:
+            return float("-inf")
+        context = [t for i, c in enumerate(candidate_chunks) if i != target_index for t in c] + target
+        joint = prefix_ids + context + query_ids
+        p_len, c_len, q_len = len(prefix_ids), len(context), len(query_ids)
+        if score_token_mask is not None:
+            if len(score_token_mask) != q_len:
+                return float("-inf")
+            local = [i for i, keep in enumerate(score_token_mask) if keep]
+        elif score_token_count is None:
+            window = min(q_len, cfg.score_query_window or q_len)
+            local = list(range(q_len - window, q_len))
+        else:
+            local = list(range(min(q_len, max(0, int(score_token_count)))))
+        if not local:
+            return float("-inf")
+        label_pos = [p_len + c_len + i for i in local]
+        if min(label_pos) <= 0:
+            return float("-inf")
+        mask_args = self._mask_args(cfg.score_attention_mask, rows_before_chunk=p_len, chunk_len=c_len, query_len=q_len)
+        logits, _ = self._forward_packed([joint], [list(range(len(joint)))], logit_rows=[p - 1 for p in label_pos], **mask_args)
+        value = float(ops.self_information_scores(logits, self.model.ids_tensor([query_ids[i] for i in local]), 1)[0].item())
+        return value if math.isfinite(value) else float("-inf")
+
+    @torch.inference_mode()
+    def score_chunk_next_block_logits(self, prefix_ids, chunk_ids, query_ids) -> float:
+        """Mean fp32 max-probability of `score_draft_tokens` MASK slots appended to [prefix ‖ chunk ‖ query], one bidirectional
+        forward (reference :1507-1529; Dream reads slot j at the logit row before it)."""
+        cfg = self.config
+        draft_len = max(1, int(cfg.score_draft_tokens or cfg.block_length or 1))
+        if not chunk_ids or not query_ids:
+            return float("-inf")
+        joint = list(prefix_ids) + list(chunk_ids) + list(query_ids) + [self._mask_token_id()] * draft_len
+        first = len(joint) - draft_len
+        shift = 1 if self.arch.logit_shift else 0
+        rows = [max(0, first + j - shift) for j in range(draft_len)]
+        logits, _ = self._forward_packed([joint], [list(range(len(joint)))], causal=False, logit_rows=rows)
+        return float(torch.softmax(logits.float(), dim=-1).max(dim=-1).values.mean().item())
 
     def select_chunks(self, prefix_ids, candidate_chunks, scoring_query_ids):
         """(selected ascending, scores, selection query ids, label mask) — reference :1857-1953."""
@@ -577,12 +742,40 @@ class FastDLLMParallelComp:
             if cfg.topk_chunks > 0:
                 selected = selected[:cfg.topk_chunks]
             return selected, {}, selection, mask
-        if cfg.score_mode not in {"self_information", "draft_self_information"}:
-            raise NotImplementedError(f"score_mode={cfg.score_mode!r} is not built")
-        if cfg.score_context_mode != "single_chunk":
-            raise NotImplementedError(f"score_context_mode={cfg.score_context_mode!r} is not built")
-        scores = self.score_chunks_self_information_batched(prefix_ids, candidate_chunks, selection, score_token_count=count,
-                                                            score_token_mask=mask)
+        scores: Dict[int, float] = {}
+        if cfg.score_mode in {"self_information", "draft_self_information"}:
+            if cfg.score_context_mode == "single_chunk":
+                # the batched and the one-by-one scorer of the reference compute the same value per chunk; batch size 1 packs one
+                scores = self.score_chunks_self_information_batched(prefix_ids, candidate_chunks, selection, score_token_count=count,
+                                                                    score_token_mask=mask)
+            elif cfg.score_context_mode == "joint_chunks_target_last":
+                for idx in range(len(candidate_chunks)):
+                    scores[idx] = self.score_chunk_self_information_joint_chunks(prefix_ids, candidate_chunks, idx, selection,
+                                                                                 score_token_count=count, score_token_mask=mask)
+            else:
+                raise ValueError(f"Unsupported score_context_mode: {cfg.score_context_mode}")
+        elif cfg.score_mode == "per_chunk_draft_self_information":
+            for idx, chunk in enumerate(candidate_chunks):
+                per_chunk_query = list(scoring_query_ids)
+                if cfg.score_draft_tokens > 0:
+                    per_chunk_query += self.generate_from_cache(
+                        past_key_values=None, cache_positions=[], query_ids=list(prefix_ids) + list(chunk) + list(scoring_query_ids),
+                        query_rope_start=0, max_new_tokens=int(cfg.score_draft_tokens), diffusion_steps=int(cfg.score_draft_steps or 1),
+                        force_diffusion=bool(cfg.score_draft_fixed_steps))
+                scores[idx] = self.score_chunk_self_information(prefix_ids, chunk, per_chunk_query)
+        elif cfg.score_mode == "next_block_logits":
+            for idx, chunk in enumerate(candidate_chunks):
+                scores[idx] = self.score_chunk_next_block_logits(prefix_ids, chunk, scoring_query_ids)
+        elif cfg.score_mode == "attention":
+            for idx, chunk in enumerate(candidate_chunks):
+                token_scores = self.query_attention_token_scores(
+                    prefix_ids, chunk, selection, query_window=cfg.attention_query_window, layer_window=cfg.attention_score_layers,
+                    layer_mode="last", reduce_mode=cfg.token_score_reduce, pooling=cfg.token_score_pooling,
+                    pool_kernel=cfg.token_score_pool_kernel, head_reduce=cfg.token_score_head_reduce, layer_reduce=cfg.token_score_layer_reduce)
+                scores[idx] = float(token_scores.mean().item()) if token_scores.numel() else float("-inf")
+        else:
+            raise ValueError(f"Unsupported score_mode: {cfg.score_mode}")
+        scores = {i: (v if math.isfinite(v) else float("-inf")) for i, v in scores.items()}
         dense = torch.tensor([scores.get(i, float("-inf")) for i in range(len(candidate_chunks))], dtype=torch.float32,
                              device=self.device)
         sel, cnt = ops.topk_chunks(dense, int(cfg.topk_chunks), bool(cfg.keep_first_chunk))
@@ -598,33 +791,108 @@ class FastDLLMParallelComp:
 
     # ------------------------------------------------------------------------------------------------ token eviction
     @torch.inference_mode()
-    def _chunk_head_scores(self, prefix_ids, chunk_ids, query_ids) -> Optional[Tuple[torch.Tensor, List[int]]]:
-        """fp32 [selected layers, Hq, chunk_len] query→chunk attention mass of the last `token_score_query_window` query
-        tokens (reference query_attention_token_scores :1531-1637, via the fused scorer instead of eager attention)."""
+    def _chunk_head_scores(self, prefix_ids, chunk_ids, query_ids, *, query_window=None, layer_window=None, layer_mode=None,
+                           reduce_mode=None) -> Optional[Tuple[torch.Tensor, List[int]]]:
+        """fp32 [selected layers, Hq, chunk_len] attention mass between the last `query_window` query tokens and the chunk's
+        tokens (reference query_attention_token_scores :1531-1637 / _chunk_attention_head_scores :1639-1667). Direction
+        query→chunk comes from the fused scorer on the layer's rotated (q, k); chunk→query (and their sum, "bidirectional")
+        needs the chunk rows' own softmax and is computed from the same (q, k) with device-side matrix products."""
         cfg = self.config
-        query_ids = self._window_query(query_ids, cfg.token_score_query_window)
+        query_ids = self._window_query(query_ids, cfg.token_score_query_window if query_window is None else query_window)
         if not chunk_ids or not query_ids:
             return None
         prefix = list(prefix_ids) if cfg.token_score_include_prefix else []
         joint = prefix + list(chunk_ids) + list(query_ids)
-        layers = self._select_attention_layer_indices(self.arch.num_hidden_layers, cfg.token_score_layers, cfg.token_score_layer_mode)
+        layers = self._select_attention_layer_indices(self.arch.num_hidden_layers,
+                                                      cfg.token_score_layers if layer_window is None else layer_window,
+                                                      cfg.token_score_layer_mode if layer_mode is None else layer_mode)
         if not layers:
             return None
-        causal = self._mask_is_causal(cfg.token_attention_mask)
-        _, captured = self._forward_packed([joint], [list(range(len(joint)))], causal=causal, want_logits=False, capture_layers=layers)
-        per_layer = [ops.query_to_chunk_attention_scores(captured[l][0], captured[l][1], prefix_len=len(prefix), chunk_len=len(chunk_ids),
-                                                         query_len=len(query_ids), scale=self.model.scale,
-                                                         reduce_mode=cfg.token_score_reduce, attention_mask=cfg.token_attention_mask)
-                     for l in layers]
+        p_len, c_len, q_len = len(prefix), len(chunk_ids), len(query_ids)
+        reduce_mode = cfg.token_score_reduce if reduce_mode is None else reduce_mode
+        mask_args = self._mask_args(cfg.token_attention_mask, rows_before_chunk=p_len, chunk_len=c_len, query_len=q_len)
+        _, captured = self._forward_packed([joint], [list(range(len(joint)))], want_logits=False, capture_layers=layers, **mask_args)
+        direction = cfg.token_score_direction
+        per_layer = []
+        for l in layers:
+            q, k = captured[l]
+            parts = []
+            if direction in {"query_to_chunk", "bidirectional"}:
+                parts.append(ops.query_to_chunk_attention_scores(q, k, prefix_len=p_len, chunk_len=c_len, query_len=q_len, scale=self.model.scale,
+                                                                 reduce_mode=reduce_mode, attention_mask=cfg.token_attention_mask))
+            if direction in {"chunk_to_query", "bidirectional"}:
+                parts.append(self._chunk_to_query_mass(q, k, p_len, c_len, q_len, reduce_mode, mask_args))
+            per_layer.append(parts[0] if len(parts) == 1 else parts[0] + parts[1])
         return torch.stack(per_layer, dim=0).contiguous(), layers
 
-    def _check_reductions(self):
+    def _chunk_to_query_mass(self, q: torch.Tensor, k: torch.Tensor, p_len: int, c_len: int, q_len: int, reduce_mode: str, mask_args: dict):
+        """fp32 [Hq, chunk_len]: attention probability that each chunk row puts on the query's keys, summed (or averaged) over
+        those keys, under the forward's own mask. Zero under the causal and query_to_chunk masks (chunk rows do not see the query)."""
+        hq, hkv = self.arch.num_attention_heads, self.arch.num_key_value_heads
+        if mask_args.get("causal") or mask_args.get("row_mask") is not None:
+            return torch.zeros((hq, c_len), dtype=torch.float32, device=self.device)
+        rows = q[p_len:p_len + c_len].float().transpose(0, 1)                              # [Hq, C, D]
+        keys = k.float().transpose(0, 1).repeat_interleave(hq // hkv, dim=0)               # [Hq, L, D]
+        prob = torch.softmax(torch.matmul(rows, keys.transpose(1, 2)) * self.model.scale, dim=-1)
+        part = prob[:, :, p_len + c_len:p_len + c_len + q_len]
+        return part.mean(dim=2) if reduce_mode == "mean" else part.sum(dim=2)
+
+    @staticmethod
+    def _pool_head_scores(head_scores: torch.Tensor, pooling: str, pool_kernel: int) -> torch.Tensor:
+        """avg / max pooling along the chunk axis with stride 1 and half-kernel zero / -inf padding (reference :1607-1617)."""
+        if pooling == "none" or head_scores.shape[-1] == 0:
+            return head_scores
+        kernel = max(1, min(int(pool_kernel), head_scores.shape[-1]))
+        flat = head_scores.reshape(-1, 1, head_scores.shape[-1])
+        if pooling == "avgpool":
+            flat = torch.nn.functional.avg_pool1d(flat, kernel_size=kernel, padding=kernel // 2, stride=1)
+        elif pooling == "maxpool":
+            flat = torch.nn.functional.max_pool1d(flat, kernel_size=kernel, padding=kernel // 2, stride=1)
+        else:
+            raise ValueError(f"Unsupported token_score_pooling: {pooling}")
+        return flat[..., :head_scores.shape[-1]].reshape(head_scores.shape)
+
+    @torch.inference_mode()
+    def query_attention_token_scores(self, prefix_ids, chunk_ids, query_ids, *, query_window: int, layer_window: int, layer_mode: str,
+                                     reduce_mode: str, pooling: Optional[str] = None, pool_kernel: Optional[int] = None,
+                                     head_reduce: Optional[str] = None, layer_reduce: Optional[str] = None) -> torch.Tensor:
+        """fp32 [chunk_len] token scores: per selected layer pool each head's scores along the chunk, reduce over heads, then
+        over layers (reference :1531-1637). Empty tensor when nothing can be scored."""
+        cfg = self.config
+        scored = self._chunk_head_scores(prefix_ids, chunk_ids, query_ids, query_window=query_window, layer_window=layer_window,
+                                         layer_mode=layer_mode, reduce_mode=reduce_mode)
+        if scored is None:
+            return torch.empty(0, device=self.device)
+        pooling = (pooling or cfg.token_score_pooling or "none").lower()
+        head_reduce = (head_reduce or cfg.token_score_head_reduce or "sum").lower()
+        layer_reduce = (layer_reduce or cfg.token_score_layer_reduce or "mean").lower()
+        pooled = self._pool_head_scores(scored[0], pooling, int(pool_kernel or cfg.token_score_pool_kernel or 1))
+        if head_reduce == "mean":
+            per_layer = pooled.mean(dim=1)
+        elif head_reduce == "sum":
+            per_layer = pooled.sum(dim=1)
+        elif head_reduce == "max":
+            per_layer = pooled.max(dim=1).values
+        else:
+            raise ValueError(f"Unsupported token_score_head_reduce: {head_reduce}")
+        if layer_reduce == "mean":
+            return per_layer.mean(dim=0)
+        if layer_reduce == "sum":
+            return per_layer.sum(dim=0)
+        if layer_reduce == "max":
+            return per_layer.max(dim=0).values
+        raise ValueError(f"Unsupported token_score_layer_reduce: {layer_reduce}")
+
+    def _fused_reductions(self) -> Optional[int]:
+        """The pool kernel width when the configured reductions are the ones the fused eviction kernel computes (max-pooling or
+        none, heads summed, layers averaged); None when they have to be applied with tensor ops first."""
         cfg = self.config
         pooling = (cfg.token_score_pooling or "none").lower()
-        if pooling not in {"none", "maxpool"}:
-            raise NotImplementedError(f"token_score_pooling={pooling!r} is not built (maxpool / none)")
-        if (cfg.token_score_head_reduce or "sum").lower() != "sum" or (cfg.token_score_layer_reduce or "mean").lower() != "mean":
-            raise NotImplementedError("only head_reduce='sum' and layer_reduce='mean' are built")
+        if pooling not in {"none", "maxpool", "avgpool"}:
+            raise ValueError(f"Unsupported token_score_pooling: {pooling}")
+        if pooling == "avgpool" or (cfg.token_score_head_reduce or "sum").lower() != "sum" \
+                or (cfg.token_score_layer_reduce or "mean").lower() != "mean":
+            return None
         return 1 if pooling == "none" else int(cfg.token_score_pool_kernel or 1)
 
     def _keep_positions_for_chunk(self, prefix_ids, chunk_ids, query_ids) -> List[int]:
@@ -632,14 +900,22 @@ class FastDLLMParallelComp:
         capacity, chunk_len = int(cfg.token_capacity or 0), len(chunk_ids)
         if capacity <= 0 or chunk_len <= capacity:
             return list(range(chunk_len))
-        pool_kernel = self._check_reductions()
-        scored = self._chunk_head_scores(prefix_ids, chunk_ids, query_ids)
+        pool_kernel = self._fused_reductions()
         force_bos = bool(cfg.force_keep_chunk_bos and cfg.chunk_bos)
-        if scored is None:
+        if pool_kernel is not None:
+            scored = self._chunk_head_scores(prefix_ids, chunk_ids, query_ids)
+            head_scores, n_heads = (None, 0) if scored is None else (scored[0], self.arch.num_key_value_heads)
+        else:
+            # reductions the fused kernel does not compute: reduce with tensor ops, then let the kernel rank one "head" of one "layer"
+            token_scores = self.query_attention_token_scores(
+                prefix_ids, chunk_ids, query_ids, query_window=cfg.token_score_query_window, layer_window=cfg.token_score_layers,
+                layer_mode=cfg.token_score_layer_mode, reduce_mode=cfg.token_score_reduce)
+            head_scores, n_heads, pool_kernel = (None, 0, 1) if token_scores.numel() != chunk_len else (token_scores.reshape(1, 1, -1).contiguous(), 1, 1)
+        if head_scores is None:
             head = capacity // 2
             keep = sorted(set(list(range(head)) + list(range(chunk_len - (capacity - head), chunk_len))))
         else:
-            keep = ops.evict_select(scored[0], num_kv_heads=self.arch.num_key_value_heads, keep_count=min(max(1, capacity), chunk_len),
+            keep = ops.evict_select(head_scores, num_kv_heads=n_heads, keep_count=min(max(1, capacity), chunk_len),
                                     pool_kernel=pool_kernel, per_head=False, force_keep_first=force_bos,
                                     keep_high=cfg.token_score_keep == "high")[0].tolist()
         if force_bos and chunk_len > 0:
@@ -657,9 +933,16 @@ class FastDLLMParallelComp:
         if capacity <= 0 or chunk_len <= capacity:
             base = torch.arange(chunk_len, device=self.device, dtype=torch.long)
             return [base.unsqueeze(0).expand(hkv, -1).clone() for _ in range(n_layers)]
-        pool_kernel = self._check_reductions()
+        pool_kernel = self._fused_reductions()
         keep_count = min(capacity, chunk_len)
         scored = self._chunk_head_scores(prefix_ids, chunk_ids, query_ids)
+        pooling = (cfg.token_score_pooling or "none").lower()
+        if scored is not None and pooling == "avgpool":
+            # per-head lists only pool and average the heads of a KV group (reference :1741-1760): pool here, group in the kernel
+            scored = (self._pool_head_scores(scored[0], pooling, int(cfg.token_score_pool_kernel or 1)).contiguous(), scored[1])
+            pool_kernel = 1
+        elif pool_kernel is None:
+            pool_kernel = 1 if pooling == "none" else int(cfg.token_score_pool_kernel or 1)
         if scored is None:
             head = keep_count // 2
             fb = torch.tensor(sorted(set(list(range(head)) + list(range(chunk_len - (keep_count - head), chunk_len))))[:keep_count],
@@ -677,15 +960,20 @@ class FastDLLMParallelComp:
     # ------------------------------------------------------------------------------------------------ block denoising
     def _denoise_blocks(self, cache: PagedCache, *, suffix_pos_start: int, last_logit: torch.Tensor,
                         first_token: Optional[torch.Tensor], tail_in_cache: int, max_new: int,
-                        fixed_steps_per_block: Optional[int] = None) -> List[int]:
+                        fixed_steps_per_block: Optional[int] = None, confidence_alg: Optional[str] = None) -> List[int]:
         """Fast-dLLM dual-cache block loop over the paged cache (reference :2932-2998, :2399-2441): `model.denoise_blocks`
         with this runtime's settings — softmax in the model dtype, as the eval class computes it."""
         if self.config.generation_position_mode != "after_query":
             raise ValueError(f"Unsupported generation_position_mode: {self.config.generation_position_mode}")
+        alg = confidence_alg or self.config.alg
+        sampled = self._custom_sampling()
         return denoise_blocks(self.model, cache, suffix_pos_start=suffix_pos_start, last_logit=last_logit, first_token=first_token,
                               tail_in_cache=tail_in_cache, max_new=max_new, block_length=self.block_length, mask_id=self._mask_token_id(),
                               threshold=float(self.config.threshold), softmax_dtype=None, use_graph=bool(self.config.decode_cuda_graph),
-                              fixed_steps_per_block=fixed_steps_per_block, fill_most_confident=self._fill_most_confident)
+                              fixed_steps_per_block=fixed_steps_per_block,
+                              fill_most_confident=lambda lg, blk, last, count: self._fill_most_confident(lg, blk, last, count, alg=alg),
+                              pick_first_token=self._pick_first_token if sampled else None,
+                              threshold_step=self._threshold_step_sampled if sampled else None)
 
     # ------------------------------------------------------------------------------------------------ chunk-local caches
     def _prefill_one_chunk(self, cache: "PagedCache", dst: int, prefix_ids, chunk, order: int, ci: int, evict_q, window_q):
@@ -695,7 +983,6 @@ class FastDLLMParallelComp:
         cfg = self.config
         p_len = len(prefix_ids)
         per_head = cfg.token_eviction_granularity == "per_head"
-        causal = cfg.cache_build_mode == "chunk_query" and self._mask_is_causal(cfg.token_attention_mask)
         c_start = self._chunk_rope_start(p_len, order, ci)
         c_pos = self._range_positions(c_start, len(chunk))
         if per_head:
@@ -711,14 +998,18 @@ class FastDLLMParallelComp:
             tq_start = self._chunk_query_rope_start(p_len, c_start, len(chunk))
             rows_ids = chunk + window_q
             rows_pos = c_pos + self._range_positions(tq_start, len(window_q))
+            # the prefix is cached context (always visible); the mask applies among the new rows [chunk ‖ query window]
+            mask_args = self._mask_args(cfg.token_attention_mask, rows_before_chunk=0, chunk_len=len(chunk), query_len=len(window_q))
+        else:
+            mask_args = dict(causal=False)
         if per_head and keep_ph and kept < len(chunk):
             # all chunk rows go to a staging area behind the destination, K un-rotated; a per-head compaction moves
             # the kept ones; then kept row j of EVERY head is rotated to the j-th chunk position, as the reference's
             # model does when it rotates cached keys at read time with the compacted position list (:2284-2288)
             stage = dst + kept
             slots = cache.slots(stage, len(chunk)) + [-1] * (len(rows_ids) - len(chunk))
-            self._forward_packed([rows_ids], [rows_pos], causal=causal, cache=cache if p_len else None, ctx_len=p_len,
-                                 store_slots=slots, want_logits=False, store_unrotated_k=True)
+            self._forward_packed([rows_ids], [rows_pos], cache=cache if p_len else None, ctx_len=p_len,
+                                 store_slots=slots, want_logits=False, store_unrotated_k=True, **mask_args)
             for layer in range(self.arch.num_hidden_layers):
                 for kv in self.model.layer_cache(layer):
                     ops.compact_pages_per_head(kv, cache.page_ids, cache.page_ids, keep_ph[layer] + stage,
@@ -729,8 +1020,8 @@ class FastDLLMParallelComp:
             keep_set = set(keep_union)
             next_slot = iter(cache.slots(dst, kept))
             slots = [next(next_slot) if i in keep_set else -1 for i in range(len(chunk))] + [-1] * (len(rows_ids) - len(chunk))
-            self._forward_packed([rows_ids], [rows_pos], causal=causal, cache=cache if p_len else None, ctx_len=p_len,
-                                 store_slots=slots, want_logits=False)
+            self._forward_packed([rows_ids], [rows_pos], cache=cache if p_len else None, ctx_len=p_len,
+                                 store_slots=slots, want_logits=False, **mask_args)
             kept_pos = [c_pos[i] for i in keep_union]
         return kept, kept_pos, keep_union, c_start
 
@@ -811,7 +1102,8 @@ class FastDLLMParallelComp:
                                              store_slots=cache.slots(base, len(query_ids)), logit_rows=[len(query_ids) - 1])
             cache.length = base + len(query_ids)
             return self._denoise_blocks(cache, suffix_pos_start=query_rope_start + len(query_ids), last_logit=logits[0],
-                                        first_token=None, tail_in_cache=0, max_new=max_new, fixed_steps_per_block=fixed_steps)
+                                        first_token=None, tail_in_cache=0, max_new=max_new, fixed_steps_per_block=fixed_steps,
+                                        confidence_alg="origin" if force_diffusion else None)
         finally:
             if own:
                 cache.release()
@@ -911,7 +1203,7 @@ class FastDLLMParallelComp:
                 self.model.rope_rows(cache.page_ids, 0, stored_pos)
             else:
                 suffix_start = full_q_start + len(query_ids)
-            first = torch.argmax(last_logit) if (with_masks and self.arch.logit_shift) else None
+            first = self._first_block_token(last_logit) if (with_masks and self.arch.logit_shift) else None
             fixed_steps = None
             if cfg.alg != "confidence_threshold":     # reference :2927-2929, :2977-2985
                 fixed_steps = max(1, math.ceil(int(self.diffusion_steps) / max(1, math.ceil(max_new / self.block_length))))

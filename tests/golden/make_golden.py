@@ -223,6 +223,35 @@ VARIANTS128 = {
     "evict_per_head_cap128_full_prompt": dict(README_FLAGS, token_capacity=128, token_eviction_granularity="per_head"),
 }
 
+# flags off the README path (fp32 toy): score context / mask / mode, pooling and reductions of the token scores, score direction,
+# deterministic sampler options (top-k / top-p at temperature 0, margin and entropy confidence with fixed-step diffusion)
+_CHUNK_QUERY = dict(cache_build_mode="chunk_query", chunk_position_mode="reuse", query_position_mode="after_reused_window")
+FLAG_VARIANTS = {
+    "score_joint_chunks_target_last": dict(README_FLAGS, score_context_mode="joint_chunks_target_last"),
+    "score_mask_query_to_chunk": dict(README_FLAGS, score_attention_mask="query_to_chunk"),
+    "score_mask_full": dict(README_FLAGS, score_attention_mask="full"),
+    "score_mode_self_information_window16": dict(README_FLAGS, score_mode="self_information", score_query_window=16),
+    "score_mode_next_block_logits": dict(README_FLAGS, score_mode="next_block_logits"),
+    "score_mode_attention": dict(README_FLAGS, score_mode="attention"),
+    "score_mode_per_chunk_draft": dict(README_FLAGS, score_mode="per_chunk_draft_self_information"),
+    "evict_avgpool_head_max_layer_sum": dict(README_FLAGS, token_capacity=128, token_score_pooling="avgpool", token_score_head_reduce="max",
+                                             token_score_layer_reduce="sum"),
+    "evict_nopool_head_mean_layer_max_keep_low": dict(README_FLAGS, token_capacity=128, token_score_pooling="none",
+                                                      token_score_head_reduce="mean", token_score_layer_reduce="max", token_score_keep="low"),
+    "evict_per_head_avgpool_chunk_query": dict(README_FLAGS, token_capacity=128, token_eviction_granularity="per_head",
+                                               token_score_pooling="avgpool", **_CHUNK_QUERY),
+    "evict_bidirectional_full_mask": dict(README_FLAGS, token_capacity=128, token_score_direction="bidirectional", token_attention_mask="full"),
+    "evict_query_to_chunk_mask_chunk_query": dict(README_FLAGS, token_capacity=128, token_attention_mask="query_to_chunk", **_CHUNK_QUERY),
+    "evict_use_generated_query": dict(README_FLAGS, token_capacity=128, token_score_use_generated=True),
+    "sample_top_k_top_p_greedy": dict(README_FLAGS, top_k=8, top_p=0.7),
+    # temperature > 0 draws from a categorical; with one candidate left per slot the draw is deterministic, every slot has
+    # confidence 1 and a block fills in one step. Three draft rounds fill all four draft slots: WHICH of several slots of
+    # confidence exactly 1 a single round takes is torch.topk's unspecified choice among ties
+    "sample_temperature_top_k_1": dict(README_FLAGS, temperature=0.7, top_k=1, score_draft_partial_rounds=3),
+    "alg_topk_margin": dict(README_FLAGS, alg="topk_margin", diffusion_steps=8),
+    "alg_entropy": dict(README_FLAGS, alg="entropy", diffusion_steps=8),
+}
+
 
 def main():
     ap = argparse.ArgumentParser()
@@ -230,7 +259,8 @@ def main():
                     help="root of the reference checkout (or set PDLLM_REFERENCE_ROOT)")
     ap.add_argument("--out", default=os.path.join(HERE, "toy_reference.json"))
     ap.add_argument("--out128", default=os.path.join(HERE, "toy128_reference.json"))
-    ap.add_argument("--only", choices=["toy", "toy128"], default=None)
+    ap.add_argument("--out-flags", default=os.path.join(HERE, "toy_flags_reference.json"))
+    ap.add_argument("--only", choices=["toy", "toy128", "flags"], default=None)
     args = ap.parse_args()
     torch.manual_seed(0)
     torch.set_num_threads(max(1, os.cpu_count() or 1))
@@ -252,6 +282,18 @@ def main():
             with open(args.out, "w") as handle:
                 json.dump(golden, handle)
             print("wrote", args.out, os.path.getsize(args.out), "bytes")
+        if args.only in (None, "flags"):
+            context, query = toy_inputs()
+            golden = {"config": dict(TOY), "flags": dict(README_FLAGS), "context_seed": 0, "runs": {}}
+            ckpt = os.path.join(tmp, "ckpt_toy_flags")
+            write_toy_checkpoint(ckpt)
+            for name, flags in FLAG_VARIANTS.items():
+                _, runtime = load_reference(args.reference, ckpt, **flags)
+                golden["runs"][name] = dict(flags=flags, **record_run(runtime, context, query))
+                print(name, golden["runs"][name]["selected_chunk_indices"], golden["runs"][name]["sequences"][:8], flush=True)
+            with open(args.out_flags, "w") as handle:
+                json.dump(golden, handle)
+            print("wrote", args.out_flags, os.path.getsize(args.out_flags), "bytes")
         if args.only in (None, "toy128"):
             context, query = toy_inputs(vocab=TOY128["vocab_size"])
             golden = {"config": dict(TOY128), "flags": dict(README_FLAGS), "context_seed": 0, "runs": {}}

@@ -419,6 +419,26 @@ def test_engine_to_engine_copy_survives_reuse_of_the_source_pages(engine, ckpt):
     assert other._prefix_cache.num_free_pages == 16
 
 
+def test_batched_decode_of_several_blocks_equals_one_by_one(engine):
+    """Records of three blocks (80 new tokens: 32 + 32 + 16) with different prompt lengths, one of them a prefix-cache hit whose
+    last prompt page is shared: decoded in shared steps they give the ids and forward counts of decoding each on its own."""
+    prompts = [_prompt(600, seed=41), _prompt(300, seed=42), _prompt(512, seed=43)]
+    free0 = engine._prefix_cache.num_free_pages
+    single = [engine.decode_from_pd_record(engine.prefill_to_pd_record(p, max_new_tokens=80), max_new_tokens=80) for p in prompts]
+    records = [engine.prefill_to_pd_record(p, max_new_tokens=80) for p in prompts]
+    assert all(r.cached_prefix is not None for r in records)
+    batched = engine.decode_from_pd_records(records, max_new_tokens=80)
+    for one, many in zip(single, batched):
+        assert len(many.token_ids) == len(one.token_ids)
+        assert many.token_ids == one.token_ids and many.n_diff_steps == one.n_diff_steps
+    from prefilling_dllm_b200 import ops
+
+    ops.check_status(engine.device)
+    while engine._prefix_cache.evict_one():
+        pass
+    assert engine._prefix_cache.num_free_pages == free0
+
+
 def test_batched_decode_equals_one_by_one(engine):
     """Three requests with different prompt lengths denoised in shared steps: same ids and step counts as decoding each
     record on its own; every page comes back."""
