@@ -572,15 +572,15 @@ def denoise_step_breakdown(model, rows: int, ctx: int, device):
 
     def linears():
         for w in model.layers:
-            ops.linear(h, w["wqkv"], w["bqkv"]); ops.linear(attn, w["wo"]); ops.linear(h, w["wgu"], silu_mul_interleaved=True); ops.linear(hi, w["wd"])
-        ops.linear(h, model.lm_head)
+            ops.linear(h, w["wqkv"], w["bqkv"], weights_at_rest=True); ops.linear(attn, w["wo"], weights_at_rest=True)
+            ops.linear(h, w["wgu"], silu_mul_interleaved=True, weights_at_rest=True); ops.linear(hi, w["wd"], weights_at_rest=True)
+        ops.linear(h, model.lm_head, weights_at_rest=True)
 
     def row_ops():
         for li in range(layers):
             kc, vc = model.layer_cache(li)
             ops.add_rmsnorm(h, model.layers[li]["ln1"], a.rms_norm_eps, h)
-            ops.rope_inplace(qkv[:, : hq + hkv], cos.reshape(-1, d), sin.reshape(-1, d))
-            ops.store_kvcache_unified_layout(qkv[:, hq:hq + hkv], qkv[:, hq + hkv:], kc, vc, slots, "diffusion_lm")
+            ops.rope_store(qkv, cos.reshape(-1, d), sin.reshape(-1, d), hq, hkv, kc, vc, slots)
             ops.add_rmsnorm(h, model.layers[li]["ln2"], a.rms_norm_eps, h)
         ops.add_rmsnorm(h, model.final_norm, a.rms_norm_eps)
 
@@ -603,9 +603,9 @@ def denoise_step_breakdown(model, rows: int, ctx: int, device):
     total = t_lin + t_rows + t_attn + t_unm
     return {
         "rows": rows, "cached_tokens": ctx, "sum_of_groups_ms": total,
-        "groups_ms": {"linear_sm100_kernel": t_lin, "attention (+ split-KV merge)": t_attn, "rmsnorm / rope / page write": t_rows, "unmask_kernel": t_unm},
+        "groups_ms": {"linear_sm100_kernel": t_lin, "attention (+ split-KV merge)": t_attn, "rmsnorm / rope + page write": t_rows, "unmask_kernel": t_unm},
         "share": {"linear_sm100_kernel": t_lin / total, "attention": t_attn / total, "row_ops": t_rows / total, "unmask": t_unm / total},
-        "launches": {"linear_sm100_kernel": n_linear, "attention": layers, "row_ops": 4 * layers + 1, "unmask": 1},
+        "launches": {"linear_sm100_kernel": n_linear, "attention": layers, "row_ops": 3 * layers + 1, "unmask": 1},
         "linear_bytes": weight_bytes + act_bytes, "linear_ms": t_lin, "linear_launches": n_linear,
         "attention_kv_gbs": kv_bytes / (t_attn * 1e-3) / 1e9,
     }

@@ -23,7 +23,7 @@
 extern "C" {
 #endif
 
-#define PDLLM_ABI_VERSION 4
+#define PDLLM_ABI_VERSION 5
 
 /* element types of floating-point tensors */
 #define PDLLM_F32 0
@@ -311,6 +311,15 @@ int pdllm_add_rmsnorm(void* x, const void* delta, const void* weight, void* out,
  * cos_tab / sin_tab: [n_tokens, head_dim] in the same dtype (cat(freqs, freqs) layout) */
 int pdllm_rope_inplace(void* x, const void* cos_tab, const void* sin_tab, int64_t n_tokens, int num_heads, int head_dim,
                        int64_t row_stride, int dtype, void* stream);
+/* RoPE of the q and k heads of a fused projection output qkv [n_tokens, num_q_heads + 2 num_kv_heads, head_dim] (row stride in
+ * elements) in place AND the page write of its k and v heads, one launch (bf16 / fp16, head_dim a multiple of 16):
+ * replaces the pair  q, k = self.rotary_emb(positions, q, k)          prefilling_dllm_engine/prefilling_dllm/models/dream.py:75-76
+ *                    store_kvcache_unified_layout(k, v, k_cache, ...)  .../layers/attention/attention_v4.py:330-331
+ * k_cache / v_cache: this layer's unified pools [num_slots, num_kv_heads, head_dim]; slot_mapping [n_tokens] int32 (slot < 0:
+ * not stored; NULL with NULL caches: rotation only). k_before_rotation != 0 stores the k rows as projected (un-rotated). */
+int pdllm_rope_store(void* qkv, int64_t row_stride, const void* cos_tab, const void* sin_tab, int64_t n_tokens, int num_q_heads,
+                     int num_kv_heads, int head_dim, void* k_cache, void* v_cache, const int32_t* slot_mapping, int64_t num_slots,
+                     int k_before_rotation, int dtype, int32_t* status, void* stream);
 /* out[t, i] = dtype(silu(gate_up[t, i])) * gate_up[t, inter + i] */
 int pdllm_silu_mul(const void* gate_up, void* out, int64_t n_tokens, int inter, int64_t gu_stride, int64_t out_stride, int dtype,
                    void* stream);
@@ -328,9 +337,13 @@ int pdllm_silu_mul(const void* gate_up, void* out, int64_t n_tokens, int inter, 
  * Up to 128 rows the weights are streamed once from HBM with the k-blocks dealt evenly over all SMs (stream-K); that
  * path needs pdllm_linear_workspace_bytes() of workspace whose first 64 KB hold arrival counters: zero-fill it once and
  * pass workspace_zeroed != 0 (the kernel returns every counter to zero), or pass 0 and a memset is enqueued first.
- * ---------------------------------------------------------------------------------------------- */
+ * PDLLM_LINEAR_WEIGHTS_AT_REST, OR-ed into `epilogue`: the caller vouches that nothing still in flight on the stream writes
+ *   `weight` (model weights after loading); the kernel may then start streaming weights while the kernel before it on the
+ *   stream is still finishing (programmatic dependent launch) and reads x, bias and the workspace only afterwards.
+ */
 #define PDLLM_EPI_NONE 0
 #define PDLLM_EPI_SILU_MUL 1
+#define PDLLM_LINEAR_WEIGHTS_AT_REST 0x100
 int64_t pdllm_linear_workspace_bytes(int64_t m, int64_t n, int64_t k);
 int pdllm_linear(const void* x, int64_t x_stride, const void* weight, int64_t w_stride, const void* bias, void* out,
                  int64_t out_stride, int64_t m, int64_t n, int64_t k, int dtype, int epilogue, void* workspace,

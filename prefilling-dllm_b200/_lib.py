@@ -14,7 +14,7 @@ from ctypes import POINTER, Structure, c_char_p, c_float, c_int, c_int32, c_int6
 PKG_DIR = os.path.dirname(os.path.abspath(__file__))
 LIB_PATH = os.path.join(PKG_DIR, "libpdllm_b200.so")
 
-ABI_VERSION = 4
+ABI_VERSION = 5
 # dtype codes
 F32, BF16, F16 = 0, 1, 2
 # cache layouts
@@ -101,6 +101,8 @@ _SIGNATURES = {
                                              c_int, c_int, c_int64, c_void_p, c_void_p, c_void_p]),
     "pdllm_add_rmsnorm": (c_int, [c_void_p, c_void_p, c_void_p, c_void_p, c_int64, c_int, c_int64, c_int64, c_int64, c_float, c_int, c_void_p]),
     "pdllm_rope_inplace": (c_int, [c_void_p, c_void_p, c_void_p, c_int64, c_int, c_int, c_int64, c_int, c_void_p]),
+    "pdllm_rope_store": (c_int, [c_void_p, c_int64, c_void_p, c_void_p, c_int64, c_int, c_int, c_int, c_void_p, c_void_p, c_void_p, c_int64,
+                                 c_int, c_int, c_void_p, c_void_p]),
     "pdllm_silu_mul": (c_int, [c_void_p, c_void_p, c_int64, c_int, c_int64, c_int64, c_int, c_void_p]),
     "pdllm_linear_workspace_bytes": (c_int64, [c_int64, c_int64, c_int64]),
     "pdllm_linear": (c_int, [c_void_p, c_int64, c_void_p, c_int64, c_void_p, c_void_p, c_int64, c_int64, c_int64, c_int64, c_int, c_int,

@@ -60,6 +60,8 @@ struct Args {
   int cluster_parts;     // > 1: launched as thread-block clusters of this many CTAs; the CTAs of a cluster split the k-blocks of ONE
                          // feature tile and add their accumulators through distributed shared memory (few rows, few tiles)
   int epilogue;
+  int weights_ahead;     // the weight copies of the first pipeline stages may be issued before the predecessor kernel has finished
+                         // (the caller vouches that no kernel still in flight on the stream writes the weight matrix)
 };
 
 __device__ __forceinline__ void tma_load_2d(const CUtensorMap* map, uint64_t* bar, void* dst, int c0, int c1) {
@@ -219,27 +221,53 @@ linear_sm100_kernel(const __grid_constant__ CUtensorMap a_map, const __grid_cons
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
-  // barriers and TMEM are set up; from here on the kernel reads what its predecessor wrote
-  grid_dependency_wait();
-  grid_launch_dependents();
 
   Schedule<kSwap, kBN> sched;
   sched.init(a);
   Segment seg;
 
+  // Barriers and TMEM are set up; from here on the kernel reads what its predecessor wrote, so every thread waits for the
+  // predecessor's completion first. The one exception is the producer thread when the weights are known to be at rest: it
+  // first fills the pipeline with the WEIGHT halves of the first stages, so that the weight stream of this kernel starts while
+  // the kernel before it is still finishing, and issues the activation halves after its wait.
+  const bool producer_thread = warp == 0 && lane == 0;
+  if (!producer_thread) {
+    grid_dependency_wait();
+    grid_launch_dependents();
+  }
+
   if (warp == 0) {
     // =========================== TMA producer ===========================
     if (lane == 0) {
+      int ahead = 0;                                  // stages whose weight half is already on its way
+      if (kSwap && a.weights_ahead) {
+        Schedule<kSwap, kBN> peek = sched;
+        Segment s0;
+        const int limit = a.weights_ahead < kStages ? a.weights_ahead : kStages;
+        while (ahead < limit && peek.next(a, s0)) {
+          for (int kb = s0.kb0; kb < s0.kb1 && ahead < limit; ++kb, ++ahead) {
+            mbar_expect_tx(&full[ahead], kStageBytes);
+            tma_load_2d(&a_map, &full[ahead], smem + ahead * kStageBytes, kb * kBlockK, s0.a_row0);
+          }
+        }
+      }
+      grid_dependency_wait();
+      grid_launch_dependents();
       int stage = 0; uint32_t phase = 0;
+      int step = 0;
       bool ok = true;
       while (ok && sched.next(a, seg)) {
-        for (int kb = seg.kb0; kb < seg.kb1 && ok; ++kb) {
-          ok = mbar_wait(&empty[stage], phase ^ 1, abort_flag, a);   // a fresh barrier passes the first lap
-          if (!ok) break;
+        for (int kb = seg.kb0; kb < seg.kb1 && ok; ++kb, ++step) {
           uint8_t* sa = smem + stage * kStageBytes;
-          mbar_expect_tx(&full[stage], kStageBytes);
-          tma_load_2d(&a_map, &full[stage], sa, kb * kBlockK, seg.a_row0);
-          tma_load_2d(&b_map, &full[stage], sa + kABytes, kb * kBlockK, seg.b_row0);
+          if (step < ahead) {                         // first lap: the stage is free and its weight half was issued above
+            tma_load_2d(&b_map, &full[stage], sa + kABytes, kb * kBlockK, seg.b_row0);
+          } else {
+            ok = mbar_wait(&empty[stage], phase ^ 1, abort_flag, a);   // a fresh barrier passes the first lap
+            if (!ok) break;
+            mbar_expect_tx(&full[stage], kStageBytes);
+            tma_load_2d(&a_map, &full[stage], sa, kb * kBlockK, seg.a_row0);
+            tma_load_2d(&b_map, &full[stage], sa + kABytes, kb * kBlockK, seg.b_row0);
+          }
           if (++stage == kStages) { stage = 0; phase ^= 1; }
         }
       }
@@ -679,6 +707,15 @@ inline int launch_typed(const Plan& pl, const CUtensorMap& a_map, const CUtensor
   return launch_one<false, 128, T>(a_map, b_map, a, pl.grid, stream);
 }
 
+// pipeline stages whose weight half is requested before the dependency wait (PDLLM_WEIGHTS_AHEAD overrides, for experiments)
+inline int stages_ahead() {
+  static const int n = [] {
+    const char* v = std::getenv("PDLLM_WEIGHTS_AHEAD");
+    return v != nullptr && v[0] != '\0' ? std::atoi(v) : 4;
+  }();
+  return n;
+}
+
 inline int launch(const void* x, int64_t x_stride, const void* w, int64_t w_stride, const void* bias, void* out, int64_t out_stride,
                   int64_t m, int64_t n, int64_t k, int dtype, int epilogue, void* workspace, int64_t ws_bytes, int workspace_zeroed,
                   int32_t* status, cudaStream_t stream) {
@@ -702,7 +739,8 @@ inline int launch(const void* x, int64_t x_stride, const void* w, int64_t w_stri
   a.out = out; a.bias = bias; a.status = status; a.trace = nullptr;
   a.out_stride = out_stride; a.m = m; a.n = n; a.k = k;
   a.kb_total = pl.kb_total; a.m_tiles = pl.m_tiles; a.n_tiles = pl.n_tiles; a.whole_tiles = pl.whole_tiles; a.units = pl.units; a.sk_grid = pl.sk_grid; a.cluster_parts = pl.cluster_parts;
-  a.epilogue = epilogue;
+  a.epilogue = epilogue & 0xff;
+  a.weights_ahead = (epilogue & PDLLM_LINEAR_WEIGHTS_AT_REST) ? stages_ahead() : 0;
   a.partials = nullptr; a.tile_counters = nullptr;
   if (pl.shared_tiles > 0) {
     const int64_t need = workspace_bytes(m, n, k);

@@ -424,6 +424,19 @@ int pdllm_add_rmsnorm(void* x, const void* delta, const void* weight, void* out,
   if (n_tokens < 0 || hidden <= 0) return fail(PDLLM_E_INVALID, "add_rmsnorm: bad sizes");
   if (n_tokens == 0) return 0;
   if (!x || !weight || !out) return fail(PDLLM_E_INVALID, "add_rmsnorm: null pointer");
+  if (dtype != PDLLM_F32 && hidden % 8 == 0 && hidden <= 8 * 1024 && x_stride % 8 == 0 && out_stride % 8 == 0 &&
+      (delta == nullptr || (delta_stride % 8 == 0 && aligned16(delta))) && aligned16(x) && aligned16(weight) && aligned16(out)) {
+    const int vec_threads = ((hidden / 8 + 31) / 32) * 32;          // one 16-byte vector per thread
+    if (dtype == PDLLM_BF16)
+      (void)launch_dependent(add_rmsnorm_vec_kernel<__nv_bfloat16>, dim3(static_cast<unsigned>(n_tokens)), dim3(vec_threads), 0, as_stream(stream),
+                             static_cast<__nv_bfloat16*>(x), static_cast<const __nv_bfloat16*>(delta), static_cast<const __nv_bfloat16*>(weight),
+                             static_cast<__nv_bfloat16*>(out), hidden, x_stride, delta_stride, out_stride, eps);
+    else
+      (void)launch_dependent(add_rmsnorm_vec_kernel<__half>, dim3(static_cast<unsigned>(n_tokens)), dim3(vec_threads), 0, as_stream(stream),
+                             static_cast<__half*>(x), static_cast<const __half*>(delta), static_cast<const __half*>(weight),
+                             static_cast<__half*>(out), hidden, x_stride, delta_stride, out_stride, eps);
+    return check_launch("add_rmsnorm");
+  }
   const int threads = hidden >= 2048 ? 512 : 256;
   PDLLM_DISPATCH_DTYPE(dtype, "add_rmsnorm",
                        (void)launch_dependent(add_rmsnorm_kernel<T>, dim3(static_cast<unsigned>(n_tokens)), dim3(threads), 0, as_stream(stream),
@@ -443,6 +456,32 @@ int pdllm_rope_inplace(void* x, const void* cos_tab, const void* sin_tab, int64_
                                                                                    static_cast<const T*>(sin_tab), n_tokens, num_heads,
                                                                                    head_dim, row_stride));
   return check_launch("rope_inplace");
+}
+
+int pdllm_rope_store(void* qkv, int64_t row_stride, const void* cos_tab, const void* sin_tab, int64_t n_tokens, int num_q_heads,
+                     int num_kv_heads, int head_dim, void* k_cache, void* v_cache, const int32_t* slot_mapping, int64_t num_slots,
+                     int k_before_rotation, int dtype, int32_t* status, void* stream) {
+  if (n_tokens < 0 || num_q_heads < 0 || num_kv_heads < 0 || num_q_heads + num_kv_heads <= 0 || head_dim <= 0)
+    return fail(PDLLM_E_INVALID, "rope_store: bad sizes");
+  if (n_tokens == 0) return 0;
+  if (!qkv || !cos_tab || !sin_tab) return fail(PDLLM_E_INVALID, "rope_store: null pointer");
+  if (slot_mapping != nullptr && (!k_cache || !v_cache || num_slots <= 0)) return fail(PDLLM_E_INVALID, "rope_store: slot mapping without caches");
+  if (dtype != PDLLM_BF16 && dtype != PDLLM_F16) return fail(PDLLM_E_UNSUPPORTED, "rope_store: 16-bit dtypes only (use rope_inplace + store_kvcache_unified)");
+  if (head_dim % 16 != 0 || row_stride % 8 != 0 || row_stride < static_cast<int64_t>(num_q_heads + 2 * num_kv_heads) * head_dim ||
+      !aligned16(qkv) || !aligned16(cos_tab) || !aligned16(sin_tab) || (slot_mapping != nullptr && (!aligned16(k_cache) || !aligned16(v_cache))))
+    return fail(PDLLM_E_UNSUPPORTED, "rope_store: head_dim must be a multiple of 16 and every row 16-byte aligned");
+  const int64_t work = n_tokens * (num_q_heads + 2 * num_kv_heads) * (head_dim / 16);
+  const int grid = grid_for(work, 128);
+  if (dtype == PDLLM_BF16)
+    (void)launch_dependent(rope_store_kernel<__nv_bfloat16>, dim3(grid), dim3(128), 0, as_stream(stream), static_cast<__nv_bfloat16*>(qkv),
+                           static_cast<const __nv_bfloat16*>(cos_tab), static_cast<const __nv_bfloat16*>(sin_tab), n_tokens, num_q_heads, num_kv_heads,
+                           head_dim, row_stride, static_cast<__nv_bfloat16*>(k_cache), static_cast<__nv_bfloat16*>(v_cache), slot_mapping, num_slots,
+                           k_before_rotation, status);
+  else
+    (void)launch_dependent(rope_store_kernel<__half>, dim3(grid), dim3(128), 0, as_stream(stream), static_cast<__half*>(qkv),
+                           static_cast<const __half*>(cos_tab), static_cast<const __half*>(sin_tab), n_tokens, num_q_heads, num_kv_heads, head_dim,
+                           row_stride, static_cast<__half*>(k_cache), static_cast<__half*>(v_cache), slot_mapping, num_slots, k_before_rotation, status);
+  return check_launch("rope_store");
 }
 
 int pdllm_silu_mul(const void* gate_up, void* out, int64_t n_tokens, int inter, int64_t gu_stride, int64_t out_stride, int dtype,
@@ -551,6 +590,8 @@ int pdllm_linear(const void* x, int64_t x_stride, const void* weight, int64_t w_
   if (m == 0) return 0;
   if (!x || !weight || !out) return fail(PDLLM_E_INVALID, "linear: null pointer");
   if (dtype != PDLLM_BF16 && dtype != PDLLM_F16) return fail(PDLLM_E_UNSUPPORTED, "linear: dtype must be bf16 or fp16 (tensor-core operands)");
+  const int flags = epilogue;
+  epilogue &= ~PDLLM_LINEAR_WEIGHTS_AT_REST;
   if (epilogue != PDLLM_EPI_NONE && epilogue != PDLLM_EPI_SILU_MUL) return fail(PDLLM_E_INVALID, "linear: unknown epilogue %d", epilogue);
   if (epilogue == PDLLM_EPI_SILU_MUL && (bias != nullptr || n % 2 != 0))
     return fail(PDLLM_E_INVALID, "linear: the SiLU-mul epilogue takes an even number of interleaved (gate, up) rows and no bias");
@@ -561,7 +602,7 @@ int pdllm_linear(const void* x, int64_t x_stride, const void* weight, int64_t w_
   if (m > 128 && (out_stride % 8 != 0 || !aligned16(out) || out_cols % 8 != 0))
     return fail(PDLLM_E_UNSUPPORTED, "linear: with more than 128 rows, out needs 16-byte aligned rows and a column count that is a multiple of 8");
   if (m >= (1ll << 31) || n >= (1ll << 31) || k >= (1ll << 31)) return fail(PDLLM_E_UNSUPPORTED, "linear: extent exceeds the tensor-map coordinate range");
-  return gemm::launch(x, x_stride, weight, w_stride, bias, out, out_stride, m, n, k, dtype, epilogue, workspace, workspace_bytes,
+  return gemm::launch(x, x_stride, weight, w_stride, bias, out, out_stride, m, n, k, dtype, epilogue | (flags & PDLLM_LINEAR_WEIGHTS_AT_REST), workspace, workspace_bytes,
                       workspace_zeroed, status, as_stream(stream));
 }
 

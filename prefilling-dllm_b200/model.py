@@ -338,18 +338,25 @@ class PagedDreamModel:
         attn_out = torch.empty((total, hq, d), dtype=self.dtype, device=self.device)
         eps = a.rms_norm_eps
         delta = None                                                     # output of the previous sub-block, not yet added to x
+        fused_rope_store = self.dtype in (torch.bfloat16, torch.float16) and d % 16 == 0
         for li, w in enumerate(self.layers):
             h = ops.add_rmsnorm(x, w["ln1"], eps, delta)                 # x += delta; h = norm(x)
             qkv = self._linear(h, w["wqkv"], w["bqkv"]).view(total, hq + 2 * hkv, d)
             q, k, v = qkv[:, :hq], qkv[:, hq:hq + hkv], qkv[:, hq + hkv:]   # strided views of one buffer: no copies
             k_cache, v_cache = self.layer_cache(li)
-            if slot_mapping is not None and store_unrotated_k:
-                ops.store_kvcache_unified_layout(k, v, k_cache, v_cache, slot_mapping, "diffusion_lm")
-            ops.rope_inplace(qkv[:, :hq + hkv], cos2, sin2)              # q and k heads are adjacent: one launch
+            if fused_rope_store:
+                # rotation of the q and k heads and the page write of k and v in ONE launch (the write waits when it must follow attention)
+                write_now = slot_mapping is not None and not store_after_attention
+                ops.rope_store(qkv, cos2, sin2, hq, hkv, k_cache if write_now else None, v_cache if write_now else None,
+                               slot_mapping if write_now else None, k_before_rotation=store_unrotated_k)
+            else:
+                if slot_mapping is not None and store_unrotated_k:
+                    ops.store_kvcache_unified_layout(k, v, k_cache, v_cache, slot_mapping, "diffusion_lm")
+                ops.rope_inplace(qkv[:, :hq + hkv], cos2, sin2)              # q and k heads are adjacent: one launch
+                if slot_mapping is not None and not store_after_attention and not store_unrotated_k:
+                    ops.store_kvcache_unified_layout(k, v, k_cache, v_cache, slot_mapping, "diffusion_lm")
             if li in capture:
                 captured[li] = (q.contiguous(), k.contiguous())
-            if slot_mapping is not None and not store_after_attention and not store_unrotated_k:
-                ops.store_kvcache_unified_layout(k, v, k_cache, v_cache, slot_mapping, "diffusion_lm")
             if block_table is not None:
                 ops.paged_attention(q, k, v, attn_out, cu_seqlens_q=cu_seqlens, max_query_len=max_query_len, key_cache=k_cache,
                                     value_cache=v_cache, block_table=block_table, seq_lens=seq_lens, max_seq_len=max_seq_len,
@@ -364,7 +371,7 @@ class PagedDreamModel:
             proj = self._linear(attn_out.view(total, hq * d), w["wo"])
             h = ops.add_rmsnorm(x, w["ln2"], eps, proj)                  # x += attention output; h = norm(x)
             if self.tensor_core_linear:
-                delta = ops.linear(ops.linear(h, w["wgu"], silu_mul_interleaved=True), w["wd"])   # SiLU(gate)·up in the GEMM epilogue
+                delta = ops.linear(ops.linear(h, w["wgu"], silu_mul_interleaved=True, weights_at_rest=True), w["wd"], weights_at_rest=True)   # SiLU(gate)·up in the GEMM epilogue
             else:
                 delta = F.linear(ops.silu_mul(F.linear(h, w["wgu"])), w["wd"])
         if delta is not None:
@@ -376,7 +383,7 @@ class PagedDreamModel:
         return logits, captured
 
     def _linear(self, x: torch.Tensor, weight: torch.Tensor, bias: Optional[torch.Tensor] = None) -> torch.Tensor:
-        return ops.linear(x, weight, bias) if self.tensor_core_linear else F.linear(x, weight, bias)
+        return ops.linear(x, weight, bias, weights_at_rest=True) if self.tensor_core_linear else F.linear(x, weight, bias)
 
     def rope_rows(self, page_ids, start: int, positions: Sequence[int]) -> None:
         """Rotate the un-rotated K rows `[start, start + len(positions))` of `page_ids` in place, in every layer."""
@@ -422,7 +429,7 @@ def denoise_blocks(model: "PagedDreamModel", cache, *, suffix_pos_start: int, la
     `cache`: a handle with `page_ids`, `length` (valid tokens: prompt, finished blocks and `tail_in_cache` later-block MASK
     slots; updated here) and `slots(start, n)`. Layout while block b is active: [prompt ‖ finished blocks ‖ MASK slots of the
     later blocks]; the active block's rows are the new rows of every forward, so they replace their own slots by
-    construction. After the block is committed its K/V take the place of the first later-MASK slots and the later slots are
+    construction (the LAST block is returned but never written to the cache). After the block is committed its K/V take the place of the first later-MASK slots and the later slots are
     recomputed by the next block's suffix initialisation (reference :2368-2397).
     `first_token`: the first token of block 0 when the prefill already produced it together with the later-MASK slots
     (full_prompt_mask mode); None = every block starts with a suffix initialisation.
@@ -509,6 +516,8 @@ def denoise_blocks(model: "PagedDreamModel", cache, *, suffix_pos_start: int, la
         if steps_out is not None:
             steps_out.append(guard)
         generated.extend(block.tolist())
+        if later <= 0:
+            break       # the reference commits the last block too (:2764-2771); nothing reads that K/V or logit afterwards
         # commit forward: the finished block's K/V take the first slots behind prompt + finished; its last logit is the next
         # block's "last context logit". The store comes after attention so the later-MASK slots are still seen.
         logits, _ = forward(block, block_pos, ctx, store_slots=cache.slots(done, blen), logit_rows=[blen - 1], store_after_attention=True)
@@ -587,6 +596,8 @@ def denoise_blocks_batched(model: "PagedDreamModel", caches, *, suffix_pos_start
                 steps_out[i].append(needed[i])
         for i, block in enumerate(runner.blocks):
             generated[i].extend(block.tolist())
+        if later <= 0:
+            break       # the last block's K/V and logit are read by nothing
         # commit: the finished blocks' K/V take the first slots behind prompt + finished blocks (stored after attention, which
         # still reads the later-MASK slots there); the last row's logit is the next block's last-context logit
         ctx = [d + later for d in done]

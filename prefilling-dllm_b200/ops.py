@@ -655,12 +655,46 @@ def rope_inplace(x: torch.Tensor, cos: torch.Tensor, sin: torch.Tensor) -> None:
     check(_lib.load().pdllm_rope_inplace(x.data_ptr(), cos.data_ptr(), sin.data_ptr(), t, h, d, x.stride(0), dtype_code(x.dtype), _stream(device)))
 
 
+def rope_store(qkv: torch.Tensor, cos: torch.Tensor, sin: torch.Tensor, num_q_heads: int, num_kv_heads: int,
+               k_cache: Optional[torch.Tensor] = None, v_cache: Optional[torch.Tensor] = None, slot_mapping: Optional[torch.Tensor] = None,
+               *, k_before_rotation: bool = False) -> None:
+    """Rotate the q and k heads of `qkv` `[T, Hq + 2 Hkv, D]` (any row stride) in place and, when `slot_mapping` is given, write
+    its k and v heads into the unified pools `k_cache` / `v_cache` `[pages, page_size, Hkv, D]` — the model's rotary embedding and
+    `store_kvcache_unified_layout` (.../models/dream.py:75-76, .../layers/attention/attention_v4.py:330-331) in one launch.
+    bf16 / fp16 with D a multiple of 16; other inputs raise NotImplementedError (use `rope_inplace` + the store op)."""
+    device = _require_cuda(qkv, cos, sin, k_cache, v_cache, slot_mapping)
+    t, heads, d = qkv.shape
+    if heads != num_q_heads + 2 * num_kv_heads or qkv.stride(2) != 1 or qkv.stride(1) != d:
+        raise ValueError("qkv must be [T, Hq + 2 Hkv, D] with contiguous heads and head_dim")
+    cos, sin = cos.reshape(-1, d), sin.reshape(-1, d)
+    if cos.shape[0] != t or sin.shape != cos.shape or cos.dtype != qkv.dtype or sin.dtype != qkv.dtype or not (cos.is_contiguous() and sin.is_contiguous()):
+        raise ValueError("cos / sin must be contiguous [tokens, head_dim] tables in the dtype of qkv")
+    num_slots = 0
+    if slot_mapping is not None:
+        if k_cache is None or v_cache is None or k_cache.shape != v_cache.shape or k_cache.dim() != 4:
+            raise ValueError("the page write needs k_cache and v_cache [pages, page_size, Hkv, D]")
+        if tuple(k_cache.shape[2:]) != (num_kv_heads, d) or k_cache.dtype != qkv.dtype or not (k_cache.is_contiguous() and v_cache.is_contiguous()):
+            raise ValueError("caches must be contiguous [pages, page_size, Hkv, D] pools of the dtype of qkv")
+        if slot_mapping.dtype != torch.int32 or slot_mapping.numel() != t or not slot_mapping.is_contiguous():
+            raise ValueError("slot_mapping must be a contiguous int32 [T] tensor")
+        num_slots = k_cache.shape[0] * k_cache.shape[1]
+    check(_lib.load().pdllm_rope_store(qkv.data_ptr(), qkv.stride(0), cos.data_ptr(), sin.data_ptr(), t, num_q_heads, num_kv_heads, d,
+                                       _ptr(k_cache) if slot_mapping is not None else None, _ptr(v_cache) if slot_mapping is not None else None,
+                                       _ptr(slot_mapping), num_slots, 1 if k_before_rotation else 0, dtype_code(qkv.dtype),
+                                       status_word(device).data_ptr(), _stream(device)))
+
+
+LINEAR_WEIGHTS_AT_REST = 0x100      # PDLLM_LINEAR_WEIGHTS_AT_REST
+
+
 def linear(x: torch.Tensor, weight: torch.Tensor, bias: Optional[torch.Tensor] = None, *, silu_mul_interleaved: bool = False,
-           out: Optional[torch.Tensor] = None) -> torch.Tensor:
+           out: Optional[torch.Tensor] = None, weights_at_rest: bool = False) -> torch.Tensor:
     """`x @ weight.T (+ bias)` on the tcgen05 GEMM kernel: x `[M, K]`, weight `[N, K]` (the nn.Linear layout), bf16 / fp16.
 
     silu_mul_interleaved: `weight` holds gate and up rows interleaved (row 2i = gate_i, 2i + 1 = up_i) and the result is
     `silu(gate) * up`, `[M, N / 2]`, with the rounding of the unfused projection -> activation -> product sequence.
+    weights_at_rest: nothing still in flight on the stream writes `weight` (model weights after loading): the kernel may start
+    streaming them while the kernel before it on the stream is still finishing.
     Takes the place of F.linear in QKVParallelLinear / MergedColumnParallelLinear / RowParallelLinear / ParallelLMHead
     (prefilling_dllm_engine/prefilling_dllm/layers/linear.py:108-244, layers/embed_head.py:63-74)."""
     device = _require_cuda(x, weight, bias)
@@ -686,7 +720,8 @@ def linear(x: torch.Tensor, weight: torch.Tensor, bias: Optional[torch.Tensor] =
         ws = _workspace(device, "linear", need, zero=True)   # zero-filled at creation; the kernel keeps its counters at zero
         ws_ptr, ws_bytes = ws.data_ptr(), ws.numel()
     check(lib.pdllm_linear(x.data_ptr(), x.stride(0), weight.data_ptr(), weight.stride(0), _ptr(bias), out.data_ptr(), out.stride(0),
-                           m, n, k, dtype_code(x.dtype), 1 if silu_mul_interleaved else 0, ws_ptr, ws_bytes, 1,
+                           m, n, k, dtype_code(x.dtype), (1 if silu_mul_interleaved else 0) | (LINEAR_WEIGHTS_AT_REST if weights_at_rest else 0),
+                           ws_ptr, ws_bytes, 1,
                            status_word(device).data_ptr(), _stream(device)))
     return out
 

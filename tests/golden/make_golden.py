@@ -245,9 +245,9 @@ FLAG_VARIANTS = {
     "evict_use_generated_query": dict(README_FLAGS, token_capacity=128, token_score_use_generated=True),
     "sample_top_k_top_p_greedy": dict(README_FLAGS, top_k=8, top_p=0.7),
     # temperature > 0 draws from a categorical; with one candidate left per slot the draw is deterministic, every slot has
-    # confidence 1 and a block fills in one step. Three draft rounds fill all four draft slots: WHICH of several slots of
-    # confidence exactly 1 a single round takes is torch.topk's unspecified choice among ties
-    "sample_temperature_top_k_1": dict(README_FLAGS, temperature=0.7, top_k=1, score_draft_partial_rounds=3),
+    # confidence 1 and a block fills in one step. Scored without a draft: WHICH of several slots of confidence exactly 1 a
+    # draft round takes is torch.topk's unspecified choice among ties, and later rounds depend on it
+    "sample_temperature_top_k_1": dict(README_FLAGS, score_mode="self_information", temperature=0.7, top_k=1),
     "alg_topk_margin": dict(README_FLAGS, alg="topk_margin", diffusion_steps=8),
     "alg_entropy": dict(README_FLAGS, alg="entropy", diffusion_steps=8),
 }

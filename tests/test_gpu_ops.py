@@ -722,6 +722,74 @@ def test_rope_pages_in_place(ops, cuda_device, dtype):
         ops.rope_pages(dev_cache, [0], 0, cos.to(cuda_device), sin.to(cuda_device))
 
 
+@pytest.mark.parametrize("hidden,rows", [(3584, 32), (4096, 5), (8192, 3), (520, 9), (8200, 2)])
+def test_add_rmsnorm_one_vector_per_thread(ops, cuda_device, hidden, rows):
+    """16-bit rows of up to 8192 elements take the one-pass kernel (a 16-byte vector per thread, ragged last warp at 520);
+    8200 is past it and takes the loop kernel. Same gates as against eager: the residual row bit-exact, the normed row equal
+    but for stray last bits from the order of the fp32 sum."""
+    g = torch.Generator().manual_seed(hidden + rows)
+    for dtype in (torch.bfloat16, torch.float16):
+        x = torch.randn(rows, hidden, generator=g).to(dtype)
+        delta = torch.randn(rows, hidden, generator=g).to(dtype)
+        w = (1 + 0.1 * torch.randn(hidden, generator=g)).to(dtype)
+        xd = x.to(cuda_device)
+        out = ops.add_rmsnorm(xd, w.to(cuda_device), 1e-6, delta.to(cuda_device))
+        x_ref = x + delta
+        xf = x_ref.float()
+        ref = w * (xf * torch.rsqrt(xf.pow(2).mean(-1, keepdim=True) + 1e-6)).to(dtype)
+        assert torch.equal(xd.cpu(), x_ref)
+        assert torch.allclose(out.cpu().float(), ref.float(), rtol=2 ** -7, atol=1e-3)
+        assert (out.cpu() != ref).float().mean() < 0.01
+        plain = ops.add_rmsnorm(x.to(cuda_device), w.to(cuda_device), 1e-6)
+        xf = x.float()
+        assert (plain.cpu() != w * (xf * torch.rsqrt(xf.pow(2).mean(-1, keepdim=True) + 1e-6)).to(dtype)).float().mean() < 0.01
+    ops.check_status(cuda_device)
+
+
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
+@pytest.mark.parametrize("k_before_rotation", [False, True])
+def test_rope_and_page_write_in_one_launch(ops, cuda_device, dtype, k_before_rotation):
+    """`rope_store` = `rope_inplace` on the q and k heads + `store_kvcache_unified_layout` of k and v, bit for bit: rotated rows in
+    the buffer, rotated (or, on request, un-rotated) k and v rows at their slots, untouched pages elsewhere, skipped negative
+    slots, a reported out-of-range slot; without a slot mapping only the rotation happens."""
+    g = torch.Generator().manual_seed(123)
+    t, hq, hkv, d, pages, page = 45, 4, 2, 128, 3, 32
+    buf = torch.randn(t, (hq + 2 * hkv) * d + 64, generator=g).to(dtype)          # a padded row stride
+    pos = torch.randint(0, 30000, (t,), generator=g)
+    inv = 1.0 / (1e6 ** (torch.arange(0, d, 2).float() / d))
+    emb = torch.cat((pos.float().unsqueeze(-1) * inv,) * 2, dim=-1)
+    cos, sin = emb.cos().to(dtype).to(cuda_device), emb.sin().to(dtype).to(cuda_device)
+    slots = torch.randperm(pages * page, generator=g)[:t].to(torch.int32)
+    slots[5] = -1
+    kc0 = torch.randn(pages, page, hkv, d, generator=g).to(dtype)
+    vc0 = torch.randn(pages, page, hkv, d, generator=g).to(dtype)
+
+    def view(b):
+        return b[:, : (hq + 2 * hkv) * d].view(t, hq + 2 * hkv, d)
+
+    ref_buf, ref_k, ref_v = buf.to(cuda_device), kc0.to(cuda_device), vc0.to(cuda_device)
+    rq = view(ref_buf)
+    if k_before_rotation:
+        ops.store_kvcache_unified_layout(rq[:, hq:hq + hkv], rq[:, hq + hkv:], ref_k, ref_v, slots.to(cuda_device), "diffusion_lm")
+    ops.rope_inplace(rq[:, : hq + hkv], cos, sin)
+    if not k_before_rotation:
+        ops.store_kvcache_unified_layout(rq[:, hq:hq + hkv], rq[:, hq + hkv:], ref_k, ref_v, slots.to(cuda_device), "diffusion_lm")
+    got_buf, got_k, got_v = buf.to(cuda_device), kc0.to(cuda_device), vc0.to(cuda_device)
+    ops.rope_store(view(got_buf), cos, sin, hq, hkv, got_k, got_v, slots.to(cuda_device), k_before_rotation=k_before_rotation)
+    ops.check_status(cuda_device)
+    assert torch.equal(got_buf, ref_buf) and torch.equal(got_k, ref_k) and torch.equal(got_v, ref_v)
+    only = buf.to(cuda_device)
+    ops.rope_store(view(only), cos, sin, hq, hkv)
+    assert torch.equal(only, ref_buf)
+    bad = slots.clone()
+    bad[0] = pages * page
+    ops.rope_store(view(buf.to(cuda_device)), cos, sin, hq, hkv, got_k, got_v, bad.to(cuda_device))
+    with pytest.raises(RuntimeError):
+        ops.check_status(cuda_device)
+    with pytest.raises(NotImplementedError):
+        ops.rope_store(view(buf.float().to(cuda_device)), cos.float(), sin.float(), hq, hkv)
+
+
 @pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16])
 def test_dense_row_ops_match_eager(ops, cuda_device, dtype):
     """RMSNorm (+ residual add), in-place RoPE on a strided QKV buffer and SiLU*mul against the eager expressions of the
