@@ -90,6 +90,50 @@ def prefill_and_decode(model, prompt_ids: Sequence[int], *, block_length: int, m
     return dict(first_token=first, last_context_logit=last, token_ids=ids, n_diff_steps=steps, past=past, key_positions=key_positions)
 
 
+def decode_blocks(model, prompt_ids: Sequence[int], *, max_new: int, block_length: int, mask_id: int, threshold: float,
+                  shift: bool = True, softmax_dtype: Optional[torch.dtype] = torch.float32):
+    """A record of several generation blocks: joint prefill of [prompt ‖ max_new MASK slots] (only the prompt's K/V and the
+    last-context logit are kept), then the eval class's dual-cache block loop (fastdllm_parallelcomp.py:2678-2774, :2368-2441):
+    every block forwards all remaining MASK slots against [prompt ‖ finished blocks] (suffix initialisation), the active
+    block's rows replace their slots at every step, a commit forward stores the finished block. `shift=False`: the first
+    token of a block is the arg-max of the first MASK slot's OWN row of the suffix forward and the steps read slot p from
+    logits[p] (:1017-1024). The reference engine stops at one block (fastdllm_engine.py:1911-1915); parity of this function
+    with the reference is pinned for shift=True through the eval goldens (tests/test_oracle_golden.py).
+    Returns dict(token_ids, n_diff_steps)."""
+    prompt_ids = list(prompt_ids)
+    n0 = len(prompt_ids)
+    total = n0 + max_new
+    positions = _positions(range(total))
+    generated: List[int] = []
+    steps = 0
+    with torch.no_grad():
+        out = model(torch.tensor([prompt_ids + [mask_id] * max_new]), attention_mask=None, position_ids=positions, use_cache=True)
+        cache = [(k[:, :n0], v[:, :n0]) for k, v in out.past_key_values]
+        last_logit = out.logits[0, n0 - 1]
+        for start in range(0, max_new, block_length):
+            blen = min(block_length, max_new - start)
+            lo = n0 + start
+            done = [(k[:, :lo], v[:, :lo]) for k, v in cache]
+            suffix = torch.full((1, total - lo), mask_id, dtype=torch.long)
+            init = model(suffix, attention_mask=None, position_ids=positions, past_key_values=done, use_cache=True)
+            cache = init.past_key_values
+            block = torch.full((blen,), mask_id, dtype=torch.long)
+            block[0] = int(torch.argmax(last_logit if shift else init.logits[0, 0]))
+            replace = torch.zeros((1, total), dtype=torch.bool)
+            replace[0, lo:lo + blen] = True
+            while bool((block == mask_id).any()):
+                steps += 1
+                step = model(block.unsqueeze(0), attention_mask=None, position_ids=positions, past_key_values=cache, use_cache=False,
+                             dual_cache=True, replace_position=replace)
+                block, _, _ = O.unmask_step(step.logits[0], block, mask_token_id=mask_id, threshold=threshold,
+                                            last_logit=last_logit if shift else None, shift=shift, softmax_dtype=softmax_dtype)
+            generated.extend(block.tolist())
+            commit = model(block.unsqueeze(0), attention_mask=None, position_ids=positions, past_key_values=cache, use_cache=True,
+                           dual_cache=True, replace_position=replace)
+            cache, last_logit = commit.past_key_values, commit.logits[0, -1]
+    return dict(token_ids=generated, n_diff_steps=steps)
+
+
 def engine_draft(model, prompt_ids: Sequence[int], *, draft_len: int, partial_rounds: int, mask_id: int) -> Tuple[List[int], List[bool]]:
     """generate_partial_draft_rounds_for_selection :1014-1060 — nothing cached, one full bidirectional forward per round."""
     prompt_ids = list(prompt_ids)

@@ -31,8 +31,14 @@ def _causal_mask(length: int) -> torch.Tensor:
     return torch.triu(mask, diagonal=1)
 
 
-def run_port(model, context: Sequence[int], query: Sequence[int], flags: Dict, *, bos: int = 1, mask_id: int = 1023) -> Dict:
-    """README flow (full_prompt_mask, partial draft rounds, single-chunk causal scoring, no eviction) from oracle/hotpath.py."""
+def run_port(model, context: Sequence[int], query: Sequence[int], flags: Dict, *, bos: int = 1, mask_id: int = 1023,
+             backend: str = "dream") -> Dict:
+    """README flow (full_prompt_mask, partial draft rounds, single-chunk causal scoring, no eviction) from oracle/hotpath.py.
+    backend "llada": the reference's un-shifted read-out on the same weights (E:fastdllm_parallelcomp.py:1017-1024) — a block's
+    first token comes from the first MASK slot's own row (:2390-2397, :2915-2922), every step reads slot p from logits[p], and
+    chunks are scored leave-one-out (:1166-1201): one forward per label with that label masked, its log-probability read at
+    its own row. PARITY UNPINNED for this backend: the reference needs the Fast-dLLM v1 LLaDA plug-in to run it."""
+    shift = backend != "llada"
     if flags.get("cache_build_mode") != "full_prompt_mask" or int(flags.get("token_capacity") or 0) != 0 or flags.get("score_draft_partial_rounds") is None:
         raise ValueError("run_port covers the README flags only")
     query = list(query)
@@ -46,12 +52,18 @@ def run_port(model, context: Sequence[int], query: Sequence[int], flags: Dict, *
         out = model(torch.tensor([ctx]), attention_mask=None, position_ids=_positions(range(len(ctx))), use_cache=True)
         last_logit = out.logits[0, -1]
         block = torch.full((n_draft,), mask_id, dtype=torch.long)
-        block[0] = int(torch.argmax(last_logit))
+        if shift:
+            block[0] = int(torch.argmax(last_logit))
+        else:
+            init = model(block.unsqueeze(0), attention_mask=None, position_ids=_positions(range(len(ctx) + n_draft)),
+                         past_key_values=out.past_key_values, use_cache=False)
+            block[0] = int(torch.argmax(init.logits[0, 0]))
         confirmed = [True] + [False] * (n_draft - 1)
         for _ in range(int(flags["score_draft_partial_rounds"])):
             step = model(block.unsqueeze(0), attention_mask=None, position_ids=_positions(range(len(ctx) + n_draft)),
                          past_key_values=out.past_key_values, use_cache=False)
-            new_block, _, _ = O.unmask_step(step.logits[0], block, mask_token_id=mask_id, threshold=2.0, last_logit=last_logit)
+            new_block, _, _ = O.unmask_step(step.logits[0], block, mask_token_id=mask_id, threshold=2.0,
+                                            last_logit=last_logit if shift else None, shift=shift)
             confirmed = [c or bool(a != b) for c, a, b in zip(confirmed, new_block.tolist(), block.tolist())]
             block = new_block
         secs["draft"] = time.perf_counter() - t0
@@ -63,8 +75,17 @@ def run_port(model, context: Sequence[int], query: Sequence[int], flags: Dict, *
         for chunk in chunks:
             row = [bos] + chunk + selection
             label_pos, labels = O.score_labels(1, len(chunk), selection, label_mask)
-            res = model(torch.tensor([row]), attention_mask=_causal_mask(len(row)), position_ids=_positions(range(len(row))))
-            rows = res.logits[0, [p - 1 for p in label_pos]]
+            if shift:
+                res = model(torch.tensor([row]), attention_mask=_causal_mask(len(row)), position_ids=_positions(range(len(row))))
+                rows = res.logits[0, [p - 1 for p in label_pos]]
+            else:
+                picked = []
+                for p in label_pos:
+                    hidden_label = list(row)
+                    hidden_label[p] = mask_id
+                    res = model(torch.tensor([hidden_label]), attention_mask=_causal_mask(len(row)), position_ids=_positions(range(len(row))))
+                    picked.append(res.logits[0, p])
+                rows = torch.stack(picked, dim=0)
             score, _ = O.self_information_scores(rows.unsqueeze(0), torch.tensor(labels))
             scores.append(float(score[0]))
         selected = O.rank_chunks(scores, int(flags["topk_chunks"]))
@@ -78,6 +99,7 @@ def run_port(model, context: Sequence[int], query: Sequence[int], flags: Dict, *
         positions = _positions(range(len(full)))
         res = model(torch.tensor([full]), attention_mask=None, position_ids=positions, use_cache=True)
         cache, last_logit = res.past_key_values, res.logits[0, n0 - 1]
+        first_logit = last_logit if shift else res.logits[0, n0]
         secs["prefill"] = time.perf_counter() - t2
         t3 = time.perf_counter()
         generated: List[int] = []
@@ -86,15 +108,18 @@ def run_port(model, context: Sequence[int], query: Sequence[int], flags: Dict, *
             if b > 0:
                 done = [(k[:, :lo], v[:, :lo]) for k, v in cache]
                 suffix = torch.full((1, len(full) - lo), mask_id, dtype=torch.long)
-                cache = model(suffix, attention_mask=None, position_ids=positions, past_key_values=done, use_cache=True).past_key_values
+                init = model(suffix, attention_mask=None, position_ids=positions, past_key_values=done, use_cache=True)
+                cache = init.past_key_values
+                first_logit = last_logit if shift else init.logits[0, 0]
             block = torch.full((blen,), mask_id, dtype=torch.long)
-            block[0] = int(torch.argmax(last_logit))
+            block[0] = int(torch.argmax(first_logit))
             replace = torch.zeros((1, len(full)), dtype=torch.bool)
             replace[0, lo:lo + blen] = True
             while bool((block == mask_id).any()):
                 step = model(block.unsqueeze(0), attention_mask=None, position_ids=positions, past_key_values=cache, use_cache=False,
                              dual_cache=True, replace_position=replace)
-                block, _, _ = O.unmask_step(step.logits[0], block, mask_token_id=mask_id, threshold=float(flags["threshold"]), last_logit=last_logit)
+                block, _, _ = O.unmask_step(step.logits[0], block, mask_token_id=mask_id, threshold=float(flags["threshold"]),
+                                            last_logit=last_logit if shift else None, shift=shift)
             generated.extend(block.tolist())
             commit = model(block.unsqueeze(0), attention_mask=None, position_ids=positions, past_key_values=cache, use_cache=True,
                            dual_cache=True, replace_position=replace)

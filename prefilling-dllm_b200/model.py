@@ -469,17 +469,21 @@ def denoise_blocks(model: "PagedDreamModel", cache, *, suffix_pos_start: int, la
         block_pos = list(range(suffix_pos_start + start, suffix_pos_start + start + blen))
         later = max_new - start - blen          # MASK slots of the blocks after this one
         if first_token is None or b > 0:
-            # suffix initialisation: forward all remaining MASKs against prompt + finished blocks; the later blocks' K/V go
-            # behind the finished ones, the active block's rows are not stored
-            if later > 0:
+            # suffix initialisation (reference :2368-2397): forward all remaining MASKs against prompt + finished blocks; the
+            # later blocks' K/V go behind the finished ones, the active block's rows are not stored. Dream reads the block's first
+            # token from the last context logit; an un-shifted architecture (LLaDA) from the first MASK slot's own row of this
+            # forward, which therefore runs even when no later block is left.
+            first_logit = last_logit
+            if later > 0 or not arch.logit_shift:
                 suffix_pos = list(range(suffix_pos_start + start, suffix_pos_start + start + blen + later))
-                slots = [-1] * blen + cache.slots(done, later)
-                forward(torch.full((blen + later,), mask_id, dtype=torch.long, device=dev), suffix_pos, done, store_slots=slots, want_logits=False)
+                slots = ([-1] * blen + cache.slots(done, later)) if later > 0 else None
+                out, _ = forward(torch.full((blen + later,), mask_id, dtype=torch.long, device=dev), suffix_pos, done, store_slots=slots,
+                                 logit_rows=None if arch.logit_shift else [0], want_logits=not arch.logit_shift)
+                if not arch.logit_shift:
+                    first_logit = out[0]
             tail_len = later
-            if not arch.logit_shift:
-                raise NotImplementedError("un-shifted (LLaDA) block initialisation is not built")
             # softmax is monotone: a greedy sampler's first token is the arg-max of the logit
-            first = torch.argmax(last_logit) if pick_first_token is None else pick_first_token(last_logit)
+            first = torch.argmax(first_logit) if pick_first_token is None else pick_first_token(first_logit)
         else:
             first = first_token
         ctx = done + tail_len
@@ -538,9 +542,6 @@ def denoise_blocks_batched(model: "PagedDreamModel", caches, *, suffix_pos_start
     import math
 
     arch, dev, n_req = model.arch, model.device, len(caches)
-    if not arch.logit_shift:
-        raise NotImplementedError("un-shifted (LLaDA) block initialisation is not built")
-    page = model.page_size
 
     def packed_forward(ids_rows, pos_rows, ctx_lens, *, slot_rows=None, logit_rows=None, want_logits=True, store_after_attention=False):
         lens = [len(p) for p in pos_rows]
@@ -570,17 +571,22 @@ def denoise_blocks_batched(model: "PagedDreamModel", caches, *, suffix_pos_start
         later = max_new - start - blen
         done = [n0 + start for n0 in prompt_lens]
         block_pos = [list(range(s0 + start, s0 + start + blen)) for s0 in suffix_pos_starts]
-        if later > 0:
+        first_logits = last_logits
+        if later > 0 or not arch.logit_shift:     # un-shifted read-out: the first token comes from the first MASK slot's own row
             masks = torch.full((blen + later,), mask_id, dtype=torch.long, device=dev)
-            packed_forward([masks] * n_req, [list(range(s0 + start, s0 + start + blen + later)) for s0 in suffix_pos_starts], done,
-                           slot_rows=[[-1] * blen + c.slots(d, later) for c, d in zip(caches, done)], want_logits=False)
+            out, _ = packed_forward([masks] * n_req, [list(range(s0 + start, s0 + start + blen + later)) for s0 in suffix_pos_starts], done,
+                                    slot_rows=[[-1] * blen + c.slots(d, later) for c, d in zip(caches, done)] if later > 0 else None,
+                                    logit_rows=None if arch.logit_shift else [i * (blen + later) for i in range(n_req)],
+                                    want_logits=not arch.logit_shift)
+            if not arch.logit_shift:
+                first_logits = [out[i] for i in range(n_req)]
         requests = [dict(positions=block_pos[i], ctx_page_ids=caches[i].page_ids, ctx_len=done[i] + later, last_logit=last_logits[i])
                     for i in range(n_req)]
         runner = model.batched_step_runner(block_len=blen, requests=requests, mask_token_id=mask_id, threshold=float(threshold),
-                                           shift=True, softmax_dtype=softmax_dtype, use_graph=bool(use_graph))
+                                           shift=arch.logit_shift, softmax_dtype=softmax_dtype, use_graph=bool(use_graph))
         for i, block in enumerate(runner.blocks):
             block.fill_(mask_id)
-            block[0] = torch.argmax(last_logits[i])
+            block[0] = torch.argmax(first_logits[i])
         left, step, needed = [blen - 1] * n_req, 0, [0] * n_req
         while any(x > 0 for x in left):
             step += 1

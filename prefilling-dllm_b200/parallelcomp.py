@@ -15,7 +15,10 @@ The default flags run on the fused kernels. Flags off the default path — sampl
 `topk_margin` / `entropy` confidence rules, `alg_temp`, avg-pooling and the other head / layer reductions, the chunk→query score
 direction, the `attention` / `next_block_logits` / per-chunk-draft score modes — reuse the same forwards and finish with a few
 device-side torch ops on [rows, vocab] or [heads, chunk] tensors instead of a fused tail.
-Not built (raise NotImplementedError): YaRN RoPE scaling, the LLaDA leave-one-out scorer.
+`model_backend="llada"` (un-shifted read-out, leave-one-out chunk scores) is built for the joint-prefill cache modes without token
+eviction: the reference's LLaDA model takes no position ids, so a key's position is its index in the concatenated cache, which
+equals this runtime's explicit positions only there.
+Not built (raise NotImplementedError): YaRN RoPE scaling, the LLaDA backend with chunk-local caches or token eviction.
 """
 
 from __future__ import annotations
@@ -275,6 +278,10 @@ class FastDLLMParallelComp:
             raise ValueError(f"Unsupported token_eviction_granularity: {config.token_eviction_granularity}")
         # one generator per runtime for the sampled paths (temperature > 0, alg_temp > 0); seed it with `manual_seed`
         self.sampling_generator: Optional[torch.Generator] = None
+        if self.model_backend == "llada" and (int(config.token_capacity or 0) > 0 or config.cache_build_mode not in {"full_prompt_mask", "full_prompt_query"}):
+            # the reference's LLaDA model takes no position ids: a key's RoPE position is its index in the concatenated cache,
+            # which equals this runtime's positions only for a jointly prefilled, un-evicted prompt
+            raise NotImplementedError("model_backend='llada' is built for the joint-prefill cache modes without token eviction")
         if float(config.rope_scale_factor or 1.0) > 1.0:
             raise NotImplementedError("RoPE (YaRN) scaling is not built")
 
@@ -451,7 +458,7 @@ class FastDLLMParallelComp:
             block = torch.full((draft_len,), mask_id, dtype=torch.long, device=self.device)
             confirmed = torch.zeros(draft_len, dtype=torch.bool, device=self.device)
             if last_logit is not None:
-                block[0] = self._first_block_token(last_logit)
+                block[0] = self._first_block_token(last_logit, cache, block_pos)
             else:
                 raise ValueError("draft needs at least one context token")
             confirmed[0] = True
@@ -572,7 +579,7 @@ class FastDLLMParallelComp:
             target = min(draft_len, max(0, int(partial_steps)))
             filled = 0
             if target > 0:
-                block[0] = self._first_block_token(last_logit)
+                block[0] = self._first_block_token(last_logit, cache, block_pos)
                 filled = 1
             while filled < target and bool((block == mask_id).any()):
                 logits, _ = self._forward_packed([[0] * draft_len], [block_pos], causal=False, cache=cache, ctx_len=cache.length,
@@ -585,9 +592,17 @@ class FastDLLMParallelComp:
         finally:
             cache.release()
 
-    def _first_block_token(self, last_logit: torch.Tensor) -> torch.Tensor:
+    def _first_block_token(self, last_logit: torch.Tensor, cache: Optional[PagedCache] = None, block_pos: Optional[Sequence[int]] = None) -> torch.Tensor:
+        """First token of a block (reference _initialize_fastdllm_suffix_cache :2368-2397): Dream reads it from the last context
+        logit; an un-shifted architecture (LLaDA) from the first MASK slot's own row of a forward of the all-MASK block over
+        the cached context."""
         if not self.arch.logit_shift:
-            raise NotImplementedError("un-shifted (LLaDA) block initialisation is not built")
+            if cache is None or block_pos is None:
+                raise ValueError("the un-shifted read-out needs the cached context to initialise a block")
+            n = len(block_pos)
+            logits, _ = self._forward_packed([[self._mask_token_id()] * n], [list(block_pos)], causal=False, cache=cache, ctx_len=cache.length,
+                                             logit_rows=[0])
+            last_logit = logits[0]
         if self._custom_sampling():
             return self._pick_first_token(last_logit)
         return torch.argmax(last_logit)   # softmax is monotone: the arg-max of the logit
@@ -665,6 +680,10 @@ class FastDLLMParallelComp:
             row_len = p_len + c_len + q_len
             positions = list(range(row_len))
             mask_args = self._mask_args(cfg.score_attention_mask, rows_before_chunk=p_len, chunk_len=c_len, query_len=q_len)
+            if self.model_backend == "llada" and not cfg.score_llada_shift_logits:
+                for idx, chunk in group:
+                    scores[idx] = self._leave_one_out_score(prefix_ids + chunk + query_ids, label_pos, [query_ids[i] for i in local], mask_args)
+                continue
             for off in range(0, len(group), batch_size):
                 batch = group[off:off + batch_size]
                 rows = [prefix_ids + chunk + query_ids for _, chunk in batch]
@@ -674,6 +693,31 @@ class FastDLLMParallelComp:
                 for (idx, _), v in zip(batch, vals):
                     scores[idx] = v if math.isfinite(v) else float("-inf")
         return scores
+
+    def _leave_one_out_score(self, joint_ids: Sequence[int], label_positions: Sequence[int], label_ids: Sequence[int], mask_args: dict) -> float:
+        """Masked-diffusion self-information (reference _llada_leave_one_out_score :1166-1201): one copy of the row per label with
+        that label replaced by MASK, `llada_score_batch_size` copies per packed forward, the label's log-probability read at
+        its OWN row; the mean over the labels."""
+        if not label_positions:
+            return float("-inf")
+        mask_id = self._mask_token_id()
+        batch_size = max(1, int(self.config.llada_score_batch_size or 1))
+        row_len = len(joint_ids)
+        positions = list(range(row_len))
+        base = self.model.ids_tensor(list(joint_ids))
+        total, count = 0.0, 0
+        for off in range(0, len(label_positions), batch_size):
+            pos = [int(p) for p in label_positions[off:off + batch_size]]
+            ids = base.repeat(len(pos))
+            rows = [b * row_len + p for b, p in enumerate(pos)]
+            ids[self.model.ids_tensor(rows)] = mask_id
+            logits, _ = self._forward_packed([joint_ids] * len(pos), [positions] * len(pos), ids_tensor=ids, logit_rows=rows, **mask_args)
+            labels = self.model.ids_tensor([int(t) for t in label_ids[off:off + batch_size]])
+            _, nll = ops.self_information_scores(logits, labels, 1, return_nll=True)      # row i against label i: -log p
+            total -= float(nll.sum().item())
+            count += len(pos)
+        value = total / max(1, count)
+        return value if math.isfinite(value) else float("-inf")
 
     def score_chunk_self_information(self, prefix_ids, chunk_ids, query_ids, score_token_count=None, score_token_mask=None) -> float:
         """One chunk's score (reference :1258-1312): the batched scorer on a batch of one."""
@@ -712,6 +756,8 @@ class FastDLLMParallelComp:
         if min(label_pos) <= 0:
             return float("-inf")
         mask_args = self._mask_args(cfg.score_attention_mask, rows_before_chunk=p_len, chunk_len=c_len, query_len=q_len)
+        if self.model_backend == "llada" and not cfg.score_llada_shift_logits:
+            return self._leave_one_out_score(joint, label_pos, [query_ids[i] for i in local], mask_args)
         logits, _ = self._forward_packed([joint], [list(range(len(joint)))], logit_rows=[p - 1 for p in label_pos], **mask_args)
         value = float(ops.self_information_scores(logits, self.model.ids_tensor([query_ids[i] for i in local]), 1)[0].item())
         return value if math.isfinite(value) else float("-inf")
@@ -1203,6 +1249,8 @@ class FastDLLMParallelComp:
                 self.model.rope_rows(cache.page_ids, 0, stored_pos)
             else:
                 suffix_start = full_q_start + len(query_ids)
+            # un-shifted architectures take the first token from the first MASK slot's own row: the block loop's suffix
+            # initialisation recomputes that row (and the MASK-slot K/V, with the same values) from the prompt K/V
             first = self._first_block_token(last_logit) if (with_masks and self.arch.logit_shift) else None
             fixed_steps = None
             if cfg.alg != "confidence_threshold":     # reference :2927-2929, :2977-2985

@@ -121,6 +121,32 @@ def test_pd_split_with_unshifted_logits(ckpt, cpu_model):
         eng.generate_partial_draft_rounds_for_selection(prompt, max_new_tokens=4, partial_rounds=1)
 
 
+def test_several_blocks_with_unshifted_logits(ckpt, cpu_model):
+    """Records of three blocks (80 tokens) on the un-shifted read-out: every block's first token comes from the first MASK
+    slot's own row of the suffix initialisation. One by one and in shared steps, against the restated block loop."""
+    import dataclasses
+
+    from oracle import engine_flow as E
+
+    eng = _engine(ckpt, pages=24)
+    eng.model.arch = dataclasses.replace(eng.model.arch, logit_shift=False)
+    prompts = [_prompt(500, seed=51), _prompt(333, seed=52)]
+    wants = [E.decode_blocks(cpu_model, p, max_new=80, block_length=BLOCK, mask_id=MASK, threshold=0.9, shift=False) for p in prompts]
+    free0 = eng._prefix_cache.num_free_pages
+    for p, want in zip(prompts, wants):
+        out = eng.decode_from_pd_record(eng.prefill_to_pd_record(p, max_new_tokens=80), max_new_tokens=80)
+        assert out.token_ids == want["token_ids"] and out.n_diff_steps == want["n_diff_steps"]
+    shared = eng.decode_from_pd_records([eng.prefill_to_pd_record(p, max_new_tokens=80) for p in prompts], max_new_tokens=80)
+    for out, want in zip(shared, wants):
+        assert out.token_ids == want["token_ids"] and out.n_diff_steps == want["n_diff_steps"]
+    from prefilling_dllm_b200 import ops
+
+    ops.check_status(eng.device)
+    while eng._prefix_cache.evict_one():
+        pass
+    assert eng._prefix_cache.num_free_pages == free0
+
+
 def test_snapshot_load_and_engine_to_engine_copy(engine, ckpt):
     other = _engine(ckpt, pages=16)
     prompt = _prompt(700, seed=5)

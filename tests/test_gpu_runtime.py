@@ -211,6 +211,32 @@ def _check_against_golden(ref, toy_ckpt, variant):
     assert frac >= 0.99
 
 
+def test_llada_backend_matches_the_restated_flow(toy_ckpt):
+    """model_backend="llada" on the toy weights: un-shifted read-out (a block's first token from the first MASK slot's own row,
+    slot p read at logits[p]), leave-one-out chunk scores, joint prefill. The reference needs the Fast-dLLM v1 LLaDA plug-in to
+    run this backend, so the checker is the CPU restatement `oracle.toy_request.run_port(backend="llada")`."""
+    import make_golden
+    from oracle import toy_request
+    from oracle.contract_model.model.modeling_dream import DreamModel
+    from prefilling_dllm_b200 import ops
+    from prefilling_dllm_b200.parallelcomp import load_fastdllm_parallelcomp
+
+    context, query = make_golden.toy_inputs()
+    flags = dict(make_golden.README_FLAGS)
+    want = toy_request.run_port(DreamModel.from_pretrained(toy_ckpt).eval(), context, query, flags, backend="llada")
+    shifted = toy_request.run_port(DreamModel.from_pretrained(toy_ckpt).eval(), context, query, flags)
+    assert want["selected"] != shifted["selected"]          # the two backends really differ on this input
+    rt = load_fastdllm_parallelcomp(pretrained=toy_ckpt, device="cuda", dtype="float32", model_backend="llada", **flags)
+    result = rt.generate(prefix_ids=rt.bos_ids(), context_ids=context, query_ids=query)
+    ops.check_status(rt.device)
+    assert max(abs(result.chunk_scores[i] - s) for i, s in enumerate(want["scores"])) < 1e-4
+    assert result.selected_chunk_indices == want["selected"]
+    assert _match_fraction(result.sequences, want["sequences"]) >= 0.99
+    assert rt.model.allocator.num_free_pages == rt.model.num_pages
+    with pytest.raises(NotImplementedError):
+        load_fastdllm_parallelcomp(pretrained=toy_ckpt, dtype="float32", model_backend="llada", **dict(flags, token_capacity=128))
+
+
 def test_runtime_rejects_what_is_not_built(toy_ckpt):
     from prefilling_dllm_b200.parallelcomp import load_fastdllm_parallelcomp
 

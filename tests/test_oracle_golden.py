@@ -258,6 +258,22 @@ def test_block_denoising(golden, model, inputs, chunks, variant):
     assert states == [s for s in ref["block_states_before_each_forward"] if len(s) == blen]
 
 
+def test_engine_flow_block_loop_reproduces_the_two_block_golden(golden, model, inputs, chunks):
+    """`oracle.engine_flow.decode_blocks` (the checker of the engine's records of several blocks) on the prompt of the reference
+    class's `two_blocks` run: its ids. That run keeps the prefill's MASK-slot K/V for the first block where this function
+    recomputes them from the prompt K/V, which gives the same values."""
+    from oracle import engine_flow as E
+
+    ref = golden["runs"]["two_blocks"]
+    _, query = inputs
+    prompt = [BOS] + [t for ci in ref["selected_chunk_indices"] for t in chunks[ci]] + query
+    out = E.decode_blocks(model, prompt, max_new=64, block_length=32, mask_id=MASK, threshold=ref["flags"]["threshold"], shift=True,
+                          softmax_dtype=None)
+    assert out["token_ids"] == ref["sequences"]
+    unshifted = E.decode_blocks(model, prompt, max_new=40, block_length=32, mask_id=MASK, threshold=ref["flags"]["threshold"], shift=False)
+    assert len(unshifted["token_ids"]) == 40 and MASK not in unshifted["token_ids"] and unshifted["token_ids"] != ref["sequences"][:40]
+
+
 def test_whole_request_port_and_staged_reference_class(golden, model, inputs, tmp_path):
     """The chained CPU restatement of a whole README-flags request reproduces the golden ids and selection; when the
     reference's own class is staged under oracle/_ref it is run as well (it is what produced the golden)."""
