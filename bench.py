@@ -782,7 +782,7 @@ def run_request(args, rank: int, world: int, local_rank: int):
             "e2e": {"value": world * new_tokens / (ms_request * 1e-3), "unit": "tok/s", "request_latency_ms": ms_request,
                     "h2d_bytes_per_step": (len(context) + len(query) + 1) * 8 * 2, "d2h_bytes_per_step": new_tokens * 8 + denoise_steps * 4,
                     "what": "host token-id lists in (ids and RoPE positions uploaded), generated ids out as a host list; one 4-byte count read per denoise step"},
-            "phases_ms": phases, "denoise_steps": denoise_steps, "ms_per_denoise_step": phases["decode"] / (denoise_steps + 1),
+            "phases_ms": phases, "denoise_steps": denoise_steps, "ms_per_denoise_step": phases["decode"] / max(1, denoise_steps),
             "selected_chunks": list(result.selected_chunk_indices),
             "gpu_launches": launches, "clocks": clocks,
         }
@@ -1089,6 +1089,24 @@ def run_byte_kernels(args, local_rank: int):
         ops.unmask_step(logit_sets[i % 2][i % 16], ids, mask_token_id=vocab - 1, threshold=0.9, last_logit=last, shift=True,
                         softmax_dtype=torch.float32)
     timed("unmask_kernel (+ a 256-byte copy that resets the block)", "[32, 152064] bf16 logits, one block", rows * vocab * 2, unmask, 32)
+
+    # row ops of the transformer block at the two shapes of a request: one denoise block (32 rows) and the scoring prefill (8744 rows)
+    hq, hidden = 28, 3584
+    ln_w = torch.ones(hidden, device=device, dtype=torch.bfloat16)
+    for n_rows, sets in ((32, 16), (8744, 4)):
+        xs = [torch.randn(n_rows, hidden, device=device, dtype=torch.bfloat16, generator=g) for _ in range(sets)]
+        ds = [torch.randn(n_rows, hidden, device=device, dtype=torch.bfloat16, generator=g) for _ in range(sets)]
+        timed("add_rmsnorm_vec_kernel (residual add + RMSNorm)", f"{n_rows} rows x 3584 bf16", n_rows * hidden * 2 * 5,
+              lambda i, xs=xs, ds=ds: ops.add_rmsnorm(xs[i], ln_w, 1e-6, ds[i]), sets)
+        qkvs = [torch.randn(n_rows, hq + 2 * hkv, d, device=device, dtype=torch.bfloat16, generator=g) for _ in range(sets)]
+        cos = torch.randn(n_rows, d, device=device, dtype=torch.bfloat16, generator=g)
+        rs_k = torch.zeros(40, page, hkv, d, device=device, dtype=torch.bfloat16)
+        rs_v = torch.zeros_like(rs_k)
+        rs_slots = torch.randperm(40 * page, device=device, generator=g)[:n_rows].to(torch.int32)
+        timed("rope_store_kernel (RoPE of q, k in place + page write of k, v)", f"{n_rows} rows x (28 + 2 x 4) heads x 128 bf16",
+              n_rows * ((hq + hkv) * d * 2 * 2 + 2 * hkv * d * 2 * 2 + 2 * d * 2),
+              lambda i, qkvs=qkvs: ops.rope_store(qkvs[i], cos, cos, hq, hkv, rs_k, rs_v, rs_slots), sets)
+        del xs, ds, qkvs
 
     # (2a) self-information tail: 8 chunks x 66 label rows of bf16 logits
     n_chunks, n_lab = 8, 66

@@ -224,6 +224,7 @@ class PagedDreamModel:
                 wqkv=wqkv.contiguous(), bqkv=bqkv, wo=get(p + "self_attn.o_proj.weight"), wgu=wgu,
                 wd=get(p + "mlp.down_proj.weight")))
         self.inv_freq = (1.0 / (a.rope_theta ** (torch.arange(0, a.head_dim, 2, dtype=torch.int64).float() / a.head_dim))).to(dev)
+        self.rope_attention_scaling = 1.0      # YaRN's factor on cos / sin (1 without scaling)
         # pool [2 (k,v), layers, pages, page_size, Hkv, D] — same shape as the engine's kv_cache (engine/model_runner.py:557-567)
         self.kv_cache = torch.zeros((2, a.num_hidden_layers, self.num_pages, self.page_size, a.num_key_value_heads, a.head_dim),
                                     dtype=dt, device=dev)
@@ -276,10 +277,42 @@ class PagedDreamModel:
         return cls(arch, state, device=dev, dtype=dtype, num_pages=num_pages, page_size=page_size)
 
     # ---- pieces ----
+    def apply_yarn_rope_scaling(self, factor: float, original_max_position_embeddings: Optional[int] = None,
+                                beta_fast: float = 32.0, beta_slow: float = 1.0) -> None:
+        """YaRN context extension (Peng et al. 2023) as the reference applies it (prefilling_dllm_eval/fastdllm_parallelcomp.py
+        :539-553: rope_scaling = {rope_type: yarn, factor, original_max_position_embeddings}, the rotary table rebuilt): the
+        high-frequency dimensions keep their frequency, the low-frequency ones are divided by `factor`, a linear ramp between the
+        dimensions that complete `beta_fast` and `beta_slow` rotations within the original context blends the two, and cos / sin
+        are multiplied by 0.1 ln(factor) + 1. Pages written before the call keep their old rotation."""
+        if factor <= 1.0:
+            return
+        import math
+
+        a = self.arch
+        dim, base = a.head_dim, float(a.rope_theta)
+        original = int(original_max_position_embeddings or a.max_position_embeddings)
+        pos_freqs = base ** (torch.arange(0, dim, 2).float() / dim)
+        extrapolation, interpolation = 1.0 / pos_freqs, 1.0 / (factor * pos_freqs)
+
+        def correction_dim(rotations: float) -> float:
+            return (dim * math.log(original / (rotations * 2 * math.pi))) / (2 * math.log(base))
+
+        low = max(math.floor(correction_dim(beta_fast)), 0)
+        high = min(math.ceil(correction_dim(beta_slow)), dim - 1)
+        if low == high:
+            high += 0.001
+        keep = 1 - torch.clamp((torch.arange(dim // 2, dtype=torch.float32) - low) / (high - low), 0, 1)
+        self.inv_freq = (interpolation * (1 - keep) + extrapolation * keep).to(self.device)
+        self.rope_attention_scaling = 0.1 * math.log(factor) + 1.0
+        self.__dict__.pop("_step_graphs", None)        # captured steps hold no tables, but shapes may change with longer contexts
+
     def _rope_tables(self, positions: torch.Tensor) -> Tuple[torch.Tensor, torch.Tensor]:
         freqs = positions.float().unsqueeze(-1) * self.inv_freq.unsqueeze(0)  # [T, D/2] fp32
         emb = torch.cat((freqs, freqs), dim=-1)
-        return emb.cos().to(self.dtype).unsqueeze(1), emb.sin().to(self.dtype).unsqueeze(1)  # [T, 1, D]
+        cos, sin = emb.cos(), emb.sin()
+        if self.rope_attention_scaling != 1.0:
+            cos, sin = cos * self.rope_attention_scaling, sin * self.rope_attention_scaling
+        return cos.to(self.dtype).unsqueeze(1), sin.to(self.dtype).unsqueeze(1)  # [T, 1, D]
 
     def layer_cache(self, layer: int) -> Tuple[torch.Tensor, torch.Tensor]:
         return self.kv_cache[0, layer], self.kv_cache[1, layer]

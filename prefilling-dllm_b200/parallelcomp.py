@@ -18,7 +18,7 @@ device-side torch ops on [rows, vocab] or [heads, chunk] tensors instead of a fu
 `model_backend="llada"` (un-shifted read-out, leave-one-out chunk scores) is built for the joint-prefill cache modes without token
 eviction: the reference's LLaDA model takes no position ids, so a key's position is its index in the concatenated cache, which
 equals this runtime's explicit positions only there.
-Not built (raise NotImplementedError): YaRN RoPE scaling, the LLaDA backend with chunk-local caches or token eviction.
+Not built (raise NotImplementedError): the LLaDA backend with chunk-local caches or token eviction.
 """
 
 from __future__ import annotations
@@ -282,8 +282,6 @@ class FastDLLMParallelComp:
             # the reference's LLaDA model takes no position ids: a key's RoPE position is its index in the concatenated cache,
             # which equals this runtime's positions only for a jointly prefilled, un-evicted prompt
             raise NotImplementedError("model_backend='llada' is built for the joint-prefill cache modes without token eviction")
-        if float(config.rope_scale_factor or 1.0) > 1.0:
-            raise NotImplementedError("RoPE (YaRN) scaling is not built")
 
         if model is None:
             dtype = _resolve_dtype(config.dtype)
@@ -296,6 +294,10 @@ class FastDLLMParallelComp:
             model = PagedDreamModel.from_pretrained(config.pretrained, device=self.device, dtype=dtype, num_pages=pages, arch=arch)
         self.model = model
         self.arch = model.arch
+        if float(config.rope_scale_factor or 1.0) > 1.0:
+            if self.model_backend == "llada" and (config.rope_scaling_type or "yarn").lower() != "yarn":
+                raise NotImplementedError("linear RoPE scaling of the LLaDA backend is not built (yarn is)")
+            model.apply_yarn_rope_scaling(float(config.rope_scale_factor))      # reference _apply_rope_scaling :539-553
         if tokenizer is None:
             tokenizer = _load_tokenizer(config.pretrained, config.trust_remote_code) or _SimpleTokenizer(self.arch)
         self.tokenizer = tokenizer

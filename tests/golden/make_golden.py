@@ -249,6 +249,8 @@ FLAG_VARIANTS = {
     # draft round takes is torch.topk's unspecified choice among ties, and later rounds depend on it
     "sample_temperature_top_k_1": dict(README_FLAGS, score_mode="self_information", temperature=0.7, top_k=1),
     "alg_topk_margin": dict(README_FLAGS, alg="topk_margin", diffusion_steps=8),
+    # YaRN context extension: inverse frequencies blended between extrapolation and interpolation, cos / sin scaled
+    "rope_yarn_factor_4": dict(README_FLAGS, rope_scale_factor=4.0),
     "alg_entropy": dict(README_FLAGS, alg="entropy", diffusion_steps=8),
 }
 

@@ -125,12 +125,13 @@ def test_runtime_matches_reference_golden(golden, toy_ckpt, variant):
                                      "score_mode_per_chunk_draft", "evict_avgpool_head_max_layer_sum",
                                      "evict_nopool_head_mean_layer_max_keep_low", "evict_per_head_avgpool_chunk_query",
                                      "evict_bidirectional_full_mask", "evict_query_to_chunk_mask_chunk_query", "evict_use_generated_query",
-                                     "sample_top_k_top_p_greedy", "sample_temperature_top_k_1", "alg_topk_margin", "alg_entropy"])
+                                     "sample_top_k_top_p_greedy", "sample_temperature_top_k_1", "alg_topk_margin", "alg_entropy",
+                                     "rope_yarn_factor_4"])
 def test_runtime_matches_reference_golden_off_the_default_flags(golden_flags, toy_ckpt, variant):
     """Flags off the README path, each against what the unmodified reference class produced with the same flags: joint-chunk
     scoring, the query_to_chunk and full score masks, the other score modes, avg-pooling and the other head / layer reductions,
-    the bidirectional score direction, top-k / top-p filtering, a temperature draw made deterministic by top-k 1, and the margin
-    and entropy confidence rules of the fixed-step sampler."""
+    the bidirectional score direction, top-k / top-p filtering, a temperature draw made deterministic by top-k 1, the margin
+    and entropy confidence rules of the fixed-step sampler, and YaRN RoPE scaling."""
     _check_against_golden(golden_flags["runs"][variant], toy_ckpt, variant)
 
 
@@ -241,7 +242,7 @@ def test_runtime_rejects_what_is_not_built(toy_ckpt):
     from prefilling_dllm_b200.parallelcomp import load_fastdllm_parallelcomp
 
     with pytest.raises(NotImplementedError):
-        load_fastdllm_parallelcomp(pretrained=toy_ckpt, dtype="float32", rope_scale_factor=2.0)
+        load_fastdllm_parallelcomp(pretrained=toy_ckpt, dtype="float32", model_backend="llada", cache_build_mode="chunk_query")
     with pytest.raises(ValueError):
         load_fastdllm_parallelcomp(pretrained=toy_ckpt, dtype="float32", token_eviction_granularity="rows")
     with pytest.raises(ValueError):
