@@ -411,7 +411,7 @@ def op_linear(device: torch.device, steps: int, only: str = ""):
     g = torch.Generator(device=device).manual_seed(4000)
     rec = {}
     shapes = [("qkv", 4608, 3584), ("o", 3584, 3584), ("gate_up", 37888, 3584), ("down", 3584, 18944), ("lm_head", 152064, 3584)]
-    for m in (32, 8744):
+    for m in (32, 512, 8744):          # one block of rows, 16 blocks sharing a step, the scoring prefill
         for name, n, k in shapes:
             if (m > 128 and name == "lm_head") or (only and only != f"{name}_m{m}"):
                 continue
@@ -420,7 +420,7 @@ def op_linear(device: torch.device, steps: int, only: str = ""):
             x = torch.randn(m, k, device=device, dtype=torch.bfloat16, generator=g)
             out = torch.empty(m, n, device=device, dtype=torch.bfloat16)
             calls = 8
-            t_mine = timed_graph(lambda: [ops.linear(x, ws[i % copies], out=out) for i in range(calls)], device, replays=max(3, min(steps, 10))) / calls * 1e3
+            t_mine = timed_graph(lambda: [ops.linear(x, ws[i % copies], out=out, weights_at_rest=True) for i in range(calls)], device, replays=max(3, min(steps, 10))) / calls * 1e3
             t_lib = timed_graph(lambda: [torch.matmul(x, ws[i % copies].t(), out=out) for i in range(calls)], device, replays=max(3, min(steps, 10))) / calls * 1e3
             ops.check_status(device)
             nbytes = (n * k + m * k + m * n) * 2
