@@ -1096,7 +1096,7 @@ def run_byte_kernels(args, local_rank: int):
     for n_rows, sets in ((32, 16), (8744, 4)):
         xs = [torch.randn(n_rows, hidden, device=device, dtype=torch.bfloat16, generator=g) for _ in range(sets)]
         ds = [torch.randn(n_rows, hidden, device=device, dtype=torch.bfloat16, generator=g) for _ in range(sets)]
-        timed("add_rmsnorm_vec_kernel (residual add + RMSNorm)", f"{n_rows} rows x 3584 bf16", n_rows * hidden * 2 * 5,
+        timed("add_rmsnorm_vec_kernel (residual add + RMSNorm)", f"{n_rows} rows x 3584 bf16", n_rows * hidden * 2 * 4,      # x and delta read, x and out written
               lambda i, xs=xs, ds=ds: ops.add_rmsnorm(xs[i], ln_w, 1e-6, ds[i]), sets)
         qkvs = [torch.randn(n_rows, hq + 2 * hkv, d, device=device, dtype=torch.bfloat16, generator=g) for _ in range(sets)]
         cos = torch.randn(n_rows, d, device=device, dtype=torch.bfloat16, generator=g)
