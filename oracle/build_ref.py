@@ -10,6 +10,11 @@ to a GPU machine, where the checkout itself does not exist:
     kv_cache_kernels, triton_eviction_scorer}.py — the reference's Triton kernels, which on a GPU machine pin the op-level
     oracle (tests/test_gpu_reference_kernels.py) and are the same-box baseline that bench.py times.
 
+  * prefilling_dllm_engine/prefilling_dllm/ (the whole engine package, 0.7 MB) + prefilling_dllm_eval/model_cache/dream/
+    configuration_dream.py — the reference's PD engine `FastDLLMDreamEngine`, which constructs CUDA state and therefore runs
+    on a GPU machine only: tests/golden/make_engine_golden.py drives it there, unmodified, over the toy checkpoint and
+    writes the fixture that pins oracle/engine_flow.py and the engine facade of this library.
+
     python oracle/build_ref.py --reference /path/to/reference        (or PDLLM_REFERENCE_ROOT)
 
 `load_eval_module()` / `load_engine_ops()` import the staged files; they raise RefUnavailable when nothing was staged.
@@ -44,7 +49,38 @@ def stage(reference_root: str) -> str:
         os.makedirs(dst_dir, exist_ok=True)
         for name in names:
             shutil.copyfile(os.path.join(src_dir, name), os.path.join(dst_dir, name))
+    # the engine package as a tree, and the configuration class a Dream checkpoint names in its auto_map
+    engine_dst = os.path.join(REF_DIR, "engine")
+    if os.path.isdir(os.path.join(engine_dst, "prefilling_dllm")):
+        shutil.rmtree(os.path.join(engine_dst, "prefilling_dllm"))
+    shutil.copytree(os.path.join(reference_root, "prefilling_dllm_engine", "prefilling_dllm"), os.path.join(engine_dst, "prefilling_dllm"),
+                    ignore=shutil.ignore_patterns("__pycache__", "*.pyc"))
+    shutil.copyfile(os.path.join(reference_root, "prefilling_dllm_eval", "model_cache", "dream", "configuration_dream.py"),
+                    os.path.join(engine_dst, "configuration_dream.py"))
     return REF_DIR
+
+
+def engine_staged() -> bool:
+    return os.path.exists(os.path.join(REF_DIR, "engine", "prefilling_dllm", "fastdllm_engine.py"))
+
+
+def load_reference_engine():
+    """The reference's `prefilling_dllm.fastdllm_engine` module, imported from the staged package tree (GPU machine only: its
+    model runner initialises CUDA and NCCL). `easydict` is served by oracle/shims when the image lacks it."""
+    if not engine_staged():
+        raise RefUnavailable("oracle/_ref/engine is empty: run oracle/build_ref.py where a reference checkout exists")
+    for name in [n for n in sys.modules if n == "prefilling_dllm" or n.startswith("prefilling_dllm.")]:
+        del sys.modules[name]           # stand-ins left by load_engine_ops()
+    root = os.path.join(REF_DIR, "engine")
+    if root not in sys.path:
+        sys.path.insert(0, root)
+    try:
+        import easydict  # noqa: F401
+    except ImportError:
+        sys.path.append(os.path.join(HERE, "shims"))
+    import prefilling_dllm.fastdllm_engine as module  # noqa: the staged, unmodified reference engine
+
+    return module
 
 
 def staged() -> bool:

@@ -7,9 +7,10 @@ make every chunk's work depend only on `[prefix ‖ chunk ‖ query ‖ draft]`,
   2. rank r scores the chunks it owns — `[r·N/W, (r+1)·N/W)` with the remainder on the first ranks;
   3. ONE all-gather of the fp32 scores; every rank then ranks all N scores with the same stable rule and holds the
      same selection (no second collective);
-  4. the owner of each selected chunk evicts and prefills it locally, which needs the selection only for the chunk's
-     RoPE start in `continuous` position mode;
-  5. the owners send the kept KV rows of all layers (one contiguous `[kept, layers, 2, Hkv, D]` payload per chunk — ONE gather
+  4. the selected chunks are dealt round-robin over the ranks, starting at the decode rank (a chunk's prefill needs only its
+     token ids and the selection, not its scoring pass, and selected chunks cluster where the relevant text is: no rank
+     prefills more than ceil(K / W) of them); each rank evicts and prefills its share locally;
+  5. those ranks send the kept KV rows of all layers (one contiguous `[kept, layers, 2, Hkv, D]` payload per chunk — ONE gather
      launch over the pool seen as `2 * layers * pages` pages — plus the kept RoPE positions) to the decode rank with grouped
      point-to-point operations. The decode rank receives every payload straight into its slice of one buffer and writes
      all layers of all chunks into its own page pool with ONE page-write launch (a slot mapping over every layer), in
@@ -97,9 +98,20 @@ class KVTransfer:
     kept_tokens: int
 
 
-def plan_kv_transfers(selected: Sequence[int], kept_tokens: Dict[int, int], plan: ChunkShardPlan) -> List[KVTransfer]:
-    """One transfer per selected chunk, in selected-index order (the order of the decode cache)."""
-    return [KVTransfer(chunk_index=ci, order=order, src_rank=plan.owner(ci), kept_tokens=int(kept_tokens[ci]))
+def prefill_ranks(selected: Sequence[int], world_size: int, decode_rank: int = 0) -> Dict[int, int]:
+    """Which rank prefills which SELECTED chunk. Scoring is sharded by contiguous ownership (`ChunkShardPlan`), but the
+    selected chunks cluster wherever the relevant text is, and a chunk's prefill needs nothing of its scoring pass — every rank
+    holds the token ids and, after the all-gather, the selection. So the selected chunks are dealt round-robin, starting
+    at the decode rank (whose share then needs no transfer): no rank prefills more than ceil(K / W) chunks."""
+    return {ci: (decode_rank + order) % world_size for order, ci in enumerate(selected)}
+
+
+def plan_kv_transfers(selected: Sequence[int], kept_tokens: Dict[int, int], plan: ChunkShardPlan,
+                      src_ranks: Optional[Dict[int, int]] = None) -> List[KVTransfer]:
+    """One transfer per selected chunk, in selected-index order (the order of the decode cache). `src_ranks[ci]`: the rank that
+    holds chunk ci's prefilled KV (default: the chunk's scoring owner)."""
+    return [KVTransfer(chunk_index=ci, order=order, src_rank=plan.owner(ci) if src_ranks is None else int(src_ranks[ci]),
+                       kept_tokens=int(kept_tokens[ci]))
             for order, ci in enumerate(selected)]
 
 
@@ -206,7 +218,8 @@ class ShardedChunkPrefill:
         all_scores = all_gather_chunk_scores(local_t, plan, self.rank, self.group).tolist()
         selected = rank_chunks(all_scores, int(cfg.topk_chunks), bool(cfg.keep_first_chunk))
         scores = {i: (s if math.isfinite(s) else float("-inf")) for i, s in enumerate(all_scores)}
-        # 4: owners evict + prefill their selected chunks into a scratch cache [prefix ‖ chunk rows]
+        # 4: the selected chunks, dealt evenly over the ranks, are evicted + prefilled into a scratch cache [prefix ‖ chunk rows]
+        prefill_on = prefill_ranks(selected, self.world, decode_rank)
         evict_q = rt._token_eviction_query_ids(scoring_query_ids, selection_q, mask)
         window_q = rt._window_query(selection_q, cfg.token_score_query_window)
         p_len = len(prefix_ids)
@@ -216,7 +229,7 @@ class ShardedChunkPrefill:
         positions: Dict[int, torch.Tensor] = {}
         unions: Dict[int, List[int]] = {}
         for order, ci in enumerate(selected):
-            if plan.owner(ci) != self.rank:
+            if prefill_on[ci] != self.rank:
                 continue
             chunk = list(chunks[ci])
             scratch = PagedCache(rt, p_len + 2 * len(chunk) + rt.model.page_size)
@@ -234,7 +247,7 @@ class ShardedChunkPrefill:
             finally:
                 scratch.release()
         # 5: hand-off to the decode rank
-        transfers = plan_kv_transfers(selected, kept_tokens, plan)
+        transfers = plan_kv_transfers(selected, kept_tokens, plan, prefill_on)
         recv_into = None
         if self.rank == decode_rank and selected:
             # every chunk's payload lands in its slice of one [sum kept, layers, 2, Hkv, D] buffer, in selected order

@@ -12,7 +12,7 @@ import torch.multiprocessing as mp
 
 sys.path.insert(0, os.path.dirname(os.path.dirname(os.path.abspath(__file__))))
 
-from prefilling_dllm_b200.sharded import (ChunkShardPlan, all_gather_chunk_scores, exchange_chunk_kv, plan_kv_transfers,  # noqa: E402
+from prefilling_dllm_b200.sharded import (ChunkShardPlan, all_gather_chunk_scores, exchange_chunk_kv, plan_kv_transfers, prefill_ranks,  # noqa: E402
                                           rank_chunks)
 
 
@@ -97,3 +97,17 @@ def test_two_ranks_agree_on_selection_and_hand_off_kv(n_chunks):
     assert all(p.exitcode == 0 for p in procs), [p.exitcode for p in procs]
     results = dict(out.get(timeout=5) for _ in range(2))
     assert results[0] == results[1] and len(results[0]) == 3
+
+
+def test_selected_chunks_are_dealt_evenly_for_the_prefill():
+    """Selected chunks cluster (here six of eight in one rank's scoring range); their prefill is dealt round-robin from the
+    decode rank, and the transfers follow that assignment."""
+    selected = [8, 9, 10, 11, 12, 13, 20, 31]
+    for world, decode_rank in ((2, 0), (4, 1), (8, 0), (3, 2)):
+        ranks = prefill_ranks(selected, world, decode_rank)
+        load = [sum(1 for r in ranks.values() if r == w) for w in range(world)]
+        assert max(load) == -(-len(selected) // world) and ranks[selected[0]] == decode_rank
+        plan = ChunkShardPlan(32, world)
+        transfers = plan_kv_transfers(selected, {ci: 256 for ci in selected}, plan, ranks)
+        assert [t.src_rank for t in transfers] == [ranks[ci] for ci in selected]
+        assert [t.src_rank for t in plan_kv_transfers(selected, {ci: 256 for ci in selected}, plan)] == [plan.owner(ci) for ci in selected]
