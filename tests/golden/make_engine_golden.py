@@ -3,7 +3,7 @@
 `FastDLLMDreamEngine` (prefilling_dllm_engine/prefilling_dllm/fastdllm_engine.py:170) builds a model runner that initialises
 CUDA and NCCL, so unlike the eval class (make_golden.py) it cannot run on a CPU box. This script runs it where a GPU is
 present, from the copy staged under oracle/_ref/engine (oracle/build_ref.py; byte-for-byte, git-ignored), over the seeded toy
-checkpoint of make_golden.py in float32, and records what the engine-side parity tests compare:
+checkpoint of make_golden.py, and records what the engine-side parity tests compare:
 
   * the prefill/decode split: first token, last-context logit, denoised ids and step count of `prefill_to_pd_record` →
     `decode_from_pd_record` for three prompts, a checksum of the snapshot KV, and the same request through
@@ -15,6 +15,14 @@ checkpoint of make_golden.py in float32, and records what the engine-side parity
 
     python oracle/build_ref.py --reference <checkout>          # where the checkout exists
     python tests/golden/make_engine_golden.py --out tests/golden/engine_reference.json     # on a machine with a GPU
+
+Model dtype. The fixture is made with the checkpoint declared float64 and the reference's `sdpa` attention backend. In float32
+the reference engine does not compute the model: its RMSNorm (layers/layernorm.py:18-41) converts with `x.to(torch.float32)`,
+which for a float32 input is the SAME tensor, and then normalises in place — so the residual stream is overwritten by its own
+normalised copy in every layer (in bfloat16, the dtype it is deployed in, the conversion copies and the arithmetic is the
+model's). Declared float64, every conversion copies again: norms and RoPE are evaluated in float32 as in deployment, the
+products in float64, and the result is the model's arithmetic to ~1e-7 — what a float32 restatement can be held to bit for
+bit on discrete outputs. `--dtype float32` reproduces the aliasing artefact (first token 989 instead of 290 on the first prompt).
 
 If the reference engine cannot be constructed there, the script writes {"unavailable": "<exception>"} so that the reason
 is on record; the tests then keep oracle/engine_flow.py as their checker.
@@ -45,7 +53,7 @@ def prompt(n=600, seed=3):
     return [BOS] + torch.randint(3, 1000, (n - 1,), generator=g).tolist()
 
 
-def toy_checkpoint_for_the_engine(path: str) -> None:
+def toy_checkpoint_for_the_engine(path: str, dtype: str) -> None:
     """The toy checkpoint plus what the engine's loader wants: an auto_map to the Dream configuration class the reference
     vendors (staged copy), since its Config resolves the model through AutoConfig with trust_remote_code."""
     from oracle import build_ref
@@ -57,6 +65,7 @@ def toy_checkpoint_for_the_engine(path: str) -> None:
         cfg = json.load(handle)
     cfg["auto_map"] = {"AutoConfig": "configuration_dream.DreamConfig"}
     cfg["architectures"] = ["DreamModel"]
+    cfg["torch_dtype"] = dtype
     with open(cfg_path, "w") as handle:
         json.dump(cfg, handle)
 
@@ -82,12 +91,16 @@ def record(engine) -> dict:
         runs.append(item)
     out["pd_split"] = runs
     # ---- post-hoc eviction with head-independent keep indices ----
-    ids = prompt(600, 3)
-    keep = [0] + list(range(7, 600, 3))
+    ids = prompt(600, 7)
+    keep = [0] + list(range(1, 600, 3))
     nested = [[list(keep) for _ in range(2)] for _ in range(2)]
-    rec = engine.prefill_to_pd_record(ids, max_new_tokens=BLOCK, prompt_keep_indices_per_layer_per_head=nested)
+    rec = engine.prefill_to_pd_record(ids, max_new_tokens=BLOCK, prompt_keep_indices_per_layer_per_head=nested, active_prompt_positions=keep)
+    item = dict(prompt_len=600, seed=7, keep=keep, kv_mode=str(rec.kv_mode), prompt_len_record=int(rec.prompt_len),
+                full_prompt_len=int(rec.full_prompt_len), first_token_id=int(rec.first_token_id),
+                suffix_positions=[int(p) for p in rec.suffix_positions])
     res = engine.decode_from_pd_record(rec, max_new_tokens=BLOCK)
-    out["posthoc_eviction"] = dict(keep=keep, token_ids=[int(t) for t in res.token_ids], n_diff_steps=int(res.n_diff_steps))
+    item.update(token_ids=[int(t) for t in res.token_ids], n_diff_steps=int(res.n_diff_steps))
+    out["posthoc_eviction"] = item
     # ---- selection twins ----
     context, query = make_golden.toy_inputs()
     chunks = []
@@ -132,15 +145,21 @@ def make_golden_split(ids, size):
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--out", default=os.path.join(HERE, "engine_reference.json"))
+    ap.add_argument("--dtype", default="float64", choices=["float64", "float32", "bfloat16"],
+                    help="model dtype of the reference engine (see the module docstring for why float64)")
+    ap.add_argument("--attention-backend", default="sdpa", choices=["sdpa", "flex"],
+                    help="the reference's PREFILLING_DLLM_ENGINE_ATTENTION_BACKEND (attention_v4.py:38); flex has no float64 kernel")
     args = ap.parse_args()
-    golden = {"config": dict(make_golden.TOY), "dtype": "float32", "block_length": BLOCK, "threshold": 0.9}
+    os.environ["PREFILLING_DLLM_ENGINE_ATTENTION_BACKEND"] = args.attention_backend
+    golden = {"config": dict(make_golden.TOY), "dtype": args.dtype, "attention_backend": args.attention_backend, "block_length": BLOCK,
+              "threshold": 0.9}
     tmp = tempfile.mkdtemp()
     try:
         from oracle import build_ref
 
         module = build_ref.load_reference_engine()
         ckpt = os.path.join(tmp, "ckpt_toy_engine")
-        toy_checkpoint_for_the_engine(ckpt)
+        toy_checkpoint_for_the_engine(ckpt, args.dtype)
         engine = module.FastDLLMDreamEngine(ckpt, max_model_len=8192, block_length=BLOCK, mask_token_id=MASK, threshold=0.9,
                                             gpu_memory_utilization=0.05, enforce_eager=True)
         try:
