@@ -712,6 +712,106 @@ def run_full_reencode(args, local_rank: int):
                                          "speedup_of_this_path": naive_ms / path_ms}}
 
 
+def run_reference_engine_8k(args, local_rank: int):
+    """`--workload reference_engine_8k`: the UNMODIFIED reference PD engine (`FastDLLMDreamEngine`, staged under oracle/_ref/engine
+    by oracle/build_ref.py) on THIS GPU on the 8K request of the default line: a random-init Dream-7B checkpoint is written to
+    a temporary directory (bf16, the engine's deployment dtype), then draft + scoring of the 8 chunks
+    (`select_chunks_by_engine`), the joint prefill of [BOS, 4 selected chunks, query] + 32 MASK slots (`prefill_to_pd_record`) and
+    the block denoising (`decode_from_pd_record`) are timed with device synchronisation around each. A same-box baseline of the
+    reference's own GPU code; nothing of it runs in the product path. If any step fails, the exception text is the result."""
+    import json as _json
+    import shutil
+    import tempfile
+    import traceback
+
+    device = torch.device("cuda", local_rank)
+    torch.cuda.set_device(device)
+    out = {"metric": "decode_tok_per_s", "unit": "tok/s", "n_gpus": 1, "impl": "reference_engine_same_gpu", "dtype": "bf16", "data": "synthetic",
+           "higher_is_better": True, "steps": max(1, min(args.steps, 2)), "warmup": 1,
+           "config": {"workload": "the reference's FastDLLMDreamEngine on this GPU: Dream-7B architecture (random init, bf16), 8192-token random "
+                                  "prefix in 8 chunks of 1024 (chunk BOS) + 64-token query, its own draft (4 tokens, 1 round) + per-chunk scoring, "
+                                  "top-4, joint prefill, block 32, 32 new tokens, threshold 0.9, enforce_eager, flex attention backend"}}
+    tmp = tempfile.mkdtemp(prefix="pdllm_ref_engine_")
+    try:
+        from safetensors.torch import save_file
+        from tokenizers import Tokenizer
+        from tokenizers.models import WordLevel
+        from tokenizers.pre_tokenizers import Whitespace
+
+        from oracle import build_ref
+
+        module = build_ref.load_reference_engine()
+        hidden, inter, layers, hq, hkv, d, vocab, mask_id, bos = 3584, 18944, 28, 28, 4, 128, 152064, 151666, 151643
+        cfg = dict(model_type="Dream", architectures=["DreamModel"], auto_map={"AutoConfig": "configuration_dream.DreamConfig"},
+                   vocab_size=vocab, hidden_size=hidden, intermediate_size=inter, num_hidden_layers=layers, num_attention_heads=hq,
+                   num_key_value_heads=hkv, max_position_embeddings=131072, rope_theta=1000000.0, rms_norm_eps=1e-6, hidden_act="silu",
+                   mask_token_id=mask_id, pad_token_id=bos, bos_token_id=bos, eos_token_id=bos, torch_dtype="bfloat16", tie_word_embeddings=False)
+        with open(os.path.join(tmp, "config.json"), "w") as handle:
+            _json.dump(cfg, handle)
+        shutil.copyfile(os.path.join(build_ref.REF_DIR, "engine", "configuration_dream.py"), os.path.join(tmp, "configuration_dream.py"))
+        tok = Tokenizer(WordLevel({"<pad>": 0, "<bos>": 1, "<eos>": 2, "<mask>": 3}, unk_token="<pad>"))
+        tok.pre_tokenizer = Whitespace()
+        tok.save(os.path.join(tmp, "tokenizer.json"))
+        with open(os.path.join(tmp, "tokenizer_config.json"), "w") as handle:
+            _json.dump({"tokenizer_class": "PreTrainedTokenizerFast", "bos_token": "<bos>", "eos_token": "<eos>", "mask_token": "<mask>",
+                        "pad_token": "<pad>", "unk_token": "<pad>"}, handle)
+        g = torch.Generator(device=device).manual_seed(0)
+
+        def rnd(*shape):
+            return (torch.randn(*shape, device=device, dtype=torch.float32, generator=g) * 0.02).to(torch.bfloat16).cpu()
+
+        save_file({"model.embed_tokens.weight": rnd(vocab, hidden), "lm_head.weight": rnd(vocab, hidden),
+                   "model.norm.weight": torch.ones(hidden, dtype=torch.bfloat16)}, os.path.join(tmp, "model-head.safetensors"))
+        for i in range(layers):
+            p = f"model.layers.{i}."
+            save_file({p + "self_attn.q_proj.weight": rnd(hq * d, hidden), p + "self_attn.q_proj.bias": rnd(hq * d),
+                       p + "self_attn.k_proj.weight": rnd(hkv * d, hidden), p + "self_attn.k_proj.bias": rnd(hkv * d),
+                       p + "self_attn.v_proj.weight": rnd(hkv * d, hidden), p + "self_attn.v_proj.bias": rnd(hkv * d),
+                       p + "self_attn.o_proj.weight": rnd(hidden, hq * d), p + "mlp.gate_proj.weight": rnd(inter, hidden),
+                       p + "mlp.up_proj.weight": rnd(inter, hidden), p + "mlp.down_proj.weight": rnd(hidden, inter),
+                       p + "input_layernorm.weight": torch.ones(hidden, dtype=torch.bfloat16),
+                       p + "post_attention_layernorm.weight": torch.ones(hidden, dtype=torch.bfloat16)},
+                      os.path.join(tmp, f"model-layer{i:02d}.safetensors"))
+        engine = module.FastDLLMDreamEngine(tmp, max_model_len=8192, block_length=32, mask_token_id=mask_id, threshold=0.9,
+                                            gpu_memory_utilization=0.5, enforce_eager=True)
+        gen = torch.Generator().manual_seed(0)
+        context = torch.randint(0, 151000, (8192,), generator=gen).tolist()
+        query = torch.randint(0, 151000, (64,), generator=gen).tolist()
+        chunks = [([bos] + context[i:i + 1024])[:1024] for i in range(0, 8192, 1024)]
+
+        def sync_ms(fn):
+            torch.cuda.synchronize(device)
+            t0 = time.perf_counter()
+            r = fn()
+            torch.cuda.synchronize(device)
+            return r, (time.perf_counter() - t0) * 1e3
+
+        runs = []
+        with torch.inference_mode():
+            for it in range(out["steps"] + 1):
+                (selected, scores, _, _), t_sel = sync_ms(lambda: engine.select_chunks_by_engine([bos], chunks, query, topk_chunks=4))
+                prompt = [bos] + [t for ci in selected for t in chunks[ci]] + query
+                rec, t_pre = sync_ms(lambda: engine.prefill_to_pd_record(prompt, max_new_tokens=32))
+                res, t_dec = sync_ms(lambda: engine.decode_from_pd_record(rec, max_new_tokens=32))
+                if it > 0:          # the first request carries torch.compile and autotuning
+                    runs.append(dict(draft_and_scoring_ms=t_sel, prefill_ms=t_pre, decode_ms=t_dec, denoise_steps=int(res.n_diff_steps),
+                                     new_tokens=len(res.token_ids), selected=[int(i) for i in selected]))
+        try:
+            engine.close()
+        except Exception:
+            pass
+        mean = {k: sum(r[k] for r in runs) / len(runs) for k in ("draft_and_scoring_ms", "prefill_ms", "decode_ms")}
+        total = sum(mean.values())
+        out.update(value=32 / (mean["decode_ms"] * 1e-3), ms_per_step=total, phases_ms=mean, runs=runs,
+                   e2e={"value": 32 / (total * 1e-3), "unit": "tok/s", "request_latency_ms": total})
+    except BaseException as exc:
+        out["unavailable"] = f"{type(exc).__name__}: {exc}"[:600]
+        out["traceback"] = traceback.format_exc()[-3000:]
+    finally:
+        shutil.rmtree(tmp, ignore_errors=True)
+    return out
+
+
 def run_request(args, rank: int, world: int, local_rank: int):
     from prefilling_dllm_b200 import ops
     from prefilling_dllm_b200 import sharded as sharded_mod
@@ -877,6 +977,15 @@ def run_request(args, rank: int, world: int, local_rank: int):
                        "reference_triton_same_gpu": reference_triton_on_this_gpu(device)}
         if world == 1:
             line["cpu_baseline"], line["toy_same_config"] = cpu_toy_baseline(), gpu_toy_same_config(device)
+            if not args.skip_reference_engine:
+                # the reference's own GPU engine on the same request, on this GPU (about a minute: checkpoint, load, compile warm-up)
+                torch.cuda.empty_cache()
+                ref = run_reference_engine_8k(args, local_rank)
+                keep = ("value", "unit", "ms_per_step", "phases_ms", "e2e", "unavailable", "config")
+                line["reference_engine_same_gpu"] = {k: ref[k] for k in keep if k in ref}
+                if "value" in ref:
+                    line["reference_engine_same_gpu"]["this_build_over_reference"] = {
+                        "decode_tok_per_s": line["value"] / ref["value"], "request_latency": ref["ms_per_step"] / line["ms_per_step"]}
     barrier()
     return line
 
@@ -1189,10 +1298,12 @@ def main():
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="native", choices=["native", "reference"])
     ap.add_argument("--workload", default="request",
-                    choices=["request", "request_once", "full_reencode", "op", "op_mha_decode", "op_decode_rows", "op_prefill", "linear", "byte_kernels", "dream7b_decode_batch",
+                    choices=["request", "request_once", "full_reencode", "reference_engine_8k", "op", "op_mha_decode", "op_decode_rows", "op_prefill", "linear", "byte_kernels", "dream7b_decode_batch",
                              "llada8b_decode_batch"],
                     help="request (default): the 8K request per GPU + the sharded 32K request + op-level records; the others run one piece alone")
     ap.add_argument("--shape", default="", help="--workload linear: run one shape only, e.g. gate_up_m32 (for a profiler capture)")
+    ap.add_argument("--skip-reference-engine", action="store_true",
+                    help="default workload at N = 1: do not run the reference's own GPU engine on the same request at the end")
     ap.add_argument("--ctx", type=int, default=8192, help="--workload full_reencode: context length (8192 or 32768)")
     ap.add_argument("--concurrent", type=int, default=16, help="requests per GPU that share a denoise step (decode_batch workloads, op_mha_decode)")
     args = ap.parse_args()
@@ -1238,6 +1349,8 @@ def main():
             line = op_linear(device, args.steps, args.shape) if rank == 0 else None
         elif args.workload == "op_decode_rows":
             line = op_decode_rows(device, args.steps) if rank == 0 else None
+        elif args.workload == "reference_engine_8k":
+            line = run_reference_engine_8k(args, local_rank) if rank == 0 else None
         elif args.workload == "full_reencode":
             line = run_full_reencode(args, local_rank) if rank == 0 else None
         elif args.workload == "request_once":
