@@ -37,6 +37,7 @@ from __future__ import annotations
 
 import argparse
 import json
+import gc
 import math
 import os
 import subprocess
@@ -712,6 +713,133 @@ def run_full_reencode(args, local_rank: int):
                                          "speedup_of_this_path": naive_ms / path_ms}}
 
 
+def _write_random_dream7b_checkpoint(path: str, device, *, single_file: bool):
+    """config.json, a stub tokenizer and bf16 N(0, 0.02) weights of the Dream-7B architecture under HF parameter names, for the
+    reference's own loaders (its engine reads any *.safetensors; the eval-class plug-in contract reads one model.safetensors).
+    Returns (mask_token_id, bos_token_id)."""
+    import json as _json
+    import shutil
+
+    from safetensors.torch import save_file
+    from tokenizers import Tokenizer
+    from tokenizers.models import WordLevel
+    from tokenizers.pre_tokenizers import Whitespace
+
+    from oracle import build_ref
+
+    hidden, inter, layers, hq, hkv, d, vocab, mask_id, bos = 3584, 18944, 28, 28, 4, 128, 152064, 151666, 151643
+    cfg = dict(model_type="Dream", architectures=["DreamModel"], auto_map={"AutoConfig": "configuration_dream.DreamConfig"},
+               vocab_size=vocab, hidden_size=hidden, intermediate_size=inter, num_hidden_layers=layers, num_attention_heads=hq,
+               num_key_value_heads=hkv, max_position_embeddings=131072, rope_theta=1000000.0, rms_norm_eps=1e-6, hidden_act="silu",
+               mask_token_id=mask_id, pad_token_id=bos, bos_token_id=bos, eos_token_id=bos, torch_dtype="bfloat16", tie_word_embeddings=False)
+    with open(os.path.join(path, "config.json"), "w") as handle:
+        _json.dump(cfg, handle)
+    if build_ref.engine_staged():
+        shutil.copyfile(os.path.join(build_ref.REF_DIR, "engine", "configuration_dream.py"), os.path.join(path, "configuration_dream.py"))
+    tok = Tokenizer(WordLevel({"<pad>": 0, "<bos>": 1, "<eos>": 2, "<mask>": 3}, unk_token="<pad>"))
+    tok.pre_tokenizer = Whitespace()
+    tok.save(os.path.join(path, "tokenizer.json"))
+    with open(os.path.join(path, "tokenizer_config.json"), "w") as handle:
+        _json.dump({"tokenizer_class": "PreTrainedTokenizerFast", "bos_token": "<bos>", "eos_token": "<eos>", "mask_token": "<mask>",
+                    "pad_token": "<pad>", "unk_token": "<pad>"}, handle)
+    g = torch.Generator(device=device).manual_seed(0)
+
+    def rnd(*shape):
+        return (torch.randn(*shape, device=device, dtype=torch.float32, generator=g) * 0.02).to(torch.bfloat16).cpu()
+
+    tensors = {"model.embed_tokens.weight": rnd(vocab, hidden), "lm_head.weight": rnd(vocab, hidden),
+               "model.norm.weight": torch.ones(hidden, dtype=torch.bfloat16)}
+    if not single_file:
+        save_file(tensors, os.path.join(path, "model-head.safetensors"))
+        tensors = {}
+    for i in range(layers):
+        p = f"model.layers.{i}."
+        tensors.update({p + "self_attn.q_proj.weight": rnd(hq * d, hidden), p + "self_attn.q_proj.bias": rnd(hq * d),
+                        p + "self_attn.k_proj.weight": rnd(hkv * d, hidden), p + "self_attn.k_proj.bias": rnd(hkv * d),
+                        p + "self_attn.v_proj.weight": rnd(hkv * d, hidden), p + "self_attn.v_proj.bias": rnd(hkv * d),
+                        p + "self_attn.o_proj.weight": rnd(hidden, hq * d), p + "mlp.gate_proj.weight": rnd(inter, hidden),
+                        p + "mlp.up_proj.weight": rnd(inter, hidden), p + "mlp.down_proj.weight": rnd(hidden, inter),
+                        p + "input_layernorm.weight": torch.ones(hidden, dtype=torch.bfloat16),
+                        p + "post_attention_layernorm.weight": torch.ones(hidden, dtype=torch.bfloat16)})
+        if not single_file:
+            save_file(tensors, os.path.join(path, f"model-layer{i:02d}.safetensors"))
+            tensors = {}
+    if single_file:
+        save_file(tensors, os.path.join(path, "model.safetensors"))
+    return mask_id, bos
+
+
+def run_reference_class_8k(args, local_rank: int):
+    """`--workload reference_class_8k`: the UNMODIFIED reference eval class (`FastDLLMParallelComp`, staged under oracle/_ref/eval)
+    with `device="cuda"` on THIS GPU on the 8K request of the default line, over the restated Dream plug-in model
+    (oracle/contract_model: the Fast-dLLM v1 model the reference imports by directory is absent) with random-init Dream-7B
+    weights in bf16. Phases timed by wrapping its bound methods between device synchronisations. A same-box baseline of the
+    reference's host logic and cache handling on a plain PyTorch model; nothing of it runs in the product path."""
+    import shutil
+    import tempfile
+    import traceback
+
+    device = torch.device("cuda", local_rank)
+    torch.cuda.set_device(device)
+    out = {"metric": "decode_tok_per_s", "unit": "tok/s", "n_gpus": 1, "impl": "reference_class_same_gpu", "dtype": "bf16", "data": "synthetic",
+           "higher_is_better": True, "steps": max(1, min(args.steps, 2)), "warmup": 1,
+           "config": {"workload": "the reference's FastDLLMParallelComp (device=cuda) on this GPU over the restated Dream plug-in model: Dream-7B "
+                                  "architecture (random init, bf16), 8192-token random prefix + 64-token query, chunk 1024 with chunk BOS, "
+                                  "draft-self-information scoring at batch 8, top-4, joint full_prompt_mask prefill, block 32, 32 new tokens, threshold 0.9"}}
+    tmp = tempfile.mkdtemp(prefix="pdllm_ref_class_")
+    try:
+        from oracle import build_ref
+
+        ref = build_ref.load_eval_module()
+        _write_random_dream7b_checkpoint(tmp, device, single_file=True)
+        runtime = ref.load_fastdllm_parallelcomp(pretrained=tmp, fastdllm_dream_dir=os.path.join(ROOT, "oracle", "contract_model"), device=f"cuda:{local_rank}",
+                                                 dtype="bfloat16", trust_remote_code=False, chunk_size=1024, topk_chunks=4, max_new_tokens=32,
+                                                 max_length=16384, cache_build_mode="full_prompt_mask", chunk_position_mode="continuous",
+                                                 query_position_mode="after_selected_chunks", token_capacity=0, **README_FLAGS)
+        secs = {"draft": 0.0, "scoring": 0.0, "decode": 0.0}
+
+        def timed(name, fn):
+            def wrapper(*a, **k):
+                torch.cuda.synchronize(device)
+                t = time.perf_counter()
+                try:
+                    return fn(*a, **k)
+                finally:
+                    torch.cuda.synchronize(device)
+                    secs[name] += time.perf_counter() - t
+            return wrapper
+
+        runtime._selection_query_ids_with_score_target = timed("draft", runtime._selection_query_ids_with_score_target)
+        runtime.score_chunks_self_information_batched = timed("scoring", runtime.score_chunks_self_information_batched)
+        runtime._denoise_block_confidence_threshold = timed("decode", runtime._denoise_block_confidence_threshold)
+        gen = torch.Generator().manual_seed(0)
+        context = torch.randint(0, 151000, (8192,), generator=gen).tolist()
+        query = torch.randint(0, 151000, (64,), generator=gen).tolist()
+        runs = []
+        for it in range(out["steps"] + 1):
+            for k in secs:
+                secs[k] = 0.0
+            torch.cuda.synchronize(device)
+            t0 = time.perf_counter()
+            result = runtime.generate(prefix_ids=runtime.bos_ids(), context_ids=context, query_ids=query)
+            torch.cuda.synchronize(device)
+            total = (time.perf_counter() - t0) * 1e3
+            if it > 0:
+                ph = {k: v * 1e3 for k, v in secs.items()}
+                ph["prefill"] = max(0.0, total - sum(ph.values()))
+                runs.append(dict(request_ms=total, phases_ms=ph, new_tokens=len(result.sequences), selected=list(result.selected_chunk_indices)))
+        mean = {k: sum(r["phases_ms"][k] for r in runs) / len(runs) for k in ("draft", "scoring", "prefill", "decode")}
+        total = sum(r["request_ms"] for r in runs) / len(runs)
+        out.update(value=32 / (mean["decode"] * 1e-3), ms_per_step=total, phases_ms=mean, runs=runs,
+                   e2e={"value": 32 / (total * 1e-3), "unit": "tok/s", "request_latency_ms": total})
+    except BaseException as exc:
+        out["unavailable"] = f"{type(exc).__name__}: {exc}"[:600]
+        out["traceback"] = traceback.format_exc()[-3000:]
+    finally:
+        shutil.rmtree(tmp, ignore_errors=True)
+    return out
+
+
 def run_reference_engine_8k(args, local_rank: int):
     """`--workload reference_engine_8k`: the UNMODIFIED reference PD engine (`FastDLLMDreamEngine`, staged under oracle/_ref/engine
     by oracle/build_ref.py) on THIS GPU on the 8K request of the default line: a random-init Dream-7B checkpoint is written to
@@ -733,45 +861,10 @@ def run_reference_engine_8k(args, local_rank: int):
                                   "top-4, joint prefill, block 32, 32 new tokens, threshold 0.9, enforce_eager, flex attention backend"}}
     tmp = tempfile.mkdtemp(prefix="pdllm_ref_engine_")
     try:
-        from safetensors.torch import save_file
-        from tokenizers import Tokenizer
-        from tokenizers.models import WordLevel
-        from tokenizers.pre_tokenizers import Whitespace
-
         from oracle import build_ref
 
         module = build_ref.load_reference_engine()
-        hidden, inter, layers, hq, hkv, d, vocab, mask_id, bos = 3584, 18944, 28, 28, 4, 128, 152064, 151666, 151643
-        cfg = dict(model_type="Dream", architectures=["DreamModel"], auto_map={"AutoConfig": "configuration_dream.DreamConfig"},
-                   vocab_size=vocab, hidden_size=hidden, intermediate_size=inter, num_hidden_layers=layers, num_attention_heads=hq,
-                   num_key_value_heads=hkv, max_position_embeddings=131072, rope_theta=1000000.0, rms_norm_eps=1e-6, hidden_act="silu",
-                   mask_token_id=mask_id, pad_token_id=bos, bos_token_id=bos, eos_token_id=bos, torch_dtype="bfloat16", tie_word_embeddings=False)
-        with open(os.path.join(tmp, "config.json"), "w") as handle:
-            _json.dump(cfg, handle)
-        shutil.copyfile(os.path.join(build_ref.REF_DIR, "engine", "configuration_dream.py"), os.path.join(tmp, "configuration_dream.py"))
-        tok = Tokenizer(WordLevel({"<pad>": 0, "<bos>": 1, "<eos>": 2, "<mask>": 3}, unk_token="<pad>"))
-        tok.pre_tokenizer = Whitespace()
-        tok.save(os.path.join(tmp, "tokenizer.json"))
-        with open(os.path.join(tmp, "tokenizer_config.json"), "w") as handle:
-            _json.dump({"tokenizer_class": "PreTrainedTokenizerFast", "bos_token": "<bos>", "eos_token": "<eos>", "mask_token": "<mask>",
-                        "pad_token": "<pad>", "unk_token": "<pad>"}, handle)
-        g = torch.Generator(device=device).manual_seed(0)
-
-        def rnd(*shape):
-            return (torch.randn(*shape, device=device, dtype=torch.float32, generator=g) * 0.02).to(torch.bfloat16).cpu()
-
-        save_file({"model.embed_tokens.weight": rnd(vocab, hidden), "lm_head.weight": rnd(vocab, hidden),
-                   "model.norm.weight": torch.ones(hidden, dtype=torch.bfloat16)}, os.path.join(tmp, "model-head.safetensors"))
-        for i in range(layers):
-            p = f"model.layers.{i}."
-            save_file({p + "self_attn.q_proj.weight": rnd(hq * d, hidden), p + "self_attn.q_proj.bias": rnd(hq * d),
-                       p + "self_attn.k_proj.weight": rnd(hkv * d, hidden), p + "self_attn.k_proj.bias": rnd(hkv * d),
-                       p + "self_attn.v_proj.weight": rnd(hkv * d, hidden), p + "self_attn.v_proj.bias": rnd(hkv * d),
-                       p + "self_attn.o_proj.weight": rnd(hidden, hq * d), p + "mlp.gate_proj.weight": rnd(inter, hidden),
-                       p + "mlp.up_proj.weight": rnd(inter, hidden), p + "mlp.down_proj.weight": rnd(hidden, inter),
-                       p + "input_layernorm.weight": torch.ones(hidden, dtype=torch.bfloat16),
-                       p + "post_attention_layernorm.weight": torch.ones(hidden, dtype=torch.bfloat16)},
-                      os.path.join(tmp, f"model-layer{i:02d}.safetensors"))
+        mask_id, bos = _write_random_dream7b_checkpoint(tmp, device, single_file=False)
         engine = module.FastDLLMDreamEngine(tmp, max_model_len=8192, block_length=32, mask_token_id=mask_id, threshold=0.9,
                                             gpu_memory_utilization=0.5, enforce_eager=True)
         gen = torch.Generator().manual_seed(0)
@@ -978,14 +1071,17 @@ def run_request(args, rank: int, world: int, local_rank: int):
         if world == 1:
             line["cpu_baseline"], line["toy_same_config"] = cpu_toy_baseline(), gpu_toy_same_config(device)
             if not args.skip_reference_engine:
-                # the reference's own GPU engine on the same request, on this GPU (about a minute: checkpoint, load, compile warm-up)
-                torch.cuda.empty_cache()
-                ref = run_reference_engine_8k(args, local_rank)
+                # the reference's own GPU code on the same request, on this GPU (about a minute each: checkpoint, load, warm-up):
+                # its PD engine, and its eval class (device=cuda) over the restated plain-PyTorch plug-in model
                 keep = ("value", "unit", "ms_per_step", "phases_ms", "e2e", "unavailable", "config")
-                line["reference_engine_same_gpu"] = {k: ref[k] for k in keep if k in ref}
-                if "value" in ref:
-                    line["reference_engine_same_gpu"]["this_build_over_reference"] = {
-                        "decode_tok_per_s": line["value"] / ref["value"], "request_latency": ref["ms_per_step"] / line["ms_per_step"]}
+                for key, fn in (("reference_engine_same_gpu", run_reference_engine_8k), ("reference_class_same_gpu", run_reference_class_8k)):
+                    gc.collect()
+                    torch.cuda.empty_cache()
+                    ref = fn(args, local_rank)
+                    line[key] = {k: ref[k] for k in keep if k in ref}
+                    if "value" in ref:
+                        line[key]["this_build_over_reference"] = {"decode_tok_per_s": line["value"] / ref["value"],
+                                                                  "request_latency": ref["ms_per_step"] / line["ms_per_step"]}
     barrier()
     return line
 
@@ -1298,7 +1394,7 @@ def main():
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="native", choices=["native", "reference"])
     ap.add_argument("--workload", default="request",
-                    choices=["request", "request_once", "full_reencode", "reference_engine_8k", "op", "op_mha_decode", "op_decode_rows", "op_prefill", "linear", "byte_kernels", "dream7b_decode_batch",
+                    choices=["request", "request_once", "full_reencode", "reference_engine_8k", "reference_class_8k", "op", "op_mha_decode", "op_decode_rows", "op_prefill", "linear", "byte_kernels", "dream7b_decode_batch",
                              "llada8b_decode_batch"],
                     help="request (default): the 8K request per GPU + the sharded 32K request + op-level records; the others run one piece alone")
     ap.add_argument("--shape", default="", help="--workload linear: run one shape only, e.g. gate_up_m32 (for a profiler capture)")
@@ -1349,6 +1445,8 @@ def main():
             line = op_linear(device, args.steps, args.shape) if rank == 0 else None
         elif args.workload == "op_decode_rows":
             line = op_decode_rows(device, args.steps) if rank == 0 else None
+        elif args.workload == "reference_class_8k":
+            line = run_reference_class_8k(args, local_rank) if rank == 0 else None
         elif args.workload == "reference_engine_8k":
             line = run_reference_engine_8k(args, local_rank) if rank == 0 else None
         elif args.workload == "full_reencode":
