@@ -1078,6 +1078,8 @@ def run_request(args, rank: int, world: int, local_rank: int):
                     gc.collect()
                     torch.cuda.empty_cache()
                     ref = fn(args, local_rank)
+                    torch.set_default_device("cpu")            # the reference's model runner changes both while it builds its model
+                    torch.set_default_dtype(torch.float32)
                     line[key] = {k: ref[k] for k in keep if k in ref}
                     if "value" in ref:
                         line[key]["this_build_over_reference"] = {"decode_tok_per_s": line["value"] / ref["value"],
