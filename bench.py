@@ -1008,6 +1008,7 @@ def run_request(args, rank: int, world: int, local_rank: int):
     timer.wrap(rt32, "score_chunks_self_information_batched", "scoring")
     timer.wrap(rt32, "_denoise_blocks", "decode")
     timer.wrap(rt32, "_prefill_one_chunk", "chunk_eviction_and_prefill")
+    timer.wrap(rt32, "_prefill_chunks_packed", "chunk_eviction_and_prefill")      # one GPU: the selected chunks in packed forwards
     moved = {"all_gather_bytes": 0, "kv_bytes_received": 0}
     if sharded is not None:
         timer.wrap(sharded_mod, "all_gather_chunk_scores", "score_all_gather")

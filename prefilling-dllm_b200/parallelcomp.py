@@ -203,6 +203,9 @@ def sample_tokens(logits: torch.Tensor, temperature: float = 0.0, top_p: Optiona
     return confidence, token
 
 
+_NOT_SCORED = object()      # "no precomputed head scores": distinct from None, which means "nothing could be scored"
+
+
 class PagedCache:
     """Handle to a request's KV in the paged pool: logical token order → pages, plus the RoPE position of each token."""
 
@@ -873,6 +876,31 @@ class FastDLLMParallelComp:
             per_layer.append(parts[0] if len(parts) == 1 else parts[0] + parts[1])
         return torch.stack(per_layer, dim=0).contiguous(), layers
 
+    @torch.inference_mode()
+    def _chunk_head_scores_packed(self, prefix_ids, chunks: Sequence[Sequence[int]], query_ids):
+        """`_chunk_head_scores` of several chunks of ONE length in one packed forward (the chunks are independent sequences: same
+        arithmetic per chunk, one pass over the weights for all of them). Returns one (head scores, layers) pair per chunk,
+        or None where `_chunk_head_scores` would return None."""
+        cfg = self.config
+        window = self._window_query(query_ids, cfg.token_score_query_window)
+        layers = self._select_attention_layer_indices(self.arch.num_hidden_layers, cfg.token_score_layers, cfg.token_score_layer_mode)
+        if not window or not layers or not chunks or not chunks[0]:
+            return [None] * len(chunks)
+        prefix = list(prefix_ids) if cfg.token_score_include_prefix else []
+        p_len, c_len, q_len = len(prefix), len(chunks[0]), len(window)
+        row_len = p_len + c_len + q_len
+        mask_args = self._mask_args(cfg.token_attention_mask, rows_before_chunk=p_len, chunk_len=c_len, query_len=q_len)
+        _, captured = self._forward_packed([prefix + list(c) + window for c in chunks], [list(range(row_len))] * len(chunks), want_logits=False,
+                                           capture_layers=layers, **mask_args)
+        out = []
+        for b in range(len(chunks)):
+            rows = slice(b * row_len, (b + 1) * row_len)
+            per_layer = [ops.query_to_chunk_attention_scores(captured[l][0][rows], captured[l][1][rows], prefix_len=p_len, chunk_len=c_len,
+                                                             query_len=q_len, scale=self.model.scale, reduce_mode=cfg.token_score_reduce,
+                                                             attention_mask=cfg.token_attention_mask) for l in layers]
+            out.append((torch.stack(per_layer, dim=0).contiguous(), layers))
+        return out
+
     def _chunk_to_query_mass(self, q: torch.Tensor, k: torch.Tensor, p_len: int, c_len: int, q_len: int, reduce_mode: str, mask_args: dict):
         """fp32 [Hq, chunk_len]: attention probability that each chunk row puts on the query's keys, summed (or averaged) over
         those keys, under the forward's own mask. Zero under the causal and query_to_chunk masks (chunk rows do not see the query)."""
@@ -943,7 +971,9 @@ class FastDLLMParallelComp:
             return None
         return 1 if pooling == "none" else int(cfg.token_score_pool_kernel or 1)
 
-    def _keep_positions_for_chunk(self, prefix_ids, chunk_ids, query_ids) -> List[int]:
+    def _keep_positions_for_chunk(self, prefix_ids, chunk_ids, query_ids, scored=_NOT_SCORED) -> List[int]:
+        """Kept positions of one chunk (reference :1955-1995). `scored`: the chunk's head scores when the caller already ran the
+        scoring forward for several chunks at once (`_chunk_head_scores_packed`)."""
         cfg = self.config
         capacity, chunk_len = int(cfg.token_capacity or 0), len(chunk_ids)
         if capacity <= 0 or chunk_len <= capacity:
@@ -951,7 +981,8 @@ class FastDLLMParallelComp:
         pool_kernel = self._fused_reductions()
         force_bos = bool(cfg.force_keep_chunk_bos and cfg.chunk_bos)
         if pool_kernel is not None:
-            scored = self._chunk_head_scores(prefix_ids, chunk_ids, query_ids)
+            if scored is _NOT_SCORED:
+                scored = self._chunk_head_scores(prefix_ids, chunk_ids, query_ids)
             head_scores, n_heads = (None, 0) if scored is None else (scored[0], self.arch.num_key_value_heads)
         else:
             # reductions the fused kernel does not compute: reduce with tensor ops, then let the kernel rank one "head" of one "layer"
@@ -1073,6 +1104,72 @@ class FastDLLMParallelComp:
             kept_pos = [c_pos[i] for i in keep_union]
         return kept, kept_pos, keep_union, c_start
 
+    def _prefill_chunks_packed(self, cache: "PagedCache", dst: int, prefix_ids, items, evict_q, window_q):
+        """`_prefill_one_chunk` for all selected chunks at once when eviction is global: the chunks are independent sequences
+        (each attends the prefix KV and itself), so the token-scoring forwards of same-length chunks are ONE packed forward and so
+        are their prefill forwards — one pass over the weights instead of one per chunk, and row counts at which the GEMM runs
+        wide tiles. `items`: (order, chunk index, chunk ids) in cache order. Returns one (kept, kept positions, kept indices, rope
+        start) per item with the kept rows laid out consecutively from cache token `dst`, or None when the per-chunk path has to
+        run (per-head eviction, reductions or score directions the packed scorer does not cover, a single chunk)."""
+        cfg = self.config
+        if cfg.token_eviction_granularity == "per_head" or len(items) < 2:
+            return None
+        capacity = int(cfg.token_capacity or 0)
+        evicting = capacity > 0 and any(len(chunk) > capacity for _, _, chunk in items)
+        if evicting and (self._fused_reductions() is None or cfg.token_score_direction != "query_to_chunk"):
+            return None
+        p_len = len(prefix_ids)
+        batch = max(1, int(cfg.score_batch_size or 1))
+        by_len: Dict[int, List[int]] = {}
+        for n, (_, _, chunk) in enumerate(items):
+            by_len.setdefault(len(chunk), []).append(n)
+        # kept positions: one scoring forward per group of same-length chunks, then the usual per-chunk selection
+        keeps: List[Optional[List[int]]] = [None] * len(items)
+        for c_len, members in by_len.items():
+            if capacity <= 0 or c_len <= capacity:
+                for n in members:
+                    keeps[n] = self._keep_positions_for_chunk(prefix_ids, items[n][2], evict_q)
+                continue
+            for off in range(0, len(members), batch):
+                part = members[off:off + batch]
+                scored = self._chunk_head_scores_packed(prefix_ids, [items[n][2] for n in part], evict_q)
+                for n, sc in zip(part, scored):
+                    keeps[n] = self._keep_positions_for_chunk(prefix_ids, items[n][2], evict_q, sc)
+        # destinations in cache order
+        out: List[Optional[tuple]] = [None] * len(items)
+        dsts, at = [], dst
+        for n in range(len(items)):
+            dsts.append(at)
+            at += len(keeps[n])
+        cache.slots(dst, at - dst)                                                  # capacity check
+        # prefill: one packed forward per group, every sequence against the prefix KV, kept rows written to their slots
+        for c_len, members in by_len.items():
+            for off in range(0, len(members), batch):
+                part = members[off:off + batch]
+                rows_ids, rows_pos, slots = [], [], []
+                for n in part:
+                    order, ci, chunk = items[n]
+                    c_start = self._chunk_rope_start(p_len, order, ci)
+                    c_pos = self._range_positions(c_start, len(chunk))
+                    ids, pos = chunk, c_pos
+                    if cfg.cache_build_mode == "chunk_query":
+                        tq_start = self._chunk_query_rope_start(p_len, c_start, len(chunk))
+                        ids = chunk + window_q
+                        pos = c_pos + self._range_positions(tq_start, len(window_q))
+                    keep_set = set(keeps[n])
+                    next_slot = iter(cache.slots(dsts[n], len(keeps[n])))
+                    slots += [next(next_slot) if i in keep_set else -1 for i in range(len(chunk))] + [-1] * (len(ids) - len(chunk))
+                    rows_ids.append(ids)
+                    rows_pos.append(pos)
+                    out[n] = (len(keeps[n]), [c_pos[i] for i in keeps[n]], keeps[n], c_start)
+                if cfg.cache_build_mode == "chunk_query":
+                    mask_args = self._mask_args(cfg.token_attention_mask, rows_before_chunk=0, chunk_len=c_len, query_len=len(window_q))
+                else:
+                    mask_args = dict(causal=False)
+                self._forward_packed(rows_ids, rows_pos, cache=cache if p_len else None, ctx_len=p_len, store_slots=slots, want_logits=False,
+                                     **mask_args)
+        return out
+
     @torch.inference_mode()
     def build_prefill_cache(self, *, prefix_ids, context_ids, query_ids, scoring_query_ids=None):
         """Independent per-chunk prefill (cache_build_mode chunk_query / chunk_only) → (PagedCache, cache_positions, meta).
@@ -1102,10 +1199,15 @@ class FastDLLMParallelComp:
             meta: List[FastDLLMChunkMeta] = []
             total_removed = 0
             window_q = self._window_query(selection_q, cfg.token_score_query_window)
+            packed = self._prefill_chunks_packed(cache, cache.length, prefix_ids, [(order, ci, list(chunks[ci])) for order, ci in enumerate(selected)],
+                                                 evict_q, window_q)
             for order, ci in enumerate(selected):
                 chunk = list(chunks[ci])
                 dst = cache.length
-                kept, kept_pos, keep_union, c_start = self._prefill_one_chunk(cache, dst, prefix_ids, chunk, order, ci, evict_q, window_q)
+                if packed is not None:
+                    kept, kept_pos, keep_union, c_start = packed[order]
+                else:
+                    kept, kept_pos, keep_union, c_start = self._prefill_one_chunk(cache, dst, prefix_ids, chunk, order, ci, evict_q, window_q)
                 removed = max(0, len(chunk) - kept)
                 total_removed += removed
                 cache.length = dst + kept

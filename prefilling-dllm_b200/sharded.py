@@ -228,8 +228,31 @@ class ShardedChunkPrefill:
         payloads: Dict[int, torch.Tensor] = {}
         positions: Dict[int, torch.Tensor] = {}
         unions: Dict[int, List[int]] = {}
+        mine_items = [(order, ci, list(chunks[ci])) for order, ci in enumerate(selected) if prefill_on[ci] == self.rank]
+        done_packed = False
+        if len(mine_items) >= 2:
+            # this rank's share in packed forwards (one pass over the weights for all of it), into one scratch cache
+            scratch = PagedCache(rt, p_len + sum(2 * len(c) for _, _, c in mine_items) + rt.model.page_size)
+            try:
+                if prefix_ids:
+                    rt._forward_packed([prefix_ids], [rt._range_positions(0, p_len)], causal=False, store_slots=scratch.slots(0, p_len),
+                                       want_logits=False)
+                    scratch.length = p_len
+                packed = rt._prefill_chunks_packed(scratch, p_len, prefix_ids, mine_items, evict_q, window_q)
+                if packed is not None:
+                    at = p_len
+                    for (order, ci, chunk), (kept, kept_pos, union, _) in zip(mine_items, packed):
+                        if kept != kept_tokens[ci]:
+                            raise RuntimeError(f"chunk {ci}: kept {kept} tokens, the plan expected {kept_tokens[ci]}")
+                        payloads[ci] = self._gather_rows(scratch, at, kept)
+                        positions[ci] = torch.tensor(kept_pos, dtype=torch.int64, device=rt.device)
+                        unions[ci] = list(union)
+                        at += kept
+                    done_packed = True
+            finally:
+                scratch.release()
         for order, ci in enumerate(selected):
-            if prefill_on[ci] != self.rank:
+            if prefill_on[ci] != self.rank or done_packed:
                 continue
             chunk = list(chunks[ci])
             scratch = PagedCache(rt, p_len + 2 * len(chunk) + rt.model.page_size)
