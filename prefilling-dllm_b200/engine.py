@@ -826,16 +826,14 @@ class FastDLLMDreamEngine:
     # ------------------------------------------------------------------------------------------------ chunk selection
     @staticmethod
     def _select_attention_layer_indices(total_layers: int, layer_window: int, layer_mode: str) -> List[int]:
-        if total_layers <= 0:
-            return []
-        if layer_mode == "all" or layer_window <= 0:
-            return list(range(total_layers))
-        window = min(max(1, int(layer_window)), total_layers)
-        if layer_mode == "first":
-            return list(range(window))
-        if layer_mode == "last":
-            return list(range(total_layers - window, total_layers))
-        raise ValueError(f"Unsupported attention layer mode: {layer_mode}")
+        """Layers whose attention is scored: all of them, or a window of `layer_window` at either end."""
+        every = list(range(max(0, total_layers)))
+        if not every or layer_mode == "all" or layer_window <= 0:
+            return every
+        if layer_mode not in ("first", "last"):
+            raise ValueError(f"Unsupported attention layer mode: {layer_mode}")
+        width = min(max(1, int(layer_window)), total_layers)
+        return every[:width] if layer_mode == "first" else every[-width:]
 
     @staticmethod
     def _window_query(query_ids: Sequence[int], window: int) -> List[int]:

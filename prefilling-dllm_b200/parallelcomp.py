@@ -345,46 +345,46 @@ class FastDLLMParallelComp:
     def _range_positions(start: int, length: int) -> List[int]:
         return list(range(int(start), int(start) + int(length)))
 
+    # RoPE position of the first token of a chunk / of the query window behind a chunk / of the final query, per position mode
+    # (reference :922-948). One window of `chunk_size` positions is the unit: "reuse" puts every chunk in the same window right
+    # behind the prefix, "continuous" stacks the selected chunks in selection order, "absolute" keeps a chunk where the full
+    # context had it.
+    def _window(self) -> int:
+        return max(1, self.config.chunk_size)
+
     def _chunk_rope_start(self, prefix_len: int, chunk_order: int, chunk_index: int) -> int:
         mode = self.config.chunk_position_mode
-        size = max(1, self.config.chunk_size)
-        if mode == "reuse":
-            return prefix_len
-        if mode == "continuous":
-            return prefix_len + chunk_order * size
-        if mode == "absolute":
-            return prefix_len + chunk_index * size
-        raise ValueError(f"Unsupported chunk_position_mode: {mode}")
+        windows_before = {"reuse": 0, "continuous": chunk_order, "absolute": chunk_index}
+        if mode not in windows_before:
+            raise ValueError(f"Unsupported chunk_position_mode: {mode}")
+        return prefix_len + windows_before[mode] * self._window()
 
     def _chunk_query_rope_start(self, prefix_len: int, chunk_start: int, chunk_len: int) -> int:
         mode = self.config.chunk_query_position_mode
-        if mode == "after_reused_window":
-            return prefix_len + max(1, self.config.chunk_size)
-        if mode == "after_chunk":
-            return chunk_start + chunk_len
-        raise ValueError(f"Unsupported chunk_query_position_mode: {mode}")
+        starts = {"after_reused_window": prefix_len + self._window(), "after_chunk": chunk_start + chunk_len}
+        if mode not in starts:
+            raise ValueError(f"Unsupported chunk_query_position_mode: {mode}")
+        return starts[mode]
 
     def _final_query_rope_start(self, prefix_len: int, cache_positions: Sequence[int], selected_count: int) -> int:
         mode = self.config.query_position_mode
-        if mode == "after_reused_window":
-            return prefix_len + max(1, self.config.chunk_size)
-        if mode == "after_selected_chunks":
-            return prefix_len + selected_count * max(1, self.config.chunk_size)
         if mode == "after_cache":
-            return (max(cache_positions) + 1) if cache_positions else prefix_len
-        raise ValueError(f"Unsupported query_position_mode: {mode}")
+            return max(cache_positions, default=prefix_len - 1) + 1
+        windows_before = {"after_reused_window": 1, "after_selected_chunks": selected_count}
+        if mode not in windows_before:
+            raise ValueError(f"Unsupported query_position_mode: {mode}")
+        return prefix_len + windows_before[mode] * self._window()
 
-    def _select_attention_layer_indices(self, total_layers: int, layer_window: int, layer_mode: str) -> List[int]:
-        if total_layers <= 0:
-            return []
-        if layer_mode == "all" or layer_window <= 0:
-            return list(range(total_layers))
-        window = min(max(1, int(layer_window)), total_layers)
-        if layer_mode == "first":
-            return list(range(window))
-        if layer_mode == "last":
-            return list(range(total_layers - window, total_layers))
-        raise ValueError(f"Unsupported attention layer mode: {layer_mode}")
+    @staticmethod
+    def _select_attention_layer_indices(total_layers: int, layer_window: int, layer_mode: str) -> List[int]:
+        """Layers whose attention is scored: all of them, or a window of `layer_window` at either end (reference :1770-1780)."""
+        every = list(range(max(0, total_layers)))
+        if not every or layer_mode == "all" or layer_window <= 0:
+            return every
+        if layer_mode not in ("first", "last"):
+            raise ValueError(f"Unsupported attention layer mode: {layer_mode}")
+        width = min(max(1, int(layer_window)), total_layers)
+        return every[:width] if layer_mode == "first" else every[-width:]
 
     @staticmethod
     def _mask_kind(mode: str) -> str:
