@@ -5,10 +5,11 @@ Follows prefilling_dllm_engine/prefilling_dllm/fastdllm_engine.py on the CPU con
 prompt KV with an fp32 softmax (:2111-2157, :1658-1681), the engine's own draft for chunk selection, which re-forwards
 the whole prompt every round (:1014-1060), chunk scoring (:1097-1152) and the chunk-local KV generate (:1683-1876).
 
-Parity unpinned: the reference engine cannot be imported without a GPU (its model runner initialises CUDA and NCCL at
-construction), and it ships no golden vectors for this path, so these functions are checked only against the call
-sites they restate. The arithmetic they share with the eval class (model, unmask rule, score tail) is pinned by
-tests/golden/toy_reference.json.
+Parity pinned: tests/golden/engine_reference.json holds what the UNMODIFIED reference engine produced on a B200 in
+float64 with its sdpa attention backend (tests/golden/make_engine_golden.py drives a staged copy; the engine cannot be
+imported without a GPU, its model runner initialises CUDA and NCCL at construction). tests/test_engine_golden.py holds
+every function below to that file; the arithmetic shared with the eval class (model, unmask rule, score tail) is also
+pinned by tests/golden/toy_reference.json.
 
 The contract model caches un-rotated keys and takes the position of every key on each call, which expresses the
 engine's post-RoPE pages exactly as long as all KV heads keep the same tokens (one position list per key).
@@ -247,3 +248,138 @@ def chunk_local_generate(model, *, prefix_ids, prefix_positions, chunk_ids_list,
     ids, steps = denoise_block(model, past_q, key_positions + list(query_positions), block_positions, first, last, mask_id=mask_id,
                                threshold=threshold)
     return dict(first_token=first, token_ids=ids, n_diff_steps=steps)
+
+
+# --------------------------------------------------------------------------------------------------------------------
+# Sparse prefill over an eviction mask and the decode-time delta correction (layers/attention/attention_v4.py:86-289).
+# These change what an attention layer computes, so the layers are walked explicitly here instead of through the contract
+# model's forward: per layer, rotated q/k and v per head, one `attention(layer, q, k, v)` call, the residual and the MLP.
+# --------------------------------------------------------------------------------------------------------------------
+def _walk_layers(model, ids: Sequence[int], positions: Sequence[int], attention):
+    """`attention(layer, q [H, n, D], k [Hkv, n, D], v [Hkv, n, D]) -> [H, n, D]` with q and k already rotated to `positions`.
+    Returns the logits [n, vocab]."""
+    from .contract_model.model.modeling_dream import rotate_half
+
+    base = model.model
+    h = base.embed_tokens(torch.tensor([list(ids)], dtype=torch.long))
+    cos, sin = base.rotary_emb(h, _positions(positions))
+    n = h.shape[1]
+    for li, layer in enumerate(base.layers):
+        a = layer.self_attn
+        x = layer.input_layernorm(h)
+        q = a.q_proj(x).view(n, a.num_heads, a.head_dim).transpose(0, 1)
+        k = a.k_proj(x).view(n, a.num_key_value_heads, a.head_dim).transpose(0, 1)
+        v = a.v_proj(x).view(n, a.num_key_value_heads, a.head_dim).transpose(0, 1)
+        q = q * cos + rotate_half(q) * sin
+        k = k * cos + rotate_half(k) * sin
+        o = attention(li, q, k, v)
+        h = h + a.o_proj(o.transpose(0, 1).reshape(1, n, a.num_heads * a.head_dim))
+        h = h + layer.mlp(layer.post_attention_layernorm(h))
+    return model.lm_head(base.norm(h))[0]
+
+
+def _attend(q, k, v, allowed: Optional[torch.Tensor] = None):
+    """softmax(q k^T / sqrt(d)) v per query head, KV heads repeated; `allowed` [rows, keys] bool or None."""
+    group = q.shape[0] // k.shape[0]
+    k, v = k.repeat_interleave(group, dim=0), v.repeat_interleave(group, dim=0)
+    scores = torch.matmul(q, k.transpose(1, 2)) / (q.shape[-1] ** 0.5)
+    if allowed is not None:
+        scores = scores.masked_fill(~allowed, float("-inf"))
+    return torch.matmul(torch.softmax(scores, dim=-1), v)
+
+
+def _spread_delta(out, dense_at_anchors, anchors: Sequence[int], *, left: int, right: int, direction: str, scale: float):
+    """attention_v4.py:145-158, :274-288 — out + the delta of every anchor row added to the rows of its window."""
+    n = out.shape[1]
+    delta = (dense_at_anchors - out[:, list(anchors)]) * scale
+    fixed = out.clone()
+    for idx, a in enumerate(anchors):
+        lo = a if direction == "right" else max(0, a - left)
+        hi = a if direction == "left" else min(n - 1, a + right)
+        fixed[:, lo:hi + 1] += delta[:, idx:idx + 1]
+    return fixed
+
+
+def sparse_prefill_and_decode(model, prompt_ids: Sequence[int], keep_nested, *, block_length: int, mask_id: int, threshold: float,
+                              delta: bool = False, stride: int = 8, left: int = 7, right: int = 0, direction: str = "left",
+                              scale: float = 1.0):
+    """prefill_sparse_mode="eviction_mask" (fastdllm_engine.py:2010-2040, attention_v4.py:164-289): in layer l every row of
+    the joint prefill attends only the union over KV heads of `keep_nested[l]` plus the MASK slots; with `delta` the dense
+    attention is evaluated at every stride-th row (from stride-1, or from 0 for direction "right") and the difference is
+    spread over that anchor's window. The prompt KV is NOT compacted: the block decodes against all of it, densely.
+    Returns dict(first_token, last_context_logit, token_ids, n_diff_steps)."""
+    prompt_ids = list(prompt_ids)
+    n0, n = len(prompt_ids), len(prompt_ids) + block_length
+    offset = 0 if direction == "right" else stride - 1
+    anchors = list(range(offset, n, stride))
+    kept_kv = []
+
+    def attention(layer, q, k, v):
+        kept_kv.append((k[:, :n0], v[:, :n0]))
+        key_ok = torch.zeros(n, dtype=torch.bool)
+        key_ok[torch.tensor(sorted({int(i) for head in keep_nested[layer] for i in head if 0 <= int(i) < n}), dtype=torch.long)] = True
+        key_ok[n0:] = True
+        out = _attend(q, k, v, key_ok.unsqueeze(0).expand(n, n))
+        if delta and anchors:
+            out = _spread_delta(out, _attend(q[:, anchors], k, v), anchors, left=left, right=right, direction=direction, scale=scale)
+        return out
+
+    with torch.no_grad():
+        logits = _walk_layers(model, prompt_ids + [mask_id] * block_length, range(n), attention)
+        last = logits[n0 - 1]
+        first = int(torch.argmax(last))
+        block = torch.full((block_length,), mask_id, dtype=torch.long)
+        block[0] = first
+        steps = 0
+        while bool((block == mask_id).any()):
+            steps += 1
+            step = _walk_layers(model, block.tolist(), range(n0, n),
+                                lambda layer, q, k, v: _attend(q, torch.cat([kept_kv[layer][0], k], dim=1), torch.cat([kept_kv[layer][1], v], dim=1)))
+            block, _, _ = O.unmask_step(step, block, mask_token_id=mask_id, threshold=threshold, last_logit=last, shift=True,
+                                        softmax_dtype=torch.float32)
+    return dict(first_token=first, last_context_logit=last, token_ids=block.tolist(), n_diff_steps=steps)
+
+
+def posthoc_eviction_with_decode_delta(model, prompt_ids: Sequence[int], keep_nested, active_positions: Sequence[int], *, block_length: int,
+                                       mask_id: int, threshold: float, stride: int = 4, left: int = 3, scale: float = 1.0):
+    """Per-layer, per-KV-head post-hoc eviction with decode_delta_mode="s4_left3" (fastdllm_engine.py:2061-2082,
+    attention_v4.py:86-162): after a dense joint prefill, head h of layer l keeps the rotated K/V rows `keep_nested[l][h]`;
+    the block is denoised at positions max(active_positions)+1.. against them, and in every layer of every step the rows
+    stride-1, 2*stride-1, ... are also evaluated against the FULL prompt KV (kept aside before the eviction); that
+    difference, times `scale`, is added to the anchor row and the `left` rows before it.
+    Returns dict(first_token, last_context_logit, token_ids, n_diff_steps)."""
+    prompt_ids = list(prompt_ids)
+    n0, n = len(prompt_ids), len(prompt_ids) + block_length
+    full_kv = []
+
+    def dense(layer, q, k, v):
+        full_kv.append((k[:, :n0], v[:, :n0]))
+        return _attend(q, k, v)
+
+    anchors = list(range(stride - 1, block_length, stride))
+    start = max(int(p) for p in active_positions) + 1
+
+    def corrected(layer, q, k, v):
+        fk, fv = full_kv[layer]
+        idx = [torch.tensor([int(i) for i in head], dtype=torch.long) for head in keep_nested[layer]]
+        kk = torch.stack([fk[h, idx[h]] for h in range(fk.shape[0])])
+        kv = torch.stack([fv[h, idx[h]] for h in range(fv.shape[0])])
+        out = _attend(q, torch.cat([kk, k], dim=1), torch.cat([kv, v], dim=1))
+        if not anchors:
+            return out
+        exact = _attend(q[:, anchors], torch.cat([fk, k], dim=1), torch.cat([fv, v], dim=1))
+        return _spread_delta(out, exact, anchors, left=left, right=0, direction="left", scale=scale)
+
+    with torch.no_grad():
+        logits = _walk_layers(model, prompt_ids + [mask_id] * block_length, range(n), dense)
+        last = logits[n0 - 1]
+        first = int(torch.argmax(last))
+        block = torch.full((block_length,), mask_id, dtype=torch.long)
+        block[0] = first
+        steps = 0
+        while bool((block == mask_id).any()):
+            steps += 1
+            step = _walk_layers(model, block.tolist(), range(start, start + block_length), corrected)
+            block, _, _ = O.unmask_step(step, block, mask_token_id=mask_id, threshold=threshold, last_logit=last, shift=True,
+                                        softmax_dtype=torch.float32)
+    return dict(first_token=first, last_context_logit=last, token_ids=block.tolist(), n_diff_steps=steps)

@@ -32,6 +32,7 @@ from . import ops
 from .model import denoise_blocks_batched, CachedPrefix, DreamArch, PageAllocator, PagedDreamModel, denoise_blocks, slots_for
 
 _OFF = {"none", "off", "0", ""}
+_DELTA_MODES = {"s4_left3", "delta_s4_left3", "sampled_delta_s4_left3"}
 
 
 def _on_device(method):
@@ -193,7 +194,8 @@ class FastDLLMDreamEngine:
     # ------------------------------------------------------------------------------------------------ forwards
     def _forward(self, ids, positions: Sequence[int], *, ctx_page_ids: Optional[Sequence[int]] = None, ctx_len: int = 0,
                  store_slots: Optional[Sequence[int]] = None, causal: bool = False, mask: Optional[torch.Tensor] = None,
-                 logit_rows: Optional[Sequence[int]] = None, want_logits: bool = True, capture_layers=None, on_layer_stored=None):
+                 logit_rows: Optional[Sequence[int]] = None, want_logits: bool = True, capture_layers=None, on_layer_stored=None,
+                 attention_fn=None):
         """One sequence of new rows at `positions`, seeing the first `ctx_len` tokens held by `ctx_page_ids`."""
         m = self.model
         ids_t = ids if isinstance(ids, torch.Tensor) else m.ids_tensor(ids)
@@ -207,7 +209,8 @@ class FastDLLMDreamEngine:
             return m.forward(ids_t, torch.tensor(list(positions), dtype=torch.long, device=m.device), cu_seqlens=m.i32([0, n]),
                              max_query_len=n, slot_mapping=None if store_slots is None else m.i32(list(store_slots)),
                              causal=causal, new_row_mask=mask, logit_rows=None if logit_rows is None else m.ids_tensor(logit_rows),
-                             want_logits=want_logits, capture_qk_layers=capture_layers, on_layer_stored=on_layer_stored, **kwargs)
+                             want_logits=want_logits, capture_qk_layers=capture_layers, on_layer_stored=on_layer_stored,
+                             attention_fn=attention_fn, **kwargs)
 
     def _selection_mask(self, mode: str, *, seq_len: int, prefix_len: int, chunk_len: int, query_len: int):
         """(causal flag, dense mask or None) for a selection forward (reference _selection_prefill_mask :930-953)."""
@@ -436,15 +439,24 @@ class FastDLLMDreamEngine:
         last = source.last_context_logit
         if last is not None:
             last = last.to(device=self.device).contiguous()
-        if source.decode_delta_state is not None:
-            raise NotImplementedError("decode delta state is not built")
-        return self._record_like(source, prompt_pages, block_pages, last, None)
+        return self._record_like(source, prompt_pages, block_pages, last, self._delta_state_on(source.decode_delta_state, self.device))
+
+    @staticmethod
+    def _delta_state_on(state: Optional[dict], device) -> Optional[dict]:
+        """A record's decode-delta state with its full-prompt KV on `device` (reference :784-798)."""
+        if state is None:
+            return None
+        moved = dict(state)
+        for key in ("full_k", "full_v"):
+            if moved.get(key) is not None:
+                moved[key] = [None if t is None else t.to(device=device).contiguous() for t in moved[key]]
+        return moved
 
     # ------------------------------------------------------------------------------------------------ prefill half
     @staticmethod
-    def _reject_unbuilt_modes(*, prefill_sparse_mode, prefill_delta_mode, prefill_delta_selection_mode, prefill_delta_direction,
+    def _check_modes(*, prefill_sparse_mode, prefill_delta_mode, prefill_delta_selection_mode, prefill_delta_direction,
                               decode_delta_mode, has_keep: bool) -> None:
-        """Argument checks of reference :1924-1935, :2012-2017, :2074-2075, then the refusal of what is not built."""
+        """Argument checks of reference :1924-1935, :2012-2017, :2074-2075, and the refusal of the one mode that is not built."""
         sparse = (prefill_sparse_mode or "none").lower()
         use_sparse = sparse not in _OFF
         if use_sparse and sparse != "eviction_mask":
@@ -458,11 +470,10 @@ class FastDLLMDreamEngine:
                 raise ValueError(f"Unsupported prefill_delta_selection_mode: {prefill_delta_selection_mode}")
             if (prefill_delta_direction or "left").lower() not in {"left", "right", "both"}:
                 raise ValueError(f"Unsupported prefill_delta_direction: {prefill_delta_direction}")
-            raise NotImplementedError("prefill_sparse_mode=eviction_mask (sparse prefill with delta correction) is not built")
+            if (prefill_delta_selection_mode or "none").lower() not in _OFF:
+                raise NotImplementedError("prefill_delta_selection_mode (anchor outputs reused from the selection pass) is not built")
         delta = (decode_delta_mode or "none").lower()
-        if delta in {"s4_left3", "delta_s4_left3", "sampled_delta_s4_left3"}:
-            raise NotImplementedError("decode_delta_mode (delta attention over a full-KV reservoir) is not built")
-        if delta not in _OFF and has_keep:
+        if delta not in _OFF | _DELTA_MODES and has_keep and not use_sparse:
             raise ValueError(f"Unsupported decode_delta_mode: {delta}")
 
     @_on_device
@@ -495,7 +506,7 @@ class FastDLLMDreamEngine:
         # them in the joint prefill, as the eval class's full_prompt_mask flow does (fastdllm_parallelcomp.py:2896-2912).
         decode_len = self.block_length if max_new_tokens <= self.block_length else int(max_new_tokens)
         has_keep = prompt_keep_indices_per_layer_per_head is not None
-        self._reject_unbuilt_modes(prefill_sparse_mode=prefill_sparse_mode, prefill_delta_mode=prefill_delta_mode,
+        self._check_modes(prefill_sparse_mode=prefill_sparse_mode, prefill_delta_mode=prefill_delta_mode,
                                    prefill_delta_selection_mode=prefill_delta_selection_mode,
                                    prefill_delta_direction=prefill_delta_direction, decode_delta_mode=decode_delta_mode, has_keep=has_keep)
         keep: Optional[List[torch.Tensor]] = None
@@ -513,14 +524,16 @@ class FastDLLMDreamEngine:
 
         prefill_suffix_start = (max(prompt_positions) + 1) if prompt_positions else 0
         prefill_suffix_positions = list(range(prefill_suffix_start, prefill_suffix_start + decode_len))
-        if keep is not None:
+        use_sparse = (prefill_sparse_mode or "none").lower() not in _OFF
+        if keep is not None and not use_sparse:
             suffix_start = (max(active_prompt_positions) + 1) if active_prompt_positions else 0
             suffix_positions = list(range(suffix_start, suffix_start + decode_len))
             prompt_len, full_prompt_len, kv_mode = int(active_len or 0), len(prompt_ids), "compacted_posthoc_eviction"
         else:
+            # dense prefill, or a prefill whose attention is restricted to the kept keys: the whole prompt KV stays in pages
             suffix_positions = prefill_suffix_positions
             prompt_len = full_prompt_len = len(prompt_ids)
-            kv_mode = "full_dense"
+            kv_mode = "full_prefill_sparse_delta" if use_sparse else "full_dense"
         if full_prompt_len + decode_len > self.config.max_model_len:
             raise ValueError(f"full_prompt_mask length {full_prompt_len + decode_len} exceeds max_model_len={self.config.max_model_len}")
 
@@ -532,6 +545,7 @@ class FastDLLMDreamEngine:
         cache_key = prompt_ids if decode_len == self.block_length else prompt_ids + [-decode_len]
         cached = self._prefix_cache.lookup_prefix(cache_key) if use_prefix_cache else None
         owns_prompt_pages = False
+        decode_delta_state: Optional[dict] = None
         stream_header = dict(prompt_ids=prompt_ids, prompt_positions=prompt_positions, suffix_positions=suffix_positions,
                              full_prompt_len=full_prompt_len, decode_len=decode_len, kv_mode=kv_mode) if kv_stream is not None else None
         if cached is not None:
@@ -573,11 +587,32 @@ class FastDLLMDreamEngine:
                 first_row = full_prompt_len - 1 if self.model.arch.logit_shift else full_prompt_len
                 if kv_stream is not None:
                     kv_stream.begin(prompt_page_ids=prompt_page_ids, prompt_len=prompt_len, header=stream_header)
+                sparse_attention = None
+                if use_sparse:
+                    stride = max(1, int(prefill_delta_stride or 1))
+                    direction = (prefill_delta_direction or "left").lower()
+                    sparse_attention = self._sparse_prefill_attention(
+                        keep, full_prompt_len=full_prompt_len, seq_len=full_prompt_len + decode_len,
+                        delta=(prefill_delta_mode or "none").lower() in _DELTA_MODES, stride=stride, left=max(0, int(prefill_delta_left)),
+                        right=max(0, int(prefill_delta_right)), direction=direction,
+                        anchor_offset=0 if direction == "right" else stride - 1, scale=float(prefill_delta_scale))
                 logits, _ = self._forward(full_ids, list(prompt_positions) + prefill_suffix_positions, store_slots=slots,
-                                          logit_rows=[first_row], on_layer_stored=None if kv_stream is None else kv_stream.on_layer_stored)
+                                          logit_rows=[first_row], on_layer_stored=None if kv_stream is None else kv_stream.on_layer_stored,
+                                          attention_fn=sparse_attention)
                 last_context_logit = logits[0].detach()
                 first_token = int(torch.argmax(last_context_logit).item())
-                if keep is not None:
+                if keep is not None and not use_sparse:
+                    if (decode_delta_mode or "none").lower() in _DELTA_MODES:
+                        if decode_len != self.block_length:
+                            raise NotImplementedError("the decode delta correction serves one-block records")
+                        # the un-evicted prompt KV, kept beside the record: decode corrects every stride-th block row with dense
+                        # attention over it (reference :2059-2073)
+                        full = self._snapshot_prompt_cache_per_layer(prompt_page_ids, full_prompt_len)
+                        stride = max(1, int(decode_delta_stride or 4))
+                        decode_delta_state = {"enabled": True, "mode": "s4_left3", "full_k": full[0], "full_v": full[1],
+                                              "full_prompt_len": full_prompt_len, "active_prompt_len": int(active_len or 0), "stride": stride,
+                                              "left": max(0, int(decode_delta_left)), "anchor_offset": stride - 1,
+                                              "scale": float(decode_delta_scale), "debug": bool(decode_delta_debug)}
                     self._compact_prompt_cache_per_layer_per_head(prompt_page_ids, keep, src_tokens=full_prompt_len)
                     active_pages = math.ceil(prompt_len / self.page_size)
                     if active_pages < len(prompt_page_ids):
@@ -593,7 +628,7 @@ class FastDLLMDreamEngine:
         record = DreamPrefillRecord(
             prompt_ids=prompt_ids, prompt_positions=prompt_positions, suffix_positions=suffix_positions, prompt_len=prompt_len,
             full_prompt_len=full_prompt_len, decode_len=decode_len, prompt_page_ids=prompt_page_ids, block_page_ids=block_page_ids,
-            first_token_id=first_token, last_context_logit=last_context_logit, decode_delta_state=None,
+            first_token_id=first_token, last_context_logit=last_context_logit, decode_delta_state=decode_delta_state,
             owns_prompt_pages=owns_prompt_pages, cached_prefix=cached, kv_mode=kv_mode)
         if kv_stream is not None:
             kv_stream.finish(record)
@@ -621,6 +656,108 @@ class FastDLLMDreamEngine:
             if n_steps > decode_len + 8:
                 raise RuntimeError("denoising did not converge: every step must unmask at least one slot")
         return block.clone(), n_steps
+
+    @staticmethod
+    def _spread_rows(anchors: Sequence[int], seq_len: int, *, left: int, right: int, direction: str):
+        """(row, anchor index) pairs of the strided correction (reference attention_v4.py:145-158, :274-288): the delta measured
+        at an anchor row is added to the rows of its window — [anchor - left, anchor] ("left"), [anchor, anchor + right]
+        ("right") or both sides — clipped to the sequence."""
+        rows, which = [], []
+        for idx, a in enumerate(anchors):
+            lo = a if direction == "right" else max(0, a - left)
+            hi = a if direction == "left" else min(seq_len - 1, a + right)
+            for r in range(lo, hi + 1):
+                rows.append(r)
+                which.append(idx)
+        return rows, which
+
+    def _apply_delta(self, out: torch.Tensor, dense: torch.Tensor, *, stride: int, left: int, right: int, direction: str,
+                     anchor_offset: int, scale: float) -> None:
+        """out += spread((dense - out)[anchors] * scale): `out` holds the cheap attention of every row, `dense` the full one."""
+        seq_len = int(out.shape[0])
+        offset = stride - 1 if anchor_offset < 0 else min(anchor_offset, stride - 1)
+        anchors = list(range(offset, seq_len, stride))
+        if not anchors:
+            return
+        a_idx = torch.tensor(anchors, dtype=torch.long, device=out.device)
+        delta = (dense.index_select(0, a_idx) - out.index_select(0, a_idx)) * scale
+        rows, which = self._spread_rows(anchors, seq_len, left=left, right=right, direction=direction)
+        out.index_add_(0, torch.tensor(rows, dtype=torch.long, device=out.device),
+                       delta.index_select(0, torch.tensor(which, dtype=torch.long, device=out.device)))
+
+    def _sparse_prefill_attention(self, keep: Sequence[torch.Tensor], *, full_prompt_len: int, seq_len: int, delta: bool, stride: int,
+                                  left: int, right: int, direction: str, anchor_offset: int, scale: float):
+        """The attention of the engine's sparse prefill (reference attention_v4.py:164-289) as a composition of standard calls:
+        in layer l every row attends only the keys some KV head keeps in that layer (the union of `keep[l]`) and the MASK slots;
+        with `delta`, a second, dense pass gives the exact output at every stride-th row and the difference is spread over the
+        rows of that anchor's window. (The reference evaluates the dense pass at the anchor rows only; rows are independent, so
+        evaluating it for all rows and reading the anchors gives the same numbers.)"""
+        device = self.device
+
+        def attention(layer: int, run, out: torch.Tensor) -> None:
+            key_mask = torch.zeros(seq_len, dtype=torch.bool, device=device)
+            kept = keep[layer].to(device=device, dtype=torch.long).reshape(-1)
+            kept = kept[(kept >= 0) & (kept < seq_len)]
+            if kept.numel() == 0:
+                run(out)
+                return
+            key_mask[kept] = True
+            key_mask[full_prompt_len:] = True
+            run(out, mask=key_mask.unsqueeze(0).expand(seq_len, seq_len).contiguous())
+            if delta:
+                dense = torch.empty_like(out)
+                run(dense)
+                self._apply_delta(out, dense, stride=stride, left=left, right=right, direction=direction, anchor_offset=anchor_offset,
+                                  scale=scale)
+
+        return attention
+
+    def _decode_with_delta(self, record: DreamPrefillRecord, max_new_tokens: int, stop_token_ids) -> FastDLLMEngineOutput:
+        """Block denoising over a compacted prompt with the decode-time delta correction (reference attention_v4.py:86-162): in
+        every layer of every step the block rows attend the kept prompt KV as usual, a second pass attends the FULL prompt KV
+        (the record's reservoir, loaded into pages of its own for the duration of the decode) plus the block, and the
+        difference at every stride-th row is spread over the `left` rows before it. Eager steps (no captured graph)."""
+        state = record.decode_delta_state
+        page = self.page_size
+        full_len = int(state["full_prompt_len"])
+        n = int(record.decode_len)
+        reservoir: List[int] = []
+        try:
+            n_pages = math.ceil(full_len / page)
+            self._prefix_cache.ensure_free(n_pages)
+            reservoir = self._prefix_cache.allocate_pages(n_pages)
+            self._load_prompt_cache_per_layer(reservoir, full_len, state["full_k"], state["full_v"])
+            m = self.model
+            res_table = m.i32(reservoir).view(1, -1)
+            res_lens = m.i32([full_len + n])
+            stride, left, scale = max(1, int(state.get("stride", 4))), max(0, int(state.get("left", 3))), float(state.get("scale", 1.0))
+            anchor_offset = int(state.get("anchor_offset", stride - 1))
+
+            def attention(layer: int, run, out: torch.Tensor) -> None:
+                run(out)
+                dense = torch.empty_like(out)
+                run(dense, block_table=res_table, seq_lens=res_lens, max_seq_len=full_len + n)
+                self._apply_delta(out, dense, stride=stride, left=left, right=0, direction="left", anchor_offset=anchor_offset, scale=scale)
+
+            block = torch.full((n,), self.mask_token_id, dtype=torch.long, device=self.device)
+            block[0] = int(record.first_token_id)
+            slots = slots_for(record.block_page_ids, 0, n, page)
+            n_steps, remaining = 0, n - 1
+            while remaining > 0:
+                n_steps += 1
+                if n_steps > n + 8:
+                    raise RuntimeError("denoising did not converge: every step must unmask at least one slot")
+                logits, _ = self._forward(block, record.suffix_positions, ctx_page_ids=record.prompt_page_ids, ctx_len=record.prompt_len,
+                                          store_slots=slots, attention_fn=attention)
+                counts = ops.unmask_step(logits, block, mask_token_id=self.mask_token_id, threshold=self.threshold,
+                                         last_logit=record.last_context_logit, shift=self.model.arch.logit_shift, softmax_dtype=torch.float32)
+                remaining = int(counts[2].item())
+            ops.check_status(self.device)
+            return self._finish(block.clone(), max_new_tokens, stop_token_ids, n_steps)
+        finally:
+            if reservoir:
+                self._prefix_cache.release_pages(reservoir)
+            self.release_pd_record(record)
 
     def _finish(self, block: torch.Tensor, max_new_tokens: int, stop_token_ids, n_steps: int) -> FastDLLMEngineOutput:
         generated = block[:max_new_tokens].tolist()
@@ -650,6 +787,8 @@ class FastDLLMDreamEngine:
             raise ValueError(f"max_new_tokens={max_new_tokens} exceeds record decode_len={record.decode_len}.")
         if record.decode_len > self.block_length:
             return self._decode_blocks(record, max_new_tokens, stop_token_ids)
+        if record.decode_delta_state and record.decode_delta_state.get("enabled", False):
+            return self._decode_with_delta(record, max_new_tokens, stop_token_ids)
         try:
             block, n_steps = self._denoise_block(
                 ctx_page_ids=record.prompt_page_ids, ctx_len=record.prompt_len,
@@ -728,6 +867,9 @@ class FastDLLMDreamEngine:
         if max_new_tokens <= 0:
             return [FastDLLMEngineOutput(text="", token_ids=[], n_diff_steps=0) for _ in records]
         decode_len = records[0].decode_len
+        if any(r.decode_delta_state and r.decode_delta_state.get("enabled", False) for r in records):
+            # the delta correction runs a second attention pass per record: such records are decoded one after the other
+            return [self.decode_from_pd_record(r, max_new_tokens=max_new_tokens, stop_token_ids=stop_token_ids) for r in records]
         try:
             for r in records:
                 if r.decode_len != decode_len:

@@ -339,7 +339,8 @@ class PagedDreamModel:
                 seq_lens: Optional[torch.Tensor] = None, max_seq_len: int = 0, causal: bool = False,
                 logit_rows: Optional[torch.Tensor] = None, want_logits: bool = True,
                 capture_qk_layers: Optional[Sequence[int]] = None, store_after_attention: bool = False,
-                store_unrotated_k: bool = False, new_row_mask: Optional[torch.Tensor] = None, on_layer_stored=None):
+                store_unrotated_k: bool = False, new_row_mask: Optional[torch.Tensor] = None, on_layer_stored=None,
+                attention_fn=None):
         """Packed forward of `ids` [T] (several sequences delimited by cu_seqlens) at RoPE `positions` [T].
 
         slot_mapping [T] int32 (optional): where each row's K/V goes in the pool (-1 = do not store).
@@ -356,6 +357,10 @@ class PagedDreamModel:
         capture_qk_layers: layers whose rotated (q, k) are returned for the eviction scorer.
         on_layer_stored: callable(layer index), invoked right after a layer's K/V rows were written to pages (their final
         values in a forward that stores before attention): lets a transfer of layer l overlap the compute of layer l + 1.
+        attention_fn: callable(layer index, run, out) that takes the place of a layer's attention call. `run(out, mask=...,
+        block_table=..., seq_lens=..., max_seq_len=...)` performs the standard call of this forward into `out` [rows, Hq, D] with
+        any of its mask / cached-context arguments replaced; the callable must leave the layer's result in `out`. For attention
+        variants that are compositions of standard calls (sparse key masks, corrections from a second pass over other pages).
         Returns (logits or None, {layer: (q, k)}).
         """
         a = self.arch
@@ -390,13 +395,20 @@ class PagedDreamModel:
                     ops.store_kvcache_unified_layout(k, v, k_cache, v_cache, slot_mapping, "diffusion_lm")
             if li in capture:
                 captured[li] = (q.contiguous(), k.contiguous())
-            if block_table is not None:
-                ops.paged_attention(q, k, v, attn_out, cu_seqlens_q=cu_seqlens, max_query_len=max_query_len, key_cache=k_cache,
-                                    value_cache=v_cache, block_table=block_table, seq_lens=seq_lens, max_seq_len=max_seq_len,
-                                    sm_scale=self.scale, causal=causal, bidirectional=True, mask=new_row_mask)
+            def run_attention(out, mask=new_row_mask, block_table=block_table, seq_lens=seq_lens, max_seq_len=max_seq_len,
+                              q=q, k=k, v=v, k_cache=k_cache, v_cache=v_cache):
+                if block_table is not None:
+                    ops.paged_attention(q, k, v, out, cu_seqlens_q=cu_seqlens, max_query_len=max_query_len, key_cache=k_cache,
+                                        value_cache=v_cache, block_table=block_table, seq_lens=seq_lens, max_seq_len=max_seq_len,
+                                        sm_scale=self.scale, causal=causal, bidirectional=True, mask=mask)
+                else:
+                    ops.paged_attention(q, k, v, out, cu_seqlens_q=cu_seqlens, max_query_len=max_query_len,
+                                        sm_scale=self.scale, causal=causal, bidirectional=True, mask=mask)
+
+            if attention_fn is None:
+                run_attention(attn_out)
             else:
-                ops.paged_attention(q, k, v, attn_out, cu_seqlens_q=cu_seqlens, max_query_len=max_query_len,
-                                    sm_scale=self.scale, causal=causal, bidirectional=True, mask=new_row_mask)
+                attention_fn(li, run_attention, attn_out)
             if slot_mapping is not None and store_after_attention:
                 ops.store_kvcache_unified_layout(k, v, k_cache, v_cache, slot_mapping, "diffusion_lm")
             if on_layer_stored is not None and slot_mapping is not None:

@@ -135,7 +135,49 @@ def record(engine) -> dict:
                                                         chunk_keep_indices_per_layer_per_head=nested, query_ids=query, query_positions=q_pos,
                                                         local_query_ids=query[-8:], max_new_tokens=BLOCK)
     out["chunk_local"] = dict(keeps=keeps, token_ids=[int(t) for t in res.token_ids], n_diff_steps=int(res.n_diff_steps))
+    out["sparse_and_delta"] = record_sparse_and_delta(engine)
     return out
+
+
+def per_head_keep_lists(n: int = 600, kept: int = 200):
+    """[layer][head] ascending keep indices of equal length that differ per layer and head (their union is what a sparse
+    prefill may attend)."""
+    return [[([0] + list(range(1 + (h + 2 * layer) % 3, n, 3)))[:kept] for h in range(2)] for layer in range(2)]
+
+
+SPARSE_DELTA_CASES = {
+    "sparse_prefill": dict(prefill_sparse_mode="eviction_mask"),
+    "sparse_prefill_delta_left": dict(prefill_sparse_mode="eviction_mask", prefill_delta_mode="s4_left3"),
+    "sparse_prefill_delta_both": dict(prefill_sparse_mode="eviction_mask", prefill_delta_mode="s4_left3", prefill_delta_stride=4,
+                                      prefill_delta_left=1, prefill_delta_right=2, prefill_delta_direction="both", prefill_delta_scale=0.5),
+    "sparse_prefill_delta_right": dict(prefill_sparse_mode="eviction_mask", prefill_delta_mode="s4_left3", prefill_delta_stride=4,
+                                       prefill_delta_right=3, prefill_delta_direction="right"),
+    "posthoc_decode_delta": dict(decode_delta_mode="s4_left3"),
+    "posthoc_decode_delta_stride8": dict(decode_delta_mode="s4_left3", decode_delta_stride=8, decode_delta_left=5, decode_delta_scale=0.5),
+}
+
+
+def record_sparse_and_delta(engine) -> dict:
+    """The engine's sparse prefill over an eviction mask (with and without the strided delta correction) and its decode-time
+    delta correction against a full-KV reservoir (fastdllm_engine.py:1924-2080, layers/attention/attention_v4.py:86-289)."""
+    ids = prompt(600, 13)
+    nested = per_head_keep_lists()
+    active = nested[0][0]
+    cases = {}
+    for name, kwargs in SPARSE_DELTA_CASES.items():
+        try:
+            rec = engine.prefill_to_pd_record(ids, max_new_tokens=BLOCK, prompt_keep_indices_per_layer_per_head=nested,
+                                              active_prompt_positions=active, **kwargs)
+            item = dict(kv_mode=str(rec.kv_mode), prompt_len_record=int(rec.prompt_len), full_prompt_len=int(rec.full_prompt_len),
+                        first_token_id=int(rec.first_token_id), suffix_positions=[int(p) for p in rec.suffix_positions],
+                        last_context_logit=[float(x) for x in rec.last_context_logit.float().reshape(-1).tolist()],
+                        n_prompt_pages=len(rec.prompt_page_ids))
+            res = engine.decode_from_pd_record(rec, max_new_tokens=BLOCK)
+            item.update(token_ids=[int(t) for t in res.token_ids], n_diff_steps=int(res.n_diff_steps))
+        except Exception as exc:  # a mode the reference itself cannot run is recorded as such
+            item = dict(error=f"{type(exc).__name__}: {exc}"[:300])
+        cases[name] = item
+    return dict(prompt_len=600, seed=13, cases=cases)
 
 
 def make_golden_split(ids, size):

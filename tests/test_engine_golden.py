@@ -1,7 +1,7 @@
 """The CPU restatement of the ENGINE's PD flow (oracle/engine_flow.py) against golden vectors of the reference engine itself.
 
 tests/golden/engine_reference.json holds what the UNMODIFIED reference `FastDLLMDreamEngine` produced on a B200 for the seeded
-toy checkpoint in float32 (tests/golden/make_engine_golden.py drives the staged copy; the engine cannot run on a CPU box).
+toy checkpoint in float64 with its sdpa attention backend (tests/golden/make_engine_golden.py drives the staged copy; the engine cannot run on a CPU box).
 These tests pin the restatement that the GPU engine tests use as their checker; tests/test_gpu_engine.py holds the library's
 engine facade to the same file directly.
 """
@@ -127,3 +127,38 @@ def test_chunk_local_generate(golden, model):
                                  prefix_ids=[BOS], prefix_positions=[0], chunk_ids_list=chunks[:2], chunk_positions_list=chunk_pos,
                                  query_ids=query, query_positions=q_pos, local_query_ids=query[-8:])
     assert got["token_ids"] == ref["token_ids"] and got["n_diff_steps"] == ref["n_diff_steps"]
+
+
+def test_sparse_prefill_and_decode_delta(golden, model):
+    """Sparse prefill over the eviction mask (plain, and with the strided delta correction in its three directions) and the
+    decode-time delta correction against the full-KV reservoir: every case the reference engine recorded."""
+    import make_engine_golden as G
+    from oracle import engine_flow as E
+
+    ref = golden["sparse_and_delta"]
+    prompt = G.prompt(ref["prompt_len"], ref["seed"])
+    nested = G.per_head_keep_lists()
+    model = model.double()
+    try:
+        for name, kwargs in G.SPARSE_DELTA_CASES.items():
+            case = ref["cases"][name]
+            assert "error" not in case, (name, case)
+            if "prefill_sparse_mode" in kwargs:
+                got = E.sparse_prefill_and_decode(
+                    model, prompt, nested, block_length=BLOCK, mask_id=MASK, threshold=golden["threshold"],
+                    delta=kwargs.get("prefill_delta_mode", "none") != "none", stride=kwargs.get("prefill_delta_stride", 8),
+                    left=kwargs.get("prefill_delta_left", 7), right=kwargs.get("prefill_delta_right", 0),
+                    direction=kwargs.get("prefill_delta_direction", "left"), scale=kwargs.get("prefill_delta_scale", 1.0))
+                assert case["kv_mode"] == "full_prefill_sparse_delta" and case["prompt_len_record"] == case["full_prompt_len"] == len(prompt)
+            else:
+                got = E.posthoc_eviction_with_decode_delta(
+                    model, prompt, nested, nested[0][0], block_length=BLOCK, mask_id=MASK, threshold=golden["threshold"],
+                    stride=kwargs.get("decode_delta_stride", 4), left=kwargs.get("decode_delta_left", 3), scale=kwargs.get("decode_delta_scale", 1.0))
+                assert case["kv_mode"] == "compacted_posthoc_eviction" and case["prompt_len_record"] == len(nested[0][0])
+                assert case["suffix_positions"][0] == max(nested[0][0]) + 1
+            assert got["first_token"] == case["first_token_id"], name
+            assert torch.allclose(got["last_context_logit"], torch.tensor(case["last_context_logit"], dtype=torch.float64), atol=2e-4), name
+            assert got["token_ids"] == case["token_ids"], name
+            assert got["n_diff_steps"] == case["n_diff_steps"], name
+    finally:
+        model.float()

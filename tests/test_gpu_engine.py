@@ -101,8 +101,8 @@ def test_engine_facade_matches_the_reference_engine(engine):
     """The same calls that tests/golden/make_engine_golden.py made on the UNMODIFIED reference `FastDLLMDreamEngine` (run on a
     B200, float64 model, its sdpa backend), made on this library's engine in float32: the prefill/decode split (first token,
     last-context logit, ids, step counts, KV checksums — both keep rotated keys in their pages), post-hoc eviction, the engine's
-    draft, chunk scores and selection, per-head keep lists (up to swaps between tied scores at the cut) and the chunk-local KV
-    generate."""
+    draft, chunk scores and selection, per-head keep lists (up to swaps between tied scores at the cut), the chunk-local KV
+    generate, the sparse prefill over an eviction mask and the decode-time delta correction."""
     import make_engine_golden as G
 
     with open(os.path.join(HERE, "golden", "engine_reference.json")) as handle:
@@ -136,6 +136,14 @@ def test_engine_facade_matches_the_reference_engine(engine):
     print(f"per-head keep lists: {swaps} positions differ from the reference engine's (exact ties at the cut)")
     assert swaps <= 8         # oracle-side test (tests/test_engine_golden.py) checks that every such swap is between exactly tied scores
     assert got["chunk_local"] == ref["chunk_local"]
+    # sparse prefill over the eviction mask (plain and with the strided delta correction, three directions) and the decode-time
+    # delta correction against the full-KV reservoir
+    for name, theirs in ref["sparse_and_delta"]["cases"].items():
+        mine = got["sparse_and_delta"]["cases"][name]
+        assert "error" not in mine and "error" not in theirs, (name, mine.get("error"), theirs.get("error"))
+        for key in ("kv_mode", "prompt_len_record", "full_prompt_len", "first_token_id", "suffix_positions", "n_prompt_pages", "token_ids", "n_diff_steps"):
+            assert mine[key] == theirs[key], (name, key)
+        assert torch.allclose(torch.tensor(mine["last_context_logit"]), torch.tensor(theirs["last_context_logit"]), atol=2e-4), name
     while engine._prefix_cache.evict_one():
         pass
     assert engine._prefix_cache.num_free_pages == free0
@@ -527,3 +535,24 @@ def test_batched_decode_equals_one_by_one(engine):
     while engine._prefix_cache.evict_one():
         pass
     assert engine._prefix_cache.num_free_pages == free0
+
+
+def test_decode_delta_state_travels_with_the_record(ckpt):
+    """A record with a decode-delta reservoir handed to another engine (snapshot path and direct page copy) decodes to the
+    same ids there; batched decode falls back to one record after the other for such records."""
+    import make_engine_golden as G
+
+    a, b = _engine(ckpt, pages=16), _engine(ckpt, pages=16)
+    ids, nested = G.prompt(600, 13), G.per_head_keep_lists()
+    kwargs = dict(max_new_tokens=BLOCK, prompt_keep_indices_per_layer_per_head=nested, active_prompt_positions=nested[0][0],
+                  decode_delta_mode="s4_left3")
+    want = a.decode_from_pd_record(a.prefill_to_pd_record(ids, **kwargs), max_new_tokens=BLOCK)
+    free_a, free_b = a._prefix_cache.num_free_pages, b._prefix_cache.num_free_pages
+    src = a.prefill_to_pd_record(ids, **kwargs)
+    assert src.decode_delta_state["full_k"][0].shape[0] == 600 and src.prompt_len == 200
+    moved = b.make_pd_record_from_remote_engine(a, src)
+    loaded = b.make_pd_record_from_kv_snapshot(src, a.snapshot_pd_record_kv(src))
+    a.release_pd_record(src)
+    outs = b.decode_from_pd_records([moved, loaded], max_new_tokens=BLOCK)
+    assert [o.token_ids for o in outs] == [want.token_ids, want.token_ids] and outs[0].n_diff_steps == want.n_diff_steps
+    assert a._prefix_cache.num_free_pages == free_a and b._prefix_cache.num_free_pages == free_b
