@@ -7,7 +7,7 @@
 //   * few rows (M <= 128: one block of decode rows, a draft, a commit): the WEIGHTS are A. A CTA streams 128 weight rows
 //     x K through shared memory once, the activations are the narrow B side (16..128 columns), the accumulator is
 //     out^T [128 features x M tokens]. The step is bound by reading the weights from HBM, so the (feature tile, k-block)
-//     units are dealt to the CTAs stream-K style: every CTA of the grid (one per SM) gets the same number of 16 KB weight
+//     units are dealt to the CTAs stream-K style: every CTA of the grid (one per CTA slot: two per SM for up to 64 rows) gets the same number of 16 KB weight
 //     blocks to stream, whatever N and K are; a feature tile that ends up spread over several CTAs is summed by the CTA
 //     that finishes it last, in CTA order, through fp32 partials in the workspace (an arrival counter per tile; no CTA
 //     ever waits for another).
@@ -34,14 +34,34 @@ constexpr int kThreads = 192;          // warp 0: TMA producer, warp 1: MMA issu
 constexpr int kEpiWarp0 = 2;
 constexpr int kEpiThreads = 128;
 constexpr int kSmemBudget = 200 * 1024;
+// Few rows with a B tile of at most 64 tokens (a block of decode rows): TWO CTAs per SM, each with half the ring. The same
+// number of weight bytes is in flight per SM, but one CTA's set-up, first-copy latency and reduction tail overlap the other's
+// streaming, and with programmatic dependent launch a CTA of the NEXT projection moves in (and requests its first weight
+// stages) as soon as one of this launch's two CTAs on an SM leaves, instead of waiting for a whole 200 KB CTA to retire.
+#ifndef PDLLM_GEMM_CTAS_PER_SM_FEW_ROWS
+#define PDLLM_GEMM_CTAS_PER_SM_FEW_ROWS 1
+#endif
+constexpr int kSmemBudgetShared = 96 * 1024;
+constexpr int kSmemLimit = 224 * 1024;  // ring + receive buffer + barriers stay under the 227 KB a CTA may have
+__host__ __device__ constexpr int ctas_per_sm(bool swap, int bn) { return swap && bn <= 64 ? PDLLM_GEMM_CTAS_PER_SM_FEW_ROWS : 1; }
+// Few rows: room for the shares of an accumulator that the CTAs of a cluster send one another (fp32 [sender][column][128 rows];
+// a CTA finishes every parts-th column, so at most bn + 7 columns arrive). Outside the ring: a peer may be done, and sending,
+// while this CTA's copies are still landing in its stages.
+__host__ __device__ constexpr int recv_bytes(bool swap, int bn) { return swap ? (bn + 8) * kRowsA * 4 : 0; }
 constexpr int kMaxStages = 12;
 constexpr int64_t kCounterHeaderBytes = 64 * 1024;   // arrival counters of the feature tiles (stream-K), zero between launches
 
 __host__ __device__ constexpr int stage_bytes(int bn) { return kRowsA * kBlockK * 2 + bn * kBlockK * 2; }
-__host__ __device__ constexpr int num_stages(int bn) {
-  return kSmemBudget / stage_bytes(bn) < kMaxStages ? kSmemBudget / stage_bytes(bn) : kMaxStages;
+__host__ __device__ constexpr int ring_budget(bool swap, int bn) {
+  return ctas_per_sm(swap, bn) > 1 ? kSmemBudgetShared
+                                   : (kSmemBudget < kSmemLimit - recv_bytes(swap, bn) ? kSmemBudget : kSmemLimit - recv_bytes(swap, bn));
 }
-__host__ __device__ constexpr int smem_bytes(int bn) { return num_stages(bn) * stage_bytes(bn) + 1024 /* align */ + 512 /* barriers */; }
+__host__ __device__ constexpr int num_stages(bool swap, int bn) {
+  return ring_budget(swap, bn) / stage_bytes(bn) < kMaxStages ? ring_budget(swap, bn) / stage_bytes(bn) : kMaxStages;
+}
+__host__ __device__ constexpr int smem_bytes(bool swap, int bn) {
+  return num_stages(swap, bn) * stage_bytes(bn) + 1024 /* align */ + 512 /* barriers */ + recv_bytes(swap, bn);
+}
 __host__ __device__ constexpr uint32_t tmem_cols(int bn) { return 2 * bn < 32 ? 32u : static_cast<uint32_t>(2 * bn); }
 
 struct Args {
@@ -85,13 +105,18 @@ __device__ __forceinline__ void cluster_sync_all() {   // every thread of every 
   asm volatile("barrier.cluster.arrive.release.aligned;" ::: "memory");
   asm volatile("barrier.cluster.wait.acquire.aligned;" ::: "memory");
 }
-// fp32 word at the same shared-memory offset in the CTA of rank `cta` of this cluster
-__device__ __forceinline__ float ld_peer_shared_f32(const void* local_smem, uint32_t cta) {
-  uint32_t remote;
-  float v;
-  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(remote) : "r"(smem_u32(local_smem)), "r"(cta));
-  asm volatile("ld.shared::cluster.f32 %0, [%1];" : "=f"(v) : "r"(remote) : "memory");
-  return v;
+// `bytes` (a multiple of 16) from this CTA's shared memory to the same offset as `dst_local` in the CTA of rank `cta`, counted
+// on the mbarrier at the offset of `bar_local` there (asynchronous copy between the shared memories of a cluster)
+__device__ __forceinline__ void bulk_copy_to_peer(void* dst_local, const void* src, uint32_t bytes, uint64_t* bar_local, uint32_t cta) {
+  uint32_t dst, bar;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(dst) : "r"(smem_u32(dst_local)), "r"(cta));
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(bar) : "r"(smem_u32(bar_local)), "r"(cta));
+  asm volatile("cp.async.bulk.shared::cluster.shared::cta.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];"
+               ::"r"(dst), "r"(smem_u32(src)), "r"(bytes), "r"(bar) : "memory");
+}
+__device__ __forceinline__ void cluster_sync_relaxed() {   // execution barrier only: orders no memory accesses
+  asm volatile("barrier.cluster.arrive.relaxed.aligned;" ::: "memory");
+  asm volatile("barrier.cluster.wait.aligned;" ::: "memory");
 }
 
 // One piece of work of a CTA: k-blocks [kb0, kb1) of the tile at (a_row0, b_row0).
@@ -184,9 +209,9 @@ __device__ __forceinline__ uint32_t pack2(T lo, T hi) {
 constexpr int kChunk = 16;   // accumulator columns handled at a time by an epilogue thread
 
 template <bool kSwap, int kBN, typename T>
-__global__ void __launch_bounds__(kThreads, 1)
+__global__ void __launch_bounds__(kThreads, ctas_per_sm(kSwap, kBN))
 linear_sm100_kernel(const __grid_constant__ CUtensorMap a_map, const __grid_constant__ CUtensorMap b_map, const Args a) {
-  constexpr int kStages = num_stages(kBN);
+  constexpr int kStages = num_stages(kSwap, kBN);
   constexpr int kStageBytes = stage_bytes(kBN);
   constexpr int kABytes = kRowsA * kBlockK * 2;
   constexpr bool kBf16 = std::is_same<T, __nv_bfloat16>::value;
@@ -199,7 +224,8 @@ linear_sm100_kernel(const __grid_constant__ CUtensorMap a_map, const __grid_cons
   uint64_t* acc_empty = acc_full + 2;       // [2] accumulator drained (4 arrivals: one per epilogue warp)
   uint64_t* epi_all = acc_empty + 2;        // 128 arrivals: every epilogue thread published its partial
   uint64_t* epi_go = epi_all + 1;           // 1 arrival: the verdict "this CTA reduces the tile" is in shared memory
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(epi_go + 1);
+  uint64_t* recv_bar = epi_go + 1;          // cluster reduction: 128 arrivals per CTA of the cluster, every share has landed
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(recv_bar + 1);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
   volatile int* reduce_flag = abort_flag + 1;
 
@@ -211,8 +237,16 @@ linear_sm100_kernel(const __grid_constant__ CUtensorMap a_map, const __grid_cons
       for (int i = 0; i < 2; ++i) { mbar_init(&acc_full[i], 1); mbar_init(&acc_empty[i], 4); }
       mbar_init(epi_all, kEpiThreads);
       mbar_init(epi_go, 1);
+      mbar_init(recv_bar, 1);
       abort_flag[0] = 0;
       fence_barrier_init();
+      if (kSwap && a.cluster_parts > 1) {
+        // cluster reduction: this CTA finishes the token columns rank, rank + parts, ... and expects that many 512-byte
+        // columns from every CTA of the cluster (its own share included)
+        const int n_cols = static_cast<int>(a.m < kBN ? a.m : kBN), rank = static_cast<int>(cluster_ctarank());
+        const int my_cols = n_cols > rank ? (n_cols - 1 - rank) / a.cluster_parts + 1 : 0;
+        mbar_expect_tx(recv_bar, static_cast<uint32_t>(a.cluster_parts * my_cols * kRowsA * 4));
+      }
     }
     __syncwarp();
     tmem_alloc_cols(tmem_slot, tmem_cols(kBN));
@@ -221,6 +255,9 @@ linear_sm100_kernel(const __grid_constant__ CUtensorMap a_map, const __grid_cons
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
+  // the peers' receive barriers exist before anyone can arrive on them (ahead of the dependency wait: the CTAs of a cluster
+  // start together, and the predecessor kernel is still finishing)
+  if (kSwap && a.cluster_parts > 1) cluster_sync_all();
 
   Schedule<kSwap, kBN> sched;
   sched.init(a);
@@ -339,15 +376,25 @@ linear_sm100_kernel(const __grid_constant__ CUtensorMap a_map, const __grid_cons
       if (kSwap && bias != nullptr && row_id < a.n) bias_r = to_f32<T>(bias[row_id]);
       auto store_chunk = [&](int c0, const float* v) {
         if (kSwap) {
+          if (silu) {
+            // all sixteen activations first, as independent chains (one warp per scheduler: nothing else hides the latency
+            // of the exponential and the division), then the stores
+            T res[kChunk];
 #pragma unroll
-          for (int i = 0; i < kChunk; ++i) {
-            const int j = c0 + i;
-            if (j >= n_cols) break;                       // uniform across the warp
-            if (silu) {
+            for (int i = 0; i < kChunk; ++i) {
               const float other = __shfl_xor_sync(0xffffffffu, v[i], 1);
-              if ((lane & 1) == 0 && row_id + 1 < a.n) out[static_cast<int64_t>(j) * a.out_stride + (row_id >> 1)] = silu_mul<T>(v[i], other);
-            } else if (row_id < a.n) {
-              out[static_cast<int64_t>(j) * a.out_stride + row_id] = from_f32<T>(v[i] + bias_r);
+              res[i] = silu_mul<T>(v[i], other);
+            }
+            if ((lane & 1) == 0 && row_id + 1 < a.n) {
+#pragma unroll
+              for (int i = 0; i < kChunk; ++i) {
+                if (c0 + i < n_cols) out[static_cast<int64_t>(c0 + i) * a.out_stride + (row_id >> 1)] = res[i];
+              }
+            }
+          } else if (row_id < a.n) {
+#pragma unroll
+            for (int i = 0; i < kChunk; ++i) {
+              if (c0 + i < n_cols) out[static_cast<int64_t>(c0 + i) * a.out_stride + row_id] = from_f32<T>(v[i] + bias_r);
             }
           }
         } else {
@@ -384,21 +431,70 @@ linear_sm100_kernel(const __grid_constant__ CUtensorMap a_map, const __grid_cons
       };
 
       if (kSwap && a.cluster_parts > 1) {
-        // this CTA's accumulator → its own shared memory as fp32 [column][128 rows]; the pipeline stages are idle by now
-        // (the accumulator is complete, so every copy has landed and every MMA has read its stage). Summed after the
-        // cluster barrier below.
-        float* red = reinterpret_cast<float*>(smem);
+        // The CTAs of the cluster hold shares of ONE tile; the CTA of rank p finishes the token columns p, p + parts, ....
+        // Every CTA lays its accumulator out by finisher in its own (by now idle) pipeline stages — fp32
+        // [finisher][column][128 rows] — and ONE thread sends each finisher its columns with an asynchronous copy between
+        // shared memories that counts on the finisher's barrier. A finisher adds the shares out of its own receive buffer
+        // ([sender][column][128 rows], outside the ring: a fast peer sends while this CTA's stages are still in use).
+        // Nobody waits for a slower peer except for the shares it has to add.
+        const int parts = a.cluster_parts;
+        const int rank = static_cast<int>(cluster_ctarank());
+        const int per = (n_cols + parts - 1) / parts;       // columns of the largest share
+        float* send = reinterpret_cast<float*>(smem);
+        float* recv = reinterpret_cast<float*>(smem + kStages * kStageBytes + 512);
 #pragma unroll 1
         for (int c0 = 0; c0 < n_cols; c0 += kChunk) {
           uint32_t raw[kChunk];
           tc::tmem_ld16(t_acc + c0, raw);
           tc_wait_ld();
+          int dst = c0 % parts, lc = c0 / parts;
 #pragma unroll
-          for (int i = 0; i < kChunk; ++i) red[(c0 + i) * kRowsA + r] = __uint_as_float(raw[i]);
+          for (int i = 0; i < kChunk; ++i) {
+            if (c0 + i < n_cols) send[(dst * per + lc) * kRowsA + r] = __uint_as_float(raw[i]);
+            if (++dst == parts) { dst = 0; ++lc; }
+          }
         }
         tc_fence_before();
-        __syncwarp();
+        tc::fence_proxy_async();                              // the copies below read what this thread just wrote
+        asm volatile("bar.sync 1, %0;" ::"n"(kEpiThreads) : "memory");
         if (lane == 0) mbar_arrive(&acc_empty[acc]);
+        if (et == 0) {
+          for (int p = 0; p < parts; ++p) {
+            const int cols_p = n_cols > p ? (n_cols - 1 - p) / parts + 1 : 0;
+            if (cols_p > 0)
+              bulk_copy_to_peer(recv + rank * per * kRowsA, send + p * per * kRowsA, static_cast<uint32_t>(cols_p * kRowsA * 4), recv_bar, static_cast<uint32_t>(p));
+          }
+        }
+        ok = mbar_wait(recv_bar, 0, abort_flag, a);
+        if (!ok) break;
+        // shares added in rank order: the result does not depend on timing. All loads of a column group first.
+        const int my_cols = n_cols > rank ? (n_cols - 1 - rank) / parts + 1 : 0;
+#pragma unroll 1
+        for (int l0 = 0; l0 < my_cols; l0 += 4) {
+          float v[8][4];
+#pragma unroll
+          for (int p = 0; p < 8; ++p) {
+#pragma unroll
+            for (int i = 0; i < 4; ++i) v[p][i] = (p < parts && l0 + i < my_cols) ? recv[(p * per + l0 + i) * kRowsA + r] : 0.f;
+          }
+          float sum[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+          for (int p = 0; p < 8; ++p) {
+#pragma unroll
+            for (int i = 0; i < 4; ++i) sum[i] += v[p][i];
+          }
+#pragma unroll
+          for (int i = 0; i < 4; ++i) {
+            if (l0 + i >= my_cols) break;             // uniform across the warp
+            const int j = (l0 + i) * parts + rank;
+            if (silu) {
+              const float other = __shfl_xor_sync(0xffffffffu, sum[i], 1);
+              if ((lane & 1) == 0 && row_id + 1 < a.n) out[static_cast<int64_t>(j) * a.out_stride + (row_id >> 1)] = silu_mul<T>(sum[i], other);
+            } else if (row_id < a.n) {
+              out[static_cast<int64_t>(j) * a.out_stride + row_id] = from_f32<T>(sum[i] + bias_r);
+            }
+          }
+        }
       } else if (!seg.partial) {
 #pragma unroll 1
         for (int c0 = 0; c0 < n_cols; c0 += kChunk) {
@@ -486,57 +582,10 @@ linear_sm100_kernel(const __grid_constant__ CUtensorMap a_map, const __grid_cons
     }
   }
 
-  // ---- cluster reduction (few rows, few feature tiles): the CTAs of a cluster hold shares of ONE tile ----
-  if (kSwap && a.cluster_parts > 1) {
-    __syncwarp();
-    cluster_sync_all();                 // every CTA's share is in its shared memory
-    if (warp >= kEpiWarp0) {
-      // CTA of rank p finishes the token columns j = p, p + parts, ...: thread r adds the shares of all ranks (in rank order:
-      // the result does not depend on timing) straight out of the peers' shared memory and writes out[j, n].
-      const int r = (warp & 3) * 32 + lane;
-      const int parts = a.cluster_parts;
-      const int rank = static_cast<int>(cluster_ctarank());
-      const int n_cols = static_cast<int>(a.m < kBN ? a.m : kBN);
-      const int64_t row_id = static_cast<int64_t>(blockIdx.x / parts) * kRowsA + r;
-      const float* red = reinterpret_cast<const float*>(smem);
-      T* out = reinterpret_cast<T*>(a.out);
-      const T* bias = reinterpret_cast<const T*>(a.bias);
-      const bool silu = a.epilogue == PDLLM_EPI_SILU_MUL;
-      const float bias_r = (bias != nullptr && row_id < a.n) ? to_f32<T>(bias[row_id]) : 0.f;
-#pragma unroll 1
-      for (int j0 = rank; j0 < n_cols; j0 += 4 * parts) {
-        // 4 columns x up to 8 ranks: every load is issued before the first value is used (a load from a peer's shared
-        // memory takes a few hundred cycles)
-        float v[8][4];
-#pragma unroll
-        for (int p = 0; p < 8; ++p) {
-#pragma unroll
-          for (int i = 0; i < 4; ++i) v[p][i] = (p < parts && j0 + i * parts < n_cols) ? ld_peer_shared_f32(red + (j0 + i * parts) * kRowsA + r, p) : 0.f;
-        }
-        float sum[4] = {0.f, 0.f, 0.f, 0.f};
-#pragma unroll
-        for (int p = 0; p < 8; ++p) {          // rank order: the result does not depend on timing
-#pragma unroll
-          for (int i = 0; i < 4; ++i) sum[i] += v[p][i];
-        }
-#pragma unroll
-        for (int i = 0; i < 4; ++i) {
-          const int j = j0 + i * parts;
-          if (j >= n_cols) break;             // uniform across the warp
-          if (silu) {
-            const float other = __shfl_xor_sync(0xffffffffu, sum[i], 1);
-            if ((lane & 1) == 0 && row_id + 1 < a.n) out[static_cast<int64_t>(j) * a.out_stride + (row_id >> 1)] = silu_mul<T>(sum[i], other);
-          } else if (row_id < a.n) {
-            out[static_cast<int64_t>(j) * a.out_stride + row_id] = from_f32<T>(sum[i] + bias_r);
-          }
-        }
-      }
-    }
-    __syncwarp();
-    cluster_sync_all();                 // no CTA leaves while a peer may still read its shared memory
-  }
-
   // ---- teardown ----
+  // A CTA of a cluster leaves only when every peer holds all its shares: the copies out of this CTA's shared memory are then
+  // complete. (Execution barrier only: nobody has to see this CTA's output stores before it may go.)
+  if (kSwap && a.cluster_parts > 1) cluster_sync_relaxed();
   tc_fence_before();
   __syncthreads();
   if (warp == 1) {
@@ -560,13 +609,14 @@ struct Plan {
 
 inline Plan make_plan(int64_t m, int64_t n, int64_t k) {
   Plan pl;
-  const int sms = sm_count();
+  int sms = sm_count();
   pl.kb_total = static_cast<int>((k + kBlockK - 1) / kBlockK);
   pl.swap = m <= 128;
   int64_t tiles, sk_ctas = 0;
   if (pl.swap) {
     // bound by streaming the weights: every k-block of every feature tile is a unit, all dealt evenly
     pl.bn = m <= 16 ? 16 : m <= 32 ? 32 : m <= 64 ? 64 : 128;
+    sms *= ctas_per_sm(true, pl.bn);     // CTA slots: the grid fills them all at once
     pl.m_tiles = 1;
     pl.n_tiles = static_cast<int>((n + kRowsA - 1) / kRowsA);
     tiles = pl.n_tiles;
@@ -619,8 +669,8 @@ inline Plan make_plan(int64_t m, int64_t n, int64_t k) {
 inline int64_t workspace_bytes(int64_t m, int64_t n, int64_t k) {
   if (m <= 0 || n <= 0) return 0;
   const Plan pl = make_plan(m, n, k);
-  // a grid never exceeds the SM count; sized for it so that one workspace serves every layer of a model
-  return kCounterHeaderBytes + static_cast<int64_t>(2) * sm_count() * pl.bn * kRowsA * 4;
+  // a grid never exceeds the CTA slots of the device; sized for them so that one workspace serves every layer of a model
+  return kCounterHeaderBytes + static_cast<int64_t>(2) * sm_count() * ctas_per_sm(pl.swap, pl.bn) * pl.bn * kRowsA * 4;
 }
 
 template <bool kSwap, int kBN, typename T>
@@ -633,18 +683,18 @@ inline int launch_one(const CUtensorMap& a_map, const CUtensorMap& b_map, const 
     cudaGetDevice(&dev);
     std::lock_guard<std::mutex> lock(mu);
     if (dev < 0 || dev >= 64 || !done[dev]) {
-      cudaError_t e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, smem_bytes(kBN));
+      cudaError_t e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, smem_bytes(kSwap, kBN));
       if (e != cudaSuccess) return fail(static_cast<int>(e), "cudaFuncSetAttribute(linear): %s", cudaGetErrorString(e));
       if (dev >= 0 && dev < 64) done[dev] = true;
     }
   }
   if (a.cluster_parts > 1) {
-    // All clusters of the launch must be resident at once (one CTA per SM, clusters packed per GPC): take the largest
+    // All clusters of the launch must be resident at once (one or two CTAs per SM, clusters packed per GPC): take the largest
     // cluster size, from the planned one down, for which the device says that many clusters fit; with none, one CTA per tile.
     const int tiles = grid / a.cluster_parts;
     cudaLaunchConfig_t cfg = {};
     cfg.blockDim = dim3(kThreads, 1, 1);
-    cfg.dynamicSmemBytes = smem_bytes(kBN);
+    cfg.dynamicSmemBytes = smem_bytes(kSwap, kBN);
     cfg.stream = stream;
     cudaLaunchAttribute attr[2];
     attr[0].id = cudaLaunchAttributeClusterDimension;
@@ -688,10 +738,10 @@ inline int launch_one(const CUtensorMap& a_map, const CUtensorMap& b_map, const 
     }
     // no cluster size fits: every tile whole in one CTA (no workspace needed)
     b.whole_tiles = tiles; b.units = 0; b.sk_grid = 0;
-    (void)launch_dependent(fn, dim3(static_cast<unsigned>(tiles)), dim3(kThreads), smem_bytes(kBN), stream, a_map, b_map, b);
+    (void)launch_dependent(fn, dim3(static_cast<unsigned>(tiles)), dim3(kThreads), smem_bytes(kSwap, kBN), stream, a_map, b_map, b);
     return check_launch("linear_sm100_kernel");
   }
-  (void)launch_dependent(fn, dim3(static_cast<unsigned>(grid)), dim3(kThreads), smem_bytes(kBN), stream, a_map, b_map, a);
+  (void)launch_dependent(fn, dim3(static_cast<unsigned>(grid)), dim3(kThreads), smem_bytes(kSwap, kBN), stream, a_map, b_map, a);
   return check_launch("linear_sm100_kernel");
 }
 
