@@ -30,9 +30,9 @@ using tc::umma_ss; using tc::umma_commit; using tc::desc_kmajor_sw128; using tc:
 
 constexpr int kRowsA = 128;            // rows of the A tile = TMEM lanes
 constexpr int kBlockK = 64;            // elements of K per stage: one 128-byte swizzle row
-constexpr int kThreads = 192;          // warp 0: TMA producer, warp 1: MMA issuer + TMEM owner, warps 2-5: epilogue
+constexpr int kThreads = 320;          // warp 0: TMA producer, warp 1: MMA issuer + TMEM owner, warps 2-9: epilogue
 constexpr int kEpiWarp0 = 2;
-constexpr int kEpiThreads = 128;
+constexpr int kEpiThreads = 256;       // two warps per TMEM lane quarter: they take alternate 16-column chunks of the accumulator
 constexpr int kSmemBudget = 200 * 1024;
 // Few rows with a B tile of at most 64 tokens (a block of decode rows): TWO CTAs per SM, each with half the ring. The same
 // number of weight bytes is in flight per SM, but one CTA's set-up, first-copy latency and reduction tail overlap the other's
@@ -62,6 +62,11 @@ __host__ __device__ constexpr int num_stages(bool swap, int bn) {
 __host__ __device__ constexpr int smem_bytes(bool swap, int bn) {
   return num_stages(swap, bn) * stage_bytes(bn) + 1024 /* align */ + 512 /* barriers */ + recv_bytes(swap, bn);
 }
+// CTA pairs (many rows, 256-feature tiles): a stage holds this CTA's 128 token rows and ITS HALF of the 256 weight rows
+constexpr int kBandM = 8;              // token tiles per band of the pairs' tile order
+constexpr int kPairStageBytes = 2 * kRowsA * kBlockK * 2;
+constexpr int kPairStages = 7;           // 224 KB of stages + barriers: all the shared memory a CTA may have (227 KB); 1.9 us of MMA work in flight
+constexpr int kPairSmemBytes = kPairStages * kPairStageBytes + 1024 + 512;
 __host__ __device__ constexpr uint32_t tmem_cols(int bn) { return 2 * bn < 32 ? 32u : static_cast<uint32_t>(2 * bn); }
 
 struct Args {
@@ -105,6 +110,42 @@ __device__ __forceinline__ void cluster_sync_all() {   // every thread of every 
   asm volatile("barrier.cluster.arrive.release.aligned;" ::: "memory");
   asm volatile("barrier.cluster.wait.acquire.aligned;" ::: "memory");
 }
+// ---- CTA pairs: one tcgen05.mma over two SMs (cta_group::2), issued by the CTA of even rank ----
+__device__ __forceinline__ uint32_t peer_addr(const void* local_smem, uint32_t cta) {   // the same offset in the CTA of rank `cta`
+  uint32_t remote;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(remote) : "r"(smem_u32(local_smem)), "r"(cta));
+  return remote;
+}
+// tile → this CTA's shared memory; the bytes are counted on a barrier that may live in the other CTA of the pair
+__device__ __forceinline__ void tma_load_2d_pair(const CUtensorMap* map, uint32_t bar_cluster_addr, void* dst, int c0, int c1) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%3, %4}], [%2];"
+      ::"r"(smem_u32(dst)), "l"(reinterpret_cast<uint64_t>(map)), "r"(bar_cluster_addr), "r"(c0), "r"(c1)
+      : "memory");
+}
+__device__ __forceinline__ void tmem_alloc_cols_pair(uint32_t* dst_smem, uint32_t cols) {   // the same warp of BOTH CTAs
+  asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(dst_smem)), "r"(cols) : "memory");
+  asm volatile("tcgen05.relinquish_alloc_permit.cta_group::2.sync.aligned;" ::: "memory");
+}
+__device__ __forceinline__ void tmem_dealloc_pair(uint32_t taddr, uint32_t cols) {
+  asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(cols) : "memory");
+}
+// D[tmem of both CTAs, 256 rows] (+)= A[128 rows in each CTA's shared memory] * B[half of the N rows in each CTA's]
+__device__ __forceinline__ void umma_ss_pair(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc, uint32_t idesc, uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::2.kind::f16 [%0], %1, %2, %3, p;\n\t}"
+      ::"r"(d_tmem), "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate) : "memory");
+}
+// one arrival, once every MMA issued so far has completed, on the barrier at this cluster address (either CTA of the pair)
+__device__ __forceinline__ void umma_commit_pair(uint32_t bar_cluster_addr) {
+  asm volatile("tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(bar_cluster_addr) : "memory");
+}
+__device__ __forceinline__ void mbar_arrive_cluster(uint32_t bar_cluster_addr) {
+  asm volatile("mbarrier.arrive.shared::cluster.b64 _, [%0];" ::"r"(bar_cluster_addr) : "memory");
+}
+
 // `bytes` (a multiple of 16) from this CTA's shared memory to the same offset as `dst_local` in the CTA of rank `cta`, counted
 // on the mbarrier at the offset of `bar_local` there (asynchronous copy between the shared memories of a cluster)
 __device__ __forceinline__ void bulk_copy_to_peer(void* dst_local, const void* src, uint32_t bytes, uint64_t* bar_local, uint32_t cta) {
@@ -135,12 +176,12 @@ __device__ __forceinline__ int sk_cta_of(int64_t unit, int64_t units, int64_t gr
 
 // A CTA's list of segments: first its whole tiles (tile = blockIdx + i * grid: concurrent CTAs work on neighbouring tiles,
 // which share a weight tile through L2), then its share of the (tile, k-block) units of the remaining tiles.
-template <bool kSwap, int kBN>
+template <bool kSwap, int kBN, bool kPair = false>
 struct Schedule {
   int64_t tile;             // next whole tile
   int64_t cursor, end;      // unit range of the shared tiles
   __device__ __forceinline__ void init(const Args& a) {
-    tile = blockIdx.x;
+    tile = kPair ? blockIdx.x >> 1 : blockIdx.x;      // a pair of CTAs walks the 256-token tiles together
     cursor = end = 0;
     if (a.cluster_parts > 1) {          // one segment: this CTA's share of the k-blocks of tile blockIdx / parts
       const int64_t p = blockIdx.x % a.cluster_parts;
@@ -157,6 +198,19 @@ struct Schedule {
     if (kSwap) {
       s.a_row0 = static_cast<int>(t) * kRowsA;   // weight rows; all tokens (M <= kBN) are the B side
       s.b_row0 = 0;
+    } else if (kPair) {
+      // Bands of at most kBandM token tiles (all bands about equally tall), each swept feature tile by feature tile with the band's token tiles adjacent: the pairs
+      // that run at the same time cover a roughly square patch (8 token tiles x 9 feature tiles on 74 pairs), so a tile of
+      // either operand that one pair brings into L2 serves as many others as possible (a long K makes either operand larger
+      // than L2: what is not shared between concurrent pairs is read from HBM again).
+      const int n_bands = (a.m_tiles + kBandM - 1) / kBandM;
+      const int tall = (a.m_tiles + n_bands - 1) / n_bands;                    // 17 token tiles: bands of 6, 6 and 5
+      const int band = static_cast<int>(t / (static_cast<int64_t>(tall) * a.n_tiles));
+      const int m0 = band * tall;
+      const int rows = a.m_tiles - m0 < tall ? a.m_tiles - m0 : tall;          // token tiles of this band (the last may be shorter)
+      const int in_band = static_cast<int>(t - static_cast<int64_t>(band) * tall * a.n_tiles);
+      s.a_row0 = (m0 + in_band % rows) * (2 * kRowsA) + static_cast<int>(blockIdx.x & 1) * kRowsA;   // this CTA's half
+      s.b_row0 = (in_band / rows) * kBN;      // all 256 weight rows of the tile (the accumulator's columns)
     } else {
       s.a_row0 = static_cast<int>(t % a.m_tiles) * kRowsA;   // tokens, fastest
       s.b_row0 = static_cast<int>(t / a.m_tiles) * kBN;      // weight rows
@@ -173,7 +227,7 @@ struct Schedule {
     if (tile < a.whole_tiles) {
       place(a, tile, s);
       s.kb0 = 0; s.kb1 = a.kb_total; s.shared_tile = -1; s.partial = false;
-      tile += gridDim.x;
+      tile += kPair ? gridDim.x >> 1 : gridDim.x;
       return true;
     }
     if (cursor >= end) return false;
@@ -208,11 +262,12 @@ __device__ __forceinline__ uint32_t pack2(T lo, T hi) {
 
 constexpr int kChunk = 16;   // accumulator columns handled at a time by an epilogue thread
 
-template <bool kSwap, int kBN, typename T>
+template <bool kSwap, int kBN, typename T, bool kPair = false>
 __global__ void __launch_bounds__(kThreads, ctas_per_sm(kSwap, kBN))
 linear_sm100_kernel(const __grid_constant__ CUtensorMap a_map, const __grid_constant__ CUtensorMap b_map, const Args a) {
-  constexpr int kStages = num_stages(kSwap, kBN);
-  constexpr int kStageBytes = stage_bytes(kBN);
+  static_assert(!kPair || (!kSwap && kBN == 256), "CTA pairs serve the 256-feature tiles of the many-row plan");
+  constexpr int kStages = kPair ? kPairStages : num_stages(kSwap, kBN);
+  constexpr int kStageBytes = kPair ? kPairStageBytes : stage_bytes(kBN);
   constexpr int kABytes = kRowsA * kBlockK * 2;
   constexpr bool kBf16 = std::is_same<T, __nv_bfloat16>::value;
   extern __shared__ uint8_t smem_raw[];
@@ -221,8 +276,8 @@ linear_sm100_kernel(const __grid_constant__ CUtensorMap a_map, const __grid_cons
   uint64_t* full = bars;                    // [kStages] TMA landed
   uint64_t* empty = bars + kStages;         // [kStages] MMAs that read the stage are done
   uint64_t* acc_full = bars + 2 * kStages;  // [2] accumulator complete
-  uint64_t* acc_empty = acc_full + 2;       // [2] accumulator drained (4 arrivals: one per epilogue warp)
-  uint64_t* epi_all = acc_empty + 2;        // 128 arrivals: every epilogue thread published its partial
+  uint64_t* acc_empty = acc_full + 2;       // [2] accumulator drained (one arrival per epilogue warp; pairs: of both CTAs, on the leader's)
+  uint64_t* epi_all = acc_empty + 2;        // kEpiThreads arrivals: every epilogue thread published its partial
   uint64_t* epi_go = epi_all + 1;           // 1 arrival: the verdict "this CTA reduces the tile" is in shared memory
   uint64_t* recv_bar = epi_go + 1;          // cluster reduction: 128 arrivals per CTA of the cluster, every share has landed
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(recv_bar + 1);
@@ -234,7 +289,7 @@ linear_sm100_kernel(const __grid_constant__ CUtensorMap a_map, const __grid_cons
   if (warp == 1) {
     if (lane == 0) {
       for (int i = 0; i < kStages; ++i) { mbar_init(&full[i], 1); mbar_init(&empty[i], 1); }
-      for (int i = 0; i < 2; ++i) { mbar_init(&acc_full[i], 1); mbar_init(&acc_empty[i], 4); }
+      for (int i = 0; i < 2; ++i) { mbar_init(&acc_full[i], 1); mbar_init(&acc_empty[i], (kPair ? 2 : 1) * (kEpiThreads / 32)); }   // every epilogue warp (pairs: of both CTAs)
       mbar_init(epi_all, kEpiThreads);
       mbar_init(epi_go, 1);
       mbar_init(recv_bar, 1);
@@ -249,7 +304,8 @@ linear_sm100_kernel(const __grid_constant__ CUtensorMap a_map, const __grid_cons
       }
     }
     __syncwarp();
-    tmem_alloc_cols(tmem_slot, tmem_cols(kBN));
+    if (kPair) tmem_alloc_cols_pair(tmem_slot, tmem_cols(kBN));
+    else tmem_alloc_cols(tmem_slot, tmem_cols(kBN));
   }
   tc_fence_before();
   __syncthreads();
@@ -257,9 +313,12 @@ linear_sm100_kernel(const __grid_constant__ CUtensorMap a_map, const __grid_cons
   const uint32_t tmem_base = *tmem_slot;
   // the peers' receive barriers exist before anyone can arrive on them (ahead of the dependency wait: the CTAs of a cluster
   // start together, and the predecessor kernel is still finishing)
-  if (kSwap && a.cluster_parts > 1) cluster_sync_all();
+  if ((kSwap && a.cluster_parts > 1) || kPair) cluster_sync_all();
+  // pairs: the CTA of even rank (the leader) owns the barriers that say "stage filled" and "accumulator drained", and issues
+  // every MMA; each CTA owns its "stage free" and "accumulator complete" barriers, on which the leader's commits arrive
+  const uint32_t pair_rank = kPair ? cluster_ctarank() : 0u;
 
-  Schedule<kSwap, kBN> sched;
+  Schedule<kSwap, kBN, kPair> sched;
   sched.init(a);
   Segment seg;
 
@@ -278,7 +337,7 @@ linear_sm100_kernel(const __grid_constant__ CUtensorMap a_map, const __grid_cons
     if (lane == 0) {
       int ahead = 0;                                  // stages whose weight half is already on its way
       if (kSwap && a.weights_ahead) {
-        Schedule<kSwap, kBN> peek = sched;
+        Schedule<kSwap, kBN, kPair> peek = sched;
         Segment s0;
         const int limit = a.weights_ahead < kStages ? a.weights_ahead : kStages;
         while (ahead < limit && peek.next(a, s0)) {
@@ -298,6 +357,14 @@ linear_sm100_kernel(const __grid_constant__ CUtensorMap a_map, const __grid_cons
           uint8_t* sa = smem + stage * kStageBytes;
           if (step < ahead) {                         // first lap: the stage is free and its weight half was issued above
             tma_load_2d(&b_map, &full[stage], sa + kABytes, kb * kBlockK, seg.b_row0);
+          } else if (kPair) {
+            ok = mbar_wait(&empty[stage], phase ^ 1, abort_flag, a);
+            if (!ok) break;
+            // both CTAs' copies of the stage are counted on the leader's barrier, which expects the bytes of both
+            if (pair_rank == 0) mbar_expect_tx(&full[stage], 2 * kStageBytes);
+            const uint32_t bar = peer_addr(&full[stage], 0);
+            tma_load_2d_pair(&a_map, bar, sa, kb * kBlockK, seg.a_row0);
+            tma_load_2d_pair(&b_map, bar, sa + kABytes, kb * kBlockK, seg.b_row0 + static_cast<int>(pair_rank) * (kBN / 2));
           } else {
             ok = mbar_wait(&empty[stage], phase ^ 1, abort_flag, a);   // a fresh barrier passes the first lap
             if (!ok) break;
@@ -316,8 +383,9 @@ linear_sm100_kernel(const __grid_constant__ CUtensorMap a_map, const __grid_cons
     __syncwarp();
   } else if (warp == 1) {
     // =========================== MMA issuer ===========================
-    if (lane == 0) {
-      const uint32_t idesc = make_idesc(kBf16, false, kBN);
+    if (lane == 0 && pair_rank == 0) {
+      // pairs: M = 256 (bits 24-28 hold M / 16), N = 256; one instruction covers both CTAs' token rows
+      const uint32_t idesc = kPair ? (make_idesc(kBf16, false, kBN) & ~(0x1fu << 24)) | ((2u * kRowsA >> 4) << 24) : make_idesc(kBf16, false, kBN);
       int stage = 0; uint32_t phase = 0;
       int n_seg = 0;
       bool ok = true;
@@ -336,12 +404,17 @@ linear_sm100_kernel(const __grid_constant__ CUtensorMap a_map, const __grid_cons
           const uint32_t sa = smem_u32(smem + stage * kStageBytes), sb = sa + kABytes;
 #pragma unroll
           for (int kk = 0; kk < kBlockK / 16; ++kk) {
-            umma_ss(d, desc_kmajor_sw128(sa + kk * 32), desc_kmajor_sw128(sb + kk * 32), idesc, (kb > seg.kb0 || kk > 0) ? 1u : 0u);
+            if (kPair) umma_ss_pair(d, desc_kmajor_sw128(sa + kk * 32), desc_kmajor_sw128(sb + kk * 32), idesc, (kb > seg.kb0 || kk > 0) ? 1u : 0u);
+            else umma_ss(d, desc_kmajor_sw128(sa + kk * 32), desc_kmajor_sw128(sb + kk * 32), idesc, (kb > seg.kb0 || kk > 0) ? 1u : 0u);
           }
-          umma_commit(&empty[stage]);
+          if (kPair) { umma_commit_pair(smem_u32(&empty[stage])); umma_commit_pair(peer_addr(&empty[stage], 1)); }
+          else umma_commit(&empty[stage]);
           if (++stage == kStages) { stage = 0; phase ^= 1; }
         }
-        if (ok) umma_commit(&acc_full[acc]);
+        if (ok) {
+          if (kPair) { umma_commit_pair(smem_u32(&acc_full[acc])); umma_commit_pair(peer_addr(&acc_full[acc], 1)); }
+          else umma_commit(&acc_full[acc]);
+        }
       }
     }
     __syncwarp();
@@ -349,7 +422,8 @@ linear_sm100_kernel(const __grid_constant__ CUtensorMap a_map, const __grid_cons
     // =========================== epilogue: warps 2-5, thread = accumulator row ===========================
     const int quarter = warp & 3;                       // the TMEM lanes a warp may read: 32 * (warp id mod 4)
     const int r = quarter * 32 + lane;                  // accumulator row
-    const int et = threadIdx.x - kEpiWarp0 * 32;        // 0..127
+    const int et = threadIdx.x - kEpiWarp0 * 32;        // 0..255
+    const int half = (warp - kEpiWarp0) >> 2;           // chunks half, half + 2, ... of the accumulator's columns
     const uint32_t lane_base = static_cast<uint32_t>(quarter * 32) << 16;
     T* out = reinterpret_cast<T*>(a.out);
     const T* bias = reinterpret_cast<const T*>(a.bias);
@@ -443,7 +517,7 @@ linear_sm100_kernel(const __grid_constant__ CUtensorMap a_map, const __grid_cons
         float* send = reinterpret_cast<float*>(smem);
         float* recv = reinterpret_cast<float*>(smem + kStages * kStageBytes + 512);
 #pragma unroll 1
-        for (int c0 = 0; c0 < n_cols; c0 += kChunk) {
+        for (int c0 = half * kChunk; c0 < n_cols; c0 += 2 * kChunk) {
           uint32_t raw[kChunk];
           tc::tmem_ld16(t_acc + c0, raw);
           tc_wait_ld();
@@ -470,7 +544,7 @@ linear_sm100_kernel(const __grid_constant__ CUtensorMap a_map, const __grid_cons
         // shares added in rank order: the result does not depend on timing. All loads of a column group first.
         const int my_cols = n_cols > rank ? (n_cols - 1 - rank) / parts + 1 : 0;
 #pragma unroll 1
-        for (int l0 = 0; l0 < my_cols; l0 += 4) {
+        for (int l0 = half * 4; l0 < my_cols; l0 += 8) {
           float v[8][4];
 #pragma unroll
           for (int p = 0; p < 8; ++p) {
@@ -497,7 +571,7 @@ linear_sm100_kernel(const __grid_constant__ CUtensorMap a_map, const __grid_cons
         }
       } else if (!seg.partial) {
 #pragma unroll 1
-        for (int c0 = 0; c0 < n_cols; c0 += kChunk) {
+        for (int c0 = half * kChunk; c0 < n_cols; c0 += 2 * kChunk) {
           uint32_t raw[kChunk];
           tc::tmem_ld16(t_acc + c0, raw);
           tc_wait_ld();
@@ -508,14 +582,17 @@ linear_sm100_kernel(const __grid_constant__ CUtensorMap a_map, const __grid_cons
         }
         tc_fence_before();
         __syncwarp();
-        if (lane == 0) mbar_arrive(&acc_empty[acc]);
+        if (lane == 0) {
+          if (kPair) mbar_arrive_cluster(peer_addr(&acc_empty[acc], 0));   // the leader waits for both CTAs' epilogues
+          else mbar_arrive(&acc_empty[acc]);
+        }
       } else {
         // This CTA holds only some k-blocks of the tile: publish its share as fp32 [128 rows][kBN columns]; slot 0 = the first
         // shared tile of the CTA's unit range, slot 1 = its last.
         const int first_st = static_cast<int>(sk_first_unit(blockIdx.x, a.units, a.sk_grid) / a.kb_total);
         float* mine = a.partials + (static_cast<int64_t>(blockIdx.x) * 2 + (seg.shared_tile == first_st ? 0 : 1)) * (kBN * kRowsA) + r * kBN;
 #pragma unroll 1
-        for (int c0 = 0; c0 < n_cols; c0 += kChunk) {
+        for (int c0 = half * kChunk; c0 < n_cols; c0 += 2 * kChunk) {
           uint32_t raw[kChunk];
           tc::tmem_ld16(t_acc + c0, raw);
           tc_wait_ld();
@@ -552,7 +629,7 @@ linear_sm100_kernel(const __grid_constant__ CUtensorMap a_map, const __grid_cons
           const int first_slot = sk_first_unit(c_first, a.units, a.sk_grid) == t0 ? 0 : 1;
           constexpr int kBatch = 4;
 #pragma unroll 1
-          for (int c0 = 0; c0 < n_cols; c0 += kChunk) {
+          for (int c0 = half * kChunk; c0 < n_cols; c0 += 2 * kChunk) {
             float sum[kChunk];
 #pragma unroll
             for (int i = 0; i < kChunk; ++i) sum[i] = 0.f;
@@ -586,17 +663,22 @@ linear_sm100_kernel(const __grid_constant__ CUtensorMap a_map, const __grid_cons
   // A CTA of a cluster leaves only when every peer holds all its shares: the copies out of this CTA's shared memory are then
   // complete. (Execution barrier only: nobody has to see this CTA's output stores before it may go.)
   if (kSwap && a.cluster_parts > 1) cluster_sync_relaxed();
+  // Pairs: the leader's MMAs read the other CTA's shared memory and write its TMEM, the other CTA's copies and arrivals
+  // land on the leader's barriers: neither leaves, nor frees TMEM, before both are done.
+  if (kPair) { tc_fence_before(); cluster_sync_all(); }
   tc_fence_before();
   __syncthreads();
   if (warp == 1) {
     tc_fence_after();
-    tc::tmem_dealloc(tmem_base, tmem_cols(kBN));
+    if (kPair) tmem_dealloc_pair(tmem_base, tmem_cols(kBN));
+    else tc::tmem_dealloc(tmem_base, tmem_cols(kBN));
   }
 }
 
 // ---- host side ---------------------------------------------------------------------------------------------
 struct Plan {
   bool swap;
+  bool pair;      // many rows: 256 x 256 tiles worked by pairs of CTAs (one MMA over two SMs)
   int bn;         // B-tile rows: token tile (few rows) or feature tile (many rows)
   int m_tiles, n_tiles, kb_total;
   int whole_tiles;   // tiles that run whole, round-robin
@@ -607,8 +689,18 @@ struct Plan {
   int grid;
 };
 
+// PDLLM_GEMM_PAIRS=0: every many-row tile in one CTA (for comparisons)
+inline bool pairs_enabled() {
+  static const bool on = [] {
+    const char* v = std::getenv("PDLLM_GEMM_PAIRS");
+    return !(v != nullptr && v[0] == '0');
+  }();
+  return on;
+}
+
 inline Plan make_plan(int64_t m, int64_t n, int64_t k) {
   Plan pl;
+  pl.pair = false;
   int sms = sm_count();
   pl.kb_total = static_cast<int>((k + kBlockK - 1) / kBlockK);
   pl.swap = m <= 128;
@@ -627,6 +719,20 @@ inline Plan make_plan(int64_t m, int64_t n, int64_t k) {
     // Narrower tiles when wide ones would leave SMs without work. (Keeping the wide tile and dealing the (tile, k-block) units of
     // ALL tiles over the SMs was measured at 512 rows: 3x slower — every CTA then trades a 128 KB fp32 partial through L2.)
     pl.bn = tiles256 >= sms ? 256 : 128;
+    if (pl.bn == 256 && m >= 512 && pairs_enabled()) {
+      // Two CTAs per 256-token x 256-feature tile: each stages its 128 token rows and HALF of the weight rows, and one
+      // tcgen05.mma (cta_group::2, M = 256) reads both shared memories — half the shared-memory traffic per flop of the
+      // single-CTA 128 x 256 tile, and a ring of 6 stages instead of 4. Whole tiles only, dealt round-robin over the pairs.
+      pl.pair = true;
+      pl.m_tiles = static_cast<int>((m + 2 * kRowsA - 1) / (2 * kRowsA));
+      pl.n_tiles = static_cast<int>((n + 255) / 256);
+      tiles = static_cast<int64_t>(pl.m_tiles) * pl.n_tiles;
+      pl.whole_tiles = static_cast<int>(tiles);
+      pl.shared_tiles = 0; pl.units = 0; pl.sk_grid = 0; pl.cluster_parts = 1;
+      const int64_t pairs = tiles < sms / 2 ? tiles : sms / 2;
+      pl.grid = static_cast<int>(2 * pairs);
+      return pl;
+    }
     pl.n_tiles = static_cast<int>((n + pl.bn - 1) / pl.bn);
     tiles = static_cast<int64_t>(pl.m_tiles) * pl.n_tiles;
     // Full waves of whole tiles. A last wave that fills less than three quarters of the SMs is cut along K instead: each of
@@ -746,7 +852,42 @@ inline int launch_one(const CUtensorMap& a_map, const CUtensorMap& b_map, const 
 }
 
 template <typename T>
+inline int launch_pairs(const CUtensorMap& a_map, const CUtensorMap& b_map, const Args& a, int grid, cudaStream_t stream) {
+  auto* fn = linear_sm100_kernel<false, 256, T, true>;
+  {
+    static std::mutex mu;
+    static bool done[64] = {false};
+    int dev = 0;
+    cudaGetDevice(&dev);
+    std::lock_guard<std::mutex> lock(mu);
+    if (dev < 0 || dev >= 64 || !done[dev]) {
+      cudaError_t e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, kPairSmemBytes);
+      if (e != cudaSuccess) return fail(static_cast<int>(e), "cudaFuncSetAttribute(linear, pairs): %s", cudaGetErrorString(e));
+      if (dev >= 0 && dev < 64) done[dev] = true;
+    }
+  }
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(static_cast<unsigned>(grid), 1, 1);
+  cfg.blockDim = dim3(kThreads, 1, 1);
+  cfg.dynamicSmemBytes = kPairSmemBytes;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[2];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = 2;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[1].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = dependent_launch_enabled() ? 2 : 1;
+  cudaError_t e = cudaLaunchKernelEx(&cfg, fn, a_map, b_map, a);
+  if (e != cudaSuccess) return fail(static_cast<int>(e), "linear_sm100_kernel (CTA pairs): %s", cudaGetErrorString(e));
+  return check_launch("linear_sm100_kernel");
+}
+
+template <typename T>
 inline int launch_typed(const Plan& pl, const CUtensorMap& a_map, const CUtensorMap& b_map, const Args& a, cudaStream_t stream) {
+  if (pl.pair) return launch_pairs<T>(a_map, b_map, a, pl.grid, stream);
   if (pl.swap) {
     switch (pl.bn) {
       case 16: return launch_one<true, 16, T>(a_map, b_map, a, pl.grid, stream);
@@ -784,7 +925,7 @@ inline int launch(const void* x, int64_t x_stride, const void* w, int64_t w_stri
   {
     uint64_t dims[2] = {static_cast<uint64_t>(k), static_cast<uint64_t>(n)};
     uint64_t str[1] = {static_cast<uint64_t>(w_stride) * 2};
-    uint32_t box[2] = {kBlockK, static_cast<uint32_t>(pl.swap ? kRowsA : pl.bn)};
+    uint32_t box[2] = {kBlockK, static_cast<uint32_t>(pl.swap ? kRowsA : (pl.pair ? pl.bn / 2 : pl.bn))};   // pairs: each CTA copies its half
     if ((rc = tc::encode_map(&w_map, bf16, w, 2, dims, str, box)) != 0) return rc;
   }
   Args a;

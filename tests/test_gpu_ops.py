@@ -914,6 +914,32 @@ def test_linear_fused_silu_mul(ops, cuda_device, m):
     assert rel_err(fused, ref) < 5e-3
 
 
+def test_linear_cta_pairs(ops, cuda_device):
+    """512 rows and more with at least one 256-wide feature tile per SM: 256 x 256 tiles worked by pairs of CTAs (one MMA over two
+    SMs, each CTA staging its token rows and half of the weight rows). Ragged last tiles in M (a second CTA with no rows at
+    all), N and K, bias, fp16, and the fused activation; every tile is whole, so the fused result has the unfused one's bits."""
+    g = torch.Generator().manual_seed(91)
+    for (m, n, k, with_bias, dtype) in ((1300, 4000, 1376, True, torch.bfloat16), (513, 37888, 512, False, torch.float16),
+                                        (2049, 5120, 704, True, torch.bfloat16), (640, 9472, 256, False, torch.bfloat16)):
+        x = (torch.randn(m, k, generator=g) * 0.5).to(dtype)
+        w = (torch.randn(n, k, generator=g) * 0.05).to(dtype)
+        b = torch.randn(n, generator=g).to(dtype) if with_bias else None
+        xd, wd, bd = x.to(cuda_device), w.to(cuda_device), None if b is None else b.to(cuda_device)
+        out = ops.linear(xd, wd, bd)
+        again = ops.linear(xd, wd, bd)
+        ops.check_status(cuda_device)
+        _assert_within_one_ulp(out, _linear_reference(x, w, b, False), dtype)
+        assert torch.equal(out, again), (m, n, k)
+    m, inter, k = 1300, 4096, 512
+    x = (torch.randn(m, k, generator=g) * 0.5).bfloat16().to(cuda_device)
+    gate = (torch.randn(inter, k, generator=g) * 0.1).bfloat16().to(cuda_device)
+    up = (torch.randn(inter, k, generator=g) * 0.1).bfloat16().to(cuda_device)
+    fused = ops.linear(x, torch.stack([gate, up], dim=1).reshape(2 * inter, k).contiguous(), silu_mul_interleaved=True)
+    unfused = ops.silu_mul(ops.linear(x, torch.cat([gate, up], dim=0).contiguous()))
+    ops.check_status(cuda_device)
+    assert torch.equal(fused, unfused)
+
+
 def test_linear_rejects_what_it_cannot_run(ops, cuda_device):
     x = torch.zeros(8, 64, dtype=torch.float32, device=cuda_device)
     with pytest.raises(NotImplementedError):
