@@ -189,9 +189,10 @@ struct Schedule {
       end = (p + 1) * a.kb_total / a.cluster_parts;
       return;
     }
-    if (static_cast<int>(blockIdx.x) < a.sk_grid) {
-      cursor = sk_first_unit(blockIdx.x, a.units, a.sk_grid);
-      end = sk_first_unit(static_cast<int64_t>(blockIdx.x) + 1, a.units, a.sk_grid);
+    const int64_t owner = kPair ? blockIdx.x >> 1 : blockIdx.x;     // pairs: both CTAs work the same unit range, each on its rows
+    if (owner < a.sk_grid) {
+      cursor = sk_first_unit(owner, a.units, a.sk_grid);
+      end = sk_first_unit(owner + 1, a.units, a.sk_grid);
     }
   }
   __device__ __forceinline__ void place(const Args& a, int64_t t, Segment& s) const {
@@ -589,7 +590,10 @@ linear_sm100_kernel(const __grid_constant__ CUtensorMap a_map, const __grid_cons
       } else {
         // This CTA holds only some k-blocks of the tile: publish its share as fp32 [128 rows][kBN columns]; slot 0 = the first
         // shared tile of the CTA's unit range, slot 1 = its last.
-        const int first_st = static_cast<int>(sk_first_unit(blockIdx.x, a.units, a.sk_grid) / a.kb_total);
+        // (pairs: the unit ranges belong to pairs; each CTA publishes, counts and reduces its own 128 rows independently)
+        const int64_t owner = kPair ? blockIdx.x >> 1 : blockIdx.x;
+        const int side = kPair ? static_cast<int>(blockIdx.x & 1) : 0;
+        const int first_st = static_cast<int>(sk_first_unit(owner, a.units, a.sk_grid) / a.kb_total);
         float* mine = a.partials + (static_cast<int64_t>(blockIdx.x) * 2 + (seg.shared_tile == first_st ? 0 : 1)) * (kBN * kRowsA) + r * kBN;
 #pragma unroll 1
         for (int c0 = half * kChunk; c0 < n_cols; c0 += 2 * kChunk) {
@@ -602,7 +606,10 @@ linear_sm100_kernel(const __grid_constant__ CUtensorMap a_map, const __grid_cons
         }
         tc_fence_before();
         __syncwarp();
-        if (lane == 0) mbar_arrive(&acc_empty[acc]);
+        if (lane == 0) {
+          if (kPair) mbar_arrive_cluster(peer_addr(&acc_empty[acc], 0));
+          else mbar_arrive(&acc_empty[acc]);
+        }
         __threadfence();
         mbar_arrive(epi_all);
         const int64_t t0 = static_cast<int64_t>(seg.shared_tile) * a.kb_total;
@@ -610,9 +617,10 @@ linear_sm100_kernel(const __grid_constant__ CUtensorMap a_map, const __grid_cons
           ok = mbar_wait(epi_all, epi_phase, abort_flag, a);
           if (ok) {
             const int parts = sk_cta_of(t0 + a.kb_total - 1, a.units, a.sk_grid) - sk_cta_of(t0, a.units, a.sk_grid) + 1;
-            const int prev = atomicAdd(&a.tile_counters[seg.shared_tile], 1);
+            int* counter = &a.tile_counters[kPair ? 2 * seg.shared_tile + side : seg.shared_tile];
+            const int prev = atomicAdd(counter, 1);
             const int last = prev == parts - 1 ? 1 : 0;
-            if (last) a.tile_counters[seg.shared_tile] = 0;      // every share has arrived: ready for the next launch
+            if (last) *counter = 0;      // every share has arrived: ready for the next launch
             reduce_flag[0] = last;
             mbar_arrive(epi_go);
           }
@@ -640,7 +648,7 @@ linear_sm100_kernel(const __grid_constant__ CUtensorMap a_map, const __grid_cons
               for (int p = 0; p < kBatch; ++p) {
                 const int c = cb + p;
                 const float4* part = reinterpret_cast<const float4*>(
-                    a.partials + (static_cast<int64_t>(c) * 2 + (c == c_first ? first_slot : 0)) * (kBN * kRowsA) + r * kBN + c0);
+                    a.partials + ((kPair ? static_cast<int64_t>(c) * 2 + side : static_cast<int64_t>(c)) * 2 + (c == c_first ? first_slot : 0)) * (kBN * kRowsA) + r * kBN + c0);
 #pragma unroll
                 for (int i = 0; i < kChunk / 4; ++i) v[p][i] = c <= c_last ? __ldcg(part + i) : make_float4(0.f, 0.f, 0.f, 0.f);
               }
@@ -729,8 +737,23 @@ inline Plan make_plan(int64_t m, int64_t n, int64_t k) {
       tiles = static_cast<int64_t>(pl.m_tiles) * pl.n_tiles;
       pl.whole_tiles = static_cast<int>(tiles);
       pl.shared_tiles = 0; pl.units = 0; pl.sk_grid = 0; pl.cluster_parts = 1;
-      const int64_t pairs = tiles < sms / 2 ? tiles : sms / 2;
-      pl.grid = static_cast<int>(2 * pairs);
+      const int64_t slots = sms / 2;
+      // as with single CTAs: a last wave that fills less than three quarters of the pairs is cut along K, `parts` pairs per tile
+      const int64_t rest_p = tiles % slots;
+      if (rest_p > 0 && rest_p * 4 < slots * 3) {
+        // (at least 32 k-blocks per share: a share costs a 128 KB fp32 partial per CTA through L2, measured to outweigh the
+        // saved wave at K = 3584 and to pay at K = 18944)
+        int64_t parts = slots / rest_p;
+        if (parts > pl.kb_total / 32) parts = pl.kb_total / 32;
+        if (parts >= 2 && rest_p * 2 * 4 <= kCounterHeaderBytes) {
+          pl.whole_tiles = static_cast<int>(tiles - rest_p);
+          pl.shared_tiles = static_cast<int>(rest_p);
+          pl.units = rest_p * pl.kb_total;
+          pl.sk_grid = static_cast<int>(rest_p * parts);
+        }
+      }
+      const int64_t busy = pl.whole_tiles >= slots ? slots : (pl.whole_tiles > pl.sk_grid ? pl.whole_tiles : pl.sk_grid);
+      pl.grid = static_cast<int>(2 * (busy < 1 ? 1 : busy));
       return pl;
     }
     pl.n_tiles = static_cast<int>((n + pl.bn - 1) / pl.bn);
@@ -944,7 +967,7 @@ inline int launch(const void* x, int64_t x_stride, const void* w, int64_t w_stri
     a.tile_counters = reinterpret_cast<int*>(workspace);
     a.partials = reinterpret_cast<float*>(static_cast<char*>(workspace) + kCounterHeaderBytes);
     if (!workspace_zeroed) {
-      cudaError_t e = cudaMemsetAsync(a.tile_counters, 0, static_cast<size_t>(pl.shared_tiles) * 4, stream);
+      cudaError_t e = cudaMemsetAsync(a.tile_counters, 0, static_cast<size_t>(pl.shared_tiles) * (pl.pair ? 8 : 4), stream);
       if (e != cudaSuccess) return fail(static_cast<int>(e), "cudaMemsetAsync(linear counters): %s", cudaGetErrorString(e));
     }
   }

@@ -920,7 +920,8 @@ def test_linear_cta_pairs(ops, cuda_device):
     all), N and K, bias, fp16, and the fused activation; every tile is whole, so the fused result has the unfused one's bits."""
     g = torch.Generator().manual_seed(91)
     for (m, n, k, with_bias, dtype) in ((1300, 4000, 1376, True, torch.bfloat16), (513, 37888, 512, False, torch.float16),
-                                        (2049, 5120, 704, True, torch.bfloat16), (640, 9472, 256, False, torch.bfloat16)):
+                                        (2049, 5120, 704, True, torch.bfloat16), (640, 9472, 256, False, torch.bfloat16),
+                                        (1300, 4096, 4160, True, torch.bfloat16)):     # its last wave is cut along K, two pairs per tile
         x = (torch.randn(m, k, generator=g) * 0.5).to(dtype)
         w = (torch.randn(n, k, generator=g) * 0.05).to(dtype)
         b = torch.randn(n, generator=g).to(dtype) if with_bias else None
