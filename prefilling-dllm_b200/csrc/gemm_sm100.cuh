@@ -438,7 +438,9 @@ linear_sm100_kernel(const __grid_constant__ CUtensorMap a_map, const __grid_cons
       const int acc = n_seg & 1;
       const uint32_t acc_phase = (n_seg >> 1) & 1;
       ++n_seg;
-      ok = mbar_wait(&acc_full[acc], acc_phase, abort_flag, a);
+      // (sleeping between polls: 256 threads wait here for a whole main loop, tens of microseconds on the many-row shapes,
+      // and the part runs against its power limit there)
+      ok = mbar_wait<true>(&acc_full[acc], acc_phase, abort_flag, a);
       if (!ok) break;
       tc_fence_after();
       const uint32_t t_acc = tmem_base + lane_base + static_cast<uint32_t>(acc * kBN);
