@@ -729,7 +729,10 @@ inline Plan make_plan(int64_t m, int64_t n, int64_t k) {
     // Narrower tiles when wide ones would leave SMs without work. (Keeping the wide tile and dealing the (tile, k-block) units of
     // ALL tiles over the SMs was measured at 512 rows: 3x slower — every CTA then trades a 128 KB fp32 partial through L2.)
     pl.bn = tiles256 >= sms ? 256 : 128;
-    if (pl.bn == 256 && m >= 512 && pairs_enabled()) {
+    // (pairs also for fewer wide tiles than SMs when K is long: the tiles are then cut along K over the idle pairs — the down
+    // projection at a few hundred rows, 28 tiles of 296 k-blocks)
+    if ((pl.bn == 256 || pl.kb_total >= 128) && m >= 512 && pairs_enabled()) {
+      pl.bn = 256;
       // Two CTAs per 256-token x 256-feature tile: each stages its 128 token rows and HALF of the weight rows, and one
       // tcgen05.mma (cta_group::2, M = 256) reads both shared memories — half the shared-memory traffic per flop of the
       // single-CTA 128 x 256 tile, and a ring of 6 stages instead of 4. Whole tiles only, dealt round-robin over the pairs.
