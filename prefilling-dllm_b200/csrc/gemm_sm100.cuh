@@ -1,18 +1,22 @@
 // Linear layers on the 5th-generation tensor cores (sm_100a): out[M, N] = x[M, K] · W[N, K]^T (+ bias) with an optional
 // fused SiLU(gate)·up epilogue, for the QKV / O / gate-up / down projections and the LM head of the Dream / LLaDA block.
 // bf16 or fp16 operands, fp32 accumulation in TMEM, operands staged by TMA (128-byte swizzle) through a ring of
-// shared-memory stages, one thread issuing tcgen05.mma, four warps draining the accumulator.
+// shared-memory stages, one thread issuing tcgen05.mma, eight warps draining the accumulator.
 //
 // Both operands are K-major ([rows, K] row-major), so either can be the 128-row "A" side of the instruction:
 //   * few rows (M <= 128: one block of decode rows, a draft, a commit): the WEIGHTS are A. A CTA streams 128 weight rows
 //     x K through shared memory once, the activations are the narrow B side (16..128 columns), the accumulator is
 //     out^T [128 features x M tokens]. The step is bound by reading the weights from HBM, so the (feature tile, k-block)
-//     units are dealt to the CTAs stream-K style: every CTA of the grid (one per CTA slot: two per SM for up to 64 rows) gets the same number of 16 KB weight
+//     units are dealt to the CTAs stream-K style: every CTA of the grid (one per SM) gets the same number of 16 KB weight
 //     blocks to stream, whatever N and K are; a feature tile that ends up spread over several CTAs is summed by the CTA
 //     that finishes it last, in CTA order, through fp32 partials in the workspace (an arrival counter per tile; no CTA
-//     ever waits for another).
+//     ever waits for another). A product with few feature tiles (QKV, O, down of a 7B model) instead gives every tile to a
+//     thread-block cluster whose CTAs split its k-blocks and send one another their shares with asynchronous copies between
+//     shared memories.
 //   * many rows (prefill, scoring): the ACTIVATIONS are A: tiles of 128 tokens x 256 (or 128) features, all of K per tile,
-//     tiles dealt round-robin with the token tiles of one weight tile adjacent so that concurrent CTAs share it in L2.
+//     tiles dealt round-robin with the token tiles of one weight tile adjacent so that concurrent CTAs share it in L2; from
+//     512 rows, tiles of 256 tokens x 256 features worked by PAIRS of CTAs: one tcgen05.mma over two SMs (cta_group::2), each
+//     CTA staging its 128 token rows and half of the weight rows.
 // The accumulator is double-buffered in TMEM: while the epilogue warps drain tile i, the tensor core works on tile i+1.
 // Every mbarrier wait is bounded; on expiry the CTA raises PDLLM_S_WAIT_TIMEOUT, stops issuing and frees its TMEM.
 #pragma once
@@ -34,16 +38,7 @@ constexpr int kThreads = 320;          // warp 0: TMA producer, warp 1: MMA issu
 constexpr int kEpiWarp0 = 2;
 constexpr int kEpiThreads = 256;       // two warps per TMEM lane quarter: they take alternate 16-column chunks of the accumulator
 constexpr int kSmemBudget = 200 * 1024;
-// Few rows with a B tile of at most 64 tokens (a block of decode rows): TWO CTAs per SM, each with half the ring. The same
-// number of weight bytes is in flight per SM, but one CTA's set-up, first-copy latency and reduction tail overlap the other's
-// streaming, and with programmatic dependent launch a CTA of the NEXT projection moves in (and requests its first weight
-// stages) as soon as one of this launch's two CTAs on an SM leaves, instead of waiting for a whole 200 KB CTA to retire.
-#ifndef PDLLM_GEMM_CTAS_PER_SM_FEW_ROWS
-#define PDLLM_GEMM_CTAS_PER_SM_FEW_ROWS 1
-#endif
-constexpr int kSmemBudgetShared = 96 * 1024;
 constexpr int kSmemLimit = 224 * 1024;  // ring + receive buffer + barriers stay under the 227 KB a CTA may have
-__host__ __device__ constexpr int ctas_per_sm(bool swap, int bn) { return swap && bn <= 64 ? PDLLM_GEMM_CTAS_PER_SM_FEW_ROWS : 1; }
 // Few rows: room for the shares of an accumulator that the CTAs of a cluster send one another (fp32 [sender][column][128 rows];
 // a CTA finishes every parts-th column, so at most bn + 7 columns arrive). Outside the ring: a peer may be done, and sending,
 // while this CTA's copies are still landing in its stages.
@@ -53,8 +48,7 @@ constexpr int64_t kCounterHeaderBytes = 64 * 1024;   // arrival counters of the 
 
 __host__ __device__ constexpr int stage_bytes(int bn) { return kRowsA * kBlockK * 2 + bn * kBlockK * 2; }
 __host__ __device__ constexpr int ring_budget(bool swap, int bn) {
-  return ctas_per_sm(swap, bn) > 1 ? kSmemBudgetShared
-                                   : (kSmemBudget < kSmemLimit - recv_bytes(swap, bn) ? kSmemBudget : kSmemLimit - recv_bytes(swap, bn));
+  return kSmemBudget < kSmemLimit - recv_bytes(swap, bn) ? kSmemBudget : kSmemLimit - recv_bytes(swap, bn);
 }
 __host__ __device__ constexpr int num_stages(bool swap, int bn) {
   return ring_budget(swap, bn) / stage_bytes(bn) < kMaxStages ? ring_budget(swap, bn) / stage_bytes(bn) : kMaxStages;
@@ -264,7 +258,7 @@ __device__ __forceinline__ uint32_t pack2(T lo, T hi) {
 constexpr int kChunk = 16;   // accumulator columns handled at a time by an epilogue thread
 
 template <bool kSwap, int kBN, typename T, bool kPair = false>
-__global__ void __launch_bounds__(kThreads, ctas_per_sm(kSwap, kBN))
+__global__ void __launch_bounds__(kThreads, 1)
 linear_sm100_kernel(const __grid_constant__ CUtensorMap a_map, const __grid_constant__ CUtensorMap b_map, const Args a) {
   static_assert(!kPair || (!kSwap && kBN == 256), "CTA pairs serve the 256-feature tiles of the many-row plan");
   constexpr int kStages = kPair ? kPairStages : num_stages(kSwap, kBN);
@@ -420,7 +414,7 @@ linear_sm100_kernel(const __grid_constant__ CUtensorMap a_map, const __grid_cons
     }
     __syncwarp();
   } else {
-    // =========================== epilogue: warps 2-5, thread = accumulator row ===========================
+    // =========================== epilogue: warps 2-9, thread = accumulator row, two warps per row ===========================
     const int quarter = warp & 3;                       // the TMEM lanes a warp may read: 32 * (warp id mod 4)
     const int r = quarter * 32 + lane;                  // accumulator row
     const int et = threadIdx.x - kEpiWarp0 * 32;        // 0..255
@@ -711,14 +705,13 @@ inline bool pairs_enabled() {
 inline Plan make_plan(int64_t m, int64_t n, int64_t k) {
   Plan pl;
   pl.pair = false;
-  int sms = sm_count();
+  const int sms = sm_count();
   pl.kb_total = static_cast<int>((k + kBlockK - 1) / kBlockK);
   pl.swap = m <= 128;
   int64_t tiles, sk_ctas = 0;
   if (pl.swap) {
     // bound by streaming the weights: every k-block of every feature tile is a unit, all dealt evenly
     pl.bn = m <= 16 ? 16 : m <= 32 ? 32 : m <= 64 ? 64 : 128;
-    sms *= ctas_per_sm(true, pl.bn);     // CTA slots: the grid fills them all at once
     pl.m_tiles = 1;
     pl.n_tiles = static_cast<int>((n + kRowsA - 1) / kRowsA);
     tiles = pl.n_tiles;
@@ -803,8 +796,8 @@ inline Plan make_plan(int64_t m, int64_t n, int64_t k) {
 inline int64_t workspace_bytes(int64_t m, int64_t n, int64_t k) {
   if (m <= 0 || n <= 0) return 0;
   const Plan pl = make_plan(m, n, k);
-  // a grid never exceeds the CTA slots of the device; sized for them so that one workspace serves every layer of a model
-  return kCounterHeaderBytes + static_cast<int64_t>(2) * sm_count() * ctas_per_sm(pl.swap, pl.bn) * pl.bn * kRowsA * 4;
+  // a grid never exceeds the SM count; sized for it so that one workspace serves every layer of a model
+  return kCounterHeaderBytes + static_cast<int64_t>(2) * sm_count() * pl.bn * kRowsA * 4;
 }
 
 template <bool kSwap, int kBN, typename T>
@@ -823,7 +816,7 @@ inline int launch_one(const CUtensorMap& a_map, const CUtensorMap& b_map, const 
     }
   }
   if (a.cluster_parts > 1) {
-    // All clusters of the launch must be resident at once (one or two CTAs per SM, clusters packed per GPC): take the largest
+    // All clusters of the launch must be resident at once (one CTA per SM, clusters packed per GPC): take the largest
     // cluster size, from the planned one down, for which the device says that many clusters fit; with none, one CTA per tile.
     const int tiles = grid / a.cluster_parts;
     cudaLaunchConfig_t cfg = {};
