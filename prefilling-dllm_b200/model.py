@@ -372,6 +372,9 @@ class PagedDreamModel:
         cos2, sin2 = cos.reshape(-1, d), sin.reshape(-1, d)
         captured = {}
         capture = set(capture_qk_layers) if capture_qk_layers is not None else ()
+        # A forward that is run only for the (q, k) of some layers — the eviction scorer's, which by default reads the first layer —
+        # ends at the last of them: nothing after it is returned or stored.
+        ends_at = max(capture) if capture and not want_logits and slot_mapping is None and on_layer_stored is None else None
         total = ids.numel()
         attn_out = torch.empty((total, hq, d), dtype=self.dtype, device=self.device)
         eps = a.rms_norm_eps
@@ -395,6 +398,8 @@ class PagedDreamModel:
                     ops.store_kvcache_unified_layout(k, v, k_cache, v_cache, slot_mapping, "diffusion_lm")
             if li in capture:
                 captured[li] = (q.contiguous(), k.contiguous())
+                if li == ends_at:
+                    return None, captured
             def run_attention(out, mask=new_row_mask, block_table=block_table, seq_lens=seq_lens, max_seq_len=max_seq_len,
                               q=q, k=k, v=v, k_cache=k_cache, v_cache=v_cache):
                 if block_table is not None:
