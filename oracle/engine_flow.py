@@ -48,8 +48,49 @@ def selection_mask(mode: str, seq_len: int, prefix_len: int, chunk_len: int) -> 
     raise ValueError(mode)
 
 
+def sample_tokens(logits: torch.Tensor, *, temperature: float = 0.0, top_k: Optional[int] = None, top_p: Optional[float] = None):
+    """The engine's sampler (fastdllm_engine.py:1658-1681): fp32, temperature, top-k BEFORE top-p (the eval class filters the
+    other way round), softmax; (max probability, arg-max) at temperature 0, else a categorical draw and its probability."""
+    work = logits.float()
+    if temperature > 0:
+        work = work / temperature
+    floor = torch.finfo(work.dtype).min
+    if top_k is not None:
+        kth = torch.topk(work, min(int(top_k), work.shape[-1]), dim=-1).values[..., -1, None]
+        work = work.masked_fill(work < kth, floor)
+    if top_p is not None and top_p < 1:
+        ordered, order = torch.sort(work, descending=True, dim=-1)
+        gone = torch.cumsum(torch.softmax(ordered, dim=-1), dim=-1) > float(top_p)
+        gone = torch.cat([torch.zeros_like(gone[..., :1]), gone[..., :-1]], dim=-1)
+        work = work.masked_fill(torch.zeros_like(gone).scatter(-1, order, gone), floor)
+    probs = torch.softmax(work, dim=-1)
+    if temperature > 0:
+        token = torch.distributions.Categorical(probs=probs).sample()
+        return torch.gather(probs, -1, token.unsqueeze(-1)).squeeze(-1), token
+    return probs.max(dim=-1)
+
+
+def sampled_unmask(logits: torch.Tensor, block: torch.Tensor, last_logit: Optional[torch.Tensor], *, mask_id: int, threshold: float,
+                   sampler: dict, shift: bool = True) -> torch.Tensor:
+    """fastdllm_engine.py:2143-2157 — the masked slots are sampled; the most confident is accepted, and every other one whose
+    confidence reaches the threshold. Returns the new block."""
+    shifted = logits
+    if shift:
+        shifted = torch.cat([(logits[:1] if last_logit is None else last_logit.reshape(1, -1).to(logits.dtype)), logits[:-1]], dim=0)
+    masked = block == mask_id
+    confidence, sampled = sample_tokens(shifted[masked], **sampler)
+    order = torch.argsort(confidence, descending=True, stable=True)
+    slots = masked.nonzero(as_tuple=True)[0]
+    out = block.clone()
+    for rank, j in enumerate(order.tolist()):
+        if rank == 0 or float(confidence[j]) >= threshold:
+            out[slots[j]] = sampled[j]
+    return out
+
+
 def denoise_block(model, past, key_positions: Sequence[int], block_positions: Sequence[int], first_token: int,
-                  last_context_logit: torch.Tensor, *, mask_id: int, threshold: float, shift: bool = True) -> Tuple[List[int], int]:
+                  last_context_logit: torch.Tensor, *, mask_id: int, threshold: float, shift: bool = True,
+                  sampler: Optional[dict] = None) -> Tuple[List[int], int]:
     """:2133-2157 — every step forwards the whole block against `past` (concatenated, not stored). `shift=False`: the
     un-shifted read-out of the eval class's LLaDA backend (fastdllm_parallelcomp.py:1017-1024); the reference engine has
     no such model."""
@@ -61,13 +102,18 @@ def denoise_block(model, past, key_positions: Sequence[int], block_positions: Se
         while bool((block == mask_id).any()):
             steps += 1
             out = model(block.unsqueeze(0), attention_mask=None, position_ids=pos, past_key_values=past, use_cache=False)
+            if sampler:
+                block = sampled_unmask(out.logits[0], block, last_context_logit if shift else None, mask_id=mask_id, threshold=threshold,
+                                       sampler=sampler, shift=shift)
+                continue
             block, _, _ = O.unmask_step(out.logits[0], block, mask_token_id=mask_id, threshold=threshold,
                                         last_logit=last_context_logit if shift else None, shift=shift, softmax_dtype=torch.float32)
     return block.tolist(), steps
 
 
 def prefill_and_decode(model, prompt_ids: Sequence[int], *, block_length: int, mask_id: int, threshold: float,
-                       prompt_positions: Optional[Sequence[int]] = None, keep: Optional[Sequence[int]] = None, shift: bool = True):
+                       prompt_positions: Optional[Sequence[int]] = None, keep: Optional[Sequence[int]] = None, shift: bool = True,
+                       sampler: Optional[dict] = None):
     """prefill_to_pd_record + decode_from_pd_record. `keep`: ONE ascending index list applied to every layer and KV
     head (post-hoc eviction with head-independent indices); keys keep the rotation of their original position and
     the block moves to max(kept positions) + 1 (:1953-1958).
@@ -81,13 +127,13 @@ def prefill_and_decode(model, prompt_ids: Sequence[int], *, block_length: int, m
         out = model(torch.tensor([prompt_ids + [mask_id] * block_length]), attention_mask=None, position_ids=_positions(full_pos),
                     use_cache=True)
     last = out.logits[0, n - 1] if shift else out.logits[0, n]   # un-shifted: the first MASK slot's own row
-    first = int(torch.argmax(last))
+    first = int(sample_tokens(last.reshape(1, -1), **sampler)[1][0]) if sampler and sampler.get("temperature", 0.0) > 0 else int(torch.argmax(last))
     idx = torch.arange(n) if keep is None else torch.tensor(list(keep), dtype=torch.long)
     past = [(k[:, idx], v[:, idx]) for k, v in out.past_key_values]
     key_positions = [prompt_positions[i] for i in idx.tolist()]
     block_start = max(key_positions) + 1
     ids, steps = denoise_block(model, past, key_positions, list(range(block_start, block_start + block_length)), first, last,
-                               mask_id=mask_id, threshold=threshold, shift=shift)
+                               mask_id=mask_id, threshold=threshold, shift=shift, sampler=sampler)
     return dict(first_token=first, last_context_logit=last, token_ids=ids, n_diff_steps=steps, past=past, key_positions=key_positions)
 
 

@@ -15,9 +15,10 @@ What differs in mechanism, not in result:
   * the unmask step is one kernel with one host read per step (reference :2135-2157 reads once per slot);
   * KV snapshots, loads and per-head compaction are page-copy kernels over all layers (reference: 2 x layers
     advanced-index gathers / scatters, staged through the CPU by default).
-Not built (the arguments are accepted and rejected with NotImplementedError): sparse "eviction_mask" prefill with
-delta correction, the decode delta reservoir, sampling with temperature / top-p / top-k, tensor parallelism, the
-"distinct" KV layout for this facade, chunk_to_query / bidirectional token-score directions.
+Sampling (temperature / top-k / top-p, reference :1658-1681) runs as eager steps on torch ops: the fused unmask kernel and the
+captured step graph serve the greedy rule.
+Not built (the arguments are accepted and rejected with NotImplementedError): the selection-dense variants of the sparse
+prefill, tensor parallelism, the "distinct" KV layout for this facade, chunk_to_query / bidirectional token-score directions.
 """
 
 from __future__ import annotations
@@ -27,6 +28,7 @@ from dataclasses import dataclass
 from typing import Dict, Iterable, List, Optional, Sequence, Tuple
 
 import torch
+import torch.nn.functional as F
 
 from . import ops
 from .model import denoise_blocks_batched, CachedPrefix, DreamArch, PageAllocator, PagedDreamModel, denoise_blocks, slots_for
@@ -143,8 +145,6 @@ class FastDLLMDreamEngine:
             raise NotImplementedError("this facade keeps its pool in the unified layout; the distinct layout is served by the ops only")
         if int(tensor_parallel_size) != 1:
             raise NotImplementedError("tensor parallelism is not built: one replica per GPU, data parallel over requests")
-        if self.temperature > 0 or top_p is not None or top_k is not None:
-            raise NotImplementedError("only greedy decoding (temperature 0, no top-p / top-k) is built")
         if not torch.cuda.is_available():
             raise RuntimeError("FastDLLMDreamEngine needs a CUDA device; there is no CPU path")
         self.tokenizer = None
@@ -564,7 +564,7 @@ class FastDLLMDreamEngine:
                 raise
             # the reference runs an all-MASK replace forward here (:2088-2094) and reads only row 0 of its SHIFTED logits,
             # which is the cached last-context logit: the forward changes nothing, so it is not run
-            first_token = int(torch.argmax(last_context_logit).item())
+            first_token = self._first_token(last_context_logit)
         else:
             self._prefix_cache.ensure_free(n_prompt_pages + n_block_pages)
             prompt_page_ids = self._prefix_cache.allocate_pages(n_prompt_pages)
@@ -600,7 +600,7 @@ class FastDLLMDreamEngine:
                                           logit_rows=[first_row], on_layer_stored=None if kv_stream is None else kv_stream.on_layer_stored,
                                           attention_fn=sparse_attention)
                 last_context_logit = logits[0].detach()
-                first_token = int(torch.argmax(last_context_logit).item())
+                first_token = self._first_token(last_context_logit)
                 if keep is not None and not use_sparse:
                     if (decode_delta_mode or "none").lower() in _DELTA_MODES:
                         if decode_len != self.block_length:
@@ -643,6 +643,17 @@ class FastDLLMDreamEngine:
         decode_len = len(block_positions)
         n_steps = 0
         remaining = decode_len - 1
+        if self._uses_sampler():
+            # eager steps: the forward through the C-ABI kernels, the sampler and the transfer rule on torch ops
+            block = torch.full((decode_len,), self.mask_token_id, dtype=torch.long, device=self.device)
+            block[0] = int(first_token_id)
+            while remaining > 0:
+                n_steps += 1
+                if n_steps > decode_len + 8:
+                    raise RuntimeError("denoising did not converge: every step must unmask at least one slot")
+                logits, _ = self._forward(block, block_positions, ctx_page_ids=ctx_page_ids, ctx_len=ctx_len, store_slots=block_slots)
+                remaining = self._sampled_unmask(logits, block, last_context_logit)
+            return block.clone(), n_steps
         runner = self.model.block_step_runner(block_len=decode_len, positions=block_positions, ctx_page_ids=ctx_page_ids, ctx_len=ctx_len,
                                               mask_token_id=self.mask_token_id, threshold=self.threshold, last_logit=last_context_logit,
                                               shift=self.model.arch.logit_shift, softmax_dtype=torch.float32, store_slots=block_slots,
@@ -749,15 +760,82 @@ class FastDLLMDreamEngine:
                     raise RuntimeError("denoising did not converge: every step must unmask at least one slot")
                 logits, _ = self._forward(block, record.suffix_positions, ctx_page_ids=record.prompt_page_ids, ctx_len=record.prompt_len,
                                           store_slots=slots, attention_fn=attention)
-                counts = ops.unmask_step(logits, block, mask_token_id=self.mask_token_id, threshold=self.threshold,
-                                         last_logit=record.last_context_logit, shift=self.model.arch.logit_shift, softmax_dtype=torch.float32)
-                remaining = int(counts[2].item())
+                if self._uses_sampler():
+                    remaining = self._sampled_unmask(logits, block, record.last_context_logit)
+                else:
+                    counts = ops.unmask_step(logits, block, mask_token_id=self.mask_token_id, threshold=self.threshold,
+                                             last_logit=record.last_context_logit, shift=self.model.arch.logit_shift, softmax_dtype=torch.float32)
+                    remaining = int(counts[2].item())
             ops.check_status(self.device)
             return self._finish(block.clone(), max_new_tokens, stop_token_ids, n_steps)
         finally:
             if reservoir:
                 self._prefix_cache.release_pages(reservoir)
             self.release_pd_record(record)
+
+    # ------------------------------------------------------------------------------------------------ sampling
+    def _uses_sampler(self) -> bool:
+        """True when the settings change the greedy fp32-softmax rule that the unmask kernel implements."""
+        return self.temperature > 0 or self.top_k is not None or (self.top_p is not None and self.top_p < 1)
+
+    def _sample_tokens(self, logits: torch.Tensor) -> Tuple[torch.Tensor, torch.Tensor]:
+        """(confidence, token) per row (reference :1658-1681): fp32 logits over the temperature, top-k filter (what is below the
+        k-th largest goes to the floor), THEN the nucleus filter (the smallest sorted prefix whose mass exceeds top_p, its first
+        token always kept), softmax; the arg-max and its probability at temperature 0, otherwise one categorical draw from the
+        global generator and the drawn token's probability."""
+        work = logits.float()
+        if self.temperature > 0:
+            work = work / self.temperature
+        floor = torch.finfo(work.dtype).min
+        if self.top_k is not None:
+            kth = torch.topk(work, min(int(self.top_k), work.shape[-1]), dim=-1).values[..., -1, None]
+            work = work.masked_fill(work < kth, floor)
+        if self.top_p is not None and self.top_p < 1:
+            ordered, order = torch.sort(work, descending=True, dim=-1)
+            drop_sorted = torch.cumsum(F.softmax(ordered, dim=-1), dim=-1) > float(self.top_p)
+            drop_sorted[..., 1:] = drop_sorted[..., :-1].clone()
+            drop_sorted[..., 0] = False
+            drop = torch.zeros_like(work, dtype=torch.bool)
+            drop.scatter_(-1, order, drop_sorted)
+            work = work.masked_fill(drop, floor)
+        probs = F.softmax(work, dim=-1)
+        if self.temperature > 0:
+            token = torch.distributions.Categorical(probs=probs).sample()
+            return torch.gather(probs, -1, token.unsqueeze(-1)).squeeze(-1), token
+        return probs.max(dim=-1)
+
+    def _first_token(self, logit_row: torch.Tensor) -> int:
+        """The first token of a block from the logit row that predicts it: the arg-max (no filter moves it) or, at a positive
+        temperature, a draw."""
+        if self.temperature > 0:
+            return int(self._sample_tokens(logit_row.reshape(1, -1))[1][0].item())
+        return int(torch.argmax(logit_row).item())
+
+    def _sampled_unmask(self, logits: torch.Tensor, block: torch.Tensor, last_logit: Optional[torch.Tensor]) -> int:
+        """One confidence-threshold transfer with the sampler's confidences (reference :2143-2157): the masked slots are
+        sampled, the most confident one is always accepted and every other one whose confidence reaches the threshold.
+        `block` is updated in place; returns the MASK slots left."""
+        if self.model.arch.logit_shift:
+            shifted = torch.empty_like(logits)
+            shifted[1:] = logits[:-1]
+            shifted[0] = logits[0] if last_logit is None else last_logit.reshape(-1)
+        else:
+            shifted = logits
+        masked = block == self.mask_token_id
+        n_masked = int(masked.sum().item())
+        if n_masked == 0:
+            return 0
+        confidence, sampled = self._sample_tokens(shifted[masked])
+        candidate = torch.full_like(block, self.mask_token_id)
+        candidate[masked] = sampled
+        full_confidence = torch.full(block.shape, -torch.inf, dtype=confidence.dtype, device=block.device)
+        full_confidence[masked] = confidence
+        best_confidence, best = torch.topk(full_confidence, n_masked)
+        accept = torch.zeros_like(block, dtype=torch.bool)
+        accept[best[0]] = True
+        accept[best[1:][best_confidence[1:] >= self.threshold]] = True
+        block[accept] = candidate[accept]
+        return int((block == self.mask_token_id).sum().item())
 
     def _finish(self, block: torch.Tensor, max_new_tokens: int, stop_token_ids, n_steps: int) -> FastDLLMEngineOutput:
         generated = block[:max_new_tokens].tolist()
@@ -844,7 +922,9 @@ class FastDLLMDreamEngine:
             generated = denoise_blocks(self.model, view, suffix_pos_start=int(record.suffix_positions[0]), last_logit=record.last_context_logit,
                                        first_token=None, tail_in_cache=0, max_new=int(max_new_tokens), block_length=self.block_length,
                                        mask_id=self.mask_token_id, threshold=self.threshold, softmax_dtype=torch.float32,
-                                       use_graph=not self.config.enforce_eager, steps_out=steps)
+                                       use_graph=not self.config.enforce_eager, steps_out=steps,
+                                       pick_first_token=(lambda row: torch.tensor(self._first_token(row), device=self.device)) if self.temperature > 0 else None,
+                                       threshold_step=self._sampled_unmask if self._uses_sampler() else None)
             ops.check_status(self.device)
             block = torch.tensor(generated, dtype=torch.long)
             return self._finish(block, max_new_tokens, stop_token_ids, sum(steps))
@@ -867,8 +947,8 @@ class FastDLLMDreamEngine:
         if max_new_tokens <= 0:
             return [FastDLLMEngineOutput(text="", token_ids=[], n_diff_steps=0) for _ in records]
         decode_len = records[0].decode_len
-        if any(r.decode_delta_state and r.decode_delta_state.get("enabled", False) for r in records):
-            # the delta correction runs a second attention pass per record: such records are decoded one after the other
+        if self._uses_sampler() or any(r.decode_delta_state and r.decode_delta_state.get("enabled", False) for r in records):
+            # the delta correction runs a second attention pass per record, and a sampler runs eager steps: one record after the other
             return [self.decode_from_pd_record(r, max_new_tokens=max_new_tokens, stop_token_ids=stop_token_ids) for r in records]
         try:
             for r in records:
@@ -1002,7 +1082,7 @@ class FastDLLMDreamEngine:
         prompt_t = self.model.ids_tensor(prompt_ids)
         rows = list(range(p_len - 1, p_len + draft_len - 1))        # shifted: slot j reads the logits of row p_len + j - 1
         logits, _ = self._forward(torch.cat([prompt_t, block]), positions, logit_rows=rows[:1])
-        block[0] = torch.argmax(logits[0])
+        block[0] = self._first_token(logits[0])
         confirmed = torch.zeros(draft_len, dtype=torch.bool, device=self.device)
         confirmed[0] = True
         for _ in range(max(0, int(partial_rounds or 0))):
@@ -1010,6 +1090,14 @@ class FastDLLMDreamEngine:
                 break
             before = block.clone()
             logits, _ = self._forward(torch.cat([prompt_t, block]), positions, logit_rows=rows)
+            if self._uses_sampler():
+                # the most confident masked slot by the sampler's confidences takes its sampled token (reference :1053-1059)
+                masked = (block == self.mask_token_id).nonzero(as_tuple=True)[0]
+                confidence, sampled = self._sample_tokens(logits.index_select(0, masked))
+                best = int(torch.argmax(confidence).item())
+                block[masked[best]] = sampled[best]
+                confirmed[masked[best]] = True
+                continue
             with torch.cuda.device(self.device):
                 # rows are already the shifted ones; a threshold no probability reaches leaves only the top-1 transfer
                 ops.unmask_step(logits, block, mask_token_id=self.mask_token_id, threshold=2.0, shift=False, softmax_dtype=torch.float32)
@@ -1314,7 +1402,7 @@ class FastDLLMDreamEngine:
             logits, _ = self._forward(suffix_ids, query_positions + block_positions, ctx_page_ids=all_pages, ctx_len=base_len,
                                       store_slots=slots_for(all_pages, base_len, len(suffix_ids), self.page_size), logit_rows=[q_len - 1])
             last_context_logit = logits[0].detach()
-            first_token = int(torch.argmax(last_context_logit).item())
+            first_token = self._first_token(last_context_logit)
             block, n_steps = self._denoise_block(ctx_page_ids=all_pages, ctx_len=prompt_len,
                                                  block_slots=slots_for(all_pages, prompt_len, decode_len, self.page_size),
                                                  block_positions=block_positions, first_token_id=first_token,

@@ -136,6 +136,7 @@ def record(engine) -> dict:
                                                         local_query_ids=query[-8:], max_new_tokens=BLOCK)
     out["chunk_local"] = dict(keeps=keeps, token_ids=[int(t) for t in res.token_ids], n_diff_steps=int(res.n_diff_steps))
     out["sparse_and_delta"] = record_sparse_and_delta(engine)
+    out["sampling"] = record_sampling(engine)
     return out
 
 
@@ -178,6 +179,38 @@ def record_sparse_and_delta(engine) -> dict:
             item = dict(error=f"{type(exc).__name__}: {exc}"[:300])
         cases[name] = item
     return dict(prompt_len=600, seed=13, cases=cases)
+
+
+SAMPLING_CASES = {
+    "top_k_1": dict(top_k=1),                              # every probability is 1: the whole block in one step
+    "top_k_2": dict(top_k=2),
+    "top_p_half": dict(top_p=0.5),
+    "top_k_4_top_p_0.8": dict(top_k=4, top_p=0.8),
+    "temperature_0.7_top_k_8": dict(temperature=0.7, top_k=8),
+}
+
+
+def record_sampling(engine) -> dict:
+    """The engine's sampler settings (fastdllm_engine.py:1658-1681, :2143-2157), switched on the one engine between requests:
+    filters at temperature 0 change the confidences the threshold rule sees (several slots per step even with random weights);
+    the positive temperature draws from the global generator, seeded before the request."""
+    ids = prompt(500, 21)
+    saved = (engine.temperature, engine.top_k, engine.top_p)
+    cases = {}
+    try:
+        for name, kwargs in SAMPLING_CASES.items():
+            engine.temperature, engine.top_k, engine.top_p = float(kwargs.get("temperature", 0.0)), kwargs.get("top_k"), kwargs.get("top_p")
+            torch.manual_seed(77)
+            try:
+                rec = engine.prefill_to_pd_record(ids, max_new_tokens=BLOCK)
+                first = int(rec.first_token_id)
+                res = engine.decode_from_pd_record(rec, max_new_tokens=BLOCK)
+                cases[name] = dict(first_token_id=first, token_ids=[int(t) for t in res.token_ids], n_diff_steps=int(res.n_diff_steps))
+            except Exception as exc:
+                cases[name] = dict(error=f"{type(exc).__name__}: {exc}"[:300])
+    finally:
+        engine.temperature, engine.top_k, engine.top_p = saved
+    return dict(prompt_len=500, seed=21, cases=cases)
 
 
 def make_golden_split(ids, size):

@@ -162,3 +162,28 @@ def test_sparse_prefill_and_decode_delta(golden, model):
             assert got["n_diff_steps"] == case["n_diff_steps"], name
     finally:
         model.float()
+
+
+def test_sampler_settings_at_temperature_zero(golden, model):
+    """top-k / top-p at temperature 0 leave the arg-max alone but change the confidences the threshold rule sees: the whole block in
+    one step at top_k = 1, several slots per step otherwise. (The positive-temperature case of the fixture draws from the CUDA
+    generator and is held to the engine on the GPU only.)"""
+    import make_engine_golden as G
+    from oracle import engine_flow as E
+
+    ref = golden["sampling"]
+    prompt = G.prompt(ref["prompt_len"], ref["seed"])
+    model = model.double()
+    try:
+        for name, kwargs in G.SAMPLING_CASES.items():
+            case = ref["cases"][name]
+            assert "error" not in case, (name, case)
+            if kwargs.get("temperature", 0.0) > 0:
+                continue
+            got = E.prefill_and_decode(model, prompt, block_length=BLOCK, mask_id=MASK, threshold=golden["threshold"], sampler=dict(kwargs))
+            assert got["first_token"] == case["first_token_id"], name
+            assert got["token_ids"] == case["token_ids"], name
+            assert got["n_diff_steps"] == case["n_diff_steps"], name
+        assert ref["cases"]["top_k_1"]["n_diff_steps"] == 1
+    finally:
+        model.float()

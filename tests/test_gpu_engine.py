@@ -144,6 +144,12 @@ def test_engine_facade_matches_the_reference_engine(engine):
         for key in ("kv_mode", "prompt_len_record", "full_prompt_len", "first_token_id", "suffix_positions", "n_prompt_pages", "token_ids", "n_diff_steps"):
             assert mine[key] == theirs[key], (name, key)
         assert torch.allclose(torch.tensor(mine["last_context_logit"]), torch.tensor(theirs["last_context_logit"]), atol=2e-4), name
+    # the sampler settings: filters at temperature 0 (several slots per step), and a positive temperature from a seeded generator
+    for name, theirs in ref["sampling"]["cases"].items():
+        mine = got["sampling"]["cases"][name]
+        assert "error" not in mine and "error" not in theirs, (name, mine.get("error"), theirs.get("error"))
+        for key in ("first_token_id", "token_ids", "n_diff_steps"):
+            assert mine[key] == theirs[key], (name, key)
     while engine._prefix_cache.evict_one():
         pass
     assert engine._prefix_cache.num_free_pages == free0
