@@ -219,9 +219,12 @@ def score_chunk(model, prefix_ids, chunk_ids, query_ids, label_mask, attention_m
 
 
 def per_head_keep(model, prefix_ids, chunk_ids, window_ids, *, capacity: int, num_kv_heads: int, layers: Sequence[int],
-                  attention_mask: str = "causal", pool_kernel: int = 7) -> Tuple[List[torch.Tensor], List[torch.Tensor]]:
+                  attention_mask: str = "causal", pool_kernel: int = 7, pooling: str = "maxpool", reduce_mode: str = "sum",
+                  direction: str = "query_to_chunk", keep_high: bool = True) -> Tuple[List[torch.Tensor], List[torch.Tensor]]:
     """compute_prompt_keep_indices_per_layer_per_head :1365-1470 for one chunk: the hidden states run under FULL attention
-    and only the score softmax applies `attention_mask`. Returns (keep [Hkv, capacity] per selected layer, pooled scores)."""
+    and only the score softmax applies `attention_mask`. `direction` (:1296-1323): the mass the query window's rows put on each
+    chunk token, the mass each chunk row puts on the window's keys (zero unless the mask is "full": chunk rows do not see the
+    window under the other two), or their sum. Returns (keep [Hkv, capacity] per selected layer, pooled scores)."""
     joint = list(prefix_ids) + list(chunk_ids) + list(window_ids)
     length, p, c, w = len(joint), len(prefix_ids), len(chunk_ids), len(window_ids)
     captured = {}
@@ -248,10 +251,23 @@ def per_head_keep(model, prefix_ids, chunk_ids, window_ids, *, capacity: int, nu
             half = x.shape[-1] // 2
             return x * cos[0].unsqueeze(1) + torch.cat((-x[..., half:], x[..., :half]), dim=-1) * sin[0].unsqueeze(1)
 
-        scores = O.query_to_chunk_scores(rot(q), rot(k), prefix_len=p, chunk_len=c, query_len=w, scale=attn.head_dim ** -0.5,
-                                         causal=(attention_mask == "causal"))
-        pooled = O.per_head_token_scores(scores, num_kv_heads, "maxpool", pool_kernel)
-        keeps.append(torch.stack([O.select_positions_from_token_scores(pooled[h], capacity=capacity, chunk_len=c) for h in range(num_kv_heads)]))
+        qr, kr, scale = rot(q), rot(k), attn.head_dim ** -0.5
+        parts = []
+        if direction in ("query_to_chunk", "bidirectional"):
+            parts.append(O.query_to_chunk_scores(qr, kr, prefix_len=p, chunk_len=c, query_len=w, scale=scale, reduce_mode=reduce_mode,
+                                                 causal=(attention_mask == "causal")))
+        if direction in ("chunk_to_query", "bidirectional"):
+            if attention_mask in ("full", "none"):
+                group = qr.shape[1] // kr.shape[1]
+                logits = torch.einsum("chd,lhd->hcl", qr.float()[p:p + c], kr.float().repeat_interleave(group, dim=1)) * scale
+                mass = torch.softmax(logits, dim=-1)[:, :, p + c:p + c + w]
+                parts.append(mass.mean(dim=2) if reduce_mode == "mean" else mass.sum(dim=2))
+            else:
+                parts.append(torch.zeros(qr.shape[1], c))
+        scores = parts[0] if len(parts) == 1 else parts[0] + parts[1]
+        pooled = O.per_head_token_scores(scores, num_kv_heads, pooling, pool_kernel)
+        keeps.append(torch.stack([O.select_positions_from_token_scores(pooled[h], capacity=capacity, chunk_len=c, keep_high=keep_high)
+                                  for h in range(num_kv_heads)]))
         pooled_all.append(pooled)
     return keeps, pooled_all
 

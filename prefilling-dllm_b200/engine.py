@@ -18,7 +18,7 @@ What differs in mechanism, not in result:
 Sampling (temperature / top-k / top-p, reference :1658-1681) runs as eager steps on torch ops: the fused unmask kernel and the
 captured step graph serve the greedy rule.
 Not built (the arguments are accepted and rejected with NotImplementedError): the selection-dense variants of the sparse
-prefill, tensor parallelism, the "distinct" KV layout for this facade, chunk_to_query / bidirectional token-score directions.
+prefill, tensor parallelism, the "distinct" KV layout for this facade.
 """
 
 from __future__ import annotations
@@ -1248,19 +1248,21 @@ class FastDLLMDreamEngine:
         `chunk_spans`: dicts with `chunk_ids`, `start`, `end` (span of the chunk inside the full prompt). For a chunk
         longer than `token_capacity`: one bidirectional forward over `[prefix ‖ chunk ‖ query window]` with nothing
         stored, the rotated q / k of the selected layers go to the fused scorer (query→chunk attention mass under
-        `token_attention_mask`), then max-pool, mean over each KV head's query heads, BOS + top-(capacity - 1), ascending.
+        `token_attention_mask`; with `token_score_direction` "chunk_to_query" / "bidirectional" also the mass the chunk rows put
+        on the window), then max / average / no pooling, mean over each KV head's query heads, BOS + top-(capacity - 1) (or the
+        lowest, `token_score_keep="low"`), ascending.
         Returns (keep `[layers][Hkv][active_len]` as nested lists, per-chunk meta). `token_score_backend` is accepted for
         signature parity: there is one backend."""
         if return_selection_dense_outputs:
             raise NotImplementedError("selection dense outputs (for the sparse delta prefill) are not built")
-        if (token_score_direction or "query_to_chunk").lower() != "query_to_chunk":
-            raise NotImplementedError("only token_score_direction='query_to_chunk' is built")
+        direction = (token_score_direction or "query_to_chunk").lower()
+        if direction not in {"query_to_chunk", "chunk_to_query", "bidirectional"}:
+            raise ValueError(f"Unsupported token_score_direction: {token_score_direction}")
         pooling = (token_score_pooling or "none").lower()
-        if pooling not in {"none", "maxpool"}:
-            if pooling == "avgpool":
-                raise NotImplementedError("token_score_pooling='avgpool' is not built (maxpool / none)")
+        if pooling not in {"none", "maxpool", "avgpool"}:
             raise ValueError(f"Unsupported token_score_pooling: {token_score_pooling}")
-        pool_kernel = 1 if pooling == "none" else int(token_score_pool_kernel or 1)
+        # the selection kernel max-pools; average pooling is applied to the head scores beforehand (torch), the kernel then pools over 1
+        pool_kernel = int(token_score_pool_kernel or 1) if pooling == "maxpool" else 1
         capacity = int(token_capacity or 0)
         query_ids = self._window_query(query_ids, token_score_query_window)
         arch = self.model.arch
@@ -1286,10 +1288,13 @@ class FastDLLMDreamEngine:
                 _, captured = self._forward(joint, list(range(len(joint))), want_logits=False, capture_layers=selected_layers)
                 with torch.cuda.device(self.device):
                     head_scores = torch.stack([
-                        ops.query_to_chunk_attention_scores(captured[l][0], captured[l][1], prefix_len=len(prefix), chunk_len=chunk_len,
-                                                            query_len=len(query_ids), scale=self.model.scale, reduce_mode=token_score_reduce,
-                                                            attention_mask=token_attention_mask)
+                        self._chunk_head_scores(captured[l][0], captured[l][1], prefix_len=len(prefix), chunk_len=chunk_len, query_len=len(query_ids),
+                                                direction=direction, reduce_mode=token_score_reduce, attention_mask=token_attention_mask)
                         for l in selected_layers], dim=0).contiguous()
+                    if pooling == "avgpool":
+                        kernel = max(1, min(int(token_score_pool_kernel or 1), chunk_len))
+                        flat = head_scores.reshape(-1, 1, chunk_len)
+                        head_scores = F.avg_pool1d(flat, kernel_size=kernel, padding=kernel // 2, stride=1)[..., :chunk_len].reshape(head_scores.shape).contiguous()
                     keeps = ops.evict_select(head_scores, num_kv_heads=hkv, keep_count=keep_count, pool_kernel=pool_kernel, per_head=True,
                                              force_keep_first=True, keep_high=token_score_keep == "high")
                 per_layer_keep = [keeps[min(layer_idx, len(selected_layers) - 1)].clone() for layer_idx in range(num_layers)]
@@ -1320,6 +1325,30 @@ class FastDLLMDreamEngine:
             prompt_keep.append(torch.stack(heads, dim=0).tolist())
         ops.check_status(self.device)
         return prompt_keep, chunk_meta
+
+    def _chunk_head_scores(self, q: torch.Tensor, k: torch.Tensor, *, prefix_len: int, chunk_len: int, query_len: int, direction: str,
+                           reduce_mode: str, attention_mask: str) -> torch.Tensor:
+        """fp32 [Hq, chunk_len] (reference _engine_chunk_attention_head_scores :1230-1323): the attention mass the query window's
+        rows put on each chunk token (the fused scorer), and / or the mass each chunk row puts on the query window's keys — that
+        one on torch ops: a softmax over all keys of the chunk rows, under the score mask (zero under the causal and
+        query_to_chunk masks, where chunk rows do not see the query)."""
+        parts = []
+        if direction in {"query_to_chunk", "bidirectional"}:
+            parts.append(ops.query_to_chunk_attention_scores(q, k, prefix_len=prefix_len, chunk_len=chunk_len, query_len=query_len,
+                                                             scale=self.model.scale, reduce_mode=reduce_mode, attention_mask=attention_mask))
+        if direction in {"chunk_to_query", "bidirectional"}:
+            hq, hkv = int(q.shape[1]), int(k.shape[1])
+            if (attention_mask or "full").lower() in {"full", "none"}:
+                rows = q[prefix_len:prefix_len + chunk_len].float().transpose(0, 1)                       # [Hq, C, D]
+                keys = k.float().transpose(0, 1).repeat_interleave(hq // hkv, dim=0)                      # [Hq, L, D]
+                prob = torch.softmax(torch.matmul(rows, keys.transpose(1, 2)) * self.model.scale, dim=-1)
+                mass = prob[:, :, prefix_len + chunk_len:prefix_len + chunk_len + query_len]
+                parts.append(mass.mean(dim=2) if reduce_mode == "mean" else mass.sum(dim=2))
+            elif (attention_mask or "").lower() in {"causal", "query_to_chunk"}:
+                parts.append(torch.zeros((hq, chunk_len), dtype=torch.float32, device=q.device))
+            else:
+                raise ValueError(f"Unsupported token attention mask: {attention_mask}")
+        return parts[0] if len(parts) == 1 else parts[0] + parts[1]
 
     # ------------------------------------------------------------------------------------------------ chunk-local KV
     @_on_device

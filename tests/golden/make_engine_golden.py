@@ -137,6 +137,7 @@ def record(engine) -> dict:
     out["chunk_local"] = dict(keeps=keeps, token_ids=[int(t) for t in res.token_ids], n_diff_steps=int(res.n_diff_steps))
     out["sparse_and_delta"] = record_sparse_and_delta(engine)
     out["sampling"] = record_sampling(engine)
+    out["per_head_keep_variants"] = record_keep_variants(engine, spans, full_len, query)
     return out
 
 
@@ -179,6 +180,32 @@ def record_sparse_and_delta(engine) -> dict:
             item = dict(error=f"{type(exc).__name__}: {exc}"[:300])
         cases[name] = item
     return dict(prompt_len=600, seed=13, cases=cases)
+
+
+KEEP_VARIANTS = {
+    "avgpool": dict(token_score_pooling="avgpool"),
+    "no_pooling_mean_reduce": dict(token_score_pooling="none", token_score_reduce="mean"),
+    "keep_low": dict(token_score_keep="low"),
+    "chunk_to_query_full_mask": dict(token_score_direction="chunk_to_query", token_attention_mask="full"),
+    "bidirectional_full_mask_avgpool": dict(token_score_direction="bidirectional", token_attention_mask="full", token_score_pooling="avgpool",
+                                            token_score_pool_kernel=5),
+    "two_layers_last": dict(token_score_layers=2, token_score_layer_mode="last", token_attention_mask="query_to_chunk"),
+}
+
+
+def record_keep_variants(engine, spans, full_len, query) -> dict:
+    """compute_prompt_keep_indices_per_layer_per_head (fastdllm_engine.py:1325-1563) off its defaults: pooling, reduce, keep-low, the
+    chunk->query and bidirectional directions (_engine_chunk_attention_head_scores :1230-1323), the layer window."""
+    cases = {}
+    for name, kwargs in KEEP_VARIANTS.items():
+        try:
+            keep, meta = engine.compute_prompt_keep_indices_per_layer_per_head(full_prompt_len=full_len, prefix_ids=[BOS], chunk_spans=spans,
+                                                                               query_ids=query, token_capacity=128, **kwargs)
+            cases[name] = dict(keep=[[[int(i) for i in head] for head in layer] for layer in keep],
+                               kept=[int(m["kept_tokens"]) for m in meta])
+        except Exception as exc:
+            cases[name] = dict(error=f"{type(exc).__name__}: {exc}"[:300])
+    return dict(full_prompt_len=full_len, cases=cases)
 
 
 SAMPLING_CASES = {

@@ -187,3 +187,38 @@ def test_sampler_settings_at_temperature_zero(golden, model):
         assert ref["cases"]["top_k_1"]["n_diff_steps"] == 1
     finally:
         model.float()
+
+
+def test_per_head_keep_variants(golden, model):
+    """Keep lists off the defaults (average pooling, no pooling + mean reduce, keep-low, chunk->query and bidirectional directions, a
+    window of last layers): every list of the reference engine, up to swaps between scores tied at the cut."""
+    import make_engine_golden as G
+    from oracle import engine_flow as E
+
+    ref = golden["per_head_keep_variants"]
+    sel = golden["selection"]["selected"]
+    chunks, query = _chunks()
+    spans = golden["per_head_keep"]["meta"]
+    swaps = 0
+    for name, kwargs in G.KEEP_VARIANTS.items():
+        case = ref["cases"][name]
+        assert "error" not in case, (name, case)
+        n_layers = int(kwargs.get("token_score_layers", 1))
+        layers = [0] if kwargs.get("token_score_layer_mode", "first") == "first" else list(range(2 - n_layers, 2))
+        for span_meta, ci in zip(spans, sel[:2]):
+            mine, pooled = E.per_head_keep(
+                model, [BOS], chunks[ci], query[-8:], capacity=128, num_kv_heads=2, layers=layers,
+                attention_mask=kwargs.get("token_attention_mask", "causal"), pool_kernel=int(kwargs.get("token_score_pool_kernel", 7)),
+                pooling=kwargs.get("token_score_pooling", "maxpool"), reduce_mode=kwargs.get("token_score_reduce", "sum"),
+                direction=kwargs.get("token_score_direction", "query_to_chunk"), keep_high=kwargs.get("token_score_keep", "high") == "high")
+            for layer in range(2):            # layers beyond the scored window reuse the last scored layer's lists
+                scored = min(layer, len(layers) - 1)
+                for h in range(2):
+                    theirs = [i - span_meta["start"] for i in case["keep"][layer][h] if span_meta["start"] <= i < span_meta["end"]]
+                    ours = mine[scored][h].tolist()
+                    diff = set(ours) ^ set(theirs)
+                    values = pooled[scored][h].detach()
+                    cut = (min if kwargs.get("token_score_keep", "high") == "high" else max)(float(values[i]) for i in ours[1:])
+                    assert len(theirs) == 128 and all(abs(float(values[i]) - cut) <= 1e-5 * max(abs(cut), 1e-12) for i in diff), (name, ci, layer, h, sorted(diff))
+                    swaps += len(diff) // 2
+    assert swaps < 64
