@@ -1108,7 +1108,7 @@ TOY_WORKLOAD = ("CPU toy: Dream architecture, 2 layers, hidden 256, 4/2 heads of
                 "context ids + 32-token query, chunk 512 with chunk BOS, top-4, 4 draft tokens / 1 round, block 32, 32 new tokens, threshold 0.9")
 
 
-def cpu_toy_baseline(repeats: int = 3):
+def cpu_toy_baseline(repeats: int = 3, warmup: int = 1):
     """One toy request on the host cores: the reference's own class when it is staged under oracle/_ref, else the chained CPU
     restatement. A bounded sample by construction: the toy is the only configuration the reference can run on a CPU in seconds."""
     import tempfile
@@ -1120,7 +1120,8 @@ def cpu_toy_baseline(repeats: int = 3):
     with tempfile.TemporaryDirectory() as tmp:
         ckpt, context, query, flags = _toy_setup(tmp)
         try:
-            toy_request.run_reference_class(ckpt, context, query, flags)        # warm-up
+            for _ in range(max(1, warmup)):
+                toy_request.run_reference_class(ckpt, context, query, flags)    # warm-up
             got = toy_request.run_reference_class(ckpt, context, query, flags, repeats=repeats)
             kind = "reference"
         except build_ref.RefUnavailable:
@@ -1164,12 +1165,12 @@ def gpu_toy_same_config(device):
 def run_reference(args, rank: int, world: int):
     if rank != 0:
         return None
-    steps = max(1, min(args.steps, 5))
+    steps, warmup = max(1, min(args.steps, 200)), max(1, min(args.warmup, 50))      # a toy request takes a fraction of a second
     t0 = time.perf_counter()
-    base = cpu_toy_baseline(repeats=steps)
+    base = cpu_toy_baseline(repeats=steps, warmup=warmup)
     wall = time.perf_counter() - t0
     return {
-        "impl": "reference", "metric": "decode_tok_per_s", "value": base["value"], "unit": "tok/s", "n_gpus": world, "steps": steps, "warmup": 1,
+        "impl": "reference", "metric": "decode_tok_per_s", "value": base["value"], "unit": "tok/s", "n_gpus": world, "steps": steps, "warmup": warmup,
         "ms_per_step": base["request_latency_ms"], "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
         "data": "synthetic", "config": {"workload": TOY_WORKLOAD, "note": "the one configuration the reference's CPU path finishes in seconds; "
                                        "the native arm reports this runtime on the same toy as toy_same_config", "wall_s": wall},
