@@ -306,8 +306,21 @@ class PagedDreamModel:
         self.rope_attention_scaling = 0.1 * math.log(factor) + 1.0
         self.__dict__.pop("_step_graphs", None)        # captured steps hold no tables, but shapes may change with longer contexts
 
+    def apply_linear_rope_scaling(self, factor: float) -> None:
+        """Position interpolation as the reference applies it to its LLaDA backend (prefilling_dllm_eval/fastdllm_parallelcomp.py
+        :555-690, scaling type "linear"): positions are divided by `factor` before they meet the unchanged frequencies; no
+        attention scaling. Pages written before the call keep their old rotation."""
+        if factor <= 1.0:
+            return
+        self.rope_position_divisor = float(factor)
+        self.__dict__.pop("_step_graphs", None)
+
     def _rope_tables(self, positions: torch.Tensor) -> Tuple[torch.Tensor, torch.Tensor]:
-        freqs = positions.float().unsqueeze(-1) * self.inv_freq.unsqueeze(0)  # [T, D/2] fp32
+        positions = positions.float()
+        divisor = getattr(self, "rope_position_divisor", 1.0)
+        if divisor != 1.0:
+            positions = positions / divisor
+        freqs = positions.unsqueeze(-1) * self.inv_freq.unsqueeze(0)  # [T, D/2] fp32
         emb = torch.cat((freqs, freqs), dim=-1)
         cos, sin = emb.cos(), emb.sin()
         if self.rope_attention_scaling != 1.0:

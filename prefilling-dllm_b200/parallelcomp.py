@@ -23,6 +23,7 @@ Not built (raise NotImplementedError): the LLaDA backend with chunk-local caches
 
 from __future__ import annotations
 
+import json
 import math
 import os
 import time
@@ -298,9 +299,22 @@ class FastDLLMParallelComp:
         self.model = model
         self.arch = model.arch
         if float(config.rope_scale_factor or 1.0) > 1.0:
-            if self.model_backend == "llada" and (config.rope_scaling_type or "yarn").lower() != "yarn":
-                raise NotImplementedError("linear RoPE scaling of the LLaDA backend is not built (yarn is)")
-            model.apply_yarn_rope_scaling(float(config.rope_scale_factor))      # reference _apply_rope_scaling :539-553
+            kind = (config.rope_scaling_type or "yarn").lower()
+            if self.model_backend == "llada" and kind not in {"linear", "yarn"}:
+                raise ValueError(f"Unsupported LLaDA RoPE scaling type: {config.rope_scaling_type}")     # reference :560-561
+            if self.model_backend == "llada" and kind == "linear":
+                model.apply_linear_rope_scaling(float(config.rope_scale_factor))                          # reference :555-690
+            elif self.model_backend == "llada":
+                # the LLaDA rotary module measures the correction range against `max_sequence_length` (4096 when absent), :566, :645
+                original = 4096
+                try:
+                    with open(os.path.join(config.pretrained or "", "config.json")) as handle:
+                        original = int(json.load(handle).get("max_sequence_length") or 4096)
+                except (OSError, ValueError):
+                    pass
+                model.apply_yarn_rope_scaling(float(config.rope_scale_factor), original_max_position_embeddings=original)   # reference :583-617
+            else:
+                model.apply_yarn_rope_scaling(float(config.rope_scale_factor))                            # reference :539-553
         if tokenizer is None:
             tokenizer = _load_tokenizer(config.pretrained, config.trust_remote_code) or _SimpleTokenizer(self.arch)
         self.tokenizer = tokenizer

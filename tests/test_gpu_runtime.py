@@ -270,3 +270,22 @@ def test_sampled_decoding_is_seeded_and_fills_every_slot(toy_ckpt):
         outs.append(res.sequences)
     assert outs[0] == outs[1]
     assert outs[0] != outs[2]
+
+
+@pytest.mark.gpu
+def test_linear_rope_scaling_divides_the_positions(toy_ckpt):
+    """The LLaDA backend's "linear" RoPE scaling (reference fastdllm_parallelcomp.py:555-690): cos / sin of position / factor over
+    the unchanged frequencies, no attention scaling; the Dream path keeps YaRN."""
+    import torch
+
+    from prefilling_dllm_b200.model import PagedDreamModel
+
+    model = PagedDreamModel.from_pretrained(toy_ckpt, device=torch.device("cuda", 0), dtype=torch.float32, num_pages=4)
+    pos = torch.tensor([0, 1, 7, 1000, 4097], dtype=torch.long, device=model.device)
+    cos0, sin0 = model._rope_tables(pos)
+    model.apply_linear_rope_scaling(4.0)
+    cos1, sin1 = model._rope_tables(pos)
+    freqs = (pos.float() / 4.0).unsqueeze(-1) * model.inv_freq.unsqueeze(0)
+    want = torch.cat((freqs, freqs), dim=-1)
+    assert torch.equal(cos1[:, 0], want.cos()) and torch.equal(sin1[:, 0], want.sin())
+    assert torch.equal(cos1[0], cos0[0]) and not torch.equal(cos1[3], cos0[3])
