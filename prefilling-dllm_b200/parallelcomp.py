@@ -451,6 +451,29 @@ class FastDLLMParallelComp:
                          store_unrotated_k=store_unrotated_k, new_row_mask=row_mask, **kwargs)
 
     # ------------------------------------------------------------------------------------------------ draft
+    def _draft_cache(self, past: Optional[PagedCache], extra_tokens: int) -> PagedCache:
+        """The cache a draft works in: empty, or a PRIVATE copy of the given cache's pages (one copy launch over the K and V planes
+        of all layers) with room for the query and the draft block behind it — the reference concatenates new tensors and
+        leaves its caller's cache alone (:2614-2624); pages would otherwise be written past the caller's length."""
+        if past is None or past.length <= 0:
+            return PagedCache(self, extra_tokens)
+        m = self.model
+        cache = PagedCache(self, past.length + extra_tokens)
+        try:
+            n_pages = math.ceil(past.length / m.page_size)
+            layers, pool_pages = int(m.kv_cache.shape[1]), int(m.kv_cache.shape[2])
+            offsets = (torch.arange(2 * layers, dtype=torch.int32, device=m.device) * pool_pages).unsqueeze(1)
+            pools = m.kv_cache.view(2 * layers * pool_pages, m.kv_cache.shape[3], m.kv_cache.shape[4], m.kv_cache.shape[5])
+            src = (offsets + m.i32(past.page_ids[:n_pages]).unsqueeze(0)).reshape(-1)
+            dst = (offsets + m.i32(cache.page_ids[:n_pages]).unsqueeze(0)).reshape(-1)
+            ops.copy_pages(pools, src, pools, dst, n_lists=2 * layers, tokens_per_list=past.length)
+            cache.length = past.length
+            cache.positions = list(past.positions)
+        except BaseException:
+            cache.release()
+            raise
+        return cache
+
     @torch.inference_mode()
     def generate_partial_draft_rounds_from_cache(self, *, past_key_values: Optional[PagedCache], cache_positions: Sequence[int],
                                                  query_ids: Sequence[int], query_rope_start: int, max_new_tokens: int,
@@ -460,19 +483,18 @@ class FastDLLMParallelComp:
         draft_len = int(max_new_tokens)
         if draft_len <= 0:
             return [], []
-        if past_key_values is not None:
-            raise NotImplementedError("drafting on top of an existing cache is not needed by the selection path")
         query_ids = list(query_ids)
         mask_id = self._mask_token_id()
         q_pos = self._range_positions(query_rope_start, len(query_ids))
-        cache = PagedCache(self, len(query_ids) + draft_len)
+        cache = self._draft_cache(past_key_values, len(query_ids) + draft_len)
         try:
             last_logit = None
             if query_ids:
-                logits, _ = self._forward_packed([query_ids], [q_pos], causal=False, store_slots=cache.slots(0, len(query_ids)),
-                                                 logit_rows=[len(query_ids) - 1])
+                base = cache.length       # the given cache's tokens (a private copy of its pages): the query rows see them
+                logits, _ = self._forward_packed([query_ids], [q_pos], causal=False, store_slots=cache.slots(base, len(query_ids)),
+                                                 logit_rows=[len(query_ids) - 1], cache=cache if base else None, ctx_len=base)
                 last_logit = logits[0]
-                cache.length = len(query_ids)
+                cache.length = base + len(query_ids)
             block_pos = self._range_positions(query_rope_start + len(query_ids), draft_len)
             block = torch.full((draft_len,), mask_id, dtype=torch.long, device=self.device)
             confirmed = torch.zeros(draft_len, dtype=torch.bool, device=self.device)
@@ -580,19 +602,18 @@ class FastDLLMParallelComp:
         draft_len = int(max_new_tokens)
         if draft_len <= 0:
             return [], 0
-        if past_key_values is not None:
-            raise NotImplementedError("drafting on top of an existing cache is not needed by the selection path")
         query_ids = list(query_ids)
         if not query_ids:
             raise ValueError("draft needs at least one context token")
         mask_id = self._mask_token_id()
-        cache = PagedCache(self, len(query_ids) + draft_len)
+        cache = self._draft_cache(past_key_values, len(query_ids) + draft_len)
         try:
             q_pos = self._range_positions(query_rope_start, len(query_ids))
-            logits, _ = self._forward_packed([query_ids], [q_pos], causal=False, store_slots=cache.slots(0, len(query_ids)),
-                                             logit_rows=[len(query_ids) - 1])
+            base = cache.length
+            logits, _ = self._forward_packed([query_ids], [q_pos], causal=False, store_slots=cache.slots(base, len(query_ids)),
+                                             logit_rows=[len(query_ids) - 1], cache=cache if base else None, ctx_len=base)
             last_logit = logits[0]
-            cache.length = len(query_ids)
+            cache.length = base + len(query_ids)
             block_pos = self._range_positions(query_rope_start + len(query_ids), draft_len)
             block = torch.full((draft_len,), mask_id, dtype=torch.long, device=self.device)
             target = min(draft_len, max(0, int(partial_steps)))

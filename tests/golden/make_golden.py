@@ -255,6 +255,29 @@ FLAG_VARIANTS = {
 }
 
 
+def record_drafts_on_cache(runtime, context, query) -> dict:
+    """The two partial drafts of the reference class on top of an EXISTING cache (fastdllm_parallelcomp.py:2512-2676): the cache of the
+    independently prefilled selected chunks (build_prefill_cache), the query forwarded against it, then the draft block."""
+    cache, positions, _ = runtime.build_prefill_cache(prefix_ids=runtime.bos_ids(), context_ids=context, query_ids=query)
+    start = max(positions) + 1
+    rounds_ids, rounds_mask = runtime.generate_partial_draft_rounds_from_cache(
+        past_key_values=cache, cache_positions=positions, query_ids=query, query_rope_start=start, max_new_tokens=6, partial_rounds=3)
+    steps_ids, steps_filled = runtime.generate_partial_draft_from_cache(
+        past_key_values=cache, cache_positions=positions, query_ids=query, query_rope_start=start, max_new_tokens=6, partial_steps=4)
+    alone_ids, alone_mask = runtime.generate_partial_draft_rounds_from_cache(
+        past_key_values=None, cache_positions=[], query_ids=query, query_rope_start=start, max_new_tokens=6, partial_rounds=3)
+    return dict(cache_tokens=len(positions), query_rope_start=int(start), rounds=dict(ids=[int(t) for t in rounds_ids], mask=[bool(m) for m in rounds_mask]),
+                steps=dict(ids=[int(t) for t in steps_ids], filled=int(steps_filled)),
+                without_cache=dict(ids=[int(t) for t in alone_ids], mask=[bool(m) for m in alone_mask]))
+
+
+DRAFT_ON_CACHE_VARIANTS = {
+    "chunk_query_reuse": dict(README_FLAGS, cache_build_mode="chunk_query", chunk_position_mode="reuse", query_position_mode="after_reused_window"),
+    "chunk_query_evict_global_cap128": dict(README_FLAGS, cache_build_mode="chunk_query", chunk_position_mode="reuse",
+                                            query_position_mode="after_reused_window", token_capacity=128),
+}
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--reference", default=os.environ.get("PDLLM_REFERENCE_ROOT"), required="PDLLM_REFERENCE_ROOT" not in os.environ,
@@ -262,7 +285,8 @@ def main():
     ap.add_argument("--out", default=os.path.join(HERE, "toy_reference.json"))
     ap.add_argument("--out128", default=os.path.join(HERE, "toy128_reference.json"))
     ap.add_argument("--out-flags", default=os.path.join(HERE, "toy_flags_reference.json"))
-    ap.add_argument("--only", choices=["toy", "toy128", "flags"], default=None)
+    ap.add_argument("--out-drafts", default=os.path.join(HERE, "toy_draft_on_cache_reference.json"))
+    ap.add_argument("--only", choices=["toy", "toy128", "flags", "drafts"], default=None)
     args = ap.parse_args()
     torch.manual_seed(0)
     torch.set_num_threads(max(1, os.cpu_count() or 1))
@@ -296,6 +320,18 @@ def main():
             with open(args.out_flags, "w") as handle:
                 json.dump(golden, handle)
             print("wrote", args.out_flags, os.path.getsize(args.out_flags), "bytes")
+        if args.only in (None, "drafts"):
+            context, query = toy_inputs()
+            golden = {"config": dict(TOY), "context_seed": 0, "runs": {}}
+            ckpt = os.path.join(tmp, "ckpt_toy_drafts")
+            write_toy_checkpoint(ckpt)
+            for name, flags in DRAFT_ON_CACHE_VARIANTS.items():
+                _, runtime = load_reference(args.reference, ckpt, **flags)
+                golden["runs"][name] = dict(flags=flags, **record_drafts_on_cache(runtime, context, query))
+                print(name, golden["runs"][name]["rounds"], golden["runs"][name]["steps"], golden["runs"][name]["without_cache"], flush=True)
+            with open(args.out_drafts, "w") as handle:
+                json.dump(golden, handle)
+            print("wrote", args.out_drafts, os.path.getsize(args.out_drafts), "bytes")
         if args.only in (None, "toy128"):
             context, query = toy_inputs(vocab=TOY128["vocab_size"])
             golden = {"config": dict(TOY128), "flags": dict(README_FLAGS), "context_seed": 0, "runs": {}}

@@ -289,3 +289,37 @@ def test_linear_rope_scaling_divides_the_positions(toy_ckpt):
     want = torch.cat((freqs, freqs), dim=-1)
     assert torch.equal(cos1[:, 0], want.cos()) and torch.equal(sin1[:, 0], want.sin())
     assert torch.equal(cos1[0], cos0[0]) and not torch.equal(cos1[3], cos0[3])
+
+
+@pytest.mark.gpu
+def test_drafts_on_top_of_an_existing_cache(toy_ckpt):
+    """The two partial drafts of the reference class with `past_key_values` given (fastdllm_parallelcomp.py:2512-2676): the
+    query is forwarded against the cache of the independently prefilled chunks, then the draft block against both. Golden:
+    the unmodified reference class on CPU (tests/golden/make_golden.py --only drafts). The caller's cache is left alone."""
+    import make_golden
+    from prefilling_dllm_b200.parallelcomp import load_fastdllm_parallelcomp
+
+    with open(os.path.join(HERE, "golden", "toy_draft_on_cache_reference.json")) as handle:
+        golden = json.load(handle)
+    context, query = make_golden.toy_inputs()
+    for name, ref in golden["runs"].items():
+        rt = load_fastdllm_parallelcomp(pretrained=toy_ckpt, device="cuda", dtype="float32", **ref["flags"])
+        free0 = rt.model.allocator.num_free_pages
+        cache, positions, _ = rt.build_prefill_cache(prefix_ids=rt.bos_ids(), context_ids=context, query_ids=query)
+        try:
+            assert len(positions) == ref["cache_tokens"] and max(positions) + 1 == ref["query_rope_start"], name
+            length, pages = cache.length, list(cache.page_ids)
+            start = ref["query_rope_start"]
+            ids, mask = rt.generate_partial_draft_rounds_from_cache(past_key_values=cache, cache_positions=positions, query_ids=query,
+                                                                    query_rope_start=start, max_new_tokens=6, partial_rounds=3)
+            assert (list(ids), list(mask)) == (ref["rounds"]["ids"], ref["rounds"]["mask"]), name
+            ids, filled = rt.generate_partial_draft_from_cache(past_key_values=cache, cache_positions=positions, query_ids=query,
+                                                               query_rope_start=start, max_new_tokens=6, partial_steps=4)
+            assert (list(ids), int(filled)) == (ref["steps"]["ids"], ref["steps"]["filled"]), name
+            ids, mask = rt.generate_partial_draft_rounds_from_cache(past_key_values=None, cache_positions=[], query_ids=query,
+                                                                    query_rope_start=start, max_new_tokens=6, partial_rounds=3)
+            assert (list(ids), list(mask)) == (ref["without_cache"]["ids"], ref["without_cache"]["mask"]), name
+            assert (cache.length, list(cache.page_ids)) == (length, pages)
+        finally:
+            cache.release()
+        assert rt.model.allocator.num_free_pages == free0, name
