@@ -159,3 +159,34 @@ def test_engine_facade_has_the_reference_api():
                 assert p.default is inspect.Parameter.empty, f"{name}.{pname} must be required"
             elif isinstance(default, (int, float, str, bool)) or default is None:
                 assert p.default == default, f"{name}.{pname}: default {p.default!r} != {default!r}"
+
+
+def test_delta_windows_and_mode_checks_of_the_engine_facade():
+    """Host side of the sparse prefill / decode delta paths: which rows an anchor's correction reaches (reference
+    attention_v4.py:145-158) equals the oracle's windows, and the argument checks raise what the reference raises
+    (fastdllm_engine.py:1924-1935, :2012-2017, :2079-2080)."""
+    from oracle import engine_flow as E
+    from prefilling_dllm_b200.engine import FastDLLMDreamEngine as Engine
+
+    for direction, left, right in (("left", 3, 0), ("right", 0, 2), ("both", 1, 2), ("left", 0, 0)):
+        anchors = list(range(0 if direction == "right" else 3, 19, 4))
+        rows, which = Engine._spread_rows(anchors, 19, left=left, right=right, direction=direction)
+        mine = torch.zeros(1, 19, 1)
+        for r, w in zip(rows, which):
+            mine[0, r, 0] += float(w + 1)
+        dense = torch.zeros(1, len(anchors), 1) + torch.arange(1, len(anchors) + 1).view(1, -1, 1)
+        theirs = E._spread_delta(torch.zeros(1, 19, 1), dense, anchors, left=left, right=right, direction=direction, scale=1.0)
+        assert torch.equal(mine, theirs), direction
+
+    ok = dict(prefill_sparse_mode="none", prefill_delta_mode="none", prefill_delta_selection_mode="none", prefill_delta_direction="left",
+              decode_delta_mode="none", has_keep=True)
+    Engine._check_modes(**ok)
+    Engine._check_modes(**dict(ok, prefill_sparse_mode="eviction_mask", prefill_delta_mode="s4_left3", prefill_delta_direction="both"))
+    Engine._check_modes(**dict(ok, decode_delta_mode="s4_left3"))
+    for bad, error in ((dict(prefill_sparse_mode="other"), ValueError), (dict(prefill_sparse_mode="eviction_mask", has_keep=False), ValueError),
+                       (dict(prefill_sparse_mode="eviction_mask", prefill_delta_mode="s8"), ValueError),
+                       (dict(prefill_sparse_mode="eviction_mask", prefill_delta_direction="up"), ValueError),
+                       (dict(decode_delta_mode="s8"), ValueError),
+                       (dict(prefill_sparse_mode="eviction_mask", prefill_delta_selection_mode="selection_dense_add"), NotImplementedError)):
+        with pytest.raises(error):
+            Engine._check_modes(**dict(ok, **bad))
